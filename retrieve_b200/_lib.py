@@ -1,0 +1,87 @@
+"""ctypes binding of ``libretrieve_b200.so`` (the C-ABI declared in
+``include/retrieve_b200.h``).
+
+The library is built in-tree by ``retrieve_b200.build``; there is no fallback:
+if it is missing or fails to load, :func:`lib` raises ``ImportError`` naming
+the cause, so no op can silently run on another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libretrieve_b200.so"
+HEADER_PATH = Path(__file__).resolve().parent.parent / "include" / "retrieve_b200.h"
+
+RB_OK = 0
+RB_ERR_INVALID_ARG = 1
+RB_ERR_TYPE = 2
+RB_ERR_UNSUPPORTED = 3
+RB_ERR_WORKSPACE = 4
+RB_ERR_CUDA = 5
+RB_ERR_DEVICE = 6
+
+RB_F16, RB_BF16, RB_I8, RB_F32 = 0, 1, 2, 3
+
+_c_int = ctypes.c_int
+_c_i64 = ctypes.c_int64
+_c_size = ctypes.c_size_t
+_vp = ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/retrieve_b200.h
+_SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "rb_last_error": (ctypes.c_char_p, []),
+    "rb_abi_version": (_c_int, []),
+    "rb_dense_topk_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "rb_dense_topk": (
+        _c_int,
+        [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp, _c_size, _vp],
+    ),
+    "rb_dense_topk_launches": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_int)]),
+    "rb_merge_topk_workspace_size": (_c_int, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "rb_merge_topk": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),
+    "rb_set_profile_events": (_c_int, [_vp, _vp]),
+    "rb_workspace_device_error": (_c_int, [_vp, _c_size, ctypes.POINTER(_c_int)]),
+}
+
+_LIB: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (loaded once). Raises ``ImportError`` if it is absent."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH.name} is not built; run `python -m retrieve_b200.build` "
+            "(the CUDA kernels are the only implementation of these ops)"
+        )
+    handle = ctypes.CDLL(str(LIB_PATH))
+    for name, (restype, argtypes) in _SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _LIB = handle
+    return handle
+
+
+def header_symbols() -> list[str]:
+    """Every function the public header declares (``RB_API`` prototypes)."""
+    text = HEADER_PATH.read_text()
+    return re.findall(r"^RB_API\s+[\w\s\*]+?\b(rb_\w+)\s*\(", text, flags=re.M)
+
+
+def check(rc: int, what: str) -> None:
+    """Maps a C-ABI status to the reference's Python exception convention."""
+    if rc == RB_OK:
+        return
+    msg = lib().rb_last_error().decode(errors="replace")
+    text = f"{what}: {msg}" if msg else what
+    if rc == RB_ERR_INVALID_ARG or rc == RB_ERR_UNSUPPORTED:
+        raise ValueError(text)
+    if rc == RB_ERR_TYPE:
+        raise TypeError(text)
+    raise RuntimeError(f"{text} (status {rc})")

@@ -1,0 +1,149 @@
+// extern "C" entry points of libretrieve_b200: argument checks, workspace
+// carving and the sequence of kernel launches for each op.
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "rb_capi_internal.h"
+
+namespace rb {
+
+static thread_local std::string g_last_error;
+
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
+ProfileEvents& profile_events() {
+  static thread_local ProfileEvents ev;
+  return ev;
+}
+
+void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stream);
+
+static int fail(int code, const char* msg) {
+  set_last_error(msg);
+  return code;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Workspace tail: one device error word, 256-byte aligned at the end.
+static int* ws_err_word(void* ws, size_t ws_bytes) {
+  return reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + ws_bytes - 256);
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" {
+
+const char* rb_last_error(void) { return g_last_error.c_str(); }
+
+int rb_abi_version(void) { return 1; }
+
+int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* bytes) {
+  if (bytes == nullptr) return fail(RB_ERR_INVALID_ARG, "bytes is null");
+  if (B < 0 || N < 0 || D <= 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk: bad shape or k");
+  (void)dtype;
+  *bytes = dense_workspace_bytes(B, N, k);
+  return RB_OK;
+}
+
+int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int64_t id_offset,
+                  int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk: dtype must be f16 or bf16");
+  if (B < 0 || N < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk: bad B, N or k");
+  if (k > 256) return fail(RB_ERR_UNSUPPORTED, "dense_topk: k > 256 is not supported");
+  if (D * 2 != 128 && D * 2 != 256) return fail(RB_ERR_UNSUPPORTED, "dense_topk: D must be 64 or 128");
+  if (B == 0) return RB_OK;
+  if (out_ids == nullptr || out_scores == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_topk: null output");
+  if (N == 0) {
+    fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, stream);
+    return cudaGetLastError() == cudaSuccess ? RB_OK : fail(RB_ERR_CUDA, "fill_empty launch failed");
+  }
+  if (!aligned16(queries) || !aligned16(items)) return fail(RB_ERR_INVALID_ARG, "dense_topk: 16-byte alignment");
+  const size_t need = dense_workspace_bytes(B, N, k);
+  if (workspace == nullptr || workspace_bytes < need) return fail(RB_ERR_WORKSPACE, "dense_topk: workspace too small");
+
+  DensePlan pl;
+  dense_plan(B, N, k, pl);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  uint2* lists = reinterpret_cast<uint2*>(w);
+  w += align_up(static_cast<size_t>(B) * pl.n_splits * pl.cap * sizeof(uint2), 256);
+  int* counts = reinterpret_cast<int*>(w);
+  w += align_up(static_cast<size_t>(B) * pl.n_splits * sizeof(int), 256);
+  float* thresh = reinterpret_cast<float*>(w);
+  int* err = ws_err_word(workspace, workspace_bytes);
+  if (cudaMemsetAsync(err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
+
+  const int elem = (dtype == RB_BF16) ? 1 : 0;
+  ProfileEvents& pe = profile_events();
+  for (int lv = 0; lv < pl.n_levels; ++lv) {
+    const float* seed = (lv == 0) ? nullptr : thresh + static_cast<size_t>((lv - 1) & 1) * B;
+    const bool last = (lv == pl.n_levels - 1);
+    if (last && pe.start) cudaEventRecord(pe.start, stream);
+    int rc = dense_scan_pass(elem, queries, items, B, N, D, pl, lv, k, seed, lists, counts, err, stream);
+    if (rc != RB_OK) return rc;
+    if (last && pe.stop) cudaEventRecord(pe.stop, stream);
+    rc = merge_lists(lists, counts, B, pl.n_splits, pl.cap, k, id_offset, last ? out_ids : nullptr,
+                     last ? out_scores : nullptr, last ? nullptr : thresh + static_cast<size_t>(lv & 1) * B, stream);
+    if (rc != RB_OK) return rc;
+  }
+  return RB_OK;
+}
+
+int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launches) {
+  if (n_launches == nullptr) return fail(RB_ERR_INVALID_ARG, "n_launches is null");
+  (void)D;
+  (void)dtype;
+  if (B <= 0) {
+    *n_launches = 0;
+    return RB_OK;
+  }
+  if (N == 0) {
+    *n_launches = 1;
+    return RB_OK;
+  }
+  DensePlan pl;
+  dense_plan(B, N, k, pl);
+  *n_launches = 2 * pl.n_levels;
+  return RB_OK;
+}
+
+int rb_merge_topk_workspace_size(int W, int B, int kin, size_t* bytes) {
+  if (bytes == nullptr || W < 1 || B < 0 || kin < 0) return fail(RB_ERR_INVALID_ARG, "merge_topk: bad arguments");
+  *bytes = merge_shard_ws_bytes(W, B, kin);
+  return RB_OK;
+}
+
+int rb_merge_topk(const int64_t* ids, const float* scores, int W, int B, int kin, int k, int64_t* out_ids,
+                  float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+  if (W < 1 || B < 0 || kin < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "merge_topk: bad arguments");
+  if (k > 1024) return fail(RB_ERR_UNSUPPORTED, "merge_topk: k > 1024");
+  if (B == 0) return RB_OK;
+  if (workspace == nullptr || workspace_bytes < merge_shard_ws_bytes(W, B, kin))
+    return fail(RB_ERR_WORKSPACE, "merge_topk: workspace too small");
+  return merge_shard_lists(ids, scores, W, B, kin, k, out_ids, out_scores, workspace,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int rb_set_profile_events(void* start_event, void* stop_event) {
+  ProfileEvents& pe = profile_events();
+  pe.start = static_cast<cudaEvent_t>(start_event);
+  pe.stop = static_cast<cudaEvent_t>(stop_event);
+  return RB_OK;
+}
+
+int rb_workspace_device_error(const void* workspace, size_t workspace_bytes, int* err_out) {
+  if (workspace == nullptr || err_out == nullptr || workspace_bytes < 256)
+    return fail(RB_ERR_INVALID_ARG, "workspace_device_error: bad arguments");
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, ws_err_word(const_cast<void*>(workspace), workspace_bytes), sizeof(int),
+                             cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(RB_ERR_CUDA, cudaGetErrorString(e));
+  *err_out = v;
+  return RB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,472 @@
+// Fused dense scoring + exact top-k for sm_100a (B200).
+//
+// One persistent CTA per SM. A task is (query group, item split): the CTA
+// holds NG x 128 queries resident in shared memory (TMA, 128-byte swizzle) and
+// streams its split's item tiles (128 items each) through a STAGES-deep TMA
+// ring. One elected thread issues tcgen05.mma (M = 128 queries, N = 128 items,
+// K = the embedding dim) into a double-buffered TMEM accumulator; the epilogue
+// warps read their query row out of TMEM (thread = query, 32 columns at a
+// time), drop every 32-item chunk whose max is below the query's threshold and
+// append the rest to the query's candidate list (rb_select.cuh). No [B, N]
+// score matrix ever reaches HBM.
+//
+// Warp roles (NG = 2: 320 threads):
+//   warp 0      TMA producer (queries once per task, item tiles per stage)
+//   warp 1      TMEM allocator + MMA issuer
+//   warps 2..   epilogue, 4 warps per query group (TMEM lane quadrant = warp % 4)
+//
+// Reference semantics replaced: PostfilterKNN.score + masked_topk
+// (retrieve/src/retrieve/modules/knn.py:62-76, functional.py:57-85), i.e.
+// torch.mm(q_fp16, E_t, out_dtype=fp32) followed by torch.topk, with ties broken
+// toward the lower item id.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "rb_capi_internal.h"
+#include "rb_common.cuh"
+#include "rb_select.cuh"
+
+namespace rb {
+
+constexpr int kTileItems = 128;  // N of one MMA = items per pipeline stage
+constexpr int kQTile = 128;      // M of one MMA = queries per group
+
+struct alignas(64) DenseScanParams {
+  CUtensorMap tmap_q;
+  CUtensorMap tmap_x;
+  const float* seed;  // [B] pass threshold per query (>=), or null for -inf
+  uint2* lists;       // [B, n_splits, cap]
+  int* counts;        // [B, n_splits]
+  int* err;           // device error word
+  int B, N;
+  int n_qsg, n_splits;
+  int tile_stride, tile_offset, pass_tiles;
+  int k, cap;
+};
+
+template <int KB, int NG, int STAGES>
+struct DenseSmemLayout {
+  static constexpr int kOpTile = kQTile * 128;  // bytes of one 128-row x 128-byte K-block
+  static constexpr int kA = NG * KB * kOpTile;
+  static constexpr int kB = STAGES * KB * kOpTile;
+  static constexpr int kEpiWarps = 4 * NG;
+  static constexpr int kHist = kEpiWarps * 256 * 4;
+  static constexpr int kBar = (2 * STAGES + 2 + 4 + 1) * 8;
+  static constexpr int kMisc = 16;
+  static constexpr int kTotal = kA + kB + kHist + kBar + kMisc + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ void split_range(int split, int n_splits, int pass_tiles, int& lo, int& hi) {
+  lo = static_cast<int>((static_cast<int64_t>(split) * pass_tiles) / n_splits);
+  hi = static_cast<int>((static_cast<int64_t>(split + 1) * pass_tiles) / n_splits);
+}
+
+template <int ELEM, int KB, int NG, int STAGES, int EPL>
+__global__ void __launch_bounds__(64 + 128 * NG, 1)
+    dense_scan_kernel(const __grid_constant__ DenseScanParams p) {
+  using L = DenseSmemLayout<KB, NG, STAGES>;
+  constexpr int kElemBytes = (ELEM == 2) ? 1 : 2;
+  constexpr int kElemsPerKBlock = 128 / kElemBytes;
+  constexpr int kKSteps = 128 / 32;  // MMA K = 32 bytes per instruction
+  constexpr uint32_t kTmemCols = 2 * NG * 128;
+  constexpr uint32_t kIdesc =
+      (ELEM == 2) ? make_idesc(2, 1, kQTile, kTileItems) : make_idesc(1, ELEM == 1 ? 1 : 0, kQTile, kTileItems);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + L::kA;
+  uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* a_full = bars + 2 * STAGES;
+  uint64_t* a_empty = a_full + 1;
+  uint64_t* acc_full = a_full + 2;   // [2]
+  uint64_t* acc_empty = a_full + 4;  // [2]
+  uint64_t* drain_bar = a_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tasks = p.n_qsg * p.n_splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(a_full, 1);
+    mbar_init(a_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], L::kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_q);
+    tma_prefetch_desc(&p.tmap_x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int a_iter = 0;
+      uint32_t armed = 0;  // item stages armed in total
+      for (int t = blockIdx.x; t < n_tasks && !*abort_flag; t += gridDim.x) {
+        const int qsg = t % p.n_qsg, split = t / p.n_qsg;
+        if (a_iter > 0 && !mbar_wait(a_empty, (a_iter - 1) & 1, abort_flag)) {
+          atomicCAS(p.err, 0, kDevTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(a_full, NG * KB * L::kOpTile);
+        for (int g = 0; g < NG; ++g)
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d(smA + (g * KB + kb) * L::kOpTile, &p.tmap_q, a_full, kb * kElemsPerKBlock,
+                        qsg * NG * kQTile + g * kQTile);
+        ++a_iter;
+        int lo, hi;
+        split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+        for (int pt = lo; pt < hi; ++pt) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
+            atomicCAS(p.err, 0, kDevTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          const int tile = pt * p.tile_stride + p.tile_offset;
+          mbar_arrive_expect_tx(&full_bar[stage], KB * L::kOpTile);
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d(smB + (stage * KB + kb) * L::kOpTile, &p.tmap_x, &full_bar[stage], kb * kElemsPerKBlock,
+                        tile * kTileItems);
+          ++armed;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every TMA this thread issued has landed before the CTA may exit.
+      if (a_iter > 0) mbar_wait_drain(a_full, (a_iter - 1) & 1);
+      for (int s = 0; s < STAGES; ++s) {
+        const uint32_t n_s = armed / STAGES + (static_cast<uint32_t>(s) < armed % STAGES ? 1u : 0u);
+        if (n_s > 0) mbar_wait_drain(&full_bar[s], (n_s - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int a_iter = 0;
+      const uint32_t a_base = smem_u32(smA), b_base = smem_u32(smB);
+      for (int t = blockIdx.x; t < n_tasks && !*abort_flag; t += gridDim.x) {
+        const int split = t / p.n_qsg;
+        if (!mbar_wait(a_full, a_iter & 1, abort_flag)) {
+          atomicCAS(p.err, 0, kDevTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        ++a_iter;
+        int lo, hi;
+        split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+        bool ok = true;
+        for (int pt = lo; pt < hi; ++pt) {
+          if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag) ||
+              !mbar_wait(&full_bar[stage], phase, abort_flag)) {
+            atomicCAS(p.err, 0, kDevTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_col = tmem_base + static_cast<uint32_t>(acc * NG * 128);
+#pragma unroll
+          for (int g = 0; g < NG; ++g) {
+#pragma unroll
+            for (int kb = 0; kb < KB; ++kb) {
+#pragma unroll
+              for (int j = 0; j < kKSteps; ++j) {
+                const uint64_t ad = sw128_kmajor_desc(a_base + (g * KB + kb) * L::kOpTile + j * 32);
+                const uint64_t bd = sw128_kmajor_desc(b_base + (stage * KB + kb) * L::kOpTile + j * 32);
+                if constexpr (ELEM == 2)
+                  mma_i8(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+                else
+                  mma_f16(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+              }
+            }
+          }
+          mma_commit(&empty_bar[stage]);
+          mma_commit(&acc_full[acc]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1;
+        }
+        if (!ok) break;
+        mma_commit(a_empty);
+      }
+      // Drain: no MMA may still be writing TMEM when it is released.
+      mma_commit(drain_bar);
+      mbar_wait_drain(drain_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;             // 0 .. 4*NG-1
+    const int g = ew >> 2;               // query group
+    const int quad = warp & 3;           // TMEM lane quadrant this warp may access
+    uint32_t* hist = hist_all + ew * 256;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    for (int t = blockIdx.x; t < n_tasks; t += gridDim.x) {
+      const int qsg = t % p.n_qsg, split = t / p.n_qsg;
+      const int q = qsg * NG * kQTile + g * kQTile + quad * 32 + lane;
+      const bool valid_q = q < p.B;
+      float thresh = (valid_q && p.seed != nullptr) ? p.seed[q] : -INFINITY;
+      int count = 0;
+      uint2* list = p.lists + (static_cast<size_t>(valid_q ? q : 0) * p.n_splits + split) * p.cap;
+      int lo, hi;
+      split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+      bool ok = true;
+      for (int pt = lo; pt < hi; ++pt) {
+        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
+          if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
+        const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
+#pragma unroll 1
+        for (int ch = 0; ch < kTileItems / 32; ++ch) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32x32(col0 + ch * 32, r);
+          tmem_wait_ld();
+          float s[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(r[j]);
+          float m0 = fmaxf(s[0], s[1]), m1 = fmaxf(s[2], s[3]);
+#pragma unroll
+          for (int j = 4; j < 32; j += 4) {
+            m0 = fmaxf(m0, fmaxf(s[j], s[j + 1]));
+            m1 = fmaxf(m1, fmaxf(s[j + 2], s[j + 3]));
+          }
+          const bool pass = valid_q && fmaxf(m0, m1) >= thresh;
+          if (__any_sync(RB_FULL_MASK, pass)) {
+            const bool need = pass && (count > p.cap - 32);
+            warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+            if (pass) append_chunk(list, count, thresh, s, row0 + ch * 32, static_cast<uint32_t>(p.N));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (!ok) break;
+      const bool need = valid_q && count > p.k;
+      warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+      if (valid_q) p.counts[static_cast<size_t>(q) * p.n_splits + split] = count;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) == cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D K-major tensor map: rows x cols elements, box 128 rows x 128 bytes, 128-B swizzle.
+static bool make_tmap(CUtensorMap* map, const void* base, int elem, uint64_t rows, uint64_t cols) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const int eb = (elem == 2) ? 1 : 2;
+  CUtensorMapDataType dt = (elem == 2)   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                           : (elem == 1) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * eb};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / eb), 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int ELEM, int KB, int NG, int STAGES, int EPL>
+static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaStream_t stream) {
+  using L = DenseSmemLayout<KB, NG, STAGES>;
+  auto kern = dense_scan_kernel<ELEM, KB, NG, STAGES, EPL>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, 64 + 128 * NG, L::kTotal, stream>>>(prm);
+  return cudaGetLastError();
+}
+
+}  // namespace rb
+
+// ---------------------------------------------------------------------------
+// Scan-plan shared by the dense entry points.
+// ---------------------------------------------------------------------------
+namespace rb {
+
+int dense_ng(int B) { return B <= kQTile ? 1 : 2; }
+
+int list_cap(int k) {
+  // room for k survivors + one 32-item chunk + slack; multiple of 32; <= 512
+  int cap = ((2 * k + 64) + 31) / 32 * 32;
+  return std::min(cap, 512);
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+void dense_plan(int B, int N, int k, DensePlan& pl) {
+  pl.ng = dense_ng(B);
+  pl.n_qsg = (B + pl.ng * kQTile - 1) / (pl.ng * kQTile);
+  const int sms = num_sms();
+  pl.n_splits = std::max(1, sms / std::max(1, pl.n_qsg));
+  pl.cap = list_cap(k);
+  pl.tiles = (N + kTileItems - 1) / kTileItems;
+  // Sampled threshold levels: level 0 keeps about n_splits * cap / 2 items so
+  // no list overflows; level 1 about 16x more; the last level scans all tiles.
+  pl.n_levels = 0;
+  const int64_t target0 = static_cast<int64_t>(pl.n_splits) * pl.cap / 2;
+  const int64_t tiles0 = std::max<int64_t>(1, target0 / kTileItems);
+  if (pl.tiles >= 64 * tiles0 && pl.tiles * static_cast<int64_t>(kTileItems) >= 8 * static_cast<int64_t>(k)) {
+    int s1 = 16;
+    int s0 = static_cast<int>(pl.tiles / tiles0);
+    s0 = std::max(s1, s0 / s1 * s1);
+    pl.level_stride[pl.n_levels++] = s0;
+    pl.level_stride[pl.n_levels++] = s1;
+  }
+  pl.level_stride[pl.n_levels++] = 1;
+}
+
+size_t dense_workspace_bytes(int B, int N, int k) {
+  DensePlan pl;
+  dense_plan(B, N, k, pl);
+  size_t lists = static_cast<size_t>(B) * pl.n_splits * pl.cap * sizeof(uint2);
+  size_t counts = static_cast<size_t>(B) * pl.n_splits * sizeof(int);
+  size_t th = 2 * static_cast<size_t>(B) * sizeof(float);
+  return align_up(lists, 256) + align_up(counts, 256) + align_up(th, 256) + 256;
+}
+
+int dense_scan_pass(int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl, int level,
+                    int k, const float* seed, uint2* lists, int* counts, int* err, cudaStream_t stream) {
+  DenseScanParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  const int eb = (elem == 2) ? 1 : 2;
+  const int row_bytes = D * eb;
+  if (!make_tmap(&prm.tmap_q, q, elem, static_cast<uint64_t>(B), static_cast<uint64_t>(D)) ||
+      !make_tmap(&prm.tmap_x, x, elem, static_cast<uint64_t>(N), static_cast<uint64_t>(D))) {
+    set_last_error("cuTensorMapEncodeTiled failed (alignment or driver entry point)");
+    return RB_ERR_CUDA;
+  }
+  const int stride = pl.level_stride[level];
+  prm.seed = seed;
+  prm.lists = lists;
+  prm.counts = counts;
+  prm.err = err;
+  prm.B = B;
+  prm.N = N;
+  prm.n_qsg = pl.n_qsg;
+  prm.n_splits = pl.n_splits;
+  prm.tile_stride = stride;
+  prm.tile_offset = 0;
+  prm.pass_tiles = (pl.tiles + stride - 1) / stride;
+  prm.k = k;
+  prm.cap = pl.cap;
+  const int n_tasks = pl.n_qsg * pl.n_splits;
+  const int grid = std::min(n_tasks, num_sms());
+  cudaError_t e = cudaSuccess;
+  const int kb = row_bytes / 128;
+#define RB_DISPATCH(ELEM, KB, NG, ST)                                                    \
+  if (elem == ELEM && kb == KB && pl.ng == NG) {                                          \
+    e = (pl.cap <= 256) ? launch_dense_scan<ELEM, KB, NG, ST, 8>(prm, grid, stream)       \
+                        : launch_dense_scan<ELEM, KB, NG, ST, 16>(prm, grid, stream);     \
+    handled = true;                                                                       \
+  }
+  bool handled = false;
+  RB_DISPATCH(0, 1, 1, 8)
+  RB_DISPATCH(0, 1, 2, 8)
+  RB_DISPATCH(0, 2, 1, 4)
+  RB_DISPATCH(0, 2, 2, 4)
+  RB_DISPATCH(1, 1, 1, 8)
+  RB_DISPATCH(1, 1, 2, 8)
+  RB_DISPATCH(1, 2, 1, 4)
+  RB_DISPATCH(1, 2, 2, 4)
+#undef RB_DISPATCH
+  if (!handled) {
+    set_last_error("dense scan: unsupported dtype / row width");
+    return RB_ERR_UNSUPPORTED;
+  }
+  if (e != cudaSuccess) {
+    set_last_error(cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
+}  // namespace rb

@@ -1,0 +1,49 @@
+// Host-side declarations shared by the .cu files behind the C-ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/retrieve_b200.h"
+
+namespace rb {
+
+void set_last_error(const char* msg);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// How one dense top-k call is cut into scan passes (see dense_scan_sm100.cu).
+struct DensePlan {
+  int ng;        // query groups of 128 per CTA (1 or 2)
+  int n_qsg;     // query super-groups of ng * 128
+  int n_splits;  // item splits per super-group
+  int cap;       // candidate-list capacity per (query, split)
+  int tiles;     // 128-item tiles in the corpus
+  int n_levels;  // scan passes; the last one covers every tile
+  int level_stride[4];
+};
+
+void dense_plan(int B, int N, int k, DensePlan& pl);
+size_t dense_workspace_bytes(int B, int N, int k);
+int num_sms();
+int dense_scan_pass(int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl, int level,
+                    int k, const float* seed, uint2* lists, int* counts, int* err, cudaStream_t stream);
+
+// Merge of per-(query, split) candidate lists into the final sorted top-k.
+int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,
+                int64_t* out_ids, float* out_scores, float* out_kth, cudaStream_t stream);
+
+int merge_shard_lists(const int64_t* ids, const float* scores, int W, int B, int kin, int k, int64_t* out_ids,
+                      float* out_scores, void* ws, cudaStream_t stream);
+size_t merge_shard_ws_bytes(int W, int B, int kin);
+
+// Caller-owned events recorded around the dominant kernel of the next call on
+// this thread (profiling hook, see rb_set_profile_events).
+struct ProfileEvents {
+  cudaEvent_t start = nullptr, stop = nullptr;
+};
+ProfileEvents& profile_events();
+
+}  // namespace rb

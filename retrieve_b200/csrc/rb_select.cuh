@@ -1,0 +1,245 @@
+// Exact top-k selection building blocks shared by every scan kernel.
+//
+// The scan kernels keep, per (query, split), an append-only candidate list in
+// global memory: entries {score bits, item id} that passed the query's current
+// threshold. When a list nears its capacity, the owning warp compacts it in
+// place to its k best entries (radix select over the composite key) and raises
+// the query's threshold. A split scans its items in ascending id order, so an
+// item tied with the k-th entry on score always loses the tie: after an exact
+// compaction the threshold becomes strict (next float above the k-th score).
+//
+// The merge kernel then selects, per query, the k best entries over all of its
+// splits' lists (block-wide radix select), sorts them and writes the output.
+#pragma once
+
+#include "rb_common.cuh"
+
+namespace rb {
+
+// Warp-wide suffix-scan radix step over a 256-bin histogram in shared memory.
+// Each lane owns bins [8*lane, 8*lane+8). Finds the digit d whose bucket holds
+// the need-th largest element; returns d, the count strictly above it and the
+// bucket's own count (all warp-uniform).
+__device__ __forceinline__ void warp_find_digit(const uint32_t* hist, uint32_t need, uint32_t& digit,
+                                                uint32_t& above_digit, uint32_t& in_digit) {
+  const int lane = threadIdx.x & 31;
+  uint32_t b[8];
+  uint32_t total = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    b[j] = hist[8 * lane + j];
+    total += b[j];
+  }
+  uint32_t incl = total;  // inclusive suffix sum over lanes >= lane
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint32_t v = __shfl_down_sync(RB_FULL_MASK, incl, off);
+    if (lane + off < 32) incl += v;
+  }
+  const uint32_t above = incl - total;
+  const bool here = (above < need) && (need <= incl);
+  const uint32_t hb = __ballot_sync(RB_FULL_MASK, here);
+  const int src = hb ? (__ffs(hb) - 1) : 0;
+  uint32_t d = 0, a = 0, c = 0;
+  if (lane == src) {
+    uint32_t acc = above;
+#pragma unroll
+    for (int j = 7; j >= 0; --j) {
+      if (acc + b[j] >= need) {
+        d = 8 * lane + j;
+        a = acc;
+        c = b[j];
+        break;
+      }
+      acc += b[j];
+    }
+  }
+  digit = __shfl_sync(RB_FULL_MASK, d, src);
+  above_digit = __shfl_sync(RB_FULL_MASK, a, src);
+  in_digit = __shfl_sync(RB_FULL_MASK, c, src);
+}
+
+// Warp radix select over register-resident keys (EPL per lane, key 0 = empty
+// slot, never selected because callers ask for need <= number of valid keys).
+// Returns the cut: exactly `k` keys are >= cut.
+template <int EPL>
+__device__ __forceinline__ uint64_t warp_radix_cut(const uint64_t (&key)[EPL], const bool (&valid)[EPL], int k,
+                                                   uint32_t* hist) {
+  const int lane = threadIdx.x & 31;
+  uint64_t prefix = 0, mask = 0;
+  uint32_t need = static_cast<uint32_t>(k);
+  for (int shift = 56; shift >= 0; shift -= 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hist[8 * lane + j] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      if (valid[e] && (key[e] & mask) == prefix) atomicAdd(&hist[(key[e] >> shift) & 0xffu], 1u);
+    }
+    __syncwarp();
+    uint32_t digit, above, in_digit;
+    warp_find_digit(hist, need, digit, above, in_digit);
+    __syncwarp();
+    prefix |= static_cast<uint64_t>(digit) << shift;
+    mask |= static_cast<uint64_t>(0xffu) << shift;
+    need -= above;
+    if (in_digit == need) break;  // every key with this prefix is in: cut is exact
+  }
+  return prefix;
+}
+
+__device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    uint64_t o = __shfl_xor_sync(RB_FULL_MASK, v, off);
+    v = o < v ? o : v;
+  }
+  return v;
+}
+
+// Compacts, one lane at a time, the candidate list of every lane with `need`
+// set: keeps its k best entries (in list order) and raises its threshold to
+// just above the k-th score. `list`/`count`/`thresh` are the calling lane's own
+// state. Requires count <= 32 * EPL and count > k for the lanes that need it.
+// All 32 lanes must call it (warp-collective).
+template <int EPL>
+__device__ __noinline__ void warp_compact_lists(uint2* list, int& count, float& thresh, bool need, int k,
+                                                uint32_t* hist) {
+  const int lane = threadIdx.x & 31;
+  uint32_t pending = __ballot_sync(RB_FULL_MASK, need);
+  while (pending) {
+    const int src = __ffs(pending) - 1;
+    pending &= pending - 1;
+    uint2* l = reinterpret_cast<uint2*>(
+        __shfl_sync(RB_FULL_MASK, reinterpret_cast<unsigned long long>(list), src));
+    const int cnt = __shfl_sync(RB_FULL_MASK, count, src);
+    uint64_t key[EPL];
+    bool valid[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int i = e * 32 + lane;
+      valid[e] = i < cnt;
+      key[e] = 0;
+      if (valid[e]) {
+        const uint2 v = l[i];
+        key[e] = make_key(v.x, v.y);
+      }
+    }
+    const uint64_t cut = warp_radix_cut<EPL>(key, valid, k, hist);
+    // Stable in-place compaction: an entry moves to a slot <= its own.
+    int out = 0;
+    uint64_t kmin = ~0ull;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const bool keep = valid[e] && key[e] >= cut;
+      const uint32_t b = __ballot_sync(RB_FULL_MASK, keep);
+      if (keep) {
+        l[out + __popc(b & lanemask_lt())] = key_to_entry(key[e]);
+        kmin = key[e] < kmin ? key[e] : kmin;
+      }
+      out += __popc(b);
+    }
+    kmin = warp_min_u64(kmin);
+    if (lane == src) {
+      count = out;
+      const uint32_t hi = static_cast<uint32_t>(kmin >> 32);
+      // strict: a later item (higher id) tied with the k-th score loses the tie
+      const float t = (hi == 0xffffffffu) ? ord2f(hi) : ord2f(hi + 1u);
+      thresh = fmaxf(thresh, t);
+    }
+    __syncwarp();
+  }
+}
+
+// Appends the passing entries of a 32-item chunk to the calling lane's list.
+// Scores s[j] for items id0 + j; only ids < n_valid count.
+__device__ __forceinline__ void append_chunk(uint2* list, int& count, float thresh, const float (&s)[32],
+                                             uint32_t id0, uint32_t n_valid) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (s[j] >= thresh && id0 + j < n_valid) {
+      list[count] = make_uint2(__float_as_uint(s[j]), id0 + j);
+      ++count;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Block-level (256 threads) radix select over entries in global memory.
+// ---------------------------------------------------------------------------
+constexpr int kMergeThreads = 256;
+
+struct MergeSmem {
+  uint32_t hist[256];
+  uint32_t warp_tot[kMergeThreads / 32];
+  uint32_t digit, above, in_digit;
+  uint32_t n_out;
+};
+
+// Finds, for the 256-bin histogram in smem (one bin per thread), the digit
+// holding the need-th largest element.
+__device__ __forceinline__ void block_find_digit(MergeSmem& sm, uint32_t need) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // bin index descending order: thread tid owns bin (255 - tid), so an inclusive
+  // prefix over tid is a suffix sum over bins.
+  const uint32_t mine = sm.hist[255 - tid];
+  uint32_t incl = mine;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint32_t v = __shfl_up_sync(RB_FULL_MASK, incl, off);
+    if (lane >= off) incl += v;
+  }
+  if (lane == 31) sm.warp_tot[warp] = incl;
+  __syncthreads();
+  uint32_t base = 0;
+  for (int w = 0; w < warp; ++w) base += sm.warp_tot[w];
+  incl += base;
+  const uint32_t excl = incl - mine;
+  if (excl < need && need <= incl) {
+    sm.digit = 255 - tid;
+    sm.above = excl;
+    sm.in_digit = mine;
+  }
+  __syncthreads();
+}
+
+// Loads entry i of the concatenated lists. Lists are `n_lists` runs of
+// `stride` entries; run r holds counts[r] valid entries.
+struct ListSet {
+  const uint2* base;
+  const int* counts;
+  int n_lists;
+  int stride;
+};
+
+// Returns the cut key: exactly min(k, total) entries have key >= cut (cut = 0
+// when total <= k, i.e. keep everything).
+__device__ __forceinline__ uint64_t block_radix_cut(const ListSet& ls, int total, int k, MergeSmem& sm) {
+  if (total <= k) return 0;
+  uint64_t prefix = 0, mask = 0;
+  uint32_t need = static_cast<uint32_t>(k);
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    sm.hist[threadIdx.x] = 0;
+    __syncthreads();
+    for (int r = 0; r < ls.n_lists; ++r) {
+      const int c = ls.counts[r];
+      const uint2* l = ls.base + static_cast<size_t>(r) * ls.stride;
+      for (int i = threadIdx.x; i < c; i += kMergeThreads) {
+        const uint2 v = l[i];
+        const uint64_t key = make_key(v.x, v.y);
+        if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 0xffu], 1u);
+      }
+    }
+    __syncthreads();
+    block_find_digit(sm, need);
+    prefix |= static_cast<uint64_t>(sm.digit) << shift;
+    mask |= static_cast<uint64_t>(0xffu) << shift;
+    need -= sm.above;
+    const bool done = (sm.in_digit == need);
+    __syncthreads();
+    if (done) break;
+  }
+  return prefix;
+}
+
+}  // namespace rb

@@ -1,0 +1,93 @@
+"""Row-sharded search over several GPUs (one process per GPU).
+
+The corpus is split row-wise into contiguous shards; rank ``r`` holds rows
+``[offset_r, offset_r + n_r)``. A query batch (replicated on every rank) is
+scored against the local shard with the fused kernel, giving each rank its
+local top-k with global ids; one NCCL all-gather brings the ``W`` local lists to
+every rank and ``rb_merge_topk`` reduces them to the global top-k with the same
+ordering (score descending, ties to the lower id). Exact for any ``W``: the
+global top-k is contained in the union of the local top-k lists, and a shard's
+scores do not depend on which shard scores it.
+
+The reference is single-GPU (its harness merges chunked top-k lists the same
+way on one device, evaluation/bench/oracle.py:83-92); this module is the
+multi-GPU extension of ``PostfilterKNN`` (retrieve/src/retrieve/modules/knn.py:23-76).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from retrieve_b200 import _lib, ops
+
+
+def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
+    """``[start, end)`` rows of shard ``rank`` of an ``n``-row corpus."""
+    return (n * rank) // world, (n * (rank + 1)) // world
+
+
+def merge_topk(ids: Tensor, scores: Tensor, k: int) -> tuple[Tensor, Tensor]:
+    """``[W, B, kin]`` per-shard results → global ``[B, k]`` (C-ABI ``rb_merge_topk``)."""
+    if ids.dim() != 3 or ids.shape != scores.shape:
+        raise ValueError("ids and scores must both be [W, B, kin]")
+    ids = ids.contiguous()
+    scores = scores.to(torch.float32).contiguous()
+    w, b, kin = ids.shape
+    dev = ids.device
+    out_i = torch.empty((b, k), dtype=torch.int64, device=dev)
+    out_s = torch.empty((b, k), dtype=torch.float32, device=dev)
+    lib = _lib.lib()
+    nb = ctypes.c_size_t(0)
+    _lib.check(lib.rb_merge_topk_workspace_size(w, b, kin, ctypes.byref(nb)), "merge_topk")
+    ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
+    rc = lib.rb_merge_topk(
+        ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(scores.data_ptr()), w, b, kin, k,
+        ctypes.c_void_p(out_i.data_ptr()), ctypes.c_void_p(out_s.data_ptr()),
+        ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+        ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream),
+    )
+    _lib.check(rc, "merge_topk")
+    return out_i, out_s
+
+
+class ShardedDenseTopK:
+    """The local shard of a row-sharded dense index plus the exchange step.
+
+    ``item_shard`` is this rank's ``[n_r, D]`` fp16/bf16 rows (contiguous) and
+    ``id_offset`` their first global id. ``search(query)`` returns the global
+    ``(ids [B, k], scores [B, k])`` on every rank."""
+
+    def __init__(self, item_shard: Tensor, id_offset: int, k: int, group=None) -> None:
+        ops.check_contiguous(item_shard=item_shard)
+        self.items = item_shard
+        self.id_offset = int(id_offset)
+        self.k = int(k)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+
+    def local(self, query: Tensor) -> tuple[Tensor, Tensor]:
+        return ops.dense_topk_sharded(query, self.items, self.k, self.id_offset)
+
+    def search(self, query: Tensor) -> tuple[Tensor, Tensor]:
+        ids, scores = self.local(query)
+        if self.world == 1:
+            return ids, scores
+        b = ids.shape[0]
+        all_i = torch.empty((self.world, b, self.k), dtype=ids.dtype, device=ids.device)
+        all_s = torch.empty((self.world, b, self.k), dtype=scores.dtype, device=scores.device)
+        dist.all_gather_into_tensor(all_i, ids, group=self.group)
+        dist.all_gather_into_tensor(all_s, scores, group=self.group)
+        return merge_topk(all_i, all_s, self.k)
+
+    def launches_per_search(self, b: int) -> int:
+        lib = _lib.lib()
+        n = ctypes.c_int(0)
+        _lib.check(
+            lib.rb_dense_topk_launches(b, self.items.shape[0], self.items.shape[1], 1, self.k, ctypes.byref(n)),
+            "launches",
+        )
+        return n.value + (2 if self.world > 1 else 0)
