@@ -79,18 +79,21 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
 
   const int elem = (dtype == RB_BF16) ? 1 : 0;
   ProfileEvents& pe = profile_events();
-  for (int lv = 0; lv < pl.n_levels; ++lv) {
-    const float* seed = (lv == 0) ? nullptr : thresh + static_cast<size_t>((lv - 1) & 1) * B;
-    const bool last = (lv == pl.n_levels - 1);
-    if (last && pe.start) cudaEventRecord(pe.start, stream);
-    int rc = dense_scan_pass(elem, queries, items, B, N, D, pl, lv, k, seed, lists, counts, err, stream);
+  const float* seed = nullptr;
+  if (pl.sample_stride > 0) {
+    float* chunk_max = reinterpret_cast<float*>(lists);  // dead before the full pass writes lists
+    int rc = dense_scan_pass(1, elem, queries, items, B, N, D, pl, k, nullptr, lists, counts, chunk_max, err, stream);
     if (rc != RB_OK) return rc;
-    if (last && pe.stop) cudaEventRecord(pe.stop, stream);
-    rc = merge_lists(lists, counts, B, pl.n_splits, pl.cap, k, id_offset, last ? out_ids : nullptr,
-                     last ? out_scores : nullptr, last ? nullptr : thresh + static_cast<size_t>(lv & 1) * B, stream);
+    const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
+    rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, k, thresh, stream);
     if (rc != RB_OK) return rc;
+    seed = thresh;
   }
-  return RB_OK;
+  if (pe.start) cudaEventRecord(pe.start, stream);
+  int rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, lists, counts, nullptr, err, stream);
+  if (rc != RB_OK) return rc;
+  if (pe.stop) cudaEventRecord(pe.stop, stream);
+  return merge_lists(lists, counts, B, pl.n_splits, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
 }
 
 int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launches) {
@@ -107,7 +110,7 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
   }
   DensePlan pl;
   dense_plan(B, N, k, pl);
-  *n_launches = 2 * pl.n_levels;
+  *n_launches = (pl.sample_stride > 0) ? 4 : 2;
   return RB_OK;
 }
 

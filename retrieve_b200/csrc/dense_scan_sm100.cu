@@ -36,6 +36,7 @@ namespace rb {
 
 constexpr int kTileItems = 128;  // N of one MMA = items per pipeline stage
 constexpr int kQTile = 128;      // M of one MMA = queries per group
+constexpr int kSampleStride = 16;  // sampling pass: every 16th tile
 
 struct alignas(64) DenseScanParams {
   CUtensorMap tmap_q;
@@ -44,6 +45,8 @@ struct alignas(64) DenseScanParams {
   uint2* lists;       // [B, n_splits, cap]
   int* counts;        // [B, n_splits]
   int* err;           // device error word
+  float* chunk_max;   // MODE 1: [B, chunk_stride] max score of every 32-item chunk
+  int chunk_stride;
   int B, N;
   int n_qsg, n_splits;
   int tile_stride, tile_offset, pass_tiles;
@@ -67,7 +70,7 @@ __device__ __forceinline__ void split_range(int split, int n_splits, int pass_ti
   hi = static_cast<int>((static_cast<int64_t>(split + 1) * pass_tiles) / n_splits);
 }
 
-template <int ELEM, int KB, int NG, int STAGES, int EPL>
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL>
 __global__ void __launch_bounds__(64 + 128 * NG, 1)
     dense_scan_kernel(const __grid_constant__ DenseScanParams p) {
   using L = DenseSmemLayout<KB, NG, STAGES>;
@@ -255,6 +258,12 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
       split_range(split, p.n_splits, p.pass_tiles, lo, hi);
       bool ok = true;
       for (int pt = lo; pt < hi; ++pt) {
+        if constexpr (MODE == 0) {
+          // Room for a whole tile of appends; compacting here keeps no scores live
+          // across the (non-inlined) compaction.
+          const bool need = valid_q && (count > p.cap - kTileItems);
+          if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        }
         if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
           if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
           *abort_flag = 1;
@@ -264,38 +273,51 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_after();
         const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
-#pragma unroll 1
-        for (int ch = 0; ch < kTileItems / 32; ++ch) {
-          uint32_t r[32];
-          __syncwarp();
-          tmem_ld_32x32(col0 + ch * 32, r);
-          tmem_wait_ld();
-          float s[32];
+        // The whole 128-column row in one go, then the accumulator goes back to
+        // the MMA warp before any filtering work.
+        uint32_t r[4][32];
+        __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(r[j]);
-          float m0 = fmaxf(s[0], s[1]), m1 = fmaxf(s[2], s[3]);
-#pragma unroll
-          for (int j = 4; j < 32; j += 4) {
-            m0 = fmaxf(m0, fmaxf(s[j], s[j + 1]));
-            m1 = fmaxf(m1, fmaxf(s[j + 2], s[j + 3]));
-          }
-          const bool pass = valid_q && fmaxf(m0, m1) >= thresh;
-          if (__any_sync(RB_FULL_MASK, pass)) {
-            const bool need = pass && (count > p.cap - 32);
-            warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
-            if (pass) append_chunk(list, count, thresh, s, row0 + ch * 32, static_cast<uint32_t>(p.N));
-          }
-        }
+        for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r[ch]);
+        tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        if (row0 + kTileItems > static_cast<uint32_t>(p.N)) {
+          // last, partial tile: rows past N were zero-filled by TMA
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch)
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (row0 + ch * 32 + j >= static_cast<uint32_t>(p.N)) r[ch][j] = 0xff800000u;  // -inf
+        }
+        float cmax[4];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) cmax[ch] = max32(r[ch]);
+        if constexpr (MODE == 1) {
+          // sampling pass: the max of every 32-item chunk, nothing else
+          if (valid_q)
+            *reinterpret_cast<float4*>(p.chunk_max + static_cast<size_t>(q) * p.chunk_stride + pt * 4) =
+                make_float4(cmax[0], cmax[1], cmax[2], cmax[3]);
+        } else {
+          const float tmax = fmaxf(fmaxf(cmax[0], cmax[1]), fmaxf(cmax[2], cmax[3]));
+          if (__any_sync(RB_FULL_MASK, valid_q && tmax >= thresh)) {
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+              const bool pass = valid_q && cmax[ch] >= thresh;
+              if (pass) append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32, static_cast<uint32_t>(p.N));
+            }
+          }
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
       if (!ok) break;
-      const bool need = valid_q && count > p.k;
-      warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
-      if (valid_q) p.counts[static_cast<size_t>(q) * p.n_splits + split] = count;
+      if constexpr (MODE == 0) {
+        const bool need = valid_q && count > p.k;
+        warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        if (valid_q) p.counts[static_cast<size_t>(q) * p.n_splits + split] = count;
+      }
     }
   }
 
@@ -346,10 +368,10 @@ static bool make_tmap(CUtensorMap* map, const void* base, int elem, uint64_t row
   return r == CUDA_SUCCESS;
 }
 
-template <int ELEM, int KB, int NG, int STAGES, int EPL>
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL>
 static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaStream_t stream) {
   using L = DenseSmemLayout<KB, NG, STAGES>;
-  auto kern = dense_scan_kernel<ELEM, KB, NG, STAGES, EPL>;
+  auto kern = dense_scan_kernel<MODE, ELEM, KB, NG, STAGES, EPL>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
   kern<<<grid, 64 + 128 * NG, L::kTotal, stream>>>(prm);
@@ -366,8 +388,9 @@ namespace rb {
 int dense_ng(int B) { return B <= kQTile ? 1 : 2; }
 
 int list_cap(int k) {
-  // room for k survivors + one 32-item chunk + slack; multiple of 32; <= 512
-  int cap = ((2 * k + 64) + 31) / 32 * 32;
+  // room for k survivors + one 128-item tile of appends + slack; multiple of 32;
+  // <= 512 (the register-resident compaction holds 16 entries per lane)
+  int cap = ((k + 256) + 31) / 32 * 32;
   return std::min(cap, 512);
 }
 
@@ -389,19 +412,18 @@ void dense_plan(int B, int N, int k, DensePlan& pl) {
   pl.n_splits = std::max(1, sms / std::max(1, pl.n_qsg));
   pl.cap = list_cap(k);
   pl.tiles = (N + kTileItems - 1) / kTileItems;
-  // Sampled threshold levels: level 0 keeps about n_splits * cap / 2 items so
-  // no list overflows; level 1 about 16x more; the last level scans all tiles.
-  pl.n_levels = 0;
-  const int64_t target0 = static_cast<int64_t>(pl.n_splits) * pl.cap / 2;
-  const int64_t tiles0 = std::max<int64_t>(1, target0 / kTileItems);
-  if (pl.tiles >= 64 * tiles0 && pl.tiles * static_cast<int64_t>(kTileItems) >= 8 * static_cast<int64_t>(k)) {
-    int s1 = 16;
-    int s0 = static_cast<int>(pl.tiles / tiles0);
-    s0 = std::max(s1, s0 / s1 * s1);
-    pl.level_stride[pl.n_levels++] = s0;
-    pl.level_stride[pl.n_levels++] = s1;
-  }
-  pl.level_stride[pl.n_levels++] = 1;
+  // Optional sampling pass over every kSampleStride-th tile: it records the
+  // max of each 32-item chunk; the k-th largest chunk max is a lower bound on
+  // the k-th best score of the corpus (k distinct items reach it) and seeds the
+  // full pass. Taken when the sample holds at least 4k chunks.
+  pl.sample_stride = 0;
+  const int64_t sample_tiles = (pl.tiles + kSampleStride - 1) / kSampleStride;
+  if (sample_tiles * 4 >= 4 * static_cast<int64_t>(k)) pl.sample_stride = kSampleStride;
+}
+
+size_t dense_chunk_stride(const DensePlan& pl) {
+  if (pl.sample_stride == 0) return 0;
+  return static_cast<size_t>((pl.tiles + pl.sample_stride - 1) / pl.sample_stride) * 4;
 }
 
 size_t dense_workspace_bytes(int B, int N, int k) {
@@ -410,11 +432,14 @@ size_t dense_workspace_bytes(int B, int N, int k) {
   size_t lists = static_cast<size_t>(B) * pl.n_splits * pl.cap * sizeof(uint2);
   size_t counts = static_cast<size_t>(B) * pl.n_splits * sizeof(int);
   size_t th = 2 * static_cast<size_t>(B) * sizeof(float);
-  return align_up(lists, 256) + align_up(counts, 256) + align_up(th, 256) + 256;
+  size_t cm = static_cast<size_t>(B) * dense_chunk_stride(pl) * sizeof(float);
+  // the chunk maxima are dead once the seed is known: they share the list space
+  return align_up(std::max(lists, cm), 256) + align_up(counts, 256) + align_up(th, 256) + 256;
 }
 
-int dense_scan_pass(int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl, int level,
-                    int k, const float* seed, uint2* lists, int* counts, int* err, cudaStream_t stream) {
+int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
+                    int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
+                    cudaStream_t stream) {
   DenseScanParams prm;
   std::memset(&prm, 0, sizeof(prm));
   const int eb = (elem == 2) ? 1 : 2;
@@ -424,11 +449,13 @@ int dense_scan_pass(int elem, const void* q, const void* x, int B, int N, int D,
     set_last_error("cuTensorMapEncodeTiled failed (alignment or driver entry point)");
     return RB_ERR_CUDA;
   }
-  const int stride = pl.level_stride[level];
+  const int stride = (mode == 1) ? pl.sample_stride : 1;
   prm.seed = seed;
   prm.lists = lists;
   prm.counts = counts;
   prm.err = err;
+  prm.chunk_max = chunk_max;
+  prm.chunk_stride = static_cast<int>(dense_chunk_stride(pl));
   prm.B = B;
   prm.N = N;
   prm.n_qsg = pl.n_qsg;
@@ -442,13 +469,16 @@ int dense_scan_pass(int elem, const void* q, const void* x, int B, int N, int D,
   const int grid = std::min(n_tasks, num_sms());
   cudaError_t e = cudaSuccess;
   const int kb = row_bytes / 128;
-#define RB_DISPATCH(ELEM, KB, NG, ST)                                                    \
-  if (elem == ELEM && kb == KB && pl.ng == NG) {                                          \
-    e = (pl.cap <= 256) ? launch_dense_scan<ELEM, KB, NG, ST, 8>(prm, grid, stream)       \
-                        : launch_dense_scan<ELEM, KB, NG, ST, 16>(prm, grid, stream);     \
-    handled = true;                                                                       \
-  }
   bool handled = false;
+#define RB_DISPATCH(ELEM, KB, NG, ST)                                                         \
+  if (elem == ELEM && kb == KB && pl.ng == NG) {                                               \
+    if (mode == 1)                                                                             \
+      e = launch_dense_scan<1, ELEM, KB, NG, ST, 8>(prm, grid, stream);                        \
+    else                                                                                       \
+      e = (pl.cap <= 256) ? launch_dense_scan<0, ELEM, KB, NG, ST, 8>(prm, grid, stream)       \
+                          : launch_dense_scan<0, ELEM, KB, NG, ST, 16>(prm, grid, stream);     \
+    handled = true;                                                                            \
+  }
   RB_DISPATCH(0, 1, 1, 8)
   RB_DISPATCH(0, 1, 2, 8)
   RB_DISPATCH(0, 2, 1, 4)

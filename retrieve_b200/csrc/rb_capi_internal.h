@@ -21,15 +21,20 @@ struct DensePlan {
   int n_splits;  // item splits per super-group
   int cap;       // candidate-list capacity per (query, split)
   int tiles;     // 128-item tiles in the corpus
-  int n_levels;  // scan passes; the last one covers every tile
-  int level_stride[4];
+  int sample_stride;  // 0: no sampling pass; else the tile stride of the sample
 };
 
 void dense_plan(int B, int N, int k, DensePlan& pl);
 size_t dense_workspace_bytes(int B, int N, int k);
 int num_sms();
-int dense_scan_pass(int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl, int level,
-                    int k, const float* seed, uint2* lists, int* counts, int* err, cudaStream_t stream);
+size_t dense_chunk_stride(const DensePlan& pl);
+// mode 0: candidate pass over every tile; mode 1: chunk-max sampling pass.
+int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
+                    int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
+                    cudaStream_t stream);
+// Per row of vals [B, n] (row stride `stride`): a lower bound on the k-th
+// largest value (exact to 22 leading key bits), -inf when n < k.
+int row_kth_lower_bound(const float* vals, int B, int n, int stride, int k, float* out, cudaStream_t stream);
 
 // Merge of per-(query, split) candidate lists into the final sorted top-k.
 int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,

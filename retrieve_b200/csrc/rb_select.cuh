@@ -164,6 +164,31 @@ __device__ __forceinline__ void append_chunk(uint2* list, int& count, float thre
   }
 }
 
+// Same, with the scores still as raw fp32 bit patterns (as read from TMEM).
+__device__ __forceinline__ void append_chunk_bits(uint2* list, int& count, float thresh, const uint32_t (&s)[32],
+                                                  uint32_t id0, uint32_t n_valid) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (__uint_as_float(s[j]) >= thresh && id0 + j < n_valid) {
+      list[count] = make_uint2(s[j], id0 + j);
+      ++count;
+    }
+  }
+}
+
+// Max of 32 fp32 values (raw bits) as a balanced tree (depth 5).
+__device__ __forceinline__ float max32(const uint32_t (&s)[32]) {
+  float a[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = fmaxf(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w; ++i) a[i] = fmaxf(a[2 * i], a[2 * i + 1]);
+  }
+  return a[0];
+}
+
 // ---------------------------------------------------------------------------
 // Block-level (256 threads) radix select over entries in global memory.
 // ---------------------------------------------------------------------------
