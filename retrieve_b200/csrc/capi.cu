@@ -70,9 +70,9 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
   dense_plan(B, N, k, pl);
   uint8_t* w = static_cast<uint8_t*>(workspace);
   uint2* lists = reinterpret_cast<uint2*>(w);
-  w += align_up(static_cast<size_t>(B) * pl.n_splits * pl.cap * sizeof(uint2), 256);
+  w += align_up(static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2), 256);
   int* counts = reinterpret_cast<int*>(w);
-  w += align_up(static_cast<size_t>(B) * pl.n_splits * sizeof(int), 256);
+  w += align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
   float* thresh = reinterpret_cast<float*>(w);
   int* err = ws_err_word(workspace, workspace_bytes);
   if (cudaMemsetAsync(err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
@@ -93,7 +93,7 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
   int rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, lists, counts, nullptr, err, stream);
   if (rc != RB_OK) return rc;
   if (pe.stop) cudaEventRecord(pe.stop, stream);
-  return merge_lists(lists, counts, B, pl.n_splits, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
+  return merge_lists(lists, counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
 }
 
 int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launches) {

@@ -6,7 +6,7 @@
 #include <cstddef>
 #include <cstdint>
 
-#include "../../include/retrieve_b200.h"
+#include "retrieve_b200.h"
 
 namespace rb {
 
@@ -16,9 +16,11 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // How one dense top-k call is cut into scan passes (see dense_scan_sm100.cu).
 struct DensePlan {
-  int ng;        // query groups of 128 per CTA (1 or 2)
-  int n_qsg;     // query super-groups of ng * 128
+  bool two_sm;   // CTA-pair kernel (M = 256 per group) or the 1-SM kernel (M = 128)
+  int ng;        // query groups per CTA (pair)
+  int n_qsg;     // query super-groups (ng groups each)
   int n_splits;  // item splits per super-group
+  int n_lists;   // candidate lists per query (splits x column halves)
   int cap;       // candidate-list capacity per (query, split)
   int tiles;     // 128-item tiles in the corpus
   int sample_stride;  // 0: no sampling pass; else the tile stride of the sample

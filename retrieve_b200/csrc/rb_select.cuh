@@ -165,15 +165,33 @@ __device__ __forceinline__ void append_chunk(uint2* list, int& count, float thre
 }
 
 // Same, with the scores still as raw fp32 bit patterns (as read from TMEM).
+// Padding slots hold NaN, which never passes.
 __device__ __forceinline__ void append_chunk_bits(uint2* list, int& count, float thresh, const uint32_t (&s)[32],
-                                                  uint32_t id0, uint32_t n_valid) {
+                                                  uint32_t id0) {
+  uint2* w = list + count;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    if (__uint_as_float(s[j]) >= thresh && id0 + j < n_valid) {
-      list[count] = make_uint2(s[j], id0 + j);
-      ++count;
+    if (__uint_as_float(s[j]) >= thresh) {
+      *w = make_uint2(s[j], id0 + j);
+      ++w;
     }
   }
+  count = static_cast<int>(w - list);
+}
+
+// AND over a chunk of the bit patterns of (s[j] - thresh): the sign bit of the
+// result is set iff every s[j] < thresh (NaN scores count as passing here and
+// are rejected by the exact test of the append).
+__device__ __forceinline__ uint32_t chunk_all_below(const uint32_t (&s)[32], float thresh) {
+  uint32_t d[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) d[j] = __float_as_uint(__uint_as_float(s[j]) - thresh);
+  uint32_t a[11];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) a[i] = d[3 * i] & d[3 * i + 1] & d[3 * i + 2];
+  a[10] = d[30] & d[31];
+  const uint32_t b0 = a[0] & a[1] & a[2], b1 = a[3] & a[4] & a[5], b2 = a[6] & a[7] & a[8];
+  return b0 & b1 & b2 & a[9] & a[10];
 }
 
 // Max of 32 fp32 values (raw bits) as a balanced tree (depth 5).

@@ -72,6 +72,24 @@ def test_dense_topk_ascending_scores_compaction_storm():
     assert_topk_exact(ids, scores, ref_ids, ref_scores)
 
 
+@pytest.mark.parametrize("b", [64, 200, 512])
+def test_dense_topk_compaction_storm_all_kernels(b):
+    """Rising scores for every query (1-SM kernel at B <= 128, the CTA-pair
+    kernel with one and two query groups above)."""
+    n, d, k = 30_000, 128, 100
+    g = torch.Generator().manual_seed(b)
+    q = torch.zeros(b, d)
+    q[:, 0] = 1.0
+    q[:, 1] = torch.randint(0, 3, (b,), generator=g).float()
+    x = torch.zeros(n, d)
+    x[:, 0] = (torch.arange(n) // 5).float()
+    x[:, 1] = torch.randint(0, 4, (n,), generator=g).float()
+    q, x = q.to(torch.bfloat16), x.to(torch.bfloat16)
+    ids, scores = _run(q, x, k)
+    ref_ids, ref_scores = oracle_dense_topk(q, x, k)
+    assert_topk_exact(ids, scores, ref_ids, ref_scores)
+
+
 def test_dense_topk_all_ties_lowest_ids_win():
     b, n, d, k = 200, 9000, 128, 50
     q = torch.ones(b, d, dtype=torch.bfloat16)
