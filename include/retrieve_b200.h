@@ -92,6 +92,23 @@ RB_API int rb_merge_topk(const int64_t* ids, const float* scores, int W, int B, 
 RB_API int rb_set_profile_events(void* start_event, void* stop_event);
 
 /*
+ * rb_dense_topk without a caller workspace, for callers that cannot allocate
+ * device memory on the call path (a host recording the search into a CUDA
+ * graph, where cudaMalloc is not allowed during capture, or a host whose device
+ * memory is fixed at start-up by another allocator). The scratch is one static
+ * device array of rb_dense_topk_noalloc_scratch_bytes() bytes (32 MiB) that
+ * every GPU loading this library keeps until the process exits; calls whose
+ * scratch need is larger return RB_ERR_WORKSPACE. The first call on a device
+ * looks the array's device address up (it may load the module): make it before
+ * any stream capture. All calls share the array: calls that overlap on the GPU
+ * race and must be serialised. Same arguments, results and limits as
+ * rb_dense_topk otherwise. This entry point has no counterpart in the reference.
+ */
+RB_API size_t rb_dense_topk_noalloc_scratch_bytes(void);
+RB_API int rb_dense_topk_noalloc(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
+                                 int64_t id_offset, int64_t* out_ids, float* out_scores, void* stream);
+
+/*
  * Reads (synchronously) the device error word a scan kernel leaves in
  * `workspace` (0 = none; non-zero = a bounded wait ran out). Test / debug aid.
  */

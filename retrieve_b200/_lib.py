@@ -44,6 +44,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_merge_topk": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),
     "rb_set_profile_events": (_c_int, [_vp, _vp]),
     "rb_workspace_device_error": (_c_int, [_vp, _c_size, ctypes.POINTER(_c_int)]),
+    "rb_dense_topk_noalloc_scratch_bytes": (_c_size, []),
+    "rb_dense_topk_noalloc": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp]),
 }
 
 _LIB: ctypes.CDLL | None = None
