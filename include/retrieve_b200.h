@@ -69,6 +69,74 @@ RB_API int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, s
 RB_API int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int64_t id_offset,
                   int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Exact clause filter over items [N, C, A] int64 (-1 pad), reverse flags
+ * [C] uint8, queries [B, C] int64 (-1 = inactive clause).
+ * scores == NULL: out is [B, N] uint8 (bool) -> retrieve::clause_mask
+ *   (retrieve/src/retrieve/ops/triton/clause_mask.py:270-283).
+ * scores != NULL ([B, N] fp32): out is [B, N] fp32 with failing items at -inf
+ *   -> retrieve::clause_mask_scores (clause_mask.py:286-303).
+ * B <= 65535.
+ */
+RB_API int rb_clause_mask(const int64_t* item_attrs, int N, int C, int A, const uint8_t* is_reverse,
+                          const int64_t* query_attrs, int B, const float* scores, void* out, void* stream);
+
+/*
+ * Clause filter + stream compaction -> retrieve::clause_compact
+ * (retrieve/src/retrieve/ops/triton/clause_compact.py:174-196): out_ids [B, N]
+ * int64 holds each row's passing ids in ascending order on [0, out_counts[b]),
+ * the tail is left unwritten; out_counts [B] int64. B <= 65535.
+ */
+RB_API int rb_clause_compact_workspace_size(int B, int N, size_t* bytes);
+RB_API int rb_clause_compact(const int64_t* item_attrs, int N, int C, int A, const uint8_t* is_reverse,
+                             const int64_t* query_attrs, int B, int64_t* out_ids, int64_t* out_counts,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Single fp16 query [1, D] against the fp16 table items_t [D, N] -> out [N]
+ * fp32, one fp32 FMA per k in order k = 0 .. D-1 -> retrieve::gemv_scores
+ * (retrieve/src/retrieve/ops/triton/gemv_scores.py:19-43).
+ */
+RB_API int rb_gemv_scores(const void* query, const void* items_t, int D, int N, float* out, void* stream);
+
+/*
+ * Top-k over per-query candidates positive_indices [B, P] int64 bounded by
+ * counts [B] int64.
+ * kind 0 -> retrieve::fused_masked_knn_topk
+ *   (retrieve/src/retrieve/ops/triton/fused_masked_knn_topk.py:289-310):
+ *   fp32 dot of query [B, D] and item_embs [N, D] (each fp16 or fp32),
+ *   output [B, k], non-finite winners id -1; 1 <= k <= 224.
+ * kind 1 -> retrieve::oporp_1bit_match_topk_indirect
+ *   (retrieve/src/retrieve/ops/triton/oporp_1bit_match_topk.py:276-292):
+ *   score 64*W - 2*popcount(q ^ x) over int64 words (D = W), output
+ *   [B, min(k, P)]; min(k, P) <= 224.
+ * Ties go to the lower candidate index. Ids outside [0, N) are never scored.
+ */
+RB_API int rb_candidate_topk_workspace_size(int B, int P, size_t* bytes);
+RB_API int rb_candidate_topk(int kind, const void* query, int query_dtype, const void* items, int item_dtype, int N,
+                             int D, const int64_t* positive_indices, int P, const int64_t* counts, int B, int k,
+                             int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/*
+ * Full-scan 1-bit Hamming top-k -> retrieve::oporp_1bit_match_topk_full
+ * (retrieve/src/retrieve/ops/triton/oporp_1bit_match_topk.py:261-273):
+ * query_bits [B, W], item_bits [N, W] int64, score 64*W - 2*popcount as fp32,
+ * output [B, k] (ids = item rows), ties to the lower row. W even, <= 16;
+ * k <= 384.
+ */
+RB_API int rb_hamming_topk_workspace_size(int B, int N, int W, int k, size_t* bytes);
+RB_API int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, int B, int N, int W, int k,
+                           int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/*
+ * Per-row symmetric int8 quantization of x [B, D] fp32 -> codes [B, D] int8,
+ * scales [B] fp32 (retrieve/src/retrieve/indexing/quantize.py:9-18
+ * `quantize_int8`, bit for bit).
+ */
+RB_API int rb_quantize_int8(const float* x, int B, int D, int8_t* codes, float* scales, void* stream);
+
 /* Number of kernel launches one rb_dense_topk call with these sizes makes. */
 RB_API int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launches);
 

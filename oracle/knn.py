@@ -1,0 +1,116 @@
+"""Candidate-path, 1-bit and quantization oracles (test infrastructure).
+
+* ``fused_masked_knn_topk``: ops/reference/fused_masked_knn_topk.py:9-29 —
+  fp32 dots of the candidates ``positive_indices[b, :counts[b]]``, ``-inf``
+  past counts, top-k, ids through ``positive_indices``, non-finite winners -1;
+  ties toward the lower candidate index.
+* ``oporp_full`` / ``oporp_indirect``: ops/reference/oporp_1bit_match_topk.py:9-41
+  — ``64*W - 2*popcount(q ^ x)``; the indirect form returns ``min(k, P)``
+  columns.
+* ``gemv_scores``: ops/triton/gemv_scores.py:19-28 via the C restatement.
+* ``quantize_int8``: indexing/quantize.py:9-18.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from oracle.dense import as_f32
+from oracle.select import topk_strict
+
+
+def fused_masked_knn_topk(query, items, positive_indices, counts, k):
+    q = as_f32(query)
+    x = as_f32(items)
+    pos = np.asarray(positive_indices, dtype=np.int64)
+    cnt = np.asarray(counts, dtype=np.int64)
+    b, p = pos.shape
+    scores = np.full((b, p), -np.inf, dtype=np.float32)
+    for bi in range(b):
+        c = int(min(max(cnt[bi], 0), p))
+        ids = pos[bi, :c]
+        ok = (ids >= 0) & (ids < x.shape[0])
+        s = np.full(c, np.nan, dtype=np.float32)
+        if ok.any():
+            s[ok] = (x[ids[ok]].astype(np.float64) @ q[bi].astype(np.float64)).astype(np.float32)
+        scores[bi, :c] = np.where(ok, s, -np.inf)
+    lane_ids, top = topk_strict(scores, k)
+    out = np.where(lane_ids >= 0, np.take_along_axis(pos, np.maximum(lane_ids, 0), axis=1), -1)
+    out = np.where(np.isfinite(top), out, -1)
+    return out, top
+
+
+def _hamming(qbits: np.ndarray, xbits: np.ndarray) -> np.ndarray:
+    """[B, W] x [M, W] uint64 → [B, M] popcount of xor."""
+    qb = np.asarray(qbits).view(np.uint64)
+    xb = np.asarray(xbits).view(np.uint64)
+    return np.bitwise_count(qb[:, None, :] ^ xb[None, :, :]).sum(axis=-1).astype(np.int64)
+
+
+def oporp_full(query_bits, item_bits, k, chunk=1 << 16):
+    qb = np.ascontiguousarray(np.asarray(query_bits, dtype=np.int64))
+    xb = np.ascontiguousarray(np.asarray(item_bits, dtype=np.int64))
+    w = qb.shape[1]
+    best_i = np.zeros((qb.shape[0], 0), dtype=np.int64)
+    best_s = np.zeros((qb.shape[0], 0), dtype=np.float32)
+    for lo in range(0, xb.shape[0], chunk):
+        h = _hamming(qb, xb[lo : lo + chunk])
+        s = (64 * w - 2 * h).astype(np.float32)
+        ci, cs = topk_strict(s, k, pad_to_k=False)
+        all_i = np.concatenate([best_i, ci + lo], axis=1)
+        all_s = np.concatenate([best_s, cs], axis=1)
+        best_i, best_s = topk_strict(all_s, k, ids=all_i, pad_to_k=False)
+    return best_i, best_s
+
+
+def oporp_indirect(query_bits, item_bits, k, positive_indices, counts):
+    qb = np.asarray(query_bits, dtype=np.int64)
+    xb = np.asarray(item_bits, dtype=np.int64)
+    pos = np.asarray(positive_indices, dtype=np.int64)
+    cnt = np.asarray(counts, dtype=np.int64)
+    b, p = pos.shape
+    w = qb.shape[1]
+    scores = np.full((b, p), -np.inf, dtype=np.float32)
+    for bi in range(b):
+        c = int(min(max(cnt[bi], 0), p))
+        ids = pos[bi, :c]
+        h = _hamming(qb[bi : bi + 1], xb[ids])[0]
+        scores[bi, :c] = (64 * w - 2 * h).astype(np.float32)
+    lane_ids, top = topk_strict(scores, k, pad_to_k=False)
+    out = np.where(lane_ids >= 0, np.take_along_axis(pos, np.maximum(lane_ids, 0), axis=1), -1)
+    out = np.where(np.isfinite(top), out, -1)
+    return out, top
+
+
+_CLIB = None
+
+
+def _clib():
+    global _CLIB
+    if _CLIB is None:
+        from oracle.build_c import build
+
+        _CLIB = ctypes.CDLL(str(build()))
+        _CLIB.oracle_gemv.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_void_p]
+    return _CLIB
+
+
+def gemv_scores(query_f16, items_t_f16) -> np.ndarray:
+    q = np.ascontiguousarray(np.asarray(query_f16, dtype=np.float16).reshape(-1))
+    et = np.ascontiguousarray(np.asarray(items_t_f16, dtype=np.float16))
+    d, n = et.shape
+    out = np.empty(n, dtype=np.float32)
+    _clib().oracle_gemv(q.ctypes.data, et.ctypes.data, d, n, out.ctypes.data)
+    return out.reshape(1, n)
+
+
+def quantize_int8(x):
+    x = np.asarray(x, dtype=np.float32)
+    abs_max = np.maximum(np.abs(x).max(axis=1, keepdims=True), np.float32(1e-8)).astype(np.float32)
+    scales = (abs_max / np.float32(127.0)).astype(np.float32)[:, 0]
+    ratio = (x.astype(np.float64) / abs_max.astype(np.float64)).astype(np.float32)
+    codes = np.clip(np.rint(ratio * np.float32(127.0)), -128, 127).astype(np.int8)
+    return codes, scales

@@ -44,6 +44,21 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_merge_topk": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),
     "rb_set_profile_events": (_c_int, [_vp, _vp]),
     "rb_workspace_device_error": (_c_int, [_vp, _c_size, ctypes.POINTER(_c_int)]),
+    "rb_clause_mask": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp]),
+    "rb_clause_compact_workspace_size": (_c_int, [_c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "rb_clause_compact": (
+        _c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp, _c_size, _vp]
+    ),
+    "rb_gemv_scores": (_c_int, [_vp, _vp, _c_int, _c_int, _vp, _vp]),
+    "rb_candidate_topk_workspace_size": (_c_int, [_c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "rb_candidate_topk": (
+        _c_int,
+        [_c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp,
+         _c_size, _vp],
+    ),
+    "rb_hamming_topk_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "rb_hamming_topk": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),
+    "rb_quantize_int8": (_c_int, [_vp, _c_int, _c_int, _vp, _vp, _vp]),
     "rb_dense_topk_noalloc_scratch_bytes": (_c_size, []),
     "rb_dense_topk_noalloc": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp]),
 }

@@ -17,8 +17,6 @@ ProfileEvents& profile_events() {
   return ev;
 }
 
-void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stream);
-
 static int fail(int code, const char* msg) {
   set_last_error(msg);
   return code;

@@ -42,6 +42,8 @@ int row_kth_lower_bound(const float* vals, int B, int n, int stride, int k, floa
 int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,
                 int64_t* out_ids, float* out_scores, float* out_kth, cudaStream_t stream);
 
+void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stream);
+
 int merge_shard_lists(const int64_t* ids, const float* scores, int W, int B, int kin, int k, int64_t* out_ids,
                       float* out_scores, void* ws, cudaStream_t stream);
 size_t merge_shard_ws_bytes(int W, int B, int kin);

@@ -110,4 +110,290 @@ def dense_topk_sharded(query: Tensor, item_shard: Tensor, k: int, id_offset: int
     return _dense_topk_impl(query, item_shard, k, id_offset)
 
 
-__all__ = ["check_contiguous", "dense_topk", "dense_topk_sharded"]
+# ---------------------------------------------------------------------------
+# clause filter (retrieve/src/retrieve/ops/triton/clause_mask.py,
+# clause_compact.py; predicate functional.py:173-185)
+# ---------------------------------------------------------------------------
+def _clause_prep(item_clause_attrs: Tensor, clause_is_reverse: Tensor, query_clause_attrs: Tensor):
+    """Validation + contiguity, as ``_clause_mask_prep`` (clause_mask.py:150-183)."""
+    if item_clause_attrs.dim() != 3:
+        raise ValueError("item_clause_attrs must be [N, C, A_max]")
+    if query_clause_attrs.dim() != 2:
+        raise ValueError("query_clause_attrs must be [B, C]")
+    n, c, a_max = item_clause_attrs.shape
+    b, c_q = query_clause_attrs.shape
+    if c != c_q:
+        raise ValueError(f"clause-count mismatch: items C={c}, query C={c_q}")
+    if item_clause_attrs.dtype != torch.int64:
+        raise TypeError(f"item_clause_attrs must be int64, got {item_clause_attrs.dtype}")
+    if b > 65535:
+        raise ValueError("the clause kernels take at most 65535 query rows per call")
+    _require_cuda(item_clause_attrs, query_clause_attrs)
+    check_contiguous(item_clause_attrs=item_clause_attrs)
+    rev = clause_is_reverse.to(device=item_clause_attrs.device, dtype=torch.uint8).contiguous()
+    if rev.numel() != c:
+        raise ValueError(f"clause_is_reverse must have {c} entries, got {rev.numel()}")
+    qa = query_clause_attrs.to(torch.int64).contiguous()
+    return item_clause_attrs, rev, qa, b, n, c, a_max
+
+
+@torch.library.custom_op("retrieve::clause_mask", mutates_args=(), device_types="cuda")
+def clause_mask(item_clause_attrs: Tensor, clause_is_reverse: Tensor, query_clause_attrs: Tensor) -> Tensor:
+    """Exact clause evaluation → ``[B, N]`` bool (clause_mask.py:270-283)."""
+    attrs, rev, qa, b, n, c, a = _clause_prep(item_clause_attrs, clause_is_reverse, query_clause_attrs)
+    out = torch.empty((b, n), dtype=torch.bool, device=attrs.device)
+    if b and n:
+        rc = _lib.lib().rb_clause_mask(_ptr(attrs), n, c, a, _ptr(rev), _ptr(qa), b, None, _ptr(out),
+                                       _stream_ptr(attrs.device))
+        _lib.check(rc, "clause_mask")
+    return out
+
+
+@clause_mask.register_fake
+def _(item_clause_attrs, clause_is_reverse, query_clause_attrs):
+    return query_clause_attrs.new_empty((query_clause_attrs.shape[0], item_clause_attrs.shape[0]), dtype=torch.bool)
+
+
+@torch.library.custom_op("retrieve::clause_mask_scores", mutates_args=(), device_types="cuda")
+def clause_mask_scores(
+    scores: Tensor, item_clause_attrs: Tensor, clause_is_reverse: Tensor, query_clause_attrs: Tensor
+) -> Tensor:
+    """``where(clause_mask(...), scores, -inf)`` in one pass (clause_mask.py:286-303)."""
+    attrs, rev, qa, b, n, c, a = _clause_prep(item_clause_attrs, clause_is_reverse, query_clause_attrs)
+    if scores.shape != (b, n) or scores.dtype != torch.float32:
+        raise ValueError(f"scores must be [B, N] = {[b, n]} float32, got {scores.shape} {scores.dtype}")
+    sc = scores.contiguous()
+    out = torch.empty((b, n), dtype=torch.float32, device=attrs.device)
+    if b and n:
+        rc = _lib.lib().rb_clause_mask(_ptr(attrs), n, c, a, _ptr(rev), _ptr(qa), b, _ptr(sc), _ptr(out),
+                                       _stream_ptr(attrs.device))
+        _lib.check(rc, "clause_mask_scores")
+    return out
+
+
+@clause_mask_scores.register_fake
+def _(scores, item_clause_attrs, clause_is_reverse, query_clause_attrs):
+    return torch.empty_like(scores)
+
+
+@torch.library.custom_op("retrieve::clause_compact", mutates_args=(), device_types="cuda")
+def clause_compact(
+    item_clause_attrs: Tensor, clause_is_reverse: Tensor, query_clause_attrs: Tensor
+) -> tuple[Tensor, Tensor]:
+    """Clause evaluation + compaction → ``(positive_indices [B, N] int64, counts
+    [B] int64)``: each row's passing ids in ascending order on ``[0, counts[b])``,
+    the tail unwritten (clause_compact.py:174-196)."""
+    attrs, rev, qa, b, n, c, a = _clause_prep(item_clause_attrs, clause_is_reverse, query_clause_attrs)
+    ids = torch.empty((b, n), dtype=torch.int64, device=attrs.device)
+    counts = torch.empty((b,), dtype=torch.int64, device=attrs.device)
+    if b:
+        lib = _lib.lib()
+        nb = ctypes.c_size_t(0)
+        _lib.check(lib.rb_clause_compact_workspace_size(b, n, ctypes.byref(nb)), "clause_compact")
+        ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=attrs.device)
+        rc = lib.rb_clause_compact(_ptr(attrs), n, c, a, _ptr(rev), _ptr(qa), b, _ptr(ids), _ptr(counts), _ptr(ws),
+                                   ws.numel(), _stream_ptr(attrs.device))
+        _lib.check(rc, "clause_compact")
+    return ids, counts
+
+
+@clause_compact.register_fake
+def _(item_clause_attrs, clause_is_reverse, query_clause_attrs):
+    b, n = query_clause_attrs.shape[0], item_clause_attrs.shape[0]
+    return (
+        query_clause_attrs.new_empty((b, n), dtype=torch.int64),
+        query_clause_attrs.new_empty((b,), dtype=torch.int64),
+    )
+
+
+# ---------------------------------------------------------------------------
+# gemv_scores (ops/triton/gemv_scores.py:31-43)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("retrieve::gemv_scores", mutates_args=(), device_types="cuda")
+def gemv_scores(query: Tensor, item_embs_t: Tensor) -> Tensor:
+    """``query [1, D]`` fp16 against ``item_embs_t [D, N]`` fp16 (contiguous) →
+    ``[1, N]`` fp32, one fp32 FMA per k in order (the order of cuBLAS's gemv2N)."""
+    if query.shape[0] != 1 or query.dtype != torch.float16 or item_embs_t.dtype != torch.float16:
+        raise ValueError("gemv_scores takes one fp16 query row and an fp16 [D, N] table")
+    _require_cuda(query, item_embs_t)
+    check_contiguous(item_embs_t=item_embs_t)
+    d, n = item_embs_t.shape
+    q = query.contiguous()
+    out = torch.empty((1, n), dtype=torch.float32, device=q.device)
+    rc = _lib.lib().rb_gemv_scores(_ptr(q), _ptr(item_embs_t), d, n, _ptr(out), _stream_ptr(q.device))
+    _lib.check(rc, "gemv_scores")
+    return out
+
+
+@gemv_scores.register_fake
+def _(query, item_embs_t):
+    return query.new_empty((1, item_embs_t.shape[1]), dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# candidate top-k: fused_masked_knn_topk / oporp indirect
+# ---------------------------------------------------------------------------
+_CAND_DTYPES = {torch.float16: _lib.RB_F16, torch.float32: _lib.RB_F32}
+
+
+def _candidate_topk(kind, query, items, positive_indices, counts, k, k_out):
+    lib = _lib.lib()
+    b, p = positive_indices.shape
+    dev = query.device
+    ids = torch.empty((b, k_out), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k_out), dtype=torch.float32, device=dev)
+    if b == 0 or k_out == 0:
+        return ids, scores
+    nb = ctypes.c_size_t(0)
+    _lib.check(lib.rb_candidate_topk_workspace_size(b, p, ctypes.byref(nb)), "candidate_topk")
+    ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
+    qd = _CAND_DTYPES.get(query.dtype, _lib.RB_F32)
+    xd = _CAND_DTYPES.get(items.dtype, _lib.RB_F32)
+    rc = lib.rb_candidate_topk(
+        kind, _ptr(query), qd, _ptr(items), xd, items.shape[0], query.shape[1], _ptr(positive_indices), p,
+        _ptr(counts), b, k, _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream_ptr(dev),
+    )
+    _lib.check(rc, "candidate_topk")
+    return ids, scores
+
+
+@torch.library.custom_op("retrieve::fused_masked_knn_topk", mutates_args=(), device_types="cuda")
+def fused_masked_knn_topk(
+    query: Tensor, item_embs: Tensor, positive_indices: Tensor, counts: Tensor, k: int
+) -> tuple[Tensor, Tensor]:
+    """Fused gather + fp32 dot + top-k over ``positive_indices[b, :counts[b]]`` →
+    ``(ids [B, k], scores [B, k])``; requires ``P >= k`` (``ValueError``
+    otherwise, as the reference op, fused_masked_knn_topk.py:289-310); rows
+    short of candidates end in ``-1`` / ``-inf``."""
+    if positive_indices.shape[1] < k:
+        raise ValueError(f"positive_indices has {positive_indices.shape[1]} columns, fewer than k={k}")
+    if query.dim() != 2 or item_embs.dim() != 2:
+        raise ValueError("query must be [B, D] and item_embs [N, D]")
+    if query.dtype not in _CAND_DTYPES or item_embs.dtype not in _CAND_DTYPES:
+        raise TypeError(
+            f"query and item_embs must be float16 or float32, got {query.dtype} and {item_embs.dtype}"
+        )
+    if query.shape[1] != item_embs.shape[1]:
+        raise ValueError("query and item_embs must have the same D")
+    _require_cuda(query, item_embs, positive_indices, counts)
+    check_contiguous(item_embs=item_embs, positive_indices=positive_indices)
+    return _candidate_topk(
+        0, query.contiguous(), item_embs, positive_indices.to(torch.int64), counts.to(torch.int64).contiguous(),
+        k, k,
+    )
+
+
+@fused_masked_knn_topk.register_fake
+def _(query, item_embs, positive_indices, counts, k):
+    b = query.shape[0]
+    return query.new_empty((b, k), dtype=torch.int64), query.new_empty((b, k), dtype=torch.float32)
+
+
+def _oporp_check(query_bits: Tensor, item_bits: Tensor) -> None:
+    """As ``_oporp_prep`` (oporp_1bit_match_topk.py:134-163)."""
+    if query_bits.dim() != 2 or item_bits.dim() != 2:
+        raise ValueError("query_bits must be [B, W] and item_bits [N, W]")
+    if query_bits.dtype != torch.int64 or item_bits.dtype != torch.int64:
+        raise TypeError("query_bits and item_bits must be int64")
+    if query_bits.shape[1] != item_bits.shape[1]:
+        raise ValueError(
+            f"W mismatch: query_bits W={query_bits.shape[1]} vs item_bits W={item_bits.shape[1]}"
+        )
+    _require_cuda(query_bits, item_bits)
+    check_contiguous(item_bits=item_bits)
+
+
+@torch.library.custom_op("retrieve::oporp_1bit_match_topk_full", mutates_args=(), device_types="cuda")
+def oporp_1bit_match_topk_full(query_bits: Tensor, item_bits: Tensor, k: int) -> tuple[Tensor, Tensor]:
+    """Full-scan 1-bit Hamming top-k: score ``64*W - 2*popcount(q ^ item)`` over
+    every row of ``item_bits`` → ``(ids [B, k], scores [B, k])``, ties to the
+    lower row (oporp_1bit_match_topk.py:261-273)."""
+    _oporp_check(query_bits, item_bits)
+    b, w = query_bits.shape
+    n = item_bits.shape[0]
+    if k > n:
+        raise RuntimeError(f"selected index k={k} out of range for {n} items")
+    q = query_bits.contiguous()
+    dev = q.device
+    ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return ids, scores
+    lib = _lib.lib()
+    nb = ctypes.c_size_t(0)
+    _lib.check(lib.rb_hamming_topk_workspace_size(b, n, w, k, ctypes.byref(nb)), "oporp_1bit_match_topk_full")
+    ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
+    rc = lib.rb_hamming_topk(_ptr(q), _ptr(item_bits), b, n, w, k, _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(),
+                             _stream_ptr(dev))
+    _lib.check(rc, "oporp_1bit_match_topk_full")
+    return ids, scores
+
+
+@oporp_1bit_match_topk_full.register_fake
+def _(query_bits, item_bits, k):
+    b = query_bits.shape[0]
+    return query_bits.new_empty((b, k), dtype=torch.int64), query_bits.new_empty((b, k), dtype=torch.float32)
+
+
+@torch.library.custom_op("retrieve::oporp_1bit_match_topk_indirect", mutates_args=(), device_types="cuda")
+def oporp_1bit_match_topk_indirect(
+    query_bits: Tensor, item_bits: Tensor, k: int, positive_indices: Tensor, counts: Tensor
+) -> tuple[Tensor, Tensor]:
+    """Hamming top-k over ``positive_indices[b, :counts[b]]`` only; returns
+    ``min(k, P)`` columns with ``-1`` / ``-inf`` where a row runs out of
+    candidates (oporp_1bit_match_topk.py:276-292)."""
+    _oporp_check(query_bits, item_bits)
+    _require_cuda(positive_indices, counts)
+    check_contiguous(positive_indices=positive_indices)
+    p = positive_indices.shape[1]
+    return _candidate_topk(
+        1, query_bits.contiguous(), item_bits, positive_indices.to(torch.int64),
+        counts.to(torch.int64).contiguous(), k, min(k, p),
+    )
+
+
+@oporp_1bit_match_topk_indirect.register_fake
+def _(query_bits, item_bits, k, positive_indices, counts):
+    b, p = positive_indices.shape
+    kk = min(k, p)
+    return query_bits.new_empty((b, kk), dtype=torch.int64), query_bits.new_empty((b, kk), dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# query-side int8 quantization (indexing/quantize.py:9-18)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("retrieve::quantize_int8", mutates_args=(), device_types="cuda")
+def quantize_int8(embs: Tensor) -> tuple[Tensor, Tensor]:
+    """Per-row symmetric int8 codes and fp32 scales, bit for bit
+    ``retrieve.indexing.quantize.quantize_int8``."""
+    if embs.dim() != 2:
+        raise ValueError(f"expected 2-D [B, D] input, got shape {tuple(embs.shape)}")
+    _require_cuda(embs)
+    x = embs.to(torch.float32).contiguous()
+    b, d = x.shape
+    codes = torch.empty((b, d), dtype=torch.int8, device=x.device)
+    scales = torch.empty((b,), dtype=torch.float32, device=x.device)
+    if b:
+        rc = _lib.lib().rb_quantize_int8(_ptr(x), b, d, _ptr(codes), _ptr(scales), _stream_ptr(x.device))
+        _lib.check(rc, "quantize_int8")
+    return codes, scales
+
+
+@quantize_int8.register_fake
+def _(embs):
+    return embs.new_empty(embs.shape, dtype=torch.int8), embs.new_empty((embs.shape[0],), dtype=torch.float32)
+
+
+__all__ = [
+    "check_contiguous",
+    "clause_compact",
+    "clause_mask",
+    "clause_mask_scores",
+    "dense_topk",
+    "dense_topk_sharded",
+    "fused_masked_knn_topk",
+    "gemv_scores",
+    "oporp_1bit_match_topk_full",
+    "oporp_1bit_match_topk_indirect",
+    "quantize_int8",
+]
