@@ -177,6 +177,20 @@ RB_API int rb_dense_topk_noalloc(const void* queries, const void* items, int B, 
                                  int64_t id_offset, int64_t* out_ids, float* out_scores, void* stream);
 
 /*
+ * Int8 scoring + top-k (tensor-core int8 x int8 -> int32 dots, kind::i8):
+ * query_codes [B, D] and item_codes [N, D] int8, per-query and per-item fp32
+ * scales; score = (fp32(dot) * query_scale) * item_scale in that order
+ * (the dequant of retrieve/src/retrieve/ops/official/adapter.py:338-367 and
+ * silvertorch fork_search_cuda.cu:585-591; with one global item scale this is
+ * SilverTorch's int32 scoring path over every item). D in {128, 256};
+ * k <= 256. Workspace as rb_dense_topk_workspace_size.
+ */
+RB_API int rb_dense_topk_i8(const int8_t* query_codes, const float* query_scales, const int8_t* item_codes,
+                            const float* item_scales, int B, int N, int D, int k, int64_t id_offset,
+                            int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/*
  * Reads (synchronously) the device error word a scan kernel leaves in
  * `workspace` (0 = none; non-zero = a bounded wait ran out). Test / debug aid.
  */

@@ -114,3 +114,36 @@ def quantize_int8(x):
     ratio = (x.astype(np.float64) / abs_max.astype(np.float64)).astype(np.float32)
     codes = np.clip(np.rint(ratio * np.float32(127.0)), -128, 127).astype(np.int8)
     return codes, scales
+
+
+def int8_topk(query, item_codes, item_scales, k, *, chunk=1 << 18):
+    """Int8 scoring oracle: query quantized by ``quantize_int8``; exact int64
+    dots; score = (fp32(dot) * q_scale) * item_scale with fp32 rounding after
+    each multiply (ops/official/adapter.py:338-367 order); top-k, ties to the
+    lower id."""
+    codes, qs = quantize_int8(np.asarray(query, dtype=np.float32))
+    xc = np.asarray(item_codes, dtype=np.int8)
+    xs = np.asarray(item_scales, dtype=np.float32)
+    qc = codes.astype(np.int64)
+    best_i = np.zeros((qc.shape[0], 0), dtype=np.int64)
+    best_s = np.zeros((qc.shape[0], 0), dtype=np.float32)
+    for lo in range(0, xc.shape[0], chunk):
+        dots = qc @ xc[lo : lo + chunk].astype(np.int64).T
+        s = (dots.astype(np.float32) * qs[:, None]).astype(np.float32) * xs[None, lo : lo + chunk]
+        ci, cs = topk_strict(s.astype(np.float32), k, pad_to_k=False)
+        all_i = np.concatenate([best_i, ci + lo], axis=1)
+        all_s = np.concatenate([best_s, cs], axis=1)
+        best_i, best_s = topk_strict(all_s, k, ids=all_i, pad_to_k=False)
+    return best_i, best_s
+
+
+def silvertorch_fullprobe(query, item_codes, global_scale, k):
+    """SilverTorch's int32 path with every cluster probed (st::search semantics,
+    silvertorch fork_search_cuda.cu:1405-1411 and 585-591): rank on the raw int32
+    dot, ties in index order, then score = (fp32(dot) * q_scale) * global_scale."""
+    codes, qs = quantize_int8(np.asarray(query, dtype=np.float32))
+    dots = codes.astype(np.int64) @ np.asarray(item_codes, dtype=np.int64).T
+    ids, top = topk_strict(dots.astype(np.float64).astype(np.float32) if dots.max() < 2**24 else dots, k)
+    d = np.take_along_axis(dots, ids, axis=1).astype(np.float32)
+    scores = (d * qs[:, None]).astype(np.float32) * np.float32(global_scale)
+    return ids, scores.astype(np.float32)

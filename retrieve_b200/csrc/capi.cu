@@ -47,13 +47,15 @@ int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* 
   return RB_OK;
 }
 
-int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int64_t id_offset,
-                  int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes, void* stream_) {
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk: dtype must be f16 or bf16");
+// Shared body of the dense entry points (elem 0 f16, 1 bf16, 2 int8).
+static int dense_topk_impl(int elem, const void* queries, const float* q_scale, const void* items,
+                           const float* x_scale, int B, int N, int D, int k, int64_t id_offset, int64_t* out_ids,
+                           float* out_scores, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (B < 0 || N < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk: bad B, N or k");
   if (k > 256) return fail(RB_ERR_UNSUPPORTED, "dense_topk: k > 256 is not supported");
-  if (D * 2 != 128 && D * 2 != 256) return fail(RB_ERR_UNSUPPORTED, "dense_topk: D must be 64 or 128");
+  const int row_bytes = (elem == 2) ? D : 2 * D;
+  if (row_bytes != 128 && row_bytes != 256)
+    return fail(RB_ERR_UNSUPPORTED, "dense_topk: rows must be 128 or 256 bytes (D = 64/128 fp16/bf16, 128/256 int8)");
   if (B == 0) return RB_OK;
   if (out_ids == nullptr || out_scores == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_topk: null output");
   if (N == 0) {
@@ -61,6 +63,8 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
     return cudaGetLastError() == cudaSuccess ? RB_OK : fail(RB_ERR_CUDA, "fill_empty launch failed");
   }
   if (!aligned16(queries) || !aligned16(items)) return fail(RB_ERR_INVALID_ARG, "dense_topk: 16-byte alignment");
+  if (elem == 2 && (q_scale == nullptr || x_scale == nullptr || !aligned16(x_scale)))
+    return fail(RB_ERR_INVALID_ARG, "dense_topk_i8: scales must be given (item scales 16-byte aligned)");
   const size_t need = dense_workspace_bytes(B, N, k);
   if (workspace == nullptr || workspace_bytes < need) return fail(RB_ERR_WORKSPACE, "dense_topk: workspace too small");
 
@@ -75,12 +79,12 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
   int* err = ws_err_word(workspace, workspace_bytes);
   if (cudaMemsetAsync(err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
 
-  const int elem = (dtype == RB_BF16) ? 1 : 0;
   ProfileEvents& pe = profile_events();
   const float* seed = nullptr;
   if (pl.sample_stride > 0) {
     float* chunk_max = reinterpret_cast<float*>(lists);  // dead before the full pass writes lists
-    int rc = dense_scan_pass(1, elem, queries, items, B, N, D, pl, k, nullptr, lists, counts, chunk_max, err, stream);
+    int rc = dense_scan_pass(1, elem, queries, items, B, N, D, pl, k, nullptr, lists, counts, chunk_max, err, stream,
+                             q_scale, x_scale);
     if (rc != RB_OK) return rc;
     const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
     rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, k, thresh, stream);
@@ -88,10 +92,25 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
     seed = thresh;
   }
   if (pe.start) cudaEventRecord(pe.start, stream);
-  int rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, lists, counts, nullptr, err, stream);
+  int rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, lists, counts, nullptr, err, stream,
+                           q_scale, x_scale);
   if (rc != RB_OK) return rc;
   if (pe.stop) cudaEventRecord(pe.stop, stream);
   return merge_lists(lists, counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
+}
+
+int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int64_t id_offset,
+                  int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk: dtype must be f16 or bf16");
+  return dense_topk_impl(dtype == RB_BF16 ? 1 : 0, queries, nullptr, items, nullptr, B, N, D, k, id_offset, out_ids,
+                         out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rb_dense_topk_i8(const int8_t* query_codes, const float* query_scales, const int8_t* item_codes,
+                     const float* item_scales, int B, int N, int D, int k, int64_t id_offset, int64_t* out_ids,
+                     float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+  return dense_topk_impl(2, query_codes, query_scales, item_codes, item_scales, B, N, D, k, id_offset, out_ids,
+                         out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launches) {

@@ -47,6 +47,8 @@ struct alignas(64) DenseScanParams {
   int* err;           // device error word
   float* chunk_max;   // MODE 1: [B, chunk_stride] max score of every 32-item chunk
   int chunk_stride;
+  const float* q_scale;  // int8 only: [B] per-query scale
+  const float* x_scale;  // int8 only: [N] per-item scale
   int B, N;
   int n_qsg, n_splits;
   int tile_stride, tile_offset, pass_tiles;
@@ -75,10 +77,40 @@ __device__ __forceinline__ void split_range(int split, int n_splits, int pass_ti
 // Filtering work on NCH 32-item chunks of scores already in registers:
 // r[ch][j] = score of item row0 + 32 * ch + j for this thread's query; the
 // chunks are chunk numbers c0 .. c0 + NCH - 1 of their 128-item tile.
-template <int MODE, int NCH>
+// For int8 (ELEM 2) the registers first hold int32 dots, turned here into the
+// exact fp32 score (fp32(dot) * q_scale) * item_scale, left to right as the
+// reference dequantizes (ops/official/adapter.py:338-367).
+template <int MODE, int NCH, int ELEM = 1>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list) {
+  if constexpr (ELEM == 2) {
+    const float qs = valid_q ? p.q_scale[q] : 0.f;
+    const bool full = row0 + NCH * 32 <= static_cast<uint32_t>(p.N);
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const uint32_t id = row0 + ch * 32 + 4 * j4;
+        float4 xs;
+        if (full) {
+          xs = __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
+        } else {
+          xs.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
+          xs.y = id + 1 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 1] : 0.f;
+          xs.z = id + 2 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 2] : 0.f;
+          xs.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
+        }
+        const float xv[4] = {xs.x, xs.y, xs.z, xs.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          // |dot| <= 2^22 for D <= 256: exact int32 -> fp32 through the fp32 magic constant
+          const float f = __uint_as_float(r[ch][4 * j4 + u] + 0x4B400000u) - 12582912.0f;
+          r[ch][4 * j4 + u] = __float_as_uint(__fmul_rn(__fmul_rn(f, qs), xv[u]));
+        }
+      }
+    }
+  }
   if (row0 + NCH * 32 > static_cast<uint32_t>(p.N)) {
     // last, partial tile: rows past N were zero-filled by TMA; NaN never passes
     // a threshold test and is ignored by fmaxf
@@ -328,7 +360,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        process_chunks<MODE, 4>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -617,7 +649,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
-        process_chunks<MODE, 4>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
         if (++acc == kAcc) {
           acc = 0;
           acc_phase ^= 1;
@@ -802,9 +834,11 @@ size_t dense_workspace_bytes(int B, int N, int k) {
 
 int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
                     int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, const float* q_scale, const float* x_scale) {
   DenseScanParams prm;
   std::memset(&prm, 0, sizeof(prm));
+  prm.q_scale = q_scale;
+  prm.x_scale = x_scale;
   const int eb = (elem == 2) ? 1 : 2;
   const int row_bytes = D * eb;
   const int item_box = pl.two_sm ? kHalfItems : kTileItems;
@@ -852,6 +886,10 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
     RB_DISPATCH2(1, 1, 2, 12)
     RB_DISPATCH2(1, 2, 1, 8)
     RB_DISPATCH2(1, 2, 2, 8)
+    RB_DISPATCH2(2, 1, 1, 12)
+    RB_DISPATCH2(2, 1, 2, 12)
+    RB_DISPATCH2(2, 2, 1, 8)
+    RB_DISPATCH2(2, 2, 2, 8)
 #undef RB_DISPATCH2
   } else {
     const int grid = std::min(n_tasks, num_sms());
@@ -868,6 +906,8 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
     RB_DISPATCH(0, 2, 1, 4)
     RB_DISPATCH(1, 1, 1, 8)
     RB_DISPATCH(1, 2, 1, 4)
+    RB_DISPATCH(2, 1, 1, 8)
+    RB_DISPATCH(2, 2, 1, 4)
 #undef RB_DISPATCH
   }
   if (!handled) {

@@ -384,8 +384,55 @@ def _(embs):
     return embs.new_empty(embs.shape, dtype=torch.int8), embs.new_empty((embs.shape[0],), dtype=torch.float32)
 
 
+# ---------------------------------------------------------------------------
+# int8 scoring (SilverTorch's int32 scoring path)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("retrieve::int8_topk", mutates_args=(), device_types="cuda")
+def int8_topk(query: Tensor, item_codes: Tensor, item_scales: Tensor, k: int) -> tuple[Tensor, Tensor]:
+    """Int8 scoring + top-k: the fp32 query batch is quantized per row exactly as
+    ``quantize_int8`` (indexing/quantize.py:9-18), scored against ``item_codes
+    [N, D]`` int8 with int32 accumulation on the tensor cores, and dequantized as
+    ``(fp32(dot) * q_scale) * item_scale`` (the reference's order,
+    ops/official/adapter.py:338-367). ``item_scales`` is ``[N]`` fp32 (all equal
+    for SilverTorch's global scale). Ties go to the lower item id."""
+    if query.dim() != 2 or item_codes.dim() != 2:
+        raise ValueError("query must be [B, D] and item_codes [N, D]")
+    if item_codes.dtype != torch.int8:
+        raise TypeError(f"item_codes must be int8, got {item_codes.dtype}")
+    if item_scales.dim() != 1 or item_scales.shape[0] != item_codes.shape[0]:
+        raise ValueError("item_scales must be [N]")
+    if query.shape[1] != item_codes.shape[1]:
+        raise ValueError("query and item_codes must have the same D")
+    _require_cuda(query, item_codes, item_scales)
+    check_contiguous(item_codes=item_codes, item_scales=item_scales)
+    xs = item_scales.to(torch.float32)
+    codes, qs = quantize_int8(query)
+    b, d = codes.shape
+    n = item_codes.shape[0]
+    dev = codes.device
+    ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return ids, scores
+    lib = _lib.lib()
+    nb = ctypes.c_size_t(0)
+    _lib.check(lib.rb_dense_topk_workspace_size(b, n, d, _lib.RB_I8, k, ctypes.byref(nb)), "int8_topk")
+    ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
+    rc = lib.rb_dense_topk_i8(_ptr(codes), _ptr(qs), _ptr(item_codes), _ptr(xs), b, n, d, k, 0, _ptr(ids),
+                              _ptr(scores), _ptr(ws), ws.numel(), _stream_ptr(dev))
+    _lib.check(rc, "int8_topk")
+    return ids, scores
+
+
+@int8_topk.register_fake
+def _(query, item_codes, item_scales, k):
+    b = query.shape[0]
+    return query.new_empty((b, k), dtype=torch.int64), query.new_empty((b, k), dtype=torch.float32)
+
+
 __all__ = [
     "check_contiguous",
+    "int8_topk",
     "clause_compact",
     "clause_mask",
     "clause_mask_scores",
