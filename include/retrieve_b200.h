@@ -177,6 +177,61 @@ RB_API int rb_dense_topk_noalloc(const void* queries, const void* items, int B, 
                                  int64_t id_offset, int64_t* out_ids, float* out_scores, void* stream);
 
 /*
+ * Attribute predicates for the filtered dense search. Per query up to
+ * RB_MAX_TERMS terms "clause == value", each possibly negated (flags bit 3),
+ * combined as AND over groups (flags bits 0-2) of OR over the group's terms.
+ * This covers LiNR's exact clause filter (one group per active clause, negate
+ * = clause_is_reverse; retrieve/src/retrieve/functional.py:173-185) and the
+ * AND / OR / NOT expressions of SilverTorch's query DSL once put in
+ * conjunctive form (silvertorch/silvertorch/ops/csrc/EXPRESSION_SYNTAX.md).
+ * A term matches exactly when some value of the item's clause equals `value`
+ * (item_attrs [N, n_clauses, attr_width] int64, -1 pads), or through the
+ * item's 64-bit Bloom word when every bit of `bloom_mask` is set
+ * (silvertorch bloom_index_search_cuda.cu:304-349 on a 64-bit-per-doc index).
+ * Mode BLOOM_RECHECK requires both the Bloom and the exact predicate.
+ */
+#define RB_MAX_TERMS 8
+#define RB_FILTER_NONE 0
+#define RB_FILTER_EXACT 1
+#define RB_FILTER_BLOOM 2
+#define RB_FILTER_BLOOM_RECHECK 3
+typedef struct {
+  int64_t value;
+  uint64_t bloom_mask;
+  int32_t clause;
+  int32_t flags;
+} rb_pred_term;
+typedef struct {
+  int mode;
+  const void* terms;       /* rb_pred_term [B, RB_MAX_TERMS] */
+  const int32_t* n_terms;  /* [B]; 0 = every item passes */
+  const int64_t* item_attrs;
+  int n_clauses;
+  int attr_width;
+  const uint64_t* item_bloom;
+} rb_filter;
+
+/*
+ * Dense fused scoring + top-k with an attribute predicate folded into the scan
+ * (LiNR V1 with its filter, retrieve/src/retrieve/modules/linr.py:75-79, and the
+ * bloom-filtered scan): items failing the predicate never enter the top-k; rows
+ * with fewer than k passing items end in -1 / -inf. Other arguments and limits
+ * as rb_dense_topk; workspace as rb_dense_topk_workspace_size.
+ */
+RB_API int rb_dense_topk_filtered(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
+                                  int64_t id_offset, const rb_filter* filter, int64_t* out_ids, float* out_scores,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Per-item 64-bit Bloom words from item_attrs [N, C, A] int64 (-1 pads; the
+ * clause index is the feature id): bit p of word n is set iff p is one of the
+ * first k distinct murmur_hash3_2x64(clause, value, seed) % 64 over
+ * seed = 0, 1, ... for some (clause, value) of item n
+ * (silvertorch bloom_index_util.cuh:61-107, 185-208). Build time.
+ */
+RB_API int rb_bloom_build(const int64_t* item_attrs, int N, int C, int A, int k, uint64_t* out_words, void* stream);
+
+/*
  * Int8 scoring + top-k (tensor-core int8 x int8 -> int32 dots, kind::i8):
  * query_codes [B, D] and item_codes [N, D] int8, per-query and per-item fp32
  * scales; score = (fp32(dot) * query_scale) * item_scale in that order

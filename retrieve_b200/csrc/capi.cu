@@ -50,7 +50,8 @@ int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* 
 // Shared body of the dense entry points (elem 0 f16, 1 bf16, 2 int8).
 static int dense_topk_impl(int elem, const void* queries, const float* q_scale, const void* items,
                            const float* x_scale, int B, int N, int D, int k, int64_t id_offset, int64_t* out_ids,
-                           float* out_scores, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                           float* out_scores, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                           const FilterArgs* filter = nullptr) {
   if (B < 0 || N < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk: bad B, N or k");
   if (k > 256) return fail(RB_ERR_UNSUPPORTED, "dense_topk: k > 256 is not supported");
   const int row_bytes = (elem == 2) ? D : 2 * D;
@@ -84,7 +85,7 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   if (pl.sample_stride > 0) {
     float* chunk_max = reinterpret_cast<float*>(lists);  // dead before the full pass writes lists
     int rc = dense_scan_pass(1, elem, queries, items, B, N, D, pl, k, nullptr, lists, counts, chunk_max, err, stream,
-                             q_scale, x_scale);
+                             q_scale, x_scale, filter);
     if (rc != RB_OK) return rc;
     const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
     rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, k, thresh, stream);
@@ -93,7 +94,7 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   }
   if (pe.start) cudaEventRecord(pe.start, stream);
   int rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, lists, counts, nullptr, err, stream,
-                           q_scale, x_scale);
+                           q_scale, x_scale, filter);
   if (rc != RB_OK) return rc;
   if (pe.stop) cudaEventRecord(pe.stop, stream);
   return merge_lists(lists, counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
@@ -104,6 +105,31 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
   if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk: dtype must be f16 or bf16");
   return dense_topk_impl(dtype == RB_BF16 ? 1 : 0, queries, nullptr, items, nullptr, B, N, D, k, id_offset, out_ids,
                          out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int rb_dense_topk_filtered(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
+                           int64_t id_offset, const rb_filter* filter, int64_t* out_ids, float* out_scores,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk_filtered: dtype must be f16 or bf16");
+  if (filter == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: filter is null");
+  FilterArgs f;
+  f.mode = filter->mode;
+  f.terms = static_cast<const PredTerm*>(filter->terms);
+  f.n_terms = filter->n_terms;
+  f.attrs = filter->item_attrs;
+  f.C = filter->n_clauses;
+  f.A = filter->attr_width;
+  f.bloom = filter->item_bloom;
+  if (f.mode < RB_FILTER_NONE || f.mode > RB_FILTER_BLOOM_RECHECK)
+    return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: unknown filter mode");
+  if (f.mode != RB_FILTER_NONE && (f.terms == nullptr || f.n_terms == nullptr))
+    return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: predicate terms missing");
+  if ((f.mode == RB_FILTER_EXACT || f.mode == RB_FILTER_BLOOM_RECHECK) && (f.attrs == nullptr || f.C <= 0 || f.A <= 0))
+    return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: exact attributes missing");
+  if ((f.mode == RB_FILTER_BLOOM || f.mode == RB_FILTER_BLOOM_RECHECK) && f.bloom == nullptr)
+    return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: bloom words missing");
+  return dense_topk_impl(dtype == RB_BF16 ? 1 : 0, queries, nullptr, items, nullptr, B, N, D, k, id_offset, out_ids,
+                         out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), &f);
 }
 
 int rb_dense_topk_i8(const int8_t* query_codes, const float* query_scales, const int8_t* item_codes,

@@ -49,6 +49,7 @@ struct alignas(64) DenseScanParams {
   int chunk_stride;
   const float* q_scale;  // int8 only: [B] per-query scale
   const float* x_scale;  // int8 only: [N] per-item scale
+  FilterArgs filter;     // attribute predicate (mode kFilterNone: none)
   int B, N;
   int n_qsg, n_splits;
   int tile_stride, tile_offset, pass_tiles;
@@ -120,6 +121,18 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
       for (int j = 0; j < 32; ++j)
         if (row0 + ch * 32 + j >= static_cast<uint32_t>(p.N)) r[ch][j] = 0x7fc00000u;
   }
+  if (p.filter.mode != kFilterNone && valid_q) {
+    if constexpr (MODE == 1) {
+      // sampling pass: items that fail the predicate do not count
+#pragma unroll 1
+      for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll 4
+        for (int j = 0; j < 32; ++j) {
+          const uint32_t id = row0 + ch * 32 + j;
+          if (id < static_cast<uint32_t>(p.N) && !pred_pass(p.filter, q, id)) r[ch][j] = 0x7fc00000u;
+        }
+    }
+  }
   if constexpr (MODE == 1) {
     // sampling pass: the max of every 32-item chunk, nothing else
     if (valid_q) {
@@ -141,7 +154,12 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
     if (__any_sync(RB_FULL_MASK, valid_q && !(all >> 31))) {
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
-        if (valid_q && !(sg[ch] >> 31)) append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
+        if (valid_q && !(sg[ch] >> 31)) {
+          if (p.filter.mode == kFilterNone)
+            append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
+          else
+            append_chunk_bits_pred(list, count, thresh, r[ch], row0 + ch * 32, p.filter, q);
+        }
       }
     }
   }
@@ -834,9 +852,10 @@ size_t dense_workspace_bytes(int B, int N, int k) {
 
 int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
                     int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
-                    cudaStream_t stream, const float* q_scale, const float* x_scale) {
+                    cudaStream_t stream, const float* q_scale, const float* x_scale, const FilterArgs* filter) {
   DenseScanParams prm;
   std::memset(&prm, 0, sizeof(prm));
+  if (filter != nullptr) prm.filter = *filter;
   prm.q_scale = q_scale;
   prm.x_scale = x_scale;
   const int eb = (elem == 2) ? 1 : 2;

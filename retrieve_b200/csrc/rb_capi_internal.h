@@ -7,6 +7,7 @@
 #include <cstdint>
 
 #include "retrieve_b200.h"
+#include "rb_common.cuh"
 
 namespace rb {
 
@@ -33,7 +34,8 @@ size_t dense_chunk_stride(const DensePlan& pl);
 // mode 0: candidate pass over every tile; mode 1: chunk-max sampling pass.
 int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
                     int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
-                    cudaStream_t stream, const float* q_scale = nullptr, const float* x_scale = nullptr);
+                    cudaStream_t stream, const float* q_scale = nullptr, const float* x_scale = nullptr,
+                    const FilterArgs* filter = nullptr);
 // Per row of vals [B, n] (row stride `stride`): a lower bound on the k-th
 // largest value (exact to 22 leading key bits), -inf when n < k.
 int row_kth_lower_bound(const float* vals, int B, int n, int stride, int k, float* out, cudaStream_t stream);

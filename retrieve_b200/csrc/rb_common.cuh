@@ -77,6 +77,65 @@ __device__ __forceinline__ uint2 key_to_entry(uint64_t key) {
 }
 
 // ---------------------------------------------------------------------------
+// Attribute predicates: per query up to kMaxTerms terms "clause c == value v",
+// each possibly negated, combined as AND over groups of OR over the group's
+// terms (conjunctive normal form; groups 0..7). A term matches an item exactly
+// (some value of the item's clause c equals v; -1 pads) or through the item's
+// 64-bit Bloom word (every bit of the term's mask set).
+// ---------------------------------------------------------------------------
+constexpr int kMaxTerms = 8;
+struct PredTerm {        // 24 bytes, layout shared with the C-ABI rb_pred_term
+  int64_t value;
+  uint64_t bloom_mask;
+  int32_t clause;
+  int32_t flags;         // bits 0-2 group, bit 3 negate
+};
+enum FilterMode : int { kFilterNone = 0, kFilterExact = 1, kFilterBloom = 2, kFilterBloomRecheck = 3 };
+
+struct FilterArgs {
+  int mode;
+  const PredTerm* terms;  // [B, kMaxTerms]
+  const int* n_terms;     // [B]
+  const int64_t* attrs;   // [N, C, A] int64, -1 pads (exact / recheck)
+  int C, A;
+  const uint64_t* bloom;  // [N] (bloom / recheck)
+};
+
+__device__ __forceinline__ bool pred_eval_one(const PredTerm* t, int nt, bool use_bloom, const int64_t* row,
+                                              int A, uint64_t word) {
+  uint32_t need = 0, got = 0;
+  for (int i = 0; i < nt; ++i) {
+    const PredTerm tm = t[i];
+    const uint32_t g = 1u << (tm.flags & 7);
+    need |= g;
+    bool m;
+    if (use_bloom) {
+      m = (word & tm.bloom_mask) == tm.bloom_mask;
+    } else {
+      m = false;
+      const int64_t* cell = row + static_cast<int64_t>(tm.clause) * A;
+      for (int a = 0; a < A; ++a) m |= (cell[a] == tm.value);
+    }
+    if (tm.flags & 8) m = !m;
+    if (m) got |= g;
+  }
+  return (got & need) == need;
+}
+
+// Does item `id` pass query q's predicate?
+__device__ __forceinline__ bool pred_pass(const FilterArgs& f, int q, uint32_t id) {
+  const PredTerm* t = f.terms + static_cast<size_t>(q) * kMaxTerms;
+  const int nt = f.n_terms[q];
+  if (nt == 0) return true;
+  bool ok = true;
+  if (f.mode == kFilterBloom || f.mode == kFilterBloomRecheck)
+    ok = pred_eval_one(t, nt, true, nullptr, 0, f.bloom[id]);
+  if (ok && (f.mode == kFilterExact || f.mode == kFilterBloomRecheck))
+    ok = pred_eval_one(t, nt, false, f.attrs + static_cast<size_t>(id) * f.C * f.A, f.A, 0ull);
+  return ok;
+}
+
+// ---------------------------------------------------------------------------
 // mbarrier (shared::cta) with bounded waits.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -179,6 +179,20 @@ __device__ __forceinline__ void append_chunk_bits(uint2* list, int& count, float
   count = static_cast<int>(w - list);
 }
 
+// Same, appending only the items that pass query q's attribute predicate.
+__device__ __forceinline__ void append_chunk_bits_pred(uint2* list, int& count, float thresh, const uint32_t (&s)[32],
+                                                       uint32_t id0, const FilterArgs& f, int q) {
+  uint2* w = list + count;
+#pragma unroll 4
+  for (int j = 0; j < 32; ++j) {
+    if (__uint_as_float(s[j]) >= thresh && pred_pass(f, q, id0 + j)) {
+      *w = make_uint2(s[j], id0 + j);
+      ++w;
+    }
+  }
+  count = static_cast<int>(w - list);
+}
+
 // AND over a chunk of the bit patterns of (s[j] - thresh): the sign bit of the
 // result is set iff every s[j] < thresh (NaN scores count as passing here and
 // are rejected by the exact test of the append).

@@ -111,6 +111,109 @@ def dense_topk_sharded(query: Tensor, item_shard: Tensor, k: int, id_offset: int
 
 
 # ---------------------------------------------------------------------------
+# dense_topk with an attribute predicate (LiNR V1 with its filter; bloom scan)
+# ---------------------------------------------------------------------------
+FILTER_MODES = {"exact": 1, "bloom": 2, "bloom_recheck": 3}
+
+
+class _RbFilter(ctypes.Structure):
+    _fields_ = [
+        ("mode", ctypes.c_int),
+        ("terms", ctypes.c_void_p),
+        ("n_terms", ctypes.c_void_p),
+        ("item_attrs", ctypes.c_void_p),
+        ("n_clauses", ctypes.c_int),
+        ("attr_width", ctypes.c_int),
+        ("item_bloom", ctypes.c_void_p),
+    ]
+
+
+@torch.library.custom_op("retrieve::dense_topk_filtered", mutates_args=(), device_types="cuda")
+def dense_topk_filtered(
+    query: Tensor,
+    item_embs: Tensor,
+    k: int,
+    terms: Tensor,
+    n_terms: Tensor,
+    mode: str,
+    item_attrs: Tensor | None = None,
+    item_bloom: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:
+    """``dense_topk`` over the items that pass each query's predicate
+    (``retrieve_b200.predicates``): ``mode`` ``"exact"`` tests ``item_attrs
+    [N, C, A]`` int64, ``"bloom"`` the per-item 64-bit words ``item_bloom [N]``
+    (false positives possible, no false negatives for NOT-free predicates),
+    ``"bloom_recheck"`` both. Rows with fewer than k passing items end in
+    ``-1`` / ``-inf``. The predicate is evaluated inside the fused scan, only on
+    items whose score already clears the running top-k threshold."""
+    if mode not in FILTER_MODES:
+        raise ValueError(f"mode must be one of {sorted(FILTER_MODES)}, got {mode!r}")
+    if query.dim() != 2 or item_embs.dim() != 2:
+        raise ValueError("query must be [B, D] and item_embs [N, D]")
+    if item_embs.dtype not in _DTYPE_CODE:
+        raise TypeError(f"item_embs must be float16 or bfloat16, got {item_embs.dtype}")
+    b, n = query.shape[0], item_embs.shape[0]
+    if terms.shape != (b, 8 * 24) or terms.dtype != torch.uint8 or n_terms.shape != (b,):
+        raise ValueError("terms must be [B, 192] uint8 and n_terms [B] int32 (retrieve_b200.predicates)")
+    _require_cuda(query, item_embs, terms, n_terms)
+    check_contiguous(item_embs=item_embs)
+    m = FILTER_MODES[mode]
+    attrs = None
+    if m in (1, 3):
+        if item_attrs is None or item_attrs.dim() != 3 or item_attrs.dtype != torch.int64:
+            raise ValueError("exact filtering needs item_attrs [N, C, A] int64")
+        if item_attrs.shape[0] != n:
+            raise ValueError("item_attrs must have one row per item")
+        check_contiguous(item_attrs=item_attrs)
+        attrs = item_attrs
+    if m in (2, 3):
+        if item_bloom is None or item_bloom.shape != (n,) or item_bloom.dtype not in (torch.int64, torch.uint64):
+            raise ValueError("bloom filtering needs item_bloom [N] 64-bit words")
+        check_contiguous(item_bloom=item_bloom)
+    q = query.to(item_embs.dtype).contiguous()
+    tt = terms.contiguous()
+    nt = n_terms.to(torch.int32).contiguous()
+    dev = q.device
+    ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return ids, scores
+    f = _RbFilter(
+        m, tt.data_ptr(), nt.data_ptr(), 0 if attrs is None else attrs.data_ptr(),
+        0 if attrs is None else attrs.shape[1], 0 if attrs is None else attrs.shape[2],
+        0 if item_bloom is None else item_bloom.data_ptr(),
+    )
+    lib = _lib.lib()
+    code = _DTYPE_CODE[item_embs.dtype]
+    nb = ctypes.c_size_t(0)
+    _lib.check(lib.rb_dense_topk_workspace_size(b, n, q.shape[1], code, k, ctypes.byref(nb)), "dense_topk_filtered")
+    ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
+    rc = lib.rb_dense_topk_filtered(_ptr(q), _ptr(item_embs), b, n, q.shape[1], code, k, 0, ctypes.addressof(f),
+                                    _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream_ptr(dev))
+    _lib.check(rc, "dense_topk_filtered")
+    return ids, scores
+
+
+@dense_topk_filtered.register_fake
+def _(query, item_embs, k, terms, n_terms, mode, item_attrs=None, item_bloom=None):
+    b = query.shape[0]
+    return query.new_empty((b, k), dtype=torch.int64), query.new_empty((b, k), dtype=torch.float32)
+
+
+def bloom_build(item_attrs: Tensor, k: int = 3) -> Tensor:
+    """Per-item 64-bit Bloom words (int64 view of the uint64 words) of
+    ``item_attrs [N, C, A]`` int64 (``rb_bloom_build``). Build time."""
+    if item_attrs.dim() != 3 or item_attrs.dtype != torch.int64:
+        raise ValueError("item_attrs must be [N, C, A] int64")
+    _require_cuda(item_attrs)
+    a = item_attrs.contiguous()
+    out = torch.empty((a.shape[0],), dtype=torch.int64, device=a.device)
+    rc = _lib.lib().rb_bloom_build(_ptr(a), a.shape[0], a.shape[1], a.shape[2], k, _ptr(out), _stream_ptr(a.device))
+    _lib.check(rc, "bloom_build")
+    return out
+
+
+# ---------------------------------------------------------------------------
 # clause filter (retrieve/src/retrieve/ops/triton/clause_mask.py,
 # clause_compact.py; predicate functional.py:173-185)
 # ---------------------------------------------------------------------------
@@ -431,6 +534,8 @@ def _(query, item_codes, item_scales, k):
 
 
 __all__ = [
+    "bloom_build",
+    "dense_topk_filtered",
     "check_contiguous",
     "int8_topk",
     "clause_compact",

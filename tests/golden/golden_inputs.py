@@ -62,3 +62,33 @@ def quantize_inputs():
 def simhash_inputs():
     g = torch.Generator().manual_seed(8)
     return torch.randn(32, 128, generator=g)
+
+
+C3_CARDS = (10, 20, 50, 100, 200, 500, 1000, 1000)
+
+
+def zipf_attrs(n: int, seed: int, cards=C3_CARDS, alpha: float = 1.1):
+    """BASELINE config 3 attributes: one value per attribute, value v of
+    attribute c drawn with P(v) proportional to (v + 1)^-alpha over [0, card_c)."""
+    g = torch.Generator().manual_seed(seed)
+    cols = []
+    for card in cards:
+        w = (torch.arange(card, dtype=torch.float64) + 1.0) ** (-alpha)
+        cols.append(torch.multinomial(w, n, replacement=True, generator=g))
+    return torch.stack(cols, dim=1).to(torch.int64)
+
+
+BLOOM_EXPRESSIONS = [
+    "0:0",
+    "1:3 OR 2:7",
+    "0:1 AND 3:2",
+    "NOT 0:0",
+    "(4:5 OR 5:1) AND 0:2",
+    "6:0 OR 7:0 OR 2:1",
+    "1:0 AND NOT 2:0",
+    "3:10 OR (0:4 AND 1:1)",
+    "5:0 AND 6:1 AND 7:2",
+    "NOT (0:0 OR 1:0)",
+    "2:3",
+    "7:999 OR 0:9",
+]

@@ -1,0 +1,85 @@
+"""Filtered dense top-k (BASELINE config 3 semantics) against the oracle:
+integer-valued embeddings make every score exact, so ids and scores match bit
+for bit, ties toward the lower id; exact, Bloom and Bloom+recheck predicates;
+the device Bloom build equals the oracle's (pinned to the reference's own
+build)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import bloom, predicate
+from oracle.dense import as_f32
+from oracle.select import topk_strict
+from retrieve_b200 import predicates as P
+from tests.golden import golden_inputs as gi
+from tests.helpers import assert_topk_exact, make_int_rows
+
+pytestmark = pytest.mark.gpu
+
+EXPRS = gi.BLOOM_EXPRESSIONS
+
+
+def _oracle(q, x, k, masks):
+    sc = as_f32(q) @ as_f32(x).T
+    return topk_strict(sc, k, valid=masks, sentinel=True)
+
+
+def _masks(exprs, b, attrs=None, words=None):
+    return np.stack([predicate.eval_items(predicate.parse(exprs[i % len(exprs)]), attrs=attrs, words=words)
+                     for i in range(b)])
+
+
+def test_bloom_build_matches_oracle():
+    from retrieve_b200 import ops
+
+    attrs = gi.zipf_attrs(5000, seed=3)
+    words = ops.bloom_build(attrs[:, :, None].contiguous().cuda(), 3).cpu().numpy().view(np.uint64)
+    assert np.array_equal(words, bloom.item_words(attrs.numpy(), k=3))
+
+
+@pytest.mark.parametrize("mode", ["exact", "bloom", "bloom_recheck"])
+@pytest.mark.parametrize("b,n,k", [(64, 20_000, 50), (300, 60_000, 100), (130, 400_000, 100)])
+def test_filtered_topk_exact(mode, b, n, k):
+    from retrieve_b200 import ops
+
+    attrs = gi.zipf_attrs(n, seed=n)
+    attrs3 = attrs[:, :, None].contiguous()
+    q = make_int_rows(b, 128, seed=1)
+    x = make_int_rows(n, 128, seed=2)
+    exprs = [EXPRS[i % len(EXPRS)] for i in range(b)]
+    preds = P.from_expressions(exprs).to("cuda")
+    words = ops.bloom_build(attrs3.cuda(), 3)
+    ids, scores = ops.dense_topk_filtered(q.cuda(), x.cuda(), k, preds.terms, preds.n_terms, mode,
+                                          attrs3.cuda(), words)
+    wn = words.cpu().numpy().view(np.uint64)
+    if mode == "exact":
+        masks = _masks(exprs, b, attrs=attrs.numpy())
+    elif mode == "bloom":
+        masks = _masks(exprs, b, words=wn)
+    else:
+        masks = _masks(exprs, b, attrs=attrs.numpy()) & _masks(exprs, b, words=wn)
+    ref_ids, ref_scores = _oracle(q, x, k, masks)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+
+
+def test_linr_clause_queries_filtered():
+    """LiNR V1 semantics: AND of clause values with reverse clauses."""
+    from oracle import filters
+    from retrieve_b200 import ops
+
+    b, n, k = 96, 30_000, 64
+    g = torch.Generator().manual_seed(4)
+    attrs = torch.randint(0, 5, (n, 4, 2), generator=g)
+    attrs[torch.rand(n, 4, 2, generator=g) < 0.3] = -1
+    qa = torch.randint(0, 5, (b, 4), generator=g)
+    qa[torch.rand(b, 4, generator=g) < 0.4] = -1
+    rev = torch.tensor([False, False, True, False])
+    preds = P.from_clause_attrs(qa, rev).to("cuda")
+    q, x = make_int_rows(b, 128, seed=3), make_int_rows(n, 128, seed=4)
+    ids, scores = ops.dense_topk_filtered(q.cuda(), x.cuda(), k, preds.terms, preds.n_terms, "exact",
+                                          attrs.cuda(), None)
+    ref_ids, ref_scores = _oracle(q, x, k, filters.clause_mask(attrs.numpy(), rev.numpy(), qa.numpy()))
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
