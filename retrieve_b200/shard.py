@@ -54,6 +54,20 @@ def merge_topk(ids: Tensor, scores: Tensor, k: int) -> tuple[Tensor, Tensor]:
     return out_i, out_s
 
 
+def exchange_and_merge(ids: Tensor, scores: Tensor, k: int, group=None, merge=None) -> tuple[Tensor, Tensor]:
+    """The exchange step of a row-sharded search: all-gather every rank's local
+    ``[B, k]`` (ids already global) and reduce the ``[W, B, k]`` stack to the
+    global top-k with ``merge`` (default: the CUDA merge kernel). Every rank
+    takes the same collective steps in the same order."""
+    world = dist.get_world_size(group)
+    b, kin = ids.shape
+    all_i = torch.empty((world * b, kin), dtype=ids.dtype, device=ids.device)
+    all_s = torch.empty((world * b, kin), dtype=scores.dtype, device=scores.device)
+    dist.all_gather_into_tensor(all_i, ids.contiguous(), group=group)
+    dist.all_gather_into_tensor(all_s, scores.contiguous(), group=group)
+    return (merge or merge_topk)(all_i.view(world, b, kin), all_s.view(world, b, kin), k)
+
+
 class ShardedDenseTopK:
     """The local shard of a row-sharded dense index plus the exchange step.
 
@@ -76,12 +90,7 @@ class ShardedDenseTopK:
         ids, scores = self.local(query)
         if self.world == 1:
             return ids, scores
-        b = ids.shape[0]
-        all_i = torch.empty((self.world, b, self.k), dtype=ids.dtype, device=ids.device)
-        all_s = torch.empty((self.world, b, self.k), dtype=scores.dtype, device=scores.device)
-        dist.all_gather_into_tensor(all_i, ids, group=self.group)
-        dist.all_gather_into_tensor(all_s, scores, group=self.group)
-        return merge_topk(all_i, all_s, self.k)
+        return exchange_and_merge(ids, scores, self.k, self.group)
 
     def launches_per_search(self, b: int) -> int:
         lib = _lib.lib()
