@@ -1,5 +1,6 @@
 // extern "C" entry points of libretrieve_b200: argument checks, workspace
 // carving and the sequence of kernel launches for each op.
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <string>
@@ -21,6 +22,7 @@ static int fail(int code, const char* msg) {
   set_last_error(msg);
   return code;
 }
+static int fail(int code, const std::string& msg) { return fail(code, msg.c_str()); }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -48,56 +50,132 @@ int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* 
 }
 
 // Shared body of the dense entry points (elem 0 f16, 1 bf16, 2 int8).
+// Threshold shared by the shards of a row-sharded search: seed_vals is the
+// [W, B, k] stack of every shard's rb_dense_seed_sample output and n_total the
+// corpus size over all shards.
+struct SharedSeed {
+  const float* vals;
+  int W;
+  int64_t n_total;
+};
+
+static int dense_check(int elem, const void* queries, const float* q_scale, const void* items, const float* x_scale,
+                       int B, int N, int D, int k, const char* what) {
+  if (B < 0 || N < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, std::string(what) + ": bad B, N or k");
+  if (k > 256) return fail(RB_ERR_UNSUPPORTED, std::string(what) + ": k > 256 is not supported");
+  const int row_bytes = (elem == 2) ? D : 2 * D;
+  if (row_bytes != 128 && row_bytes != 256)
+    return fail(RB_ERR_UNSUPPORTED,
+                std::string(what) + ": rows must be 128 or 256 bytes (D = 64/128 fp16/bf16, 128/256 int8)");
+  if (B > 0 && N > 0) {
+    if (!aligned16(queries) || !aligned16(items)) return fail(RB_ERR_INVALID_ARG, std::string(what) + ": 16-byte alignment");
+    if (elem == 2 && (q_scale == nullptr || x_scale == nullptr || !aligned16(x_scale)))
+      return fail(RB_ERR_INVALID_ARG, std::string(what) + ": scales must be given (item scales 16-byte aligned)");
+  }
+  return RB_OK;
+}
+
+struct DenseWs {
+  uint2* lists;
+  int* counts;
+  float* thresh;
+  int* err;
+};
+
+static DenseWs dense_ws(void* workspace, size_t workspace_bytes, int B, const DensePlan& pl) {
+  DenseWs d;
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  d.lists = reinterpret_cast<uint2*>(w);
+  w += align_up(static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2), 256);
+  d.counts = reinterpret_cast<int*>(w);
+  w += align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
+  d.thresh = reinterpret_cast<float*>(w);
+  d.err = ws_err_word(workspace, workspace_bytes);
+  return d;
+}
+
 static int dense_topk_impl(int elem, const void* queries, const float* q_scale, const void* items,
                            const float* x_scale, int B, int N, int D, int k, int64_t id_offset, int64_t* out_ids,
                            float* out_scores, void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                           const FilterArgs* filter = nullptr) {
-  if (B < 0 || N < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk: bad B, N or k");
-  if (k > 256) return fail(RB_ERR_UNSUPPORTED, "dense_topk: k > 256 is not supported");
-  const int row_bytes = (elem == 2) ? D : 2 * D;
-  if (row_bytes != 128 && row_bytes != 256)
-    return fail(RB_ERR_UNSUPPORTED, "dense_topk: rows must be 128 or 256 bytes (D = 64/128 fp16/bf16, 128/256 int8)");
+                           const FilterArgs* filter = nullptr, const SharedSeed* shared = nullptr) {
+  int rc = dense_check(elem, queries, q_scale, items, x_scale, B, N, D, k, "dense_topk");
+  if (rc != RB_OK) return rc;
   if (B == 0) return RB_OK;
   if (out_ids == nullptr || out_scores == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_topk: null output");
   if (N == 0) {
     fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, stream);
     return cudaGetLastError() == cudaSuccess ? RB_OK : fail(RB_ERR_CUDA, "fill_empty launch failed");
   }
-  if (!aligned16(queries) || !aligned16(items)) return fail(RB_ERR_INVALID_ARG, "dense_topk: 16-byte alignment");
-  if (elem == 2 && (q_scale == nullptr || x_scale == nullptr || !aligned16(x_scale)))
-    return fail(RB_ERR_INVALID_ARG, "dense_topk_i8: scales must be given (item scales 16-byte aligned)");
   const size_t need = dense_workspace_bytes(B, N, k);
   if (workspace == nullptr || workspace_bytes < need) return fail(RB_ERR_WORKSPACE, "dense_topk: workspace too small");
 
   DensePlan pl;
-  dense_plan(B, N, k, pl);
-  uint8_t* w = static_cast<uint8_t*>(workspace);
-  uint2* lists = reinterpret_cast<uint2*>(w);
-  w += align_up(static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2), 256);
-  int* counts = reinterpret_cast<int*>(w);
-  w += align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
-  float* thresh = reinterpret_cast<float*>(w);
-  int* err = ws_err_word(workspace, workspace_bytes);
-  if (cudaMemsetAsync(err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
+  dense_plan(B, N, k, pl, shared ? shared->n_total : N);
+  const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
+  if (cudaMemsetAsync(d.err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
 
   ProfileEvents& pe = profile_events();
   const float* seed = nullptr;
-  if (pl.sample_stride > 0) {
-    float* chunk_max = reinterpret_cast<float*>(lists);  // dead before the full pass writes lists
-    int rc = dense_scan_pass(1, elem, queries, items, B, N, D, pl, k, nullptr, lists, counts, chunk_max, err, stream,
-                             q_scale, x_scale, filter);
+  if (shared != nullptr) {
+    // k-th largest of the union of the shards' samples (a [W, B, k] stack)
+    rc = row_kth_lower_bound(shared->vals, B, k, k, shared->W, static_cast<int64_t>(B) * k, k, d.thresh, nullptr,
+                             stream);
+    if (rc != RB_OK) return rc;
+    seed = d.thresh;
+  } else if (pl.sample_stride > 0) {
+    float* chunk_max = reinterpret_cast<float*>(d.lists);  // dead before the full pass writes lists
+    rc = dense_scan_pass(1, elem, queries, items, B, N, D, pl, k, nullptr, d.lists, d.counts, chunk_max, d.err,
+                         stream, q_scale, x_scale, filter);
     if (rc != RB_OK) return rc;
     const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
-    rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, k, thresh, stream);
+    rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, k, d.thresh, nullptr, stream);
     if (rc != RB_OK) return rc;
-    seed = thresh;
+    seed = d.thresh;
   }
   if (pe.start) cudaEventRecord(pe.start, stream);
-  int rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, lists, counts, nullptr, err, stream,
-                           q_scale, x_scale, filter);
+  rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, d.lists, d.counts, nullptr, d.err, stream,
+                       q_scale, x_scale, filter);
   if (rc != RB_OK) return rc;
   if (pe.stop) cudaEventRecord(pe.stop, stream);
-  return merge_lists(lists, counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
+  return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
+}
+
+int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
+                         int64_t n_total, float* out_vals, void* workspace, size_t workspace_bytes, void* stream_) {
+  if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_seed_sample: dtype must be f16 or bf16");
+  const int elem = dtype == RB_BF16 ? 1 : 0;
+  int rc = dense_check(elem, queries, nullptr, items, nullptr, B, N, D, k, "dense_seed_sample");
+  if (rc != RB_OK) return rc;
+  if (B == 0) return RB_OK;
+  if (out_vals == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_seed_sample: null output");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const size_t need = dense_workspace_bytes(B, N, k);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(RB_ERR_WORKSPACE, "dense_seed_sample: workspace too small");
+  DensePlan pl;
+  dense_plan(B, N, k, pl, std::max<int64_t>(n_total, N));
+  const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
+  if (N == 0 || pl.sample_stride == 0) {
+    // nothing sampled on this shard: k times -inf per query
+    return row_kth_lower_bound(nullptr, B, 0, 0, 1, 0, k, d.thresh, out_vals, stream);
+  }
+  if (cudaMemsetAsync(d.err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
+  float* chunk_max = reinterpret_cast<float*>(d.lists);
+  rc = dense_scan_pass(1, elem, queries, items, B, N, D, pl, k, nullptr, d.lists, d.counts, chunk_max, d.err, stream,
+                       nullptr, nullptr, nullptr);
+  if (rc != RB_OK) return rc;
+  const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
+  return row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, k, d.thresh, out_vals, stream);
+}
+
+int rb_dense_topk_seeded(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
+                         int64_t id_offset, int64_t n_total, const float* seed_vals, int W, int64_t* out_ids,
+                         float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk_seeded: dtype must be f16 or bf16");
+  if (seed_vals == nullptr || W < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk_seeded: seed values missing");
+  const SharedSeed shared{seed_vals, W, std::max<int64_t>(n_total, N)};
+  return dense_topk_impl(dtype == RB_BF16 ? 1 : 0, queries, nullptr, items, nullptr, B, N, D, k, id_offset, out_ids,
+                         out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, &shared);
 }
 
 int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int64_t id_offset,
@@ -152,7 +230,7 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
     return RB_OK;
   }
   DensePlan pl;
-  dense_plan(B, N, k, pl);
+  dense_plan(B, N, k, pl, N);
   *n_launches = (pl.sample_stride > 0) ? 4 : 2;
   return RB_OK;
 }

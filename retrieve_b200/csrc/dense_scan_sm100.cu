@@ -81,7 +81,7 @@ __device__ __forceinline__ void split_range(int split, int n_splits, int pass_ti
 // For int8 (ELEM 2) the registers first hold int32 dots, turned here into the
 // exact fp32 score (fp32(dot) * q_scale) * item_scale, left to right as the
 // reference dequantizes (ops/official/adapter.py:338-367).
-template <int MODE, int NCH, int ELEM = 1>
+template <int MODE, int NCH, int ELEM, bool FILT>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list) {
@@ -121,16 +121,21 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
       for (int j = 0; j < 32; ++j)
         if (row0 + ch * 32 + j >= static_cast<uint32_t>(p.N)) r[ch][j] = 0x7fc00000u;
   }
-  if (p.filter.mode != kFilterNone && valid_q) {
-    if constexpr (MODE == 1) {
-      // sampling pass: items that fail the predicate do not count
-#pragma unroll 1
-      for (int ch = 0; ch < NCH; ++ch)
-#pragma unroll 4
-        for (int j = 0; j < 32; ++j) {
-          const uint32_t id = row0 + ch * 32 + j;
-          if (id < static_cast<uint32_t>(p.N) && !pred_pass(p.filter, q, id)) r[ch][j] = 0x7fc00000u;
-        }
+  if constexpr (FILT && MODE == 1) {
+    if (valid_q) {
+      // sampling pass: items that fail the predicate do not count. The
+      // predicate is evaluated into a bit mask first, so that every index into
+      // r stays a compile-time constant and r stays in registers.
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const uint32_t id0 = row0 + ch * 32;
+        const uint32_t n_in = id0 >= static_cast<uint32_t>(p.N) ? 0u : min(32u, static_cast<uint32_t>(p.N) - id0);
+        const uint32_t valid = n_in == 32 ? 0xffffffffu : ((1u << n_in) - 1u);
+        const uint32_t pm = pred_pass_bits(p.filter, q, id0, valid);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (!((pm >> j) & 1u)) r[ch][j] = 0x7fc00000u;
+      }
     }
   }
   if constexpr (MODE == 1) {
@@ -141,31 +146,35 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         p.chunk_max[static_cast<size_t>(q) * p.chunk_stride + chunk0 + ch] = max32(r[ch]);
     }
   } else {
-    // Filter on the FMA pipe: s - thresh is negative exactly when s < thresh
-    // (a difference of floats that is >= 0 never rounds below 0), so the sign
-    // bit of the AND over a chunk is set iff no score of the chunk passes.
+    // Threshold filter on the FMA pipe (paired fp32 subtracts) and the ALU
+    // (AND tree): the sign bit of sg[ch] is set iff no score of chunk ch
+    // passes; then the exact append of the chunks that may pass.
+    const uint64_t tt = pack_pair(thresh);
     uint32_t sg[NCH];
     uint32_t all = 0xffffffffu;
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      sg[ch] = chunk_all_below(r[ch], thresh);
+      sg[ch] = chunk_all_below(r[ch], tt);
       all &= sg[ch];
     }
     if (__any_sync(RB_FULL_MASK, valid_q && !(all >> 31))) {
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         if (valid_q && !(sg[ch] >> 31)) {
-          if (p.filter.mode == kFilterNone)
+          if constexpr (!FILT) {
             append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
-          else
-            append_chunk_bits_pred(list, count, thresh, r[ch], row0 + ch * 32, p.filter, q);
+          } else {
+            const uint32_t id0 = row0 + ch * 32;
+            const uint32_t pm = pred_pass_bits(p.filter, q, id0, chunk_pass_bits(r[ch], thresh));
+            append_chunk_mask(list, count, r[ch], pm, id0);
+          }
         }
       }
     }
   }
 }
 
-template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL>
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 __global__ void __launch_bounds__(64 + 128 * NG, 1)
     dense_scan_kernel(const __grid_constant__ DenseScanParams p) {
   using L = DenseSmemLayout<KB, NG, STAGES>;
@@ -378,7 +387,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        process_chunks<MODE, 4, ELEM>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM, FILT>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -426,7 +435,7 @@ struct Dense2SmLayout {
   static constexpr int kTotal = kA + kB + kHist + kBar + kMisc + 1024;
 };
 
-template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL>
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     dense_scan_2sm_kernel(const __grid_constant__ DenseScanParams p) {
   using L = Dense2SmLayout<KB, NG, STAGES>;
@@ -667,7 +676,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
-        process_chunks<MODE, 4, ELEM>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM, FILT>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
         if (++acc == kAcc) {
           acc = 0;
           acc_phase ^= 1;
@@ -736,20 +745,20 @@ static bool make_tmap(CUtensorMap* map, const void* base, int elem, uint64_t row
   return r == CUDA_SUCCESS;
 }
 
-template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL>
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaStream_t stream) {
   using L = DenseSmemLayout<KB, NG, STAGES>;
-  auto kern = dense_scan_kernel<MODE, ELEM, KB, NG, STAGES, EPL>;
+  auto kern = dense_scan_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
   kern<<<grid, 64 + 128 * NG, L::kTotal, stream>>>(prm);
   return cudaGetLastError();
 }
 
-template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL>
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 static cudaError_t launch_dense_scan_2sm(const DenseScanParams& prm, int n_pairs, cudaStream_t stream) {
   using L = Dense2SmLayout<KB, NG, STAGES>;
-  auto kern = dense_scan_2sm_kernel<MODE, ELEM, KB, NG, STAGES, EPL>;
+  auto kern = dense_scan_2sm_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
   kern<<<2 * n_pairs, 64 + 128 * NG, L::kTotal, stream>>>(prm);
@@ -761,7 +770,7 @@ static int max_pairs() {
   static int n = 0;
   if (n == 0) {
     using L = Dense2SmLayout<2, 2, 8>;
-    auto kern = dense_scan_2sm_kernel<0, 1, 2, 2, 8, 16>;
+    auto kern = dense_scan_2sm_kernel<0, 1, 2, 2, 8, 16, false>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74, 1, 1);
@@ -809,7 +818,7 @@ int num_sms() {
   return n;
 }
 
-void dense_plan(int B, int N, int k, DensePlan& pl) {
+void dense_plan(int B, int N, int k, DensePlan& pl, int64_t n_total) {
   // B > 128: 2-SM kernel, 256 queries per group, 1 or 2 groups per CTA pair.
   pl.two_sm = B > kQTile;
   if (pl.two_sm) {
@@ -825,13 +834,24 @@ void dense_plan(int B, int N, int k, DensePlan& pl) {
   }
   pl.cap = list_cap(k);
   pl.tiles = (N + kTileItems - 1) / kTileItems;
-  // Optional sampling pass over every kSampleStride-th tile: it records the
-  // max of each 32-item chunk; the k-th largest chunk max is a lower bound on
-  // the k-th best score of the corpus (k distinct items reach it) and seeds the
-  // full pass. Taken when the sample holds at least 4k chunks.
+  // Optional sampling pass over every s-th tile: it records the max of each
+  // 32-item chunk; the k-th largest chunk max is a lower bound on the k-th best
+  // score of the corpus (k distinct items reach it) and seeds the full pass.
+  // That bound sits near rank k * s of the corpus, so the full pass appends
+  // about k * s candidates per query: s is the sparsest stride (at most
+  // kSampleStride) that keeps those at no more than 0.1 per query row and
+  // 128-item tile (over a corpus of n_total items: the union of every shard's
+  // sample when the seed is shared) and still samples at least 4k chunks.
   pl.sample_stride = 0;
-  const int64_t sample_tiles = (pl.tiles + kSampleStride - 1) / kSampleStride;
-  if (sample_tiles * 4 >= 4 * static_cast<int64_t>(k)) pl.sample_stride = kSampleStride;
+  const int64_t n_scale = std::max<int64_t>(n_total, N);
+  for (int s = kSampleStride; s >= 1; s >>= 1) {
+    const int64_t chunks = (pl.tiles + s - 1) / s * 4;
+    const bool dense_enough = static_cast<double>(k) * s * kTileItems <= 0.1 * static_cast<double>(n_scale);
+    if (chunks >= 4 * static_cast<int64_t>(k) && (dense_enough || s == 1)) {
+      pl.sample_stride = s;
+      break;
+    }
+  }
 }
 
 size_t dense_chunk_stride(const DensePlan& pl) {
@@ -841,7 +861,7 @@ size_t dense_chunk_stride(const DensePlan& pl) {
 
 size_t dense_workspace_bytes(int B, int N, int k) {
   DensePlan pl;
-  dense_plan(B, N, k, pl);
+  dense_plan(B, N, k, pl, N);
   size_t lists = static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2);
   size_t counts = static_cast<size_t>(B) * pl.n_lists * sizeof(int);
   size_t th = 2 * static_cast<size_t>(B) * sizeof(float);
@@ -855,7 +875,8 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
                     cudaStream_t stream, const float* q_scale, const float* x_scale, const FilterArgs* filter) {
   DenseScanParams prm;
   std::memset(&prm, 0, sizeof(prm));
-  if (filter != nullptr) prm.filter = *filter;
+  const bool filtered = filter != nullptr && filter->mode != kFilterNone;
+  if (filtered) prm.filter = *filter;
   prm.q_scale = q_scale;
   prm.x_scale = x_scale;
   const int eb = (elem == 2) ? 1 : 2;
@@ -888,15 +909,16 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
   bool handled = false;
   if (pl.two_sm) {
     const int n_pairs = std::min(n_tasks, max_pairs());
-#define RB_DISPATCH2(ELEM, KB, NG, ST)                                                              \
-  if (!handled && elem == ELEM && kb == KB && pl.ng == NG) {                                         \
+#define RB_DISPATCH2F(ELEM, KB, NG, ST, F)                                                          \
+  if (!handled && elem == ELEM && kb == KB && pl.ng == NG && filtered == F) {                        \
     if (mode == 1)                                                                                   \
-      e = launch_dense_scan_2sm<1, ELEM, KB, NG, ST, 8>(prm, n_pairs, stream);                       \
+      e = launch_dense_scan_2sm<1, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream);                    \
     else                                                                                             \
-      e = (pl.cap <= 256) ? launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 8>(prm, n_pairs, stream)      \
-                          : launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 16>(prm, n_pairs, stream);    \
+      e = (pl.cap <= 256) ? launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream)   \
+                          : launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 16, F>(prm, n_pairs, stream); \
     handled = true;                                                                                  \
   }
+#define RB_DISPATCH2(ELEM, KB, NG, ST) RB_DISPATCH2F(ELEM, KB, NG, ST, false)
     RB_DISPATCH2(0, 1, 1, 12)
     RB_DISPATCH2(0, 1, 2, 12)
     RB_DISPATCH2(0, 2, 1, 8)
@@ -909,24 +931,40 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
     RB_DISPATCH2(2, 1, 2, 12)
     RB_DISPATCH2(2, 2, 1, 8)
     RB_DISPATCH2(2, 2, 2, 8)
+    // attribute-filtered variants (fp16 / bf16 only)
+    RB_DISPATCH2F(0, 1, 1, 12, true)
+    RB_DISPATCH2F(0, 1, 2, 12, true)
+    RB_DISPATCH2F(0, 2, 1, 8, true)
+    RB_DISPATCH2F(0, 2, 2, 8, true)
+    RB_DISPATCH2F(1, 1, 1, 12, true)
+    RB_DISPATCH2F(1, 1, 2, 12, true)
+    RB_DISPATCH2F(1, 2, 1, 8, true)
+    RB_DISPATCH2F(1, 2, 2, 8, true)
+#undef RB_DISPATCH2F
 #undef RB_DISPATCH2
   } else {
     const int grid = std::min(n_tasks, num_sms());
-#define RB_DISPATCH(ELEM, KB, NG, ST)                                                         \
-  if (!handled && elem == ELEM && kb == KB && pl.ng == NG) {                                   \
+#define RB_DISPATCHF(ELEM, KB, NG, ST, F)                                                     \
+  if (!handled && elem == ELEM && kb == KB && pl.ng == NG && filtered == F) {                  \
     if (mode == 1)                                                                             \
-      e = launch_dense_scan<1, ELEM, KB, NG, ST, 8>(prm, grid, stream);                        \
+      e = launch_dense_scan<1, ELEM, KB, NG, ST, 8, F>(prm, grid, stream);                     \
     else                                                                                       \
-      e = (pl.cap <= 256) ? launch_dense_scan<0, ELEM, KB, NG, ST, 8>(prm, grid, stream)       \
-                          : launch_dense_scan<0, ELEM, KB, NG, ST, 16>(prm, grid, stream);     \
+      e = (pl.cap <= 256) ? launch_dense_scan<0, ELEM, KB, NG, ST, 8, F>(prm, grid, stream)    \
+                          : launch_dense_scan<0, ELEM, KB, NG, ST, 16, F>(prm, grid, stream);  \
     handled = true;                                                                            \
   }
+#define RB_DISPATCH(ELEM, KB, NG, ST) RB_DISPATCHF(ELEM, KB, NG, ST, false)
     RB_DISPATCH(0, 1, 1, 8)
     RB_DISPATCH(0, 2, 1, 4)
     RB_DISPATCH(1, 1, 1, 8)
     RB_DISPATCH(1, 2, 1, 4)
     RB_DISPATCH(2, 1, 1, 8)
     RB_DISPATCH(2, 2, 1, 4)
+    RB_DISPATCHF(0, 1, 1, 8, true)
+    RB_DISPATCHF(0, 2, 1, 4, true)
+    RB_DISPATCHF(1, 1, 1, 8, true)
+    RB_DISPATCHF(1, 2, 1, 4, true)
+#undef RB_DISPATCHF
 #undef RB_DISPATCH
   }
   if (!handled) {

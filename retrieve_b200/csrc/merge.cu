@@ -213,38 +213,67 @@ __global__ void __launch_bounds__(kMergeThreads) merge_lists_kernel(const uint2*
 
 // Lower bound on the k-th largest value of each row (22 leading key bits
 // exact, the rest rounded down). NaN counts as -inf. Rows shorter than k: -inf.
-__global__ void __launch_bounds__(kMergeThreads) row_kth_kernel(const float* __restrict__ vals, int n, int stride,
-                                                                int k, float* __restrict__ out) {
+// Row q of the input is nseg segments of n floats, segment j at
+// vals + j * seg_stride + q * stride (nseg = 1: a plain row-major matrix;
+// nseg = W: the [W, B, k] stack of every shard's sample values). out[q] is a
+// lower bound on the k-th largest value of the row: the 22-bit prefix of the
+// order key of the k-th largest, as a float (-inf when the row holds fewer
+// than k values). NaN ranks lowest. With out_vals, also writes k values of the
+// row that are >= out[q] (any k of them; -inf pads a row of fewer than k).
+__global__ void __launch_bounds__(kMergeThreads) row_kth_kernel(const float* __restrict__ vals, int n, int64_t stride,
+                                                                int nseg, int64_t seg_stride, int k,
+                                                                float* __restrict__ out,
+                                                                float* __restrict__ out_vals) {
   __shared__ SelectShared sh;
   const int q = blockIdx.x;
-  const float* row = vals + static_cast<size_t>(q) * stride;
-  if (n < k) {
-    if (threadIdx.x == 0) out[q] = -INFINITY;
-    return;
-  }
+  const int total = n * nseg;
+  auto value_at = [&](int i) -> float {
+    const int seg = i / n;
+    return vals[seg * seg_stride + static_cast<int64_t>(q) * stride + (i - seg * n)];
+  };
   uint32_t prefix = 0, mask = 0;
-  uint32_t need = static_cast<uint32_t>(k);
-  for (int shift = 21; shift >= 10; shift -= 11) {
-    for (int i = threadIdx.x; i < kBins; i += kMergeThreads) sh.hist[i] = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += kMergeThreads) {
-      const float v = row[i];
-      const uint32_t key = isnan(v) ? 0u : f2ord(v);
-      if ((key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & 0x7ffu], 1u);
+  if (total >= k) {
+    uint32_t need = static_cast<uint32_t>(k);
+    for (int shift = 21; shift >= 10; shift -= 11) {
+      for (int i = threadIdx.x; i < kBins; i += kMergeThreads) sh.hist[i] = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < total; i += kMergeThreads) {
+        const float v = value_at(i);
+        const uint32_t key = isnan(v) ? 0u : f2ord(v);
+        if ((key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & 0x7ffu], 1u);
+      }
+      __syncthreads();
+      block_find_digit_n<kBins / kMergeThreads>(sh, need);
+      prefix |= sh.digit << shift;
+      mask |= 0x7ffu << shift;
+      need -= sh.above;
+      __syncthreads();
     }
-    __syncthreads();
-    block_find_digit_n<kBins / kMergeThreads>(sh, need);
-    prefix |= sh.digit << shift;
-    mask |= 0x7ffu << shift;
-    need -= sh.above;
-    __syncthreads();
   }
-  if (threadIdx.x == 0) out[q] = (prefix <= f2ord_bits(0xff800000u)) ? -INFINITY : ord2f(prefix);
+  const float bound = (prefix <= f2ord_bits(0xff800000u)) ? -INFINITY : ord2f(prefix);
+  if (threadIdx.x == 0) {
+    out[q] = bound;
+    sh.n_out = 0;
+  }
+  if (out_vals == nullptr) return;
+  __syncthreads();
+  float* dst = out_vals + static_cast<int64_t>(q) * k;
+  for (int i = threadIdx.x; i < total; i += kMergeThreads) {
+    const float v = value_at(i);
+    const uint32_t key = isnan(v) ? 0u : f2ord(v);
+    if (key >= prefix) {
+      const uint32_t slot = atomicAdd(&sh.n_out, 1u);
+      if (slot < static_cast<uint32_t>(k)) dst[slot] = v;
+    }
+  }
+  __syncthreads();
+  for (int i = static_cast<int>(sh.n_out) + threadIdx.x; i < k; i += kMergeThreads) dst[i] = -INFINITY;
 }
 
-int row_kth_lower_bound(const float* vals, int B, int n, int stride, int k, float* out, cudaStream_t stream) {
+int row_kth_lower_bound(const float* vals, int B, int n, int64_t stride, int nseg, int64_t seg_stride, int k,
+                        float* out, float* out_vals, cudaStream_t stream) {
   if (B == 0) return RB_OK;
-  row_kth_kernel<<<B, kMergeThreads, 0, stream>>>(vals, n, stride, k, out);
+  row_kth_kernel<<<B, kMergeThreads, 0, stream>>>(vals, n, stride, nseg, seg_stride, k, out, out_vals);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_last_error(cudaGetErrorString(e));

@@ -27,7 +27,7 @@ struct DensePlan {
   int sample_stride;  // 0: no sampling pass; else the tile stride of the sample
 };
 
-void dense_plan(int B, int N, int k, DensePlan& pl);
+void dense_plan(int B, int N, int k, DensePlan& pl, int64_t n_total = 0);
 size_t dense_workspace_bytes(int B, int N, int k);
 int num_sms();
 size_t dense_chunk_stride(const DensePlan& pl);
@@ -38,7 +38,8 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
                     const FilterArgs* filter = nullptr);
 // Per row of vals [B, n] (row stride `stride`): a lower bound on the k-th
 // largest value (exact to 22 leading key bits), -inf when n < k.
-int row_kth_lower_bound(const float* vals, int B, int n, int stride, int k, float* out, cudaStream_t stream);
+int row_kth_lower_bound(const float* vals, int B, int n, int64_t stride, int nseg, int64_t seg_stride, int k,
+                        float* out, float* out_vals, cudaStream_t stream);
 
 // Merge of per-(query, split) candidate lists into the final sorted top-k.
 int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,

@@ -169,7 +169,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
+    // several tries between the abort / time checks keep a spinning warp's
+    // issue slots for the warps that share its scheduler
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait(addr, parity)) return true;
     if (*abort) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }

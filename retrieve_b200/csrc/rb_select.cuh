@@ -151,20 +151,51 @@ __device__ __noinline__ void warp_compact_lists(uint2* list, int& count, float& 
   }
 }
 
-// Appends the passing entries of a 32-item chunk to the calling lane's list.
-// Scores s[j] for items id0 + j; only ids < n_valid count.
-__device__ __forceinline__ void append_chunk(uint2* list, int& count, float thresh, const float (&s)[32],
-                                             uint32_t id0, uint32_t n_valid) {
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (s[j] >= thresh && id0 + j < n_valid) {
-      list[count] = make_uint2(__float_as_uint(s[j]), id0 + j);
-      ++count;
-    }
+// Of the items id0 + j with bit j set in sel, those that pass query q's
+// attribute predicate (bit j of the result). Touches no register array.
+__device__ __forceinline__ uint32_t pred_pass_bits(const FilterArgs& f, int q, uint32_t id0, uint32_t sel) {
+  uint32_t out = 0;
+  while (sel) {
+    const int j = __ffs(sel) - 1;
+    sel &= sel - 1;
+    if (pred_pass(f, q, id0 + j)) out |= 1u << j;
   }
+  return out;
 }
 
-// Same, with the scores still as raw fp32 bit patterns (as read from TMEM).
+// (t, t) as the 64-bit operand of the paired fp32 instructions.
+__device__ __forceinline__ uint64_t pack_pair(float t) {
+  uint64_t tt;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(tt) : "r"(__float_as_uint(t)));
+  return tt;
+}
+
+// (s0 - t, s1 - t) as bit patterns: one paired fp32 subtract, rounded to
+// nearest like two scalar subtracts.
+__device__ __forceinline__ void sub_pair(uint32_t s0, uint32_t s1, uint64_t tt, uint32_t& d0, uint32_t& d1) {
+  uint64_t x, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "r"(s0), "r"(s1));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(tt));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(d0), "=r"(d1) : "l"(d));
+}
+
+// AND over a chunk of the bit patterns of (s[j] - t): s - t is negative
+// exactly when s < t (a difference of floats that is >= 0 never rounds below
+// 0), so the sign bit of the result is set iff every s[j] < t. NaN scores count
+// as passing here and are rejected by the exact test of the append.
+__device__ __forceinline__ uint32_t chunk_all_below(const uint32_t (&s)[32], uint64_t tt) {
+  uint32_t d[32];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) sub_pair(s[2 * i], s[2 * i + 1], tt, d[2 * i], d[2 * i + 1]);
+  uint32_t a[11];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) a[i] = d[3 * i] & d[3 * i + 1] & d[3 * i + 2];
+  a[10] = d[30] & d[31];
+  const uint32_t b0 = a[0] & a[1] & a[2], b1 = a[3] & a[4] & a[5], b2 = a[6] & a[7] & a[8];
+  return b0 & b1 & b2 & a[9] & a[10];
+}
+
+// Appends the entries s[j] >= thresh of a 32-item chunk (items id0 + j).
 // Padding slots hold NaN, which never passes.
 __device__ __forceinline__ void append_chunk_bits(uint2* list, int& count, float thresh, const uint32_t (&s)[32],
                                                   uint32_t id0) {
@@ -179,33 +210,27 @@ __device__ __forceinline__ void append_chunk_bits(uint2* list, int& count, float
   count = static_cast<int>(w - list);
 }
 
-// Same, appending only the items that pass query q's attribute predicate.
-__device__ __forceinline__ void append_chunk_bits_pred(uint2* list, int& count, float thresh, const uint32_t (&s)[32],
-                                                       uint32_t id0, const FilterArgs& f, int q) {
+// Bit j set iff s[j] >= thresh. Every index into s is a compile-time constant,
+// so the score array stays in registers.
+__device__ __forceinline__ uint32_t chunk_pass_bits(const uint32_t (&s)[32], float thresh) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) m |= static_cast<uint32_t>(__uint_as_float(s[j]) >= thresh) << j;
+  return m;
+}
+
+// Appends the entries of a 32-item chunk whose bit is set in mask.
+__device__ __forceinline__ void append_chunk_mask(uint2* list, int& count, const uint32_t (&s)[32], uint32_t mask,
+                                                  uint32_t id0) {
   uint2* w = list + count;
-#pragma unroll 4
+#pragma unroll
   for (int j = 0; j < 32; ++j) {
-    if (__uint_as_float(s[j]) >= thresh && pred_pass(f, q, id0 + j)) {
+    if ((mask >> j) & 1u) {
       *w = make_uint2(s[j], id0 + j);
       ++w;
     }
   }
   count = static_cast<int>(w - list);
-}
-
-// AND over a chunk of the bit patterns of (s[j] - thresh): the sign bit of the
-// result is set iff every s[j] < thresh (NaN scores count as passing here and
-// are rejected by the exact test of the append).
-__device__ __forceinline__ uint32_t chunk_all_below(const uint32_t (&s)[32], float thresh) {
-  uint32_t d[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) d[j] = __float_as_uint(__uint_as_float(s[j]) - thresh);
-  uint32_t a[11];
-#pragma unroll
-  for (int i = 0; i < 10; ++i) a[i] = d[3 * i] & d[3 * i + 1] & d[3 * i + 2];
-  a[10] = d[30] & d[31];
-  const uint32_t b0 = a[0] & a[1] & a[2], b1 = a[3] & a[4] & a[5], b2 = a[6] & a[7] & a[8];
-  return b0 & b1 & b2 & a[9] & a[10];
 }
 
 // Max of 32 fp32 values (raw bits) as a balanced tree (depth 5).

@@ -84,6 +84,69 @@ def _dense_topk_impl(query: Tensor, item_embs: Tensor, k: int, id_offset: int = 
     return ids, scores
 
 
+def dense_workspace(query: Tensor, item_shard: Tensor, k: int) -> Tensor:
+    """Device workspace for the dense top-k entry points on this shard."""
+    b, d = query.shape
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(
+        _lib.lib().rb_dense_topk_workspace_size(b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k,
+                                                ctypes.byref(nbytes)),
+        "dense_topk",
+    )
+    return torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=query.device)
+
+
+def dense_seed_sample(query: Tensor, item_shard: Tensor, k: int, n_total: int, ws: Tensor | None = None) -> Tensor:
+    """Per query, k sampled chunk maxima of this shard (``[B, k]`` fp32) for the
+    threshold shared by all shards (C-ABI ``rb_dense_seed_sample``)."""
+    _require_cuda(query, item_shard)
+    check_contiguous(item_shard=item_shard)
+    q = query.to(item_shard.dtype).contiguous()
+    b, d = q.shape
+    dev = q.device
+    out = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return out
+    ws = dense_workspace(q, item_shard, k) if ws is None else ws
+    with torch.cuda.device(dev):
+        rc = _lib.lib().rb_dense_seed_sample(
+            _ptr(q), _ptr(item_shard), b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k, int(n_total),
+            _ptr(out), _ptr(ws), ws.numel(), _stream_ptr(dev),
+        )
+    _lib.check(rc, "dense_seed_sample")
+    return out
+
+
+def dense_topk_seeded(
+    query: Tensor, item_shard: Tensor, k: int, id_offset: int, n_total: int, seed_vals: Tensor,
+    ws: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:
+    """``dense_topk_sharded`` with the full pass seeded by the union of every
+    shard's ``dense_seed_sample`` output (``seed_vals [W, B, k]`` fp32; C-ABI
+    ``rb_dense_topk_seeded``). May return fewer than k real entries per row
+    (``-1`` / ``-inf``); the merge over all shards is the exact global top-k."""
+    _require_cuda(query, item_shard)
+    check_contiguous(item_shard=item_shard, seed_vals=seed_vals)
+    q = query.to(item_shard.dtype).contiguous()
+    b, d = q.shape
+    if seed_vals.dim() != 3 or seed_vals.shape[1:] != (b, k) or seed_vals.dtype != torch.float32:
+        raise ValueError("seed_vals must be [W, B, k] float32")
+    dev = q.device
+    ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return ids, scores
+    ws = dense_workspace(q, item_shard, k) if ws is None else ws
+    with torch.cuda.device(dev):
+        rc = _lib.lib().rb_dense_topk_seeded(
+            _ptr(q), _ptr(item_shard), b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k, int(id_offset),
+            int(n_total), _ptr(seed_vals), seed_vals.shape[0], _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(),
+            _stream_ptr(dev),
+        )
+    _lib.check(rc, "dense_topk_seeded")
+    return ids, scores
+
+
 @torch.library.custom_op("retrieve::dense_topk", mutates_args=(), device_types="cuda")
 def dense_topk(query: Tensor, item_embs: Tensor, k: int) -> tuple[Tensor, Tensor]:
     """Fused ``query @ item_embs.T`` (fp32 accumulation on the tensor cores) +

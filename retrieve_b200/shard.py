@@ -69,34 +69,67 @@ def exchange_and_merge(ids: Tensor, scores: Tensor, k: int, group=None, merge=No
 
 
 class ShardedDenseTopK:
-    """The local shard of a row-sharded dense index plus the exchange step.
+    """The local shard of a row-sharded dense index plus the exchange steps.
 
     ``item_shard`` is this rank's ``[n_r, D]`` fp16/bf16 rows (contiguous) and
-    ``id_offset`` their first global id. ``search(query)`` returns the global
-    ``(ids [B, k], scores [B, k])`` on every rank."""
+    ``id_offset`` their first global id; ``n_total`` is the corpus size over all
+    ranks (summed over the group when not given: a collective at construction).
+    ``search(query)`` returns the global ``(ids [B, k], scores [B, k])`` on every
+    rank. With more than one rank the threshold seed is shared: every rank
+    samples its shard (``dense_seed_sample``), one all-gather brings the samples
+    together, and every rank's full pass starts from the k-th largest value of
+    their union — the seed one GPU would take over the whole corpus — so each
+    shard appends about 1/W of the candidates a shard-local seed would."""
 
-    def __init__(self, item_shard: Tensor, id_offset: int, k: int, group=None) -> None:
+    def __init__(self, item_shard: Tensor, id_offset: int, k: int, group=None, n_total: int | None = None) -> None:
         ops.check_contiguous(item_shard=item_shard)
         self.items = item_shard
         self.id_offset = int(id_offset)
         self.k = int(k)
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if n_total is None:
+            n_total = item_shard.shape[0]
+            if self.world > 1:
+                t = torch.tensor([n_total], dtype=torch.int64, device=item_shard.device)
+                dist.all_reduce(t, group=group)
+                n_total = int(t.item())
+        self.n_total = int(n_total)
+        self._ws: Tensor | None = None
 
     def local(self, query: Tensor) -> tuple[Tensor, Tensor]:
         return ops.dense_topk_sharded(query, self.items, self.k, self.id_offset)
 
+    def _workspace(self, query: Tensor) -> Tensor:
+        need = ops.dense_workspace(query, self.items, self.k).numel()
+        if self._ws is None or self._ws.numel() < need or self._ws.device != query.device:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=query.device)
+        return self._ws
+
     def search(self, query: Tensor) -> tuple[Tensor, Tensor]:
-        ids, scores = self.local(query)
         if self.world == 1:
-            return ids, scores
+            return self.local(query)
+        ws = self._workspace(query)
+        vals = ops.dense_seed_sample(query, self.items, self.k, self.n_total, ws)
+        b = vals.shape[0]
+        gathered = torch.empty((self.world * b, self.k), dtype=vals.dtype, device=vals.device)
+        dist.all_gather_into_tensor(gathered, vals, group=self.group)
+        ids, scores = ops.dense_topk_seeded(
+            query, self.items, self.k, self.id_offset, self.n_total, gathered.view(self.world, b, self.k), ws
+        )
         return exchange_and_merge(ids, scores, self.k, self.group)
 
     def launches_per_search(self, b: int) -> int:
+        """Kernels of this library one search launches (NCCL's not counted)."""
         lib = _lib.lib()
         n = ctypes.c_int(0)
         _lib.check(
             lib.rb_dense_topk_launches(b, self.items.shape[0], self.items.shape[1], 1, self.k, ctypes.byref(n)),
             "launches",
         )
-        return n.value + (2 if self.world > 1 else 0)
+        if self.world == 1:
+            return n.value
+        sampled = n.value == 4
+        # sample pass + row select (or the -inf fill), union select, full pass,
+        # list merge, then the two kernels of the cross-shard merge
+        return (2 if sampled else 1) + 1 + 2 + 2

@@ -1,0 +1,83 @@
+"""Row-sharded search with the threshold seed shared by all shards.
+
+The W shards of a corpus run on one GPU here, one after the other, through
+exactly the calls a rank makes (``dense_seed_sample`` on its shard, the [W, B, k]
+stack an all-gather would build, ``dense_topk_seeded`` on its shard, then the
+cross-shard ``merge_topk``). An item's score does not depend on which shard
+scores it, so the merged result must equal single-call ``dense_topk`` over the
+whole corpus bit for bit — ids and scores, ties to the lower global id. The
+multi-rank exchange itself (NCCL / gloo all-gather) is covered by
+tests/test_shard_gloo.py on CPU.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from retrieve_b200 import ops
+from retrieve_b200.shard import merge_topk, shard_bounds
+from tests.helpers import assert_topk_exact, make_int_rows, mixture_rows
+
+pytestmark = pytest.mark.gpu
+
+
+def _sharded(q, x, k, bounds):
+    n_total = x.shape[0]
+    shards = [x[lo:hi].contiguous() for lo, hi in bounds]
+    samples = torch.stack([ops.dense_seed_sample(q, s, k, n_total) for s in shards])
+    outs = [
+        ops.dense_topk_seeded(q, s, k, lo, n_total, samples) for s, (lo, _) in zip(shards, bounds)
+    ]
+    ids = torch.stack([o[0] for o in outs])
+    scores = torch.stack([o[1] for o in outs])
+    return merge_topk(ids, scores, k)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("b,n,k", [(300, 400_003, 100), (1024, 1_000_000, 100), (96, 150_001, 37)])
+def test_shared_seed_equals_single_call_integer(world, b, n, k):
+    q = make_int_rows(b, 128, seed=11, device="cuda")
+    x = make_int_rows(n, 128, seed=12, device="cuda")
+    ref_i, ref_s = ops.dense_topk(q, x, k)
+    ids, scores = _sharded(q, x, k, [shard_bounds(n, world, r) for r in range(world)])
+    torch.cuda.synchronize()
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_shared_seed_equals_single_call_mixture(world):
+    # the benchmark's corpus family: clustered, so candidates concentrate
+    b, n, k = 1024, 2_000_000, 100
+    x, cent = mixture_rows(n, 128, n_centres=1024, sigma=0.15, seed=5, dtype=torch.bfloat16, device="cuda")
+    q, _ = mixture_rows(b, 128, n_centres=1024, sigma=0.15, seed=6, dtype=torch.bfloat16, device="cuda",
+                        centres=cent)
+    ref_i, ref_s = ops.dense_topk(q, x, k)
+    ids, scores = _sharded(q, x, k, [shard_bounds(n, world, r) for r in range(world)])
+    torch.cuda.synchronize()
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
+
+
+def test_shared_seed_uneven_shards_with_unsampled_one():
+    # one shard too small to sample (its sample is all -inf) and one empty shard
+    b, n, k = 256, 300_000, 64
+    q = make_int_rows(b, 128, seed=21, device="cuda")
+    x = make_int_rows(n, 128, seed=22, device="cuda")
+    bounds = [(0, 3_001), (3_001, 3_001), (3_001, 170_000), (170_000, n)]
+    ref_i, ref_s = ops.dense_topk(q, x, k)
+    ids, scores = _sharded(q, x, k, bounds)
+    torch.cuda.synchronize()
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
+
+
+def test_seed_sample_values_are_chunk_maxima_bounds():
+    # every sampled value is the max of some 32-item chunk of the shard, so at
+    # least k distinct items score >= the k-th largest sample value
+    b, n, k = 200, 500_000, 50
+    q = make_int_rows(b, 128, seed=31, device="cuda")
+    x = make_int_rows(n, 128, seed=32, device="cuda")
+    vals = ops.dense_seed_sample(q, x, k, n)
+    _, ref_s = ops.dense_topk(q, x, k)
+    kth_sample = vals.sort(dim=1, descending=True).values[:, k - 1]
+    assert bool((kth_sample <= ref_s[:, k - 1]).all())
+    assert bool(torch.isfinite(vals).all())
