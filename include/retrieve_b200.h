@@ -271,14 +271,23 @@ RB_API int rb_workspace_device_error(const void* workspace, size_t workspace_byt
  *
  * Both use the workspace of rb_dense_topk_workspace_size(B, N, ...); the same
  * n_total must be given to both calls. fp16 / bf16 only.
+ *
+ * With out_pairs not null, rb_dense_topk_seeded writes its [B, k] result there
+ * instead of out_ids / out_scores (which may then be null) as 8-byte pairs: the
+ * fp32 score's bits in the low 32 bits, the uint32 global id in the high 32
+ * bits (padding: -inf and 0xffffffff); global ids must stay below 2^32 - 1.
+ * One all-gather of the pairs gives the [W, B, k] stack that rb_merge_pairs
+ * reduces to the global top-k (ids int64, -1 / -inf pads).
  */
 RB_API int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
                                 int64_t n_total, float* out_vals, void* workspace, size_t workspace_bytes,
                                 void* stream);
 RB_API int rb_dense_topk_seeded(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
                                 int64_t id_offset, int64_t n_total, const float* seed_vals, int W,
-                                int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
-                                void* stream);
+                                int64_t* out_ids, float* out_scores, uint64_t* out_pairs, void* workspace,
+                                size_t workspace_bytes, void* stream);
+RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,
+                          void* stream);
 
 #ifdef __cplusplus
 }

@@ -54,8 +54,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_dense_seed_sample": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _c_size, _vp]),
     "rb_dense_topk_seeded": (
         _c_int,
-        [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64, _vp, _c_int, _vp, _vp, _vp, _c_size, _vp],
+        [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64, _vp, _c_int, _vp, _vp, _vp, _vp, _c_size,
+         _vp],
     ),
+    "rb_merge_pairs": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
     "rb_clause_mask": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp]),
     "rb_clause_compact_workspace_size": (_c_int, [_c_int, _c_int, ctypes.POINTER(_c_size)]),
     "rb_clause_compact": (

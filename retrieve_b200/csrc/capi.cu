@@ -97,13 +97,16 @@ static DenseWs dense_ws(void* workspace, size_t workspace_bytes, int B, const De
 static int dense_topk_impl(int elem, const void* queries, const float* q_scale, const void* items,
                            const float* x_scale, int B, int N, int D, int k, int64_t id_offset, int64_t* out_ids,
                            float* out_scores, void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                           const FilterArgs* filter = nullptr, const SharedSeed* shared = nullptr) {
+                           const FilterArgs* filter = nullptr, const SharedSeed* shared = nullptr,
+                           uint2* out_pairs = nullptr) {
   int rc = dense_check(elem, queries, q_scale, items, x_scale, B, N, D, k, "dense_topk");
   if (rc != RB_OK) return rc;
   if (B == 0) return RB_OK;
-  if (out_ids == nullptr || out_scores == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_topk: null output");
+  if (out_pairs == nullptr && (out_ids == nullptr || out_scores == nullptr))
+    return fail(RB_ERR_INVALID_ARG, "dense_topk: null output");
   if (N == 0) {
-    fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, stream);
+    if (out_pairs != nullptr) fill_empty_pairs(out_pairs, static_cast<size_t>(B) * k, stream);
+    else fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, stream);
     return cudaGetLastError() == cudaSuccess ? RB_OK : fail(RB_ERR_CUDA, "fill_empty launch failed");
   }
   const size_t need = dense_workspace_bytes(B, N, k);
@@ -137,7 +140,7 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
                        q_scale, x_scale, filter);
   if (rc != RB_OK) return rc;
   if (pe.stop) cudaEventRecord(pe.stop, stream);
-  return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
+  return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, out_pairs, stream);
 }
 
 int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
@@ -170,12 +173,28 @@ int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, i
 
 int rb_dense_topk_seeded(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
                          int64_t id_offset, int64_t n_total, const float* seed_vals, int W, int64_t* out_ids,
-                         float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+                         float* out_scores, uint64_t* out_pairs, void* workspace, size_t workspace_bytes,
+                         void* stream) {
   if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk_seeded: dtype must be f16 or bf16");
   if (seed_vals == nullptr || W < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk_seeded: seed values missing");
+  if (out_pairs != nullptr && (id_offset < 0 || id_offset + static_cast<int64_t>(N) > 0xffffffffll))
+    return fail(RB_ERR_UNSUPPORTED, "dense_topk_seeded: pair output needs global ids below 2^32 - 1");
   const SharedSeed shared{seed_vals, W, std::max<int64_t>(n_total, N)};
   return dense_topk_impl(dtype == RB_BF16 ? 1 : 0, queries, nullptr, items, nullptr, B, N, D, k, id_offset, out_ids,
-                         out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, &shared);
+                         out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, &shared,
+                         reinterpret_cast<uint2*>(out_pairs));
+}
+
+int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,
+                   void* stream) {
+  if (W < 1 || B < 0 || kin < 1 || k < 1) return fail(RB_ERR_INVALID_ARG, "merge_pairs: bad arguments");
+  if (k > 1024) return fail(RB_ERR_UNSUPPORTED, "merge_pairs: k > 1024");
+  if (W > 1024) return fail(RB_ERR_UNSUPPORTED, "merge_pairs: more than 1024 shards");
+  if (B == 0) return RB_OK;
+  if (pairs == nullptr || out_ids == nullptr || out_scores == nullptr)
+    return fail(RB_ERR_INVALID_ARG, "merge_pairs: null pointer");
+  return merge_pair_stack(reinterpret_cast<const uint2*>(pairs), W, B, kin, k, out_ids, out_scores,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int64_t id_offset,

@@ -24,11 +24,15 @@ constexpr int kMaxK = 1024;
 constexpr int kSmemKeys = 2048;
 constexpr int kBins = 2048;
 
+constexpr int kMaxLists = 1024;
+
 struct SelectShared {
   uint32_t hist[kBins];
   uint32_t warp_tot[kMergeThreads / 32];
   uint32_t digit, above, in_digit;
   uint32_t n_keys, n_out;
+  uint64_t kmax, kmin;
+  int pre[kMaxLists + 1];  // prefix sums of the list lengths
   uint64_t keys[kSmemKeys];
   uint64_t out[kMaxK];
 };
@@ -75,88 +79,109 @@ __device__ __forceinline__ void block_find_digit_n(SelectShared& sh, uint32_t ne
   __syncthreads();
 }
 
-// Radix select with 11-bit digits (the last one 9 bits) over 64-bit keys that
-// `visit` enumerates (each thread visits a strided share). Returns the cut:
-// exactly k keys are >= cut. Requires total > k.
+// Radix select over 64-bit keys that `visit` enumerates (each thread visits a
+// strided share), given that every key agrees with `prefix` on the bits above
+// `hi` (prefix's lower bits are zero). 11-bit digits from bit hi down. Returns
+// the cut: exactly k keys are >= cut. Requires more than k distinct keys.
 template <class Visit>
-__device__ uint64_t block_radix_cut11(const Visit& visit, int k, SelectShared& sh) {
-  uint64_t prefix = 0, mask = 0;
+__device__ uint64_t block_radix_cut(const Visit& visit, int k, int hi, uint64_t prefix, SelectShared& sh) {
+  uint64_t mask = (hi >= 63) ? 0ull : ~((2ull << hi) - 1ull);
   uint32_t need = static_cast<uint32_t>(k);
-  for (int shift = 53; shift >= 0; shift = (shift == 9) ? 0 : shift - 11) {
-    if (shift == 0 && mask == ~0ull) break;
-    const int bits = (shift == 0) ? 9 : 11;
-    const uint64_t dmask = (1ull << bits) - 1;
+  while (hi >= 0) {
+    const int bits = min(11, hi + 1);
+    const int shift = hi + 1 - bits;
+    const uint64_t dmask = (1ull << bits) - 1ull;
     for (int i = threadIdx.x; i < kBins; i += kMergeThreads) sh.hist[i] = 0;
     __syncthreads();
     visit([&](uint64_t key) {
       if ((key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & dmask], 1u);
     });
     __syncthreads();
-    if (bits == 11)
-      block_find_digit_n<kBins / kMergeThreads>(sh, need);
-    else
-      block_find_digit_n<512 / kMergeThreads>(sh, need);
+    block_find_digit_n<kBins / kMergeThreads>(sh, need);
     prefix |= static_cast<uint64_t>(sh.digit) << shift;
     mask |= dmask << shift;
     need -= sh.above;
     const bool done = (sh.in_digit == need);
     __syncthreads();
-    if (done || shift == 0) break;
+    if (done) break;
+    hi = shift - 1;
   }
   return prefix;
 }
 
-// Sorts sh.out[0, n) descending (bitonic, padded with zero keys to a power of two).
-__device__ void block_sort_out(SelectShared& sh, int n) {
-  const int tid = threadIdx.x;
-  int n_pad = 1;
-  while (n_pad < n) n_pad <<= 1;
-  for (int i = n + tid; i < n_pad; i += kMergeThreads) sh.out[i] = 0;
-  __syncthreads();
-  for (int size = 2; size <= n_pad; size <<= 1) {
-    for (int st = size >> 1; st > 0; st >>= 1) {
-      for (int i = tid; i < n_pad / 2; i += kMergeThreads) {
-        const int lo = 2 * st * (i / st) + (i % st);
-        const int hi = lo + st;
-        const bool desc = (lo & size) == 0;
-        const uint64_t a = sh.out[lo], b = sh.out[hi];
-        if ((a < b) == desc) {
-          sh.out[lo] = b;
-          sh.out[hi] = a;
-        }
-      }
-      __syncthreads();
-    }
+// Block max / min of one key per thread (0 / ~0 for threads without one).
+__device__ __forceinline__ void block_max_min(uint64_t vmax, uint64_t vmin, SelectShared& sh) {
+  for (int off = 16; off > 0; off >>= 1) {
+    const uint64_t a = __shfl_xor_sync(RB_FULL_MASK, vmax, off), b = __shfl_xor_sync(RB_FULL_MASK, vmin, off);
+    vmax = a > vmax ? a : vmax;
+    vmin = b < vmin ? b : vmin;
   }
+  if (threadIdx.x == 0) {
+    sh.kmax = 0;
+    sh.kmin = ~0ull;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(reinterpret_cast<unsigned long long*>(&sh.kmax), static_cast<unsigned long long>(vmax));
+    atomicMin(reinterpret_cast<unsigned long long*>(&sh.kmin), static_cast<unsigned long long>(vmin));
+  }
+  __syncthreads();
 }
 
-__global__ void __launch_bounds__(kMergeThreads) merge_lists_kernel(const uint2* __restrict__ lists,
-                                                                    const int* __restrict__ counts, int n_lists,
-                                                                    int stride, int k, int64_t id_offset,
-                                                                    int64_t* __restrict__ out_ids,
-                                                                    float* __restrict__ out_scores) {
+// Per-query merge of candidate lists into the sorted top-k. List r of query q
+// starts at lists + q * q_stride + r * r_stride and holds counts[q * n_lists + r]
+// entries (all cap entries when counts is null); an entry is (fp32 score bits,
+// uint32 id), id 0xffffffff marks padding. Output: ids + id_offset and scores,
+// or (pairs) the same as (score bits, uint32 global id); -1 / -inf (pairs:
+// 0xffffffff / -inf) pad rows with fewer than k entries. Score descending, ties
+// to the lower id, NaN lowest.
+template <bool PAIRS>
+__global__ void __launch_bounds__(kMergeThreads) merge_lists_kernel(
+    const uint2* __restrict__ lists, const int* __restrict__ counts, int n_lists, int64_t q_stride, int64_t r_stride,
+    int cap, int k, int64_t id_offset, int64_t* __restrict__ out_ids, float* __restrict__ out_scores,
+    uint2* __restrict__ out_pairs) {
   __shared__ SelectShared sh;
   const int q = blockIdx.x;
   const int tid = threadIdx.x;
-  const uint2* qlists = lists + static_cast<size_t>(q) * n_lists * stride;
-  const int* qcounts = counts + static_cast<size_t>(q) * n_lists;
-  auto visit_global = [&](auto&& f) {
-    for (int r = 0; r < n_lists; ++r) {
-      const int c = qcounts[r];
-      const uint2* l = qlists + static_cast<size_t>(r) * stride;
-      for (int i = tid; i < c; i += kMergeThreads) {
-        const uint2 v = l[i];
-        f(make_key(v.x, v.y));
+  const uint2* qlists = lists + static_cast<int64_t>(q) * q_stride;
+
+  // list lengths and their prefix sums (warp 0)
+  if (tid < 32) {
+    int carry = 0;
+    for (int r0 = 0; r0 < n_lists; r0 += 32) {
+      const int r = r0 + tid;
+      int c = 0;
+      if (r < n_lists) c = counts ? min(counts[static_cast<int64_t>(q) * n_lists + r], cap) : cap;
+      int incl = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(RB_FULL_MASK, incl, off);
+        if (tid >= off) incl += v;
       }
+      if (r < n_lists) sh.pre[r] = carry + incl - c;
+      carry += __shfl_sync(RB_FULL_MASK, incl, 31);
     }
-  };
-  int total = 0;
-  for (int r = 0; r < n_lists; ++r) total += qcounts[r];
-  if (tid == 0) {
-    sh.n_keys = 0;
-    sh.n_out = 0;
+    if (tid == 0) {
+      sh.pre[n_lists] = carry;
+      sh.n_keys = 0;
+      sh.n_out = 0;
+    }
   }
   __syncthreads();
+  const int total = sh.pre[n_lists];
+  // every entry, all threads at once: position p lies in list r with
+  // pre[r] <= p < pre[r + 1] (binary search over the prefix sums)
+  auto visit_global = [&](auto&& f) {
+    for (int p = tid; p < total; p += kMergeThreads) {
+      int lo = 0, hi = n_lists;
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (sh.pre[mid] <= p) lo = mid; else hi = mid;
+      }
+      const uint2 v = qlists[lo * r_stride + (p - sh.pre[lo])];
+      if (v.y != 0xffffffffu) f(make_key(v.x, v.y));
+    }
+  };
 
   // 1) gather into shared memory: everything, or the buckets >= the k-th's
   bool on_chip = true;
@@ -180,34 +205,67 @@ __global__ void __launch_bounds__(kMergeThreads) merge_lists_kernel(const uint2*
   }
   __syncthreads();
 
-  // 2) exact cut, 3) the <= k winners into sh.out
+  // 2) exact cut from the highest bit where the keys differ, 3) the <= k
+  // winners into sh.out
   if (on_chip) {
     const int n = static_cast<int>(sh.n_keys);
-    auto visit_smem = [&](auto&& f) {
-      for (int i = tid; i < n; i += kMergeThreads) f(sh.keys[i]);
-    };
-    const uint64_t cut = (n > k) ? block_radix_cut11(visit_smem, k, sh) : 0ull;
-    for (int i = tid; i < n; i += kMergeThreads)
-      if (sh.keys[i] >= cut) sh.out[atomicAdd(&sh.n_out, 1u)] = sh.keys[i];
+    if (n > k) {
+      uint64_t vmax = 0, vmin = ~0ull;
+      for (int i = tid; i < n; i += kMergeThreads) {
+        const uint64_t key = sh.keys[i];
+        vmax = key > vmax ? key : vmax;
+        vmin = key < vmin ? key : vmin;
+      }
+      block_max_min(vmax, vmin, sh);
+      const int hi = 63 - __clzll(static_cast<long long>(sh.kmax ^ sh.kmin));
+      const uint64_t prefix = (hi >= 63) ? 0ull : (sh.kmax & ~((2ull << hi) - 1ull));
+      auto visit_smem = [&](auto&& f) {
+        for (int i = tid; i < n; i += kMergeThreads) f(sh.keys[i]);
+      };
+      const uint64_t cut = block_radix_cut(visit_smem, k, hi, prefix, sh);
+      for (int i = tid; i < n; i += kMergeThreads)
+        if (sh.keys[i] >= cut) sh.out[atomicAdd(&sh.n_out, 1u)] = sh.keys[i];
+    } else {
+      for (int i = tid; i < n; i += kMergeThreads) sh.out[i] = sh.keys[i];
+      if (tid == 0) sh.n_out = n;
+    }
   } else {
-    const uint64_t cut = block_radix_cut11(visit_global, k, sh);
+    const uint64_t cut = block_radix_cut(visit_global, k, 63, 0ull, sh);
     visit_global([&](uint64_t key) {
       if (key >= cut) sh.out[atomicAdd(&sh.n_out, 1u)] = key;
     });
   }
   __syncthreads();
+
+  // 4) rank sort (keys are distinct): slot = number of larger keys
   const int n_out = min(static_cast<int>(sh.n_out), k);
-  block_sort_out(sh, n_out);
+  for (int i = tid; i < n_out; i += kMergeThreads) {
+    const uint64_t key = sh.out[i];
+    int rank = 0;
+    for (int j = 0; j < n_out; ++j) rank += (sh.out[j] > key);
+    sh.keys[rank] = key;
+  }
+  __syncthreads();
   for (int i = tid; i < k; i += kMergeThreads) {
-    int64_t id = -1;
-    float s = -INFINITY;
-    if (i < n_out) {
-      const uint2 e = key_to_entry(sh.out[i]);
-      id = static_cast<int64_t>(e.y) + id_offset;
-      s = __uint_as_float(e.x);
+    const size_t o = static_cast<size_t>(q) * k + i;
+    if constexpr (PAIRS) {
+      uint2 e = make_uint2(0xff800000u, 0xffffffffu);
+      if (i < n_out) {
+        e = key_to_entry(sh.keys[i]);
+        e.y = static_cast<uint32_t>(static_cast<int64_t>(e.y) + id_offset);
+      }
+      out_pairs[o] = e;
+    } else {
+      int64_t id = -1;
+      float sc = -INFINITY;
+      if (i < n_out) {
+        const uint2 e = key_to_entry(sh.keys[i]);
+        id = static_cast<int64_t>(e.y) + id_offset;
+        sc = __uint_as_float(e.x);
+      }
+      out_ids[o] = id;
+      out_scores[o] = sc;
     }
-    out_ids[static_cast<size_t>(q) * k + i] = id;
-    out_scores[static_cast<size_t>(q) * k + i] = s;
   }
 }
 
@@ -290,16 +348,24 @@ __global__ void fill_empty_kernel(int64_t* out_ids, float* out_scores, size_t n)
   }
 }
 
-int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,
-                int64_t* out_ids, float* out_scores, float* out_kth, cudaStream_t stream) {
-  (void)out_kth;
+static int merge_launch(const uint2* lists, const int* counts, int B, int n_lists, int64_t q_stride,
+                        int64_t r_stride, int cap, int k, int64_t id_offset, int64_t* out_ids, float* out_scores,
+                        uint2* out_pairs, cudaStream_t stream) {
   if (k < 1 || k > kMaxK) {
     set_last_error("merge: k must be in [1, 1024]");
     return RB_ERR_INVALID_ARG;
   }
+  if (n_lists < 1 || n_lists > kMaxLists) {
+    set_last_error("merge: between 1 and 1024 lists per query");
+    return RB_ERR_INVALID_ARG;
+  }
   if (B == 0) return RB_OK;
-  merge_lists_kernel<<<B, kMergeThreads, 0, stream>>>(lists, counts, n_lists, stride, k, id_offset, out_ids,
-                                                      out_scores);
+  if (out_pairs != nullptr)
+    merge_lists_kernel<true><<<B, kMergeThreads, 0, stream>>>(lists, counts, n_lists, q_stride, r_stride, cap, k,
+                                                               id_offset, nullptr, nullptr, out_pairs);
+  else
+    merge_lists_kernel<false><<<B, kMergeThreads, 0, stream>>>(lists, counts, n_lists, q_stride, r_stride, cap, k,
+                                                                id_offset, out_ids, out_scores, nullptr);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_last_error(cudaGetErrorString(e));
@@ -308,8 +374,18 @@ int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int s
   return RB_OK;
 }
 
-// Packs W per-shard top-k lists [W, B, kin] (id -1 = empty slot) into the
-// per-query candidate lists merge_lists_kernel reads: lists[b][w] of kin entries.
+int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,
+                int64_t* out_ids, float* out_scores, uint2* out_pairs, cudaStream_t stream) {
+  return merge_launch(lists, counts, B, n_lists, static_cast<int64_t>(n_lists) * stride, stride, stride, k, id_offset,
+                      out_ids, out_scores, out_pairs, stream);
+}
+
+int merge_pair_stack(const uint2* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,
+                     cudaStream_t stream) {
+  return merge_launch(pairs, nullptr, B, W, kin, static_cast<int64_t>(B) * kin, kin, k, 0, out_ids, out_scores,
+                      nullptr, stream);
+}
+
 __global__ void pack_shard_lists_kernel(const int64_t* __restrict__ ids, const float* __restrict__ scores, int W,
                                         int B, int kin, uint2* __restrict__ lists, int* __restrict__ counts) {
   const size_t total = static_cast<size_t>(W) * B * kin;
@@ -344,6 +420,18 @@ int merge_shard_lists(const int64_t* ids, const float* scores, int W, int B, int
 size_t merge_shard_ws_bytes(int W, int B, int kin) {
   return align_up(static_cast<size_t>(W) * B * kin * sizeof(uint2), 256) +
          align_up(static_cast<size_t>(W) * B * sizeof(int), 256);
+}
+
+__global__ void fill_empty_pairs_kernel(uint2* out, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    out[i] = make_uint2(0xff800000u, 0xffffffffu);
+}
+
+void fill_empty_pairs(uint2* out, size_t n, cudaStream_t stream) {
+  if (n == 0) return;
+  const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, 1024));
+  fill_empty_pairs_kernel<<<blocks, 256, 0, stream>>>(out, n);
 }
 
 void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stream) {

@@ -43,9 +43,12 @@ int row_kth_lower_bound(const float* vals, int B, int n, int64_t stride, int nse
 
 // Merge of per-(query, split) candidate lists into the final sorted top-k.
 int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,
-                int64_t* out_ids, float* out_scores, float* out_kth, cudaStream_t stream);
+                int64_t* out_ids, float* out_scores, uint2* out_pairs, cudaStream_t stream);
+int merge_pair_stack(const uint2* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,
+                     cudaStream_t stream);
 
 void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stream);
+void fill_empty_pairs(uint2* out, size_t n, cudaStream_t stream);
 
 int merge_shard_lists(const int64_t* ids, const float* scores, int W, int B, int kin, int k, int64_t* out_ids,
                       float* out_scores, void* ws, cudaStream_t stream);

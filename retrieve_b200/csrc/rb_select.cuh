@@ -247,81 +247,8 @@ __device__ __forceinline__ float max32(const uint32_t (&s)[32]) {
 }
 
 // ---------------------------------------------------------------------------
-// Block-level (256 threads) radix select over entries in global memory.
+// Threads of the block-level merge and select kernels.
 // ---------------------------------------------------------------------------
 constexpr int kMergeThreads = 256;
-
-struct MergeSmem {
-  uint32_t hist[256];
-  uint32_t warp_tot[kMergeThreads / 32];
-  uint32_t digit, above, in_digit;
-  uint32_t n_out;
-};
-
-// Finds, for the 256-bin histogram in smem (one bin per thread), the digit
-// holding the need-th largest element.
-__device__ __forceinline__ void block_find_digit(MergeSmem& sm, uint32_t need) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // bin index descending order: thread tid owns bin (255 - tid), so an inclusive
-  // prefix over tid is a suffix sum over bins.
-  const uint32_t mine = sm.hist[255 - tid];
-  uint32_t incl = mine;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    uint32_t v = __shfl_up_sync(RB_FULL_MASK, incl, off);
-    if (lane >= off) incl += v;
-  }
-  if (lane == 31) sm.warp_tot[warp] = incl;
-  __syncthreads();
-  uint32_t base = 0;
-  for (int w = 0; w < warp; ++w) base += sm.warp_tot[w];
-  incl += base;
-  const uint32_t excl = incl - mine;
-  if (excl < need && need <= incl) {
-    sm.digit = 255 - tid;
-    sm.above = excl;
-    sm.in_digit = mine;
-  }
-  __syncthreads();
-}
-
-// Loads entry i of the concatenated lists. Lists are `n_lists` runs of
-// `stride` entries; run r holds counts[r] valid entries.
-struct ListSet {
-  const uint2* base;
-  const int* counts;
-  int n_lists;
-  int stride;
-};
-
-// Returns the cut key: exactly min(k, total) entries have key >= cut (cut = 0
-// when total <= k, i.e. keep everything).
-__device__ __forceinline__ uint64_t block_radix_cut(const ListSet& ls, int total, int k, MergeSmem& sm) {
-  if (total <= k) return 0;
-  uint64_t prefix = 0, mask = 0;
-  uint32_t need = static_cast<uint32_t>(k);
-  for (int shift = 56; shift >= 0; shift -= 8) {
-    sm.hist[threadIdx.x] = 0;
-    __syncthreads();
-    for (int r = 0; r < ls.n_lists; ++r) {
-      const int c = ls.counts[r];
-      const uint2* l = ls.base + static_cast<size_t>(r) * ls.stride;
-      for (int i = threadIdx.x; i < c; i += kMergeThreads) {
-        const uint2 v = l[i];
-        const uint64_t key = make_key(v.x, v.y);
-        if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 0xffu], 1u);
-      }
-    }
-    __syncthreads();
-    block_find_digit(sm, need);
-    prefix |= static_cast<uint64_t>(sm.digit) << shift;
-    mask |= static_cast<uint64_t>(0xffu) << shift;
-    need -= sm.above;
-    const bool done = (sm.in_digit == need);
-    __syncthreads();
-    if (done) break;
-  }
-  return prefix;
-}
 
 }  // namespace rb

@@ -119,12 +119,14 @@ def dense_seed_sample(query: Tensor, item_shard: Tensor, k: int, n_total: int, w
 
 def dense_topk_seeded(
     query: Tensor, item_shard: Tensor, k: int, id_offset: int, n_total: int, seed_vals: Tensor,
-    ws: Tensor | None = None,
-) -> tuple[Tensor, Tensor]:
+    ws: Tensor | None = None, pairs: bool = False,
+) -> tuple[Tensor, Tensor] | Tensor:
     """``dense_topk_sharded`` with the full pass seeded by the union of every
     shard's ``dense_seed_sample`` output (``seed_vals [W, B, k]`` fp32; C-ABI
     ``rb_dense_topk_seeded``). May return fewer than k real entries per row
-    (``-1`` / ``-inf``); the merge over all shards is the exact global top-k."""
+    (``-1`` / ``-inf``); the merge over all shards is the exact global top-k.
+    With ``pairs`` the result is one ``[B, k]`` int64 tensor of packed (fp32
+    score bits, uint32 global id) pairs for ``merge_pairs``."""
     _require_cuda(query, item_shard)
     check_contiguous(item_shard=item_shard, seed_vals=seed_vals)
     q = query.to(item_shard.dtype).contiguous()
@@ -132,18 +134,42 @@ def dense_topk_seeded(
     if seed_vals.dim() != 3 or seed_vals.shape[1:] != (b, k) or seed_vals.dtype != torch.float32:
         raise ValueError("seed_vals must be [W, B, k] float32")
     dev = q.device
+    if pairs:
+        out = torch.empty((b, k), dtype=torch.int64, device=dev)
+        ids = scores = None
+    else:
+        out = None
+        ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+        scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b > 0:
+        ws = dense_workspace(q, item_shard, k) if ws is None else ws
+        with torch.cuda.device(dev):
+            rc = _lib.lib().rb_dense_topk_seeded(
+                _ptr(q), _ptr(item_shard), b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k,
+                int(id_offset), int(n_total), _ptr(seed_vals), seed_vals.shape[0],
+                None if pairs else _ptr(ids), None if pairs else _ptr(scores), _ptr(out) if pairs else None,
+                _ptr(ws), ws.numel(), _stream_ptr(dev),
+            )
+        _lib.check(rc, "dense_topk_seeded")
+    return out if pairs else (ids, scores)
+
+
+def merge_pairs(pairs: Tensor, k: int) -> tuple[Tensor, Tensor]:
+    """``[W, B, kin]`` packed (score bits, uint32 id) pairs of every shard →
+    global ``(ids [B, k] int64, scores [B, k] fp32)`` (C-ABI ``rb_merge_pairs``)."""
+    if pairs.dim() != 3 or pairs.dtype != torch.int64:
+        raise ValueError("pairs must be [W, B, kin] int64")
+    _require_cuda(pairs)
+    check_contiguous(pairs=pairs)
+    w, b, kin = pairs.shape
+    dev = pairs.device
     ids = torch.empty((b, k), dtype=torch.int64, device=dev)
     scores = torch.empty((b, k), dtype=torch.float32, device=dev)
     if b == 0:
         return ids, scores
-    ws = dense_workspace(q, item_shard, k) if ws is None else ws
     with torch.cuda.device(dev):
-        rc = _lib.lib().rb_dense_topk_seeded(
-            _ptr(q), _ptr(item_shard), b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k, int(id_offset),
-            int(n_total), _ptr(seed_vals), seed_vals.shape[0], _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(),
-            _stream_ptr(dev),
-        )
-    _lib.check(rc, "dense_topk_seeded")
+        rc = _lib.lib().rb_merge_pairs(_ptr(pairs), w, b, kin, k, _ptr(ids), _ptr(scores), _stream_ptr(dev))
+    _lib.check(rc, "merge_pairs")
     return ids, scores
 
 

@@ -2,11 +2,19 @@
 
 The corpus is split row-wise into contiguous shards; rank ``r`` holds rows
 ``[offset_r, offset_r + n_r)``. A query batch (replicated on every rank) is
-scored against the local shard with the fused kernel, giving each rank its
-local top-k with global ids; one NCCL all-gather brings the ``W`` local lists to
-every rank and ``rb_merge_topk`` reduces them to the global top-k with the same
-ordering (score descending, ties to the lower id). Exact for any ``W``: the
-global top-k is contained in the union of the local top-k lists, and a shard's
+scored against the local shard with the fused kernel. One search is:
+
+1. every rank samples its shard (``dense_seed_sample``: k chunk maxima per
+   query) and one NCCL all-gather brings the ``[W, B, k]`` samples to every rank;
+2. every rank runs the full pass over its shard seeded by the k-th largest
+   value of the union — a lower bound on the global k-th score — and keeps its
+   local top-k as packed (score, global id) pairs;
+3. a second all-gather brings the ``[W, B, k]`` pairs to every rank and
+   ``merge_pairs`` reduces them to the global top-k with the single-GPU ordering
+   (score descending, ties to the lower id).
+
+Exact for any ``W``: the global top-k is contained in the union of the local
+top-k lists (the shared seed never drops a global top-k item), and a shard's
 scores do not depend on which shard scores it.
 
 The reference is single-GPU (its harness merges chunked top-k lists the same
@@ -114,10 +122,13 @@ class ShardedDenseTopK:
         b = vals.shape[0]
         gathered = torch.empty((self.world * b, self.k), dtype=vals.dtype, device=vals.device)
         dist.all_gather_into_tensor(gathered, vals, group=self.group)
-        ids, scores = ops.dense_topk_seeded(
-            query, self.items, self.k, self.id_offset, self.n_total, gathered.view(self.world, b, self.k), ws
+        pairs = ops.dense_topk_seeded(
+            query, self.items, self.k, self.id_offset, self.n_total, gathered.view(self.world, b, self.k), ws,
+            pairs=True,
         )
-        return exchange_and_merge(ids, scores, self.k, self.group)
+        all_pairs = torch.empty((self.world * b, self.k), dtype=pairs.dtype, device=pairs.device)
+        dist.all_gather_into_tensor(all_pairs, pairs, group=self.group)
+        return ops.merge_pairs(all_pairs.view(self.world, b, self.k), self.k)
 
     def launches_per_search(self, b: int) -> int:
         """Kernels of this library one search launches (NCCL's not counted)."""
@@ -131,5 +142,5 @@ class ShardedDenseTopK:
             return n.value
         sampled = n.value == 4
         # sample pass + row select (or the -inf fill), union select, full pass,
-        # list merge, then the two kernels of the cross-shard merge
-        return (2 if sampled else 1) + 1 + 2 + 2
+        # list merge into pairs, then the merge of the gathered pairs
+        return (2 if sampled else 1) + 1 + 2 + 1

@@ -22,25 +22,30 @@ from tests.helpers import assert_topk_exact, make_int_rows, mixture_rows
 pytestmark = pytest.mark.gpu
 
 
-def _sharded(q, x, k, bounds):
+def _sharded(q, x, k, bounds, pairs=False):
     n_total = x.shape[0]
     shards = [x[lo:hi].contiguous() for lo, hi in bounds]
     samples = torch.stack([ops.dense_seed_sample(q, s, k, n_total) for s in shards])
-    outs = [
-        ops.dense_topk_seeded(q, s, k, lo, n_total, samples) for s, (lo, _) in zip(shards, bounds)
-    ]
+    if pairs:
+        # what a rank exchanges: one [B, k] int64 tensor of (score, id) pairs
+        stack = torch.stack(
+            [ops.dense_topk_seeded(q, s, k, lo, n_total, samples, pairs=True) for s, (lo, _) in zip(shards, bounds)]
+        )
+        return ops.merge_pairs(stack, k)
+    outs = [ops.dense_topk_seeded(q, s, k, lo, n_total, samples) for s, (lo, _) in zip(shards, bounds)]
     ids = torch.stack([o[0] for o in outs])
     scores = torch.stack([o[1] for o in outs])
     return merge_topk(ids, scores, k)
 
 
+@pytest.mark.parametrize("pairs", [False, True])
 @pytest.mark.parametrize("world", [2, 3, 8])
 @pytest.mark.parametrize("b,n,k", [(300, 400_003, 100), (1024, 1_000_000, 100), (96, 150_001, 37)])
-def test_shared_seed_equals_single_call_integer(world, b, n, k):
+def test_shared_seed_equals_single_call_integer(world, b, n, k, pairs):
     q = make_int_rows(b, 128, seed=11, device="cuda")
     x = make_int_rows(n, 128, seed=12, device="cuda")
     ref_i, ref_s = ops.dense_topk(q, x, k)
-    ids, scores = _sharded(q, x, k, [shard_bounds(n, world, r) for r in range(world)])
+    ids, scores = _sharded(q, x, k, [shard_bounds(n, world, r) for r in range(world)], pairs)
     torch.cuda.synchronize()
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
 
@@ -53,7 +58,7 @@ def test_shared_seed_equals_single_call_mixture(world):
     q, _ = mixture_rows(b, 128, n_centres=1024, sigma=0.15, seed=6, dtype=torch.bfloat16, device="cuda",
                         centres=cent)
     ref_i, ref_s = ops.dense_topk(q, x, k)
-    ids, scores = _sharded(q, x, k, [shard_bounds(n, world, r) for r in range(world)])
+    ids, scores = _sharded(q, x, k, [shard_bounds(n, world, r) for r in range(world)], pairs=True)
     torch.cuda.synchronize()
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
 
@@ -65,7 +70,7 @@ def test_shared_seed_uneven_shards_with_unsampled_one():
     x = make_int_rows(n, 128, seed=22, device="cuda")
     bounds = [(0, 3_001), (3_001, 3_001), (3_001, 170_000), (170_000, n)]
     ref_i, ref_s = ops.dense_topk(q, x, k)
-    ids, scores = _sharded(q, x, k, bounds)
+    ids, scores = _sharded(q, x, k, bounds, pairs=True)
     torch.cuda.synchronize()
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
 
