@@ -6,7 +6,10 @@ N(0,1), within-cluster sigma 0.15, L2-normalised, bf16), 1,024 queries sampled
 the same way, k=100, inner-product score. One step = one query batch against
 the whole corpus. With N GPUs (torchrun, one process per GPU) the corpus is
 row-sharded (strong scaling: the corpus and batch are fixed); each step is the
-local fused top-k, an NCCL all-gather of the per-shard lists and the merge.
+shard sample, an NCCL all-gather of the samples (the shared threshold seed),
+the local fused top-k, an all-gather of the per-shard results and the merge.
+The step runs as one CUDA graph (retrieve_b200.shard.GraphedSearch), captured
+after the warm-up searches.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -24,9 +27,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -91,58 +92,84 @@ def queries(cent: torch.Tensor, b: int) -> torch.Tensor:
 # clocks
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = (
-        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
-    )
+    """Samples this rank's GPU SM clock and clock-event reasons through NVML
+    (read-only queries) from a thread, every few milliseconds, while running."""
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+    REASONS = {  # NVML clocks-event reason bits
+        0x4: "sw_power_cap",
+        0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, device: torch.device, interval_s: float = 0.002):
+        self.interval = interval_s
+        self.samples: list[tuple[float, float, int]] = []
+        self.error = None
+        self._stop = None
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception as exc:  # NVML missing or the device not found
+            self.nvml = None
+            self.error = f"nvml unavailable: {type(exc).__name__}"
+
+    def _read(self):
+        nv = self.nvml
+        sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        self.samples.append((float(sm), float(mx), int(reasons)))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._read()
+            except Exception as exc:
+                self.error = f"nvml read failed: {type(exc).__name__}"
+                return
+            self._stop.wait(self.interval)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)],
-                stdout=self.file, stderr=subprocess.DEVNULL,
-            )
-        except (FileNotFoundError, OSError):
-            self.proc = None
+        import threading
 
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.file.flush()
-        self.file.seek(0)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.file.read().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        os.unlink(self.file.name)
-        return {
+        if self.nvml is None:
+            return
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+
+    def stop(self) -> list:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        return list(self.samples)
+
+    @classmethod
+    def summary(cls, per_rank: list[tuple[list, str | None]]) -> dict:
+        sm, mx, bits, errors = [], [], 0, []
+        for samples, err in per_rank:
+            if err:
+                errors.append(err)
+            for a, b, r in samples:
+                sm.append(a)
+                mx.append(b)
+                bits |= r
+        reasons = sorted(name for bit, name in cls.REASONS.items() if bits & bit)
+        out = {
             "sm_mhz": statistics.median(sm) if sm else None,
             "sm_max_mhz": max(mx) if mx else None,
-            "reasons": sorted(reasons),
+            "reasons": reasons + errors,
             "samples": len(sm),
+            "source": "NVML, every rank's GPU, sampled every 2 ms during both timed loops",
         }
+        return out
 
 
 # ---------------------------------------------------------------------------
@@ -215,7 +242,7 @@ def config_dict(args) -> dict:
         "batch": args.batch,
         "k": args.k,
         "corpus": f"{N_CENTRES}-centre Gaussian mixture, sigma {SIGMA}, L2-normalised, bf16",
-        "parallelism": f"row-shard x{args.gpus} + NCCL all-gather",
+        "parallelism": f"row-shard x{args.gpus}, shared seed; 2 NCCL all-gathers per step; one CUDA graph per step",
         "l2": "no flush: the corpus (2.56 GB, or its shard) is larger than L2 (126 MB)",
     }
 
@@ -238,7 +265,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     from retrieve_b200 import _lib
-    from retrieve_b200.shard import ShardedDenseTopK, shard_bounds
+    from retrieve_b200.shard import GraphedSearch, ShardedDenseTopK, shard_bounds
 
     lib = _lib.lib()
     n, b, k = args.n_items, args.batch, args.k
@@ -246,65 +273,87 @@ def main():
     lo, hi = shard_bounds(n, world, rank)
     x = corpus_rows(cent, lo, hi, n)
     q = queries(cent, b)
-    index = ShardedDenseTopK(x, lo, k)
+    index = ShardedDenseTopK(x, lo, k, n_total=n)
     torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # warm-up
+    # warm-up through the plain (uncaptured) search
     for _ in range(args.warmup):
         index.search(q)
     torch.cuda.synchronize()
     barrier()
 
+    # one search captured as a CUDA graph, with the full-corpus pass bracketed
+    # by two events (recorded by every replay)
     stream = torch.cuda.current_stream(dev)
-    sampler = ClockSampler(local)
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ka.record(stream)
+    kb.record(stream)
+    torch.cuda.synchronize()
+    lib.rb_set_profile_events(ka.cuda_event, kb.cuda_event)
+    graphed = GraphedSearch(index, q, warmup=1)
+    lib.rb_set_profile_events(None, None)
+    for _ in range(args.warmup):
+        graphed.replay()
+    torch.cuda.synchronize()
+    barrier()
+
+    sampler = ClockSampler(dev)
     sampler.start()
-    # device-resident timed region, with the dominant kernel timed per step
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for a, c in kev:  # torch creates the event handle on first record
-        a.record(stream)
-        c.record(stream)
+    # device-resident timed region: K back-to-back replays. Every replay
+    # re-records the kernel's event pair, so afterwards it holds the duration
+    # of the full-corpus pass in the last timed step.
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(args.steps):
-        lib.rb_set_profile_events(kev[i][0].cuda_event, kev[i][1].cuda_event)
-        index.search(q)
+    for _ in range(args.steps):
+        graphed.replay()
     e1.record(stream)
-    lib.rb_set_profile_events(None, None)
     torch.cuda.synchronize()
     barrier()
     t_ms = e0.elapsed_time(e1)
-    kern_ms = statistics.mean(a.elapsed_time(c) for a, c in kev)
+    kern_ms = ka.elapsed_time(kb)
+    # consistency check: the same kernel timed step by step (host wait between)
+    kern = []
+    for _ in range(args.steps):
+        graphed.replay()
+        kb.synchronize()
+        kern.append(ka.elapsed_time(kb))
+    kern_mean_ms = statistics.mean(kern)
+    barrier()
 
-    # end to end through the public op: pinned host query batch in, results out
+    # end to end through the public API: pinned host query batch in, results out
     q_host = q.cpu().pin_memory()
     ids_host = torch.empty((b, k), dtype=torch.int64).pin_memory()
     sc_host = torch.empty((b, k), dtype=torch.float32).pin_memory()
-    q_dev = torch.empty_like(q)
     barrier()
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for _ in range(args.steps):
-        q_dev.copy_(q_host, non_blocking=True)
-        ids, sc = index.search(q_dev)
+        ids, sc = graphed.search(q_host)
         ids_host.copy_(ids, non_blocking=True)
         sc_host.copy_(sc, non_blocking=True)
     f1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    clocks = sampler.stop()
+    samples = sampler.stop()
     e2e_ms = f0.elapsed_time(f1)
+    per_rank = [(samples, sampler.error)]
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (samples, sampler.error))
+        per_rank = gathered
+    clocks = ClockSampler.summary(per_rank)
 
-    times = torch.tensor([t_ms, e2e_ms, kern_ms], device=dev)
+    times = torch.tensor([t_ms, e2e_ms, kern_ms, kern_mean_ms], device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, kern_ms = times.tolist()
+    t_ms, e2e_ms, kern_ms, kern_mean_ms = times.tolist()
     value = b * args.steps / (t_ms / 1e3)
     e2e_value = b * args.steps / (e2e_ms / 1e3)
 
@@ -356,6 +405,8 @@ def main():
             "frac": achieved / peak,
             "traffic": traffic,
             "kernel_ms": kern_ms,
+            "kernel_ms_source": "CUDA events around the pass, last step of the timed region, max over ranks",
+            "kernel_ms_mean_after": kern_mean_ms,
         },
         "gpu_launches": launches,
         "clocks": clocks,
@@ -374,6 +425,7 @@ def main():
         line["recall_vs_ref"] = recall_at_k(ours_i.cpu().numpy(), ref_i)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    graphed.release()
     if world > 1:
         dist.destroy_process_group()
 

@@ -26,6 +26,16 @@ static int fail(int code, const std::string& msg) { return fail(code, msg.c_str(
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Records a profiling event; inside a CUDA graph capture as an event record
+// node, so that every replay of the graph records it.
+static void record_profile_event(cudaEvent_t ev, cudaStream_t stream) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &st) == cudaSuccess && st == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, stream, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, stream);
+}
+
 // Workspace tail: one device error word, 256-byte aligned at the end.
 static int* ws_err_word(void* ws, size_t ws_bytes) {
   return reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + ws_bytes - 256);
@@ -135,11 +145,11 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
     if (rc != RB_OK) return rc;
     seed = d.thresh;
   }
-  if (pe.start) cudaEventRecord(pe.start, stream);
+  if (pe.start) record_profile_event(pe.start, stream);
   rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, d.lists, d.counts, nullptr, d.err, stream,
                        q_scale, x_scale, filter);
   if (rc != RB_OK) return rc;
-  if (pe.stop) cudaEventRecord(pe.stop, stream);
+  if (pe.stop) record_profile_event(pe.stop, stream);
   return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, out_pairs, stream);
 }
 

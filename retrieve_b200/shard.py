@@ -144,3 +144,44 @@ class ShardedDenseTopK:
         # sample pass + row select (or the -inf fill), union select, full pass,
         # list merge into pairs, then the merge of the gathered pairs
         return (2 if sampled else 1) + 1 + 2 + 1
+
+
+class GraphedSearch:
+    """One search of a fixed query batch shape captured as a CUDA graph.
+
+    Repeated searches of the same batch size replay the captured kernels (and,
+    with more than one rank, the NCCL all-gathers) without host launch work.
+    ``example`` is a query batch of the shape and dtype to serve; it is used for
+    the warm-up searches that precede the capture (communicators, workspace,
+    kernel attributes). ``search(query)`` copies ``query`` (host — pinned for an
+    asynchronous copy — or device) into the static input, replays, and returns
+    the static ``(ids, scores)`` outputs, which the next call overwrites. Every
+    rank must construct and call it the same number of times."""
+
+    def __init__(self, index: ShardedDenseTopK, example: Tensor, warmup: int = 2) -> None:
+        dev = index.items.device
+        self.index = index
+        self.query = example.to(device=dev, dtype=index.items.dtype).contiguous().clone()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                index.search(self.query)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.ids, self.scores = index.search(self.query)
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> tuple[Tensor, Tensor]:
+        self.graph.replay()
+        return self.ids, self.scores
+
+    def search(self, query: Tensor) -> tuple[Tensor, Tensor]:
+        self.query.copy_(query, non_blocking=True)
+        return self.replay()
+
+    def release(self) -> None:
+        """Drops the graph (before the process group is destroyed)."""
+        self.graph.reset()

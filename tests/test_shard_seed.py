@@ -86,3 +86,20 @@ def test_seed_sample_values_are_chunk_maxima_bounds():
     kth_sample = vals.sort(dim=1, descending=True).values[:, k - 1]
     assert bool((kth_sample <= ref_s[:, k - 1]).all())
     assert bool(torch.isfinite(vals).all())
+
+
+def test_graphed_search_matches_plain_search_on_new_queries():
+    from retrieve_b200.shard import GraphedSearch, ShardedDenseTopK
+
+    b, n, k = 512, 300_000, 100
+    x = make_int_rows(n, 128, seed=41, device="cuda")
+    index = ShardedDenseTopK(x, 0, k)
+    q0 = make_int_rows(b, 128, seed=42, device="cuda")
+    g = GraphedSearch(index, q0)
+    for seed in (43, 44):
+        qn = make_int_rows(b, 128, seed=seed, device="cuda")
+        ref_i, ref_s = index.search(qn)
+        ids, scores = g.search(qn.cpu().pin_memory())
+        torch.cuda.synchronize()
+        assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
+    g.release()
