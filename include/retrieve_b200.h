@@ -63,7 +63,7 @@ RB_API int rb_abi_version(void);
  * Replaces PostfilterKNN.score + masked_topk
  *   (retrieve/src/retrieve/modules/knn.py:62-76; the reference scores with
  *   torch.mm(q, E_t, out_dtype=float32) then torch.topk, functional.py:30-85).
- * Supported: D * 2 in {128, 256} bytes, 1 <= k <= 256, N < 2^31.
+ * Supported: D * 2 in {128, 256, 512} bytes, 1 <= k <= 1024, N < 2^31.
  */
 RB_API int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* bytes);
 RB_API int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int64_t id_offset,
@@ -123,7 +123,7 @@ RB_API int rb_candidate_topk(int kind, const void* query, int query_dtype, const
  * (retrieve/src/retrieve/ops/triton/oporp_1bit_match_topk.py:261-273):
  * query_bits [B, W], item_bits [N, W] int64, score 64*W - 2*popcount as fp32,
  * output [B, k] (ids = item rows), ties to the lower row. W even, <= 16;
- * k <= 384.
+ * k <= 1024.
  */
 RB_API int rb_hamming_topk_workspace_size(int B, int N, int W, int k, size_t* bytes);
 RB_API int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, int B, int N, int W, int k,
@@ -237,13 +237,26 @@ RB_API int rb_bloom_build(const int64_t* item_attrs, int N, int C, int A, int k,
  * scales; score = (fp32(dot) * query_scale) * item_scale in that order
  * (the dequant of retrieve/src/retrieve/ops/official/adapter.py:338-367 and
  * silvertorch fork_search_cuda.cu:585-591; with one global item scale this is
- * SilverTorch's int32 scoring path over every item). D in {128, 256};
- * k <= 256. Workspace as rb_dense_topk_workspace_size.
+ * SilverTorch's int32 scoring path over every item). D in {128, 256, 512};
+ * k <= 1024. A null scale array means unit scales: the score is then the raw
+ * int32 dot as fp32 (exact; with +-1 codes from rb_bits_to_pm1 it is the
+ * 1-bit match score 64 W - 2 hamming). Workspace as rb_dense_topk_workspace_size.
  */
 RB_API int rb_dense_topk_i8(const int8_t* query_codes, const float* query_scales, const int8_t* item_codes,
                             const float* item_scales, int B, int N, int D, int k, int64_t id_offset,
                             int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
                             void* stream);
+
+/*
+ * Expands 1-bit codes [N, W] int64 (bit b of word w = coordinate 64 w + b, LSB
+ * first; retrieve/src/retrieve/indexing/quantize.py:63-72) into a +-1 int8
+ * table [N, 64 W]: +1 where the bit is set. The dot of two such rows is
+ * 64 W - 2 popcount(q ^ x), the score of oporp_1bit_match_topk
+ * (retrieve/src/retrieve/ops/reference/oporp_1bit_match_topk.py:9-41), so
+ * rb_dense_topk_i8 with null scales ranks 1-bit codes on the tensor cores.
+ * Index-build time (8x the packed size); queries per batch.
+ */
+RB_API int rb_bits_to_pm1(const int64_t* bits, int N, int W, int8_t* out, void* stream);
 
 /*
  * Reads (synchronously) the device error word a scan kernel leaves in

@@ -137,13 +137,21 @@ def int8_topk(query, item_codes, item_scales, k, *, chunk=1 << 18):
     return best_i, best_s
 
 
-def silvertorch_fullprobe(query, item_codes, global_scale, k):
-    """SilverTorch's int32 path with every cluster probed (st::search semantics,
-    silvertorch fork_search_cuda.cu:1405-1411 and 585-591): rank on the raw int32
-    dot, ties in index order, then score = (fp32(dot) * q_scale) * global_scale."""
-    codes, qs = quantize_int8(np.asarray(query, dtype=np.float32))
-    dots = codes.astype(np.int64) @ np.asarray(item_codes, dtype=np.int64).T
-    ids, top = topk_strict(dots.astype(np.float64).astype(np.float32) if dots.max() < 2**24 else dots, k)
+def silvertorch_fullprobe_codes(query_codes, item_codes, q_scales, global_scale, k):
+    """SilverTorch's int32 path with every cluster probed, on int8 codes (st::search
+    semantics, silvertorch fork_search_cuda.cu:1405-1411 and 585-591): rank on the
+    raw int32 dot (silvertorch fused_kmean_ann.cpp:60-70), ties in index order,
+    then score = (fp32(dot) * q_scale) * global_scale."""
+    dots = np.asarray(query_codes, dtype=np.int64) @ np.asarray(item_codes, dtype=np.int64).T
+    ids, _ = topk_strict(dots.astype(np.float64).astype(np.float32) if np.abs(dots).max() < 2**24 else dots, k)
     d = np.take_along_axis(dots, ids, axis=1).astype(np.float32)
+    qs = np.broadcast_to(np.asarray(q_scales, dtype=np.float32), (d.shape[0],))
     scores = (d * qs[:, None]).astype(np.float32) * np.float32(global_scale)
     return ids, scores.astype(np.float32)
+
+
+def silvertorch_fullprobe(query, item_codes, global_scale, k):
+    """``silvertorch_fullprobe_codes`` after the reference's query quantization
+    (``quantize_int8``, retrieve/src/retrieve/indexing/quantize.py:9-18)."""
+    codes, qs = quantize_int8(np.asarray(query, dtype=np.float32))
+    return silvertorch_fullprobe_codes(codes, item_codes, qs, global_scale, k)

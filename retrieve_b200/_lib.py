@@ -58,6 +58,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _vp],
     ),
     "rb_merge_pairs": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "rb_bits_to_pm1": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "rb_clause_mask": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp]),
     "rb_clause_compact_workspace_size": (_c_int, [_c_int, _c_int, ctypes.POINTER(_c_size)]),
     "rb_clause_compact": (

@@ -191,7 +191,7 @@ struct HamParams {
   int* counts;            // [B, n_splits]
 };
 
-template <int W>
+template <int W, int EPL>
 __global__ void __launch_bounds__(kHamQ) hamming_scan_kernel(HamParams p) {
   __shared__ __align__(16) uint64_t tile[2][kHamTile * W];
   __shared__ uint32_t hist_all[kHamQ / 32][256];
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kHamQ) hamming_scan_kernel(HamParams p) {
       // room for a whole tile of appends
       const bool need = valid_q && (count > p.cap - kHamTile);
       if (__any_sync(RB_FULL_MASK, need)) {
-        warp_compact_lists<16>(list, count, thresh, need, p.k, hist_all[warp]);
+        warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist_all[warp]);
         if (thresh > -INFINITY) hmax = static_cast<int>(floorf((64.f * W - thresh) * 0.5f));
       }
       for (int c = 0; c < kHamTile; c += 32) {
@@ -262,8 +262,22 @@ __global__ void __launch_bounds__(kHamQ) hamming_scan_kernel(HamParams p) {
       }
     }
     const bool need = valid_q && count > p.k;
-    warp_compact_lists<16>(list, count, thresh, need, p.k, hist_all[warp]);
+    warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist_all[warp]);
     if (valid_q) p.counts[static_cast<size_t>(q) * p.n_splits + split] = count;
+  }
+}
+
+template <int EPL>
+static void launch_hamming(int W, int grid, const HamParams& prm, cudaStream_t s) {
+  switch (W) {
+    case 2: hamming_scan_kernel<2, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
+    case 4: hamming_scan_kernel<4, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
+    case 6: hamming_scan_kernel<6, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
+    case 8: hamming_scan_kernel<8, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
+    case 10: hamming_scan_kernel<10, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
+    case 12: hamming_scan_kernel<12, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
+    case 14: hamming_scan_kernel<14, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
+    default: hamming_scan_kernel<16, EPL><<<grid, kHamQ, 0, s>>>(prm); break;
   }
 }
 
@@ -305,7 +319,9 @@ static HamPlan ham_plan(int B, int N, int k) {
   h.n_qg = (B + kHamQ - 1) / kHamQ;
   const int n_tiles = std::max(1, (N + kHamTile - 1) / kHamTile);
   h.n_splits = std::max(1, std::min(n_tiles, (4 * num_sms()) / h.n_qg));
-  h.cap = std::min(512, ((k + kHamTile + 32) + 31) / 32 * 32);
+  // k survivors + one tile of appends, multiple of 32: <= 512 entries (16 per
+  // lane in the register compaction) up to k = 352, <= 1184 (40 per lane) above
+  h.cap = ((k + kHamTile + 32) + 31) / 32 * 32;
   return h;
 }
 static size_t ham_ws_bytes(int B, int N, int k) {
@@ -407,8 +423,8 @@ int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, int B, 
     set_last_error("hamming_topk: W must be even and <= 16 words");
     return RB_ERR_UNSUPPORTED;
   }
-  if (k > 384) {
-    set_last_error("hamming_topk: k > 384 is not supported by the full-scan kernel");
+  if (k > 1024) {
+    set_last_error("hamming_topk: k > 1024 is not supported by the full-scan kernel");
     return RB_ERR_UNSUPPORTED;
   }
   if (B == 0) return RB_OK;
@@ -428,16 +444,10 @@ int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, int B, 
   HamParams prm{reinterpret_cast<const uint64_t*>(query_bits), reinterpret_cast<const uint64_t*>(item_bits), B, N, W, k,
                 h.n_qg, h.n_splits, h.cap, lists, lcounts};
   const int grid = std::min(h.n_qg * h.n_splits, 4 * num_sms());
-  switch (W) {
-    case 2: hamming_scan_kernel<2><<<grid, kHamQ, 0, s>>>(prm); break;
-    case 4: hamming_scan_kernel<4><<<grid, kHamQ, 0, s>>>(prm); break;
-    case 6: hamming_scan_kernel<6><<<grid, kHamQ, 0, s>>>(prm); break;
-    case 8: hamming_scan_kernel<8><<<grid, kHamQ, 0, s>>>(prm); break;
-    case 10: hamming_scan_kernel<10><<<grid, kHamQ, 0, s>>>(prm); break;
-    case 12: hamming_scan_kernel<12><<<grid, kHamQ, 0, s>>>(prm); break;
-    case 14: hamming_scan_kernel<14><<<grid, kHamQ, 0, s>>>(prm); break;
-    default: hamming_scan_kernel<16><<<grid, kHamQ, 0, s>>>(prm); break;
-  }
+  if (h.cap <= 512)
+    launch_hamming<16>(W, grid, prm, s);
+  else
+    launch_hamming<40>(W, grid, prm, s);
   const int rc = check_launch();
   if (rc != RB_OK) return rc;
   return merge_lists(lists, lcounts, B, h.n_splits, h.cap, k, 0, out_ids, out_scores, nullptr, s);

@@ -54,8 +54,7 @@ int rb_abi_version(void) { return 1; }
 int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* bytes) {
   if (bytes == nullptr) return fail(RB_ERR_INVALID_ARG, "bytes is null");
   if (B < 0 || N < 0 || D <= 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk: bad shape or k");
-  (void)dtype;
-  *bytes = dense_workspace_bytes(B, N, k);
+  *bytes = dense_workspace_bytes(B, N, k, dense_row_bytes(D, dtype));
   return RB_OK;
 }
 
@@ -72,15 +71,16 @@ struct SharedSeed {
 static int dense_check(int elem, const void* queries, const float* q_scale, const void* items, const float* x_scale,
                        int B, int N, int D, int k, const char* what) {
   if (B < 0 || N < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, std::string(what) + ": bad B, N or k");
-  if (k > 256) return fail(RB_ERR_UNSUPPORTED, std::string(what) + ": k > 256 is not supported");
+  if (k > 1024) return fail(RB_ERR_UNSUPPORTED, std::string(what) + ": k > 1024 is not supported");
   const int row_bytes = (elem == 2) ? D : 2 * D;
-  if (row_bytes != 128 && row_bytes != 256)
-    return fail(RB_ERR_UNSUPPORTED,
-                std::string(what) + ": rows must be 128 or 256 bytes (D = 64/128 fp16/bf16, 128/256 int8)");
+  if (row_bytes != 128 && row_bytes != 256 && row_bytes != 512)
+    return fail(RB_ERR_UNSUPPORTED, std::string(what) +
+                                        ": rows must be 128, 256 or 512 bytes (D = 64/128/256 fp16/bf16, "
+                                        "128/256/512 int8)");
   if (B > 0 && N > 0) {
     if (!aligned16(queries) || !aligned16(items)) return fail(RB_ERR_INVALID_ARG, std::string(what) + ": 16-byte alignment");
-    if (elem == 2 && (q_scale == nullptr || x_scale == nullptr || !aligned16(x_scale)))
-      return fail(RB_ERR_INVALID_ARG, std::string(what) + ": scales must be given (item scales 16-byte aligned)");
+    if (elem == 2 && x_scale != nullptr && !aligned16(x_scale))
+      return fail(RB_ERR_INVALID_ARG, std::string(what) + ": item scales must be 16-byte aligned");
   }
   return RB_OK;
 }
@@ -119,11 +119,14 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
     else fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, stream);
     return cudaGetLastError() == cudaSuccess ? RB_OK : fail(RB_ERR_CUDA, "fill_empty launch failed");
   }
-  const size_t need = dense_workspace_bytes(B, N, k);
+  const int row_bytes = (elem == 2) ? D : 2 * D;
+  if (filter != nullptr && (k > 384 || row_bytes > 256))
+    return fail(RB_ERR_UNSUPPORTED, "dense_topk_filtered: k <= 384 and rows of up to 256 bytes");
+  const size_t need = dense_workspace_bytes(B, N, k, row_bytes);
   if (workspace == nullptr || workspace_bytes < need) return fail(RB_ERR_WORKSPACE, "dense_topk: workspace too small");
 
   DensePlan pl;
-  dense_plan(B, N, k, pl, shared ? shared->n_total : N);
+  dense_plan(B, N, k, row_bytes, pl, shared ? shared->n_total : N);
   const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
   if (cudaMemsetAsync(d.err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
 
@@ -162,11 +165,11 @@ int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, i
   if (B == 0) return RB_OK;
   if (out_vals == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_seed_sample: null output");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  const size_t need = dense_workspace_bytes(B, N, k);
+  const size_t need = dense_workspace_bytes(B, N, k, 2 * D);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(RB_ERR_WORKSPACE, "dense_seed_sample: workspace too small");
   DensePlan pl;
-  dense_plan(B, N, k, pl, std::max<int64_t>(n_total, N));
+  dense_plan(B, N, k, 2 * D, pl, std::max<int64_t>(n_total, N));
   const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
   if (N == 0 || pl.sample_stride == 0) {
     // nothing sampled on this shard: k times -inf per query
@@ -259,7 +262,7 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
     return RB_OK;
   }
   DensePlan pl;
-  dense_plan(B, N, k, pl, N);
+  dense_plan(B, N, k, dense_row_bytes(D, dtype), pl, N);
   *n_launches = (pl.sample_stride > 0) ? 4 : 2;
   return RB_OK;
 }

@@ -81,20 +81,24 @@ __device__ __forceinline__ void split_range(int split, int n_splits, int pass_ti
 // For int8 (ELEM 2) the registers first hold int32 dots, turned here into the
 // exact fp32 score (fp32(dot) * q_scale) * item_scale, left to right as the
 // reference dequantizes (ops/official/adapter.py:338-367).
-template <int MODE, int NCH, int ELEM, bool FILT>
+template <int MODE, int NCH, int ELEM, bool FILT, int KB>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list) {
   if constexpr (ELEM == 2) {
-    const float qs = valid_q ? p.q_scale[q] : 0.f;
+    // null scale arrays mean unit scales (the score is then the raw dot)
+    const float qs = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
     const bool full = row0 + NCH * 32 <= static_cast<uint32_t>(p.N);
+    const bool unit_x = p.x_scale == nullptr;
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
         const uint32_t id = row0 + ch * 32 + 4 * j4;
         float4 xs;
-        if (full) {
+        if (unit_x) {
+          xs = make_float4(1.f, 1.f, 1.f, 1.f);
+        } else if (full) {
           xs = __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
         } else {
           xs.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
@@ -105,8 +109,13 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         const float xv[4] = {xs.x, xs.y, xs.z, xs.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          // |dot| <= 2^22 for D <= 256: exact int32 -> fp32 through the fp32 magic constant
-          const float f = __uint_as_float(r[ch][4 * j4 + u] + 0x4B400000u) - 12582912.0f;
+          // |dot| <= 2^22 for D <= 256: exact int32 -> fp32 through the fp32 magic
+          // constant; D = 512 reaches 2^23, still exact in fp32 (< 2^24) by conversion
+          float f;
+          if constexpr (KB <= 2)
+            f = __uint_as_float(r[ch][4 * j4 + u] + 0x4B400000u) - 12582912.0f;
+          else
+            f = __int2float_rn(static_cast<int>(r[ch][4 * j4 + u]));
           r[ch][4 * j4 + u] = __float_as_uint(__fmul_rn(__fmul_rn(f, qs), xv[u]));
         }
       }
@@ -387,7 +396,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        process_chunks<MODE, 4, ELEM, FILT>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -676,7 +685,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
-        process_chunks<MODE, 4, ELEM, FILT>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
         if (++acc == kAcc) {
           acc = 0;
           acc_phase ^= 1;
@@ -765,6 +774,28 @@ static cudaError_t launch_dense_scan_2sm(const DenseScanParams& prm, int n_pairs
   return cudaGetLastError();
 }
 
+// Picks the kernel for a pass: MODE 1 (sampling) or MODE 0 with the list
+// compaction's entries per lane (40 only in one-group kernels, and not with
+// attribute filters, whose lists stay within 512 entries).
+template <int ELEM, int KB, int NG, int ST, bool F>
+static cudaError_t launch_2sm_variant(int mode, int epl, const DenseScanParams& prm, int n_pairs,
+                                      cudaStream_t stream) {
+  if (mode == 1) return launch_dense_scan_2sm<1, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream);
+  if (epl == 8) return launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream);
+  if (epl == 16) return launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 16, F>(prm, n_pairs, stream);
+  if constexpr (NG == 1 && !F) return launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 40, F>(prm, n_pairs, stream);
+  return cudaErrorInvalidConfiguration;
+}
+
+template <int ELEM, int KB, int NG, int ST, bool F>
+static cudaError_t launch_1sm_variant(int mode, int epl, const DenseScanParams& prm, int grid, cudaStream_t stream) {
+  if (mode == 1) return launch_dense_scan<1, ELEM, KB, NG, ST, 8, F>(prm, grid, stream);
+  if (epl == 8) return launch_dense_scan<0, ELEM, KB, NG, ST, 8, F>(prm, grid, stream);
+  if (epl == 16) return launch_dense_scan<0, ELEM, KB, NG, ST, 16, F>(prm, grid, stream);
+  if constexpr (NG == 1 && !F) return launch_dense_scan<0, ELEM, KB, NG, ST, 40, F>(prm, grid, stream);
+  return cudaErrorInvalidConfiguration;
+}
+
 // CTA pairs of the 2-SM kernel that fit on the device at once.
 static int max_pairs() {
   static int n = 0;
@@ -801,11 +832,12 @@ static int max_pairs() {
 namespace rb {
 
 int list_cap(int k) {
-  // room for k survivors + one 128-item tile of appends; multiple of 32; <= 512
-  // (the register-resident compaction holds 16 entries per lane)
-  int cap = ((k + 128) + 31) / 32 * 32;
-  return std::min(cap, 512);
+  // room for k survivors + one 128-item tile of appends; multiple of 32
+  return ((k + 128) + 31) / 32 * 32;
 }
+
+// Entries per lane of the register-resident list compaction for a list of cap.
+static int dense_epl(int cap) { return cap <= 256 ? 8 : (cap <= 512 ? 16 : 40); }
 
 int num_sms() {
   static int n = 0;
@@ -818,11 +850,14 @@ int num_sms() {
   return n;
 }
 
-void dense_plan(int B, int N, int k, DensePlan& pl, int64_t n_total) {
-  // B > 128: 2-SM kernel, 256 queries per group, 1 or 2 groups per CTA pair.
+void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_total) {
+  // B > 128: 2-SM kernel, 256 queries per group, 1 or 2 groups per CTA pair
+  // (one for 512-byte rows, whose operand tiles fill shared memory, and for
+  // lists past 512 entries, whose compaction needs the registers of a
+  // 6-warp CTA).
   pl.two_sm = B > kQTile;
   if (pl.two_sm) {
-    pl.ng = B <= 2 * kQTile ? 1 : 2;
+    pl.ng = (B <= 2 * kQTile || row_bytes > 256 || list_cap(k) > 512) ? 1 : 2;
     pl.n_qsg = (B + pl.ng * 2 * kQTile - 1) / (pl.ng * 2 * kQTile);
     pl.n_splits = std::max(1, max_pairs() / pl.n_qsg);
     pl.n_lists = pl.n_splits;
@@ -859,9 +894,9 @@ size_t dense_chunk_stride(const DensePlan& pl) {
   return static_cast<size_t>((pl.tiles + pl.sample_stride - 1) / pl.sample_stride) * 4;
 }
 
-size_t dense_workspace_bytes(int B, int N, int k) {
+size_t dense_workspace_bytes(int B, int N, int k, int row_bytes) {
   DensePlan pl;
-  dense_plan(B, N, k, pl, N);
+  dense_plan(B, N, k, row_bytes, pl, N);
   size_t lists = static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2);
   size_t counts = static_cast<size_t>(B) * pl.n_lists * sizeof(int);
   size_t th = 2 * static_cast<size_t>(B) * sizeof(float);
@@ -906,32 +941,32 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
   const int n_tasks = pl.n_qsg * pl.n_splits;
   cudaError_t e = cudaSuccess;
   const int kb = row_bytes / 128;
+  const int epl = dense_epl(pl.cap);
   bool handled = false;
   if (pl.two_sm) {
     const int n_pairs = std::min(n_tasks, max_pairs());
-#define RB_DISPATCH2F(ELEM, KB, NG, ST, F)                                                          \
-  if (!handled && elem == ELEM && kb == KB && pl.ng == NG && filtered == F) {                        \
-    if (mode == 1)                                                                                   \
-      e = launch_dense_scan_2sm<1, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream);                    \
-    else                                                                                             \
-      e = (pl.cap <= 256) ? launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream)   \
-                          : launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 16, F>(prm, n_pairs, stream); \
-    handled = true;                                                                                  \
+#define RB_DISPATCH2F(ELEM, KB, NG, ST, F)                                                  \
+  if (!handled && elem == ELEM && kb == KB && pl.ng == NG && filtered == F) {                \
+    e = launch_2sm_variant<ELEM, KB, NG, ST, F>(mode, epl, prm, n_pairs, stream);            \
+    handled = true;                                                                          \
   }
 #define RB_DISPATCH2(ELEM, KB, NG, ST) RB_DISPATCH2F(ELEM, KB, NG, ST, false)
     RB_DISPATCH2(0, 1, 1, 12)
     RB_DISPATCH2(0, 1, 2, 12)
     RB_DISPATCH2(0, 2, 1, 8)
     RB_DISPATCH2(0, 2, 2, 8)
+    RB_DISPATCH2(0, 4, 1, 4)
     RB_DISPATCH2(1, 1, 1, 12)
     RB_DISPATCH2(1, 1, 2, 12)
     RB_DISPATCH2(1, 2, 1, 8)
     RB_DISPATCH2(1, 2, 2, 8)
+    RB_DISPATCH2(1, 4, 1, 4)
     RB_DISPATCH2(2, 1, 1, 12)
     RB_DISPATCH2(2, 1, 2, 12)
     RB_DISPATCH2(2, 2, 1, 8)
     RB_DISPATCH2(2, 2, 2, 8)
-    // attribute-filtered variants (fp16 / bf16 only)
+    RB_DISPATCH2(2, 4, 1, 4)
+    // attribute-filtered variants (fp16 / bf16, rows of up to 256 bytes)
     RB_DISPATCH2F(0, 1, 1, 12, true)
     RB_DISPATCH2F(0, 1, 2, 12, true)
     RB_DISPATCH2F(0, 2, 1, 8, true)
@@ -940,32 +975,31 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
     RB_DISPATCH2F(1, 1, 2, 12, true)
     RB_DISPATCH2F(1, 2, 1, 8, true)
     RB_DISPATCH2F(1, 2, 2, 8, true)
-#undef RB_DISPATCH2F
 #undef RB_DISPATCH2
+#undef RB_DISPATCH2F
   } else {
     const int grid = std::min(n_tasks, num_sms());
-#define RB_DISPATCHF(ELEM, KB, NG, ST, F)                                                     \
-  if (!handled && elem == ELEM && kb == KB && pl.ng == NG && filtered == F) {                  \
-    if (mode == 1)                                                                             \
-      e = launch_dense_scan<1, ELEM, KB, NG, ST, 8, F>(prm, grid, stream);                     \
-    else                                                                                       \
-      e = (pl.cap <= 256) ? launch_dense_scan<0, ELEM, KB, NG, ST, 8, F>(prm, grid, stream)    \
-                          : launch_dense_scan<0, ELEM, KB, NG, ST, 16, F>(prm, grid, stream);  \
-    handled = true;                                                                            \
+#define RB_DISPATCHF(ELEM, KB, NG, ST, F)                                                   \
+  if (!handled && elem == ELEM && kb == KB && pl.ng == NG && filtered == F) {                \
+    e = launch_1sm_variant<ELEM, KB, NG, ST, F>(mode, epl, prm, grid, stream);               \
+    handled = true;                                                                          \
   }
 #define RB_DISPATCH(ELEM, KB, NG, ST) RB_DISPATCHF(ELEM, KB, NG, ST, false)
     RB_DISPATCH(0, 1, 1, 8)
     RB_DISPATCH(0, 2, 1, 4)
+    RB_DISPATCH(0, 4, 1, 2)
     RB_DISPATCH(1, 1, 1, 8)
     RB_DISPATCH(1, 2, 1, 4)
+    RB_DISPATCH(1, 4, 1, 2)
     RB_DISPATCH(2, 1, 1, 8)
     RB_DISPATCH(2, 2, 1, 4)
+    RB_DISPATCH(2, 4, 1, 2)
     RB_DISPATCHF(0, 1, 1, 8, true)
     RB_DISPATCHF(0, 2, 1, 4, true)
     RB_DISPATCHF(1, 1, 1, 8, true)
     RB_DISPATCHF(1, 2, 1, 4, true)
-#undef RB_DISPATCHF
 #undef RB_DISPATCH
+#undef RB_DISPATCHF
   }
   if (!handled) {
     set_last_error("dense scan: unsupported dtype / row width");

@@ -285,9 +285,12 @@ __global__ void __launch_bounds__(kMergeThreads) row_kth_kernel(const float* __r
   __shared__ SelectShared sh;
   const int q = blockIdx.x;
   const int total = n * nseg;
-  auto value_at = [&](int i) -> float {
-    const int seg = i / n;
-    return vals[seg * seg_stride + static_cast<int64_t>(q) * stride + (i - seg * n)];
+  // every value of the row once, each thread a strided share of every segment
+  auto for_each = [&](auto&& f) {
+    for (int seg = 0; seg < nseg; ++seg) {
+      const float* row = vals + seg * seg_stride + static_cast<int64_t>(q) * stride;
+      for (int i = threadIdx.x; i < n; i += kMergeThreads) f(row[i]);
+    }
   };
   uint32_t prefix = 0, mask = 0;
   if (total >= k) {
@@ -295,11 +298,10 @@ __global__ void __launch_bounds__(kMergeThreads) row_kth_kernel(const float* __r
     for (int shift = 21; shift >= 10; shift -= 11) {
       for (int i = threadIdx.x; i < kBins; i += kMergeThreads) sh.hist[i] = 0;
       __syncthreads();
-      for (int i = threadIdx.x; i < total; i += kMergeThreads) {
-        const float v = value_at(i);
+      for_each([&](float v) {
         const uint32_t key = isnan(v) ? 0u : f2ord(v);
         if ((key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & 0x7ffu], 1u);
-      }
+      });
       __syncthreads();
       block_find_digit_n<kBins / kMergeThreads>(sh, need);
       prefix |= sh.digit << shift;
@@ -316,14 +318,13 @@ __global__ void __launch_bounds__(kMergeThreads) row_kth_kernel(const float* __r
   if (out_vals == nullptr) return;
   __syncthreads();
   float* dst = out_vals + static_cast<int64_t>(q) * k;
-  for (int i = threadIdx.x; i < total; i += kMergeThreads) {
-    const float v = value_at(i);
+  for_each([&](float v) {
     const uint32_t key = isnan(v) ? 0u : f2ord(v);
     if (key >= prefix) {
       const uint32_t slot = atomicAdd(&sh.n_out, 1u);
       if (slot < static_cast<uint32_t>(k)) dst[slot] = v;
     }
-  }
+  });
   __syncthreads();
   for (int i = static_cast<int>(sh.n_out) + threadIdx.x; i < k; i += kMergeThreads) dst[i] = -INFINITY;
 }

@@ -597,8 +597,25 @@ def int8_topk(query: Tensor, item_codes: Tensor, item_scales: Tensor, k: int) ->
         raise ValueError("query and item_codes must have the same D")
     _require_cuda(query, item_codes, item_scales)
     check_contiguous(item_codes=item_codes, item_scales=item_scales)
-    xs = item_scales.to(torch.float32)
+    xs = item_scales.to(torch.float32).contiguous()
     codes, qs = quantize_int8(query)
+    return int8_codes_topk(codes, qs, item_codes, xs, k)
+
+
+def int8_codes_topk(
+    query_codes: Tensor, query_scales: Tensor | None, item_codes: Tensor, item_scales: Tensor | None, k: int,
+    id_offset: int = 0,
+) -> tuple[Tensor, Tensor]:
+    """Tensor-core int8 scoring of already-quantized queries (C-ABI
+    ``rb_dense_topk_i8``): score ``(fp32(dot) * query_scale) * item_scale``; a
+    ``None`` scale means 1 (the score is then the exact int32 dot)."""
+    if query_codes.dtype != torch.int8 or item_codes.dtype != torch.int8:
+        raise TypeError("query_codes and item_codes must be int8")
+    if query_codes.dim() != 2 or item_codes.dim() != 2 or query_codes.shape[1] != item_codes.shape[1]:
+        raise ValueError("query_codes [B, D] and item_codes [N, D] with the same D")
+    _require_cuda(query_codes, item_codes)
+    check_contiguous(item_codes=item_codes)
+    codes = query_codes.contiguous()
     b, d = codes.shape
     n = item_codes.shape[0]
     dev = codes.device
@@ -606,14 +623,35 @@ def int8_topk(query: Tensor, item_codes: Tensor, item_scales: Tensor, k: int) ->
     scores = torch.empty((b, k), dtype=torch.float32, device=dev)
     if b == 0:
         return ids, scores
+    qs = None if query_scales is None else query_scales.to(torch.float32).contiguous()
+    xs = None if item_scales is None else item_scales.to(torch.float32).contiguous()
     lib = _lib.lib()
     nb = ctypes.c_size_t(0)
     _lib.check(lib.rb_dense_topk_workspace_size(b, n, d, _lib.RB_I8, k, ctypes.byref(nb)), "int8_topk")
     ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
-    rc = lib.rb_dense_topk_i8(_ptr(codes), _ptr(qs), _ptr(item_codes), _ptr(xs), b, n, d, k, 0, _ptr(ids),
-                              _ptr(scores), _ptr(ws), ws.numel(), _stream_ptr(dev))
+    with torch.cuda.device(dev):
+        rc = lib.rb_dense_topk_i8(_ptr(codes), _ptr(qs), _ptr(item_codes), _ptr(xs), b, n, d, k, int(id_offset),
+                                  _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream_ptr(dev))
     _lib.check(rc, "int8_topk")
     return ids, scores
+
+
+def bits_to_pm1(bits: Tensor) -> Tensor:
+    """1-bit codes ``[N, W]`` int64 → ``[N, 64 W]`` int8 of ±1 (+1 where the bit
+    is set; C-ABI ``rb_bits_to_pm1``). The int8 dot of two such rows is the
+    1-bit match score ``64 W − 2·popcount(q ^ x)``."""
+    if bits.dim() != 2 or bits.dtype != torch.int64:
+        raise ValueError("bits must be [N, W] int64")
+    _require_cuda(bits)
+    bits = bits.contiguous()
+    n, w = bits.shape
+    out = torch.empty((n, 64 * w), dtype=torch.int8, device=bits.device)
+    if n == 0:
+        return out
+    with torch.cuda.device(bits.device):
+        rc = _lib.lib().rb_bits_to_pm1(_ptr(bits), n, w, _ptr(out), _stream_ptr(bits.device))
+    _lib.check(rc, "bits_to_pm1")
+    return out
 
 
 @int8_topk.register_fake
@@ -623,10 +661,12 @@ def _(query, item_codes, item_scales, k):
 
 
 __all__ = [
+    "bits_to_pm1",
     "bloom_build",
     "dense_topk_filtered",
     "check_contiguous",
     "int8_topk",
+    "int8_codes_topk",
     "clause_compact",
     "clause_mask",
     "clause_mask_scores",

@@ -156,9 +156,11 @@ class GraphedSearch:
     kernel attributes). ``search(query)`` copies ``query`` (host — pinned for an
     asynchronous copy — or device) into the static input, replays, and returns
     the static ``(ids, scores)`` outputs, which the next call overwrites. Every
-    rank must construct and call it the same number of times."""
+    rank must construct and call it the same number of times. Graphs given the
+    same ``pool`` (``torch.cuda.graph_pool_handle()``) share memory and must
+    then be replayed in the order they were made, never concurrently."""
 
-    def __init__(self, index: ShardedDenseTopK, example: Tensor, warmup: int = 2) -> None:
+    def __init__(self, index: ShardedDenseTopK, example: Tensor, warmup: int = 2, pool=None) -> None:
         dev = index.items.device
         self.index = index
         self.query = example.to(device=dev, dtype=index.items.dtype).contiguous().clone()
@@ -170,7 +172,7 @@ class GraphedSearch:
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        with torch.cuda.graph(self.graph, pool=pool):
             self.ids, self.scores = index.search(self.query)
         torch.cuda.synchronize(dev)
 
@@ -185,3 +187,51 @@ class GraphedSearch:
     def release(self) -> None:
         """Drops the graph (before the process group is destroyed)."""
         self.graph.reset()
+
+
+class ShardedOneBitRerank:
+    """Row-sharded LiNR V3 cascade (config 5): 1-bit top-``pool`` candidates,
+    then exact rescoring to the top ``k``, with two exchanges.
+
+    1. every rank takes its shard's 1-bit top-``pool`` (global ids, tensor
+       cores), one all-gather + merge gives every rank the global pool — the
+       single-GPU pool exactly (integer scores, ties to the lower id);
+    2. every rank rescores the pool entries it owns (its rows of the fp16/bf16
+       table, ``fused_masked_knn_topk``), one all-gather + merge gives the top k.
+
+    ``item_bits`` ``[n_r, W]`` int64 and ``item_embs`` ``[n_r, D]`` are this
+    rank's rows, starting at global id ``id_offset``. Stage-2 ties (equal fp32
+    scores) between items of different shards go to the lower global id."""
+
+    def __init__(self, item_bits: Tensor, item_embs: Tensor, id_offset: int, pool: int, k: int, group=None) -> None:
+        from retrieve_b200.bitknn import PackedBitsIndex
+
+        if k > pool:
+            raise ValueError(f"k={k} exceeds candidate_pool={pool}")
+        if item_bits.shape[0] != item_embs.shape[0]:
+            raise ValueError("item_bits and item_embs must hold the same rows")
+        ops.check_contiguous(item_embs=item_embs)
+        self.bits = PackedBitsIndex(item_bits)
+        self.items = item_embs
+        self.id_offset = int(id_offset)
+        self.pool = int(pool)
+        self.k = int(k)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+
+    def _exchange(self, ids: Tensor, scores: Tensor, k: int) -> tuple[Tensor, Tensor]:
+        if self.world == 1:
+            return ids, scores
+        return exchange_and_merge(ids, scores, k, self.group)
+
+    def search(self, query: Tensor, query_bits: Tensor) -> tuple[Tensor, Tensor]:
+        ids1, sc1 = self.bits.topk(query_bits, self.pool, self.id_offset)
+        pool_ids, _ = self._exchange(ids1, sc1, self.pool)
+        # this shard's rows of the pool, as local rows (others fall outside
+        # [0, n_r) and are not scored)
+        local = pool_ids - self.id_offset
+        counts = torch.full((local.shape[0],), local.shape[1], dtype=torch.int64, device=local.device)
+        k2 = min(self.k, local.shape[1])
+        ids2, sc2 = ops.fused_masked_knn_topk(query, self.items, local, counts, k2)
+        ids2 = torch.where(ids2 >= 0, ids2 + self.id_offset, ids2)
+        return self._exchange(ids2, sc2, self.k)

@@ -48,3 +48,37 @@ def test_int8_global_scale_equals_silvertorch_full_probe():
     ids, scores = ops.int8_topk(q.cuda(), codes.cuda(), torch.full((n,), gscale).cuda(), k)
     ref_ids, ref_scores = knn.silvertorch_fullprobe(q.numpy(), codes.numpy(), gscale, k)
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+
+
+@pytest.mark.parametrize("d", [128, 256])
+def test_int8_tensor_core_dots_equal_reference_fused_kmean_ann(d):
+    """Unit scales: every returned score is the raw int32 dot as fp32, which must
+    equal SilverTorch's own CPU scorer's dot for that (query, item)
+    (tests/golden/make_golden_int8.py), and the ids are its top-k with ties to
+    the lower id."""
+    import ctypes
+    from pathlib import Path
+
+    from oracle.select import topk_strict
+    from retrieve_b200 import _lib
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "golden_int8.npz")
+    qc, xc, dots = g[f"queries_{d}"], g[f"items_{d}"], g[f"dots_{d}"]
+    b, n, k = qc.shape[0], xc.shape[0], 100
+    q = torch.from_numpy(qc).cuda()
+    x = torch.from_numpy(xc).cuda()
+    qs = torch.ones(b, dtype=torch.float32, device="cuda")
+    xs = torch.ones(n, dtype=torch.float32, device="cuda")
+    ids = torch.empty(b, k, dtype=torch.int64, device="cuda")
+    scores = torch.empty(b, k, dtype=torch.float32, device="cuda")
+    lib = _lib.lib()
+    nb = ctypes.c_size_t(0)
+    _lib.check(lib.rb_dense_topk_workspace_size(b, n, d, _lib.RB_I8, k, ctypes.byref(nb)), "ws")
+    ws = torch.empty(max(nb.value, 256), dtype=torch.uint8, device="cuda")
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    rc = lib.rb_dense_topk_i8(vp(q), vp(qs), vp(x), vp(xs), b, n, d, k, 0, vp(ids), vp(scores), vp(ws), ws.numel(),
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc, "dense_topk_i8")
+    torch.cuda.synchronize()
+    ref_ids, ref_scores = topk_strict(dots.astype(np.float32), k)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)

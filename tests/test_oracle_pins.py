@@ -115,3 +115,19 @@ def test_gemv_oracle_is_sequential_fma():
     for k in range(128):  # fp64 emulation of fp32 FMA: exact product, one rounding per step
         acc = (q[0, k].astype(np.float64) * et[k].astype(np.float64) + acc).astype(np.float32).astype(np.float64)
     np.testing.assert_array_equal(out[0], acc.astype(np.float32))
+
+
+GOLDEN_INT8 = np.load(Path(__file__).resolve().parent / "golden" / "golden_int8.npz")
+
+
+@pytest.mark.parametrize("d", [128, 256])
+def test_int8_raw_dots_match_reference_fused_kmean_ann(d):
+    # raw int32 dots of SilverTorch's CPU scorer (tests/golden/make_golden_int8.py)
+    q = GOLDEN_INT8[f"queries_{d}"].astype(np.int64)
+    x = GOLDEN_INT8[f"items_{d}"].astype(np.int64)
+    dots = q @ x.T
+    assert np.array_equal(dots.astype(np.int32), GOLDEN_INT8[f"dots_{d}"])
+    # the oracle's dequant with unit scales is the raw dot as fp32 (|dot| < 2^24)
+    ids, scores = knn.silvertorch_fullprobe_codes(GOLDEN_INT8[f"queries_{d}"], GOLDEN_INT8[f"items_{d}"], 1.0, 1.0, 50)
+    top = np.sort(GOLDEN_INT8[f"dots_{d}"], axis=1)[:, ::-1][:, :50].astype(np.float32)
+    assert np.array_equal(scores, top)
