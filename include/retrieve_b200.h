@@ -268,19 +268,22 @@ RB_API int rb_workspace_device_error(const void* workspace, size_t workspace_byt
  * Row-sharded search with one threshold for all shards (no counterpart in the
  * reference, which is single-GPU). A shard of N of the n_total corpus rows:
  *
- *   rb_dense_seed_sample writes out_vals [B, k] fp32: per query, k chunk maxima
- *   (max of 32 consecutive items) from this shard's sampling pass, all at or
- *   above the shard's own k-th largest chunk max (-inf where the shard sampled
- *   fewer). The caller gathers every shard's [B, k] into a [W, B, k] stack
- *   (one all-gather) and passes it to
+ *   rb_dense_seed_sample writes out_vals [B, m] fp32 (1 <= m <= k): per query,
+ *   m chunk maxima (max of 32 consecutive items) from this shard's sampling
+ *   pass, all at or above the shard's own m-th largest chunk max (-inf where
+ *   the shard sampled fewer). The caller gathers every shard's [B, m] into a
+ *   [W, B, m] stack (one all-gather) and passes it to
  *
  *   rb_dense_topk_seeded: as rb_dense_topk on the shard, with the full pass
- *   seeded by the k-th largest value of the union of the W samples. That is a
- *   lower bound on the k-th best score of the whole corpus (k distinct items
- *   reach it), so every item of the global top-k is kept by its shard and the
- *   per-shard results merge (rb_merge_topk) to the exact global top-k, while
- *   each shard appends only about 1/W of the candidates a shard-local seed lets
- *   through. A shard may return fewer than k real entries (-1 / -inf pads).
+ *   seeded by the k-th largest value of the union of the W samples. Any k of
+ *   those values come from k distinct chunks, so that is a lower bound on the
+ *   k-th best score of the whole corpus (whatever m is): every item of the
+ *   global top-k is kept by its shard and the per-shard results merge
+ *   (rb_merge_pairs / rb_merge_topk) to the exact global top-k, while each
+ *   shard appends only about 1/W of the candidates a shard-local seed lets
+ *   through. m about 2k/W keeps the bound as tight as m = k unless one shard
+ *   holds more than m of the global top chunks. A shard may return fewer than
+ *   k real entries (-1 / -inf pads).
  *
  * Both use the workspace of rb_dense_topk_workspace_size(B, N, ...); the same
  * n_total must be given to both calls. fp16 / bf16 only.
@@ -293,10 +296,10 @@ RB_API int rb_workspace_device_error(const void* workspace, size_t workspace_byt
  * reduces to the global top-k (ids int64, -1 / -inf pads).
  */
 RB_API int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
-                                int64_t n_total, float* out_vals, void* workspace, size_t workspace_bytes,
+                                int m, int64_t n_total, float* out_vals, void* workspace, size_t workspace_bytes,
                                 void* stream);
 RB_API int rb_dense_topk_seeded(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
-                                int64_t id_offset, int64_t n_total, const float* seed_vals, int W,
+                                int64_t id_offset, int64_t n_total, const float* seed_vals, int W, int m,
                                 int64_t* out_ids, float* out_scores, uint64_t* out_pairs, void* workspace,
                                 size_t workspace_bytes, void* stream);
 RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,

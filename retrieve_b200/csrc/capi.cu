@@ -63,8 +63,8 @@ int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* 
 // [W, B, k] stack of every shard's rb_dense_seed_sample output and n_total the
 // corpus size over all shards.
 struct SharedSeed {
-  const float* vals;
-  int W;
+  const float* vals;  // [W, B, m]
+  int W, m;
   int64_t n_total;
 };
 
@@ -134,8 +134,8 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   const float* seed = nullptr;
   if (shared != nullptr) {
     // k-th largest of the union of the shards' samples (a [W, B, k] stack)
-    rc = row_kth_lower_bound(shared->vals, B, k, k, shared->W, static_cast<int64_t>(B) * k, k, d.thresh, nullptr,
-                             stream);
+    rc = row_kth_lower_bound(shared->vals, B, shared->m, shared->m, shared->W, static_cast<int64_t>(B) * shared->m,
+                             k, d.thresh, nullptr, stream);
     if (rc != RB_OK) return rc;
     seed = d.thresh;
   } else if (pl.sample_stride > 0) {
@@ -156,7 +156,7 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, out_pairs, stream);
 }
 
-int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
+int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int m,
                          int64_t n_total, float* out_vals, void* workspace, size_t workspace_bytes, void* stream_) {
   if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_seed_sample: dtype must be f16 or bf16");
   const int elem = dtype == RB_BF16 ? 1 : 0;
@@ -164,6 +164,7 @@ int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, i
   if (rc != RB_OK) return rc;
   if (B == 0) return RB_OK;
   if (out_vals == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_seed_sample: null output");
+  if (m < 1 || m > k) return fail(RB_ERR_INVALID_ARG, "dense_seed_sample: need 1 <= m <= k");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const size_t need = dense_workspace_bytes(B, N, k, 2 * D);
   if (workspace == nullptr || workspace_bytes < need)
@@ -172,8 +173,8 @@ int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, i
   dense_plan(B, N, k, 2 * D, pl, std::max<int64_t>(n_total, N));
   const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
   if (N == 0 || pl.sample_stride == 0) {
-    // nothing sampled on this shard: k times -inf per query
-    return row_kth_lower_bound(nullptr, B, 0, 0, 1, 0, k, d.thresh, out_vals, stream);
+    // nothing sampled on this shard: m times -inf per query
+    return row_kth_lower_bound(nullptr, B, 0, 0, 1, 0, m, d.thresh, out_vals, stream);
   }
   if (cudaMemsetAsync(d.err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
   float* chunk_max = reinterpret_cast<float*>(d.lists);
@@ -181,18 +182,21 @@ int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, i
                        nullptr, nullptr, nullptr);
   if (rc != RB_OK) return rc;
   const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
-  return row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, k, d.thresh, out_vals, stream);
+  // m values at or above the shard's m-th largest chunk max: its top m, up to
+  // the 22-bit rounding of the bound
+  return row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, m, d.thresh, out_vals, stream);
 }
 
 int rb_dense_topk_seeded(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
-                         int64_t id_offset, int64_t n_total, const float* seed_vals, int W, int64_t* out_ids,
+                         int64_t id_offset, int64_t n_total, const float* seed_vals, int W, int m, int64_t* out_ids,
                          float* out_scores, uint64_t* out_pairs, void* workspace, size_t workspace_bytes,
                          void* stream) {
   if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk_seeded: dtype must be f16 or bf16");
-  if (seed_vals == nullptr || W < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk_seeded: seed values missing");
+  if (seed_vals == nullptr || W < 1 || m < 1 || m > k)
+    return fail(RB_ERR_INVALID_ARG, "dense_topk_seeded: seed values missing or 1 <= m <= k violated");
   if (out_pairs != nullptr && (id_offset < 0 || id_offset + static_cast<int64_t>(N) > 0xffffffffll))
     return fail(RB_ERR_UNSUPPORTED, "dense_topk_seeded: pair output needs global ids below 2^32 - 1");
-  const SharedSeed shared{seed_vals, W, std::max<int64_t>(n_total, N)};
+  const SharedSeed shared{seed_vals, W, m, std::max<int64_t>(n_total, N)};
   return dense_topk_impl(dtype == RB_BF16 ? 1 : 0, queries, nullptr, items, nullptr, B, N, D, k, id_offset, out_ids,
                          out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, &shared,
                          reinterpret_cast<uint2*>(out_pairs));

@@ -41,8 +41,17 @@ struct SelectShared {
 // histogram with nbins = 256 * BPT bins. Thread t owns bins
 // [nbins - BPT*(t+1), nbins - BPT*t), so a prefix over threads is a suffix over
 // bins. Results land in sh.digit / sh.above / sh.in_digit.
-template <int BPT>
-__device__ __forceinline__ void block_find_digit_n(SelectShared& sh, uint32_t need) {
+// Shared memory of the row select: the histogram only (8 KB), so that a whole
+// B = 1024 batch of rows runs in one wave.
+struct RowSelectShared {
+  uint32_t hist[kBins];
+  uint32_t warp_tot[kMergeThreads / 32];
+  uint32_t digit, above, in_digit;
+  uint32_t n_out;
+};
+
+template <int BPT, class Shared>
+__device__ __forceinline__ void block_find_digit_n(Shared& sh, uint32_t need) {
   constexpr int nbins = kMergeThreads * BPT;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t b[BPT];
@@ -282,7 +291,7 @@ __global__ void __launch_bounds__(kMergeThreads) row_kth_kernel(const float* __r
                                                                 int nseg, int64_t seg_stride, int k,
                                                                 float* __restrict__ out,
                                                                 float* __restrict__ out_vals) {
-  __shared__ SelectShared sh;
+  __shared__ RowSelectShared sh;
   const int q = blockIdx.x;
   const int total = n * nseg;
   // every value of the row once, each thread a strided share of every segment

@@ -51,7 +51,9 @@ def check_contiguous(**tables: Tensor) -> None:
 # ---------------------------------------------------------------------------
 # dense_topk
 # ---------------------------------------------------------------------------
-def _dense_topk_impl(query: Tensor, item_embs: Tensor, k: int, id_offset: int = 0) -> tuple[Tensor, Tensor]:
+def _dense_topk_impl(
+    query: Tensor, item_embs: Tensor, k: int, id_offset: int = 0, ws: Tensor | None = None
+) -> tuple[Tensor, Tensor]:
     if query.dim() != 2 or item_embs.dim() != 2:
         raise ValueError("query must be [B, D] and item_embs [N, D]")
     if item_embs.dtype not in _DTYPE_CODE:
@@ -74,7 +76,8 @@ def _dense_topk_impl(query: Tensor, item_embs: Tensor, k: int, id_offset: int = 
     code = _DTYPE_CODE[item_embs.dtype]
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.rb_dense_topk_workspace_size(b, n, d, code, k, ctypes.byref(nbytes)), "dense_topk")
-    ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
+    if ws is None or ws.numel() < nbytes.value:
+        ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         rc = lib.rb_dense_topk(
             _ptr(q), _ptr(item_embs), b, n, d, code, k, int(id_offset), _ptr(ids), _ptr(scores),
@@ -96,21 +99,25 @@ def dense_workspace(query: Tensor, item_shard: Tensor, k: int) -> Tensor:
     return torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=query.device)
 
 
-def dense_seed_sample(query: Tensor, item_shard: Tensor, k: int, n_total: int, ws: Tensor | None = None) -> Tensor:
-    """Per query, k sampled chunk maxima of this shard (``[B, k]`` fp32) for the
-    threshold shared by all shards (C-ABI ``rb_dense_seed_sample``)."""
+def dense_seed_sample(
+    query: Tensor, item_shard: Tensor, k: int, n_total: int, ws: Tensor | None = None, m: int | None = None
+) -> Tensor:
+    """Per query, this shard's top ``m`` (default k) sampled chunk maxima
+    (``[B, m]`` fp32) for the threshold shared by all shards (C-ABI
+    ``rb_dense_seed_sample``)."""
+    m = k if m is None else int(m)
     _require_cuda(query, item_shard)
     check_contiguous(item_shard=item_shard)
     q = query.to(item_shard.dtype).contiguous()
     b, d = q.shape
     dev = q.device
-    out = torch.empty((b, k), dtype=torch.float32, device=dev)
+    out = torch.empty((b, m), dtype=torch.float32, device=dev)
     if b == 0:
         return out
     ws = dense_workspace(q, item_shard, k) if ws is None else ws
     with torch.cuda.device(dev):
         rc = _lib.lib().rb_dense_seed_sample(
-            _ptr(q), _ptr(item_shard), b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k, int(n_total),
+            _ptr(q), _ptr(item_shard), b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k, m, int(n_total),
             _ptr(out), _ptr(ws), ws.numel(), _stream_ptr(dev),
         )
     _lib.check(rc, "dense_seed_sample")
@@ -122,7 +129,7 @@ def dense_topk_seeded(
     ws: Tensor | None = None, pairs: bool = False,
 ) -> tuple[Tensor, Tensor] | Tensor:
     """``dense_topk_sharded`` with the full pass seeded by the union of every
-    shard's ``dense_seed_sample`` output (``seed_vals [W, B, k]`` fp32; C-ABI
+    shard's ``dense_seed_sample`` output (``seed_vals [W, B, m]`` fp32; C-ABI
     ``rb_dense_topk_seeded``). May return fewer than k real entries per row
     (``-1`` / ``-inf``); the merge over all shards is the exact global top-k.
     With ``pairs`` the result is one ``[B, k]`` int64 tensor of packed (fp32
@@ -131,8 +138,9 @@ def dense_topk_seeded(
     check_contiguous(item_shard=item_shard, seed_vals=seed_vals)
     q = query.to(item_shard.dtype).contiguous()
     b, d = q.shape
-    if seed_vals.dim() != 3 or seed_vals.shape[1:] != (b, k) or seed_vals.dtype != torch.float32:
-        raise ValueError("seed_vals must be [W, B, k] float32")
+    if seed_vals.dim() != 3 or seed_vals.shape[1] != b or not 1 <= seed_vals.shape[2] <= k \
+            or seed_vals.dtype != torch.float32:
+        raise ValueError("seed_vals must be [W, B, m] float32 with 1 <= m <= k")
     dev = q.device
     if pairs:
         out = torch.empty((b, k), dtype=torch.int64, device=dev)
@@ -146,7 +154,7 @@ def dense_topk_seeded(
         with torch.cuda.device(dev):
             rc = _lib.lib().rb_dense_topk_seeded(
                 _ptr(q), _ptr(item_shard), b, item_shard.shape[0], d, _DTYPE_CODE[item_shard.dtype], k,
-                int(id_offset), int(n_total), _ptr(seed_vals), seed_vals.shape[0],
+                int(id_offset), int(n_total), _ptr(seed_vals), seed_vals.shape[0], seed_vals.shape[2],
                 None if pairs else _ptr(ids), None if pairs else _ptr(scores), _ptr(out) if pairs else None,
                 _ptr(ws), ws.numel(), _stream_ptr(dev),
             )
@@ -193,10 +201,13 @@ def _(query, item_embs, k):
     )
 
 
-def dense_topk_sharded(query: Tensor, item_shard: Tensor, k: int, id_offset: int) -> tuple[Tensor, Tensor]:
+def dense_topk_sharded(
+    query: Tensor, item_shard: Tensor, k: int, id_offset: int, ws: Tensor | None = None
+) -> tuple[Tensor, Tensor]:
     """``dense_topk`` over one row shard of a larger corpus: ids come back global
-    (``id_offset`` + local row). Used by :mod:`retrieve_b200.shard`."""
-    return _dense_topk_impl(query, item_shard, k, id_offset)
+    (``id_offset`` + local row); ``ws``, if large enough, is the device workspace
+    (``dense_workspace``). Used by :mod:`retrieve_b200.shard`."""
+    return _dense_topk_impl(query, item_shard, k, id_offset, ws)
 
 
 # ---------------------------------------------------------------------------

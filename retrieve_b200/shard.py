@@ -103,27 +103,36 @@ class ShardedDenseTopK:
                 dist.all_reduce(t, group=group)
                 n_total = int(t.item())
         self.n_total = int(n_total)
+        # each shard sends its top m sampled chunk maxima per query: any subset
+        # keeps the union's k-th a valid bound, and about 2k/W keeps it as tight
+        # as all k unless one shard holds more than m of the global top chunks
+        self.sample_width = min(self.k, max(16, -(-2 * self.k // max(self.world, 1))))
         self._ws: Tensor | None = None
+        self._ws_batch = 0
 
     def local(self, query: Tensor) -> tuple[Tensor, Tensor]:
-        return ops.dense_topk_sharded(query, self.items, self.k, self.id_offset)
+        return ops.dense_topk_sharded(query, self.items, self.k, self.id_offset, self._workspace(query))
 
     def _workspace(self, query: Tensor) -> Tensor:
-        need = ops.dense_workspace(query, self.items, self.k).numel()
-        if self._ws is None or self._ws.numel() < need or self._ws.device != query.device:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=query.device)
+        """One persistent device workspace per index (graphs captured from it
+        all use the same buffer)."""
+        b = query.shape[0]
+        if self._ws is None or self._ws_batch < b or self._ws.device != query.device:
+            self._ws = ops.dense_workspace(query, self.items, self.k)
+            self._ws_batch = b
         return self._ws
 
     def search(self, query: Tensor) -> tuple[Tensor, Tensor]:
         if self.world == 1:
             return self.local(query)
         ws = self._workspace(query)
-        vals = ops.dense_seed_sample(query, self.items, self.k, self.n_total, ws)
+        m = self.sample_width
+        vals = ops.dense_seed_sample(query, self.items, self.k, self.n_total, ws, m)
         b = vals.shape[0]
-        gathered = torch.empty((self.world * b, self.k), dtype=vals.dtype, device=vals.device)
+        gathered = torch.empty((self.world * b, m), dtype=vals.dtype, device=vals.device)
         dist.all_gather_into_tensor(gathered, vals, group=self.group)
         pairs = ops.dense_topk_seeded(
-            query, self.items, self.k, self.id_offset, self.n_total, gathered.view(self.world, b, self.k), ws,
+            query, self.items, self.k, self.id_offset, self.n_total, gathered.view(self.world, b, m), ws,
             pairs=True,
         )
         all_pairs = torch.empty((self.world * b, self.k), dtype=pairs.dtype, device=pairs.device)

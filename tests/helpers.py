@@ -71,3 +71,19 @@ def assert_topk_close(ids, scores, ref_ids, ref_scores, *, rtol: float, atol: fl
         hit += len(rs & set(int(v) for v in a if v >= 0))
     recall = hit / max(tot, 1)
     assert recall >= min_recall, f"recall {recall} < {min_recall}"
+
+
+def assert_topk_equal_up_to_ties(ids, scores, ref_ids, ref_scores):
+    """Scores equal slot by slot (bit for bit); ids equal within every run of
+    equal scores as a set, except the row's last run, which may hold any of the
+    tied items (two valid tie orders pick different ones at the boundary)."""
+    ids = np.asarray(ids)
+    scores = np.asarray(scores, dtype=np.float32)
+    assert ids.shape == ref_ids.shape
+    assert np.array_equal(scores, ref_scores), "scores differ"
+    for r in range(ids.shape[0]):
+        s = ref_scores[r]
+        starts = np.flatnonzero(np.r_[True, s[1:] != s[:-1]])
+        ends = np.r_[starts[1:], len(s)]
+        for a, b in zip(starts[:-1], ends[:-1]):
+            assert set(ids[r, a:b].tolist()) == set(ref_ids[r, a:b].tolist()), f"row {r}: ids differ in slots {a}:{b}"

@@ -14,7 +14,7 @@ import torch
 
 from oracle import dense, knn
 from oracle.bits import pack_signs
-from tests.helpers import assert_topk_exact, make_int_rows, make_rows
+from tests.helpers import assert_topk_equal_up_to_ties, assert_topk_exact, make_int_rows, make_rows
 
 pytestmark = pytest.mark.gpu
 
@@ -129,9 +129,10 @@ def test_onebit_rerank_cascade_equals_oracle():
 @pytest.mark.parametrize("world", [2, 8])
 def test_sharded_cascade_equals_single_gpu(world):
     """The two-exchange plan, every rank's calls in sequence on one GPU; the
-    all-gather + merge is emulated by stacking + merge_topk. Real-valued rerank
-    rows: equal fp32 scores of different items (which the cross-shard merge
-    breaks by global id, one GPU by pool position) do not occur."""
+    all-gather + merge is emulated by stacking + merge_topk. The pool is the
+    single-GPU pool exactly; in the rerank, equal fp32 scores of different items
+    are ordered by global id across shards but by pool position on one GPU, so
+    ids may differ inside runs of equal scores (the scores may not)."""
     from retrieve_b200.bitknn import PackedBitsIndex, onebit_rerank_topk
     from retrieve_b200.shard import merge_topk, shard_bounds
     from retrieve_b200 import ops
@@ -151,4 +152,4 @@ def test_sharded_cascade_equals_single_gpu(world):
         st2.append((torch.where(i2 >= 0, i2 + lo, i2), s2))
     ids, scores = merge_topk(torch.stack([a for a, _ in st2]), torch.stack([s for _, s in st2]), k)
     torch.cuda.synchronize()
-    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
+    assert_topk_equal_up_to_ties(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())

@@ -22,10 +22,13 @@ from tests.helpers import assert_topk_exact, make_int_rows, mixture_rows
 pytestmark = pytest.mark.gpu
 
 
-def _sharded(q, x, k, bounds, pairs=False):
+def _sharded(q, x, k, bounds, pairs=False, m=None):
+    """m = None: the sample width ShardedDenseTopK uses (about 2k/W)."""
     n_total = x.shape[0]
+    w = len(bounds)
+    m = min(k, max(16, -(-2 * k // w))) if m is None else m
     shards = [x[lo:hi].contiguous() for lo, hi in bounds]
-    samples = torch.stack([ops.dense_seed_sample(q, s, k, n_total) for s in shards])
+    samples = torch.stack([ops.dense_seed_sample(q, s, k, n_total, m=m) for s in shards])
     if pairs:
         # what a rank exchanges: one [B, k] int64 tensor of (score, id) pairs
         stack = torch.stack(
@@ -38,14 +41,15 @@ def _sharded(q, x, k, bounds, pairs=False):
     return merge_topk(ids, scores, k)
 
 
-@pytest.mark.parametrize("pairs", [False, True])
+@pytest.mark.parametrize("pairs,full_width", [(False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("world", [2, 3, 8])
 @pytest.mark.parametrize("b,n,k", [(300, 400_003, 100), (1024, 1_000_000, 100), (96, 150_001, 37)])
-def test_shared_seed_equals_single_call_integer(world, b, n, k, pairs):
+def test_shared_seed_equals_single_call_integer(world, b, n, k, pairs, full_width):
     q = make_int_rows(b, 128, seed=11, device="cuda")
     x = make_int_rows(n, 128, seed=12, device="cuda")
     ref_i, ref_s = ops.dense_topk(q, x, k)
-    ids, scores = _sharded(q, x, k, [shard_bounds(n, world, r) for r in range(world)], pairs)
+    bounds = [shard_bounds(n, world, r) for r in range(world)]
+    ids, scores = _sharded(q, x, k, bounds, pairs, m=k if full_width else None)
     torch.cuda.synchronize()
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
 
