@@ -56,6 +56,9 @@ def parse_args():
     p.add_argument("--ref-sample", type=int, default=32,
                    help="queries per step of --impl reference (each step a bounded sample)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=("c2", "c3", "c4", "c5", "ops"), default="c2",
+                   help="c2 (default, the headline); c3/c4/c5 and ops: one-GPU measurements of the other configs "
+                        "and of every other kernel")
     return p.parse_args()
 
 
@@ -252,6 +255,11 @@ def config_dict(args) -> dict:
 
 def main():
     args = parse_args()
+    if args.workload != "c2":
+        from bench_configs import run_workload
+
+        run_workload(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return

@@ -1,0 +1,333 @@
+"""One-GPU measurements of the configurations other than the headline, and of
+every kernel outside the dense scan, for ``bench.py --workload c3|c4|c5|ops``.
+
+Each prints one JSON line in ``bench.py``'s format (metric, value, unit, config,
+roofline with the measured peaks, clocks). Inputs are seeded synthetic data of
+the BASELINE configurations' shapes, generated on the device; timing is CUDA
+events around W untimed + K timed steps; every input is larger than L2 (or the
+step streams more than L2), so no flush is needed.
+
+  c3   attribute-filtered kNN, fp16 10M x 128, 8 Zipf(1.1) attributes, per-item
+       64-bit Bloom words (3 hashes), B = 1024, k = 100, predicates of 1-3
+       terms at about 1 %, 10 % and 50 % selectivity (Bloom test + exact recheck)
+  c4   int8 scoring, 30M x 256 with per-row scales, B = 4096, k = 100
+  c5   1-bit pool + rerank, 30M x 512-bit SimHash codes of a d = 128 mixture,
+       pool 1000 on the int8 tensor cores, fp16 rerank to k = 100, B = 1024
+  ops  the remaining kernels one by one at representative sizes
+"""
+
+from __future__ import annotations
+
+import json
+import statistics
+
+import torch
+
+import bench
+
+N_CENTRES, SIGMA = bench.N_CENTRES, bench.SIGMA
+
+
+def _centres(dim: int, device) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(0)
+    return torch.randn(N_CENTRES, dim, generator=g, device=device)
+
+
+def _mixture(cent: torch.Tensor, rows: int, seed: int) -> torch.Tensor:
+    g = torch.Generator(device=cent.device).manual_seed(seed)
+    c = torch.randint(0, cent.shape[0], (rows,), generator=g, device=cent.device)
+    x = cent[c] + SIGMA * torch.randn(rows, cent.shape[1], generator=g, device=cent.device)
+    return x / x.norm(dim=1, keepdim=True).clamp_min(1e-8)
+
+
+def _blocks(n: int, fn, block: int = 1 << 20):
+    for b, lo in enumerate(range(0, n, block)):
+        yield lo, min(lo + block, n), fn(min(lo + block, n) - lo, 1000 + b)
+
+
+def _time(step, warmup: int, steps: int) -> tuple[float, list[float]]:
+    """Mean ms per step over K timed steps (CUDA events per step), after W warm-ups."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        a.record()
+        step()
+        b.record()
+    torch.cuda.synchronize()
+    ts = [a.elapsed_time(b) for a, b in evs]
+    return statistics.mean(ts), ts
+
+
+def _peaks() -> dict:
+    pk = bench.ROOT / "MEASURED_PEAKS.json"
+    return json.loads(pk.read_text()) if pk.exists() else {}
+
+
+def _line(metric, value, unit, config, roofline, clocks, dtype, higher=True, **extra):
+    d = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "higher_is_better": higher,
+         "dtype": dtype, "data": "synthetic", "config": config, "roofline": roofline, "clocks": clocks}
+    d.update(extra)
+    print(json.dumps(d), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# C4: int8
+# ---------------------------------------------------------------------------
+def run_c4(args, dev):
+    from retrieve_b200 import ops
+
+    n = args.n_items if args.n_items != bench.N_ITEMS else 30_000_000
+    d, b, k = 256, 4096, args.k
+    cent = _centres(d, dev)
+    codes = torch.empty((n, d), dtype=torch.int8, device=dev)
+    scales = torch.empty((n,), dtype=torch.float32, device=dev)
+    for lo, hi, x in _blocks(n, lambda r, sd: _mixture(cent, r, sd)):
+        sc = x.abs().amax(dim=1).clamp_min(1e-8) / 127.0
+        codes[lo:hi] = torch.round(x / sc[:, None]).clamp(-127, 127).to(torch.int8)
+        scales[lo:hi] = sc
+        del x
+    q = _mixture(cent, b, 7)
+    torch.cuda.synchronize()
+    sampler = bench.ClockSampler(dev)
+    sampler.start()
+    ms, _ = _time(lambda: ops.int8_topk(q, codes, scales, k), args.warmup, args.steps)
+    clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
+    peak = 2 * _peaks().get("bf16_tflops_sustained", 1400.0)
+    achieved = 2.0 * b * n * d / (ms / 1e3) / 1e12
+    _line("queries/s @30M items d=256 int8 per-row scales, B=4096, k=100", b / (ms / 1e3), "queries/s",
+          {"workload": "int8 scoring (BASELINE config 4)", "n_items": n, "dim": d, "batch": b, "k": k,
+           "corpus": "1024-centre Gaussian mixture, sigma 0.15, per-row symmetric int8"},
+          {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+           "peak_source": "derived: 2 x measured bf16 sustained (int8 tensor rate is twice bf16)",
+           "step_ms": ms, "note": "step = query quantization + int8 scan (kind::i8) + merge"},
+          clocks, "int8 -> int32")
+
+
+# ---------------------------------------------------------------------------
+# C5: 1-bit pool + rerank
+# ---------------------------------------------------------------------------
+def _simhash(x: torch.Tensor, r: torch.Tensor) -> torch.Tensor:
+    bits = (x.float() @ r.t() > 0).to(torch.int64)  # [n, 64 W]
+    w = bits.shape[1] // 64
+    shifts = torch.arange(64, device=x.device, dtype=torch.int64)
+    return (bits.view(-1, w, 64) << shifts).sum(dim=2)  # disjoint bits: the sum is the OR
+
+
+def run_c5(args, dev):
+    from retrieve_b200.bitknn import PackedBitsIndex, onebit_rerank_topk
+
+    n = args.n_items if args.n_items != bench.N_ITEMS else 30_000_000
+    d, nbits, b, pool, k = 128, 512, args.batch, 1000, args.k
+    cent = _centres(d, dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    proj = torch.randn(nbits, d, generator=g, device=dev)
+    items = torch.empty((n, d), dtype=torch.float16, device=dev)
+    codes = torch.empty((n, nbits // 64), dtype=torch.int64, device=dev)
+    for lo, hi, x in _blocks(n, lambda r, sd: _mixture(cent, r, sd)):
+        items[lo:hi] = x.to(torch.float16)
+        codes[lo:hi] = _simhash(x, proj)
+        del x
+    qf = _mixture(cent, b, 7)
+    q = qf.to(torch.float16)
+    qbits = _simhash(qf, proj)
+    index = PackedBitsIndex(codes)
+    del codes
+    torch.cuda.synchronize()
+    sampler = bench.ClockSampler(dev)
+    sampler.start()
+    ms, _ = _time(lambda: onebit_rerank_topk(q, qbits, index, items, pool, k), args.warmup, args.steps)
+    clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
+    peak = 2 * _peaks().get("bf16_tflops_sustained", 1400.0)
+    achieved = 2.0 * b * n * nbits / (ms / 1e3) / 1e12  # the +-1 int8 scan's ops over the whole step
+    _line("queries/s @30M items 512-bit codes, pool 1000 + fp16 rerank d=128 to k=100, B=1024",
+          b / (ms / 1e3), "queries/s",
+          {"workload": "1-bit coarse retrieval + rerank (BASELINE config 5)", "n_items": n, "bits": nbits,
+           "batch": b, "pool": pool, "k": k, "codes": "SimHash (N(0,1) projections, seed 0) of the mixture",
+           "stage1": "codes as a +-1 int8 table, kind::i8 scan, exact 64W - 2*hamming scores"},
+          {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+           "peak_source": "derived: 2 x measured bf16 sustained (int8 tensor rate is twice bf16)",
+           "step_ms": ms, "note": "achieved counts the stage-1 scan's ops over the whole step (rerank included)"},
+          clocks, "int8 (+-1) -> int32; fp16 rerank")
+
+
+# ---------------------------------------------------------------------------
+# C3: attribute-filtered
+# ---------------------------------------------------------------------------
+CARDS = (10, 20, 50, 100, 200, 500, 1000, 1000)
+
+
+def _zipf_attrs(n: int, dev) -> torch.Tensor:
+    g = torch.Generator(device=dev).manual_seed(5)
+    cols = []
+    for card in CARDS:
+        p = 1.0 / torch.arange(1, card + 1, device=dev, dtype=torch.float64) ** 1.1
+        cols.append(torch.multinomial((p / p.sum()).float(), n, replacement=True, generator=g))
+    return torch.stack(cols, dim=1).to(torch.int64).view(n, len(CARDS), 1).contiguous()
+
+
+def _predicates_for(attrs: torch.Tensor, b: int, target: float, seed: int) -> list[str]:
+    """1-3 term expressions near the target selectivity: a term (c == v) whose
+    frequency is within a factor of 1.5 of the target; for 50 %, OR of the most
+    frequent values of a clause; for 1 %, some as the AND of two terms."""
+    import random
+
+    rnd = random.Random(seed)
+    n = attrs.shape[0]
+    freqs = [torch.bincount(attrs[:, c, 0], minlength=card).double().div(n).cpu().tolist()
+             for c, card in enumerate(CARDS)]
+    near = [(c, v) for c in range(len(CARDS)) for v, f in enumerate(freqs[c]) if target / 1.5 <= f <= target * 1.5]
+    out = []
+    for i in range(b):
+        if target >= 0.5:
+            c = rnd.randrange(3)
+            order = sorted(range(CARDS[c]), key=lambda v: -freqs[c][v])
+            acc, terms = 0.0, []
+            for v in order:
+                if acc >= target or len(terms) == 3:
+                    break
+                terms.append(f"{c}:{v}")
+                acc += freqs[c][v]
+            out.append(" OR ".join(terms))
+        elif near and (target > 0.02 or i % 2 == 0):
+            c, v = rnd.choice(near)
+            out.append(f"{c}:{v}")
+        else:  # AND of two independent ~sqrt(target) terms
+            t = target ** 0.5
+            pairs = [(c, v) for c in range(len(CARDS)) for v, f in enumerate(freqs[c]) if t / 1.5 <= f <= t * 1.5]
+            (c1, v1), (c2, v2) = rnd.sample(pairs, 2) if len(pairs) > 1 else (pairs[0], pairs[0])
+            out.append(f"{c1}:{v1} AND {c2}:{v2}")
+    return out
+
+
+def run_c3(args, dev):
+    from retrieve_b200 import ops
+    from retrieve_b200.predicates import from_expressions
+
+    n = args.n_items
+    b, k = args.batch, args.k
+    cent = bench.centres(dev)
+    items = torch.empty((n, bench.DIM), dtype=torch.float16, device=dev)
+    for lo, hi, x in _blocks(n, lambda r, sd: bench.mixture_block(cent, r, sd)):
+        items[lo:hi] = x.to(torch.float16)
+    q = bench.queries(cent, b).to(torch.float16)
+    attrs = _zipf_attrs(n, dev)
+    bloom = ops.bloom_build(attrs, 3)
+    results = {}
+    sampler = bench.ClockSampler(dev)
+    sampler.start()
+    for target in (0.01, 0.10, 0.50):
+        exprs = _predicates_for(attrs, b, target, seed=int(target * 1000))
+        preds = from_expressions(exprs).to(dev)
+        sel = _selectivity(attrs, exprs)
+        torch.cuda.synchronize()
+        ms, _ = _time(lambda: ops.dense_topk_filtered(q, items, k, preds.terms, preds.n_terms, "bloom_recheck",
+                                                      attrs, bloom), args.warmup, args.steps)
+        results[f"{int(target * 100)}%"] = {"queries_per_s": b / (ms / 1e3), "step_ms": ms,
+                                            "measured_selectivity": sel}
+    clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
+    peak = _peaks().get("bf16_tflops_sustained", 1400.0)
+    ms10 = results["10%"]["step_ms"]
+    achieved = 2.0 * b * n * bench.DIM / (ms10 / 1e3) / 1e12
+    _line("queries/s @10M items d=128 fp16, 8 attrs + 64-bit bloom, B=1024, k=100 (10 % selectivity)",
+          results["10%"]["queries_per_s"], "queries/s",
+          {"workload": "attribute-filtered kNN (BASELINE config 3)", "n_items": n, "dim": bench.DIM, "batch": b,
+           "k": k, "attrs": "8 categorical, cardinalities 10..1000, Zipf(1.1)", "bloom": "64-bit, 3 hashes",
+           "mode": "bloom test + exact recheck (exact results)", "sweep": results},
+          {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+           "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops_sustained)",
+           "note": "2*B*N*D dense-masked flops (the figure the config judges) at 10 % selectivity"},
+          clocks, "fp16")
+
+
+def _selectivity(attrs, exprs: list[str], sample: int = 1 << 20) -> float:
+    """Mean exact fraction of a strided item sample passing each query's
+    expression (the forms ``_predicates_for`` writes: one term, an AND of two,
+    an OR of up to three)."""
+    idx = torch.linspace(0, attrs.shape[0] - 1, sample, device=attrs.device).long()
+    a = attrs[idx, :, 0]
+    fracs = []
+    for e in exprs:
+        op = " OR " if " OR " in e else " AND "
+        hits = [a[:, int(t.split(":")[0])] == int(t.split(":")[1]) for t in e.split(op)]
+        m = hits[0]
+        for h in hits[1:]:
+            m = (m | h) if op == " OR " else (m & h)
+        fracs.append(m.float().mean())
+    return float(torch.stack(fracs).mean())
+
+
+# ---------------------------------------------------------------------------
+# ops: every other kernel at a representative size
+# ---------------------------------------------------------------------------
+def run_ops(args, dev):
+    from retrieve_b200 import ops
+    from retrieve_b200.shard import merge_topk
+
+    hbm = _peaks().get("hbm_gbs", 6650.0)
+    rows = []
+    sampler = bench.ClockSampler(dev)
+    sampler.start()
+
+    def measure(name, fn, bytes_, note, ops_=None, unit=None):
+        ms, _ = _time(fn, args.warmup, args.steps)
+        r = {"op": name, "ms": ms, "algorithmic_bytes": bytes_, "GB_s": bytes_ / (ms / 1e3) / 1e9,
+             "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm, "note": note}
+        if ops_ is not None:
+            r["rate"] = ops_ / (ms / 1e3)
+            r["rate_unit"] = unit
+        rows.append(r)
+
+    n = 10_000_000
+    g = torch.Generator(device=dev).manual_seed(3)
+    attrs = _zipf_attrs(n, dev)
+    rev = torch.zeros(8, dtype=torch.bool, device=dev)
+    qa = torch.full((16, 8), -1, dtype=torch.int64, device=dev)
+    qa[:, 0] = torch.arange(16, device=dev) % 10
+    measure("clause_mask", lambda: ops.clause_mask(attrs, rev, qa), n * 8 * 8 + 16 * n,
+            "attrs [10M,8,1] int64 read once per 8-query row block, [16, 10M] bool out")
+    scores = torch.randn(16, n, generator=g, device=dev)
+    measure("clause_mask_scores", lambda: ops.clause_mask_scores(scores, attrs, rev, qa), n * 64 + 16 * n * 8,
+            "+ [16, 10M] fp32 scores in and out")
+    measure("clause_compact", lambda: ops.clause_compact(attrs, rev, qa), n * 64 + 8 * int(16 * n * 0.2),
+            "attrs + passing ids out (about 20 %)")
+    items_t = torch.randn(128, n, generator=g, device=dev).to(torch.float16)
+    q1 = torch.randn(1, 128, generator=g, device=dev).to(torch.float16)
+    measure("gemv_scores", lambda: ops.gemv_scores(q1, items_t), 128 * n * 2 + 4 * n, "[1,128] x [128, 10M] fp16")
+    del items_t, scores
+    items = torch.randn(n, 128, generator=g, device=dev).to(torch.float16)
+    qb = torch.randn(1024, 128, generator=g, device=dev).to(torch.float16)
+    cand = torch.randint(0, n, (1024, 1000), generator=g, device=dev)
+    cnt = torch.full((1024,), 1000, dtype=torch.int64, device=dev)
+    measure("fused_masked_knn_topk", lambda: ops.fused_masked_knn_topk(qb, items, cand, cnt, 100),
+            1024 * 1000 * (256 + 8), "B=1024, P=1000 random row gathers, D=128 fp16, k=100")
+    bits = torch.randint(0, 256, (1_000_000, 64), generator=g, device=dev, dtype=torch.uint8).view(torch.int64)
+    qbits = torch.randint(0, 256, (1024, 64), generator=g, device=dev, dtype=torch.uint8).view(torch.int64)
+    measure("oporp_1bit_match_topk_full (popcount)", lambda: ops.oporp_1bit_match_topk_full(qbits, bits, 100),
+            bits.numel() * 8, "B=1024 x 1M items x 512 bits, k=100: POPC-pipe bound",
+            ops_=1024 * 1_000_000 * 16, unit="popc32/s")
+    measure("bits_to_pm1", lambda: ops.bits_to_pm1(bits), bits.numel() * 8 * 9, "1M x 512 bits -> 1M x 512 int8")
+    xq = torch.randn(4096, 256, generator=g, device=dev)
+    measure("quantize_int8", lambda: ops.quantize_int8(xq), 4096 * 256 * 5 + 4096 * 4, "[4096, 256] fp32")
+    measure("bloom_build", lambda: ops.bloom_build(attrs, 3), n * 64 + n * 8, "[10M, 8, 1] attrs -> [10M] words")
+    pi = torch.randint(0, n, (8, 1024, 100), generator=g, device=dev)
+    ps = torch.randn(8, 1024, 100, generator=g, device=dev)
+    measure("merge_topk (8 shards)", lambda: merge_topk(pi, ps, 100), 8 * 1024 * 100 * 12,
+            "[8, 1024, 100] per-shard lists -> [1024, 100]: latency-bound")
+    clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
+    _line("per-kernel throughput (HBM-bound kernels as a fraction of the measured copy bandwidth)",
+          statistics.mean(r["frac_of_hbm"] for r in rows if "rate" not in r and "latency" not in r["note"]),
+          "mean frac of measured HBM", {"workload": "kernel sweep", "ops": rows},
+          {"bound": "hbm", "peak": hbm, "unit": "GB/s", "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)"},
+          clocks, "mixed")
+
+
+def run_workload(args):
+    import os
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--workload c3/c4/c5/ops runs on one GPU (no torchrun)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    {"c3": run_c3, "c4": run_c4, "c5": run_c5, "ops": run_ops}[args.workload](args, dev)

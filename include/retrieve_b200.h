@@ -48,6 +48,7 @@ extern "C" {
 #define RB_BF16 1
 #define RB_I8 2
 #define RB_F32 3
+#define RB_E4M3 4
 
 /* Message of the last failed call on this thread ("" if none). */
 RB_API const char* rb_last_error(void);
@@ -257,6 +258,23 @@ RB_API int rb_dense_topk_i8(const int8_t* query_codes, const float* query_scales
  * Index-build time (8x the packed size); queries per batch.
  */
 RB_API int rb_bits_to_pm1(const int64_t* bits, int N, int W, int8_t* out, void* stream);
+
+/*
+ * Dense top-k over fp8 e4m3 rows (kind::f8f6f4, fp32 accumulation) with the
+ * int8 dequant on the accumulator: score = (dot * query_scale) * item_scale
+ * (left to right; null scale arrays mean 1). dtype must be RB_E4M3; rows of
+ * 128 / 256 / 512 bytes; k <= 1024. With +-1 codes (rb_bits_to_pm1_e4m3) every
+ * partial sum is an integer of at most 512 in magnitude, so the scores are the
+ * exact 1-bit match scores. Workspace as rb_dense_topk_workspace_size with the
+ * same dtype.
+ */
+RB_API int rb_dense_topk_scaled(const void* queries, const float* query_scales, const void* items,
+                                const float* item_scales, int B, int N, int D, int dtype, int k, int64_t id_offset,
+                                int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/* rb_bits_to_pm1 with fp8 e4m3 output (+1.0 = 0x38, -1.0 = 0xb8). */
+RB_API int rb_bits_to_pm1_e4m3(const int64_t* bits, int N, int W, uint8_t* out, void* stream);
 
 /*
  * Reads (synchronously) the device error word a scan kernel leaves in

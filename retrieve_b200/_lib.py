@@ -23,7 +23,7 @@ RB_ERR_WORKSPACE = 4
 RB_ERR_CUDA = 5
 RB_ERR_DEVICE = 6
 
-RB_F16, RB_BF16, RB_I8, RB_F32 = 0, 1, 2, 3
+RB_F16, RB_BF16, RB_I8, RB_F32, RB_E4M3 = 0, 1, 2, 3, 4
 
 _c_int = ctypes.c_int
 _c_i64 = ctypes.c_int64
@@ -61,6 +61,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "rb_merge_pairs": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
     "rb_bits_to_pm1": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
+    "rb_bits_to_pm1_e4m3": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
+    "rb_dense_topk_scaled": (
+        _c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp, _c_size, _vp]
+    ),
     "rb_clause_mask": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int, _vp, _vp, _vp]),
     "rb_clause_compact_workspace_size": (_c_int, [_c_int, _c_int, ctypes.POINTER(_c_size)]),
     "rb_clause_compact": (

@@ -8,8 +8,10 @@ codes are expanded once, at registration, into a ±1 int8 table (``bits_to_pm1``
 8 bytes per 64 code bits) and every batch is one ``kind::i8`` tensor-core scan
 with unit scales: exact int32 dots, the same scores and the same (score desc,
 id asc) ordering as the popcount path, at tensor-core rather than POPC-pipe
-throughput. Widths with 64·W in {128, 256, 512} bits use the tensor cores; other
-widths use the exact popcount kernel (``oporp_1bit_match_topk_full``).
+throughput. (``bits_to_pm1(…, "e4m3")`` with ``scaled_topk`` is the same on the
+fp8 tensor cores.) Widths with
+64·W in {128, 256, 512} bits use the tensor cores; other widths use the exact
+popcount kernel (``oporp_1bit_match_topk_full``).
 """
 
 from __future__ import annotations

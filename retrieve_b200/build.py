@@ -53,9 +53,12 @@ def _stale(obj: Path, src: Path) -> bool:
 
 
 def build(verbose: bool = False, ptxas_verbose: bool = False) -> Path:
+    """Compiles every stale translation unit (in parallel) and links the library."""
+    from concurrent.futures import ThreadPoolExecutor
+
     nvcc = nvcc_path()
     BUILD_DIR.mkdir(exist_ok=True)
-    objs = []
+    objs, cmds = [], []
     for src in sources():
         obj = BUILD_DIR / (src.stem + ".o")
         objs.append(obj)
@@ -66,7 +69,11 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> Path:
             cmd.insert(1, "-Xptxas=-v")
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
+    workers = max(1, min(len(cmds), os.cpu_count() or 1))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        for done in pool.map(lambda c: subprocess.run(c, check=True), cmds):
+            pass
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
     if verbose:
         print(" ".join(cmd), flush=True)

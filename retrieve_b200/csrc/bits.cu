@@ -20,7 +20,14 @@ __device__ __forceinline__ uint32_t nibble_pm1(uint32_t nib) {
   return 0xffffffffu ^ (spread * 0xfeu);
 }
 
+// The same in fp8 e4m3: +1.0 is 0x38, -1.0 is 0xb8 (the sign bit set).
+__device__ __forceinline__ uint32_t nibble_pm1_e4m3(uint32_t nib) {
+  const uint32_t spread = (nib & 1u) | ((nib & 2u) << 7) | ((nib & 4u) << 14) | ((nib & 8u) << 21);
+  return 0xb8b8b8b8u ^ (spread * 0x80u);
+}
+
 // One thread per 64-bit word: 64 output bytes as four 16-byte stores.
+template <bool E4M3>
 __global__ void bits_to_pm1_kernel(const uint64_t* __restrict__ bits, int64_t n_words, int4* __restrict__ out) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_words;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -29,10 +36,11 @@ __global__ void bits_to_pm1_kernel(const uint64_t* __restrict__ bits, int64_t n_
     for (int part = 0; part < 4; ++part) {
       const uint32_t v = static_cast<uint32_t>(w >> (16 * part));  // bits 16 part .. 16 part + 15
       int4 o;
-      o.x = static_cast<int>(nibble_pm1(v & 0xfu));
-      o.y = static_cast<int>(nibble_pm1((v >> 4) & 0xfu));
-      o.z = static_cast<int>(nibble_pm1((v >> 8) & 0xfu));
-      o.w = static_cast<int>(nibble_pm1((v >> 12) & 0xfu));
+      auto nib = [](uint32_t x) { return E4M3 ? nibble_pm1_e4m3(x) : nibble_pm1(x); };
+      o.x = static_cast<int>(nib(v & 0xfu));
+      o.y = static_cast<int>(nib((v >> 4) & 0xfu));
+      o.z = static_cast<int>(nib((v >> 8) & 0xfu));
+      o.w = static_cast<int>(nib((v >> 12) & 0xfu));
       out[i * 4 + part] = o;
     }
   }
@@ -42,9 +50,7 @@ __global__ void bits_to_pm1_kernel(const uint64_t* __restrict__ bits, int64_t n_
 
 using namespace rb;
 
-extern "C" {
-
-int rb_bits_to_pm1(const int64_t* bits, int N, int W, int8_t* out, void* stream) {
+static int bits_launch(bool e4m3, const int64_t* bits, int N, int W, void* out, void* stream) {
   if (N < 0 || W <= 0) {
     set_last_error("bits_to_pm1: bad sizes");
     return RB_ERR_INVALID_ARG;
@@ -56,14 +62,29 @@ int rb_bits_to_pm1(const int64_t* bits, int N, int W, int8_t* out, void* stream)
   }
   const int64_t n_words = static_cast<int64_t>(N) * W;
   const int blocks = static_cast<int>(std::min<int64_t>((n_words + 255) / 256, 8 * 1024));
-  bits_to_pm1_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint64_t*>(bits), n_words, reinterpret_cast<int4*>(out));
+  auto s = static_cast<cudaStream_t>(stream);
+  if (e4m3)
+    bits_to_pm1_kernel<true><<<blocks, 256, 0, s>>>(reinterpret_cast<const uint64_t*>(bits), n_words,
+                                                     reinterpret_cast<int4*>(out));
+  else
+    bits_to_pm1_kernel<false><<<blocks, 256, 0, s>>>(reinterpret_cast<const uint64_t*>(bits), n_words,
+                                                      reinterpret_cast<int4*>(out));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_last_error(cudaGetErrorString(e));
     return RB_ERR_CUDA;
   }
   return RB_OK;
+}
+
+extern "C" {
+
+int rb_bits_to_pm1(const int64_t* bits, int N, int W, int8_t* out, void* stream) {
+  return bits_launch(false, bits, N, W, out, stream);
+}
+
+int rb_bits_to_pm1_e4m3(const int64_t* bits, int N, int W, uint8_t* out, void* stream) {
+  return bits_launch(true, bits, N, W, out, stream);
 }
 
 }  // extern "C"

@@ -72,14 +72,14 @@ static int dense_check(int elem, const void* queries, const float* q_scale, cons
                        int B, int N, int D, int k, const char* what) {
   if (B < 0 || N < 0 || k < 1) return fail(RB_ERR_INVALID_ARG, std::string(what) + ": bad B, N or k");
   if (k > 1024) return fail(RB_ERR_UNSUPPORTED, std::string(what) + ": k > 1024 is not supported");
-  const int row_bytes = (elem == 2) ? D : 2 * D;
+  const int row_bytes = (elem == 2 || elem == 4) ? D : 2 * D;
   if (row_bytes != 128 && row_bytes != 256 && row_bytes != 512)
     return fail(RB_ERR_UNSUPPORTED, std::string(what) +
                                         ": rows must be 128, 256 or 512 bytes (D = 64/128/256 fp16/bf16, "
                                         "128/256/512 int8)");
   if (B > 0 && N > 0) {
     if (!aligned16(queries) || !aligned16(items)) return fail(RB_ERR_INVALID_ARG, std::string(what) + ": 16-byte alignment");
-    if (elem == 2 && x_scale != nullptr && !aligned16(x_scale))
+    if (elem >= 2 && x_scale != nullptr && !aligned16(x_scale))
       return fail(RB_ERR_INVALID_ARG, std::string(what) + ": item scales must be 16-byte aligned");
   }
   return RB_OK;
@@ -119,7 +119,7 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
     else fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, stream);
     return cudaGetLastError() == cudaSuccess ? RB_OK : fail(RB_ERR_CUDA, "fill_empty launch failed");
   }
-  const int row_bytes = (elem == 2) ? D : 2 * D;
+  const int row_bytes = (elem == 2 || elem == 4) ? D : 2 * D;
   if (filter != nullptr && (k > 384 || row_bytes > 256))
     return fail(RB_ERR_UNSUPPORTED, "dense_topk_filtered: k <= 384 and rows of up to 256 bytes");
   const size_t need = dense_workspace_bytes(B, N, k, row_bytes);
@@ -244,6 +244,14 @@ int rb_dense_topk_filtered(const void* queries, const void* items, int B, int N,
     return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: bloom words missing");
   return dense_topk_impl(dtype == RB_BF16 ? 1 : 0, queries, nullptr, items, nullptr, B, N, D, k, id_offset, out_ids,
                          out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), &f);
+}
+
+int rb_dense_topk_scaled(const void* queries, const float* query_scales, const void* items, const float* item_scales,
+                         int B, int N, int D, int dtype, int k, int64_t id_offset, int64_t* out_ids, float* out_scores,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != RB_E4M3) return fail(RB_ERR_TYPE, "dense_topk_scaled: dtype must be e4m3");
+  return dense_topk_impl(4, queries, query_scales, items, item_scales, B, N, D, k, id_offset,
+                         out_ids, out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int rb_dense_topk_i8(const int8_t* query_codes, const float* query_scales, const int8_t* item_codes,

@@ -1,0 +1,796 @@
+// Fused dense scoring + exact top-k for sm_100a (B200): the kernels. Each
+// element type's variants are instantiated in their own translation unit
+// (dense_scan_e<ELEM>.cu); the planning and dispatch live in dense_scan_sm100.cu.
+//
+// Element types (ELEM): 0 fp16, 1 bf16, 2 int8 (kind::i8, int32 accumulate),
+// 4 fp8 e4m3 (kind::f8f6f4; +-1 codes give exact 1-bit match scores). 2 and 4
+// apply the (dot * q_scale) * item_scale dequant. (3 is not used.)
+//
+// One persistent CTA per SM. A task is (query group, item split): the CTA
+// holds NG x 128 queries resident in shared memory (TMA, 128-byte swizzle) and
+// streams its split's item tiles (128 items each) through a STAGES-deep TMA
+// ring. One elected thread issues tcgen05.mma (M = 128 queries, N = 128 items,
+// K = the embedding dim) into a double-buffered TMEM accumulator; the epilogue
+// warps read their query row out of TMEM (thread = query, 32 columns at a
+// time), drop every 32-item chunk whose max is below the query's threshold and
+// append the rest to the query's candidate list (rb_select.cuh). No [B, N]
+// score matrix ever reaches HBM.
+//
+// Warp roles (NG = 2: 320 threads):
+//   warp 0      TMA producer (queries once per task, item tiles per stage)
+//   warp 1      TMEM allocator + MMA issuer
+//   warps 2..   epilogue, 4 warps per query group (TMEM lane quadrant = warp % 4)
+//
+// Reference semantics replaced: PostfilterKNN.score + masked_topk
+// (retrieve/src/retrieve/modules/knn.py:62-76, functional.py:57-85), i.e.
+// torch.mm(q_fp16, E_t, out_dtype=fp32) followed by torch.topk, with ties broken
+// toward the lower item id.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "rb_capi_internal.h"
+#include "rb_common.cuh"
+#include "rb_select.cuh"
+
+namespace rb {
+
+constexpr int kTileItems = 128;  // N of one MMA = items per pipeline stage
+constexpr int kQTile = 128;      // M of one MMA = queries per group
+constexpr int kSampleStride = 16;  // sampling pass: every 16th tile
+
+struct alignas(64) DenseScanParams {
+  CUtensorMap tmap_q;
+  CUtensorMap tmap_x;   // item boxes of 128 rows (1-SM kernel) or 64 rows (2-SM kernel)
+  const float* seed;  // [B] pass threshold per query (>=), or null for -inf
+  uint2* lists;       // [B, n_splits, cap]
+  int* counts;        // [B, n_splits]
+  int* err;           // device error word
+  float* chunk_max;   // MODE 1: [B, chunk_stride] max score of every 32-item chunk
+  int chunk_stride;
+  const float* q_scale;  // scaled types: [B] per-query scale (null: 1)
+  const float* x_scale;  // scaled types: [N] per-item scale (null: 1)
+  FilterArgs filter;     // attribute predicate (mode kFilterNone: none)
+  int B, N;
+  int n_qsg, n_splits;
+  int tile_stride, tile_offset, pass_tiles;
+  int k, cap;
+};
+
+template <int KB, int NG, int STAGES>
+struct DenseSmemLayout {
+  static constexpr int kOpTile = kQTile * 128;  // bytes of one 128-row x 128-byte K-block
+  static constexpr int kA = NG * KB * kOpTile;
+  static constexpr int kB = STAGES * KB * kOpTile;
+  static constexpr int kEpiWarps = 4 * NG;
+  static constexpr int kHist = kEpiWarps * 256 * 4;
+  static constexpr int kBar = (2 * STAGES + 2 + 4 + 1) * 8;
+  static constexpr int kMisc = 16;
+  static constexpr int kTotal = kA + kB + kHist + kBar + kMisc + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ void split_range(int split, int n_splits, int pass_tiles, int& lo, int& hi) {
+  lo = static_cast<int>((static_cast<int64_t>(split) * pass_tiles) / n_splits);
+  hi = static_cast<int>((static_cast<int64_t>(split + 1) * pass_tiles) / n_splits);
+}
+
+// Filtering work of one accumulator tile, on the scores already in registers
+// (r[ch][j] = score of item row0 + 32*ch + j for this thread's query).
+// Filtering work on NCH 32-item chunks of scores already in registers:
+// r[ch][j] = score of item row0 + 32 * ch + j for this thread's query; the
+// chunks are chunk numbers c0 .. c0 + NCH - 1 of their 128-item tile.
+// The scaled element types dequantize first: score = (fp32(dot) * q_scale) *
+// item_scale, left to right as the reference does (ops/official/adapter.py:
+// 338-367). For int8 (ELEM 2) the registers hold int32 dots, turned here into
+// fp32 exactly; for integer values held as bf16 (ELEM 3) or fp8 e4m3 (ELEM 4)
+// the fp32 accumulator already holds the exact integer dot (every partial sum
+// is an integer below 2^24).
+// The scaled element types (2: int8, 4: fp8 e4m3) score
+// (fp32(dot) * q_scale) * item_scale, left to right as the reference dequantizes
+// (ops/official/adapter.py:338-367); null scale arrays mean 1. For int8 the
+// registers hold int32 dots, turned into fp32 exactly; for fp8 the fp32
+// accumulator already holds the dot.
+template <int ELEM, int KB>
+__device__ __forceinline__ float raw_to_float(uint32_t raw) {
+  if constexpr (ELEM != 2)
+    return __uint_as_float(raw);
+  else if constexpr (KB <= 2)
+    return __uint_as_float(raw + 0x4B400000u) - 12582912.0f;  // |dot| < 2^22: exact magic-constant path
+  else
+    return __int2float_rn(static_cast<int>(raw));  // D = 512: |dot| < 2^24, exact by conversion
+}
+
+template <int MODE, int NCH, int ELEM, bool FILT, int KB>
+__device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
+                                               int chunk0, bool valid_q, int q, float thresh, int& count,
+                                               uint2* list) {
+  if constexpr (ELEM >= 2) {
+    const float qs = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
+    const bool full = row0 + NCH * 32 <= static_cast<uint32_t>(p.N);
+    const bool unit_x = p.x_scale == nullptr;
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const uint32_t id = row0 + ch * 32 + 4 * j4;
+        float4 xs;
+        if (unit_x) {
+          xs = make_float4(1.f, 1.f, 1.f, 1.f);
+        } else if (full) {
+          xs = __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
+        } else {
+          xs.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
+          xs.y = id + 1 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 1] : 0.f;
+          xs.z = id + 2 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 2] : 0.f;
+          xs.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
+        }
+        const float xv[4] = {xs.x, xs.y, xs.z, xs.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          r[ch][4 * j4 + u] =
+              __float_as_uint(__fmul_rn(__fmul_rn(raw_to_float<ELEM, KB>(r[ch][4 * j4 + u]), qs), xv[u]));
+      }
+    }
+  }
+  if (row0 + NCH * 32 > static_cast<uint32_t>(p.N)) {
+    // last, partial tile: rows past N were zero-filled by TMA; NaN never passes
+    // a threshold test and is ignored by fmaxf
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row0 + ch * 32 + j >= static_cast<uint32_t>(p.N)) r[ch][j] = 0x7fc00000u;
+  }
+  if constexpr (FILT && MODE == 1) {
+    if (valid_q) {
+      // sampling pass: items that fail the predicate do not count. The
+      // predicate is evaluated into a bit mask first, so that every index into
+      // r stays a compile-time constant and r stays in registers.
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const uint32_t id0 = row0 + ch * 32;
+        const uint32_t n_in = id0 >= static_cast<uint32_t>(p.N) ? 0u : min(32u, static_cast<uint32_t>(p.N) - id0);
+        const uint32_t valid = n_in == 32 ? 0xffffffffu : ((1u << n_in) - 1u);
+        const uint32_t pm = pred_pass_bits(p.filter, q, id0, valid);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (!((pm >> j) & 1u)) r[ch][j] = 0x7fc00000u;
+      }
+    }
+  }
+  if constexpr (MODE == 1) {
+    // sampling pass: the max of every 32-item chunk, nothing else
+    if (valid_q) {
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch)
+        p.chunk_max[static_cast<size_t>(q) * p.chunk_stride + chunk0 + ch] = max32(r[ch]);
+    }
+  } else {
+    // Threshold filter on the FMA pipe (paired fp32 subtracts) and the ALU
+    // (AND tree): the sign bit of sg[ch] is set iff no score of chunk ch
+    // passes; then the exact append of the chunks that may pass.
+    const uint64_t tt = pack_pair(thresh);
+    uint32_t sg[NCH];
+    uint32_t all = 0xffffffffu;
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch) {
+      sg[ch] = chunk_all_below(r[ch], tt);
+      all &= sg[ch];
+    }
+    if (__any_sync(RB_FULL_MASK, valid_q && !(all >> 31))) {
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        if (valid_q && !(sg[ch] >> 31)) {
+          if constexpr (!FILT) {
+            append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
+          } else {
+            const uint32_t id0 = row0 + ch * 32;
+            const uint32_t pm = pred_pass_bits(p.filter, q, id0, chunk_pass_bits(r[ch], thresh));
+            append_chunk_mask(list, count, r[ch], pm, id0);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
+__global__ void __launch_bounds__(64 + 128 * NG, 1)
+    dense_scan_kernel(const __grid_constant__ DenseScanParams p) {
+  using L = DenseSmemLayout<KB, NG, STAGES>;
+  constexpr int kElemBytes = (ELEM == 2 || ELEM == 4) ? 1 : 2;
+  constexpr int kElemsPerKBlock = 128 / kElemBytes;
+  constexpr int kKSteps = 128 / 32;  // MMA K = 32 bytes per instruction
+  constexpr uint32_t kTmemCols = 2 * NG * 128;
+  constexpr uint32_t kIdesc =
+      (ELEM == 2) ? make_idesc(2, 1, kQTile, kTileItems)
+                  : make_idesc(1, (ELEM == 1 || ELEM == 3) ? 1 : 0, kQTile, kTileItems);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + L::kA;
+  uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* a_full = bars + 2 * STAGES;
+  uint64_t* a_empty = a_full + 1;
+  uint64_t* acc_full = a_full + 2;   // [2]
+  uint64_t* acc_empty = a_full + 4;  // [2]
+  uint64_t* drain_bar = a_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tasks = p.n_qsg * p.n_splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(a_full, 1);
+    mbar_init(a_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], L::kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_q);
+    tma_prefetch_desc(&p.tmap_x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int a_iter = 0;
+      uint32_t armed = 0;  // item stages armed in total
+      for (int t = blockIdx.x; t < n_tasks && !*abort_flag; t += gridDim.x) {
+        const int qsg = t % p.n_qsg, split = t / p.n_qsg;
+        if (a_iter > 0 && !mbar_wait(a_empty, (a_iter - 1) & 1, abort_flag)) {
+          atomicCAS(p.err, 0, kDevTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(a_full, NG * KB * L::kOpTile);
+        for (int g = 0; g < NG; ++g)
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d(smA + (g * KB + kb) * L::kOpTile, &p.tmap_q, a_full, kb * kElemsPerKBlock,
+                        qsg * NG * kQTile + g * kQTile);
+        ++a_iter;
+        int lo, hi;
+        split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+        for (int pt = lo; pt < hi; ++pt) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
+            atomicCAS(p.err, 0, kDevTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          const int tile = pt * p.tile_stride + p.tile_offset;
+          mbar_arrive_expect_tx(&full_bar[stage], KB * L::kOpTile);
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d(smB + (stage * KB + kb) * L::kOpTile, &p.tmap_x, &full_bar[stage], kb * kElemsPerKBlock,
+                        tile * kTileItems);
+          ++armed;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every TMA this thread issued has landed before the CTA may exit.
+      if (a_iter > 0) mbar_wait_drain(a_full, (a_iter - 1) & 1);
+      for (int s = 0; s < STAGES; ++s) {
+        const uint32_t n_s = armed / STAGES + (static_cast<uint32_t>(s) < armed % STAGES ? 1u : 0u);
+        if (n_s > 0) mbar_wait_drain(&full_bar[s], (n_s - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int a_iter = 0;
+      const uint32_t a_base = smem_u32(smA), b_base = smem_u32(smB);
+      for (int t = blockIdx.x; t < n_tasks && !*abort_flag; t += gridDim.x) {
+        const int split = t / p.n_qsg;
+        if (!mbar_wait(a_full, a_iter & 1, abort_flag)) {
+          atomicCAS(p.err, 0, kDevTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        ++a_iter;
+        int lo, hi;
+        split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+        bool ok = true;
+        for (int pt = lo; pt < hi; ++pt) {
+          if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag) ||
+              !mbar_wait(&full_bar[stage], phase, abort_flag)) {
+            atomicCAS(p.err, 0, kDevTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_col = tmem_base + static_cast<uint32_t>(acc * NG * 128);
+#pragma unroll
+          for (int g = 0; g < NG; ++g) {
+#pragma unroll
+            for (int kb = 0; kb < KB; ++kb) {
+#pragma unroll
+              for (int j = 0; j < kKSteps; ++j) {
+                const uint64_t ad = sw128_kmajor_desc(a_base + (g * KB + kb) * L::kOpTile + j * 32);
+                const uint64_t bd = sw128_kmajor_desc(b_base + (stage * KB + kb) * L::kOpTile + j * 32);
+                if constexpr (ELEM == 2)
+                  mma_i8(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+                else if constexpr (ELEM == 4)
+                  mma_f8(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+                else
+                  mma_f16(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+              }
+            }
+          }
+          mma_commit(&empty_bar[stage]);
+          mma_commit(&acc_full[acc]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1;
+        }
+        if (!ok) break;
+        mma_commit(a_empty);
+      }
+      // Drain: no MMA may still be writing TMEM when it is released.
+      mma_commit(drain_bar);
+      mbar_wait_drain(drain_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;             // 0 .. 4*NG-1
+    const int g = ew >> 2;               // query group
+    const int quad = warp & 3;           // TMEM lane quadrant this warp may access
+    uint32_t* hist = hist_all + ew * 256;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    for (int t = blockIdx.x; t < n_tasks; t += gridDim.x) {
+      const int qsg = t % p.n_qsg, split = t / p.n_qsg;
+      const int q = qsg * NG * kQTile + g * kQTile + quad * 32 + lane;
+      const bool valid_q = q < p.B;
+      float thresh = (valid_q && p.seed != nullptr) ? p.seed[q] : -INFINITY;
+      int count = 0;
+      uint2* list = p.lists + (static_cast<size_t>(valid_q ? q : 0) * p.n_splits + split) * p.cap;
+      int lo, hi;
+      split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+      bool ok = true;
+      for (int pt = lo; pt < hi; ++pt) {
+        if constexpr (MODE == 0) {
+          // Room for a whole tile of appends; compacting here keeps no scores live
+          // across the (non-inlined) compaction.
+          const bool need = valid_q && (count > p.cap - kTileItems);
+          if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        }
+        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
+          if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
+        const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
+        // The whole 128-column row in one go, then the accumulator goes back to
+        // the MMA warp before any filtering work.
+        uint32_t r[4][32];
+        __syncwarp();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r[ch]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (!ok) break;
+      if constexpr (MODE == 0) {
+        const bool need = valid_q && count > p.k;
+        warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        if (valid_q) p.counts[static_cast<size_t>(q) * p.n_splits + split] = count;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+
+// ===========================================================================
+// 2-SM variant: a CTA pair (cluster of 2) runs tcgen05.mma.cta_group::2 with
+// M = 256 queries (128 per CTA) and N = 128 items (64 per CTA), NG query groups
+// per pair. Per SM this halves the item bytes read from L2 for the same MMA
+// work and cuts the operand bytes each MMA reads from shared memory, the two
+// limits of the 1-SM kernel at large batches. CTA 0 of the pair issues the MMAs;
+// both CTAs' TMA loads complete on CTA 0's barriers; CTA 0's commits reach both
+// CTAs' barriers; the epilogue of each CTA reads its own TMEM rows and releases
+// the accumulator with an arrive on CTA 0's barrier. No multicast anywhere.
+// ===========================================================================
+constexpr int kHalfItems = kTileItems / 2;
+
+template <int KB, int NG, int STAGES>
+struct Dense2SmLayout {
+  static constexpr int kATile = kQTile * 128;     // 128 query rows x 128 bytes
+  static constexpr int kBTile = kHalfItems * 128;  // 64 item rows x 128 bytes
+  static constexpr int kA = NG * KB * kATile;
+  static constexpr int kB = STAGES * KB * kBTile;
+  static constexpr int kEpiWarps = 4 * NG;  // (group, lane quadrant)
+  static constexpr int kHist = kEpiWarps * 256 * 4;
+  static constexpr int kBar = (2 * STAGES + 2 + 2 * 4 + 1) * 8;
+  static constexpr int kMisc = 16;
+  static constexpr int kTotal = kA + kB + kHist + kBar + kMisc + 1024;
+};
+
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
+    dense_scan_2sm_kernel(const __grid_constant__ DenseScanParams p) {
+  using L = Dense2SmLayout<KB, NG, STAGES>;
+  constexpr int kElemBytes = (ELEM == 2 || ELEM == 4) ? 1 : 2;
+  constexpr int kElemsPerKBlock = 128 / kElemBytes;
+  constexpr int kKSteps = 128 / 32;
+  constexpr int kAcc = 4 / NG;  // accumulator buffers: all 512 TMEM columns
+  constexpr uint32_t kTmemCols = kAcc * NG * 128;
+  constexpr uint32_t kIdesc = (ELEM == 2) ? make_idesc(2, 1, 2 * kQTile, kTileItems)
+                                          : make_idesc(1, (ELEM == 1 || ELEM == 3) ? 1 : 0, 2 * kQTile, kTileItems);
+  constexpr int kQPerPair = NG * 2 * kQTile;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + L::kA;
+  uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* a_full = bars + 2 * STAGES;
+  uint64_t* a_empty = a_full + 1;
+  uint64_t* acc_full = a_full + 2;         // [kAcc]
+  uint64_t* acc_empty = acc_full + kAcc;  // [kAcc], used on CTA 0
+  uint64_t* drain_bar = acc_empty + kAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+  const int n_tasks = p.n_qsg * p.n_splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(a_full, 1);
+    mbar_init(a_empty, 1);
+    for (int b = 0; b < kAcc; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * L::kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_q);
+    tma_prefetch_desc(&p.tmap_x);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int a_iter = 0;
+      uint32_t armed = 0;
+      for (int t = pair; t < n_tasks && !*abort_flag; t += n_pairs) {
+        const int qsg = t % p.n_qsg, split = t / p.n_qsg;
+        if (a_iter > 0 && !mbar_wait(a_empty, (a_iter - 1) & 1, abort_flag)) {
+          atomicCAS(p.err, 0, kDevTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        if (rank == 0) mbar_arrive_expect_tx(a_full, 2 * NG * KB * L::kATile);
+        for (int g = 0; g < NG; ++g)
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d_pair(smA + (g * KB + kb) * L::kATile, &p.tmap_q, a_full, kb * kElemsPerKBlock,
+                             qsg * kQPerPair + g * 2 * kQTile + static_cast<int>(rank) * kQTile);
+        ++a_iter;
+        int lo, hi;
+        split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+        for (int pt = lo; pt < hi; ++pt) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) {
+            atomicCAS(p.err, 0, kDevTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          const int tile = pt * p.tile_stride + p.tile_offset;
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * KB * L::kBTile);
+          for (int kb = 0; kb < KB; ++kb)
+            tma_load_2d_pair(smB + (stage * KB + kb) * L::kBTile, &p.tmap_x, &full_bar[stage],
+                             kb * kElemsPerKBlock, tile * kTileItems + static_cast<int>(rank) * kHalfItems);
+          ++armed;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain (CTA 0's barriers count both CTAs' bytes): every load has landed.
+      if (rank == 0) {
+        if (a_iter > 0) mbar_wait_drain(a_full, (a_iter - 1) & 1);
+        for (int s = 0; s < STAGES; ++s) {
+          const uint32_t n_s = armed / STAGES + (static_cast<uint32_t>(s) < armed % STAGES ? 1u : 0u);
+          if (n_s > 0) mbar_wait_drain(&full_bar[s], (n_s - 1) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (CTA 0)
+    // The whole warp runs the loop on warp-uniform values; one elected lane
+    // issues each tcgen05 instruction.
+    if (rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int a_iter = 0;
+      const uint64_t a_desc0 = sw128_kmajor_desc(smem_u32(smA));
+      const uint64_t b_desc0 = sw128_kmajor_desc(smem_u32(smB));
+      const uint32_t empty0 = mapa_shared(smem_u32(empty_bar), 0), empty1 = mapa_shared(smem_u32(empty_bar), 1);
+      const uint32_t accf0 = mapa_shared(smem_u32(acc_full), 0), accf1 = mapa_shared(smem_u32(acc_full), 1);
+      const uint32_t ae0 = mapa_shared(smem_u32(a_empty), 0), ae1 = mapa_shared(smem_u32(a_empty), 1);
+      for (int t = pair; t < n_tasks && !*abort_flag; t += n_pairs) {
+        const int split = t / p.n_qsg;
+        if (!__all_sync(RB_FULL_MASK, mbar_wait(a_full, a_iter & 1, abort_flag))) {
+          if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutMma);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        ++a_iter;
+        int lo, hi;
+        split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+        bool ok = true;
+        for (int pt = lo; pt < hi; ++pt) {
+          const bool ready = mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag) &&
+                             mbar_wait(&full_bar[stage], phase, abort_flag);
+          if (!__all_sync(RB_FULL_MASK, ready)) {
+            if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutMma);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_col = tmem_base + static_cast<uint32_t>(acc * NG * 128);
+          const uint64_t b_stage = b_desc0 + static_cast<uint64_t>((stage * KB * L::kBTile) >> 4);
+          if (elect_one()) {
+#pragma unroll
+            for (int g = 0; g < NG; ++g) {
+#pragma unroll
+              for (int kb = 0; kb < KB; ++kb) {
+#pragma unroll
+                for (int j = 0; j < kKSteps; ++j) {
+                  const uint64_t ad = a_desc0 + static_cast<uint64_t>(((g * KB + kb) * L::kATile + j * 32) >> 4);
+                  const uint64_t bd = b_stage + static_cast<uint64_t>((kb * L::kBTile + j * 32) >> 4);
+                  if constexpr (ELEM == 2)
+                    mma_i8_pair(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+                  else if constexpr (ELEM == 4)
+                    mma_f8_pair(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+                  else
+                    mma_f16_pair(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
+                }
+              }
+            }
+            const uint32_t so = static_cast<uint32_t>(stage) * 8u, ao = static_cast<uint32_t>(acc) * 8u;
+            mma_commit_pair(empty0 + so);
+            mma_commit_pair(empty1 + so);
+            mma_commit_pair(accf0 + ao);
+            mma_commit_pair(accf1 + ao);
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (++acc == kAcc) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        if (elect_one()) {
+          mma_commit_pair(ae0);
+          mma_commit_pair(ae1);
+        }
+        __syncwarp();
+      }
+      if (elect_one()) mma_commit_pair(mapa_shared(smem_u32(drain_bar), 0));
+      __syncwarp();
+      mbar_wait_drain(drain_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    // Warp (group g, lane quadrant): its 32 queries x the group's 128 item
+    // columns per step.
+    const int ew = warp - 2;
+    const int g = ew >> 2;
+    const int quad = warp & 3;
+    uint32_t* hist = hist_all + ew * 256;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t release0 = mapa_shared(smem_u32(acc_empty), 0);
+    for (int t = pair; t < n_tasks; t += n_pairs) {
+      const int qsg = t % p.n_qsg, split = t / p.n_qsg;
+      const int q = qsg * kQPerPair + g * 2 * kQTile + static_cast<int>(rank) * kQTile + quad * 32 + lane;
+      const bool valid_q = q < p.B;
+      float thresh = (valid_q && p.seed != nullptr) ? p.seed[q] : -INFINITY;
+      int count = 0;
+      const size_t list_id = static_cast<size_t>(valid_q ? q : 0) * p.n_splits + split;
+      uint2* list = p.lists + list_id * p.cap;
+      int lo, hi;
+      split_range(split, p.n_splits, p.pass_tiles, lo, hi);
+      bool ok = true;
+      for (int pt = lo; pt < hi; ++pt) {
+        if constexpr (MODE == 0) {
+          const bool need = valid_q && (count > p.cap - kTileItems);
+          if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        }
+        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
+          if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
+        const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
+        uint32_t r[4][32];
+        __syncwarp();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r[ch]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        if (++acc == kAcc) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if constexpr (MODE == 0) {
+        const bool need = valid_q && count > p.k;
+        warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        if (valid_q) p.counts[list_id] = count;
+      }
+    }
+  }
+
+  __syncwarp();
+  if (*abort_flag) {
+    // Error path only: a load of this CTA may still be in flight towards its
+    // own shared memory while it can no longer be tracked; let it land.
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) __nanosleep(10000);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal or read it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
+static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaStream_t stream) {
+  using L = DenseSmemLayout<KB, NG, STAGES>;
+  auto kern = dense_scan_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, 64 + 128 * NG, L::kTotal, stream>>>(prm);
+  return cudaGetLastError();
+}
+
+template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
+static cudaError_t launch_dense_scan_2sm(const DenseScanParams& prm, int n_pairs, cudaStream_t stream) {
+  using L = Dense2SmLayout<KB, NG, STAGES>;
+  auto kern = dense_scan_2sm_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return e;
+  kern<<<2 * n_pairs, 64 + 128 * NG, L::kTotal, stream>>>(prm);
+  return cudaGetLastError();
+}
+
+// Picks the kernel for a pass: MODE 1 (sampling) or MODE 0 with the list
+// compaction's entries per lane (40 only in one-group kernels, and not with
+// attribute filters, whose lists stay within 512 entries).
+template <int ELEM, int KB, int NG, int ST, bool F>
+static cudaError_t launch_2sm_variant(int mode, int epl, const DenseScanParams& prm, int n_pairs,
+                                      cudaStream_t stream) {
+  if (mode == 1) return launch_dense_scan_2sm<1, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream);
+  if (epl == 8) return launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 8, F>(prm, n_pairs, stream);
+  if (epl == 16) return launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 16, F>(prm, n_pairs, stream);
+  if constexpr (NG == 1 && !F) return launch_dense_scan_2sm<0, ELEM, KB, NG, ST, 40, F>(prm, n_pairs, stream);
+  return cudaErrorInvalidConfiguration;
+}
+
+template <int ELEM, int KB, int NG, int ST, bool F>
+static cudaError_t launch_1sm_variant(int mode, int epl, const DenseScanParams& prm, int grid, cudaStream_t stream) {
+  if (mode == 1) return launch_dense_scan<1, ELEM, KB, NG, ST, 8, F>(prm, grid, stream);
+  if (epl == 8) return launch_dense_scan<0, ELEM, KB, NG, ST, 8, F>(prm, grid, stream);
+  if (epl == 16) return launch_dense_scan<0, ELEM, KB, NG, ST, 16, F>(prm, grid, stream);
+  if constexpr (NG == 1 && !F) return launch_dense_scan<0, ELEM, KB, NG, ST, 40, F>(prm, grid, stream);
+  return cudaErrorInvalidConfiguration;
+}
+
+// CTA pairs of the 2-SM kernel that fit on the device at once (dense_scan_e1.cu).
+int dense_max_pairs();
+
+// Launches the pass for one element type; false if no variant matches.
+bool dense_launch_e0(bool two_sm, int mode, int kb, int ng, bool filtered, int epl, const DenseScanParams& prm,
+                     int grid, cudaStream_t stream, cudaError_t& e);
+bool dense_launch_e1(bool two_sm, int mode, int kb, int ng, bool filtered, int epl, const DenseScanParams& prm,
+                     int grid, cudaStream_t stream, cudaError_t& e);
+bool dense_launch_e2(bool two_sm, int mode, int kb, int ng, bool filtered, int epl, const DenseScanParams& prm,
+                     int grid, cudaStream_t stream, cudaError_t& e);
+bool dense_launch_e4(bool two_sm, int mode, int kb, int ng, bool filtered, int epl, const DenseScanParams& prm,
+                     int grid, cudaStream_t stream, cudaError_t& e);
+
+}  // namespace rb

@@ -4,6 +4,7 @@
 //   scale   = abs_max / 127                      (fp32 division)
 //   code    = clamp(round_half_even(fp32(fp64(x) / fp64(abs_max)) * 127), -128, 127)
 // One warp per row.
+#include <algorithm>
 #include <cstdint>
 
 #include "rb_capi_internal.h"

@@ -30,7 +30,7 @@ struct DensePlan {
 void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_total = 0);
 size_t dense_workspace_bytes(int B, int N, int k, int row_bytes);
 // Bytes of one item row for a dtype code (RB_I8: D, else 2 D).
-inline int dense_row_bytes(int D, int dtype) { return dtype == RB_I8 ? D : 2 * D; }
+inline int dense_row_bytes(int D, int dtype) { return (dtype == RB_I8 || dtype == RB_E4M3) ? D : 2 * D; }
 int num_sms();
 size_t dense_chunk_stride(const DensePlan& pl);
 // mode 0: candidate pass over every tile; mode 1: chunk-max sampling pass.
@@ -50,6 +50,7 @@ int merge_pair_stack(const uint2* pairs, int W, int B, int kin, int k, int64_t* 
                      cudaStream_t stream);
 
 void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stream);
+
 void fill_empty_pairs(uint2* out, size_t n, cudaStream_t stream);
 
 int merge_shard_lists(const int64_t* ids, const float* scores, int W, int B, int kin, int k, int64_t* out_ids,

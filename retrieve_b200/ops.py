@@ -613,6 +613,39 @@ def int8_topk(query: Tensor, item_codes: Tensor, item_scales: Tensor, k: int) ->
     return int8_codes_topk(codes, qs, item_codes, xs, k)
 
 
+def scaled_topk(
+    queries: Tensor, query_scales: Tensor | None, items: Tensor, item_scales: Tensor | None, k: int, dtype_code: int,
+    id_offset: int = 0,
+) -> tuple[Tensor, Tensor]:
+    """Dense top-k over fp8 e4m3 rows (uint8 tensors; ``dtype_code`` must be
+    ``RB_E4M3``) with the int8 dequant on the fp32 accumulator,
+    ``(dot * query_scale) * item_scale`` (``None`` scales mean 1). C-ABI
+    ``rb_dense_topk_scaled``."""
+    if queries.dim() != 2 or items.dim() != 2 or queries.shape[1] != items.shape[1]:
+        raise ValueError("queries [B, D] and items [N, D] with the same D")
+    _require_cuda(queries, items)
+    check_contiguous(items=items)
+    q = queries.contiguous()
+    b, d = q.shape
+    n = items.shape[0]
+    dev = q.device
+    ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return ids, scores
+    qs = None if query_scales is None else query_scales.to(torch.float32).contiguous()
+    xs = None if item_scales is None else item_scales.to(torch.float32).contiguous()
+    lib = _lib.lib()
+    nb = ctypes.c_size_t(0)
+    _lib.check(lib.rb_dense_topk_workspace_size(b, n, d, dtype_code, k, ctypes.byref(nb)), "scaled_topk")
+    ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.rb_dense_topk_scaled(_ptr(q), _ptr(qs), _ptr(items), _ptr(xs), b, n, d, dtype_code, k,
+                                      int(id_offset), _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream_ptr(dev))
+    _lib.check(rc, "scaled_topk")
+    return ids, scores
+
+
 def int8_codes_topk(
     query_codes: Tensor, query_scales: Tensor | None, item_codes: Tensor, item_scales: Tensor | None, k: int,
     id_offset: int = 0,
@@ -647,20 +680,25 @@ def int8_codes_topk(
     return ids, scores
 
 
-def bits_to_pm1(bits: Tensor) -> Tensor:
-    """1-bit codes ``[N, W]`` int64 → ``[N, 64 W]`` int8 of ±1 (+1 where the bit
-    is set; C-ABI ``rb_bits_to_pm1``). The int8 dot of two such rows is the
+def bits_to_pm1(bits: Tensor, fmt: str = "int8") -> Tensor:
+    """1-bit codes ``[N, W]`` int64 → ``[N, 64 W]`` rows of ±1 (+1 where the bit
+    is set): int8 (C-ABI ``rb_bits_to_pm1``) or fp8 e4m3 bytes as uint8
+    (``fmt="e4m3"``, ``rb_bits_to_pm1_e4m3``). The dot of two such rows is the
     1-bit match score ``64 W − 2·popcount(q ^ x)``."""
     if bits.dim() != 2 or bits.dtype != torch.int64:
         raise ValueError("bits must be [N, W] int64")
+    if fmt not in ("int8", "e4m3"):
+        raise ValueError(f"fmt must be 'int8' or 'e4m3', got {fmt!r}")
     _require_cuda(bits)
     bits = bits.contiguous()
     n, w = bits.shape
-    out = torch.empty((n, 64 * w), dtype=torch.int8, device=bits.device)
+    e4m3 = fmt == "e4m3"
+    out = torch.empty((n, 64 * w), dtype=torch.uint8 if e4m3 else torch.int8, device=bits.device)
     if n == 0:
         return out
+    fn = _lib.lib().rb_bits_to_pm1_e4m3 if e4m3 else _lib.lib().rb_bits_to_pm1
     with torch.cuda.device(bits.device):
-        rc = _lib.lib().rb_bits_to_pm1(_ptr(bits), n, w, _ptr(out), _stream_ptr(bits.device))
+        rc = fn(_ptr(bits), n, w, _ptr(out), _stream_ptr(bits.device))
     _lib.check(rc, "bits_to_pm1")
     return out
 
@@ -678,6 +716,7 @@ __all__ = [
     "check_contiguous",
     "int8_topk",
     "int8_codes_topk",
+    "scaled_topk",
     "clause_compact",
     "clause_mask",
     "clause_mask_scores",

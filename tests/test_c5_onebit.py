@@ -40,6 +40,8 @@ def test_bits_to_pm1_matches_bit_order():
     shifts = torch.arange(64)
     expect = ((bits[:, :, None] >> shifts) & 1).reshape(1000, 512) * 2 - 1
     assert torch.equal(pm1.to(torch.int64), expect)
+    e4 = ops.bits_to_pm1(bits.cuda(), "e4m3").cpu()
+    assert torch.equal(e4.view(torch.float8_e4m3fn).float().to(torch.int64), expect)
 
 
 @pytest.mark.parametrize("w,b,n,k", [(8, 64, 100_000, 1000), (8, 300, 60_001, 100), (4, 200, 50_000, 256),
@@ -56,6 +58,19 @@ def test_tensor_core_onebit_topk_equals_popcount_oracle(w, b, n, k):
     if k > n:
         ref_i = np.concatenate([ref_i, np.full((b, k - n), -1)], axis=1)
         ref_s = np.concatenate([ref_s, np.full((b, k - n), -np.inf, dtype=np.float32)], axis=1)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i, ref_s)
+
+
+def test_e4m3_pm1_scan_equals_popcount_oracle():
+    """The same 1-bit top-k on the fp8 tensor cores (+-1 as e4m3)."""
+    from retrieve_b200 import _lib, ops
+
+    b, n, w, k = 200, 40_000, 8, 300
+    x = _clustered_bits(n, w, seed=13)
+    q = _clustered_bits(b, w, seed=14)
+    ids, scores = ops.scaled_topk(ops.bits_to_pm1(q.cuda(), "e4m3"), None, ops.bits_to_pm1(x.cuda(), "e4m3"), None,
+                                  k, _lib.RB_E4M3)
+    ref_i, ref_s = knn.oporp_full(q.numpy(), x.numpy(), k)
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i, ref_s)
 
 

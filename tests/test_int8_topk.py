@@ -76,8 +76,9 @@ def test_int8_tensor_core_dots_equal_reference_fused_kmean_ann(d):
     _lib.check(lib.rb_dense_topk_workspace_size(b, n, d, _lib.RB_I8, k, ctypes.byref(nb)), "ws")
     ws = torch.empty(max(nb.value, 256), dtype=torch.uint8, device="cuda")
     vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     rc = lib.rb_dense_topk_i8(vp(q), vp(qs), vp(x), vp(xs), b, n, d, k, 0, vp(ids), vp(scores), vp(ws), ws.numel(),
-                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+                              stream)
     _lib.check(rc, "dense_topk_i8")
     torch.cuda.synchronize()
     ref_ids, ref_scores = topk_strict(dots.astype(np.float32), k)
