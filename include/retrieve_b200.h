@@ -260,13 +260,12 @@ RB_API int rb_dense_topk_i8(const int8_t* query_codes, const float* query_scales
 RB_API int rb_bits_to_pm1(const int64_t* bits, int N, int W, int8_t* out, void* stream);
 
 /*
- * Dense top-k over fp8 e4m3 rows (kind::f8f6f4, fp32 accumulation) with the
- * int8 dequant on the accumulator: score = (dot * query_scale) * item_scale
- * (left to right; null scale arrays mean 1). dtype must be RB_E4M3; rows of
- * 128 / 256 / 512 bytes; k <= 1024. With +-1 codes (rb_bits_to_pm1_e4m3) every
- * partial sum is an integer of at most 512 in magnitude, so the scores are the
- * exact 1-bit match scores. Workspace as rb_dense_topk_workspace_size with the
- * same dtype.
+ * Dense top-k over fp8 e4m3 rows (kind::f8f6f4, fp32 accumulation, score = the
+ * accumulator). dtype must be RB_E4M3 and both scale arrays null (reserved);
+ * rows of 128 / 256 / 512 bytes; k <= 1024. With +-1 codes
+ * (rb_bits_to_pm1_e4m3) every partial sum is an integer of at most 512 in
+ * magnitude, so the scores are the exact 1-bit match scores 64 W - 2 hamming.
+ * Workspace as rb_dense_topk_workspace_size with the same dtype.
  */
 RB_API int rb_dense_topk_scaled(const void* queries, const float* query_scales, const void* items,
                                 const float* item_scales, int B, int N, int D, int dtype, int k, int64_t id_offset,

@@ -1,15 +1,16 @@
-"""1-bit candidate generation on the int8 tensor cores, and the LiNR V3 cascade.
+"""1-bit candidate generation on the fp8 tensor cores, and the LiNR V3 cascade.
 
 The reference scores 1-bit codes with popcounts: ``score = 64 W − 2 Σ_w
 popcount(q_w ^ x_w)`` (retrieve/src/retrieve/ops/reference/oporp_1bit_match_topk.py:9-41),
 the ``OneBitKNN`` stage of LiNR V3 (retrieve/src/retrieve/modules/linr.py:118-162).
 For codes mapped to ±1 vectors that score is their dot product, so here the item
-codes are expanded once, at registration, into a ±1 int8 table (``bits_to_pm1``,
-8 bytes per 64 code bits) and every batch is one ``kind::i8`` tensor-core scan
-with unit scales: exact int32 dots, the same scores and the same (score desc,
-id asc) ordering as the popcount path, at tensor-core rather than POPC-pipe
-throughput. (``bits_to_pm1(…, "e4m3")`` with ``scaled_topk`` is the same on the
-fp8 tensor cores.) Widths with
+codes are expanded once, at registration, into a ±1 fp8 e4m3 table
+(``bits_to_pm1(…, "e4m3")``, 8 bytes per 64 code bits) and every batch is one
+``kind::f8f6f4`` tensor-core scan whose fp32 accumulator is the score: ±1 is
+exact in e4m3 and every partial sum is an integer of at most 64 W in
+magnitude, so the scores are exact — the same scores and the same (score
+desc, id asc) ordering as the popcount path, at tensor-core rather than
+POPC-pipe throughput. Widths with
 64·W in {128, 256, 512} bits use the tensor cores; other widths use the exact
 popcount kernel (``oporp_1bit_match_topk_full``).
 """
@@ -34,7 +35,7 @@ class PackedBitsIndex:
         self.n, self.w = item_bits.shape
         self.tensor_cores = 64 * self.w in TENSOR_CORE_BITS
         if self.tensor_cores:
-            self.table = ops.bits_to_pm1(item_bits)
+            self.table = ops.bits_to_pm1(item_bits, "e4m3")
             self.bits = None
         else:
             self.table = None
@@ -47,8 +48,10 @@ class PackedBitsIndex:
         if query_bits.dim() != 2 or query_bits.shape[1] != self.w:
             raise ValueError(f"query_bits must be [B, {self.w}] int64")
         if self.tensor_cores:
-            q = ops.bits_to_pm1(query_bits.contiguous())
-            return ops.int8_codes_topk(q, None, self.table, None, k, id_offset)
+            from retrieve_b200 import _lib
+
+            q = ops.bits_to_pm1(query_bits.contiguous(), "e4m3")
+            return ops.scaled_topk(q, None, self.table, None, k, _lib.RB_E4M3, id_offset)
         ids, scores = ops.oporp_1bit_match_topk_full(query_bits, self.bits, min(k, self.n))
         if ids.shape[1] < k:  # fewer items than k: pad like the dense paths
             pad = k - ids.shape[1]

@@ -54,7 +54,7 @@ int rb_abi_version(void) { return 1; }
 int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* bytes) {
   if (bytes == nullptr) return fail(RB_ERR_INVALID_ARG, "bytes is null");
   if (B < 0 || N < 0 || D <= 0 || k < 1) return fail(RB_ERR_INVALID_ARG, "dense_topk: bad shape or k");
-  *bytes = dense_workspace_bytes(B, N, k, dense_row_bytes(D, dtype));
+  *bytes = dense_workspace_bytes(B, N, k, dense_row_bytes(D, dtype), dense_scaled(dtype));
   return RB_OK;
 }
 
@@ -122,11 +122,11 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   const int row_bytes = (elem == 2 || elem == 4) ? D : 2 * D;
   if (filter != nullptr && (k > 384 || row_bytes > 256))
     return fail(RB_ERR_UNSUPPORTED, "dense_topk_filtered: k <= 384 and rows of up to 256 bytes");
-  const size_t need = dense_workspace_bytes(B, N, k, row_bytes);
+  const size_t need = dense_workspace_bytes(B, N, k, row_bytes, elem >= 2);
   if (workspace == nullptr || workspace_bytes < need) return fail(RB_ERR_WORKSPACE, "dense_topk: workspace too small");
 
   DensePlan pl;
-  dense_plan(B, N, k, row_bytes, pl, shared ? shared->n_total : N);
+  dense_plan(B, N, k, row_bytes, pl, shared ? shared->n_total : N, elem >= 2);
   const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
   if (cudaMemsetAsync(d.err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
 
@@ -250,6 +250,8 @@ int rb_dense_topk_scaled(const void* queries, const float* query_scales, const v
                          int B, int N, int D, int dtype, int k, int64_t id_offset, int64_t* out_ids, float* out_scores,
                          void* workspace, size_t workspace_bytes, void* stream) {
   if (dtype != RB_E4M3) return fail(RB_ERR_TYPE, "dense_topk_scaled: dtype must be e4m3");
+  if (query_scales != nullptr || item_scales != nullptr)
+    return fail(RB_ERR_UNSUPPORTED, "dense_topk_scaled: e4m3 rows take no scales (pass null)");
   return dense_topk_impl(4, queries, query_scales, items, item_scales, B, N, D, k, id_offset,
                          out_ids, out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
@@ -274,7 +276,7 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
     return RB_OK;
   }
   DensePlan pl;
-  dense_plan(B, N, k, dense_row_bytes(D, dtype), pl, N);
+  dense_plan(B, N, k, dense_row_bytes(D, dtype), pl, N, dense_scaled(dtype));
   *n_launches = (pl.sample_stride > 0) ? 4 : 2;
   return RB_OK;
 }

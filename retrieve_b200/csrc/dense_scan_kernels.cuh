@@ -2,9 +2,9 @@
 // element type's variants are instantiated in their own translation unit
 // (dense_scan_e<ELEM>.cu); the planning and dispatch live in dense_scan_sm100.cu.
 //
-// Element types (ELEM): 0 fp16, 1 bf16, 2 int8 (kind::i8, int32 accumulate),
-// 4 fp8 e4m3 (kind::f8f6f4; +-1 codes give exact 1-bit match scores). 2 and 4
-// apply the (dot * q_scale) * item_scale dequant. (3 is not used.)
+// Element types (ELEM): 0 fp16, 1 bf16, 2 int8 (kind::i8, int32 accumulate,
+// (dot * q_scale) * item_scale dequant), 4 fp8 e4m3 (kind::f8f6f4, unscaled;
+// +-1 codes give exact 1-bit match scores). (3 is not used.)
 //
 // One persistent CTA per SM. A task is (query group, item split): the CTA
 // holds NG x 128 queries resident in shared memory (TMA, 128-byte swizzle) and
@@ -91,11 +91,10 @@ __device__ __forceinline__ void split_range(int split, int n_splits, int pass_ti
 // fp32 exactly; for integer values held as bf16 (ELEM 3) or fp8 e4m3 (ELEM 4)
 // the fp32 accumulator already holds the exact integer dot (every partial sum
 // is an integer below 2^24).
-// The scaled element types (2: int8, 4: fp8 e4m3) score
-// (fp32(dot) * q_scale) * item_scale, left to right as the reference dequantizes
-// (ops/official/adapter.py:338-367); null scale arrays mean 1. For int8 the
-// registers hold int32 dots, turned into fp32 exactly; for fp8 the fp32
-// accumulator already holds the dot.
+// int8 (ELEM 2) scores (fp32(dot) * q_scale) * item_scale, left to right as the
+// reference dequantizes (ops/official/adapter.py:338-367); null scale arrays
+// mean 1. The registers hold int32 dots, turned into fp32 exactly. fp8 e4m3
+// (ELEM 4) is unscaled: the fp32 accumulator is the score.
 template <int ELEM, int KB>
 __device__ __forceinline__ float raw_to_float(uint32_t raw) {
   if constexpr (ELEM != 2)
@@ -110,7 +109,7 @@ template <int MODE, int NCH, int ELEM, bool FILT, int KB>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list) {
-  if constexpr (ELEM >= 2) {
+  if constexpr (ELEM == 2) {
     const float qs = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
     const bool full = row0 + NCH * 32 <= static_cast<uint32_t>(p.N);
     const bool unit_x = p.x_scale == nullptr;

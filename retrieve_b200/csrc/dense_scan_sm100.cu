@@ -89,11 +89,13 @@ int num_sms() {
   return n;
 }
 
-void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_total) {
+void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_total, bool scaled) {
+  (void)scaled;  // the plan is the same for every element type
   // B > 128: 2-SM kernel, 256 queries per group, 1 or 2 groups per CTA pair
   // (one for 512-byte rows, whose operand tiles fill shared memory, and for
-  // lists past 512 entries, whose compaction needs the registers of a
-  // 6-warp CTA).
+  // lists past 512 entries, whose compaction needs the registers of a 6-warp
+  // CTA). The int8 dequant epilogue runs faster with two groups despite its
+  // spills: the epilogue's issue rate, not spilling, bounds it.
   pl.two_sm = B > kQTile;
   if (pl.two_sm) {
     pl.ng = (B <= 2 * kQTile || row_bytes > 256 || list_cap(k) > 512) ? 1 : 2;
@@ -133,9 +135,9 @@ size_t dense_chunk_stride(const DensePlan& pl) {
   return static_cast<size_t>((pl.tiles + pl.sample_stride - 1) / pl.sample_stride) * 4;
 }
 
-size_t dense_workspace_bytes(int B, int N, int k, int row_bytes) {
+size_t dense_workspace_bytes(int B, int N, int k, int row_bytes, bool scaled) {
   DensePlan pl;
-  dense_plan(B, N, k, row_bytes, pl, N);
+  dense_plan(B, N, k, row_bytes, pl, N, scaled);
   size_t lists = static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2);
   size_t counts = static_cast<size_t>(B) * pl.n_lists * sizeof(int);
   size_t th = 2 * static_cast<size_t>(B) * sizeof(float);

@@ -70,7 +70,7 @@ int rb_dense_topk_noalloc(const void* queries, const void* items, int B, int N, 
     set_last_error("dense_topk_noalloc: bad B, N or k");
     return RB_ERR_INVALID_ARG;
   }
-  const size_t need = dense_workspace_bytes(B, N, k, dense_row_bytes(D, dtype));
+  const size_t need = dense_workspace_bytes(B, N, k, dense_row_bytes(D, dtype), dense_scaled(dtype));
   if (need > kNoAllocScratchBytes) {
     static thread_local char msg[192];
     std::snprintf(msg, sizeof(msg),

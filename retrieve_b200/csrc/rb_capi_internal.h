@@ -27,8 +27,10 @@ struct DensePlan {
   int sample_stride;  // 0: no sampling pass; else the tile stride of the sample
 };
 
-void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_total = 0);
-size_t dense_workspace_bytes(int B, int N, int k, int row_bytes);
+void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_total = 0, bool scaled = false);
+size_t dense_workspace_bytes(int B, int N, int k, int row_bytes, bool scaled = false);
+// Element types with the per-query / per-item dequant in the epilogue.
+inline bool dense_scaled(int dtype) { return dtype == RB_I8 || dtype == RB_E4M3; }
 // Bytes of one item row for a dtype code (RB_I8: D, else 2 D).
 inline int dense_row_bytes(int D, int dtype) { return (dtype == RB_I8 || dtype == RB_E4M3) ? D : 2 * D; }
 int num_sms();

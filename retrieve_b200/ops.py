@@ -618,9 +618,8 @@ def scaled_topk(
     id_offset: int = 0,
 ) -> tuple[Tensor, Tensor]:
     """Dense top-k over fp8 e4m3 rows (uint8 tensors; ``dtype_code`` must be
-    ``RB_E4M3``) with the int8 dequant on the fp32 accumulator,
-    ``(dot * query_scale) * item_scale`` (``None`` scales mean 1). C-ABI
-    ``rb_dense_topk_scaled``."""
+    ``RB_E4M3``, scales ``None``): the score is the fp32 accumulator (exact for
+    ±1 codes). C-ABI ``rb_dense_topk_scaled``."""
     if queries.dim() != 2 or items.dim() != 2 or queries.shape[1] != items.shape[1]:
         raise ValueError("queries [B, D] and items [N, D] with the same D")
     _require_cuda(queries, items)
