@@ -41,3 +41,48 @@ def test_dense_argument_errors_map_to_python_exceptions():
     rc = lib.rb_dense_topk(None, None, 4, 10, 96, _lib.RB_BF16, 10, 0, None, None, None, 0, None)
     with pytest.raises(ValueError):
         _lib.check(rc, "dense_topk")
+
+
+def test_workspace_grows_with_row_width_and_k():
+    lib = _lib.lib()
+    sizes = {}
+    for name, d, dt, k in [("bf16 d128", 128, _lib.RB_BF16, 100), ("bf16 d256", 256, _lib.RB_BF16, 100),
+                           ("int8 d512", 512, _lib.RB_I8, 100), ("e4m3 d512", 512, _lib.RB_E4M3, 1000),
+                           ("bf16 k1024", 128, _lib.RB_BF16, 1024)]:
+        n = ctypes.c_size_t(0)
+        assert lib.rb_dense_topk_workspace_size(1024, 1_000_000, d, dt, k, ctypes.byref(n)) == 0, name
+        sizes[name] = n.value
+    # one query group per CTA pair (512-byte rows, lists past 512 entries) halves the
+    # splits and doubles the lists per split: k = 1000 needs the largest lists
+    assert sizes["e4m3 d512"] > sizes["bf16 d128"]
+    assert sizes["bf16 k1024"] > sizes["bf16 d128"]
+
+
+def test_new_entry_points_validate_before_touching_a_device():
+    lib = _lib.lib()
+    # e4m3 scan takes no scales
+    rc = lib.rb_dense_topk_scaled(None, ctypes.c_void_p(16), None, None, 4, 10, 128, _lib.RB_E4M3, 10, 0, None,
+                                  None, None, 0, None)
+    assert rc == _lib.RB_ERR_UNSUPPORTED and b"scales" in lib.rb_last_error()
+    # only e4m3 rows
+    rc = lib.rb_dense_topk_scaled(None, None, None, None, 4, 10, 128, _lib.RB_BF16, 10, 0, None, None, None, 0,
+                                  None)
+    with pytest.raises(TypeError):
+        _lib.check(rc, "dense_topk_scaled")
+    # k beyond the selection limit
+    rc = lib.rb_dense_topk(None, None, 4, 10, 128, _lib.RB_BF16, 2000, 0, None, None, None, 0, None)
+    assert rc == _lib.RB_ERR_UNSUPPORTED and b"1024" in lib.rb_last_error()
+    # 1-bit expansion: sizes and alignment
+    assert lib.rb_bits_to_pm1(None, -1, 8, None, None) == _lib.RB_ERR_INVALID_ARG
+    assert lib.rb_bits_to_pm1_e4m3(ctypes.c_void_p(16), 4, 8, ctypes.c_void_p(17), None) == _lib.RB_ERR_INVALID_ARG
+    assert b"aligned" in lib.rb_last_error()
+    # sample width of the shared seed
+    rc = lib.rb_dense_seed_sample(None, None, 4, 10, 128, _lib.RB_BF16, 10, 11, 10, ctypes.c_void_p(16), None, 0,
+                                  None)
+    assert rc in (_lib.RB_ERR_INVALID_ARG, _lib.RB_ERR_WORKSPACE)
+    rc = lib.rb_dense_topk_seeded(None, None, 4, 10, 128, _lib.RB_BF16, 10, 0, 10, ctypes.c_void_p(16), 2, 11,
+                                  None, None, None, None, 0, None)
+    assert rc == _lib.RB_ERR_INVALID_ARG and b"m <= k" in lib.rb_last_error()
+    # merge of packed pairs
+    assert lib.rb_merge_pairs(None, 0, 4, 10, 10, None, None, None) == _lib.RB_ERR_INVALID_ARG
+    assert lib.rb_merge_pairs(None, 2, 4, 10, 2000, None, None, None) == _lib.RB_ERR_UNSUPPORTED
