@@ -105,30 +105,39 @@ __device__ __forceinline__ float raw_to_float(uint32_t raw) {
     return __int2float_rn(static_cast<int>(raw));  // D = 512: |dot| < 2^24, exact by conversion
 }
 
+// `stage` is the calling warp's 1 KB of shared scratch (its list-compaction
+// histogram, idle here): the int8 path stages the tile's 128 item scales in it.
 template <int MODE, int NCH, int ELEM, bool FILT, int KB>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
-                                               uint2* list) {
+                                               uint2* list, uint32_t* stage) {
   if constexpr (ELEM == 2) {
     const float qs = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
-    const bool full = row0 + NCH * 32 <= static_cast<uint32_t>(p.N);
     const bool unit_x = p.x_scale == nullptr;
+    // Every lane needs all 128 item scales of the tile: the warp loads them
+    // once (one float4 per lane, coalesced) into shared memory, and each lane
+    // then reads them as broadcasts instead of 32 dependent global loads.
+    float4* sx = reinterpret_cast<float4*>(stage);
+    if (!unit_x) {
+      const int lane = threadIdx.x & 31;
+      const uint32_t id = row0 + 4 * static_cast<uint32_t>(lane);
+      float4 v;
+      if (row0 + NCH * 32 <= static_cast<uint32_t>(p.N)) {
+        v = __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
+      } else {
+        v.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
+        v.y = id + 1 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 1] : 0.f;
+        v.z = id + 2 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 2] : 0.f;
+        v.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
+      }
+      sx[lane] = v;
+    }
+    __syncwarp();
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
-        const uint32_t id = row0 + ch * 32 + 4 * j4;
-        float4 xs;
-        if (unit_x) {
-          xs = make_float4(1.f, 1.f, 1.f, 1.f);
-        } else if (full) {
-          xs = __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
-        } else {
-          xs.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
-          xs.y = id + 1 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 1] : 0.f;
-          xs.z = id + 2 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 2] : 0.f;
-          xs.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
-        }
+        const float4 xs = unit_x ? make_float4(1.f, 1.f, 1.f, 1.f) : sx[ch * 8 + j4];
         const float xv[4] = {xs.x, xs.y, xs.z, xs.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u)
@@ -136,6 +145,7 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
               __float_as_uint(__fmul_rn(__fmul_rn(raw_to_float<ELEM, KB>(r[ch][4 * j4 + u]), qs), xv[u]));
       }
     }
+    __syncwarp();  // every lane has read the staged scales before the scratch is reused
   }
   if (row0 + NCH * 32 > static_cast<uint32_t>(p.N)) {
     // last, partial tile: rows past N were zero-filled by TMA; NaN never passes
@@ -415,7 +425,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -706,7 +716,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
-        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list);
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist);
         if (++acc == kAcc) {
           acc = 0;
           acc_phase ^= 1;
