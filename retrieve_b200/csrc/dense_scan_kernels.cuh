@@ -4,7 +4,8 @@
 //
 // Element types (ELEM): 0 fp16, 1 bf16, 2 int8 (kind::i8, int32 accumulate,
 // (dot * q_scale) * item_scale dequant), 4 fp8 e4m3 (kind::f8f6f4, unscaled;
-// +-1 codes give exact 1-bit match scores). (3 is not used.)
+// +-1 codes give exact 1-bit match scores). The fp16 and fp8 descriptors share
+// their format code 0 (F16 for kind::f16, E4M3 for kind::f8f6f4).
 //
 // One persistent CTA per SM. A task is (query group, item split): the CTA
 // holds NG x 128 queries resident in shared memory (TMA, 128-byte swizzle) and
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
   constexpr uint32_t kTmemCols = 2 * NG * 128;
   constexpr uint32_t kIdesc =
       (ELEM == 2) ? make_idesc(2, 1, kQTile, kTileItems)
-                  : make_idesc(1, (ELEM == 1 || ELEM == 3) ? 1 : 0, kQTile, kTileItems);
+                  : make_idesc(1, ELEM == 1 ? 1 : 0, kQTile, kTileItems);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -483,7 +484,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
   constexpr int kAcc = 4 / NG;  // accumulator buffers: all 512 TMEM columns
   constexpr uint32_t kTmemCols = kAcc * NG * 128;
   constexpr uint32_t kIdesc = (ELEM == 2) ? make_idesc(2, 1, 2 * kQTile, kTileItems)
-                                          : make_idesc(1, (ELEM == 1 || ELEM == 3) ? 1 : 0, 2 * kQTile, kTileItems);
+                                          : make_idesc(1, ELEM == 1 ? 1 : 0, 2 * kQTile, kTileItems);
   constexpr int kQPerPair = NG * 2 * kQTile;
 
   extern __shared__ uint8_t smem_raw[];

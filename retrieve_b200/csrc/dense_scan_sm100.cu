@@ -50,8 +50,8 @@ static bool make_tmap(CUtensorMap* map, const void* base, int elem, uint64_t row
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const int eb = (elem == 2 || elem == 4) ? 1 : 2;
-  CUtensorMapDataType dt = (elem == 2 || elem == 4)  ? CU_TENSOR_MAP_DATA_TYPE_UINT8
-                           : (elem == 1 || elem == 3) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+  CUtensorMapDataType dt = (elem == 2 || elem == 4) ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                           : (elem == 1)              ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols * eb};
