@@ -1,0 +1,174 @@
+"""SilverTorch's IVF probe + int8 scoring path, ``st::search``, restated on the
+CPU. Test infrastructure: only the tests, ``smoke()`` and the bench's CPU legs
+use it, as the checker.
+
+The op (schema silvertorch/ops/csrc/fork_search.cpp:13-41, body
+fork_search_cuda.cu:1256-1524), for each query row ``b``:
+
+1. Query prep (fork_search_cuda.cu:680-700): the row quantized to int8 exactly
+   as ``quantize_int8`` evaluates on a CUDA tensor (``oracle.knn.quantize_int8``:
+   the code quotient in fp64 rounded to fp32; the scale
+   ``abs_max * fp32(1/127)``).
+2. Candidates: the sorted-table positions of the probed clusters
+   ``probe_ids[b, :]`` (cluster ``c`` holds positions
+   ``cluster_offsets[c] .. cluster_offsets[c] + cluster_sizes[c]``). The scorer
+   writes them into a row of ``width = round_up(max_tensor_size_per_row, 32)``
+   slots in its own order: first every probed cluster's warp-aligned prefix
+   (``32 * (len // 32)`` positions), cluster by cluster in probe order, then
+   every cluster's remainder (``len % 32`` positions), in probe order
+   (silvertorch/ops/csrc/fused_kmean_ann_cuda.cu:100-110 and 183-215; the
+   prep's cumsums, fork_search_cuda.cu:705-760). ``probe_slots`` gives that
+   order; it decides which of several tied candidates is kept.
+3. Score per slot: the exact int32 dot of the int8 codes
+   (fused_kmean_ann.cpp:60-70); with ``divisor_for_int8 != -1`` the fp16 value
+   ``fp16(fp32(dot) / fp32(divisor))`` (fused_kmean_ann.cpp:196-200,
+   fused_kmean_ann_cuda.cu:1031). A full-``N`` ``filtering_bit_mask``
+   ``[B, ceil(N / 64)]`` int64 drops a position ``d`` whose bit is clear; the
+   CUDA scorer reads bit ``63 - d % 64`` of word ``d // 64`` (high bit first:
+   silvertorch/ops/csrc/bloom_index_util.cuh:138-147, 157-180;
+   retrieve/src/retrieve/ops/official/__init__.py:31). Dropped slots are never
+   returned.
+4. Top-k on the raw scores, larger first, ties to the lower slot
+   (fork_search_cuda.cu:1374-1480; retrieve/src/retrieve/ops/official/adapter.py:465-478),
+   over ``min(k, width)`` slots, then the ``[B, k]`` epilogue
+   (fork_search_cuda.cu:560-591): ``id = sort_perm[position]``;
+   int32 path ``score = fp32(fp32(fp32(dot) * q_scale) * global_scale)``;
+   fp16 path ``score = fp32(raw) * fp32(fp32(q_scale * divisor) * global_scale)``
+   (adapter.py:363-367, the same left-associated multiplies); ``-1`` / ``-inf``
+   past the candidates.
+
+The reference's own check of the op is "scores bit-identical, ids equal up to
+ties" against a per-row torch oracle (retrieve/tests/parity/test_official.py:128-160,
+211-217). This restatement is pinned to the reference's CPU scorer
+(``st.fused_kmean_ann``) and its adapter epilogue (``official_probe_score``) by
+``tests/golden/make_golden_ivf.py``.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from oracle.knn import quantize_int8
+
+WARP = 32
+INT32_MIN = np.iinfo(np.int32).min
+
+
+def padded_width(max_tensor_size_per_row: int) -> int:
+    """retrieve/src/retrieve/ops/official/adapter.py:655-657."""
+    return (int(max_tensor_size_per_row) + WARP - 1) // WARP * WARP
+
+
+def default_divisor(d: int) -> int:
+    """Smallest power of two ``v`` with ``127^2 * d / v <= 65504``
+    (adapter.py:30-35): the fp16 path's divisor, exact and overflow-free."""
+    need = (127 * 127 * d) / 65504.0
+    v = 1
+    while v < need:
+        v *= 2
+    return v
+
+
+def probe_slots(probe_row, cluster_offsets, cluster_sizes) -> np.ndarray:
+    """The sorted-table positions one query row scores, in the scorer's slot
+    order: warp-aligned prefixes of the probed clusters, then their remainders."""
+    heads, tails = [], []
+    for c in np.asarray(probe_row, dtype=np.int64).tolist():
+        start = int(cluster_offsets[c])
+        n = int(cluster_sizes[c])
+        full = n // WARP * WARP
+        heads.append(np.arange(start, start + full, dtype=np.int64))
+        tails.append(np.arange(start + full, start + n, dtype=np.int64))
+    return np.concatenate(heads + tails) if heads else np.zeros(0, dtype=np.int64)
+
+
+def mask_bit_high_first(words_row, pos) -> np.ndarray:
+    """Bit of sorted position ``pos`` in one packed ``filtering_bit_mask`` row:
+    bit ``63 - pos % 64`` of word ``pos // 64``."""
+    w = np.asarray(words_row, dtype=np.int64).view(np.uint64)
+    shift = (63 - pos % 64).astype(np.uint64)
+    return ((w[pos // 64] >> shift) & np.uint64(1)).astype(bool)
+
+
+def pack_mask_high_first(mask) -> np.ndarray:
+    """``[B, N]`` bool to ``[B, ceil(N / 64)]`` int64, position ``d`` at bit
+    ``63 - d % 64`` of word ``d // 64`` (adapter.py:254-267, ``high_first``)."""
+    mask = np.asarray(mask, dtype=bool)
+    b, n = mask.shape
+    w = (n + 63) // 64
+    padded = np.zeros((b, w * 64), dtype=bool)
+    padded[:, :n] = mask
+    bits = padded.reshape(b, w, 64).astype(np.uint64)
+    shifts = (63 - np.arange(64)).astype(np.uint64)
+    return np.bitwise_or.reduce(bits << shifts, axis=2).view(np.int64)
+
+
+def raw_scores(q_codes_row, item_codes, pos, divisor: int):
+    """Per-slot raw scores: int32 dots, or fp16 ``dot / divisor``."""
+    dots = np.asarray(item_codes, dtype=np.int8)[pos].astype(np.int64) @ np.asarray(q_codes_row, np.int64)
+    if divisor == -1:
+        return dots.astype(np.int32)
+    return (dots.astype(np.float32) / np.float32(divisor)).astype(np.float16)
+
+
+def search_codes(q_codes, q_scales, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm,
+                 global_scale, k, max_tensor_size_per_row, divisor_for_int8=-1, filtering_bit_mask=None):
+    """``st::search`` after the query prep: ``(ids int64 [B, k], scores fp32 [B, k])``."""
+    q_codes = np.asarray(q_codes, dtype=np.int8)
+    q_scales = np.asarray(q_scales, dtype=np.float32)
+    probe_ids = np.asarray(probe_ids, dtype=np.int64)
+    offsets = np.asarray(cluster_offsets, dtype=np.int64)
+    sizes = np.asarray(cluster_sizes, dtype=np.int64)
+    sort_perm = np.asarray(sort_perm, dtype=np.int64)
+    gs = np.float32(np.asarray(global_scale, dtype=np.float32).reshape(-1)[0])
+    width = padded_width(max_tensor_size_per_row)
+    b = q_codes.shape[0]
+    ids = np.full((b, k), -1, dtype=np.int64)
+    scores = np.full((b, k), -np.inf, dtype=np.float32)
+    for row in range(b):
+        pos = probe_slots(probe_ids[row], offsets, sizes)
+        if pos.size > width:
+            raise ValueError(f"row {row} probes {pos.size} positions > width {width}")
+        raw = raw_scores(q_codes[row], item_codes, pos, divisor_for_int8)
+        slot = np.arange(pos.size, dtype=np.int64)
+        if filtering_bit_mask is not None:
+            keep = mask_bit_high_first(np.asarray(filtering_bit_mask)[row], pos)
+            pos, raw, slot = pos[keep], raw[keep], slot[keep]
+        # larger raw first, ties to the lower slot; only min(k, width) slots are taken
+        order = np.lexsort((slot, -raw.astype(np.float64)))[: min(k, width)]
+        n = order.size
+        ids[row, :n] = sort_perm[pos[order]]
+        top = raw[order]
+        if divisor_for_int8 == -1:
+            s = (top.astype(np.float32) * q_scales[row]).astype(np.float32) * gs
+        else:
+            f = (q_scales[row] * np.float32(divisor_for_int8)).astype(np.float32) * gs
+            s = top.astype(np.float32) * np.float32(f)
+        scores[row, :n] = s.astype(np.float32)
+    return ids, scores
+
+
+def search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm, global_scale, k,
+           max_tensor_size_per_row, divisor_for_int8=-1, filtering_bit_mask=None):
+    """``st::search`` (fork_search.cpp:13-41) on fp32 queries ``[B, D]``."""
+    q_codes, q_scales = quantize_int8(np.asarray(query, dtype=np.float32))
+    return search_codes(q_codes, q_scales, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm,
+                        global_scale, k, max_tensor_size_per_row, divisor_for_int8, filtering_bit_mask)
+
+
+def probe_prep(query, probe_ids, cluster_offsets, cluster_sizes):
+    """``st::probe_prep`` (fork_search.cpp:43-49; fork_search_cuda.cu:1529-1546): the
+    nine outputs the reference checks (retrieve/tests/parity/test_official.py:676-697):
+    int8 codes, scales, probed cluster ids, their lengths and offsets, the warp
+    count of each (row, probe) flattened, the per-row cumsum of warp-rounded
+    lengths, and the global cumsums of remainders and of warp counts."""
+    codes, scales = quantize_int8(np.asarray(query, dtype=np.float32))
+    probe = np.asarray(probe_ids, dtype=np.int64)
+    sizes = np.asarray(cluster_sizes, dtype=np.int64)
+    offsets = np.asarray(cluster_offsets, dtype=np.int64)
+    length = sizes[probe]
+    warps = (length // WARP).astype(np.int32).reshape(-1)
+    rounded_cumsum = np.cumsum((warps * WARP).reshape(probe.shape), axis=1, dtype=np.int32)
+    rem_cumsum = np.cumsum((length % WARP).reshape(-1), dtype=np.int32)
+    warp_cumsum = np.cumsum(warps, dtype=np.int32)
+    return codes, scales, probe, length, offsets[probe], warps, rounded_cumsum, rem_cumsum, warp_cumsum

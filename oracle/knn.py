@@ -8,7 +8,8 @@
   — ``64*W - 2*popcount(q ^ x)``; the indirect form returns ``min(k, P)``
   columns.
 * ``gemv_scores``: ops/triton/gemv_scores.py:19-28 via the C restatement.
-* ``quantize_int8``: indexing/quantize.py:9-18.
+* ``quantize_int8``: indexing/quantize.py:9-18, with the scale as torch
+  evaluates it on a CUDA tensor (a multiply by fp32(1/127)).
 """
 
 from __future__ import annotations
@@ -107,10 +108,23 @@ def gemv_scores(query_f16, items_t_f16) -> np.ndarray:
     return out.reshape(1, n)
 
 
-def quantize_int8(x):
+def quantize_int8(x, device_scale: bool = True):
+    """indexing/quantize.py:9-18 as it evaluates on a CUDA tensor. The scale
+    ``abs_max / 127.0`` is then ``abs_max * fp32(1/127)``: torch computes a
+    division by a CPU scalar on the device as a multiply by its fp32
+    reciprocal, and SilverTorch's query prep writes the same product
+    (silvertorch/ops/csrc/fork_search_cuda.cu:686), which the reference checks
+    equal to ``quantize_int8`` on CUDA (retrieve/tests/parity/test_official.py:676-697).
+    ``device_scale=False`` gives the CPU evaluation (a correctly rounded
+    division), which is what the CPU-generated golden fixture holds. Codes are
+    the same either way: the fp64 quotient rounded to fp32, times 127, rounded
+    half to even, clamped."""
     x = np.asarray(x, dtype=np.float32)
     abs_max = np.maximum(np.abs(x).max(axis=1, keepdims=True), np.float32(1e-8)).astype(np.float32)
-    scales = (abs_max / np.float32(127.0)).astype(np.float32)[:, 0]
+    if device_scale:
+        scales = (abs_max * (np.float32(1.0) / np.float32(127.0))).astype(np.float32)[:, 0]
+    else:
+        scales = (abs_max / np.float32(127.0)).astype(np.float32)[:, 0]
     ratio = (x.astype(np.float64) / abs_max.astype(np.float64)).astype(np.float32)
     codes = np.clip(np.rint(ratio * np.float32(127.0)), -128, 127).astype(np.int8)
     return codes, scales

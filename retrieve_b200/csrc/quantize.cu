@@ -1,8 +1,13 @@
 // Per-row symmetric int8 quantization of a query batch, the query side of the
 // int8 paths (retrieve/src/retrieve/indexing/quantize.py:9-18 `quantize_int8`):
 //   abs_max = max(max_d |x[b, d]|, 1e-8)        (fp32)
-//   scale   = abs_max / 127                      (fp32 division)
+//   scale   = abs_max * fp32(1/127)              (fp32 multiply)
 //   code    = clamp(round_half_even(fp32(fp64(x) / fp64(abs_max)) * 127), -128, 127)
+// The scale is what `abs_max / 127.0` gives on a CUDA tensor: torch evaluates a division by a
+// CPU scalar on the device as a multiply by the scalar's fp32 reciprocal, and SilverTorch's
+// query prep writes the same product (silvertorch/ops/csrc/fork_search_cuda.cu:686; the
+// reference checks the two equal, retrieve/tests/parity/test_official.py:676-697). On a CPU
+// tensor torch divides, which differs in the last bit for a few rows in a hundred.
 // One warp per row.
 #include <algorithm>
 #include <cstdint>
@@ -31,7 +36,7 @@ __global__ void quantize_int8_rows_kernel(const float* __restrict__ x, int B, in
     c = fminf(fmaxf(c, -128.f), 127.f);
     cr[d] = static_cast<int8_t>(c);
   }
-  if (lane == 0) scales[row] = __fdiv_rn(abs_max, 127.f);
+  if (lane == 0) scales[row] = __fmul_rn(abs_max, 1.0f / 127.0f);
 }
 
 }  // namespace rb

@@ -168,8 +168,18 @@ def test_oporp_indirect_min_k_p_columns():
 
 def test_quantize_int8_bit_exact():
     ops = _ops()
-    x = gi.quantize_inputs()
-    codes, scales = ops.quantize_int8(x.cuda())
-    ref_c, ref_s = knn.quantize_int8(x.numpy())
-    assert np.array_equal(codes.cpu().numpy(), ref_c)
-    assert np.array_equal(scales.cpu().numpy(), ref_s)
+    g = torch.Generator().manual_seed(9)
+    for x in (gi.quantize_inputs(), torch.randn(10_000, 192, generator=g)):
+        x = x.clone()
+        x[0] = 0.0
+        x[1] = 0.0
+        x[1, 3] = 1e-30
+        x[2] = torch.arange(x.shape[1]) % 3 - 1.0
+        x[2, 0] = 2.54
+        x[2, 1:5] = torch.tensor([0.01, -0.01, 1.27, -1.27])
+        codes, scales = ops.quantize_int8(x.cuda())
+        ref_c, ref_s = knn.quantize_int8(x.numpy())
+        assert np.array_equal(codes.cpu().numpy(), ref_c)
+        assert np.array_equal(scales.cpu().numpy(), ref_s)
+        # the device form of the scale (a multiply by fp32(1/127)), not the CPU division
+        assert np.array_equal(scales.cpu().numpy(), (x.cuda().abs().amax(1).clamp(min=1e-8) / 127.0).cpu().numpy())

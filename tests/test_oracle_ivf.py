@@ -1,0 +1,146 @@
+"""Pins the ``st::search`` restatement (oracle/ivf.py) to the reference: the
+fixture made by the reference's adapter epilogue over its own CPU scorer
+(tests/golden/make_golden_ivf.py), and the slot-order and prep facts of the
+reference's CUDA op. CPU only."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import ivf, knn
+from tests.helpers import assert_topk_equal_up_to_ties
+
+GOLDEN = np.load(Path(__file__).resolve().parent / "golden" / "golden_ivf.npz")
+N_CASES = len({k.split("_")[0] for k in GOLDEN.files})
+
+
+def _case(ci):
+    p = f"c{ci}_"
+    g = {k[len(p):]: GOLDEN[k] for k in GOLDEN.files if k.startswith(p)}
+    n_lists, max_size, n_probe, d, k, b, width, div, ties = g["shape"].tolist()
+    return g, dict(k=k, width=width, div=div, d=d, b=b)
+
+
+def _args(g, meta):
+    return (g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"], g["gs"],
+            meta["k"], meta["width"])
+
+
+def _check(ids, scores, ref_ids, ref_scores):
+    assert_topk_equal_up_to_ties(ids, scores, ref_ids, ref_scores)
+    pad = np.isneginf(ref_scores)
+    assert (ids[pad] == -1).all() and (ref_ids[pad] == -1).all()
+
+
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_int32_path_matches_reference(ci):
+    g, meta = _case(ci)
+    ids, scores = ivf.search(*_args(g, meta))
+    _check(ids, scores, g["ids32"], g["sc32"])
+
+
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_fp16_path_matches_reference(ci):
+    g, meta = _case(ci)
+    assert meta["div"] == ivf.default_divisor(meta["d"])
+    ids, scores = ivf.search(*_args(g, meta), divisor_for_int8=meta["div"])
+    _check(ids, scores, g["ids16"], g["sc16"])
+
+
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_filter_mask_matches_reference(ci):
+    """The fixture's boolean mask, packed high bit first as the CUDA scorer reads it
+    (the CPU run got it packed low bit first, the CPU scorer's order)."""
+    g, meta = _case(ci)
+    words = ivf.pack_mask_high_first(g["mask"])
+    ids, scores = ivf.search(*_args(g, meta), filtering_bit_mask=words)
+    _check(ids, scores, g["idsm"], g["scm"])
+    kept = ids >= 0
+    rows = np.nonzero(kept)[0]
+    inv = np.argsort(g["sort_perm"])
+    assert g["mask"][rows, inv[ids[kept]]].all(), "a filtered-out position was returned"
+
+
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_raw_dots_match_reference_scorer(ci):
+    """The scorer's raw row (st.fused_kmean_ann on the CPU): the same (position, int32
+    dot) multiset as the restatement's slots, INT32_MIN / -1 in the pad slots."""
+    g, meta = _case(ci)
+    codes, _ = knn.quantize_int8(g["query"])
+    raw, idx = g["raw"], g["idx"]
+    assert raw.shape == (meta["b"], ivf.padded_width(meta["width"])) and raw.dtype == np.int32
+    for r in range(meta["b"]):
+        pos = ivf.probe_slots(g["probe"][r], g["offsets"], g["sizes"])
+        dots = ivf.raw_scores(codes[r], g["codes"], pos, -1)
+        valid = idx[r] >= 0
+        assert (raw[r][~valid] == ivf.INT32_MIN).all()
+        got = sorted(zip(idx[r][valid].tolist(), raw[r][valid].tolist()))
+        assert got == sorted(zip(pos.tolist(), dots.tolist()))
+
+
+def test_slot_order_is_warp_prefixes_then_remainders():
+    """Clusters of 33 and 5 items probed as [1, 0], every item tied: the kept ids
+    follow the CUDA scorer's slots (cluster 0's first 32, then the remainders in
+    probe order: cluster 1's five, cluster 0's 33rd), not the probe-order
+    concatenation."""
+    sizes = np.array([33, 5, 7], dtype=np.int64)
+    offsets = np.r_[0, np.cumsum(sizes)]
+    order = ivf.probe_slots(np.array([1, 0]), offsets, sizes)
+    assert order.tolist() == list(range(0, 32)) + list(range(33, 38)) + [32]
+    other = ivf.probe_slots(np.array([0, 1]), offsets, sizes)
+    assert other.tolist() == list(range(0, 32)) + [32] + list(range(33, 38))
+    codes = np.ones((int(offsets[-1]), 8), dtype=np.int8)
+    q = np.ones((1, 8), dtype=np.float32)
+    sort_perm = np.arange(int(offsets[-1]))[::-1].copy()
+    ids, scores = ivf.search(q, np.array([[1, 0]]), offsets, sizes, codes, sort_perm, np.float32(0.5), 40, 38)
+    assert (ids[0, :38] == sort_perm[order]).all() and (ids[0, 38:] == -1).all()
+    assert np.isneginf(scores[0, 38:]).all() and (scores[0, :38] == scores[0, 0]).all()
+
+
+def test_k_above_width_pads():
+    sizes = np.array([3], dtype=np.int64)
+    offsets = np.array([0, 3])
+    codes = np.array([[1, 0], [0, 1], [2, 2]], dtype=np.int8)
+    ids, scores = ivf.search(np.array([[1.0, 0.5]], np.float32), np.array([[0]]), offsets, sizes, codes,
+                             np.array([10, 11, 12]), np.float32(1.0), 40, 3)
+    # width rounds up to 32 slots; only the 3 written ones are returned
+    assert ids[0, :3].tolist() == [12, 10, 11] and (ids[0, 3:] == -1).all()
+    assert np.isneginf(scores[0, 3:]).all()
+
+
+def test_row_wider_than_width_is_rejected():
+    sizes = np.array([40], dtype=np.int64)
+    with pytest.raises(ValueError):
+        ivf.search(np.ones((1, 4), np.float32), np.array([[0]]), np.array([0, 40]), sizes,
+                   np.ones((40, 4), np.int8), np.arange(40), np.float32(1.0), 5, 32)
+
+
+def test_probe_prep_cumsums():
+    """st::probe_prep's outputs as the reference checks them
+    (retrieve/tests/parity/test_official.py:676-697)."""
+    rng = np.random.default_rng(9)
+    sizes = rng.integers(0, 150, 300)
+    offsets = np.r_[0, np.cumsum(sizes)]
+    probe = np.argsort(rng.random((20, 300)), axis=1)[:, :24]
+    q = rng.standard_normal((20, 128)).astype(np.float32)
+    out = ivf.probe_prep(q, probe, offsets, sizes)
+    codes, scales = knn.quantize_int8(q)
+    assert np.array_equal(out[0], codes) and np.array_equal(out[1], scales)
+    length = sizes[probe]
+    assert np.array_equal(out[3], length) and np.array_equal(out[4], offsets[probe])
+    warps = (length // 32).reshape(-1)
+    assert np.array_equal(out[5], warps)
+    assert np.array_equal(out[6], np.cumsum((warps * 32).reshape(probe.shape), axis=1))
+    assert np.array_equal(out[7], np.cumsum((length % 32).reshape(-1)))
+    assert np.array_equal(out[8], np.cumsum(warps))
+    # the slot order's split point per row is the row's last warp-rounded cumsum
+    for r in range(3):
+        pos = ivf.probe_slots(probe[r], offsets, sizes)
+        assert len(pos) == int(length[r].sum())
+        cluster = np.searchsorted(offsets, pos, side="right") - 1
+        in_warp_prefix = (pos - offsets[cluster]) < sizes[cluster] // 32 * 32
+        head = int(out[6][r, -1])
+        assert in_warp_prefix[:head].all() and not in_warp_prefix[head:].any()

@@ -69,9 +69,41 @@ def test_oporp_matches_reference():
 
 
 def test_quantize_int8_matches_reference():
-    codes, scales = knn.quantize_int8(gi.quantize_inputs().numpy())
+    """The fixture was made by the reference's ``quantize_int8`` on CPU tensors, where
+    torch divides by 127; on CUDA tensors (the path this package replaces) torch and
+    SilverTorch's prep multiply by fp32(1/127). Codes agree in both; the CPU scales
+    are pinned exactly, and the device scales sit within one ulp of them."""
+    x = gi.quantize_inputs().numpy()
+    codes, cpu_scales = knn.quantize_int8(x, device_scale=False)
     assert np.array_equal(codes, GOLDEN["q8_codes"])
-    assert np.array_equal(scales, GOLDEN["q8_scales"])
+    assert np.array_equal(cpu_scales, GOLDEN["q8_scales"])
+    dev_codes, dev_scales = knn.quantize_int8(x)
+    assert np.array_equal(dev_codes, codes)
+    gap = np.abs(dev_scales.view(np.int32).astype(np.int64) - cpu_scales.view(np.int32).astype(np.int64))
+    assert gap.max() <= 1
+    abs_max = np.maximum(np.abs(x).max(axis=1), np.float32(1e-8))
+    recip = np.float32(1.0) / np.float32(127.0)
+    assert np.array_equal(dev_scales, (abs_max * recip).astype(np.float32))
+
+
+def test_quantize_int8_device_edge_rows():
+    """The rows ``st::probe_prep`` is checked on against ``quantize_int8``
+    (retrieve/tests/parity/test_official.py:676-697): all zeros, one tiny value, and
+    quotients that land exactly on a half code (ties round to even)."""
+    d = 16
+    x = np.zeros((3, d), dtype=np.float32)
+    x[1, 3] = np.float32(1e-30)
+    x[2] = (np.arange(d) % 3 - 1.0).astype(np.float32)
+    x[2, 0] = np.float32(2.54)
+    x[2, 1:5] = np.array([0.01, -0.01, 1.27, -1.27], dtype=np.float32)
+    codes, scales = knn.quantize_int8(x)
+    assert (codes[0] == 0).all() and scales[0] == np.float32(1e-8) * (np.float32(1) / np.float32(127))
+    assert (codes[1] == 0).all()  # 1e-30 is below the 1e-8 floor of abs_max
+    # 127 * x / 2.54 for x = ±0.01, ±1.27 is ±0.5, ±63.5 up to the fp32 rounding of the quotient
+    ratio = (x[2].astype(np.float64) / np.float64(np.float32(2.54))).astype(np.float32)
+    want = np.clip(np.rint(ratio * np.float32(127.0)), -128, 127).astype(np.int8)
+    assert np.array_equal(codes[2], want)
+    assert codes[2, 0] == 127
 
 
 def test_quantize_int8_known_constants():
