@@ -134,7 +134,8 @@ RB_API int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, 
 /*
  * Per-row symmetric int8 quantization of x [B, D] fp32 -> codes [B, D] int8,
  * scales [B] fp32 (retrieve/src/retrieve/indexing/quantize.py:9-18
- * `quantize_int8`, bit for bit).
+ * `quantize_int8` as it evaluates on a CUDA tensor, bit for bit: the scale is
+ * abs_max * fp32(1/127), as in silvertorch/ops/csrc/fork_search_cuda.cu:686).
  */
 RB_API int rb_quantize_int8(const float* x, int B, int D, int8_t* codes, float* scales, void* stream);
 
@@ -321,6 +322,52 @@ RB_API int rb_dense_topk_seeded(const void* queries, const void* items, int B, i
                                 size_t workspace_bytes, void* stream);
 RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,
                           void* stream);
+
+/*
+ * SilverTorch's IVF probe search, replacing the CUDA impl of
+ *   st::search(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes,
+ *              Tensor item_codes, Tensor sort_perm, Tensor global_scale, int k,
+ *              int max_tensor_size_per_row, int divisor_for_int8=-1,
+ *              Tensor? filtering_bit_mask=None, ...) -> (Tensor, Tensor)
+ * (silvertorch/ops/csrc/fork_search.cpp:14-41; fork_search_cuda.cu:1256-1524).
+ *   query [B, D] fp32; probe_ids [B, P] int64 cluster ids; cluster_offsets
+ *   [n_lists + 1] int64; cluster_sizes [n_lists] int64; item_codes [N, D] int8,
+ *   cluster-sorted; sort_perm [N] int64 (sorted position -> item id);
+ *   global_scale: one fp32 on the device; filtering_bit_mask [B, mask_words]
+ *   int64 over sorted positions, high bit first (position d at bit 63 - d % 64
+ *   of word d / 64), or NULL; divisor_for_int8 -1 (rank on the int32 dot) or a
+ *   positive divisor (rank on fp16(dot / divisor)).
+ * Output (ids int64 [B, k], scores fp32 [B, k]): the k best probed positions by
+ * raw score, ties to the reference scorer's lower slot, id = sort_perm[pos],
+ * score = (fp32(dot) * q_scale) * global_scale, or
+ * raw * ((q_scale * divisor) * global_scale); -1 / -inf past the candidates.
+ * Limits: D <= 1024, P <= 2048, B <= 65535, min(k, round_up(width, 32)) <= 224.
+ * The bloom-plan and exact-clause filters of the reference op are not served
+ * here. Workspace from rb_st_search_workspace_size.
+ */
+RB_API int rb_st_search_workspace_size(int B, int D, int P, int k, int max_tensor_size_per_row, size_t* bytes);
+RB_API int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                        const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                        const int8_t* item_codes, int64_t N, const int64_t* sort_perm, const float* global_scale, int k,
+                        int max_tensor_size_per_row, int divisor_for_int8, const int64_t* filtering_bit_mask,
+                        int64_t mask_words, int64_t* out_ids, float* out_scores, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/*
+ * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)
+ *   -> (codes int8 [B, D], scales fp32 [B], cluster_ids int64 [B, P],
+ *       cluster_length int64 [B, P], cluster_offsets int64 [B, P], warps int32 [B * P],
+ *       warp_rounded_length_cumsum int32 [B, P] (per row), remaining_length_cumsum
+ *       int32 [B * P] (global), warp_size_cumsum int32 [B * P] (global))
+ * (silvertorch/ops/csrc/fork_search.cpp:43-49; fork_search_cuda.cu:1529-1546; the
+ * layout the reference checks at retrieve/tests/parity/test_official.py:676-697).
+ */
+RB_API int rb_st_probe_prep(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                            const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                            int8_t* out_codes, float* out_scales, int64_t* out_cluster_ids,
+                            int64_t* out_cluster_length, int64_t* out_cluster_offsets, int32_t* out_warps,
+                            int32_t* out_rounded_cumsum, int32_t* out_remaining_cumsum, int32_t* out_warp_cumsum,
+                            void* stream);
 
 #ifdef __cplusplus
 }

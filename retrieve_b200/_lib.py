@@ -60,6 +60,16 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _c_size, _vp],
     ),
     "rb_merge_pairs": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "rb_st_search_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
+    "rb_st_search": (
+        _c_int,
+        [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int, _c_int, _vp,
+         _c_i64, _vp, _vp, _vp, _c_size, _vp],
+    ),
+    "rb_st_probe_prep": (
+        _c_int,
+        [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    ),
     "rb_bits_to_pm1": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "rb_bits_to_pm1_e4m3": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "rb_dense_topk_scaled": (

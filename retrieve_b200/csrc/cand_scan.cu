@@ -13,6 +13,10 @@
 //    columns, no padding.
 //  * retrieve::oporp_1bit_match_topk_full (twin :17-24): every item, ids are
 //    rows, no sentinel.
+//  * st::search's scorer (kind 2, ivf_search.cu): int8 query codes against int8
+//    item codes, exact int32 dot; raw score fp32(dot), or fp16(dot / divisor) on
+//    the fp16 path (silvertorch/ops/csrc/fused_kmean_ann.cpp:196-200); returns
+//    candidate slots, not ids.
 //
 // Candidate paths: one warp per (query, candidate range) scans 32 candidates
 // per step (lane = candidate) and appends the passing ones to its own list
@@ -45,6 +49,7 @@ struct CandParams {
   uint2* lists;          // [B, n_lists, cap]
   int* list_counts;      // [B, n_lists]
   int n_lists;
+  int divisor;           // kind 2: -1 (int32 raw) or the fp16 path's divisor (> 0)
 };
 
 template <typename T>
@@ -92,6 +97,25 @@ __device__ __forceinline__ float dot_row(const float* __restrict__ sq, const XT*
   return acc;
 }
 
+// Exact int32 dot of the staged int8 query with an int8 item row: 16 codes per
+// 16-byte load and four dp4a when both rows allow it, else one code at a time.
+__device__ __forceinline__ int dot_i8(const int8_t* __restrict__ sq, const int8_t* __restrict__ row, int D) {
+  int acc = 0;
+  if ((D & 15) == 0 && ((reinterpret_cast<uintptr_t>(row) | reinterpret_cast<uintptr_t>(sq)) & 15u) == 0) {
+    for (int d = 0; d < D; d += 16) {
+      const int4 x = *reinterpret_cast<const int4*>(row + d);
+      const int4 q = *reinterpret_cast<const int4*>(sq + d);
+      acc = __dp4a(x.x, q.x, acc);
+      acc = __dp4a(x.y, q.y, acc);
+      acc = __dp4a(x.z, q.z, acc);
+      acc = __dp4a(x.w, q.w, acc);
+    }
+    return acc;
+  }
+  for (int d = 0; d < D; ++d) acc += static_cast<int>(sq[d]) * static_cast<int>(row[d]);
+  return acc;
+}
+
 __device__ __forceinline__ float hamming_score(const uint64_t* __restrict__ sq, const uint64_t* __restrict__ row,
                                                int W) {
   int h = 0;
@@ -99,10 +123,11 @@ __device__ __forceinline__ float hamming_score(const uint64_t* __restrict__ sq, 
   return static_cast<float>(64 * W - 2 * h);
 }
 
-// KIND 0: dot with query type QT and item type XT; KIND 1: hamming (int64 words).
+// KIND 0: dot with query type QT and item type XT; KIND 1: hamming (int64 words);
+// KIND 2: int8 codes (QT = XT = int8_t).
 template <int KIND, typename QT, typename XT>
 __global__ void __launch_bounds__(32 * kCandWarps) cand_scan_kernel(CandParams p) {
-  extern __shared__ uint8_t smem_raw[];
+  extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ uint32_t hist_all[kCandWarps][256];
   const int b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,9 +137,13 @@ __global__ void __launch_bounds__(32 * kCandWarps) cand_scan_kernel(CandParams p
     float* sq = reinterpret_cast<float*>(smem_raw);
     const QT* qrow = static_cast<const QT*>(p.query) + static_cast<size_t>(b) * p.D;
     for (int i = threadIdx.x; i < p.D; i += blockDim.x) sq[i] = to_f(qrow[i]);
-  } else {
+  } else if constexpr (KIND == 1) {
     uint64_t* sq = reinterpret_cast<uint64_t*>(smem_raw);
     const uint64_t* qrow = static_cast<const uint64_t*>(p.query) + static_cast<size_t>(b) * p.D;
+    for (int i = threadIdx.x; i < p.D; i += blockDim.x) sq[i] = qrow[i];
+  } else {
+    int8_t* sq = reinterpret_cast<int8_t*>(smem_raw);
+    const int8_t* qrow = static_cast<const int8_t*>(p.query) + static_cast<size_t>(b) * p.D;
     for (int i = threadIdx.x; i < p.D; i += blockDim.x) sq[i] = qrow[i];
   }
   __syncthreads();
@@ -136,9 +165,14 @@ __global__ void __launch_bounds__(32 * kCandWarps) cand_scan_kernel(CandParams p
       if constexpr (KIND == 0) {
         s = dot_row<XT>(reinterpret_cast<const float*>(smem_raw),
                         static_cast<const XT*>(p.items) + static_cast<size_t>(id) * p.D, p.D);
-      } else {
+      } else if constexpr (KIND == 1) {
         s = hamming_score(reinterpret_cast<const uint64_t*>(smem_raw),
                           static_cast<const uint64_t*>(p.items) + static_cast<size_t>(id) * p.D, p.D);
+      } else {
+        const int dot = dot_i8(reinterpret_cast<const int8_t*>(smem_raw),
+                               static_cast<const int8_t*>(p.items) + static_cast<size_t>(id) * p.D, p.D);
+        s = static_cast<float>(dot);
+        if (p.divisor != -1) s = __half2float(__float2half_rn(__fdiv_rn(s, static_cast<float>(p.divisor))));
       }
     }
     const bool pass = s >= thresh;
@@ -310,6 +344,26 @@ static size_t cand_ws_bytes(int B, int P) {
          align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
 }
 
+size_t cand_i8_ws_bytes(int B, int P) { return cand_ws_bytes(B, P); }
+
+int cand_i8_max_k() { return kCandCap - 32; }
+
+int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const int64_t* pos, int P,
+                 const int64_t* counts, int B, int k, int divisor, int64_t* out_slots, float* out_raw, void* workspace,
+                 cudaStream_t s) {
+  const CandPlan pl = cand_plan(B, P);
+  uint2* lists = static_cast<uint2*>(workspace);
+  int* lcounts = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
+                                        align_up(static_cast<size_t>(B) * pl.n_lists * kCandCap * sizeof(uint2), 256));
+  CandParams prm{q_codes, items, pos, counts, B, P, D, N, k, lists, lcounts, pl.n_lists, divisor};
+  const dim3 grid(pl.ctas_per_query, B);
+  const size_t smem = align_up(static_cast<size_t>(D), 16);
+  cand_scan_kernel<2, int8_t, int8_t><<<grid, 32 * kCandWarps, smem, s>>>(prm);
+  const int rc = check_launch();
+  if (rc != RB_OK) return rc;
+  return merge_lists(lists, lcounts, B, pl.n_lists, kCandCap, k, 0, out_slots, out_raw, nullptr, s);
+}
+
 // Hamming full-scan plan
 struct HamPlan {
   int n_qg, n_splits, cap;
@@ -381,7 +435,7 @@ int rb_candidate_topk(int kind, const void* query, int query_dtype, const void* 
   uint2* lists = static_cast<uint2*>(workspace);
   int* lcounts = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
                                         align_up(static_cast<size_t>(B) * pl.n_lists * kCandCap * sizeof(uint2), 256));
-  CandParams prm{query, items, positive_indices, counts, B, P, D, N, k_sel, lists, lcounts, pl.n_lists};
+  CandParams prm{query, items, positive_indices, counts, B, P, D, N, k_sel, lists, lcounts, pl.n_lists, 0};
   const dim3 grid(pl.ctas_per_query, B);
   const size_t smem = (kind == 0) ? static_cast<size_t>(D) * sizeof(float) : static_cast<size_t>(D) * 8;
   if (kind == 1)

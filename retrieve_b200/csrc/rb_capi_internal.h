@@ -53,6 +53,17 @@ int merge_pair_stack(const uint2* pairs, int W, int B, int kin, int k, int64_t* 
 
 void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stream);
 
+// The int8 candidate scan (cand_scan.cu, kind 2): per query b, the exact top-k
+// over the slots [0, counts[b]) of pos[b, :P] (positions into the int8 item
+// table; a negative position is never scored), ranked on the raw score
+// fp32(dot) (divisor -1) or fp16(dot / divisor), ties to the lower slot.
+// Writes the winners' slots and raw scores, -1 / -inf past the candidates.
+size_t cand_i8_ws_bytes(int B, int P);
+int cand_i8_max_k();
+int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const int64_t* pos, int P,
+                 const int64_t* counts, int B, int k, int divisor, int64_t* out_slots, float* out_raw, void* workspace,
+                 cudaStream_t s);
+
 void fill_empty_pairs(uint2* out, size_t n, cudaStream_t stream);
 
 int merge_shard_lists(const int64_t* ids, const float* scores, int W, int B, int kin, int k, int64_t* out_ids,

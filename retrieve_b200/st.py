@@ -1,0 +1,200 @@
+"""``torch.ops.st.search`` and ``torch.ops.st.probe_prep`` on ``libretrieve_b200.so``.
+
+SilverTorch's one-op IVF forward (silvertorch/ops/csrc/fork_search.cpp:13-49,
+fork_search_cuda.cu:1256-1546), reached by the reference through
+``adapter.fork_search`` (retrieve/src/retrieve/ops/official/adapter.py:495-544).
+Importing this module registers CUDA implementations of both ops under the
+reference's exact schemas: it defines the schemas when no other library has
+(``torch.ops.st`` absent), and otherwise adds the CUDA kernels to the
+definitions already loaded (the reference's CPU build of the other ``st::``
+ops keeps serving them).
+
+Semantics: int8 query prep as ``quantize_int8`` on a CUDA tensor, the probed
+clusters' positions in the reference scorer's slot order, exact int32 dots,
+top-k on the raw score with ties to the lower slot, ``id = sort_perm[pos]`` and
+``score = (fp32(dot) * q_scale) * global_scale`` (or the fp16 path's
+``raw * ((q_scale * divisor) * global_scale)``), ``-1`` / ``-inf`` pads. A
+full-``N`` ``filtering_bit_mask`` (high bit first) is honoured; the bloom-plan
+and exact-clause filters are not served and raise ``NotImplementedError``.
+Errors raise ``RuntimeError``, as the reference's ``TORCH_CHECK``s do.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import Tensor
+
+from retrieve_b200 import _lib
+
+SEARCH_SCHEMA = (
+    "search(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes, "
+    "Tensor item_codes, Tensor sort_perm, Tensor global_scale, int k, int max_tensor_size_per_row, "
+    "int divisor_for_int8=-1, Tensor? filtering_bit_mask=None, Tensor? bloom_index=None, "
+    "Tensor? bloom_bundle_b_offsets=None, Tensor? plans=None, int plan_count=0, int max_stack_size=0, "
+    "Tensor? query_plan_index=None, int bloom_k=0, int hash_k=0, Tensor? item_clause_attrs=None, "
+    "Tensor? clause_slots=None, Tensor? clause_is_reverse=None, Tensor? query_clause_attrs=None) "
+    "-> (Tensor, Tensor)"
+)
+PROBE_PREP_SCHEMA = (
+    "probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes) "
+    "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)"
+)
+
+
+def _ptr(t: Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _call(rc: int, what: str) -> None:
+    if rc != _lib.RB_OK:
+        msg = _lib.lib().rb_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what}: {msg} (status {rc})")
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _layout_args(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor):
+    _check(query.dim() == 2, "query must be [B, D]")
+    _check(probe_ids.dim() == 2 and probe_ids.shape[0] == query.shape[0], "probe_ids must be [B, n_probe]")
+    _check(cluster_offsets.dim() == 1 and cluster_sizes.dim() == 1, "cluster_offsets / cluster_sizes must be 1-D")
+    for name, t in (("query", query), ("probe_ids", probe_ids), ("cluster_offsets", cluster_offsets),
+                    ("cluster_sizes", cluster_sizes)):
+        _check(t.is_cuda, f"st ops run on CUDA tensors only ({name} is on {t.device})")
+    q = query.to(torch.float32).contiguous()
+    probe = probe_ids.to(torch.int64).contiguous()
+    offsets = cluster_offsets.to(torch.int64).contiguous()
+    sizes = cluster_sizes.to(torch.int64).contiguous()
+    return q, probe, offsets, sizes
+
+
+def search(
+    query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor, item_codes: Tensor,
+    sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int = -1,
+    filtering_bit_mask: Tensor | None = None, bloom_index: Tensor | None = None,
+    bloom_bundle_b_offsets: Tensor | None = None, plans: Tensor | None = None, plan_count: int = 0,
+    max_stack_size: int = 0, query_plan_index: Tensor | None = None, bloom_k: int = 0, hash_k: int = 0,
+    item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
+    clause_is_reverse: Tensor | None = None, query_clause_attrs: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:
+    """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``."""
+    if plans is not None or bloom_index is not None or query_clause_attrs is not None:
+        raise NotImplementedError("st::search: the bloom-plan and exact-clause filters are not implemented here; "
+                                  "pass a full-N filtering_bit_mask")
+    _check(item_codes.dtype == torch.int8 and item_codes.dim() == 2 and item_codes.shape[1] == query.shape[1],
+           "item_codes must be int8 [N, D] with the query's D")
+    _check(item_codes.is_contiguous(), "item_codes must be contiguous")
+    q, probe, offsets, sizes = _layout_args(query, probe_ids, cluster_offsets, cluster_sizes)
+    _check(item_codes.device == q.device, "item_codes must be on the query's device")
+    _check(offsets.numel() == sizes.numel() + 1, "cluster_offsets must have n_lists + 1 entries")
+    _check(sort_perm.dim() == 1 and sort_perm.numel() == item_codes.shape[0], "sort_perm must be [N]")
+    dev = q.device
+    perm = sort_perm.to(device=dev, dtype=torch.int64).contiguous()
+    gs = global_scale.to(device=dev, dtype=torch.float32).reshape(-1)[:1].contiguous()
+    _check(gs.numel() == 1, "global_scale must hold one value")
+    mask = None
+    mask_words = 0
+    if filtering_bit_mask is not None:
+        _check(filtering_bit_mask.dim() == 2 and filtering_bit_mask.shape[0] == q.shape[0],
+               "filtering_bit_mask must be [B, words]")
+        mask = filtering_bit_mask.to(device=dev, dtype=torch.int64).contiguous()
+        mask_words = mask.shape[1]
+    b, d = q.shape
+    p = probe.shape[1]
+    _check(k >= 1, f"k must be positive, got {k}")
+    ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return ids, scores
+    lib = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _call(lib.rb_st_search_workspace_size(b, d, p, k, int(max_tensor_size_per_row), ctypes.byref(nbytes)),
+          "st::search")
+    ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
+    rc = lib.rb_st_search(
+        _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), _ptr(item_codes),
+        item_codes.shape[0], _ptr(perm), _ptr(gs), k, int(max_tensor_size_per_row), int(divisor_for_int8),
+        _ptr(mask), mask_words, _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream(dev),
+    )
+    _call(rc, "st::search")
+    return ids, scores
+
+
+def probe_prep(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor):
+    """``st::probe_prep`` → its nine layout tensors (fork_search.cpp:43-49)."""
+    q, probe, offsets, sizes = _layout_args(query, probe_ids, cluster_offsets, cluster_sizes)
+    b, d = q.shape
+    p = probe.shape[1]
+    dev = q.device
+    codes = torch.empty((b, d), dtype=torch.int8, device=dev)
+    scales = torch.empty((b,), dtype=torch.float32, device=dev)
+    cids = torch.empty((b, p), dtype=torch.int64, device=dev)
+    length = torch.empty((b, p), dtype=torch.int64, device=dev)
+    offs = torch.empty((b, p), dtype=torch.int64, device=dev)
+    warps = torch.empty((b * p,), dtype=torch.int32, device=dev)
+    rounded = torch.empty((b, p), dtype=torch.int32, device=dev)
+    rem = torch.empty((b * p,), dtype=torch.int32, device=dev)
+    wcum = torch.empty((b * p,), dtype=torch.int32, device=dev)
+    if b > 0:
+        rc = _lib.lib().rb_st_probe_prep(
+            _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), _ptr(codes), _ptr(scales),
+            _ptr(cids), _ptr(length), _ptr(offs), _ptr(warps), _ptr(rounded), _ptr(rem), _ptr(wcum), _stream(dev),
+        )
+        _call(rc, "st::probe_prep")
+    return codes, scales, cids, length, offs, warps, rounded, rem, wcum
+
+
+def _fake_search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm, global_scale, k,
+                 max_tensor_size_per_row, *args, **kwargs):
+    b = query.shape[0]
+    return query.new_empty((b, k), dtype=torch.int64), query.new_empty((b, k), dtype=torch.float32)
+
+
+def _fake_probe_prep(query, probe_ids, cluster_offsets, cluster_sizes):
+    rows, n_probe = probe_ids.shape
+    i64 = probe_ids.new_empty((rows, n_probe), dtype=torch.int64)
+    return (
+        query.new_empty(query.shape, dtype=torch.int8),
+        query.new_empty((rows,), dtype=torch.float32),
+        i64,
+        torch.empty_like(i64),
+        torch.empty_like(i64),
+        probe_ids.new_empty((rows * n_probe,), dtype=torch.int32),
+        probe_ids.new_empty((rows, n_probe), dtype=torch.int32),
+        probe_ids.new_empty((rows * n_probe,), dtype=torch.int32),
+        probe_ids.new_empty((rows * n_probe,), dtype=torch.int32),
+    )
+
+
+_lib.lib()  # no fallback: a missing library fails the import
+_LIBRARY = torch.library.Library("st", "FRAGMENT")
+
+
+def _defined(name: str) -> bool:
+    try:
+        torch._C._dispatch_find_schema_or_throw(f"st::{name}", "")
+        return True
+    except RuntimeError:
+        return False
+
+
+def _register() -> None:
+    for name, schema, impl, fake in (("search", SEARCH_SCHEMA, search, _fake_search),
+                                     ("probe_prep", PROBE_PREP_SCHEMA, probe_prep, _fake_probe_prep)):
+        ours = not _defined(name)
+        if ours:
+            _LIBRARY.define(schema)
+        _LIBRARY.impl(name, impl, "CUDA")
+        if ours:
+            torch.library.register_fake(f"st::{name}", fake, lib=_LIBRARY)
+
+
+_register()

@@ -1,0 +1,236 @@
+"""``st::search`` / ``st::probe_prep`` (retrieve_b200/st.py over rb_st_search /
+rb_st_probe_prep) against the CPU restatement (oracle/ivf.py) and the fixture
+the reference's own code produced (tests/golden/golden_ivf.npz).
+
+CPU tests: the registered schemas equal the reference's pinned strings
+(retrieve/tests/parity/test_official.py:65-116), the fake implementations give
+the right shapes, and the C-ABI rejects bad arguments without a device. GPU
+tests: bit-exact scores and ids against the oracle (whose ties follow the
+reference scorer's slot order) and, up to ties, against the reference's fixture.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ivf, knn
+from retrieve_b200 import _lib
+from tests.helpers import assert_topk_equal_up_to_ties
+
+GOLDEN = np.load(Path(__file__).resolve().parent / "golden" / "golden_ivf.npz")
+N_CASES = len({k.split("_")[0] for k in GOLDEN.files})
+
+PINNED_SEARCH = (
+    "st::search(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes, "
+    "Tensor item_codes, Tensor sort_perm, Tensor global_scale, int k, "
+    "int max_tensor_size_per_row, int divisor_for_int8=-1, Tensor? filtering_bit_mask=None, "
+    "Tensor? bloom_index=None, Tensor? bloom_bundle_b_offsets=None, Tensor? plans=None, "
+    "int plan_count=0, int max_stack_size=0, Tensor? query_plan_index=None, int bloom_k=0, "
+    "int hash_k=0, Tensor? item_clause_attrs=None, Tensor? clause_slots=None, "
+    "Tensor? clause_is_reverse=None, Tensor? query_clause_attrs=None) -> (Tensor, Tensor)"
+)
+PINNED_PROBE_PREP = (
+    "st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes) "
+    "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)"
+)
+
+
+def _st():
+    import retrieve_b200.st  # noqa: F401  (registers the ops)
+
+    return torch.ops.st
+
+
+def _case(ci):
+    p = f"c{ci}_"
+    g = {k[len(p):]: GOLDEN[k] for k in GOLDEN.files if k.startswith(p)}
+    n_lists, max_size, n_probe, d, k, b, width, div, ties = g["shape"].tolist()
+    return g, dict(k=k, width=width, div=div, d=d, b=b)
+
+
+# --- CPU -----------------------------------------------------------------------------------
+
+
+def test_schemas_are_the_reference_ones():
+    st = _st()
+    assert str(st.search.default._schema) == PINNED_SEARCH
+    assert str(st.probe_prep.default._schema) == PINNED_PROBE_PREP
+
+
+def test_fake_shapes():
+    st = _st()
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        q = torch.empty(4, 64)
+        probe = torch.empty(4, 3, dtype=torch.int64)
+        offsets = torch.empty(9, dtype=torch.int64)
+        sizes = torch.empty(8, dtype=torch.int64)
+        out = st.probe_prep(q, probe, offsets, sizes)
+        assert [tuple(o.shape) for o in out] == [(4, 64), (4,), (4, 3), (4, 3), (4, 3), (12,), (4, 3), (12,), (12,)]
+        assert [o.dtype for o in out[5:]] == [torch.int32] * 4
+        ids, scores = st.search(q, probe, offsets, sizes, torch.empty(100, 64, dtype=torch.int8),
+                                torch.empty(100, dtype=torch.int64), torch.empty(()), 7, 90)
+        assert ids.shape == scores.shape == (4, 7) and ids.dtype == torch.int64
+
+
+def test_cpu_tensors_raise():
+    st = _st()
+    with pytest.raises(RuntimeError):
+        st.search(torch.zeros(2, 64), torch.zeros(2, 1, dtype=torch.int64), torch.tensor([0, 4]),
+                  torch.tensor([4]), torch.zeros(4, 64, dtype=torch.int8), torch.arange(4), torch.tensor(1.0), 2, 4)
+
+
+def test_capi_argument_checks_need_no_device():
+    lib = _lib.lib()
+    n = ctypes.c_size_t(0)
+    assert lib.rb_st_search_workspace_size(16, 128, 8, 32, 700, ctypes.byref(n)) == 0
+    # codes + scales + positions [16, 704] int64 + counts + winners, at least
+    assert n.value >= 16 * 704 * 8
+    assert lib.rb_st_search_workspace_size(16, 128, 8, 0, 700, ctypes.byref(n)) == _lib.RB_ERR_INVALID_ARG
+
+    def call(b=4, d=128, p=8, k=10, width=256, div=-1, ws=None, ws_bytes=0):
+        return lib.rb_st_search(None, b, d, None, p, None, None, 16, None, 1000, None, None, k, width, div, None, 0,
+                                None, None, ws, ws_bytes, None)
+
+    assert call(d=2048) == _lib.RB_ERR_UNSUPPORTED  # D > 1024
+    assert call(p=4096) == _lib.RB_ERR_UNSUPPORTED  # more than 2048 probes
+    assert call(k=300) == _lib.RB_ERR_UNSUPPORTED  # min(k, width) > 224
+    assert call(k=300, width=200) == _lib.RB_ERR_WORKSPACE  # min(300, 224) fits; then the workspace check
+    assert call(div=0) == _lib.RB_ERR_INVALID_ARG
+    assert call(b=-1) == _lib.RB_ERR_INVALID_ARG
+    assert call(b=70000) == _lib.RB_ERR_UNSUPPORTED
+    assert call() == _lib.RB_ERR_WORKSPACE
+    assert b"workspace" in lib.rb_last_error()
+    assert call(b=0) == _lib.RB_OK  # nothing to do: no device touched
+
+
+# --- GPU -----------------------------------------------------------------------------------
+
+
+def _run(st, g, meta, **kw):
+    dev = "cuda"
+    t = {k: torch.from_numpy(np.ascontiguousarray(g[k])).to(dev)
+         for k in ("query", "probe", "offsets", "sizes", "codes", "sort_perm")}
+    gs = torch.from_numpy(g["gs"]).to(dev)
+    ids, scores = st.search(t["query"], t["probe"], t["offsets"], t["sizes"], t["codes"], t["sort_perm"], gs,
+                            meta["k"], meta["width"], **kw)
+    return ids.cpu().numpy(), scores.cpu().numpy()
+
+
+def _assert_exact(ids, scores, ref_ids, ref_scores):
+    assert np.array_equal(scores, ref_scores), f"{int((scores != ref_scores).sum())} score slots differ"
+    assert np.array_equal(ids, ref_ids), f"{int((ids != ref_ids).sum())} id slots differ"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_search_int32_path(ci):
+    st = _st()
+    g, meta = _case(ci)
+    ids, scores = _run(st, g, meta)
+    want = ivf.search(g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"], g["gs"],
+                      meta["k"], meta["width"])
+    _assert_exact(ids, scores, *want)
+    assert_topk_equal_up_to_ties(ids, scores, g["ids32"], g["sc32"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_search_fp16_path(ci):
+    st = _st()
+    g, meta = _case(ci)
+    ids, scores = _run(st, g, meta, divisor_for_int8=meta["div"])
+    want = ivf.search(g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"], g["gs"],
+                      meta["k"], meta["width"], divisor_for_int8=meta["div"])
+    _assert_exact(ids, scores, *want)
+    assert_topk_equal_up_to_ties(ids, scores, g["ids16"], g["sc16"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_search_filter_mask(ci):
+    st = _st()
+    g, meta = _case(ci)
+    words = ivf.pack_mask_high_first(g["mask"])
+    ids, scores = _run(st, g, meta, filtering_bit_mask=torch.from_numpy(words).cuda())
+    want = ivf.search(g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"], g["gs"],
+                      meta["k"], meta["width"], filtering_bit_mask=words)
+    _assert_exact(ids, scores, *want)
+    assert_topk_equal_up_to_ties(ids, scores, g["idsm"], g["scm"])
+
+
+def _layout(rng, n_lists, max_size, d, b, p):
+    sizes = rng.integers(0, max_size + 1, n_lists).astype(np.int64)
+    offsets = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    n = int(offsets[-1])
+    codes = rng.integers(-128, 128, (n, d)).astype(np.int8)
+    perm = rng.permutation(n).astype(np.int64)
+    probe = np.argsort(rng.random((b, n_lists)), axis=1)[:, :p].astype(np.int64)
+    q = rng.standard_normal((b, d)).astype(np.float32)
+    width = int(sizes[probe].sum(1).max())
+    return q, probe, offsets, sizes, codes, perm, width
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k", [1, 100, 224])
+def test_search_wide_rows_and_edge_shapes(k):
+    """Wide rows (many warps of candidates per list), D not a multiple of 16 (scalar
+    dot), empty clusters, k above the probed count (pads), and ties from repeated
+    code rows."""
+    st = _st()
+    rng = np.random.default_rng(k)
+    for d, n_lists, max_size, b, p in ((128, 64, 600, 8, 32), (100, 32, 90, 5, 8), (64, 16, 40, 3, 2)):
+        q, probe, offsets, sizes, codes, perm, width = _layout(rng, n_lists, max_size, d, b, p)
+        codes[1::3] = codes[0]  # many equal dots
+        gs = np.float32(0.0123)
+        t = [torch.from_numpy(x).cuda() for x in (q, probe, offsets, sizes, codes, perm)]
+        ids, scores = st.search(*t, torch.tensor(gs).cuda(), k, width)
+        want = ivf.search(q, probe, offsets, sizes, codes, perm, gs, k, width)
+        _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), *want)
+
+
+@pytest.mark.gpu
+def test_search_zero_probes_and_zero_width():
+    st = _st()
+    q = torch.randn(3, 64, device="cuda")
+    offsets = torch.tensor([0, 10], device="cuda")
+    sizes = torch.tensor([10], device="cuda")
+    codes = torch.ones(10, 64, dtype=torch.int8, device="cuda")
+    perm = torch.arange(10, device="cuda")
+    gs = torch.tensor(1.0, device="cuda")
+    for probe, width in ((torch.zeros(3, 0, dtype=torch.int64, device="cuda"), 10),
+                         (torch.zeros(3, 1, dtype=torch.int64, device="cuda"), 0)):
+        ids, scores = st.search(q, probe, offsets, sizes, codes, perm, gs, 5, width)
+        assert (ids == -1).all() and torch.isneginf(scores).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("d", [128, 192, 768])
+def test_probe_prep_matches_oracle(d):
+    """The layout the reference checks (retrieve/tests/parity/test_official.py:676-697),
+    with its edge rows (zeros, a tiny value, exact half-code quotients)."""
+    st = _st()
+    rng = np.random.default_rng(9)
+    q = rng.standard_normal((2000, d)).astype(np.float32)
+    q[0] = 0.0
+    q[1] = 0.0
+    q[1, 3] = 1e-30
+    q[2] = (np.arange(d) % 3 - 1.0).astype(np.float32)
+    q[2, 0] = 2.54
+    q[2, 1:5] = [0.01, -0.01, 1.27, -1.27]
+    sizes = rng.integers(0, 150, 300).astype(np.int64)
+    offsets = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    probe = np.argsort(rng.random((2000, 300)), axis=1)[:, :24].astype(np.int64)
+    out = st.probe_prep(*(torch.from_numpy(x).cuda() for x in (q, probe, offsets, sizes)))
+    want = ivf.probe_prep(q, probe, offsets, sizes)
+    for got, ref in zip(out, want, strict=True):
+        got = got.cpu().numpy()
+        assert got.shape == np.shape(ref) and np.array_equal(got, ref)
+    codes, scales = knn.quantize_int8(q)
+    assert np.array_equal(out[1].cpu().numpy(), scales)
