@@ -86,6 +86,30 @@ def test_cpu_tensors_raise():
                   torch.tensor([4]), torch.zeros(4, 64, dtype=torch.int8), torch.arange(4), torch.tensor(1.0), 2, 4)
 
 
+REF_CPU_LIB = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "silvertorch_ref_cpu.so"
+
+
+@pytest.mark.skipif(not REF_CPU_LIB.exists(), reason="the reference's CPU st ops are not built here")
+def test_registers_beside_the_reference_cpu_ops():
+    """The drop-in layout: the reference's CPU build defines the st:: schemas and
+    its CPU ops; importing retrieve_b200.st then adds CUDA kernels for search and
+    probe_prep only. Run in a child process (one registry per process)."""
+    import subprocess
+    import sys
+
+    code = (
+        "import torch\n"
+        f"torch.ops.load_library({str(REF_CPU_LIB)!r})\n"
+        "import retrieve_b200.st\n"
+        "has = torch._C._dispatch_has_kernel_for_dispatch_key\n"
+        "assert has('st::search', 'CUDA') and has('st::probe_prep', 'CUDA')\n"
+        "assert has('st::fused_kmean_ann', 'CPU')\n"
+    )
+    root = Path(__file__).resolve().parent.parent
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+
+
 def test_capi_argument_checks_need_no_device():
     lib = _lib.lib()
     n = ctypes.c_size_t(0)
