@@ -139,6 +139,28 @@ RB_API int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, 
  */
 RB_API int rb_quantize_int8(const float* x, int B, int D, int8_t* codes, float* scales, void* stream);
 
+/*
+ * Per-tensor symmetric int8 quantization of x [N, D] fp32
+ * (retrieve/src/retrieve/indexing/quantize.py:34-52 `quantize_int8_global` on CUDA
+ * tensors): abs_max = max(max |x|, 1e-8) over the table (NaN propagates);
+ * codes[i] = clamp(round_half_even(fp32(x[r] / abs_max) * 127), -128, 127) for
+ * r = rows[i] (or r = i when rows is NULL; then n_rows is ignored and N rows are
+ * written); a row index outside [0, N) writes zeros; *scale (device) =
+ * abs_max * fp32(1/127). Workspace from rb_quantize_int8_global_workspace_size.
+ */
+RB_API int rb_quantize_int8_global_workspace_size(size_t* bytes);
+RB_API int rb_quantize_int8_global(const float* x, int64_t N, int D, const int64_t* rows, int64_t n_rows,
+                                   int8_t* codes, float* scale, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
+/*
+ * Sign packing of values [M, D] fp32, D a multiple of 64, into words [M, D / 64]
+ * int64: bit b of word w is set iff values[m, 64 w + b] > 0
+ * (retrieve/src/retrieve/indexing/quantize.py:63-72 `_pack_signs_to_int64`, the last
+ * step of the SimHash and Sign-OPORP projections).
+ */
+RB_API int rb_pack_signs(const float* values, int64_t M, int D, int64_t* out_words, void* stream);
+
 /* Number of kernel launches one rb_dense_topk call with these sizes makes. */
 RB_API int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launches);
 

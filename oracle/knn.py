@@ -8,8 +8,9 @@
   — ``64*W - 2*popcount(q ^ x)``; the indirect form returns ``min(k, P)``
   columns.
 * ``gemv_scores``: ops/triton/gemv_scores.py:19-28 via the C restatement.
-* ``quantize_int8``: indexing/quantize.py:9-18, with the scale as torch
-  evaluates it on a CUDA tensor (a multiply by fp32(1/127)).
+* ``quantize_int8`` / ``quantize_int8_global``: indexing/quantize.py:9-18,
+  34-52, with the scale as torch evaluates it on a CUDA tensor (a multiply by
+  fp32(1/127)).
 """
 
 from __future__ import annotations
@@ -125,9 +126,35 @@ def quantize_int8(x, device_scale: bool = True):
         scales = (abs_max * (np.float32(1.0) / np.float32(127.0))).astype(np.float32)[:, 0]
     else:
         scales = (abs_max / np.float32(127.0)).astype(np.float32)[:, 0]
-    ratio = (x.astype(np.float64) / abs_max.astype(np.float64)).astype(np.float32)
-    codes = np.clip(np.rint(ratio * np.float32(127.0)), -128, 127).astype(np.int8)
+    with np.errstate(invalid="ignore"):
+        ratio = (x.astype(np.float64) / abs_max.astype(np.float64)).astype(np.float32)
+        codes = _to_int8(np.clip(np.rint(ratio * np.float32(127.0)), -128, 127))
     return codes, scales
+
+
+def _to_int8(v):
+    """fp32 codes to int8, NaN to 0 (torch's conversion of a NaN to an integer)."""
+    return np.where(np.isnan(v), 0, v).astype(np.int8)
+
+
+def quantize_int8_global(x, rows=None, device_scale: bool = True):
+    """indexing/quantize.py:34-52: one scale for the whole table.
+    ``abs_max = max(max |x|, 1e-8)`` (NaN propagates), codes
+    ``clamp(round_half_even(fp32(x / abs_max) * 127), -128, 127)`` for the rows
+    ``rows`` (all rows when None), scale ``abs_max * fp32(1/127)`` as on a CUDA
+    tensor (``device_scale=False``: the CPU division ``abs_max / 127``). Returns
+    ``(codes [n, D] int8, scale float)``."""
+    x = np.asarray(x, dtype=np.float32)
+    am = np.float32(np.abs(x).max()) if x.size else np.float32(0.0)
+    am = np.maximum(am, np.float32(1e-8))
+    src = x if rows is None else x[np.asarray(rows, dtype=np.int64)]
+    with np.errstate(invalid="ignore", divide="ignore"):
+        codes = _to_int8(np.clip(np.rint((src / am).astype(np.float32) * np.float32(127.0)), -128, 127))
+    if device_scale:
+        scale = np.float32(am * (np.float32(1.0) / np.float32(127.0)))
+    else:
+        scale = np.float32(am / np.float32(127.0))
+    return codes, float(scale)
 
 
 def int8_topk(query, item_codes, item_scales, k, *, chunk=1 << 18):

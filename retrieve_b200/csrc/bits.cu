@@ -46,6 +46,21 @@ __global__ void bits_to_pm1_kernel(const uint64_t* __restrict__ bits, int64_t n_
   }
 }
 
+// Sign packing, the last step of the reference's 1-bit projections
+// (retrieve/src/retrieve/indexing/quantize.py:63-72 `_pack_signs_to_int64`): bit b
+// of word w is set iff values[64 w + b] > 0 (NaN and -0.0 give 0). One warp per
+// word: two coalesced 128-byte loads and two ballots, lane 0 stores the word.
+__global__ void pack_signs_kernel(const float* __restrict__ values, int64_t n_words, uint64_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); w < n_words; w += warps) {
+    const float* v = values + w * 64;
+    const uint32_t lo = __ballot_sync(0xffffffffu, v[lane] > 0.f);
+    const uint32_t hi = __ballot_sync(0xffffffffu, v[32 + lane] > 0.f);
+    if (lane == 0) out[w] = static_cast<uint64_t>(lo) | (static_cast<uint64_t>(hi) << 32);
+  }
+}
+
 }  // namespace rb
 
 using namespace rb;
@@ -85,6 +100,29 @@ int rb_bits_to_pm1(const int64_t* bits, int N, int W, int8_t* out, void* stream)
 
 int rb_bits_to_pm1_e4m3(const int64_t* bits, int N, int W, uint8_t* out, void* stream) {
   return bits_launch(true, bits, N, W, out, stream);
+}
+
+int rb_pack_signs(const float* values, int64_t M, int D, int64_t* out_words, void* stream) {
+  if (M < 0 || D <= 0 || D % 64 != 0) {
+    set_last_error("pack_signs: values must be [M, D] with D a positive multiple of 64");
+    return RB_ERR_INVALID_ARG;
+  }
+  const int64_t n_words = M * (D / 64);
+  if (n_words == 0) return RB_OK;
+  if (values == nullptr || out_words == nullptr) {
+    set_last_error("pack_signs: null pointer");
+    return RB_ERR_INVALID_ARG;
+  }
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((n_words + threads / 32 - 1) / (threads / 32), 148 * 16);
+  pack_signs_kernel<<<static_cast<int>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      values, n_words, reinterpret_cast<uint64_t*>(out_words));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error(cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
 }
 
 }  // extern "C"

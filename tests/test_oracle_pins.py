@@ -163,3 +163,53 @@ def test_int8_raw_dots_match_reference_fused_kmean_ann(d):
     ids, scores = knn.silvertorch_fullprobe_codes(GOLDEN_INT8[f"queries_{d}"], GOLDEN_INT8[f"items_{d}"], 1.0, 1.0, 50)
     top = np.sort(GOLDEN_INT8[f"dots_{d}"], axis=1)[:, ::-1][:, :50].astype(np.float32)
     assert np.array_equal(scores, top)
+
+
+QUANT = np.load(Path(__file__).resolve().parent / "golden" / "golden_quant.npz")
+
+
+def _ulp_gap(a, b):
+    return int(np.abs(np.float32(a).view(np.int32).astype(np.int64) - np.float32(b).view(np.int32).astype(np.int64)))
+
+
+def test_quantize_int8_global_matches_reference():
+    """tests/golden/make_golden_quant.py ran the reference's quantize_int8_global on CPU
+    tensors (scale = abs_max / 127); the device form multiplies by fp32(1/127)."""
+    for rows, codes_key, scale_key in ((None, "global_codes", "global_scale"),
+                                       (QUANT["global_perm"], "global_codes_perm", "global_scale_perm")):
+        codes, cpu_scale = knn.quantize_int8_global(QUANT["global_x"], rows=rows, device_scale=False)
+        assert np.array_equal(codes, QUANT[codes_key])
+        assert np.float32(cpu_scale) == QUANT[scale_key]
+        dev_codes, dev_scale = knn.quantize_int8_global(QUANT["global_x"], rows=rows)
+        assert np.array_equal(dev_codes, codes) and _ulp_gap(dev_scale, cpu_scale) <= 1
+    codes, scale = knn.quantize_int8_global(QUANT["global_nan_x"], device_scale=False)
+    assert np.array_equal(codes, QUANT["global_nan_codes"]) and np.isnan(scale) and np.isnan(QUANT["global_nan_scale"])
+
+
+def test_quantize_int8_nan_and_inf_rows_match_reference():
+    codes, scales = knn.quantize_int8(QUANT["q8_special_x"], device_scale=False)
+    assert np.array_equal(codes, QUANT["q8_special_codes"])
+    assert np.array_equal(scales, QUANT["q8_special_scales"], equal_nan=True)
+    assert np.isnan(scales[1]) and (codes[1] == 0).all() and np.isinf(scales[2])
+
+
+def test_sign_packing_matches_reference_edge_values():
+    """Zeros, negative zeros, NaN (all 0 bits) and the smallest subnormals (signed)."""
+    assert np.array_equal(bits.pack_signs(QUANT["pack_values"]), QUANT["pack_words"])
+
+
+def test_simhash_and_oporp_packing_match_reference():
+    """The reference's own projections (recomputed with torch on CPU, the same calls) packed
+    by the oracle equal the reference's codes; pins the bit order of both 1-bit builds."""
+    import torch
+
+    embs = torch.from_numpy(QUANT["sim_embs"])
+    query = torch.from_numpy(QUANT["sim_query"])
+    r = torch.from_numpy(QUANT["sim_r"])
+    assert np.array_equal(bits.pack_signs((embs @ r.t()).numpy()), QUANT["sim_bits"])
+    assert np.array_equal(bits.pack_signs((query @ r.t()).numpy()), QUANT["sim_qbits"])
+    signs = torch.from_numpy(QUANT["oporp_signs"]).to(torch.float32)
+    perm = torch.from_numpy(QUANT["oporp_perm"])
+    for x, want in ((embs, QUANT["oporp_bits"]), (query, QUANT["oporp_qbits"])):
+        proj = (x * signs).index_select(1, perm)  # k_bits = D: one coordinate a bin
+        assert np.array_equal(bits.pack_signs(proj.numpy()), want)
