@@ -359,21 +359,30 @@ RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, i
  *   int64 over sorted positions, high bit first (position d at bit 63 - d % 64
  *   of word d / 64), or NULL; divisor_for_int8 -1 (rank on the int32 dot) or a
  *   positive divisor (rank on fp16(dot / divisor)).
+ *   Exact clause filter (silvertorch/ops/csrc/fork_filters.cuh:15-41), or NULLs:
+ *   item_clause_attrs int32 [attr_rows, attr_docs >= N] (clause c in rows
+ *   clause_slots[c] .. clause_slots[c + 1], each doc's values sorted descending,
+ *   -1 pads), clause_slots int64 [n_clauses + 1], clause_is_reverse bool
+ *   [n_clauses], query_clause_attrs int32 [B, n_clauses] (-1: clause inactive).
+ *   The mask and the exact filter exclude each other.
  * Output (ids int64 [B, k], scores fp32 [B, k]): the k best probed positions by
  * raw score, ties to the reference scorer's lower slot, id = sort_perm[pos],
  * score = (fp32(dot) * q_scale) * global_scale, or
  * raw * ((q_scale * divisor) * global_scale); -1 / -inf past the candidates.
  * Limits: D <= 1024, P <= 2048, B <= 65535, min(k, round_up(width, 32)) <= 224.
- * The bloom-plan and exact-clause filters of the reference op are not served
- * here. Workspace from rb_st_search_workspace_size.
+ * The reference op's bloom-plan filter is not served here (with the exact
+ * recheck the exact filter alone gives its result). Workspace from
+ * rb_st_search_workspace_size.
  */
 RB_API int rb_st_search_workspace_size(int B, int D, int P, int k, int max_tensor_size_per_row, size_t* bytes);
 RB_API int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P,
                         const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
                         const int8_t* item_codes, int64_t N, const int64_t* sort_perm, const float* global_scale, int k,
                         int max_tensor_size_per_row, int divisor_for_int8, const int64_t* filtering_bit_mask,
-                        int64_t mask_words, int64_t* out_ids, float* out_scores, void* workspace,
-                        size_t workspace_bytes, void* stream);
+                        int64_t mask_words, const int32_t* item_clause_attrs, int64_t attr_rows,
+                        int64_t attr_docs, const int64_t* clause_slots, const uint8_t* clause_is_reverse,
+                        const int32_t* query_clause_attrs, int n_clauses, int64_t* out_ids, float* out_scores,
+                        void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)

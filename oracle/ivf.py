@@ -26,8 +26,9 @@ fork_search_cuda.cu:1256-1524), for each query row ``b``:
    ``[B, ceil(N / 64)]`` int64 drops a position ``d`` whose bit is clear; the
    CUDA scorer reads bit ``63 - d % 64`` of word ``d // 64`` (high bit first:
    silvertorch/ops/csrc/bloom_index_util.cuh:138-147, 157-180;
-   retrieve/src/retrieve/ops/official/__init__.py:31). Dropped slots are never
-   returned.
+   retrieve/src/retrieve/ops/official/__init__.py:31). The exact clause filter
+   (``exact_pass``, fork_filters.cuh:15-41, on the layout of ``exact_layout``)
+   drops the positions whose clauses fail. Dropped slots are never returned.
 4. Top-k on the raw scores, larger first, ties to the lower slot
    (fork_search_cuda.cu:1374-1480; retrieve/src/retrieve/ops/official/adapter.py:465-478),
    over ``min(k, width)`` slots, then the ``[B, k]`` epilogue
@@ -103,6 +104,49 @@ def pack_mask_high_first(mask) -> np.ndarray:
     return np.bitwise_or.reduce(bits << shifts, axis=2).view(np.int64)
 
 
+INT32_MAX = np.iinfo(np.int32).max
+
+
+def exact_layout(attrs):
+    """``[N, C, A]`` cluster-sorted attrs (values ``>= -1``, ``-1`` pads) to the exact
+    filter's layout (retrieve/src/retrieve/ops/official/adapter.py:68-81): ``slots``
+    int32 ``[R, N]``, clause ``c`` in rows ``clause_slots[c]:clause_slots[c + 1]``,
+    each doc's values sorted descending, every clause as wide as its widest doc."""
+    a = -np.sort(-np.asarray(attrs, dtype=np.int64), axis=2)  # descending
+    if a.size and (a.min() < -1 or a.max() > INT32_MAX):
+        raise ValueError("the exact filter takes attr values in [-1, 2**31 - 1]")
+    widths = (a != -1).sum(axis=2).max(axis=0) if a.shape[0] else np.zeros(a.shape[1], dtype=np.int64)
+    rows = [a[:, c, :w].T for c, w in enumerate(widths.tolist())]
+    slots = np.concatenate(rows, axis=0) if rows else np.zeros((0, a.shape[0]), dtype=np.int64)
+    clause_slots = np.zeros(a.shape[1] + 1, dtype=np.int64)
+    clause_slots[1:] = np.cumsum(widths)
+    return np.ascontiguousarray(slots.astype(np.int32)), clause_slots
+
+
+def exact_query(query_clause_attrs):
+    """``[B, C]`` query attrs to int32; a value no doc can hold becomes INT32_MIN
+    (adapter.py:84-89)."""
+    q = np.asarray(query_clause_attrs, dtype=np.int64)
+    return np.where((q >= -1) & (q <= INT32_MAX), q, INT32_MIN).astype(np.int32)
+
+
+def exact_pass(slots, clause_slots, reverse, q_row, pos) -> np.ndarray:
+    """The exact clause test of sorted positions ``pos`` for one query row
+    (silvertorch/ops/csrc/fork_filters.cuh:15-41): a clause with query value -1
+    passes; otherwise it matches when one of the doc's values equals the query's,
+    and passes when the match differs from its reverse flag."""
+    slots = np.asarray(slots, dtype=np.int64)
+    ok = np.ones(len(pos), dtype=bool)
+    for c in range(len(clause_slots) - 1):
+        qv = int(q_row[c])
+        if qv == -1:
+            continue
+        vals = slots[clause_slots[c] : clause_slots[c + 1]][:, pos]  # [width, len(pos)]
+        match = (vals == qv).any(axis=0)
+        ok &= match != bool(reverse[c])
+    return ok
+
+
 def raw_scores(q_codes_row, item_codes, pos, divisor: int):
     """Per-slot raw scores: int32 dots, or fp16 ``dot / divisor``."""
     dots = np.asarray(item_codes, dtype=np.int8)[pos].astype(np.int64) @ np.asarray(q_codes_row, np.int64)
@@ -112,8 +156,11 @@ def raw_scores(q_codes_row, item_codes, pos, divisor: int):
 
 
 def search_codes(q_codes, q_scales, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm,
-                 global_scale, k, max_tensor_size_per_row, divisor_for_int8=-1, filtering_bit_mask=None):
-    """``st::search`` after the query prep: ``(ids int64 [B, k], scores fp32 [B, k])``."""
+                 global_scale, k, max_tensor_size_per_row, divisor_for_int8=-1, filtering_bit_mask=None,
+                 exact=None):
+    """``st::search`` after the query prep: ``(ids int64 [B, k], scores fp32 [B, k])``.
+    ``exact`` = ``(slots, clause_slots, reverse, query_attrs)`` in the exact filter's
+    layout (``exact_layout`` / ``exact_query``) drops the probed positions that fail it."""
     q_codes = np.asarray(q_codes, dtype=np.int8)
     q_scales = np.asarray(q_scales, dtype=np.float32)
     probe_ids = np.asarray(probe_ids, dtype=np.int64)
@@ -134,6 +181,9 @@ def search_codes(q_codes, q_scales, probe_ids, cluster_offsets, cluster_sizes, i
         if filtering_bit_mask is not None:
             keep = mask_bit_high_first(np.asarray(filtering_bit_mask)[row], pos)
             pos, raw, slot = pos[keep], raw[keep], slot[keep]
+        if exact is not None:
+            keep = exact_pass(exact[0], exact[1], exact[2], np.asarray(exact[3])[row], pos)
+            pos, raw, slot = pos[keep], raw[keep], slot[keep]
         # larger raw first, ties to the lower slot; only min(k, width) slots are taken
         order = np.lexsort((slot, -raw.astype(np.float64)))[: min(k, width)]
         n = order.size
@@ -149,11 +199,11 @@ def search_codes(q_codes, q_scales, probe_ids, cluster_offsets, cluster_sizes, i
 
 
 def search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm, global_scale, k,
-           max_tensor_size_per_row, divisor_for_int8=-1, filtering_bit_mask=None):
+           max_tensor_size_per_row, divisor_for_int8=-1, filtering_bit_mask=None, exact=None):
     """``st::search`` (fork_search.cpp:13-41) on fp32 queries ``[B, D]``."""
     q_codes, q_scales = quantize_int8(np.asarray(query, dtype=np.float32))
     return search_codes(q_codes, q_scales, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm,
-                        global_scale, k, max_tensor_size_per_row, divisor_for_int8, filtering_bit_mask)
+                        global_scale, k, max_tensor_size_per_row, divisor_for_int8, filtering_bit_mask, exact)
 
 
 def probe_prep(query, probe_ids, cluster_offsets, cluster_sizes):

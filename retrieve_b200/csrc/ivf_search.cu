@@ -10,8 +10,9 @@
 //     order: every probed cluster's warp-aligned prefix (32 * (len / 32)
 //     positions) in probe order, then every cluster's remainder (len % 32) in
 //     probe order (fused_kmean_ann_cuda.cu:100-110, 183-215). A position whose
-//     bit is clear in the full-N filter mask becomes -1 and is never scored;
-//     the mask is read high bit first, bit 63 - d % 64 of word d / 64
+//     bit is clear in the full-N filter mask, or that fails the exact clause
+//     filter (fork_filters.cuh:15-41), becomes -1 and is never scored; the
+//     mask is read high bit first, bit 63 - d % 64 of word d / 64
 //     (bloom_index_util.cuh:138-180).
 //  3. cand_scan_kernel<2> (cand_scan.cu): exact int32 dots of the int8 codes,
 //     ranked on fp32(dot) or on fp16(dot / divisor); every |dot| <= 2^24 when
@@ -53,6 +54,39 @@ __device__ __forceinline__ void probe_range(const int64_t* __restrict__ offsets,
   len = l < N - s ? l : N - s;
 }
 
+// The exact clause filter (silvertorch/ops/csrc/fork_filters.cuh:15-41): attrs is the
+// clause-major int32 [rows, docs] slot table, clause c in slots
+// [clause_slots[c], clause_slots[c + 1]), each doc's values sorted descending with -1
+// pads last; a clause with query value -1 passes, otherwise it matches when one of the
+// doc's values equals the query's and passes when the match differs from reverse[c].
+// Consecutive lanes test consecutive positions, so each slot row reads coalesced.
+struct ExactArgs {
+  const int32_t* attrs;  // null: no exact filter
+  int64_t rows, docs;
+  const int64_t* clause_slots;
+  const uint8_t* reverse;
+  const int32_t* query;  // [B, n_clauses]
+  int n_clauses;
+};
+
+__device__ __forceinline__ bool exact_pass(const ExactArgs& ex, const int32_t* __restrict__ q, int64_t doc) {
+  for (int c = 0; c < ex.n_clauses; ++c) {
+    const int32_t qv = q[c];
+    if (qv == -1) continue;
+    bool match = false;
+    const int64_t s1 = min(ex.clause_slots[c + 1], ex.rows);
+    for (int64_t s = max(ex.clause_slots[c], int64_t{0}); s < s1; ++s) {
+      const int32_t v = ex.attrs[s * ex.docs + doc];
+      if (v == qv || v == -1) {
+        match = v == qv;
+        break;
+      }
+    }
+    if (match == (ex.reverse[c] != 0)) return false;
+  }
+  return true;
+}
+
 // Block-wide inclusive scan of two int64 values (kExpandThreads threads).
 __device__ __forceinline__ void block_scan2(int64_t (&part)[2][kExpandThreads], int64_t& a, int64_t& b) {
   const int tid = threadIdx.x;
@@ -77,7 +111,7 @@ __device__ __forceinline__ void block_scan2(int64_t (&part)[2][kExpandThreads], 
 __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
     const int64_t* __restrict__ probe_ids, int P, const int64_t* __restrict__ offsets,
     const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, const uint64_t* __restrict__ mask,
-    int64_t mask_words, int width, int64_t* __restrict__ pos, int64_t* __restrict__ counts) {
+    int64_t mask_words, ExactArgs ex, int width, int64_t* __restrict__ pos, int64_t* __restrict__ counts) {
   // per probe: start (int64), len, head slot, tail slot (int32, slots clipped to width)
   extern __shared__ __align__(16) uint8_t sm[];
   int64_t* p_start = reinterpret_cast<int64_t*>(sm);
@@ -125,6 +159,7 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
   const int warp = tid >> 5, lane = tid & 31;
   int64_t* out = pos + static_cast<int64_t>(b) * width;
   const uint64_t* mrow = mask ? mask + static_cast<int64_t>(b) * mask_words : nullptr;
+  const int32_t* qattrs = ex.attrs ? ex.query + static_cast<int64_t>(b) * ex.n_clauses : nullptr;
   auto emit = [&](int64_t slot, int64_t position) {
     if (slot >= width) return;
     int64_t v = position;
@@ -132,6 +167,7 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
       const int64_t w = position >> 6;
       if (w < mask_words && ((mrow[w] >> (63 - (position & 63))) & 1ull) == 0) v = -1;
     }
+    if (qattrs != nullptr && v >= 0 && !exact_pass(ex, qattrs, position)) v = -1;
     out[slot] = v;
   };
   for (int j = warp; j < P; j += kExpandThreads / 32) {
@@ -328,13 +364,30 @@ int rb_st_search_workspace_size(int B, int D, int P, int k, int max_tensor_size_
 int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P, const int64_t* cluster_offsets,
                  const int64_t* cluster_sizes, int64_t n_lists, const int8_t* item_codes, int64_t N,
                  const int64_t* sort_perm, const float* global_scale, int k, int max_tensor_size_per_row,
-                 int divisor_for_int8, const int64_t* filtering_bit_mask, int64_t mask_words, int64_t* out_ids,
-                 float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+                 int divisor_for_int8, const int64_t* filtering_bit_mask, int64_t mask_words,
+                 const int32_t* item_clause_attrs, int64_t attr_rows, int64_t attr_docs, const int64_t* clause_slots,
+                 const uint8_t* clause_is_reverse, const int32_t* query_clause_attrs, int n_clauses,
+                 int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = st_check(B, D, P, n_lists, N, k, max_tensor_size_per_row, divisor_for_int8);
   if (rc != RB_OK) return rc;
   if (filtering_bit_mask != nullptr && mask_words < 0) {
     set_last_error("st::search: bad filtering_bit_mask width");
     return RB_ERR_INVALID_ARG;
+  }
+  ExactArgs ex{nullptr, 0, 0, nullptr, nullptr, nullptr, 0};
+  if (query_clause_attrs != nullptr) {
+    if (filtering_bit_mask != nullptr) {
+      set_last_error("st::search takes one filter: the exact clauses or filtering_bit_mask");
+      return RB_ERR_INVALID_ARG;
+    }
+    if (item_clause_attrs == nullptr || clause_slots == nullptr || clause_is_reverse == nullptr || n_clauses < 0 ||
+        attr_rows < 0 || attr_docs < N) {
+      set_last_error("st::search: the exact filter needs item_clause_attrs [R, >= N], clause_slots and "
+                     "clause_is_reverse");
+      return RB_ERR_INVALID_ARG;
+    }
+    ex = ExactArgs{item_clause_attrs, attr_rows, attr_docs, clause_slots, clause_is_reverse, query_clause_attrs,
+                   n_clauses};
   }
   if (B == 0) return RB_OK;
   const int width = st_width(max_tensor_size_per_row);
@@ -363,7 +416,7 @@ int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int
   const size_t smem = static_cast<size_t>(P) * (sizeof(int64_t) + 3 * sizeof(int));
   probe_expand_kernel<<<B, kExpandThreads, smem, s>>>(
       probe_ids, P, cluster_offsets, cluster_sizes, n_lists, N, reinterpret_cast<const uint64_t*>(filtering_bit_mask),
-      mask_words, width, pos, counts);
+      mask_words, ex, width, pos, counts);
   rc = launch_status();
   if (rc != RB_OK) return rc;
   rc = cand_i8_topk(q_codes, item_codes, static_cast<int>(N), D, pos, width, counts, B, k_sel, divisor_for_int8,

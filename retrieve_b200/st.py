@@ -14,8 +14,10 @@ clusters' positions in the reference scorer's slot order, exact int32 dots,
 top-k on the raw score with ties to the lower slot, ``id = sort_perm[pos]`` and
 ``score = (fp32(dot) * q_scale) * global_scale`` (or the fp16 path's
 ``raw * ((q_scale * divisor) * global_scale)``), ``-1`` / ``-inf`` pads. A
-full-``N`` ``filtering_bit_mask`` (high bit first) is honoured; the bloom-plan
-and exact-clause filters are not served and raise ``NotImplementedError``.
+full-``N`` ``filtering_bit_mask`` (high bit first) and the exact clause filter
+are served; bloom plans with the exact recheck give the exact filter's result
+(the bloom has no false negatives); bloom plans alone raise
+``NotImplementedError``.
 Errors raise ``RuntimeError``, as the reference's ``TORCH_CHECK``s do.
 """
 
@@ -85,10 +87,40 @@ def search(
     item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
     clause_is_reverse: Tensor | None = None, query_clause_attrs: Tensor | None = None,
 ) -> tuple[Tensor, Tensor]:
-    """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``."""
-    if plans is not None or bloom_index is not None or query_clause_attrs is not None:
-        raise NotImplementedError("st::search: the bloom-plan and exact-clause filters are not implemented here; "
-                                  "pass a full-N filtering_bit_mask")
+    """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``.
+
+    Filters: a full-``N`` ``filtering_bit_mask``, or the exact clauses
+    (``item_clause_attrs``, ``clause_slots``, ``clause_is_reverse``,
+    ``query_clause_attrs``). With bloom ``plans`` and the exact clauses together
+    (the bloom with its exact recheck) the result is the exact filter's, since the
+    bloom has no false negatives; the plans are then not read. Bloom plans alone
+    (false positives kept) are not served."""
+    exact = query_clause_attrs is not None
+    _check(not (filtering_bit_mask is not None and (plans is not None or exact)),
+           "search takes one filter: plans (+ query_clause_attrs to recheck), query_clause_attrs or "
+           "filtering_bit_mask")
+    if plans is not None and not exact:
+        raise NotImplementedError("st::search: the bloom-plan filter without its exact recheck is not implemented "
+                                  "here; pass query_clause_attrs (recheck) or a filtering_bit_mask")
+    ex = None
+    if exact:
+        _check(item_clause_attrs is not None and clause_slots is not None and clause_is_reverse is not None,
+               "the exact filter needs item_clause_attrs, clause_slots and clause_is_reverse")
+        _check(item_clause_attrs.dim() == 2 and item_clause_attrs.dtype == torch.int32,
+               "item_clause_attrs must be int32 [R, N]")
+        _check(clause_slots.dim() == 1 and clause_slots.dtype == torch.int64, "clause_slots must be int64 [C + 1]")
+        _check(query_clause_attrs.dim() == 2 and query_clause_attrs.dtype == torch.int32,
+               "query_clause_attrs must be int32 [B, C]")
+        _check(clause_is_reverse.dtype == torch.bool, "clause_is_reverse must be bool")
+        for t in (item_clause_attrs, clause_slots, clause_is_reverse, query_clause_attrs):
+            _check(t.is_contiguous() and t.device == query.device,
+                   "the exact filter's tensors must be contiguous and on the query's device")
+        n_clauses = query_clause_attrs.shape[1]
+        _check(clause_slots.shape[0] == n_clauses + 1 and clause_is_reverse.numel() == n_clauses,
+               "clause_slots must have C + 1 entries and clause_is_reverse C")
+        _check(query_clause_attrs.shape[0] == query.shape[0], "query_clause_attrs must have B rows")
+        _check(item_clause_attrs.shape[1] >= item_codes.shape[0], "item_clause_attrs must cover the N docs")
+        ex = (item_clause_attrs, clause_slots, clause_is_reverse, query_clause_attrs)
     _check(item_codes.dtype == torch.int8 and item_codes.dim() == 2 and item_codes.shape[1] == query.shape[1],
            "item_codes must be int8 [N, D] with the query's D")
     _check(item_codes.is_contiguous(), "item_codes must be contiguous")
@@ -122,7 +154,11 @@ def search(
     rc = lib.rb_st_search(
         _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), _ptr(item_codes),
         item_codes.shape[0], _ptr(perm), _ptr(gs), k, int(max_tensor_size_per_row), int(divisor_for_int8),
-        _ptr(mask), mask_words, _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream(dev),
+        _ptr(mask), mask_words,
+        _ptr(ex[0] if ex else None), ex[0].shape[0] if ex else 0, ex[0].shape[1] if ex else 0,
+        _ptr(ex[1] if ex else None), _ptr(ex[2] if ex else None), _ptr(ex[3] if ex else None),
+        ex[3].shape[1] if ex else 0,
+        _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream(dev),
     )
     _call(rc, "st::search")
     return ids, scores

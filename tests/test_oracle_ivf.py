@@ -144,3 +144,26 @@ def test_probe_prep_cumsums():
         in_warp_prefix = (pos - offsets[cluster]) < sizes[cluster] // 32 * 32
         head = int(out[6][r, -1])
         assert in_warp_prefix[:head].all() and not in_warp_prefix[head:].any()
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_exact_layout_and_test_equal_the_clause_predicate(seed):
+    """The exact filter's layout (adapter.py:68-89) and test (fork_filters.cuh:15-41) give
+    the LiNR clause predicate (pinned to the reference by golden.npz): the reference's own
+    gate feeds both the same predicate (retrieve/tests/parity/test_official.py:278-293)."""
+    from oracle import filters
+
+    rng = np.random.default_rng(seed)
+    n, c, a = 700, 4, 3
+    attrs = rng.integers(-1, 6, (n, c, a))
+    attrs[rng.random(n) < 0.1, 2, :] = -1  # docs with no value in a clause
+    rev = rng.random(c) < 0.5
+    q = rng.integers(-1, 6, (9, c))
+    q[0, 1] = 2**40  # a value no doc can hold: matches nothing
+    slots, clause_slots = ivf.exact_layout(attrs)
+    assert slots.dtype == np.int32 and slots.shape[1] == n and clause_slots[-1] == slots.shape[0]
+    qq = ivf.exact_query(q)
+    assert qq[0, 1] == ivf.INT32_MIN
+    want = filters.clause_mask(attrs, rev, q)
+    for b in range(q.shape[0]):
+        assert np.array_equal(ivf.exact_pass(slots, clause_slots, rev, qq[b], np.arange(n)), want[b])

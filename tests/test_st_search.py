@@ -118,9 +118,10 @@ def test_capi_argument_checks_need_no_device():
     assert n.value >= 16 * 704 * 8
     assert lib.rb_st_search_workspace_size(16, 128, 8, 0, 700, ctypes.byref(n)) == _lib.RB_ERR_INVALID_ARG
 
-    def call(b=4, d=128, p=8, k=10, width=256, div=-1, ws=None, ws_bytes=0):
-        return lib.rb_st_search(None, b, d, None, p, None, None, 16, None, 1000, None, None, k, width, div, None, 0,
-                                None, None, ws, ws_bytes, None)
+    def call(b=4, d=128, p=8, k=10, width=256, div=-1, ws=None, ws_bytes=0, mask=None, qattrs=None, attrs=None,
+             docs=1000):
+        return lib.rb_st_search(None, b, d, None, p, None, None, 16, None, 1000, None, None, k, width, div, mask, 0,
+                                attrs, 3, docs, attrs, attrs, qattrs, 2, None, None, ws, ws_bytes, None)
 
     assert call(d=2048) == _lib.RB_ERR_UNSUPPORTED  # D > 1024
     assert call(p=4096) == _lib.RB_ERR_UNSUPPORTED  # more than 2048 probes
@@ -131,6 +132,11 @@ def test_capi_argument_checks_need_no_device():
     assert call(b=70000) == _lib.RB_ERR_UNSUPPORTED
     assert call() == _lib.RB_ERR_WORKSPACE
     assert b"workspace" in lib.rb_last_error()
+    fake = ctypes.c_void_p(16)  # never dereferenced: the checks fail first
+    assert call(mask=fake, qattrs=fake, attrs=fake) == _lib.RB_ERR_INVALID_ARG  # one filter only
+    assert call(qattrs=fake) == _lib.RB_ERR_INVALID_ARG  # exact filter without its tables
+    assert call(qattrs=fake, attrs=fake, docs=999) == _lib.RB_ERR_INVALID_ARG  # attrs narrower than N
+    assert call(qattrs=fake, attrs=fake) == _lib.RB_ERR_WORKSPACE
     assert call(b=0) == _lib.RB_OK  # nothing to do: no device touched
 
 
@@ -187,6 +193,48 @@ def test_search_filter_mask(ci):
                       meta["k"], meta["width"], filtering_bit_mask=words)
     _assert_exact(ids, scores, *want)
     assert_topk_equal_up_to_ties(ids, scores, g["idsm"], g["scm"])
+
+
+def _exact_inputs(rng, n, b, c=3, a_max=3, n_vocab=6, reverse=(True, False, False)):
+    """Small-vocabulary attrs (a high pass rate), about 20 % of query clauses inactive,
+    clause 0 reversed; the layout of the exact filter."""
+    attrs = rng.integers(-1, n_vocab, (n, c, a_max))
+    q = rng.integers(0, n_vocab, (b, c))
+    q[rng.random((b, c)) < 0.2] = -1
+    rev = np.array(reverse[:c], dtype=bool)
+    slots, clause_slots = ivf.exact_layout(attrs)
+    return attrs, rev, q, slots, clause_slots, ivf.exact_query(q)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(N_CASES))
+@pytest.mark.parametrize("score_path", ["int32", "fp16"])
+def test_search_exact_clause_filter(ci, score_path):
+    """The layer's exact path: the clauses tested inside st::search equal the oracle
+    bit for bit, and the same predicate given as a full-N mask; bloom plans with the
+    exact recheck give the same result."""
+    st = _st()
+    g, meta = _case(ci)
+    rng = np.random.default_rng(ci)
+    n = g["codes"].shape[0]
+    attrs, rev, q, slots, clause_slots, qq = _exact_inputs(rng, n, meta["b"])
+    div = -1 if score_path == "int32" else meta["div"]
+    ex = (torch.from_numpy(slots).cuda(), torch.from_numpy(clause_slots).cuda(), torch.from_numpy(rev).cuda(),
+          torch.from_numpy(qq).cuda())
+    ids, scores = _run(st, g, meta, divisor_for_int8=div, item_clause_attrs=ex[0], clause_slots=ex[1],
+                       clause_is_reverse=ex[2], query_clause_attrs=ex[3])
+    args = (g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"], g["gs"], meta["k"],
+            meta["width"])
+    want = ivf.search(*args, divisor_for_int8=div, exact=(slots, clause_slots, rev, qq))
+    _assert_exact(ids, scores, *want)
+    from oracle import filters
+
+    words = ivf.pack_mask_high_first(filters.clause_mask(attrs, rev, q))
+    _assert_exact(ids, scores, *ivf.search(*args, divisor_for_int8=div, filtering_bit_mask=words))
+    ids2, scores2 = _run(st, g, meta, divisor_for_int8=div, item_clause_attrs=ex[0], clause_slots=ex[1],
+                         clause_is_reverse=ex[2], query_clause_attrs=ex[3],
+                         plans=torch.zeros(8, dtype=torch.uint8, device="cuda"), plan_count=1)
+    _assert_exact(ids2, scores2, ids, scores)
 
 
 def _layout(rng, n_lists, max_size, d, b, p):
