@@ -56,7 +56,7 @@ def parse_args():
     p.add_argument("--ref-sample", type=int, default=32,
                    help="queries per step of --impl reference (each step a bounded sample)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=("c2", "c3", "c4", "c5", "ops"), default="c2",
+    p.add_argument("--workload", choices=("c2", "c3", "c4", "c5", "ivf", "ops"), default="c2",
                    help="c2 (default, the headline); c3/c4/c5 and ops: one-GPU measurements of the other configs "
                         "and of every other kernel")
     return p.parse_args()

@@ -13,6 +13,9 @@ step streams more than L2), so no flush is needed.
   c4   int8 scoring, 30M x 256 with per-row scales, B = 4096, k = 100
   c5   1-bit pool + rerank, 30M x 512-bit SimHash codes of a d = 128 mixture,
        pool 1000 on the int8 tensor cores, fp16 rerank to k = 100, B = 1024
+  ivf  SilverTorch's IVF search: phase 1 (centroid scores + probe top-k) and
+       st::search (int8 probe scoring, top-k, dequant) over an int8 table of the
+       C2 corpus in cluster-sorted order, 1024 lists, 16 probes, B = 1024, k = 100
   ops  the remaining kernels one by one at representative sizes
 """
 
@@ -323,11 +326,106 @@ def run_ops(args, dev):
           clocks, "mixed")
 
 
+# ---------------------------------------------------------------------------
+# ivf: SilverTorch's IVF phase 1 + st::search
+# ---------------------------------------------------------------------------
+def _ivf_cpu_baseline(q, probe, offsets, sizes, codes_sorted, perm, gs, k, width, sample: int = 8) -> dict:
+    """The reference's CPU path on ``sample`` queries: its CPU scorer
+    ``st.fused_kmean_ann`` (built from the reference's sources into oracle/_ref) and
+    its adapter epilogue (``torch.topk`` on the raw dots, ``sort_perm``, the two
+    multiplies); the oracle's restatement when that build is absent."""
+    import os
+    import time
+
+    ref = bench.ROOT / "oracle" / "_ref" / "silvertorch_ref_cpu.so"
+    qs = q[:sample].cpu()
+    pr = probe[:sample].cpu()
+    torch.set_num_threads(os.cpu_count() or 1)
+    if ref.exists():
+        from oracle.knn import quantize_int8
+
+        torch.ops.load_library(str(ref))
+        off, sz, cs, pm = offsets.cpu(), sizes.cpu(), codes_sorted.cpu(), perm.cpu()
+        t0 = time.perf_counter()
+        qc, qsc = quantize_int8(qs.numpy())
+        raw, idx = torch.ops.st.fused_kmean_ann(off, pr, sz[pr], cs, torch.from_numpy(qc), width, None, -1, -1,
+                                                None, None)
+        top, slot = torch.topk(torch.where(idx >= 0, raw, torch.iinfo(torch.int32).min), min(k, raw.shape[1]))
+        pos = idx.gather(1, slot).long()
+        _ = torch.where(pos >= 0, pm[pos.clamp_min(0)], -1), top.float() * torch.from_numpy(qsc)[:, None] * gs.cpu()
+        dt = time.perf_counter() - t0
+        kind = "reference"
+    else:
+        from oracle import ivf
+
+        t0 = time.perf_counter()
+        ivf.search(qs.numpy(), pr.numpy(), offsets.cpu().numpy(), sizes.cpu().numpy(), codes_sorted.cpu().numpy(),
+                   perm.cpu().numpy(), gs.cpu().numpy(), k, width)
+        dt = time.perf_counter() - t0
+        kind = "port"
+    return {"value": sample / dt, "unit": "queries/s", "cores": 1, "kind": kind,
+            "sample": f"{sample} queries of the batch, phase 2 only (probe lists given)"}
+
+
+def run_ivf(args, dev):
+    import retrieve_b200.st  # noqa: F401  (registers torch.ops.st.search)
+    from retrieve_b200 import ops
+    from retrieve_b200.quantize import quantize_int8_global
+
+    n = args.n_items
+    d, b, k, n_probe = bench.DIM, args.batch, args.k, 16
+    cent = bench.centres(dev)
+    n_lists = cent.shape[0]
+    items = torch.empty((n, d), dtype=torch.float32, device=dev)
+    assign = torch.empty((n,), dtype=torch.int64, device=dev)
+    centroids = (cent / cent.norm(dim=1, keepdim=True)).to(torch.bfloat16).contiguous()
+    for lo, hi, x in _blocks(n, lambda r, sd: bench.mixture_block(cent, r, sd)):
+        items[lo:hi] = x
+        # build time: each item's list is its nearest centroid by dot product (phase 1's metric)
+        assign[lo:hi] = (x.float() @ centroids.float().t()).argmax(dim=1)
+    perm = torch.sort(assign, stable=True).indices  # sorted position -> item id
+    sizes = torch.bincount(assign, minlength=n_lists)
+    offsets = torch.zeros(n_lists + 1, dtype=torch.int64, device=dev)
+    offsets[1:] = sizes.cumsum(0)
+    codes_sorted, gs_f = quantize_int8_global(items, rows=perm)
+    del items
+    gs = torch.tensor(gs_f, dtype=torch.float32, device=dev)
+    q = bench.queries(cent, b).to(torch.float32)
+    qb = q.to(torch.bfloat16)
+    probe0 = ops.dense_topk(qb, centroids, n_probe)[0]
+    width = int(sizes[probe0].sum(1).max()) + 32 * n_probe  # room for other batches' probe totals
+    torch.cuda.synchronize()
+
+    def step():
+        probe = ops.dense_topk(qb, centroids, n_probe)[0]
+        return torch.ops.st.search(q, probe, offsets, sizes, codes_sorted, perm, gs, k, width)
+
+    sampler = bench.ClockSampler(dev)
+    sampler.start()
+    ms, _ = _time(step, args.warmup, args.steps)
+    clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
+    scored = float(sizes[probe0].sum())  # probed (query, item) pairs per batch
+    hbm = _peaks().get("hbm_gbs", 6650.0)
+    achieved = scored * d / (ms / 1e3) / 1e9
+    cpu = _ivf_cpu_baseline(q, probe0, offsets, sizes, codes_sorted, perm, gs, k, width)
+    _line("queries/s, IVF phase 1 + st::search @10M items d=128 int8 (global scale), 1024 lists, 16 probes, "
+          "B=1024, k=100", b / (ms / 1e3), "queries/s",
+          {"workload": "SilverTorch IVF search (st::search semantics)", "n_items": n, "dim": d, "batch": b, "k": k,
+           "n_lists": n_lists, "n_probe": n_probe, "max_tensor_size_per_row": width,
+           "probed_pairs_per_batch": scored,
+           "corpus": "the C2 mixture, clustered by its nearest normalised centre, int8 with one global scale"},
+          {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+           "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
+           "note": "probed code bytes (pairs x D) per second; rows probed by several queries of a batch are "
+                   "re-read from L2, so this can exceed the HBM copy rate", "step_ms": ms},
+          clocks, "int8 -> int32", cpu_baseline=cpu)
+
+
 def run_workload(args):
     import os
 
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-        raise SystemExit("--workload c3/c4/c5/ops runs on one GPU (no torchrun)")
+        raise SystemExit("--workload c3/c4/c5/ivf/ops runs on one GPU (no torchrun)")
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    {"c3": run_c3, "c4": run_c4, "c5": run_c5, "ops": run_ops}[args.workload](args, dev)
+    {"c3": run_c3, "c4": run_c4, "c5": run_c5, "ivf": run_ivf, "ops": run_ops}[args.workload](args, dev)
