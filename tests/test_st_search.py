@@ -86,6 +86,30 @@ def test_cpu_tensors_raise():
                   torch.tensor([4]), torch.zeros(4, 64, dtype=torch.int8), torch.arange(4), torch.tensor(1.0), 2, 4)
 
 
+def test_argument_errors_raise_runtime_error():
+    """The reference's TORCH_CHECKs raise RuntimeError (fork_search_cuda.cu:1280-1295); these
+    fail before any device work (the CUDA implementation is called directly: CPU tensors
+    would not dispatch to it)."""
+    _st()
+    from retrieve_b200 import st
+
+    q = torch.zeros(2, 64)
+    probe = torch.zeros(2, 1, dtype=torch.int64)
+    off, sz = torch.tensor([0, 4]), torch.tensor([4])
+    perm, gs = torch.arange(4), torch.tensor(1.0)
+    with pytest.raises(RuntimeError, match="int8"):
+        st.search(q, probe, off, sz, torch.zeros(4, 64, dtype=torch.float16), perm, gs, 2, 4)
+    with pytest.raises(RuntimeError, match="D"):
+        st.search(q, probe, off, sz, torch.zeros(4, 32, dtype=torch.int8), perm, gs, 2, 4)
+    with pytest.raises(RuntimeError, match="one filter"):
+        st.search(q, probe, off, sz, torch.zeros(4, 64, dtype=torch.int8), perm, gs, 2, 4,
+                  filtering_bit_mask=torch.zeros(2, 1, dtype=torch.int64),
+                  query_clause_attrs=torch.zeros(2, 1, dtype=torch.int32))
+    with pytest.raises(NotImplementedError):
+        st.search(q, probe, off, sz, torch.zeros(4, 64, dtype=torch.int8), perm, gs, 2, 4,
+                  plans=torch.zeros(8, dtype=torch.uint8))
+
+
 REF_CPU_LIB = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "silvertorch_ref_cpu.so"
 
 
