@@ -385,6 +385,25 @@ RB_API int rb_st_search(const float* query, int B, int D, const int64_t* probe_i
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The same search, grouped by cluster: every (row, probe) pair is filed under its
+ * cluster, and each cluster is read once per group of up to 64 probing rows
+ * (staged in shared memory) instead of once per probing row. Same arguments,
+ * results and limits as rb_st_search, with P <= 1024; workspace from
+ * rb_st_search_grouped_workspace_size (it also depends on n_lists).
+ */
+RB_API int rb_st_search_grouped_workspace_size(int B, int D, int P, int64_t n_lists, int k,
+                                               int max_tensor_size_per_row, size_t* bytes);
+RB_API int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                                const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                                const int8_t* item_codes, int64_t N, const int64_t* sort_perm,
+                                const float* global_scale, int k, int max_tensor_size_per_row, int divisor_for_int8,
+                                const int64_t* filtering_bit_mask, int64_t mask_words,
+                                const int32_t* item_clause_attrs, int64_t attr_rows, int64_t attr_docs,
+                                const int64_t* clause_slots, const uint8_t* clause_is_reverse,
+                                const int32_t* query_clause_attrs, int n_clauses, int64_t* out_ids,
+                                float* out_scores, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)
  *   -> (codes int8 [B, D], scales fp32 [B], cluster_ids int64 [B, P],
  *       cluster_length int64 [B, P], cluster_offsets int64 [B, P], warps int32 [B * P],

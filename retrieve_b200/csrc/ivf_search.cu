@@ -30,11 +30,14 @@
 // clipped to [0, N), and slots past the row width are dropped (the
 // reference's CUDA scorer requires the probed total to fit the width and does
 // not check it).
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <cstdint>
 
 #include "rb_capi_internal.h"
 #include "rb_common.cuh"
+#include "rb_select.cuh"
 
 namespace rb {
 
@@ -344,6 +347,337 @@ static int st_check(int B, int D, int P, int64_t n_lists, int64_t N, int k, int 
   return RB_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Grouped scorer (rb_st_search_grouped): the same results as rb_st_search with
+// each probed cluster read once per (cluster, group of probing rows) instead of
+// once per probing row.
+//
+//  1. pair_count / cluster_scan / pair_scatter: the (row, probe) pairs grouped
+//     by cluster (a counting sort; order inside a cluster is free, since every
+//     pair owns its own candidate list); one task per cluster and group of at
+//     most G pairs.
+//  2. slot_starts: per pair, the row's first head slot and first tail slot of
+//     that probe (the layout of probe_expand_kernel, cluster lengths clipped to
+//     the width in the same way), and per row the total.
+//  3. ivf_group_scan_kernel, one CTA per task: the pairs' query codes and then
+//     128-row tiles of the cluster staged in shared memory; each warp takes
+//     pairs and scores a whole tile for each (4 rows a lane, dp4a), appending
+//     (raw score, slot) in ascending slot order to the pair's list, so ties keep
+//     the lower slot exactly as in the row path.
+//  4. merge_lists over each row's P lists, then st_group_epilogue_kernel: slot
+//     -> (probe, row in cluster) by binary search over the row's slot ends ->
+//     position -> sort_perm, and the dequantization.
+// ---------------------------------------------------------------------------
+constexpr int kGroupThreads = 256;
+constexpr int kGroupWarps = kGroupThreads / 32;
+constexpr int kGroupTile = 128;  // cluster rows staged per step: 4 per lane
+constexpr int kGroupCap = 256;   // candidate-list capacity per (row, probe)
+constexpr int kGroupMaxPairs = 64;
+
+static int group_pairs_per_task(int D) {
+  const int dp = (D + 15) / 16 * 16;
+  return std::max(8, std::min(kGroupMaxPairs, 16384 / dp));
+}
+
+static size_t group_smem_bytes(int D) {
+  const size_t dp = static_cast<size_t>(D + 15) / 16 * 16;
+  return static_cast<size_t>(group_pairs_per_task(D)) * dp + kGroupTile * (dp + 16);
+}
+
+// Clipped length of probe (row, j) and its warp-aligned part, as probe_expand_kernel.
+__device__ __forceinline__ void clipped_probe(const int64_t* __restrict__ offsets, const int64_t* __restrict__ sizes,
+                                              int64_t n_lists, int64_t N, int64_t c, int width, int64_t& start,
+                                              int64_t& len, int64_t& full) {
+  probe_range(offsets, sizes, n_lists, N, c, start, len);
+  if (len > width) len = width;
+  full = len / 32 * 32;
+}
+
+__global__ void pair_count_kernel(const int64_t* __restrict__ probe, int64_t n_pairs, int64_t n_lists,
+                                  int* __restrict__ cnt) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_pairs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = probe[i];
+    if (c >= 0 && c < n_lists) atomicAdd(&cnt[c], 1);
+  }
+}
+
+// Exclusive prefix sums over clusters of the pair counts (cpo) and of the task
+// counts ceil(cnt / G) (ctask), each with the total at index n_lists. One CTA.
+__global__ void __launch_bounds__(kExpandThreads) cluster_scan_kernel(const int* __restrict__ cnt, int64_t n_lists,
+                                                                      int G, int64_t* __restrict__ cpo,
+                                                                      int64_t* __restrict__ ctask) {
+  __shared__ int64_t part[2][kExpandThreads];
+  const int tid = threadIdx.x;
+  const int64_t per = (n_lists + kExpandThreads - 1) / kExpandThreads;
+  const int64_t i0 = min(n_lists, tid * per);
+  const int64_t i1 = min(n_lists, i0 + per);
+  int64_t pairs = 0, tasks = 0;
+  for (int64_t i = i0; i < i1; ++i) {
+    pairs += cnt[i];
+    tasks += (cnt[i] + G - 1) / G;
+  }
+  int64_t pairs_incl = pairs, tasks_incl = tasks;
+  block_scan2(part, pairs_incl, tasks_incl);
+  int64_t p = pairs_incl - pairs, t = tasks_incl - tasks;
+  for (int64_t i = i0; i < i1; ++i) {
+    cpo[i] = p;
+    ctask[i] = t;
+    p += cnt[i];
+    t += (cnt[i] + G - 1) / G;
+  }
+  if (tid == kExpandThreads - 1) {
+    cpo[n_lists] = pairs_incl;
+    ctask[n_lists] = tasks_incl;
+  }
+}
+
+__global__ void pair_scatter_kernel(const int64_t* __restrict__ probe, int64_t n_pairs, int64_t n_lists,
+                                    const int64_t* __restrict__ cpo, int* __restrict__ fill,
+                                    int32_t* __restrict__ pairs) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_pairs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = probe[i];
+    if (c >= 0 && c < n_lists) pairs[cpo[c] + atomicAdd(&fill[c], 1)] = static_cast<int32_t>(i);
+  }
+}
+
+// Per pair (row b, probe j): the row's first head and first tail slot of probe j;
+// per row the slot total (before the width cut). One thread per row.
+__global__ void slot_starts_kernel(const int64_t* __restrict__ probe, int B, int P, const int64_t* __restrict__ offsets,
+                                   const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, int width,
+                                   int64_t* __restrict__ head, int64_t* __restrict__ tail,
+                                   int64_t* __restrict__ row_total) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int64_t* prow = probe + static_cast<int64_t>(b) * P;
+  int64_t h = 0;
+  for (int j = 0; j < P; ++j) {
+    int64_t start, len, full;
+    clipped_probe(offsets, sizes, n_lists, N, prow[j], width, start, len, full);
+    head[static_cast<int64_t>(b) * P + j] = h;
+    h += full;
+  }
+  int64_t t = h;
+  for (int j = 0; j < P; ++j) {
+    int64_t start, len, full;
+    clipped_probe(offsets, sizes, n_lists, N, prow[j], width, start, len, full);
+    tail[static_cast<int64_t>(b) * P + j] = t;
+    t += len - full;
+  }
+  row_total[b] = t;
+}
+
+struct GroupArgs {
+  const int8_t* items;  // [N, D], cluster-sorted
+  int64_t N;
+  int D;
+  const int8_t* q_codes;  // [B, D]
+  const int64_t* probe;   // [B, P]
+  int P;
+  const int64_t* offsets;
+  const int64_t* sizes;
+  int64_t n_lists;
+  const int32_t* pairs;  // pair ids b * P + j, grouped by cluster
+  const int64_t* cpo;    // [n_lists + 1]
+  const int64_t* ctask;  // [n_lists + 1]
+  const int64_t* head;   // [B * P]
+  const int64_t* tail;   // [B * P]
+  int width;
+  int G;
+  int k;
+  int divisor;
+  const uint64_t* mask;
+  int64_t mask_words;
+  ExactArgs ex;
+  uint2* lists;      // [B * P, kGroupCap]
+  int* list_counts;  // [B * P]
+};
+
+__global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs a) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __shared__ uint32_t hist[kGroupWarps][256];
+  __shared__ int s_pair[kGroupMaxPairs];
+  __shared__ int s_count[kGroupMaxPairs];
+  __shared__ float s_thresh[kGroupMaxPairs];
+
+  const int64_t task = blockIdx.x;
+  if (task >= a.ctask[a.n_lists]) return;  // the grid is an upper bound on the tasks
+  // the cluster: the largest c with ctask[c] <= task (ctask[0] = 0, non-decreasing)
+  int64_t lo = 0, hi = a.n_lists;
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (a.ctask[mid] <= task) lo = mid; else hi = mid;
+  }
+  const int64_t c = lo;
+  const int64_t p0 = a.cpo[c] + (task - a.ctask[c]) * a.G;
+  const int64_t p1 = min(p0 + a.G, a.cpo[c + 1]);
+  const int m = static_cast<int>(p1 - p0);
+  int64_t start, len, full;
+  clipped_probe(a.offsets, a.sizes, a.n_lists, a.N, c, a.width, start, len, full);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int dp = (a.D + 15) & ~15;  // query row stride in shared memory
+  const int rs = dp + 16;           // tile row stride: 8 lanes' 16-byte loads hit distinct banks
+  int8_t* sq = reinterpret_cast<int8_t*>(gsm);
+  int8_t* sx = sq + static_cast<size_t>(a.G) * dp;
+  for (int g = tid; g < m; g += kGroupThreads) {
+    s_pair[g] = a.pairs[p0 + g];
+    s_count[g] = 0;
+    s_thresh[g] = -INFINITY;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < m * dp; idx += kGroupThreads) {
+    const int g = idx / dp, d = idx - g * dp;
+    const int64_t b = s_pair[g] / a.P;
+    sq[g * dp + d] = d < a.D ? a.q_codes[b * a.D + d] : static_cast<int8_t>(0);
+  }
+  const bool vec = (a.D & 15) == 0 && (reinterpret_cast<uintptr_t>(a.items) & 15u) == 0;
+  for (int64_t t0 = 0; t0 < len; t0 += kGroupTile) {
+    const int rows = static_cast<int>(min(static_cast<int64_t>(kGroupTile), len - t0));
+    __syncthreads();  // the previous tile has been scored (and the query codes are staged)
+    if (vec) {
+      const int chunks = a.D / 16;
+      for (int idx = tid; idx < kGroupTile * chunks; idx += kGroupThreads) {
+        const int r = idx / chunks, ch = idx - r * chunks;
+        int4 v = make_int4(0, 0, 0, 0);
+        if (r < rows) v = *reinterpret_cast<const int4*>(a.items + (start + t0 + r) * a.D + ch * 16);
+        *reinterpret_cast<int4*>(sx + r * rs + ch * 16) = v;
+      }
+    } else {
+      for (int idx = tid; idx < kGroupTile * dp; idx += kGroupThreads) {
+        const int r = idx / dp, d = idx - r * dp;
+        sx[r * rs + d] = (r < rows && d < a.D) ? a.items[(start + t0 + r) * a.D + d] : static_cast<int8_t>(0);
+      }
+    }
+    __syncthreads();
+    for (int g = warp; g < m; g += kGroupWarps) {
+      const int pr = s_pair[g];
+      const int64_t b = pr / a.P;
+      int count = s_count[g];
+      float thresh = s_thresh[g];
+      uint2* list = a.lists + static_cast<int64_t>(pr) * kGroupCap;
+      const int64_t hs = a.head[pr], ts = a.tail[pr];
+      const int4* q = reinterpret_cast<const int4*>(sq + g * dp);
+      const uint64_t* mrow = a.mask ? a.mask + b * a.mask_words : nullptr;
+      const int32_t* qattrs = a.ex.attrs ? a.ex.query + b * a.ex.n_clauses : nullptr;
+#pragma unroll 1
+      for (int r = 0; r < kGroupTile / 32; ++r) {
+        const int li = r * 32 + lane;
+        const int64_t i = t0 + li;  // row within the cluster
+        float s = __int_as_float(0x7fc00000);  // NaN: never passes
+        uint32_t slot32 = 0;
+        if (li < rows) {
+          const int64_t slot = i < full ? hs + i : ts + (i - full);
+          const int64_t position = start + i;
+          bool ok = slot < a.width;
+          if (ok && mrow != nullptr) {
+            const int64_t w = position >> 6;
+            ok = !(w < a.mask_words && ((mrow[w] >> (63 - (position & 63))) & 1ull) == 0);
+          }
+          if (ok && qattrs != nullptr) ok = exact_pass(a.ex, qattrs, position);
+          if (ok) {
+            const int4* x = reinterpret_cast<const int4*>(sx + li * rs);
+            int acc = 0;
+            for (int ch = 0; ch < dp / 16; ++ch) {
+              const int4 xv = x[ch], qv = q[ch];
+              acc = __dp4a(xv.x, qv.x, acc);
+              acc = __dp4a(xv.y, qv.y, acc);
+              acc = __dp4a(xv.z, qv.z, acc);
+              acc = __dp4a(xv.w, qv.w, acc);
+            }
+            s = static_cast<float>(acc);
+            if (a.divisor != -1) s = __half2float(__float2half_rn(__fdiv_rn(s, static_cast<float>(a.divisor))));
+            slot32 = static_cast<uint32_t>(slot);
+          }
+        }
+        const bool pass = s >= thresh;
+        if (__ballot_sync(RB_FULL_MASK, pass)) {
+          if (count > kGroupCap - 32) {
+            warp_compact_lists<kGroupCap / 32>(list, count, thresh, lane == 0, a.k, hist[warp]);
+            count = __shfl_sync(RB_FULL_MASK, count, 0);
+            thresh = __shfl_sync(RB_FULL_MASK, thresh, 0);
+          }
+          const bool pass2 = s >= thresh;
+          const uint32_t bal2 = __ballot_sync(RB_FULL_MASK, pass2);
+          if (pass2) list[count + __popc(bal2 & lanemask_lt())] = make_uint2(__float_as_uint(s), slot32);
+          count += __popc(bal2);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        s_count[g] = count;
+        s_thresh[g] = thresh;
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  for (int g = warp; g < m; g += kGroupWarps) {
+    const int pr = s_pair[g];
+    int count = s_count[g];
+    float thresh = s_thresh[g];
+    if (count > a.k) {
+      warp_compact_lists<kGroupCap / 32>(a.lists + static_cast<int64_t>(pr) * kGroupCap, count, thresh, lane == 0,
+                                         a.k, hist[warp]);
+      count = __shfl_sync(RB_FULL_MASK, count, 0);
+    }
+    if (lane == 0) a.list_counts[pr] = count;
+  }
+}
+
+// Winners (slot, raw) -> (ids, scores): the slot's probe is the first j whose
+// head (or tail) range ends past the slot; binary search over the row's starts.
+__global__ void st_group_epilogue_kernel(const int64_t* __restrict__ slots, const float* __restrict__ raw, int k_sel,
+                                         const int64_t* __restrict__ probe, int P, const int64_t* __restrict__ offsets,
+                                         const int64_t* __restrict__ sizes, int64_t n_lists,
+                                         const int64_t* __restrict__ head, const int64_t* __restrict__ tail,
+                                         const int64_t* __restrict__ row_total, int width,
+                                         const int64_t* __restrict__ sort_perm, int64_t N,
+                                         const float* __restrict__ q_scales, const float* __restrict__ global_scale,
+                                         int divisor, int B, int k, int64_t* __restrict__ ids,
+                                         float* __restrict__ scores) {
+  const int64_t n = static_cast<int64_t>(B) * k;
+  const float gs = *global_scale;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = i / k;
+    const int jo = static_cast<int>(i - b * k);
+    int64_t id = -1;
+    float score = -INFINITY;
+    if (jo < k_sel && P > 0) {
+      const int64_t slot = slots[b * k_sel + jo];
+      const int64_t* hrow = head + b * P;
+      const int64_t* trow = tail + b * P;
+      const int64_t total_head = trow[0];
+      if (slot >= 0 && slot < width && slot < row_total[b]) {
+        const bool in_head = slot < total_head;
+        // smallest j whose range [start_j, start_{j+1}) ends past the slot
+        int lo = 0, hi = P - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          const int64_t end = in_head ? (mid + 1 < P ? hrow[mid + 1] : total_head)
+                                      : (mid + 1 < P ? trow[mid + 1] : row_total[b]);
+          if (end > slot) hi = mid; else lo = mid + 1;
+        }
+        int64_t start, len, full;
+        clipped_probe(offsets, sizes, n_lists, N, probe[b * P + lo], width, start, len, full);
+        const int64_t in_cluster = in_head ? slot - hrow[lo] : full + (slot - trow[lo]);
+        const int64_t p = start + in_cluster;
+        if (in_cluster >= 0 && in_cluster < len && p >= 0 && p < N) {
+          id = sort_perm[p];
+          const float r = raw[b * k_sel + jo];
+          const float qs = q_scales[b];
+          score = divisor == -1 ? __fmul_rn(__fmul_rn(r, qs), gs)
+                                : __fmul_rn(r, __fmul_rn(__fmul_rn(qs, static_cast<float>(divisor)), gs));
+        }
+      }
+    }
+    ids[i] = id;
+    scores[i] = score;
+  }
+}
+
 }  // namespace rb
 
 using namespace rb;
@@ -426,6 +760,156 @@ int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int
   const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
   st_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, k_sel, pos, counts, width, sort_perm, N, q_scales, global_scale,
                                           divisor_for_int8, B, k, out_ids, out_scores);
+  return launch_status();
+}
+
+// Workspace of the grouped path: q codes [B, D] | q scales [B] | cnt, fill [L] int |
+// cpo, ctask [L + 1] | pairs [B P] int32 | head, tail [B P] | row totals [B] |
+// lists [B P, kGroupCap] | list counts [B P] | winner slots, raw [B, k_sel].
+struct GroupWs {
+  size_t codes, scales, cnt, fill, cpo, ctask, pairs, head, tail, total, lists, lcounts, slots, raw, bytes;
+};
+
+static GroupWs group_ws_layout(int B, int D, int P, int64_t n_lists, int k_sel) {
+  GroupWs w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align_up(bytes, 256);
+    return at;
+  };
+  const size_t pairs = static_cast<size_t>(B) * P;
+  w.codes = take(static_cast<size_t>(B) * D);
+  w.scales = take(static_cast<size_t>(B) * sizeof(float));
+  w.cnt = take(static_cast<size_t>(n_lists) * sizeof(int));
+  w.fill = take(static_cast<size_t>(n_lists) * sizeof(int));
+  w.cpo = take(static_cast<size_t>(n_lists + 1) * sizeof(int64_t));
+  w.ctask = take(static_cast<size_t>(n_lists + 1) * sizeof(int64_t));
+  w.pairs = take(pairs * sizeof(int32_t));
+  w.head = take(pairs * sizeof(int64_t));
+  w.tail = take(pairs * sizeof(int64_t));
+  w.total = take(static_cast<size_t>(B) * sizeof(int64_t));
+  w.lists = take(pairs * kGroupCap * sizeof(uint2));
+  w.lcounts = take(pairs * sizeof(int));
+  w.slots = take(static_cast<size_t>(B) * k_sel * sizeof(int64_t));
+  w.raw = take(static_cast<size_t>(B) * k_sel * sizeof(float));
+  w.bytes = off;
+  return w;
+}
+
+int rb_st_search_grouped_workspace_size(int B, int D, int P, int64_t n_lists, int k, int max_tensor_size_per_row,
+                                        size_t* bytes) {
+  if (bytes == nullptr || B < 0 || D <= 0 || P < 0 || n_lists < 0 || k < 1 || max_tensor_size_per_row < 0 ||
+      max_tensor_size_per_row > INT32_MAX - 31) {
+    set_last_error("st_search_grouped_workspace_size: bad arguments");
+    return RB_ERR_INVALID_ARG;
+  }
+  const int width = st_width(max_tensor_size_per_row);
+  *bytes = group_ws_layout(B, D, P, n_lists, std::min(k, width)).bytes;
+  return RB_OK;
+}
+
+int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                         const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                         const int8_t* item_codes, int64_t N, const int64_t* sort_perm, const float* global_scale,
+                         int k, int max_tensor_size_per_row, int divisor_for_int8, const int64_t* filtering_bit_mask,
+                         int64_t mask_words, const int32_t* item_clause_attrs, int64_t attr_rows, int64_t attr_docs,
+                         const int64_t* clause_slots, const uint8_t* clause_is_reverse,
+                         const int32_t* query_clause_attrs, int n_clauses, int64_t* out_ids, float* out_scores,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = st_check(B, D, P, n_lists, N, k, max_tensor_size_per_row, divisor_for_int8);
+  if (rc != RB_OK) return rc;
+  if (P > 1024 || static_cast<int64_t>(B) * P > INT32_MAX) {
+    set_last_error("st::search (grouped): more than 1024 probes a row or 2^31 (row, probe) pairs");
+    return RB_ERR_UNSUPPORTED;
+  }
+  if (filtering_bit_mask != nullptr && mask_words < 0) {
+    set_last_error("st::search: bad filtering_bit_mask width");
+    return RB_ERR_INVALID_ARG;
+  }
+  ExactArgs ex{nullptr, 0, 0, nullptr, nullptr, nullptr, 0};
+  if (query_clause_attrs != nullptr) {
+    if (filtering_bit_mask != nullptr) {
+      set_last_error("st::search takes one filter: the exact clauses or filtering_bit_mask");
+      return RB_ERR_INVALID_ARG;
+    }
+    if (item_clause_attrs == nullptr || clause_slots == nullptr || clause_is_reverse == nullptr || n_clauses < 0 ||
+        attr_rows < 0 || attr_docs < N) {
+      set_last_error("st::search: the exact filter needs item_clause_attrs [R, >= N], clause_slots and "
+                     "clause_is_reverse");
+      return RB_ERR_INVALID_ARG;
+    }
+    ex = ExactArgs{item_clause_attrs, attr_rows, attr_docs, clause_slots, clause_is_reverse, query_clause_attrs,
+                   n_clauses};
+  }
+  if (B == 0) return RB_OK;
+  const int width = st_width(max_tensor_size_per_row);
+  const int k_sel = std::min(k, width);
+  const GroupWs lay = group_ws_layout(B, D, P, n_lists, std::max(k_sel, 1));
+  if (workspace == nullptr || workspace_bytes < lay.bytes) {
+    set_last_error("st::search: workspace too small");
+    return RB_ERR_WORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int8_t* q_codes = reinterpret_cast<int8_t*>(ws + lay.codes);
+  float* q_scales = reinterpret_cast<float*>(ws + lay.scales);
+  rc = rb_quantize_int8(query, B, D, q_codes, q_scales, stream);
+  if (rc != RB_OK) return rc;
+  if (width == 0 || P == 0 || n_lists == 0) {
+    fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, s);
+    return launch_status();
+  }
+  int* cnt = reinterpret_cast<int*>(ws + lay.cnt);
+  int* fill = reinterpret_cast<int*>(ws + lay.fill);
+  int64_t* cpo = reinterpret_cast<int64_t*>(ws + lay.cpo);
+  int64_t* ctask = reinterpret_cast<int64_t*>(ws + lay.ctask);
+  int32_t* pairs = reinterpret_cast<int32_t*>(ws + lay.pairs);
+  int64_t* head = reinterpret_cast<int64_t*>(ws + lay.head);
+  int64_t* tail = reinterpret_cast<int64_t*>(ws + lay.tail);
+  int64_t* total = reinterpret_cast<int64_t*>(ws + lay.total);
+  uint2* lists = reinterpret_cast<uint2*>(ws + lay.lists);
+  int* lcounts = reinterpret_cast<int*>(ws + lay.lcounts);
+  int64_t* slots = reinterpret_cast<int64_t*>(ws + lay.slots);
+  float* raw = reinterpret_cast<float*>(ws + lay.raw);
+  const int64_t n_pairs = static_cast<int64_t>(B) * P;
+  const int G = group_pairs_per_task(D);
+  cudaMemsetAsync(cnt, 0, static_cast<size_t>(n_lists) * sizeof(int), s);
+  cudaMemsetAsync(fill, 0, static_cast<size_t>(n_lists) * sizeof(int), s);
+  cudaMemsetAsync(lcounts, 0, static_cast<size_t>(n_pairs) * sizeof(int), s);
+  const int pgrid = static_cast<int>(std::min<int64_t>((n_pairs + 255) / 256, 4096));
+  pair_count_kernel<<<pgrid, 256, 0, s>>>(probe_ids, n_pairs, n_lists, cnt);
+  cluster_scan_kernel<<<1, kExpandThreads, 0, s>>>(cnt, n_lists, G, cpo, ctask);
+  pair_scatter_kernel<<<pgrid, 256, 0, s>>>(probe_ids, n_pairs, n_lists, cpo, fill, pairs);
+  slot_starts_kernel<<<(B + 127) / 128, 128, 0, s>>>(probe_ids, B, P, cluster_offsets, cluster_sizes, n_lists, N,
+                                                      width, head, tail, total);
+  rc = launch_status();
+  if (rc != RB_OK) return rc;
+  const size_t smem = group_smem_bytes(D);
+  static bool smem_set = false;
+  if (!smem_set) {
+    // the largest tile (D = 1024) needs about 150 KB of the 227 KB a block may opt into
+    if (cudaFuncSetAttribute(ivf_group_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(group_smem_bytes(kMaxSearchD))) != cudaSuccess) {
+      set_last_error("st::search: cannot raise the grouped scan's shared memory limit");
+      return RB_ERR_CUDA;
+    }
+    smem_set = true;
+  }
+  const int64_t max_tasks = (n_pairs + G - 1) / G + std::min<int64_t>(n_lists, n_pairs);
+  GroupArgs ga{item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask,
+               head, tail, width, G, k_sel, divisor_for_int8, reinterpret_cast<const uint64_t*>(filtering_bit_mask),
+               mask_words, ex, lists, lcounts};
+  ivf_group_scan_kernel<<<static_cast<unsigned>(max_tasks), kGroupThreads, smem, s>>>(ga);
+  rc = launch_status();
+  if (rc != RB_OK) return rc;
+  rc = merge_lists(lists, lcounts, B, P, kGroupCap, k_sel, 0, slots, raw, nullptr, s);
+  if (rc != RB_OK) return rc;
+  const int64_t n = static_cast<int64_t>(B) * k;
+  const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
+  st_group_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, k_sel, probe_ids, P, cluster_offsets, cluster_sizes,
+                                                n_lists, head, tail, total, width, sort_perm, N, q_scales,
+                                                global_scale, divisor_for_int8, B, k, out_ids, out_scores);
   return launch_status();
 }
 

@@ -78,7 +78,21 @@ def _layout_args(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, clus
     return q, probe, offsets, sizes
 
 
-def search(
+def search(*args, **kwargs) -> tuple[Tensor, Tensor]:
+    """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``, scored row by row
+    (each row's probed positions expanded, then the int8 candidate scan)."""
+    return _search(False, *args, **kwargs)
+
+
+def search_grouped(*args, **kwargs) -> tuple[Tensor, Tensor]:
+    """``st::search`` with the scoring grouped by cluster (``rb_st_search_grouped``): the
+    same arguments and results; each probed cluster is read once per group of up to 64
+    probing rows. Up to 1024 probes a row."""
+    return _search(True, *args, **kwargs)
+
+
+def _search(
+    grouped: bool,
     query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor, item_codes: Tensor,
     sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int = -1,
     filtering_bit_mask: Tensor | None = None, bloom_index: Tensor | None = None,
@@ -87,9 +101,7 @@ def search(
     item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
     clause_is_reverse: Tensor | None = None, query_clause_attrs: Tensor | None = None,
 ) -> tuple[Tensor, Tensor]:
-    """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``.
-
-    Filters: a full-``N`` ``filtering_bit_mask``, or the exact clauses
+    """Filters: a full-``N`` ``filtering_bit_mask``, or the exact clauses
     (``item_clause_attrs``, ``clause_slots``, ``clause_is_reverse``,
     ``query_clause_attrs``). With bloom ``plans`` and the exact clauses together
     (the bloom with its exact recheck) the result is the exact filter's, since the
@@ -148,10 +160,14 @@ def search(
         return ids, scores
     lib = _lib.lib()
     nbytes = ctypes.c_size_t(0)
-    _call(lib.rb_st_search_workspace_size(b, d, p, k, int(max_tensor_size_per_row), ctypes.byref(nbytes)),
-          "st::search")
+    if grouped:
+        _call(lib.rb_st_search_grouped_workspace_size(b, d, p, sizes.numel(), k, int(max_tensor_size_per_row),
+                                                      ctypes.byref(nbytes)), "st::search")
+    else:
+        _call(lib.rb_st_search_workspace_size(b, d, p, k, int(max_tensor_size_per_row), ctypes.byref(nbytes)),
+              "st::search")
     ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
-    rc = lib.rb_st_search(
+    rc = (lib.rb_st_search_grouped if grouped else lib.rb_st_search)(
         _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), _ptr(item_codes),
         item_codes.shape[0], _ptr(perm), _ptr(gs), k, int(max_tensor_size_per_row), int(divisor_for_int8),
         _ptr(mask), mask_words,

@@ -330,3 +330,71 @@ def test_probe_prep_matches_oracle(d):
         assert got.shape == np.shape(ref) and np.array_equal(got, ref)
     codes, scales = knn.quantize_int8(q)
     assert np.array_equal(out[1].cpu().numpy(), scales)
+
+
+# --- the grouped scorer (rb_st_search_grouped) -----------------------------------------------
+
+
+def test_grouped_capi_checks_need_no_device():
+    lib = _lib.lib()
+    n = ctypes.c_size_t(0)
+    assert lib.rb_st_search_grouped_workspace_size(16, 128, 8, 1024, 32, 700, ctypes.byref(n)) == 0
+    assert n.value >= 16 * 8 * 256 * 8  # one 256-entry list per (row, probe)
+
+    def call(p=8, ws=None, ws_bytes=0):
+        return lib.rb_st_search_grouped(None, 4, 128, None, p, None, None, 16, None, 1000, None, None, 10, 256, -1,
+                                        None, 0, None, 0, 0, None, None, None, 0, None, None, ws, ws_bytes, None)
+
+    assert call(p=1500) == _lib.RB_ERR_UNSUPPORTED  # more than 1024 probes a row
+    assert call() == _lib.RB_ERR_WORKSPACE
+
+
+def _grouped(g, meta, **kw):
+    _st()
+    from retrieve_b200 import st
+
+    t = {k: torch.from_numpy(np.ascontiguousarray(g[k])).cuda()
+         for k in ("query", "probe", "offsets", "sizes", "codes", "sort_perm")}
+    ids, scores = st.search_grouped(t["query"], t["probe"], t["offsets"], t["sizes"], t["codes"], t["sort_perm"],
+                                    torch.from_numpy(g["gs"]).cuda(), meta["k"], meta["width"], **kw)
+    return ids.cpu().numpy(), scores.cpu().numpy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_grouped_equals_the_row_path_and_the_oracle(ci):
+    """Int32 and fp16 paths, the full-N mask and the exact clauses: bit for bit the
+    oracle (ties to the reference scorer's lower slot), hence the row path."""
+    g, meta = _case(ci)
+    args = (g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"], g["gs"], meta["k"],
+            meta["width"])
+    _assert_exact(*_grouped(g, meta), *ivf.search(*args))
+    _assert_exact(*_grouped(g, meta, divisor_for_int8=meta["div"]), *ivf.search(*args, divisor_for_int8=meta["div"]))
+    words = ivf.pack_mask_high_first(g["mask"])
+    _assert_exact(*_grouped(g, meta, filtering_bit_mask=torch.from_numpy(words).cuda()),
+                  *ivf.search(*args, filtering_bit_mask=words))
+    rng = np.random.default_rng(ci)
+    _, rev, _, slots, clause_slots, qq = _exact_inputs(rng, g["codes"].shape[0], meta["b"])
+    got = _grouped(g, meta, item_clause_attrs=torch.from_numpy(slots).cuda(),
+                   clause_slots=torch.from_numpy(clause_slots).cuda(), clause_is_reverse=torch.from_numpy(rev).cuda(),
+                   query_clause_attrs=torch.from_numpy(qq).cuda())
+    _assert_exact(*got, *ivf.search(*args, exact=(slots, clause_slots, rev, qq)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k", [1, 100, 224])
+def test_grouped_many_rows_per_cluster(k):
+    """More probing rows per cluster than one task holds (several tasks per cluster),
+    wide rows, D = 100 (the unaligned staging), D = 1024 (the largest tile) and ties."""
+    _st()
+    from retrieve_b200 import st
+
+    rng = np.random.default_rng(100 + k)
+    for d, n_lists, max_size, b, p in ((128, 8, 500, 200, 4), (100, 32, 90, 37, 8), (1024, 16, 70, 20, 3)):
+        q, probe, offsets, sizes, codes, perm, width = _layout(rng, n_lists, max_size, d, b, p)
+        codes[1::3] = codes[0]
+        gs = np.float32(0.0123)
+        t = [torch.from_numpy(x).cuda() for x in (q, probe, offsets, sizes, codes, perm)]
+        ids, scores = st.search_grouped(*t, torch.tensor(gs).cuda(), k, width)
+        _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), *ivf.search(q, probe, offsets, sizes, codes, perm, gs,
+                                                                          k, width))
