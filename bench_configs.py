@@ -403,13 +403,22 @@ def run_ivf(args, dev):
     width = int(sizes[probe0].sum(1).max()) + 32 * n_probe  # room for other batches' probe totals
     torch.cuda.synchronize()
 
+    from retrieve_b200 import st
+
     def step():
         probe = ops.dense_topk(qb, centroids, n_probe)[0]
         return torch.ops.st.search(q, probe, offsets, sizes, codes_sorted, perm, gs, k, width)
 
+    def step_grouped():
+        probe = ops.dense_topk(qb, centroids, n_probe)[0]
+        return st.search_grouped(q, probe, offsets, sizes, codes_sorted, perm, gs, k, width)
+
+    a, b_ = step(), step_grouped()
+    same = bool(torch.equal(a[0], b_[0]) and torch.equal(a[1], b_[1]))
     sampler = bench.ClockSampler(dev)
     sampler.start()
     ms, _ = _time(step, args.warmup, args.steps)
+    ms_grouped, _ = _time(step_grouped, args.warmup, args.steps)
     clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
     scored = float(sizes[probe0].sum())  # probed (query, item) pairs per batch
     hbm = _peaks().get("hbm_gbs", 6650.0)
@@ -420,6 +429,9 @@ def run_ivf(args, dev):
           {"workload": "SilverTorch IVF search (st::search semantics)", "n_items": n, "dim": d, "batch": b, "k": k,
            "n_lists": n_lists, "n_probe": n_probe, "max_tensor_size_per_row": width,
            "probed_pairs_per_batch": scored,
+           "scorer": "row path (the registered op)",
+           "grouped": {"queries_per_s": b / (ms_grouped / 1e3), "step_ms": ms_grouped,
+                       "identical_to_row_path": same},
            "corpus": "the C2 mixture, clustered by its nearest normalised centre, int8 with one global scale"},
           {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
            "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
