@@ -231,11 +231,8 @@ _LIBRARY = torch.library.Library("st", "FRAGMENT")
 
 
 def _defined(name: str) -> bool:
-    try:
-        torch._C._dispatch_find_schema_or_throw(f"st::{name}", "")
-        return True
-    except RuntimeError:
-        return False
+    """Whether a loaded library (the reference's CPU build, say) already defines ``st::<name>``."""
+    return hasattr(torch.ops.st, name)
 
 
 def _register() -> None:
