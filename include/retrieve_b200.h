@@ -369,7 +369,7 @@ RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, i
  * raw score, ties to the reference scorer's lower slot, id = sort_perm[pos],
  * score = (fp32(dot) * q_scale) * global_scale, or
  * raw * ((q_scale * divisor) * global_scale); -1 / -inf past the candidates.
- * Limits: D <= 1024, P <= 2048, B <= 65535, min(k, round_up(width, 32)) <= 224.
+ * Limits: D <= 1024, P <= 2048, B <= 65535, min(k, round_up(width, 32)) <= 1024.
  * The reference op's bloom-plan filter is not served here (with the exact
  * recheck the exact filter alone gives its result). Workspace from
  * rb_st_search_workspace_size.

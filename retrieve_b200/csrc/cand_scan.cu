@@ -124,8 +124,8 @@ __device__ __forceinline__ float hamming_score(const uint64_t* __restrict__ sq, 
 }
 
 // KIND 0: dot with query type QT and item type XT; KIND 1: hamming (int64 words);
-// KIND 2: int8 codes (QT = XT = int8_t).
-template <int KIND, typename QT, typename XT>
+// KIND 2: int8 codes (QT = XT = int8_t). CAP: list capacity (k <= CAP - 32).
+template <int KIND, typename QT, typename XT, int CAP = kCandCap>
 __global__ void __launch_bounds__(32 * kCandWarps) cand_scan_kernel(CandParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ uint32_t hist_all[kCandWarps][256];
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(32 * kCandWarps) cand_scan_kernel(CandParams p
   const int chunks = (cnt + 31) / 32;
   const int c_lo = static_cast<int>((static_cast<int64_t>(list_idx) * chunks) / p.n_lists);
   const int c_hi = static_cast<int>((static_cast<int64_t>(list_idx + 1) * chunks) / p.n_lists);
-  uint2* list = p.lists + (static_cast<size_t>(b) * p.n_lists + list_idx) * kCandCap;
+  uint2* list = p.lists + (static_cast<size_t>(b) * p.n_lists + list_idx) * CAP;
   int count = 0;
   float thresh = -INFINITY;
   const int64_t* prow = p.pos + static_cast<size_t>(b) * p.P;
@@ -178,9 +178,9 @@ __global__ void __launch_bounds__(32 * kCandWarps) cand_scan_kernel(CandParams p
     const bool pass = s >= thresh;
     const uint32_t bal = __ballot_sync(RB_FULL_MASK, pass);
     if (bal) {
-      if (count > kCandCap - 32) {
+      if (count > CAP - 32) {
         // lane 0 holds the list; all lanes keep identical copies of its state
-        warp_compact_lists<kCandCap / 32>(list, count, thresh, lane == 0, p.k, hist_all[warp]);
+        warp_compact_lists<CAP / 32>(list, count, thresh, lane == 0, p.k, hist_all[warp]);
         count = __shfl_sync(RB_FULL_MASK, count, 0);
         thresh = __shfl_sync(RB_FULL_MASK, thresh, 0);
       }
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(32 * kCandWarps) cand_scan_kernel(CandParams p
     }
   }
   if (count > p.k) {
-    warp_compact_lists<kCandCap / 32>(list, count, thresh, lane == 0, p.k, hist_all[warp]);
+    warp_compact_lists<CAP / 32>(list, count, thresh, lane == 0, p.k, hist_all[warp]);
     count = __shfl_sync(RB_FULL_MASK, count, 0);
   }
   if (lane == 0) p.list_counts[static_cast<size_t>(b) * p.n_lists + list_idx] = count;
@@ -344,24 +344,36 @@ static size_t cand_ws_bytes(int B, int P) {
          align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
 }
 
-size_t cand_i8_ws_bytes(int B, int P) { return cand_ws_bytes(B, P); }
+// The int8 scan's list capacity: 256 entries up to k = 224, 1280 (40 a lane) up to k = 1024.
+constexpr int kCandCapLarge = 1280;
+static int cand_i8_cap(int k) { return k <= kCandCap - 32 ? kCandCap : kCandCapLarge; }
 
-int cand_i8_max_k() { return kCandCap - 32; }
+size_t cand_i8_ws_bytes(int B, int P, int k) {
+  const CandPlan pl = cand_plan(B, P);
+  return align_up(static_cast<size_t>(B) * pl.n_lists * cand_i8_cap(k) * sizeof(uint2), 256) +
+         align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
+}
+
+int cand_i8_max_k() { return 1024; }
 
 int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const int64_t* pos, int P,
                  const int64_t* counts, int B, int k, int divisor, int64_t* out_slots, float* out_raw, void* workspace,
                  cudaStream_t s) {
   const CandPlan pl = cand_plan(B, P);
+  const int cap = cand_i8_cap(k);
   uint2* lists = static_cast<uint2*>(workspace);
   int* lcounts = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
-                                        align_up(static_cast<size_t>(B) * pl.n_lists * kCandCap * sizeof(uint2), 256));
+                                        align_up(static_cast<size_t>(B) * pl.n_lists * cap * sizeof(uint2), 256));
   CandParams prm{q_codes, items, pos, counts, B, P, D, N, k, lists, lcounts, pl.n_lists, divisor};
   const dim3 grid(pl.ctas_per_query, B);
   const size_t smem = align_up(static_cast<size_t>(D), 16);
-  cand_scan_kernel<2, int8_t, int8_t><<<grid, 32 * kCandWarps, smem, s>>>(prm);
+  if (cap == kCandCap)
+    cand_scan_kernel<2, int8_t, int8_t, kCandCap><<<grid, 32 * kCandWarps, smem, s>>>(prm);
+  else
+    cand_scan_kernel<2, int8_t, int8_t, kCandCapLarge><<<grid, 32 * kCandWarps, smem, s>>>(prm);
   const int rc = check_launch();
   if (rc != RB_OK) return rc;
-  return merge_lists(lists, lcounts, B, pl.n_lists, kCandCap, k, 0, out_slots, out_raw, nullptr, s);
+  return merge_lists(lists, lcounts, B, pl.n_lists, cap, k, 0, out_slots, out_raw, nullptr, s);
 }
 
 // Hamming full-scan plan

@@ -308,7 +308,7 @@ static StWs st_ws_layout(int B, int D, int width, int k_sel) {
   w.counts = take(static_cast<size_t>(B) * sizeof(int64_t));
   w.slots = take(static_cast<size_t>(B) * k_sel * sizeof(int64_t));
   w.raw = take(static_cast<size_t>(B) * k_sel * sizeof(float));
-  w.cand = take(cand_i8_ws_bytes(B, width));
+  w.cand = take(cand_i8_ws_bytes(B, width, k_sel));
   w.total = off;
   return w;
 }
@@ -341,7 +341,7 @@ static int st_check(int B, int D, int P, int64_t n_lists, int64_t N, int k, int 
   }
   const int k_sel = std::min(k, st_width(max_tensor_size_per_row));
   if (k_sel > cand_i8_max_k()) {
-    set_last_error("st::search: min(k, padded width) > 224 is not supported");
+    set_last_error("st::search: min(k, padded width) > 1024 is not supported");
     return RB_ERR_UNSUPPORTED;
   }
   return RB_OK;
@@ -371,7 +371,10 @@ static int st_check(int B, int D, int P, int64_t n_lists, int64_t N, int k, int 
 constexpr int kGroupThreads = 256;
 constexpr int kGroupWarps = kGroupThreads / 32;
 constexpr int kGroupTile = 128;  // cluster rows staged per step: 4 per lane
-constexpr int kGroupCap = 256;   // candidate-list capacity per (row, probe)
+// candidate-list capacity per (row, probe): 256 entries up to k = 224, 1280 up to k = 1024
+constexpr int kGroupCap = 256;
+constexpr int kGroupCapLarge = 1280;
+static int group_cap(int k) { return k <= kGroupCap - 32 ? kGroupCap : kGroupCapLarge; }
 constexpr int kGroupMaxPairs = 64;
 
 static int group_pairs_per_task(int D) {
@@ -490,10 +493,11 @@ struct GroupArgs {
   const uint64_t* mask;
   int64_t mask_words;
   ExactArgs ex;
-  uint2* lists;      // [B * P, kGroupCap]
+  uint2* lists;      // [B * P, CAP]
   int* list_counts;  // [B * P]
 };
 
+template <int CAP>
 __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs a) {
   extern __shared__ __align__(16) uint8_t gsm[];
   __shared__ uint32_t hist[kGroupWarps][256];
@@ -556,7 +560,7 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
       const int64_t b = pr / a.P;
       int count = s_count[g];
       float thresh = s_thresh[g];
-      uint2* list = a.lists + static_cast<int64_t>(pr) * kGroupCap;
+      uint2* list = a.lists + static_cast<int64_t>(pr) * CAP;
       const int64_t hs = a.head[pr], ts = a.tail[pr];
       const int4* q = reinterpret_cast<const int4*>(sq + g * dp);
       const uint64_t* mrow = a.mask ? a.mask + b * a.mask_words : nullptr;
@@ -593,8 +597,8 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
         }
         const bool pass = s >= thresh;
         if (__ballot_sync(RB_FULL_MASK, pass)) {
-          if (count > kGroupCap - 32) {
-            warp_compact_lists<kGroupCap / 32>(list, count, thresh, lane == 0, a.k, hist[warp]);
+          if (count > CAP - 32) {
+            warp_compact_lists<CAP / 32>(list, count, thresh, lane == 0, a.k, hist[warp]);
             count = __shfl_sync(RB_FULL_MASK, count, 0);
             thresh = __shfl_sync(RB_FULL_MASK, thresh, 0);
           }
@@ -618,7 +622,7 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
     int count = s_count[g];
     float thresh = s_thresh[g];
     if (count > a.k) {
-      warp_compact_lists<kGroupCap / 32>(a.lists + static_cast<int64_t>(pr) * kGroupCap, count, thresh, lane == 0,
+      warp_compact_lists<CAP / 32>(a.lists + static_cast<int64_t>(pr) * CAP, count, thresh, lane == 0,
                                          a.k, hist[warp]);
       count = __shfl_sync(RB_FULL_MASK, count, 0);
     }
@@ -765,7 +769,7 @@ int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int
 
 // Workspace of the grouped path: q codes [B, D] | q scales [B] | cnt, fill [L] int |
 // cpo, ctask [L + 1] | pairs [B P] int32 | head, tail [B P] | row totals [B] |
-// lists [B P, kGroupCap] | list counts [B P] | winner slots, raw [B, k_sel].
+// lists [B P, cap] | list counts [B P] | winner slots, raw [B, k_sel].
 struct GroupWs {
   size_t codes, scales, cnt, fill, cpo, ctask, pairs, head, tail, total, lists, lcounts, slots, raw, bytes;
 };
@@ -789,7 +793,7 @@ static GroupWs group_ws_layout(int B, int D, int P, int64_t n_lists, int k_sel) 
   w.head = take(pairs * sizeof(int64_t));
   w.tail = take(pairs * sizeof(int64_t));
   w.total = take(static_cast<size_t>(B) * sizeof(int64_t));
-  w.lists = take(pairs * kGroupCap * sizeof(uint2));
+  w.lists = take(pairs * group_cap(k_sel) * sizeof(uint2));
   w.lcounts = take(pairs * sizeof(int));
   w.slots = take(static_cast<size_t>(B) * k_sel * sizeof(int64_t));
   w.raw = take(static_cast<size_t>(B) * k_sel * sizeof(float));
@@ -889,8 +893,11 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   static bool smem_set = false;
   if (!smem_set) {
     // the largest tile (D = 1024) needs about 150 KB of the 227 KB a block may opt into
-    if (cudaFuncSetAttribute(ivf_group_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(group_smem_bytes(kMaxSearchD))) != cudaSuccess) {
+    const int most = static_cast<int>(group_smem_bytes(kMaxSearchD));
+    if (cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap>, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             most) != cudaSuccess) {
       set_last_error("st::search: cannot raise the grouped scan's shared memory limit");
       return RB_ERR_CUDA;
     }
@@ -900,10 +907,13 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   GroupArgs ga{item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask,
                head, tail, width, G, k_sel, divisor_for_int8, reinterpret_cast<const uint64_t*>(filtering_bit_mask),
                mask_words, ex, lists, lcounts};
-  ivf_group_scan_kernel<<<static_cast<unsigned>(max_tasks), kGroupThreads, smem, s>>>(ga);
+  if (group_cap(k_sel) == kGroupCap)
+    ivf_group_scan_kernel<kGroupCap><<<static_cast<unsigned>(max_tasks), kGroupThreads, smem, s>>>(ga);
+  else
+    ivf_group_scan_kernel<kGroupCapLarge><<<static_cast<unsigned>(max_tasks), kGroupThreads, smem, s>>>(ga);
   rc = launch_status();
   if (rc != RB_OK) return rc;
-  rc = merge_lists(lists, lcounts, B, P, kGroupCap, k_sel, 0, slots, raw, nullptr, s);
+  rc = merge_lists(lists, lcounts, B, P, group_cap(k_sel), k_sel, 0, slots, raw, nullptr, s);
   if (rc != RB_OK) return rc;
   const int64_t n = static_cast<int64_t>(B) * k;
   const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));

@@ -58,7 +58,7 @@ void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stre
 // table; a negative position is never scored), ranked on the raw score
 // fp32(dot) (divisor -1) or fp16(dot / divisor), ties to the lower slot.
 // Writes the winners' slots and raw scores, -1 / -inf past the candidates.
-size_t cand_i8_ws_bytes(int B, int P);
+size_t cand_i8_ws_bytes(int B, int P, int k);
 int cand_i8_max_k();
 int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const int64_t* pos, int P,
                  const int64_t* counts, int B, int k, int divisor, int64_t* out_slots, float* out_raw, void* workspace,

@@ -149,8 +149,9 @@ def test_capi_argument_checks_need_no_device():
 
     assert call(d=2048) == _lib.RB_ERR_UNSUPPORTED  # D > 1024
     assert call(p=4096) == _lib.RB_ERR_UNSUPPORTED  # more than 2048 probes
-    assert call(k=300) == _lib.RB_ERR_UNSUPPORTED  # min(k, width) > 224
+    assert call(k=2000, width=2048) == _lib.RB_ERR_UNSUPPORTED  # min(k, width) > 1024
     assert call(k=300, width=200) == _lib.RB_ERR_WORKSPACE  # min(300, 224) fits; then the workspace check
+    assert call(k=1000, width=2048) == _lib.RB_ERR_WORKSPACE  # large k: the 1280-entry lists
     assert call(div=0) == _lib.RB_ERR_INVALID_ARG
     assert call(b=-1) == _lib.RB_ERR_INVALID_ARG
     assert call(b=70000) == _lib.RB_ERR_UNSUPPORTED
@@ -274,7 +275,7 @@ def _layout(rng, n_lists, max_size, d, b, p):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("k", [1, 100, 224])
+@pytest.mark.parametrize("k", [1, 100, 224, 225, 1000])
 def test_search_wide_rows_and_edge_shapes(k):
     """Wide rows (many warps of candidates per list), D not a multiple of 16 (scalar
     dot), empty clusters, k above the probed count (pads), and ties from repeated
@@ -382,7 +383,7 @@ def test_grouped_equals_the_row_path_and_the_oracle(ci):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("k", [1, 100, 224])
+@pytest.mark.parametrize("k", [1, 100, 224, 225, 1000])
 def test_grouped_many_rows_per_cluster(k):
     """More probing rows per cluster than one task holds (several tasks per cluster),
     wide rows, D = 100 (the unaligned staging), D = 1024 (the largest tile) and ties."""
