@@ -346,6 +346,48 @@ RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, i
                           void* stream);
 
 /*
+ * The filter of one st::search call: at most one of the three groups is set (NULL
+ * pointers for the others), or pass a NULL rb_st_filter* for none.
+ *   filtering_bit_mask [B, mask_words] int64 over sorted positions, high bit first
+ *     (position d at bit 63 - d % 64 of word d / 64);
+ *   the exact clauses (silvertorch/ops/csrc/fork_filters.cuh:15-41): item_clause_attrs
+ *     int32 [attr_rows, attr_docs >= N] (clause c in rows clause_slots[c] ..
+ *     clause_slots[c + 1], each doc's values sorted descending, -1 pads), clause_slots
+ *     int64 [n_clauses + 1], clause_is_reverse bool [n_clauses], query_clause_attrs
+ *     int32 [B, n_clauses] (-1: clause inactive);
+ *   SilverTorch's bloom (bloom_index_search_cuda.cu:304-349, 469-544): bloom_index int64
+ *     [bloom_words] bundle-major, bundle_b_offsets int64 [n_bundles + 1], plans int64
+ *     [plan_words] (per slot the parser's eight byte offsets, then its data;
+ *     retrieve/src/retrieve/ops/official/adapter.py:212-236), plan_count slots,
+ *     max_stack_size (<= 16), query_plan_index int64 [B] or NULL (row b: plan b),
+ *     bloom_k distinct positions (<= 10) among hash_k stored hashes a term.
+ * With the bloom and its exact recheck (both in the reference op) pass the exact
+ * clauses only: the bloom has no false negatives, so the result is the same.
+ */
+typedef struct rb_st_filter {
+  const int64_t* filtering_bit_mask;
+  int64_t mask_words;
+  const int32_t* item_clause_attrs;
+  int64_t attr_rows;
+  int64_t attr_docs;
+  const int64_t* clause_slots;
+  const uint8_t* clause_is_reverse;
+  const int32_t* query_clause_attrs;
+  int n_clauses;
+  const int64_t* bloom_index;
+  int64_t bloom_words;
+  const int64_t* bundle_b_offsets;
+  int64_t n_bundles;
+  const int64_t* plans;
+  int64_t plan_words;
+  int plan_count;
+  int max_stack_size;
+  const int64_t* query_plan_index;
+  int bloom_k;
+  int hash_k;
+} rb_st_filter;
+
+/*
  * SilverTorch's IVF probe search, replacing the CUDA impl of
  *   st::search(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes,
  *              Tensor item_codes, Tensor sort_perm, Tensor global_scale, int k,
@@ -355,34 +397,22 @@ RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, i
  *   query [B, D] fp32; probe_ids [B, P] int64 cluster ids; cluster_offsets
  *   [n_lists + 1] int64; cluster_sizes [n_lists] int64; item_codes [N, D] int8,
  *   cluster-sorted; sort_perm [N] int64 (sorted position -> item id);
- *   global_scale: one fp32 on the device; filtering_bit_mask [B, mask_words]
- *   int64 over sorted positions, high bit first (position d at bit 63 - d % 64
- *   of word d / 64), or NULL; divisor_for_int8 -1 (rank on the int32 dot) or a
- *   positive divisor (rank on fp16(dot / divisor)).
- *   Exact clause filter (silvertorch/ops/csrc/fork_filters.cuh:15-41), or NULLs:
- *   item_clause_attrs int32 [attr_rows, attr_docs >= N] (clause c in rows
- *   clause_slots[c] .. clause_slots[c + 1], each doc's values sorted descending,
- *   -1 pads), clause_slots int64 [n_clauses + 1], clause_is_reverse bool
- *   [n_clauses], query_clause_attrs int32 [B, n_clauses] (-1: clause inactive).
- *   The mask and the exact filter exclude each other.
+ *   global_scale: one fp32 on the device; divisor_for_int8 -1 (rank on the int32
+ *   dot) or a positive divisor (rank on fp16(dot / divisor)); filter: see rb_st_filter.
  * Output (ids int64 [B, k], scores fp32 [B, k]): the k best probed positions by
  * raw score, ties to the reference scorer's lower slot, id = sort_perm[pos],
  * score = (fp32(dot) * q_scale) * global_scale, or
  * raw * ((q_scale * divisor) * global_scale); -1 / -inf past the candidates.
  * Limits: D <= 1024, P <= 2048, B <= 65535, min(k, round_up(width, 32)) <= 1024.
- * The reference op's bloom-plan filter is not served here (with the exact
- * recheck the exact filter alone gives its result). Workspace from
- * rb_st_search_workspace_size.
+ * Workspace from rb_st_search_workspace_size.
  */
 RB_API int rb_st_search_workspace_size(int B, int D, int P, int k, int max_tensor_size_per_row, size_t* bytes);
 RB_API int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P,
                         const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
                         const int8_t* item_codes, int64_t N, const int64_t* sort_perm, const float* global_scale, int k,
-                        int max_tensor_size_per_row, int divisor_for_int8, const int64_t* filtering_bit_mask,
-                        int64_t mask_words, const int32_t* item_clause_attrs, int64_t attr_rows,
-                        int64_t attr_docs, const int64_t* clause_slots, const uint8_t* clause_is_reverse,
-                        const int32_t* query_clause_attrs, int n_clauses, int64_t* out_ids, float* out_scores,
-                        void* workspace, size_t workspace_bytes, void* stream);
+                        int max_tensor_size_per_row, int divisor_for_int8, const rb_st_filter* filter,
+                        int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                        void* stream);
 
 /*
  * The same search, grouped by cluster: every (row, probe) pair is filed under its
@@ -397,11 +427,8 @@ RB_API int rb_st_search_grouped(const float* query, int B, int D, const int64_t*
                                 const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
                                 const int8_t* item_codes, int64_t N, const int64_t* sort_perm,
                                 const float* global_scale, int k, int max_tensor_size_per_row, int divisor_for_int8,
-                                const int64_t* filtering_bit_mask, int64_t mask_words,
-                                const int32_t* item_clause_attrs, int64_t attr_rows, int64_t attr_docs,
-                                const int64_t* clause_slots, const uint8_t* clause_is_reverse,
-                                const int32_t* query_clause_attrs, int n_clauses, int64_t* out_ids,
-                                float* out_scores, void* workspace, size_t workspace_bytes, void* stream);
+                                const rb_st_filter* filter, int64_t* out_ids, float* out_scores, void* workspace,
+                                size_t workspace_bytes, void* stream);
 
 /*
  * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)

@@ -222,3 +222,91 @@ def probe_prep(query, probe_ids, cluster_offsets, cluster_sizes):
     rem_cumsum = np.cumsum((length % WARP).reshape(-1), dtype=np.int32)
     warp_cumsum = np.cumsum(warps, dtype=np.int32)
     return codes, scales, probe, length, offsets[probe], warps, rounded_cumsum, rem_cumsum, warp_cumsum
+
+
+# ---------------------------------------------------------------------------
+# SilverTorch's bloom filter (the ``plans`` of st::search without the exact recheck)
+# ---------------------------------------------------------------------------
+BUNDLE_COLUMNS = 32  # 64-doc columns per bundle: 2048 docs (silvertorch bloom_index_util.h:44-46)
+OP_AND, OP_OR, OP_NOT, OP_TERM, OP_EMPTY = 1, 2, 3, 4, 5  # bloom_index_util.h:50-57
+
+
+def decode_plan(data, offsets, p):
+    """Plan ``p`` of the parser's encoding (bloom_index_util.cpp:82-125): eight byte
+    offsets per plan into ``data``, giving its operators (uint8), the operators'
+    parameter offsets (int32), the parameters (int32) and the terms' stored hashes
+    (uint64, ``hash_k`` a term)."""
+    raw = np.asarray(data).view(np.uint8)
+    o = np.asarray(offsets, dtype=np.int64)[8 * p : 8 * p + 8]
+    ops = raw[o[0] : o[1]].copy()
+    op_offsets = raw[o[2] : o[3]].copy().view(np.int32)
+    hashes = raw[o[6] : o[7]].copy().view(np.uint64)
+    return ops, op_offsets, hashes
+
+
+def plan_blob(data, offsets, slots):
+    """The prepared-plan blob st::search reads (adapter.py:212-236): int64 words, the
+    parser's eight offsets of each plan first (``8 * slots`` words), then the data."""
+    offsets = np.asarray(offsets, dtype=np.int64)
+    raw = np.asarray(data).view(np.uint8)
+    words = 8 * slots + (len(raw) + 7) // 8
+    blob = np.zeros(words, dtype=np.int64)
+    blob[: len(offsets)] = offsets
+    blob.view(np.uint8)[8 * 8 * slots : 8 * 8 * slots + len(raw)] = raw
+    return blob
+
+
+def bloom_plan_mask(bloom_index, bundle_b_offsets, data, offsets, p, k, hash_k, n):
+    """Docs ``[0, n)`` passing plan ``p`` (bloom_index_search_cuda.cu:304-349, 469-544):
+    per 64-doc column word, a term ANDs the index rows of its first ``k`` distinct
+    positions ``hash % B`` among its ``hash_k`` stored hashes (``B`` the bits of the
+    doc's 2048-doc bundle); the operators run as a postfix stack (AND / OR over as many
+    children as their parameter range holds, NOT, EMPTY = all); doc ``d`` is bit
+    ``63 - d % 64`` of its column's word."""
+    index = np.asarray(bloom_index, dtype=np.int64).view(np.uint64)
+    boff = np.asarray(bundle_b_offsets, dtype=np.int64)
+    ops, op_offsets, hashes = decode_plan(data, offsets, p)
+    n_cols = (n + 63) // 64
+    cols = np.arange(n_cols)
+    bundle = cols // BUNDLE_COLUMNS
+    b0 = boff[bundle]
+    b_bits = (boff[bundle + 1] - b0).astype(np.uint64)
+    in_bundle = cols % BUNDLE_COLUMNS
+    full = np.uint64(0xFFFFFFFFFFFFFFFF)
+
+    def term_words(t):
+        h = hashes[t * hash_k : (t + 1) * hash_k]
+        out = np.full(n_cols, full, dtype=np.uint64)
+        for ci in range(n_cols):
+            used = []
+            for x in h:
+                if len(used) == k:
+                    break
+                pos = int(x % b_bits[ci])
+                if pos not in used:
+                    used.append(pos)
+            w = full
+            for pos in used:
+                w &= index[(b0[ci] + pos) * BUNDLE_COLUMNS + in_bundle[ci]]
+            out[ci] = w
+        return out
+
+    stack = []
+    term = 0
+    for j, op in enumerate(ops.tolist()):
+        if op == OP_TERM:
+            stack.append(term_words(term))
+            term += 1
+        elif op in (OP_AND, OP_OR):
+            children = int(op_offsets[j + 1] - op_offsets[j])
+            acc = np.full(n_cols, full if op == OP_AND else 0, dtype=np.uint64)
+            for _ in range(children):
+                acc = (acc & stack.pop()) if op == OP_AND else (acc | stack.pop())
+            stack.append(acc)
+        elif op == OP_NOT:
+            stack.append(~stack.pop())
+        elif op == OP_EMPTY:
+            stack.append(np.full(n_cols, full, dtype=np.uint64))
+    words = stack.pop()
+    d = np.arange(n)
+    return ((words[d // 64] >> (np.uint64(63) - (d % 64).astype(np.uint64))) & np.uint64(1)).astype(bool)

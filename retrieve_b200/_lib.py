@@ -30,6 +30,19 @@ _c_i64 = ctypes.c_int64
 _c_size = ctypes.c_size_t
 _vp = ctypes.c_void_p
 
+class StFilter(ctypes.Structure):
+    """``rb_st_filter`` of include/retrieve_b200.h: at most one of the three filters."""
+
+    _fields_ = [
+        ("filtering_bit_mask", _vp), ("mask_words", _c_i64),
+        ("item_clause_attrs", _vp), ("attr_rows", _c_i64), ("attr_docs", _c_i64), ("clause_slots", _vp),
+        ("clause_is_reverse", _vp), ("query_clause_attrs", _vp), ("n_clauses", _c_int),
+        ("bloom_index", _vp), ("bloom_words", _c_i64), ("bundle_b_offsets", _vp), ("n_bundles", _c_i64),
+        ("plans", _vp), ("plan_words", _c_i64), ("plan_count", _c_int), ("max_stack_size", _c_int),
+        ("query_plan_index", _vp), ("bloom_k", _c_int), ("hash_k", _c_int),
+    ]  # fmt: skip
+
+
 # name -> (restype, argtypes); mirrors include/retrieve_b200.h
 _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_last_error": (ctypes.c_char_p, []),
@@ -66,16 +79,16 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_st_search_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
     "rb_st_search": (
         _c_int,
-        [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int, _c_int, _vp,
-         _c_i64, _vp, _c_i64, _c_i64, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _c_size, _vp],
+        [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int, _c_int,
+         ctypes.POINTER(StFilter), _vp, _vp, _vp, _c_size, _vp],
     ),
     "rb_st_search_grouped_workspace_size": (
         _c_int, [_c_int, _c_int, _c_int, _c_i64, _c_int, _c_int, ctypes.POINTER(_c_size)]
     ),
     "rb_st_search_grouped": (
         _c_int,
-        [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int, _c_int, _vp,
-         _c_i64, _vp, _c_i64, _c_i64, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _c_size, _vp],
+        [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_int, _c_int, _c_int,
+         ctypes.POINTER(StFilter), _vp, _vp, _vp, _c_size, _vp],
     ),
     "rb_st_probe_prep": (
         _c_int,

@@ -90,6 +90,127 @@ __device__ __forceinline__ bool exact_pass(const ExactArgs& ex, const int32_t* _
   return true;
 }
 
+// SilverTorch's bloom filter on its own index and prepared plans (the op's `plans`
+// without the exact recheck; bloom_index_search_cuda.cu:304-349, 469-544). The index
+// is bundle-major: docs in bundles of 2048 (32 columns of 64), bundle i holding
+// B_i = bundle_b_offsets[i + 1] - bundle_b_offsets[i] bit rows; doc d's bit of row r is
+// bit 63 - d % 64 of word (bundle_b_offsets[d / 2048] + r) * 32 + (d / 64) % 32. The
+// plans blob holds, per plan slot, the parser's eight byte offsets (operators uint8,
+// their parameter offsets int32, parameters int32, stored hashes uint64) into the data
+// after the 8 * slots header words. A plan runs as a postfix stack over the doc's
+// column word: a term ANDs the rows of its first k distinct positions hash % B_i among
+// its hash_k hashes; AND / OR fold as many entries as their parameter range holds;
+// NOT complements; EMPTY is all ones. Every offset and index is checked against the
+// sizes passed in; a malformed plan fails the doc.
+constexpr int kBloomMaxK = 10;    // MAX_K_V2
+constexpr int kBloomStack = 16;   // deepest plan stack served
+constexpr int kBundleColumns = 32;
+
+struct BloomArgs {
+  const uint64_t* index;  // null: no bloom filter
+  int64_t index_words;
+  const int64_t* bundle_offsets;  // [n_bundles + 1]
+  int64_t n_bundles;
+  const int64_t* blob;
+  int64_t blob_words;
+  int slots;
+  const int64_t* plan_index;  // [B], or null: row b runs plan b
+  int k, hash_k;
+};
+
+__device__ bool bloom_pass(const BloomArgs& a, int64_t row, int64_t doc) {
+  const int64_t p = a.plan_index ? a.plan_index[row] : row;
+  if (p < 0 || p >= a.slots) return false;
+  const int64_t data_bytes = (a.blob_words - 8 * static_cast<int64_t>(a.slots)) * 8;
+  int64_t o[8];
+  for (int i = 0; i < 8; ++i) o[i] = a.blob[8 * p + i];
+  for (int i = 0; i < 8; i += 2)
+    if (o[i] < 0 || o[i] > o[i + 1] || o[i + 1] > data_bytes) return false;
+  if ((o[2] & 3) || (o[6] & 7)) return false;
+  const uint8_t* data = reinterpret_cast<const uint8_t*>(a.blob + 8 * static_cast<int64_t>(a.slots));
+  const uint8_t* ops = data + o[0];
+  const int64_t n_ops = o[1] - o[0];
+  const int32_t* op_off = reinterpret_cast<const int32_t*>(data + o[2]);
+  const int64_t n_off = (o[3] - o[2]) / 4;
+  const uint64_t* hashes = reinterpret_cast<const uint64_t*>(data + o[6]);
+  const int64_t n_hash = (o[7] - o[6]) / 8;
+  const int64_t column = doc >> 6;
+  const int64_t bundle = column / kBundleColumns;
+  if (bundle >= a.n_bundles) return false;
+  const int64_t b0 = a.bundle_offsets[bundle];
+  const int64_t bb = a.bundle_offsets[bundle + 1] - b0;
+  if (bb <= 0) return false;
+  const int64_t col = column % kBundleColumns;
+  uint64_t stack[kBloomStack];
+  int sp = 0;
+  int64_t term = 0;
+  for (int64_t j = 0; j < n_ops; ++j) {
+    const uint8_t op = ops[j];
+    if (op == 4) {  // TERM
+      uint64_t w = ~0ull;
+      if ((term + 1) * a.hash_k > n_hash) {
+        w = 0;
+      } else {
+        const uint64_t* h = hashes + term * a.hash_k;
+        int64_t used[kBloomMaxK];
+        int resolved = 0;
+        for (int q = 0; q < a.hash_k && resolved < a.k; ++q) {
+          const int64_t pos = static_cast<int64_t>(h[q] % static_cast<uint64_t>(bb));
+          bool dup = false;
+          for (int i = 0; i < resolved; ++i) dup |= used[i] == pos;
+          if (!dup) used[resolved++] = pos;
+        }
+        for (int i = 0; i < resolved; ++i) {
+          const int64_t wi = (b0 + used[i]) * kBundleColumns + col;
+          w &= (wi >= 0 && wi < a.index_words) ? a.index[wi] : 0ull;
+        }
+      }
+      ++term;
+      if (sp < kBloomStack) stack[sp++] = w; else return false;
+    } else if (op == 1 || op == 2) {  // AND, OR
+      const int64_t children = j + 1 < n_off ? static_cast<int64_t>(op_off[j + 1]) - op_off[j] : 0;
+      uint64_t acc = op == 1 ? ~0ull : 0ull;
+      for (int64_t i = 0; i < children; ++i) {
+        if (sp == 0) return false;
+        const uint64_t v = stack[--sp];
+        acc = op == 1 ? (acc & v) : (acc | v);
+      }
+      if (sp < kBloomStack) stack[sp++] = acc; else return false;
+    } else if (op == 3) {  // NOT
+      if (sp == 0) return false;
+      stack[sp - 1] = ~stack[sp - 1];
+    } else if (op == 5) {  // EMPTY
+      if (sp < kBloomStack) stack[sp++] = ~0ull; else return false;
+    }
+  }
+  if (sp == 0) return false;
+  return (stack[sp - 1] >> (63 - (doc & 63))) & 1ull;
+}
+
+// The filters of one search: at most one of a full-N mask (high bit first), the exact
+// clauses, the bloom plans.
+struct FilterSet {
+  const uint64_t* mask;
+  int64_t mask_words;
+  ExactArgs ex;
+  BloomArgs bloom;
+};
+
+// BLOOM = false compiles the bloom test out (the scan kernels without a bloom filter keep
+// their registers).
+template <bool BLOOM>
+__device__ __forceinline__ bool pos_passes(const FilterSet& f, int64_t row, int64_t position) {
+  if (f.mask != nullptr) {
+    const int64_t w = position >> 6;
+    if (w < f.mask_words && ((f.mask[row * f.mask_words + w] >> (63 - (position & 63))) & 1ull) == 0) return false;
+  }
+  if (f.ex.attrs != nullptr && !exact_pass(f.ex, f.ex.query + row * f.ex.n_clauses, position)) return false;
+  if constexpr (BLOOM) {
+    if (f.bloom.index != nullptr && !bloom_pass(f.bloom, row, position)) return false;
+  }
+  return true;
+}
+
 // Block-wide inclusive scan of two int64 values (kExpandThreads threads).
 __device__ __forceinline__ void block_scan2(int64_t (&part)[2][kExpandThreads], int64_t& a, int64_t& b) {
   const int tid = threadIdx.x;
@@ -113,8 +234,8 @@ __device__ __forceinline__ void block_scan2(int64_t (&part)[2][kExpandThreads], 
 
 __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
     const int64_t* __restrict__ probe_ids, int P, const int64_t* __restrict__ offsets,
-    const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, const uint64_t* __restrict__ mask,
-    int64_t mask_words, ExactArgs ex, int width, int64_t* __restrict__ pos, int64_t* __restrict__ counts) {
+    const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, FilterSet f, int width,
+    int64_t* __restrict__ pos, int64_t* __restrict__ counts) {
   // per probe: start (int64), len, head slot, tail slot (int32, slots clipped to width)
   extern __shared__ __align__(16) uint8_t sm[];
   int64_t* p_start = reinterpret_cast<int64_t*>(sm);
@@ -161,17 +282,9 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
 
   const int warp = tid >> 5, lane = tid & 31;
   int64_t* out = pos + static_cast<int64_t>(b) * width;
-  const uint64_t* mrow = mask ? mask + static_cast<int64_t>(b) * mask_words : nullptr;
-  const int32_t* qattrs = ex.attrs ? ex.query + static_cast<int64_t>(b) * ex.n_clauses : nullptr;
   auto emit = [&](int64_t slot, int64_t position) {
     if (slot >= width) return;
-    int64_t v = position;
-    if (mrow != nullptr) {
-      const int64_t w = position >> 6;
-      if (w < mask_words && ((mrow[w] >> (63 - (position & 63))) & 1ull) == 0) v = -1;
-    }
-    if (qattrs != nullptr && v >= 0 && !exact_pass(ex, qattrs, position)) v = -1;
-    out[slot] = v;
+    out[slot] = pos_passes<true>(f, b, position) ? position : -1;
   };
   for (int j = warp; j < P; j += kExpandThreads / 32) {
     const int64_t start = p_start[j];
@@ -287,6 +400,57 @@ static int launch_status() {
 }
 
 static int st_width(int max_tensor_size_per_row) { return (max_tensor_size_per_row + 31) / 32 * 32; }
+
+// The filter of one call from the C-ABI struct: at most one of the mask, the exact
+// clauses and the bloom plans (the reference's TORCH_CHECK, fork_search_cuda.cu:1282-1290;
+// with plans and exact clauses together the caller passes the exact clauses only, as
+// the bloom with its exact recheck returns the exact filter's result).
+static int build_filters(const rb_st_filter* flt, int64_t N, FilterSet& fs) {
+  fs = FilterSet{nullptr, 0, ExactArgs{nullptr, 0, 0, nullptr, nullptr, nullptr, 0},
+                 BloomArgs{nullptr, 0, nullptr, 0, nullptr, 0, 0, nullptr, 0, 0}};
+  if (flt == nullptr) return RB_OK;
+  const int kinds = (flt->filtering_bit_mask != nullptr) + (flt->query_clause_attrs != nullptr) +
+                    (flt->bloom_index != nullptr);
+  if (kinds > 1) {
+    set_last_error("st::search takes one filter: filtering_bit_mask, the exact clauses or the bloom plans");
+    return RB_ERR_INVALID_ARG;
+  }
+  if (flt->filtering_bit_mask != nullptr) {
+    if (flt->mask_words < 0) {
+      set_last_error("st::search: bad filtering_bit_mask width");
+      return RB_ERR_INVALID_ARG;
+    }
+    fs.mask = reinterpret_cast<const uint64_t*>(flt->filtering_bit_mask);
+    fs.mask_words = flt->mask_words;
+  }
+  if (flt->query_clause_attrs != nullptr) {
+    if (flt->item_clause_attrs == nullptr || flt->clause_slots == nullptr || flt->clause_is_reverse == nullptr ||
+        flt->n_clauses < 0 || flt->attr_rows < 0 || flt->attr_docs < N) {
+      set_last_error("st::search: the exact filter needs item_clause_attrs [R, >= N], clause_slots and "
+                     "clause_is_reverse");
+      return RB_ERR_INVALID_ARG;
+    }
+    fs.ex = ExactArgs{flt->item_clause_attrs, flt->attr_rows, flt->attr_docs, flt->clause_slots,
+                      flt->clause_is_reverse, flt->query_clause_attrs, flt->n_clauses};
+  }
+  if (flt->bloom_index != nullptr) {
+    if (flt->bundle_b_offsets == nullptr || flt->n_bundles < 1 || flt->plans == nullptr || flt->plan_count < 1 ||
+        flt->plan_words < 8 * static_cast<int64_t>(flt->plan_count) || flt->bloom_words < 0 || flt->hash_k < 1 ||
+        flt->bloom_k < 1) {
+      set_last_error("st::search: the bloom filter needs bloom_index, bundle offsets, plans of plan_count slots, "
+                     "bloom_k and hash_k");
+      return RB_ERR_INVALID_ARG;
+    }
+    if (flt->bloom_k > kBloomMaxK || flt->max_stack_size > kBloomStack) {
+      set_last_error("st::search: bloom_k > 10 or a plan stack deeper than 16 is not supported");
+      return RB_ERR_UNSUPPORTED;
+    }
+    fs.bloom = BloomArgs{reinterpret_cast<const uint64_t*>(flt->bloom_index), flt->bloom_words,
+                         flt->bundle_b_offsets, flt->n_bundles, flt->plans, flt->plan_words, flt->plan_count,
+                         flt->query_plan_index, flt->bloom_k, flt->hash_k};
+  }
+  return RB_OK;
+}
 
 // Workspace: q codes [B, D] | q scales [B] | positions [B, width] | counts [B] |
 // winner slots [B, k_sel] | winner raw scores [B, k_sel] | candidate lists.
@@ -490,14 +654,12 @@ struct GroupArgs {
   int G;
   int k;
   int divisor;
-  const uint64_t* mask;
-  int64_t mask_words;
-  ExactArgs ex;
+  FilterSet f;
   uint2* lists;      // [B * P, CAP]
   int* list_counts;  // [B * P]
 };
 
-template <int CAP>
+template <int CAP, bool BLOOM>
 __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs a) {
   extern __shared__ __align__(16) uint8_t gsm[];
   __shared__ uint32_t hist[kGroupWarps][256];
@@ -563,8 +725,6 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
       uint2* list = a.lists + static_cast<int64_t>(pr) * CAP;
       const int64_t hs = a.head[pr], ts = a.tail[pr];
       const int4* q = reinterpret_cast<const int4*>(sq + g * dp);
-      const uint64_t* mrow = a.mask ? a.mask + b * a.mask_words : nullptr;
-      const int32_t* qattrs = a.ex.attrs ? a.ex.query + b * a.ex.n_clauses : nullptr;
 #pragma unroll 1
       for (int r = 0; r < kGroupTile / 32; ++r) {
         const int li = r * 32 + lane;
@@ -574,12 +734,7 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
         if (li < rows) {
           const int64_t slot = i < full ? hs + i : ts + (i - full);
           const int64_t position = start + i;
-          bool ok = slot < a.width;
-          if (ok && mrow != nullptr) {
-            const int64_t w = position >> 6;
-            ok = !(w < a.mask_words && ((mrow[w] >> (63 - (position & 63))) & 1ull) == 0);
-          }
-          if (ok && qattrs != nullptr) ok = exact_pass(a.ex, qattrs, position);
+          const bool ok = slot < a.width && pos_passes<BLOOM>(a.f, b, position);
           if (ok) {
             const int4* x = reinterpret_cast<const int4*>(sx + li * rs);
             int acc = 0;
@@ -702,31 +857,13 @@ int rb_st_search_workspace_size(int B, int D, int P, int k, int max_tensor_size_
 int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P, const int64_t* cluster_offsets,
                  const int64_t* cluster_sizes, int64_t n_lists, const int8_t* item_codes, int64_t N,
                  const int64_t* sort_perm, const float* global_scale, int k, int max_tensor_size_per_row,
-                 int divisor_for_int8, const int64_t* filtering_bit_mask, int64_t mask_words,
-                 const int32_t* item_clause_attrs, int64_t attr_rows, int64_t attr_docs, const int64_t* clause_slots,
-                 const uint8_t* clause_is_reverse, const int32_t* query_clause_attrs, int n_clauses,
-                 int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+                 int divisor_for_int8, const rb_st_filter* filter, int64_t* out_ids, float* out_scores,
+                 void* workspace, size_t workspace_bytes, void* stream) {
   int rc = st_check(B, D, P, n_lists, N, k, max_tensor_size_per_row, divisor_for_int8);
   if (rc != RB_OK) return rc;
-  if (filtering_bit_mask != nullptr && mask_words < 0) {
-    set_last_error("st::search: bad filtering_bit_mask width");
-    return RB_ERR_INVALID_ARG;
-  }
-  ExactArgs ex{nullptr, 0, 0, nullptr, nullptr, nullptr, 0};
-  if (query_clause_attrs != nullptr) {
-    if (filtering_bit_mask != nullptr) {
-      set_last_error("st::search takes one filter: the exact clauses or filtering_bit_mask");
-      return RB_ERR_INVALID_ARG;
-    }
-    if (item_clause_attrs == nullptr || clause_slots == nullptr || clause_is_reverse == nullptr || n_clauses < 0 ||
-        attr_rows < 0 || attr_docs < N) {
-      set_last_error("st::search: the exact filter needs item_clause_attrs [R, >= N], clause_slots and "
-                     "clause_is_reverse");
-      return RB_ERR_INVALID_ARG;
-    }
-    ex = ExactArgs{item_clause_attrs, attr_rows, attr_docs, clause_slots, clause_is_reverse, query_clause_attrs,
-                   n_clauses};
-  }
+  FilterSet fs;
+  rc = build_filters(filter, N, fs);
+  if (rc != RB_OK) return rc;
   if (B == 0) return RB_OK;
   const int width = st_width(max_tensor_size_per_row);
   const int k_sel = std::min(k, width);
@@ -753,8 +890,7 @@ int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int
   }
   const size_t smem = static_cast<size_t>(P) * (sizeof(int64_t) + 3 * sizeof(int));
   probe_expand_kernel<<<B, kExpandThreads, smem, s>>>(
-      probe_ids, P, cluster_offsets, cluster_sizes, n_lists, N, reinterpret_cast<const uint64_t*>(filtering_bit_mask),
-      mask_words, ex, width, pos, counts);
+      probe_ids, P, cluster_offsets, cluster_sizes, n_lists, N, fs, width, pos, counts);
   rc = launch_status();
   if (rc != RB_OK) return rc;
   rc = cand_i8_topk(q_codes, item_codes, static_cast<int>(N), D, pos, width, counts, B, k_sel, divisor_for_int8,
@@ -816,36 +952,18 @@ int rb_st_search_grouped_workspace_size(int B, int D, int P, int64_t n_lists, in
 int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_ids, int P,
                          const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
                          const int8_t* item_codes, int64_t N, const int64_t* sort_perm, const float* global_scale,
-                         int k, int max_tensor_size_per_row, int divisor_for_int8, const int64_t* filtering_bit_mask,
-                         int64_t mask_words, const int32_t* item_clause_attrs, int64_t attr_rows, int64_t attr_docs,
-                         const int64_t* clause_slots, const uint8_t* clause_is_reverse,
-                         const int32_t* query_clause_attrs, int n_clauses, int64_t* out_ids, float* out_scores,
-                         void* workspace, size_t workspace_bytes, void* stream) {
+                         int k, int max_tensor_size_per_row, int divisor_for_int8, const rb_st_filter* filter,
+                         int64_t* out_ids, float* out_scores, void* workspace, size_t workspace_bytes,
+                         void* stream) {
   int rc = st_check(B, D, P, n_lists, N, k, max_tensor_size_per_row, divisor_for_int8);
   if (rc != RB_OK) return rc;
   if (P > 1024 || static_cast<int64_t>(B) * P > INT32_MAX) {
     set_last_error("st::search (grouped): more than 1024 probes a row or 2^31 (row, probe) pairs");
     return RB_ERR_UNSUPPORTED;
   }
-  if (filtering_bit_mask != nullptr && mask_words < 0) {
-    set_last_error("st::search: bad filtering_bit_mask width");
-    return RB_ERR_INVALID_ARG;
-  }
-  ExactArgs ex{nullptr, 0, 0, nullptr, nullptr, nullptr, 0};
-  if (query_clause_attrs != nullptr) {
-    if (filtering_bit_mask != nullptr) {
-      set_last_error("st::search takes one filter: the exact clauses or filtering_bit_mask");
-      return RB_ERR_INVALID_ARG;
-    }
-    if (item_clause_attrs == nullptr || clause_slots == nullptr || clause_is_reverse == nullptr || n_clauses < 0 ||
-        attr_rows < 0 || attr_docs < N) {
-      set_last_error("st::search: the exact filter needs item_clause_attrs [R, >= N], clause_slots and "
-                     "clause_is_reverse");
-      return RB_ERR_INVALID_ARG;
-    }
-    ex = ExactArgs{item_clause_attrs, attr_rows, attr_docs, clause_slots, clause_is_reverse, query_clause_attrs,
-                   n_clauses};
-  }
+  FilterSet fs;
+  rc = build_filters(filter, N, fs);
+  if (rc != RB_OK) return rc;
   if (B == 0) return RB_OK;
   const int width = st_width(max_tensor_size_per_row);
   const int k_sel = std::min(k, width);
@@ -894,10 +1012,11 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   if (!smem_set) {
     // the largest tile (D = 1024) needs about 150 KB of the 227 KB a block may opt into
     const int most = static_cast<int>(group_smem_bytes(kMaxSearchD));
-    if (cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap>, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             most) != cudaSuccess) {
+    const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    if (cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap, false>, attr, most) != cudaSuccess ||
+        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap, true>, attr, most) != cudaSuccess ||
+        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge, false>, attr, most) != cudaSuccess ||
+        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge, true>, attr, most) != cudaSuccess) {
       set_last_error("st::search: cannot raise the grouped scan's shared memory limit");
       return RB_ERR_CUDA;
     }
@@ -905,12 +1024,20 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   }
   const int64_t max_tasks = (n_pairs + G - 1) / G + std::min<int64_t>(n_lists, n_pairs);
   GroupArgs ga{item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask,
-               head, tail, width, G, k_sel, divisor_for_int8, reinterpret_cast<const uint64_t*>(filtering_bit_mask),
-               mask_words, ex, lists, lcounts};
-  if (group_cap(k_sel) == kGroupCap)
-    ivf_group_scan_kernel<kGroupCap><<<static_cast<unsigned>(max_tasks), kGroupThreads, smem, s>>>(ga);
-  else
-    ivf_group_scan_kernel<kGroupCapLarge><<<static_cast<unsigned>(max_tasks), kGroupThreads, smem, s>>>(ga);
+               head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts};
+  const unsigned grid_tasks = static_cast<unsigned>(max_tasks);
+  const bool bloom = fs.bloom.index != nullptr;
+  if (group_cap(k_sel) == kGroupCap) {
+    if (bloom)
+      ivf_group_scan_kernel<kGroupCap, true><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+    else
+      ivf_group_scan_kernel<kGroupCap, false><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+  } else {
+    if (bloom)
+      ivf_group_scan_kernel<kGroupCapLarge, true><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+    else
+      ivf_group_scan_kernel<kGroupCapLarge, false><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+  }
   rc = launch_status();
   if (rc != RB_OK) return rc;
   rc = merge_lists(lists, lcounts, B, P, group_cap(k_sel), k_sel, 0, slots, raw, nullptr, s);

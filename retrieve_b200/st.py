@@ -14,10 +14,10 @@ clusters' positions in the reference scorer's slot order, exact int32 dots,
 top-k on the raw score with ties to the lower slot, ``id = sort_perm[pos]`` and
 ``score = (fp32(dot) * q_scale) * global_scale`` (or the fp16 path's
 ``raw * ((q_scale * divisor) * global_scale)``), ``-1`` / ``-inf`` pads. A
-full-``N`` ``filtering_bit_mask`` (high bit first) and the exact clause filter
-are served; bloom plans with the exact recheck give the exact filter's result
-(the bloom has no false negatives); bloom plans alone raise
-``NotImplementedError``.
+full-``N`` ``filtering_bit_mask`` (high bit first), the exact clause filter and
+SilverTorch's bloom over its own index and prepared plans are served; bloom plans
+with the exact recheck give the exact filter's result (the bloom has no false
+negatives), so the plans are then not read.
 Errors raise ``RuntimeError``, as the reference's ``TORCH_CHECK``s do.
 """
 
@@ -101,20 +101,20 @@ def _search(
     item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
     clause_is_reverse: Tensor | None = None, query_clause_attrs: Tensor | None = None,
 ) -> tuple[Tensor, Tensor]:
-    """Filters: a full-``N`` ``filtering_bit_mask``, or the exact clauses
+    """Filters: a full-``N`` ``filtering_bit_mask``; the exact clauses
     (``item_clause_attrs``, ``clause_slots``, ``clause_is_reverse``,
-    ``query_clause_attrs``). With bloom ``plans`` and the exact clauses together
-    (the bloom with its exact recheck) the result is the exact filter's, since the
-    bloom has no false negatives; the plans are then not read. Bloom plans alone
-    (false positives kept) are not served."""
+    ``query_clause_attrs``); or SilverTorch's bloom (``bloom_index``,
+    ``bloom_bundle_b_offsets``, the prepared ``plans`` blob of ``plan_count`` slots,
+    ``max_stack_size``, ``query_plan_index``, ``bloom_k``, ``hash_k``), false positives
+    kept. With bloom plans and the exact clauses together (the bloom with its exact
+    recheck) the result is the exact filter's, since the bloom has no false negatives;
+    the plans are then not read."""
     exact = query_clause_attrs is not None
     _check(not (filtering_bit_mask is not None and (plans is not None or exact)),
            "search takes one filter: plans (+ query_clause_attrs to recheck), query_clause_attrs or "
            "filtering_bit_mask")
-    if plans is not None and not exact:
-        raise NotImplementedError("st::search: the bloom-plan filter without its exact recheck is not implemented "
-                                  "here; pass query_clause_attrs (recheck) or a filtering_bit_mask")
-    ex = None
+    flt = _lib.StFilter()
+    use_filter = False
     if exact:
         _check(item_clause_attrs is not None and clause_slots is not None and clause_is_reverse is not None,
                "the exact filter needs item_clause_attrs, clause_slots and clause_is_reverse")
@@ -132,7 +132,39 @@ def _search(
                "clause_slots must have C + 1 entries and clause_is_reverse C")
         _check(query_clause_attrs.shape[0] == query.shape[0], "query_clause_attrs must have B rows")
         _check(item_clause_attrs.shape[1] >= item_codes.shape[0], "item_clause_attrs must cover the N docs")
-        ex = (item_clause_attrs, clause_slots, clause_is_reverse, query_clause_attrs)
+        flt.item_clause_attrs = item_clause_attrs.data_ptr()
+        flt.attr_rows, flt.attr_docs = item_clause_attrs.shape
+        flt.clause_slots = clause_slots.data_ptr()
+        flt.clause_is_reverse = clause_is_reverse.data_ptr()
+        flt.query_clause_attrs = query_clause_attrs.data_ptr()
+        flt.n_clauses = n_clauses
+        use_filter = True
+    elif plans is not None:
+        _check(bloom_index is not None and bloom_bundle_b_offsets is not None,
+               "the bloom filter needs bloom_index and bloom_bundle_b_offsets")
+        for name, t in (("bloom_index", bloom_index), ("bloom_bundle_b_offsets", bloom_bundle_b_offsets),
+                        ("plans", plans)):
+            _check(t.dtype == torch.int64 and t.dim() == 1 and t.is_contiguous() and t.device == query.device,
+                   f"{name} must be a contiguous 1-D int64 tensor on the query's device")
+        _check(plan_count >= 1 and plans.numel() >= 8 * plan_count, "plans must hold plan_count slots")
+        if query_plan_index is not None:
+            _check(query_plan_index.dtype == torch.int64 and query_plan_index.numel() == query.shape[0]
+                   and query_plan_index.is_contiguous() and query_plan_index.device == query.device,
+                   "query_plan_index must be int64 [B] on the query's device")
+        else:
+            _check(plan_count >= query.shape[0], "without query_plan_index every row needs its own plan")
+        flt.bloom_index = bloom_index.data_ptr()
+        flt.bloom_words = bloom_index.numel()
+        flt.bundle_b_offsets = bloom_bundle_b_offsets.data_ptr()
+        flt.n_bundles = bloom_bundle_b_offsets.numel() - 1
+        flt.plans = plans.data_ptr()
+        flt.plan_words = plans.numel()
+        flt.plan_count = int(plan_count)
+        flt.max_stack_size = int(max_stack_size)
+        flt.query_plan_index = 0 if query_plan_index is None else query_plan_index.data_ptr()
+        flt.bloom_k = int(bloom_k)
+        flt.hash_k = int(hash_k)
+        use_filter = True
     _check(item_codes.dtype == torch.int8 and item_codes.dim() == 2 and item_codes.shape[1] == query.shape[1],
            "item_codes must be int8 [N, D] with the query's D")
     _check(item_codes.is_contiguous(), "item_codes must be contiguous")
@@ -145,12 +177,13 @@ def _search(
     gs = global_scale.to(device=dev, dtype=torch.float32).reshape(-1)[:1].contiguous()
     _check(gs.numel() == 1, "global_scale must hold one value")
     mask = None
-    mask_words = 0
     if filtering_bit_mask is not None:
         _check(filtering_bit_mask.dim() == 2 and filtering_bit_mask.shape[0] == q.shape[0],
                "filtering_bit_mask must be [B, words]")
         mask = filtering_bit_mask.to(device=dev, dtype=torch.int64).contiguous()
-        mask_words = mask.shape[1]
+        flt.filtering_bit_mask = mask.data_ptr()
+        flt.mask_words = mask.shape[1]
+        use_filter = True
     b, d = q.shape
     p = probe.shape[1]
     _check(k >= 1, f"k must be positive, got {k}")
@@ -170,10 +203,7 @@ def _search(
     rc = (lib.rb_st_search_grouped if grouped else lib.rb_st_search)(
         _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), _ptr(item_codes),
         item_codes.shape[0], _ptr(perm), _ptr(gs), k, int(max_tensor_size_per_row), int(divisor_for_int8),
-        _ptr(mask), mask_words,
-        _ptr(ex[0] if ex else None), ex[0].shape[0] if ex else 0, ex[0].shape[1] if ex else 0,
-        _ptr(ex[1] if ex else None), _ptr(ex[2] if ex else None), _ptr(ex[3] if ex else None),
-        ex[3].shape[1] if ex else 0,
+        ctypes.byref(flt) if use_filter else None,
         _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream(dev),
     )
     _call(rc, "st::search")

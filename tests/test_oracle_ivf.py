@@ -167,3 +167,49 @@ def test_exact_layout_and_test_equal_the_clause_predicate(seed):
     want = filters.clause_mask(attrs, rev, q)
     for b in range(q.shape[0]):
         assert np.array_equal(ivf.exact_pass(slots, clause_slots, rev, qq[b], np.arange(n)), want[b])
+
+
+BLOOM = np.load(Path(__file__).resolve().parent / "golden" / "golden_bloom_st.npz")
+
+
+def test_bloom_plans_match_reference_search():
+    """SilverTorch's bloom: its own index build, parser and CPU search ran into the
+    fixture (tests/golden/make_golden_bloom_st.py); the restatement of the plan encoding
+    and the column-word evaluation gives the same mask for every plan (nested AND / OR /
+    NOT, the empty query, several bundles)."""
+    n = int(BLOOM["n"])
+    want = np.unpackbits(BLOOM["mask_bits"], axis=1)[:, :n].astype(bool)
+    assert len(BLOOM["bundle_b_offsets"]) > 2
+    for p in range(want.shape[0]):
+        got = ivf.bloom_plan_mask(BLOOM["bloom_index"], BLOOM["bundle_b_offsets"], BLOOM["plan_data"],
+                                  BLOOM["plan_offsets"], p, int(BLOOM["k"]), int(BLOOM["hash_k"]), n)
+        assert np.array_equal(got, want[p]), p
+    assert want[5].all()  # the empty query matches every doc
+
+
+def test_bloom_is_a_superset_of_the_exact_predicate():
+    """No false negatives (retrieve/tests/parity/test_official.py:455-470) for the plain
+    conjunction plans: "0:3" and "0:3 AND 1:5" against the exact clause test."""
+    from oracle import filters
+
+    n = int(BLOOM["n"])
+    bloom = np.unpackbits(BLOOM["mask_bits"], axis=1)[:, :n].astype(bool)
+    attrs = BLOOM["attrs"]
+    q = np.array([[3, -1, -1], [3, 5, -1]])
+    exact = filters.clause_mask(attrs, np.zeros(3, dtype=bool), q)
+    assert not (exact & ~bloom[:2]).any()
+
+
+def test_plan_blob_layout():
+    """The prepared blob (adapter.py:212-236): the parser's eight offsets a plan, then its
+    data after 8 * slots header words; decoding through the blob gives the same plan."""
+    data, offsets = BLOOM["plan_data"], BLOOM["plan_offsets"]
+    n_plans = len(offsets) // 8
+    blob = ivf.plan_blob(data, offsets, n_plans + 3)
+    assert np.array_equal(blob[: len(offsets)], offsets)
+    body = blob[8 * (n_plans + 3):].view(np.uint8)[: len(data)]
+    assert np.array_equal(body, np.asarray(data).view(np.uint8))
+    for p in range(n_plans):
+        a = ivf.decode_plan(data, offsets, p)
+        b = ivf.decode_plan(body, blob[: 8 * n_plans], p)
+        assert all(np.array_equal(x, y) for x, y in zip(a, b, strict=True))

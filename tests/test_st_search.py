@@ -105,9 +105,9 @@ def test_argument_errors_raise_runtime_error():
         st.search(q, probe, off, sz, torch.zeros(4, 64, dtype=torch.int8), perm, gs, 2, 4,
                   filtering_bit_mask=torch.zeros(2, 1, dtype=torch.int64),
                   query_clause_attrs=torch.zeros(2, 1, dtype=torch.int32))
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="bloom"):
         st.search(q, probe, off, sz, torch.zeros(4, 64, dtype=torch.int8), perm, gs, 2, 4,
-                  plans=torch.zeros(8, dtype=torch.uint8))
+                  plans=torch.zeros(8, dtype=torch.int64))
 
 
 REF_CPU_LIB = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "silvertorch_ref_cpu.so"
@@ -143,9 +143,13 @@ def test_capi_argument_checks_need_no_device():
     assert lib.rb_st_search_workspace_size(16, 128, 8, 0, 700, ctypes.byref(n)) == _lib.RB_ERR_INVALID_ARG
 
     def call(b=4, d=128, p=8, k=10, width=256, div=-1, ws=None, ws_bytes=0, mask=None, qattrs=None, attrs=None,
-             docs=1000):
-        return lib.rb_st_search(None, b, d, None, p, None, None, 16, None, 1000, None, None, k, width, div, mask, 0,
-                                attrs, 3, docs, attrs, attrs, qattrs, 2, None, None, ws, ws_bytes, None)
+             docs=1000, bloom=None, bloom_k=5, stack=3, plan_words=64):
+        f = _lib.StFilter(filtering_bit_mask=mask, item_clause_attrs=attrs, attr_rows=3, attr_docs=docs,
+                          clause_slots=attrs, clause_is_reverse=attrs, query_clause_attrs=qattrs, n_clauses=2,
+                          bloom_index=bloom, bloom_words=100, bundle_b_offsets=bloom, n_bundles=1, plans=bloom,
+                          plan_words=plan_words, plan_count=4, max_stack_size=stack, bloom_k=bloom_k, hash_k=7)
+        return lib.rb_st_search(None, b, d, None, p, None, None, 16, None, 1000, None, None, k, width, div,
+                                ctypes.byref(f), None, None, ws, ws_bytes, None)
 
     assert call(d=2048) == _lib.RB_ERR_UNSUPPORTED  # D > 1024
     assert call(p=4096) == _lib.RB_ERR_UNSUPPORTED  # more than 2048 probes
@@ -162,6 +166,11 @@ def test_capi_argument_checks_need_no_device():
     assert call(qattrs=fake) == _lib.RB_ERR_INVALID_ARG  # exact filter without its tables
     assert call(qattrs=fake, attrs=fake, docs=999) == _lib.RB_ERR_INVALID_ARG  # attrs narrower than N
     assert call(qattrs=fake, attrs=fake) == _lib.RB_ERR_WORKSPACE
+    assert call(bloom=fake) == _lib.RB_ERR_WORKSPACE  # a well-formed bloom filter
+    assert call(bloom=fake, qattrs=fake, attrs=fake) == _lib.RB_ERR_INVALID_ARG  # one filter only
+    assert call(bloom=fake, bloom_k=11) == _lib.RB_ERR_UNSUPPORTED  # more positions than SilverTorch resolves
+    assert call(bloom=fake, stack=17) == _lib.RB_ERR_UNSUPPORTED  # deeper plans than the device stack
+    assert call(bloom=fake, plan_words=16) == _lib.RB_ERR_INVALID_ARG  # 4 plan slots need 32 header words
     assert call(b=0) == _lib.RB_OK  # nothing to do: no device touched
 
 
@@ -344,7 +353,7 @@ def test_grouped_capi_checks_need_no_device():
 
     def call(p=8, ws=None, ws_bytes=0):
         return lib.rb_st_search_grouped(None, 4, 128, None, p, None, None, 16, None, 1000, None, None, 10, 256, -1,
-                                        None, 0, None, 0, 0, None, None, None, 0, None, None, ws, ws_bytes, None)
+                                        None, None, None, ws, ws_bytes, None)
 
     assert call(p=1500) == _lib.RB_ERR_UNSUPPORTED  # more than 1024 probes a row
     assert call() == _lib.RB_ERR_WORKSPACE
@@ -399,3 +408,48 @@ def test_grouped_many_rows_per_cluster(k):
         ids, scores = st.search_grouped(*t, torch.tensor(gs).cuda(), k, width)
         _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), *ivf.search(q, probe, offsets, sizes, codes, perm, gs,
                                                                           k, width))
+
+
+# --- SilverTorch's bloom filter (plans without the exact recheck) -------------------------------
+
+BLOOM = np.load(Path(__file__).resolve().parent / "golden" / "golden_bloom_st.npz")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("grouped", [False, True])
+@pytest.mark.parametrize("plan_index", [False, True])
+def test_search_bloom_plans(grouped, plan_index):
+    """The reference's own bloom index, parsed plans and CPU search (the fixture): the op
+    with the prepared plan blob returns the oracle's search under the reference's bloom
+    mask, bit for bit (false positives included), row by row or through query_plan_index."""
+    _st()
+    from retrieve_b200 import st
+
+    n = int(BLOOM["n"])
+    want_mask = np.unpackbits(BLOOM["mask_bits"], axis=1)[:, :n].astype(bool)
+    n_plans = want_mask.shape[0]
+    rng = np.random.default_rng(3)
+    b = 2 * n_plans if plan_index else n_plans
+    cuts = np.sort(rng.integers(0, n + 1, 59))
+    sizes = np.diff(np.r_[0, cuts, n]).astype(np.int64)  # 60 clusters covering the n docs
+    offsets = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    d = 64
+    codes = rng.integers(-128, 128, (n, d)).astype(np.int8)
+    perm = rng.permutation(n).astype(np.int64)
+    probe = np.argsort(rng.random((b, len(sizes))), axis=1)[:, :12].astype(np.int64)
+    q = rng.standard_normal((b, d)).astype(np.float32)
+    width = int(sizes[probe].sum(1).max())
+    rows = np.arange(b) % n_plans if plan_index else np.arange(b)
+    blob = ivf.plan_blob(BLOOM["plan_data"], BLOOM["plan_offsets"], n_plans)
+    t = [torch.from_numpy(x).cuda() for x in (q, probe, offsets, sizes, codes, perm)]
+    fn = st.search_grouped if grouped else st.search
+    ids, scores = fn(*t, torch.tensor(0.02).cuda(), 50, width,
+                     bloom_index=torch.from_numpy(BLOOM["bloom_index"]).cuda(),
+                     bloom_bundle_b_offsets=torch.from_numpy(BLOOM["bundle_b_offsets"]).cuda(),
+                     plans=torch.from_numpy(blob).cuda(), plan_count=n_plans,
+                     max_stack_size=int(BLOOM["max_stack"]),
+                     query_plan_index=torch.from_numpy(rows.astype(np.int64)).cuda() if plan_index else None,
+                     bloom_k=int(BLOOM["k"]), hash_k=int(BLOOM["hash_k"]))
+    words = ivf.pack_mask_high_first(want_mask[rows])
+    want = ivf.search(q, probe, offsets, sizes, codes, perm, np.float32(0.02), 50, width, filtering_bit_mask=words)
+    _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), *want)
