@@ -154,6 +154,29 @@ RB_API int rb_quantize_int8_global(const float* x, int64_t N, int D, const int64
                                    void* stream);
 
 /*
+ * SilverTorch's bundle-major bloom index on the device, replacing the CUDA impls of
+ *   st::bloom_index_build(Tensor feature_ids, Tensor feature_offsets, Tensor feature_values,
+ *                         float b_multiplier, int k, bool fast_build=False) -> (Tensor, Tensor)
+ *   st::bloom_index_build_fixed(..., int bits_per_doc, int k, bool fast_build=False)
+ * (silvertorch/ops/csrc/bloom_indexer.cpp:26-136; bloom_indexer_cuda.cu:291-340, 790-960).
+ * feature_ids int32 [C]; feature_offsets int64 [N * C + 1] (CSR over (doc, feature));
+ * feature_values int64 [n_values]. Two calls: rb_bloom_index_widths writes each
+ * 2048-doc bundle's bits per doc (widths [ceil(N / 2048)]: bits_per_doc when > 0, else
+ * trunc(fp64(max values of a doc in the bundle * k) * b_multiplier)) and their prefix
+ * sums bundle_b_offsets [ceil(N / 2048) + 1]; the caller allocates a zeroed
+ * bloom_index of bundle_b_offsets[last] * 32 words, and rb_bloom_index_fill sets, for
+ * every value, bit 63 - d % 64 of word (bundle_b_offsets[d / 2048] + p) * 32 +
+ * (d % 2048) / 64 at its first k distinct positions p = murmur3(feature id, value,
+ * seed) % B over seeds 0, 1, ... (bloom_index_util.cuh:61-107, 185-208). 1 <= k <= 64.
+ */
+RB_API int rb_bloom_index_widths(const int64_t* feature_offsets, int64_t N, int C, int k, double b_multiplier,
+                                 int64_t bits_per_doc, int64_t* widths, int64_t* bundle_b_offsets, void* stream);
+RB_API int rb_bloom_index_fill(const int32_t* feature_ids, const int64_t* feature_offsets,
+                               const int64_t* feature_values, int64_t n_values, int64_t N, int C, int k,
+                               const int64_t* bundle_b_offsets, int64_t* bloom_index, int64_t index_words,
+                               void* stream);
+
+/*
  * Sign packing of values [M, D] fp32, D a multiple of 64, into words [M, D / 64]
  * int64: bit b of word w is set iff values[m, 64 w + b] > 0
  * (retrieve/src/retrieve/indexing/quantize.py:63-72 `_pack_signs_to_int64`, the last

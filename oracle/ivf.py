@@ -310,3 +310,50 @@ def bloom_plan_mask(bloom_index, bundle_b_offsets, data, offsets, p, k, hash_k, 
     words = stack.pop()
     d = np.arange(n)
     return ((words[d // 64] >> (np.uint64(63) - (d % 64).astype(np.uint64))) & np.uint64(1)).astype(bool)
+
+
+def attrs_to_features(attrs):
+    """``[N, C, A]`` attrs (``-1`` pads) to the jagged feature layout
+    (retrieve/src/retrieve/ops/official/adapter.py:45-65): feature ids ``0 .. C-1``
+    int32, CSR offsets over (doc, feature) int64 ``[N C + 1]``, values in (doc,
+    feature, slot) order."""
+    a = np.asarray(attrs, dtype=np.int64)
+    n, c, _ = a.shape
+    valid = a != -1
+    offsets = np.zeros(n * c + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum(valid.sum(axis=2).reshape(-1))
+    return np.arange(c, dtype=np.int32), offsets, a.reshape(-1)[valid.reshape(-1)]
+
+
+def bloom_index_build(feature_ids, feature_offsets, feature_values, b_multiplier, k, bits_per_doc=0):
+    """SilverTorch's bundle-major bloom index (silvertorch/ops/csrc/bloom_indexer.cpp:26-114;
+    the fixed width of bloom_indexer_cuda.cu:330-335): per 2048-doc bundle ``B`` bits a doc
+    (``bits_per_doc``, or ``trunc(fp64(max values of a doc * k) * b_multiplier)``), and for
+    every value of feature ``f`` of doc ``d`` its first ``k`` distinct positions
+    ``murmur3(f, value, seed) % B`` set bit ``63 - d % 64`` of word
+    ``(bundle_b_offsets[d // 2048] + p) * 32 + (d % 2048) // 64``. Returns
+    ``(bloom_index int64, bundle_b_offsets int64)``."""
+    from oracle.bloom import build_positions
+
+    fid = np.asarray(feature_ids, dtype=np.int64)
+    off = np.asarray(feature_offsets, dtype=np.int64)
+    val = np.asarray(feature_values, dtype=np.int64)
+    c = len(fid)
+    n = (len(off) - 1) // c
+    n_bundles = (n + 2047) // 2048
+    per_doc = off[c::c] - off[: n * c : c]  # values of each doc
+    widths = np.zeros(n_bundles, dtype=np.int64)
+    for i in range(n_bundles):
+        m = int(per_doc[i * 2048 : (i + 1) * 2048].max()) if n else 0
+        widths[i] = bits_per_doc if bits_per_doc > 0 else int(float(m * k) * b_multiplier)
+    boff = np.zeros(n_bundles + 1, dtype=np.int64)
+    boff[1:] = np.cumsum(widths)
+    index = np.zeros(int(boff[-1]) * 32, dtype=np.uint64)
+    for d in range(n):
+        bundle, col = d // 2048, (d % 2048) // 64
+        bit = np.uint64(1) << np.uint64(63 - d % 64)
+        for f in range(c):
+            for v in val[off[d * c + f] : off[d * c + f + 1]]:
+                for p in build_positions(int(fid[f]), int(v), int(widths[bundle]), k):
+                    index[(boff[bundle] + p) * 32 + col] |= bit
+    return index.view(np.int64), boff

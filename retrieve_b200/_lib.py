@@ -76,6 +76,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_quantize_int8_global_workspace_size": (_c_int, [ctypes.POINTER(_c_size)]),
     "rb_quantize_int8_global": (_c_int, [_vp, _c_i64, _c_int, _vp, _c_i64, _vp, _vp, _vp, _c_size, _vp]),
     "rb_pack_signs": (_c_int, [_vp, _c_i64, _c_int, _vp, _vp]),
+    "rb_bloom_index_widths": (_c_int, [_vp, _c_i64, _c_int, _c_int, ctypes.c_double, _c_i64, _vp, _vp, _vp]),
+    "rb_bloom_index_fill": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _vp, _vp, _c_i64, _vp]),
     "rb_st_search_workspace_size": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
     "rb_st_search": (
         _c_int,

@@ -234,6 +234,66 @@ def probe_prep(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluste
     return codes, scales, cids, length, offs, warps, rounded, rem, wcum
 
 
+BLOOM_BUILD_SCHEMA = (
+    "bloom_index_build(Tensor feature_ids, Tensor feature_offsets, Tensor feature_values, "
+    "float b_multiplier, int k, bool fast_build=False) -> (Tensor, Tensor)"
+)
+BLOOM_BUILD_FIXED_SCHEMA = (
+    "bloom_index_build_fixed(Tensor feature_ids, Tensor feature_offsets, Tensor feature_values, "
+    "int bits_per_doc, int k, bool fast_build=False) -> (Tensor, Tensor)"
+)
+
+
+def _bloom_build(feature_ids: Tensor, feature_offsets: Tensor, feature_values: Tensor, b_multiplier: float,
+                 bits_per_doc: int, k: int) -> tuple[Tensor, Tensor]:
+    _check(feature_ids.dtype == torch.int32 and feature_offsets.dtype == torch.int64
+           and feature_values.dtype == torch.int64, "feature_ids int32, feature_offsets and feature_values int64")
+    for t in (feature_ids, feature_offsets, feature_values):
+        _check(t.is_cuda and t.dim() == 1, "the bloom build takes 1-D CUDA tensors")
+    c = feature_ids.numel()
+    _check(c > 0 and (feature_offsets.numel() - 1) % c == 0, "feature_offsets must have N * C + 1 entries")
+    if bits_per_doc <= 0:
+        _check(b_multiplier > 1.0, "b_multiplier must be greater than 1.0")
+    dev = feature_ids.device
+    fid, foff, fval = (t.contiguous() for t in (feature_ids, feature_offsets, feature_values))
+    n = (foff.numel() - 1) // c
+    n_bundles = (n + 2047) // 2048
+    widths = torch.empty(max(n_bundles, 1), dtype=torch.int64, device=dev)
+    offsets = torch.empty(n_bundles + 1, dtype=torch.int64, device=dev)
+    lib = _lib.lib()
+    _call(lib.rb_bloom_index_widths(_ptr(foff), n, c, int(k), float(b_multiplier), int(bits_per_doc), _ptr(widths),
+                                    _ptr(offsets), _stream(dev)), "bloom_index_build")
+    words = int(offsets[-1].item()) * 32  # the index size: one host read, as the reference's builders
+    index = torch.zeros(words, dtype=torch.int64, device=dev)
+    _call(lib.rb_bloom_index_fill(_ptr(fid), _ptr(foff), _ptr(fval), fval.numel(), n, c, int(k), _ptr(offsets),
+                                  _ptr(index), words, _stream(dev)), "bloom_index_build")
+    return index, offsets
+
+
+def bloom_index_build(feature_ids: Tensor, feature_offsets: Tensor, feature_values: Tensor, b_multiplier: float,
+                      k: int, fast_build: bool = False) -> tuple[Tensor, Tensor]:
+    """``st::bloom_index_build`` on the device: ``(bloom_index int64, bundle_b_offsets int64)``,
+    each 2048-doc bundle ``trunc(max values a doc * k * b_multiplier)`` bits per doc.
+    ``fast_build`` selects an algorithm in the reference and does not change the index."""
+    return _bloom_build(feature_ids, feature_offsets, feature_values, b_multiplier, 0, k)
+
+
+def bloom_index_build_fixed(feature_ids: Tensor, feature_offsets: Tensor, feature_values: Tensor,
+                            bits_per_doc: int, k: int, fast_build: bool = False) -> tuple[Tensor, Tensor]:
+    """``st::bloom_index_build_fixed``: every bundle ``bits_per_doc`` bits per doc."""
+    _check(bits_per_doc > 0, "bits_per_doc must be positive")
+    return _bloom_build(feature_ids, feature_offsets, feature_values, 2.0, bits_per_doc, k)
+
+
+def _fake_bloom(feature_ids, feature_offsets, feature_values, *args, **kwargs):
+    # the index length depends on the data (the reference's builders read it back too)
+    n = (feature_offsets.shape[0] - 1) // max(feature_ids.shape[0], 1)
+    ctx = torch.library.get_ctx()
+    words = ctx.new_dynamic_size()
+    return (feature_values.new_empty((words,), dtype=torch.int64),
+            feature_values.new_empty(((n + 2047) // 2048 + 1,), dtype=torch.int64))
+
+
 def _fake_search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm, global_scale, k,
                  max_tensor_size_per_row, *args, **kwargs):
     b = query.shape[0]
@@ -267,7 +327,10 @@ def _defined(name: str) -> bool:
 
 def _register() -> None:
     for name, schema, impl, fake in (("search", SEARCH_SCHEMA, search, _fake_search),
-                                     ("probe_prep", PROBE_PREP_SCHEMA, probe_prep, _fake_probe_prep)):
+                                     ("probe_prep", PROBE_PREP_SCHEMA, probe_prep, _fake_probe_prep),
+                                     ("bloom_index_build", BLOOM_BUILD_SCHEMA, bloom_index_build, _fake_bloom),
+                                     ("bloom_index_build_fixed", BLOOM_BUILD_FIXED_SCHEMA, bloom_index_build_fixed,
+                                      _fake_bloom)):
         ours = not _defined(name)
         if ours:
             _LIBRARY.define(schema)

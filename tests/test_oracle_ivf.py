@@ -213,3 +213,12 @@ def test_plan_blob_layout():
         a = ivf.decode_plan(data, offsets, p)
         b = ivf.decode_plan(body, blob[: 8 * n_plans], p)
         assert all(np.array_equal(x, y) for x, y in zip(a, b, strict=True))
+
+
+def test_bloom_index_build_matches_reference():
+    """The restated builder and feature layout give the reference's own CPU-built index and
+    bundle offsets bit for bit (tests/golden/make_golden_bloom_st.py)."""
+    fid, off, val = ivf.attrs_to_features(BLOOM["attrs"])
+    index, boff = ivf.bloom_index_build(fid, off, val, 10.0, int(BLOOM["k"]))
+    assert np.array_equal(boff, BLOOM["bundle_b_offsets"])
+    assert np.array_equal(index, BLOOM["bloom_index"])

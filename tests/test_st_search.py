@@ -56,10 +56,17 @@ def _case(ci):
 # --- CPU -----------------------------------------------------------------------------------
 
 
+PINNED_BLOOM_BUILD = (
+    "st::bloom_index_build(Tensor feature_ids, Tensor feature_offsets, Tensor feature_values, "
+    "float b_multiplier, int k, bool fast_build=False) -> (Tensor, Tensor)"
+)
+
+
 def test_schemas_are_the_reference_ones():
     st = _st()
     assert str(st.search.default._schema) == PINNED_SEARCH
     assert str(st.probe_prep.default._schema) == PINNED_PROBE_PREP
+    assert str(st.bloom_index_build.default._schema) == PINNED_BLOOM_BUILD
 
 
 def test_fake_shapes():
@@ -453,3 +460,20 @@ def test_search_bloom_plans(grouped, plan_index):
     words = ivf.pack_mask_high_first(want_mask[rows])
     want = ivf.search(q, probe, offsets, sizes, codes, perm, np.float32(0.02), 50, width, filtering_bit_mask=words)
     _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), *want)
+
+
+@pytest.mark.gpu
+def test_bloom_index_build_on_device():
+    """st::bloom_index_build on the device equals the reference's CPU builder bit for bit;
+    the fixed width (st::bloom_index_build_fixed, CUDA only in the reference) equals the
+    oracle's restatement, and plans searched over it equal the oracle's plan masks."""
+    st = _st()
+    fid, off, val = ivf.attrs_to_features(BLOOM["attrs"])
+    t = [torch.from_numpy(x).cuda() for x in (fid, off, val)]
+    index, boff = st.bloom_index_build(*t, 10.0, int(BLOOM["k"]))
+    assert np.array_equal(boff.cpu().numpy(), BLOOM["bundle_b_offsets"])
+    assert np.array_equal(index.cpu().numpy(), BLOOM["bloom_index"])
+    for bits in (64, 257):
+        index_f, boff_f = st.bloom_index_build_fixed(*t, bits, int(BLOOM["k"]))
+        want_i, want_b = ivf.bloom_index_build(fid, off, val, 2.0, int(BLOOM["k"]), bits_per_doc=bits)
+        assert np.array_equal(boff_f.cpu().numpy(), want_b) and np.array_equal(index_f.cpu().numpy(), want_i)
