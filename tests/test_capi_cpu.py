@@ -86,3 +86,30 @@ def test_new_entry_points_validate_before_touching_a_device():
     # merge of packed pairs
     assert lib.rb_merge_pairs(None, 0, 4, 10, 10, None, None, None) == _lib.RB_ERR_INVALID_ARG
     assert lib.rb_merge_pairs(None, 2, 4, 10, 2000, None, None, None) == _lib.RB_ERR_UNSUPPORTED
+
+
+def test_filter_struct_layout_matches_the_header(tmp_path):
+    """The ctypes twin of rb_st_filter has the C compiler's field offsets and size (a
+    mismatch would hand the kernels shifted pointers)."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    names = [name for name, _ in _lib.StFilter._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text(
+        "#include <stdio.h>\n#include <stddef.h>\n#include \"retrieve_b200.h\"\nint main(void) {\n"
+        + "".join(f'  printf("{n} %zu\\n", offsetof(rb_st_filter, {n}));\n' for n in names)
+        + '  printf("size %zu\\n", sizeof(rb_st_filter));\n  return 0;\n}\n'
+    )
+    exe = tmp_path / "layout"
+    include = Path(__file__).resolve().parent.parent / "include"
+    subprocess.run([cc, "-I", str(include), str(src), "-o", str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                         text=True).stdout.splitlines())
+    for n in names:
+        assert int(got[n]) == getattr(_lib.StFilter, n).offset, n
+    assert int(got["size"]) == ctypes.sizeof(_lib.StFilter)
