@@ -337,41 +337,23 @@ def run_ops(args, dev):
 # ivf: SilverTorch's IVF phase 1 + st::search
 # ---------------------------------------------------------------------------
 def _ivf_cpu_baseline(q, probe, offsets, sizes, codes_sorted, perm, gs, k, width, sample: int = 8) -> dict:
-    """The reference's CPU path on ``sample`` queries: its CPU scorer
-    ``st.fused_kmean_ann`` (built from the reference's sources into oracle/_ref) and
-    its adapter epilogue (``torch.topk`` on the raw dots, ``sort_perm``, the two
-    multiplies); the oracle's restatement when that build is absent."""
-    import os
+    """The reference's CPU path for phase 2 + 3 on ``sample`` queries, as the oracle's port
+    (oracle/ivf.py: the reference scorer's int32 dots, top-k on the raw score, the
+    two-multiply epilogue). The reference's own compiled CPU scorer cannot be loaded into
+    this process: its library defines the st:: schemas that retrieve_b200.st has defined."""
     import time
 
-    ref = bench.ROOT / "oracle" / "_ref" / "silvertorch_ref_cpu.so"
-    qs = q[:sample].cpu()
-    pr = probe[:sample].cpu()
-    torch.set_num_threads(os.cpu_count() or 1)
-    if ref.exists():
-        from oracle.knn import quantize_int8
+    from oracle import ivf
 
-        torch.ops.load_library(str(ref))
-        off, sz, cs, pm = offsets.cpu(), sizes.cpu(), codes_sorted.cpu(), perm.cpu()
-        t0 = time.perf_counter()
-        qc, qsc = quantize_int8(qs.numpy())
-        raw, idx = torch.ops.st.fused_kmean_ann(off, pr, sz[pr], cs, torch.from_numpy(qc), width, None, -1, -1,
-                                                None, None)
-        top, slot = torch.topk(torch.where(idx >= 0, raw, torch.iinfo(torch.int32).min), min(k, raw.shape[1]))
-        pos = idx.gather(1, slot).long()
-        _ = torch.where(pos >= 0, pm[pos.clamp_min(0)], -1), top.float() * torch.from_numpy(qsc)[:, None] * gs.cpu()
-        dt = time.perf_counter() - t0
-        kind = "reference"
-    else:
-        from oracle import ivf
-
-        t0 = time.perf_counter()
-        ivf.search(qs.numpy(), pr.numpy(), offsets.cpu().numpy(), sizes.cpu().numpy(), codes_sorted.cpu().numpy(),
-                   perm.cpu().numpy(), gs.cpu().numpy(), k, width)
-        dt = time.perf_counter() - t0
-        kind = "port"
-    return {"value": sample / dt, "unit": "queries/s", "cores": 1, "kind": kind,
-            "sample": f"{sample} queries of the batch, phase 2 only (probe lists given)"}
+    qs = q[:sample].cpu().numpy()
+    pr = probe[:sample].cpu().numpy()
+    args = (offsets.cpu().numpy(), sizes.cpu().numpy(), codes_sorted.cpu().numpy(), perm.cpu().numpy(),
+            gs.cpu().numpy())
+    t0 = time.perf_counter()
+    ivf.search(qs, pr, args[0], args[1], args[2], args[3], args[4], k, width)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "queries/s", "cores": 1, "kind": "port",
+            "sample": f"{sample} queries of the batch, phase 2 + 3 only (probe lists given)"}
 
 
 def run_ivf(args, dev):
