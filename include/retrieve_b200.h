@@ -454,6 +454,32 @@ RB_API int rb_st_search_grouped(const float* query, int B, int D, const int64_t*
                                 size_t workspace_bytes, void* stream);
 
 /*
+ * The same search over several GPUs, each holding the rows [pos_lo, pos_hi) of the sorted
+ * table (whole clusters; item_codes = those rows): rb_st_search_shard scores the probed
+ * positions in the window, keeping the global slot layout (the probe tables cluster_offsets /
+ * cluster_sizes and the filter are the whole table's), and writes its best min(k, width)
+ * as packed pairs out_pairs [B, min(k, width)]: raw score bits (fp32 of the int32 dot, or of
+ * the fp16 path's value) in the low 32 bits, the slot in the high 32 (padding -inf /
+ * 0xffffffff; workspace from rb_st_search_workspace_size). The pairs of all ranks merge with
+ * rb_merge_pairs (raw descending, slot ascending: the single-GPU tie order) into slots /
+ * raw [B, kin], and rb_st_search_finish maps each slot to its position through the whole
+ * table's layout, then to sort_perm and the dequantized score, padding to k. The result
+ * equals rb_st_search's on the whole table, ties included.
+ */
+RB_API int rb_st_search_shard(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                              const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                              int64_t N, int64_t pos_lo, int64_t pos_hi, const int8_t* item_codes, int k,
+                              int max_tensor_size_per_row, int divisor_for_int8, const rb_st_filter* filter,
+                              uint64_t* out_pairs, void* workspace, size_t workspace_bytes, void* stream);
+RB_API int rb_st_search_finish_workspace_size(int B, int D, int P, size_t* bytes);
+RB_API int rb_st_search_finish(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                               const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                               int64_t N, const int64_t* sort_perm, const float* global_scale, int k,
+                               int max_tensor_size_per_row, int divisor_for_int8, const int64_t* slots,
+                               const float* raw, int kin, int64_t* out_ids, float* out_scores, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
  * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)
  *   -> (codes int8 [B, D], scales fp32 [B], cluster_ids int64 [B, P],
  *       cluster_length int64 [B, P], cluster_offsets int64 [B, P], warps int32 [B * P],

@@ -357,3 +357,79 @@ def bloom_index_build(feature_ids, feature_offsets, feature_values, b_multiplier
                 for p in build_positions(int(fid[f]), int(v), int(widths[bundle]), k):
                     index[(boff[bundle] + p) * 32 + col] |= bit
     return index.view(np.int64), boff
+
+
+# ---------------------------------------------------------------------------
+# Row-sharded IVF search: a rank holds the positions [pos_lo, pos_hi) (whole
+# clusters), scores them in the global slot layout and returns (raw, slot) pairs;
+# the pairs of all ranks merge by (raw desc, slot asc) — the single-GPU tie order —
+# and the merged slots map back to positions through the global layout.
+# ---------------------------------------------------------------------------
+def search_shard(query, probe_ids, cluster_offsets, cluster_sizes, codes_local, pos_lo, k, max_tensor_size_per_row,
+                 divisor_for_int8=-1, filtering_bit_mask=None, exact=None):
+    """One rank's part: ``(raw [B, k'], slot [B, k'])`` of its best in-window positions
+    (``k' = min(k, width)``, ``-inf`` / ``-1`` pads); ``codes_local`` holds the rows
+    ``pos_lo ..`` of the sorted table."""
+    q_codes, _ = quantize_int8(np.asarray(query, dtype=np.float32))
+    probe_ids = np.asarray(probe_ids, dtype=np.int64)
+    codes_local = np.asarray(codes_local, dtype=np.int8)
+    pos_hi = pos_lo + codes_local.shape[0]
+    width = padded_width(max_tensor_size_per_row)
+    k_sel = min(k, width)
+    b = q_codes.shape[0]
+    raw_out = np.full((b, k_sel), -np.inf, dtype=np.float64)
+    slot_out = np.full((b, k_sel), -1, dtype=np.int64)
+    for row in range(b):
+        pos = probe_slots(probe_ids[row], cluster_offsets, cluster_sizes)
+        slot = np.arange(pos.size, dtype=np.int64)
+        keep = (pos >= pos_lo) & (pos < pos_hi) & (slot < width)
+        if filtering_bit_mask is not None:
+            keep &= mask_bit_high_first(np.asarray(filtering_bit_mask)[row], pos)
+        if exact is not None:
+            keep &= exact_pass(exact[0], exact[1], exact[2], np.asarray(exact[3])[row], pos)
+        pos, slot = pos[keep], slot[keep]
+        raw = raw_scores(q_codes[row], codes_local, pos - pos_lo, divisor_for_int8).astype(np.float64)
+        order = np.lexsort((slot, -raw))[:k_sel]
+        raw_out[row, : order.size] = raw[order]
+        slot_out[row, : order.size] = slot[order]
+    return raw_out, slot_out
+
+
+def merge_shards(raws, slots, k):
+    """The ranks' pairs to the global best ``k`` by (raw desc, slot asc)."""
+    raw = np.concatenate(raws, axis=1)
+    slot = np.concatenate(slots, axis=1)
+    b = raw.shape[0]
+    out_r = np.full((b, k), -np.inf)
+    out_s = np.full((b, k), -1, dtype=np.int64)
+    for row in range(b):
+        ok = slot[row] >= 0
+        r, s = raw[row][ok], slot[row][ok]
+        order = np.lexsort((s, -r))[:k]
+        out_r[row, : order.size] = r[order]
+        out_s[row, : order.size] = s[order]
+    return out_r, out_s
+
+
+def finish_shards(query, probe_ids, cluster_offsets, cluster_sizes, sort_perm, global_scale, raw, slot,
+                  divisor_for_int8=-1):
+    """Merged (raw, slot) to ``(ids, scores)``: the slot's position in the global layout,
+    ``sort_perm`` and the epilogue's two multiplies."""
+    _, q_scales = quantize_int8(np.asarray(query, dtype=np.float32))
+    gs = np.float32(np.asarray(global_scale, dtype=np.float32).reshape(-1)[0])
+    sort_perm = np.asarray(sort_perm, dtype=np.int64)
+    b, k = raw.shape
+    ids = np.full((b, k), -1, dtype=np.int64)
+    scores = np.full((b, k), -np.inf, dtype=np.float32)
+    for row in range(b):
+        pos = probe_slots(np.asarray(probe_ids)[row], cluster_offsets, cluster_sizes)
+        for j in range(k):
+            if slot[row, j] < 0:
+                continue
+            ids[row, j] = sort_perm[pos[slot[row, j]]]
+            r = np.float32(raw[row, j])
+            if divisor_for_int8 == -1:
+                scores[row, j] = np.float32(np.float32(r * q_scales[row]) * gs)
+            else:
+                scores[row, j] = r * np.float32(np.float32(q_scales[row] * np.float32(divisor_for_int8)) * gs)
+    return ids, scores

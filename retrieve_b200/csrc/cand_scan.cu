@@ -358,7 +358,7 @@ int cand_i8_max_k() { return 1024; }
 
 int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const int64_t* pos, int P,
                  const int64_t* counts, int B, int k, int divisor, int64_t* out_slots, float* out_raw, void* workspace,
-                 cudaStream_t s) {
+                 cudaStream_t s, uint2* out_pairs) {
   const CandPlan pl = cand_plan(B, P);
   const int cap = cand_i8_cap(k);
   uint2* lists = static_cast<uint2*>(workspace);
@@ -373,7 +373,7 @@ int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const
     cand_scan_kernel<2, int8_t, int8_t, kCandCapLarge><<<grid, 32 * kCandWarps, smem, s>>>(prm);
   const int rc = check_launch();
   if (rc != RB_OK) return rc;
-  return merge_lists(lists, lcounts, B, pl.n_lists, cap, k, 0, out_slots, out_raw, nullptr, s);
+  return merge_lists(lists, lcounts, B, pl.n_lists, cap, k, 0, out_slots, out_raw, out_pairs, s);
 }
 
 // Hamming full-scan plan

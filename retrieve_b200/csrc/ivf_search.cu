@@ -234,8 +234,8 @@ __device__ __forceinline__ void block_scan2(int64_t (&part)[2][kExpandThreads], 
 
 __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
     const int64_t* __restrict__ probe_ids, int P, const int64_t* __restrict__ offsets,
-    const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, FilterSet f, int width,
-    int64_t* __restrict__ pos, int64_t* __restrict__ counts) {
+    const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, FilterSet f, int width, int64_t pos_lo,
+    int64_t pos_hi, int64_t* __restrict__ pos, int64_t* __restrict__ counts) {
   // per probe: start (int64), len, head slot, tail slot (int32, slots clipped to width)
   extern __shared__ __align__(16) uint8_t sm[];
   int64_t* p_start = reinterpret_cast<int64_t*>(sm);
@@ -284,7 +284,10 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
   int64_t* out = pos + static_cast<int64_t>(b) * width;
   auto emit = [&](int64_t slot, int64_t position) {
     if (slot >= width) return;
-    out[slot] = pos_passes<true>(f, b, position) ? position : -1;
+    // positions outside this table's window [pos_lo, pos_hi) keep their slot but are not scored;
+    // the scorer reads the row position - pos_lo of its table
+    const bool in = position >= pos_lo && position < pos_hi;
+    out[slot] = in && pos_passes<true>(f, b, position) ? position - pos_lo : -1;
   };
   for (int j = warp; j < P; j += kExpandThreads / 32) {
     const int64_t start = p_start[j];
@@ -854,15 +857,26 @@ int rb_st_search_workspace_size(int B, int D, int P, int k, int max_tensor_size_
   return RB_OK;
 }
 
-int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P, const int64_t* cluster_offsets,
-                 const int64_t* cluster_sizes, int64_t n_lists, const int8_t* item_codes, int64_t N,
-                 const int64_t* sort_perm, const float* global_scale, int k, int max_tensor_size_per_row,
-                 int divisor_for_int8, const rb_st_filter* filter, int64_t* out_ids, float* out_scores,
-                 void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = st_check(B, D, P, n_lists, N, k, max_tensor_size_per_row, divisor_for_int8);
+}  // extern "C"
+
+// The row path over the positions [pos_lo, pos_hi) of a table of n_total positions (the
+// whole table: 0, n_total); item_codes holds the window's rows. With out_pairs the
+// winners are written as (raw score bits, slot) pairs and nothing else; otherwise the
+// epilogue writes ids (sort_perm indexed by position) and scores.
+static int st_row_search(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                         const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                         int64_t n_total, int64_t pos_lo, int64_t pos_hi, const int8_t* item_codes,
+                         const int64_t* sort_perm, const float* global_scale, int k, int max_tensor_size_per_row,
+                         int divisor_for_int8, const rb_st_filter* filter, int64_t* out_ids, float* out_scores,
+                         uint64_t* out_pairs, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = st_check(B, D, P, n_lists, n_total, k, max_tensor_size_per_row, divisor_for_int8);
   if (rc != RB_OK) return rc;
+  if (pos_lo < 0 || pos_hi < pos_lo || pos_hi > n_total) {
+    set_last_error("st::search: the position window must lie in [0, N]");
+    return RB_ERR_INVALID_ARG;
+  }
   FilterSet fs;
-  rc = build_filters(filter, N, fs);
+  rc = build_filters(filter, n_total, fs);
   if (rc != RB_OK) return rc;
   if (B == 0) return RB_OK;
   const int width = st_width(max_tensor_size_per_row);
@@ -885,22 +899,51 @@ int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int
   if (rc != RB_OK) return rc;
   if (width == 0) {
     // nothing can be probed: every row is all -1 / -inf
-    fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, s);
+    if (out_pairs != nullptr)
+      fill_empty_pairs(reinterpret_cast<uint2*>(out_pairs), static_cast<size_t>(B) * k_sel, s);
+    else
+      fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, s);
     return launch_status();
   }
   const size_t smem = static_cast<size_t>(P) * (sizeof(int64_t) + 3 * sizeof(int));
-  probe_expand_kernel<<<B, kExpandThreads, smem, s>>>(
-      probe_ids, P, cluster_offsets, cluster_sizes, n_lists, N, fs, width, pos, counts);
+  probe_expand_kernel<<<B, kExpandThreads, smem, s>>>(probe_ids, P, cluster_offsets, cluster_sizes, n_lists, n_total,
+                                                      fs, width, pos_lo, pos_hi, pos, counts);
   rc = launch_status();
   if (rc != RB_OK) return rc;
-  rc = cand_i8_topk(q_codes, item_codes, static_cast<int>(N), D, pos, width, counts, B, k_sel, divisor_for_int8,
-                    slots, raw, ws + lay.cand, s);
-  if (rc != RB_OK) return rc;
+  rc = cand_i8_topk(q_codes, item_codes, static_cast<int>(pos_hi - pos_lo), D, pos, width, counts, B, k_sel,
+                    divisor_for_int8, slots, raw, ws + lay.cand, s, reinterpret_cast<uint2*>(out_pairs));
+  if (rc != RB_OK || out_pairs != nullptr) return rc;
   const int64_t n = static_cast<int64_t>(B) * k;
   const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
-  st_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, k_sel, pos, counts, width, sort_perm, N, q_scales, global_scale,
-                                          divisor_for_int8, B, k, out_ids, out_scores);
+  st_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, k_sel, pos, counts, width, sort_perm, n_total, q_scales,
+                                          global_scale, divisor_for_int8, B, k, out_ids, out_scores);
   return launch_status();
+}
+
+extern "C" {
+
+int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P, const int64_t* cluster_offsets,
+                 const int64_t* cluster_sizes, int64_t n_lists, const int8_t* item_codes, int64_t N,
+                 const int64_t* sort_perm, const float* global_scale, int k, int max_tensor_size_per_row,
+                 int divisor_for_int8, const rb_st_filter* filter, int64_t* out_ids, float* out_scores,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  return st_row_search(query, B, D, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, N, 0, N, item_codes,
+                       sort_perm, global_scale, k, max_tensor_size_per_row, divisor_for_int8, filter, out_ids,
+                       out_scores, nullptr, workspace, workspace_bytes, stream);
+}
+
+int rb_st_search_shard(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                       const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists, int64_t N,
+                       int64_t pos_lo, int64_t pos_hi, const int8_t* item_codes, int k, int max_tensor_size_per_row,
+                       int divisor_for_int8, const rb_st_filter* filter, uint64_t* out_pairs, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  if (out_pairs == nullptr) {
+    set_last_error("st::search shard: out_pairs is required");
+    return RB_ERR_INVALID_ARG;
+  }
+  return st_row_search(query, B, D, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, N, pos_lo, pos_hi,
+                       item_codes, nullptr, nullptr, k, max_tensor_size_per_row, divisor_for_int8, filter, nullptr,
+                       nullptr, out_pairs, workspace, workspace_bytes, stream);
 }
 
 // Workspace of the grouped path: q codes [B, D] | q scales [B] | cnt, fill [L] int |
@@ -1047,6 +1090,69 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   st_group_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, k_sel, probe_ids, P, cluster_offsets, cluster_sizes,
                                                 n_lists, head, tail, total, width, sort_perm, N, q_scales,
                                                 global_scale, divisor_for_int8, B, k, out_ids, out_scores);
+  return launch_status();
+}
+
+static size_t finish_ws(int B, int D, int P, size_t* at) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t a = off;
+    off += align_up(bytes, 256);
+    return a;
+  };
+  at[0] = take(static_cast<size_t>(B) * D);                        // q codes
+  at[1] = take(static_cast<size_t>(B) * sizeof(float));            // q scales
+  at[2] = take(static_cast<size_t>(B) * P * sizeof(int64_t));      // head starts
+  at[3] = take(static_cast<size_t>(B) * P * sizeof(int64_t));      // tail starts
+  at[4] = take(static_cast<size_t>(B) * sizeof(int64_t));          // row totals
+  return off;
+}
+
+int rb_st_search_finish_workspace_size(int B, int D, int P, size_t* bytes) {
+  if (bytes == nullptr || B < 0 || D <= 0 || P < 0) {
+    set_last_error("st_search_finish_workspace_size: bad arguments");
+    return RB_ERR_INVALID_ARG;
+  }
+  size_t at[5];
+  *bytes = finish_ws(B, D, P, at);
+  return RB_OK;
+}
+
+int rb_st_search_finish(const float* query, int B, int D, const int64_t* probe_ids, int P,
+                        const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists, int64_t N,
+                        const int64_t* sort_perm, const float* global_scale, int k, int max_tensor_size_per_row,
+                        int divisor_for_int8, const int64_t* slots, const float* raw, int kin, int64_t* out_ids,
+                        float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = st_check(B, D, P, n_lists, N, k, max_tensor_size_per_row, divisor_for_int8);
+  if (rc != RB_OK) return rc;
+  if (kin < 0 || kin > k) {
+    set_last_error("st::search finish: the merged lists must hold at most k entries a row");
+    return RB_ERR_INVALID_ARG;
+  }
+  if (B == 0) return RB_OK;
+  size_t at[5];
+  const size_t need = finish_ws(B, D, P, at);
+  if (workspace == nullptr || workspace_bytes < need) {
+    set_last_error("st::search finish: workspace too small");
+    return RB_ERR_WORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* q_scales = reinterpret_cast<float*>(ws + at[1]);
+  int64_t* head = reinterpret_cast<int64_t*>(ws + at[2]);
+  int64_t* tail = reinterpret_cast<int64_t*>(ws + at[3]);
+  int64_t* total = reinterpret_cast<int64_t*>(ws + at[4]);
+  rc = rb_quantize_int8(query, B, D, reinterpret_cast<int8_t*>(ws + at[0]), q_scales, stream);
+  if (rc != RB_OK) return rc;
+  const int width = st_width(max_tensor_size_per_row);
+  if (P > 0)
+    slot_starts_kernel<<<(B + 127) / 128, 128, 0, s>>>(probe_ids, B, P, cluster_offsets, cluster_sizes, n_lists, N,
+                                                        width, head, tail, total);
+  const int64_t n = static_cast<int64_t>(B) * k;
+  const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
+  st_group_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, kin, probe_ids, P, cluster_offsets, cluster_sizes, n_lists,
+                                                head, tail, total, width, sort_perm, N, q_scales, global_scale,
+                                                divisor_for_int8, B, k, out_ids, out_scores);
   return launch_status();
 }
 

@@ -60,9 +60,10 @@ void fill_empty(int64_t* out_ids, float* out_scores, size_t n, cudaStream_t stre
 // Writes the winners' slots and raw scores, -1 / -inf past the candidates.
 size_t cand_i8_ws_bytes(int B, int P, int k);
 int cand_i8_max_k();
+// With out_pairs not null the winners go there instead, as (raw score bits, slot) pairs.
 int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const int64_t* pos, int P,
                  const int64_t* counts, int B, int k, int divisor, int64_t* out_slots, float* out_raw, void* workspace,
-                 cudaStream_t s);
+                 cudaStream_t s, uint2* out_pairs = nullptr);
 
 void fill_empty_pairs(uint2* out, size_t n, cudaStream_t stream);
 

@@ -244,3 +244,72 @@ class ShardedOneBitRerank:
         ids2, sc2 = ops.fused_masked_knn_topk(query, self.items, local, counts, k2)
         ids2 = torch.where(ids2 >= 0, ids2 + self.id_offset, ids2)
         return self._exchange(ids2, sc2, self.k)
+
+
+def ivf_shard_bounds(cluster_offsets, world: int, rank: int) -> tuple[int, int, int, int]:
+    """Rank ``rank``'s share of a cluster-sorted IVF table: clusters ``[c_lo, c_hi)`` and their
+    sorted positions ``[pos_lo, pos_hi)``. Whole clusters, cut where the position count
+    crosses ``n * r / world``."""
+    import bisect
+
+    off = [int(x) for x in (cluster_offsets.tolist() if hasattr(cluster_offsets, "tolist") else cluster_offsets)]
+    n, n_lists = off[-1], len(off) - 1
+
+    def cut(r: int) -> int:
+        return 0 if r == 0 else n_lists if r == world else bisect.bisect_left(off, (n * r) // world, 0, n_lists)
+
+    c_lo, c_hi = cut(rank), cut(rank + 1)
+    return c_lo, c_hi, off[c_lo], off[c_hi]
+
+
+class ShardedIVFSearch:
+    """``st::search`` over a cluster-sorted int8 table split across ranks by whole clusters
+    (``ivf_shard_bounds``). Every rank holds its rows ``[pos_lo, pos_hi)`` of the codes and
+    the whole table's small tables (cluster offsets and sizes, ``sort_perm``, the filter's
+    tables); the query batch and its probe lists are replicated. One search:
+
+    1. every rank scores the probed positions it holds, in the whole table's slot layout, and
+       keeps its best ``min(k, width)`` as packed (raw score, slot) pairs (``st.search_shard``);
+    2. one all-gather brings the ``[W, B, k']`` pairs to every rank and ``merge_pairs``
+       reduces them by (raw descending, slot ascending) — the single-GPU order, ties included;
+    3. ``st.search_finish`` maps each slot to its position, id and dequantized score.
+
+    The result equals ``st::search`` on the whole table on one GPU, bit for bit.
+    """
+
+    def __init__(self, codes_shard: Tensor, pos_lo: int, cluster_offsets: Tensor, cluster_sizes: Tensor,
+                 sort_perm: Tensor, global_scale: Tensor, group=None) -> None:
+        self.codes = codes_shard.contiguous()
+        self.pos_lo = int(pos_lo)
+        self.offsets = cluster_offsets
+        self.sizes = cluster_sizes
+        self.sort_perm = sort_perm
+        self.global_scale = global_scale
+        self.n_total = int(sort_perm.numel())
+        self.group = group
+
+    def local(self, query: Tensor, probe_ids: Tensor, k: int, width: int, divisor: int, filters: dict) -> Tensor:
+        from retrieve_b200 import st
+
+        return st.search_shard(query, probe_ids, self.offsets, self.sizes, self.n_total, self.pos_lo, self.codes, k,
+                               width, divisor, **filters)
+
+    def merge(self, stack: Tensor, k: int) -> tuple[Tensor, Tensor]:
+        return ops.merge_pairs(stack, k)
+
+    def finish(self, query: Tensor, probe_ids: Tensor, k: int, width: int, slots: Tensor, raw: Tensor,
+               divisor: int) -> tuple[Tensor, Tensor]:
+        from retrieve_b200 import st
+
+        return st.search_finish(query, probe_ids, self.offsets, self.sizes, self.sort_perm, self.global_scale, k,
+                                width, slots, raw, divisor)
+
+    def search(self, query: Tensor, probe_ids: Tensor, k: int, max_tensor_size_per_row: int,
+               divisor_for_int8: int = -1, **filters) -> tuple[Tensor, Tensor]:
+        pairs = self.local(query, probe_ids, k, max_tensor_size_per_row, divisor_for_int8, filters)
+        world = dist.get_world_size(self.group)
+        b, kin = pairs.shape
+        gathered = torch.empty((world * b, kin), dtype=pairs.dtype, device=pairs.device)
+        dist.all_gather_into_tensor(gathered, pairs.contiguous(), group=self.group)
+        slots, raw = self.merge(gathered.view(world, b, kin), kin)
+        return self.finish(query, probe_ids, k, max_tensor_size_per_row, slots, raw, divisor_for_int8)

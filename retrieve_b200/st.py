@@ -91,30 +91,25 @@ def search_grouped(*args, **kwargs) -> tuple[Tensor, Tensor]:
     return _search(True, *args, **kwargs)
 
 
-def _search(
-    grouped: bool,
-    query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor, item_codes: Tensor,
-    sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int = -1,
-    filtering_bit_mask: Tensor | None = None, bloom_index: Tensor | None = None,
-    bloom_bundle_b_offsets: Tensor | None = None, plans: Tensor | None = None, plan_count: int = 0,
-    max_stack_size: int = 0, query_plan_index: Tensor | None = None, bloom_k: int = 0, hash_k: int = 0,
-    item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
-    clause_is_reverse: Tensor | None = None, query_clause_attrs: Tensor | None = None,
-) -> tuple[Tensor, Tensor]:
-    """Filters: a full-``N`` ``filtering_bit_mask``; the exact clauses
-    (``item_clause_attrs``, ``clause_slots``, ``clause_is_reverse``,
-    ``query_clause_attrs``); or SilverTorch's bloom (``bloom_index``,
-    ``bloom_bundle_b_offsets``, the prepared ``plans`` blob of ``plan_count`` slots,
-    ``max_stack_size``, ``query_plan_index``, ``bloom_k``, ``hash_k``), false positives
-    kept. With bloom plans and the exact clauses together (the bloom with its exact
-    recheck) the result is the exact filter's, since the bloom has no false negatives;
-    the plans are then not read."""
+_FILTER_DOC = """Filters: a full-``N`` ``filtering_bit_mask``; the exact clauses
+    (``item_clause_attrs``, ``clause_slots``, ``clause_is_reverse``, ``query_clause_attrs``);
+    or SilverTorch's bloom (``bloom_index``, ``bloom_bundle_b_offsets``, the prepared ``plans``
+    blob of ``plan_count`` slots, ``max_stack_size``, ``query_plan_index``, ``bloom_k``,
+    ``hash_k``), false positives kept. With bloom plans and the exact clauses together (the
+    bloom with its exact recheck) the result is the exact filter's, since the bloom has no
+    false negatives; the plans are then not read."""
+
+
+def _filter(query: Tensor, n_items: int, filtering_bit_mask=None, bloom_index=None, bloom_bundle_b_offsets=None,
+            plans=None, plan_count=0, max_stack_size=0, query_plan_index=None, bloom_k=0, hash_k=0,
+            item_clause_attrs=None, clause_slots=None, clause_is_reverse=None, query_clause_attrs=None):
+    """The call's ``rb_st_filter`` (or None) and the tensors it points into."""
     exact = query_clause_attrs is not None
     _check(not (filtering_bit_mask is not None and (plans is not None or exact)),
            "search takes one filter: plans (+ query_clause_attrs to recheck), query_clause_attrs or "
            "filtering_bit_mask")
     flt = _lib.StFilter()
-    use_filter = False
+    keep: list[Tensor] = []
     if exact:
         _check(item_clause_attrs is not None and clause_slots is not None and clause_is_reverse is not None,
                "the exact filter needs item_clause_attrs, clause_slots and clause_is_reverse")
@@ -131,15 +126,15 @@ def _search(
         _check(clause_slots.shape[0] == n_clauses + 1 and clause_is_reverse.numel() == n_clauses,
                "clause_slots must have C + 1 entries and clause_is_reverse C")
         _check(query_clause_attrs.shape[0] == query.shape[0], "query_clause_attrs must have B rows")
-        _check(item_clause_attrs.shape[1] >= item_codes.shape[0], "item_clause_attrs must cover the N docs")
+        _check(item_clause_attrs.shape[1] >= n_items, "item_clause_attrs must cover the N docs")
         flt.item_clause_attrs = item_clause_attrs.data_ptr()
         flt.attr_rows, flt.attr_docs = item_clause_attrs.shape
         flt.clause_slots = clause_slots.data_ptr()
         flt.clause_is_reverse = clause_is_reverse.data_ptr()
         flt.query_clause_attrs = query_clause_attrs.data_ptr()
         flt.n_clauses = n_clauses
-        use_filter = True
-    elif plans is not None:
+        return flt, keep
+    if plans is not None:
         _check(bloom_index is not None and bloom_bundle_b_offsets is not None,
                "the bloom filter needs bloom_index and bloom_bundle_b_offsets")
         for name, t in (("bloom_index", bloom_index), ("bloom_bundle_b_offsets", bloom_bundle_b_offsets),
@@ -164,10 +159,33 @@ def _search(
         flt.query_plan_index = 0 if query_plan_index is None else query_plan_index.data_ptr()
         flt.bloom_k = int(bloom_k)
         flt.hash_k = int(hash_k)
-        use_filter = True
+        return flt, keep
+    if filtering_bit_mask is not None:
+        _check(filtering_bit_mask.dim() == 2 and filtering_bit_mask.shape[0] == query.shape[0],
+               "filtering_bit_mask must be [B, words]")
+        mask = filtering_bit_mask.to(device=query.device, dtype=torch.int64).contiguous()
+        keep.append(mask)
+        flt.filtering_bit_mask = mask.data_ptr()
+        flt.mask_words = mask.shape[1]
+        return flt, keep
+    return None, keep
+
+
+def _codes_check(item_codes: Tensor, query: Tensor) -> None:
+    """The reference's first check (fork_search_cuda.cu:1280), before any device check."""
     _check(item_codes.dtype == torch.int8 and item_codes.dim() == 2 and item_codes.shape[1] == query.shape[1],
            "item_codes must be int8 [N, D] with the query's D")
     _check(item_codes.is_contiguous(), "item_codes must be contiguous")
+
+
+def _search(
+    grouped: bool,
+    query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor, item_codes: Tensor,
+    sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int = -1,
+    **filters,
+) -> tuple[Tensor, Tensor]:
+    _codes_check(item_codes, query)
+    flt, keep = _filter(query, item_codes.shape[0], **filters)
     q, probe, offsets, sizes = _layout_args(query, probe_ids, cluster_offsets, cluster_sizes)
     _check(item_codes.device == q.device, "item_codes must be on the query's device")
     _check(offsets.numel() == sizes.numel() + 1, "cluster_offsets must have n_lists + 1 entries")
@@ -176,14 +194,6 @@ def _search(
     perm = sort_perm.to(device=dev, dtype=torch.int64).contiguous()
     gs = global_scale.to(device=dev, dtype=torch.float32).reshape(-1)[:1].contiguous()
     _check(gs.numel() == 1, "global_scale must hold one value")
-    mask = None
-    if filtering_bit_mask is not None:
-        _check(filtering_bit_mask.dim() == 2 and filtering_bit_mask.shape[0] == q.shape[0],
-               "filtering_bit_mask must be [B, words]")
-        mask = filtering_bit_mask.to(device=dev, dtype=torch.int64).contiguous()
-        flt.filtering_bit_mask = mask.data_ptr()
-        flt.mask_words = mask.shape[1]
-        use_filter = True
     b, d = q.shape
     p = probe.shape[1]
     _check(k >= 1, f"k must be positive, got {k}")
@@ -203,10 +213,77 @@ def _search(
     rc = (lib.rb_st_search_grouped if grouped else lib.rb_st_search)(
         _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), _ptr(item_codes),
         item_codes.shape[0], _ptr(perm), _ptr(gs), k, int(max_tensor_size_per_row), int(divisor_for_int8),
-        ctypes.byref(flt) if use_filter else None,
-        _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream(dev),
+        ctypes.byref(flt) if flt is not None else None, _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream(dev),
     )
     _call(rc, "st::search")
+    del keep
+    return ids, scores
+
+
+_search.__doc__ = _FILTER_DOC
+
+
+def search_shard(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor, n_total: int,
+                 pos_lo: int, item_codes: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int = -1,
+                 **filters) -> Tensor:
+    """One rank's part of a row-sharded ``st::search`` (``rb_st_search_shard``): the table's
+    rows ``[pos_lo, pos_lo + len(item_codes))`` scored in the whole table's slot layout →
+    packed ``(raw score bits, slot)`` pairs ``[B, min(k, width)]`` int64 for ``ops.merge_pairs``.
+    The probe tables and the filter are the whole table's."""
+    _codes_check(item_codes, query)
+    flt, keep = _filter(query, int(n_total), **filters)
+    q, probe, offsets, sizes = _layout_args(query, probe_ids, cluster_offsets, cluster_sizes)
+    _check(item_codes.device == q.device, "item_codes must be on the query's device")
+    b, d = q.shape
+    p = probe.shape[1]
+    _check(k >= 1, f"k must be positive, got {k}")
+    width = (int(max_tensor_size_per_row) + 31) // 32 * 32
+    pairs = torch.empty((b, min(k, width)), dtype=torch.int64, device=q.device)
+    if b == 0:
+        return pairs
+    lib = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _call(lib.rb_st_search_workspace_size(b, d, p, k, int(max_tensor_size_per_row), ctypes.byref(nbytes)),
+          "st::search shard")
+    ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=q.device)
+    rc = lib.rb_st_search_shard(
+        _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), int(n_total), int(pos_lo),
+        int(pos_lo) + item_codes.shape[0], _ptr(item_codes), k, int(max_tensor_size_per_row), int(divisor_for_int8),
+        ctypes.byref(flt) if flt is not None else None, _ptr(pairs), _ptr(ws), ws.numel(), _stream(q.device),
+    )
+    _call(rc, "st::search shard")
+    del keep
+    return pairs
+
+
+def search_finish(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor,
+                  sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, slots: Tensor,
+                  raw: Tensor, divisor_for_int8: int = -1) -> tuple[Tensor, Tensor]:
+    """Merged ``(slots, raw)`` ``[B, kin]`` of a row-sharded search → ``(ids [B, k], scores
+    [B, k])`` through the whole table's layout (``rb_st_search_finish``)."""
+    q, probe, offsets, sizes = _layout_args(query, probe_ids, cluster_offsets, cluster_sizes)
+    dev = q.device
+    b, d = q.shape
+    p = probe.shape[1]
+    perm = sort_perm.to(device=dev, dtype=torch.int64).contiguous()
+    gs = global_scale.to(device=dev, dtype=torch.float32).reshape(-1)[:1].contiguous()
+    sl = slots.to(device=dev, dtype=torch.int64).contiguous()
+    rw = raw.to(device=dev, dtype=torch.float32).contiguous()
+    _check(sl.shape == rw.shape and sl.dim() == 2 and sl.shape[0] == b, "slots and raw must both be [B, kin]")
+    ids = torch.empty((b, k), dtype=torch.int64, device=dev)
+    scores = torch.empty((b, k), dtype=torch.float32, device=dev)
+    if b == 0:
+        return ids, scores
+    lib = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _call(lib.rb_st_search_finish_workspace_size(b, d, p, ctypes.byref(nbytes)), "st::search finish")
+    ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
+    rc = lib.rb_st_search_finish(
+        _ptr(q), b, d, _ptr(probe), p, _ptr(offsets), _ptr(sizes), sizes.numel(), perm.numel(), _ptr(perm), _ptr(gs),
+        k, int(max_tensor_size_per_row), int(divisor_for_int8), _ptr(sl), _ptr(rw), sl.shape[1], _ptr(ids),
+        _ptr(scores), _ptr(ws), ws.numel(), _stream(dev),
+    )
+    _call(rc, "st::search finish")
     return ids, scores
 
 

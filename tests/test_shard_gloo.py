@@ -59,3 +59,83 @@ def test_sharded_merge_equals_global_topk(world):
     for r in range(world):
         ids, scores = out[r]
         assert np.array_equal(scores, ref_s) and np.array_equal(ids, ref_i)
+
+
+def _pack_pairs(raw, slot):
+    """(raw, slot) [B, k] to the packed int64 pairs of rb_st_search_shard (raw score bits low,
+    slot high; padding -inf / 0xffffffff)."""
+    lo = np.asarray(raw, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    hi = np.where(slot >= 0, slot, 0xFFFFFFFF).astype(np.uint64)
+    return ((hi << np.uint64(32)) | lo).view(np.int64)
+
+
+def _unpack_pairs(pairs):
+    p = np.asarray(pairs).view(np.uint64)
+    raw = (p & np.uint64(0xFFFFFFFF)).astype(np.uint32).view(np.float32).astype(np.float64)
+    slot = (p >> np.uint64(32)).astype(np.int64)
+    return raw, np.where(slot == 0xFFFFFFFF, -1, slot)
+
+
+def _ivf_worker(rank, world, port, case, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    from oracle import ivf
+    from retrieve_b200.shard import ShardedIVFSearch, ivf_shard_bounds
+
+    g, k, width = case
+    _, _, lo, hi = ivf_shard_bounds(g["offsets"], world, rank)
+
+    class OracleShards(ShardedIVFSearch):
+        # the host logic of the exchange with the oracle in place of the kernels (CPU ranks)
+        def local(self, query, probe_ids, k, width, divisor, filters):
+            raw, slot = ivf.search_shard(query.numpy(), probe_ids.numpy(), g["offsets"], g["sizes"],
+                                         self.codes.numpy(), self.pos_lo, k, width)
+            return torch.from_numpy(_pack_pairs(raw, slot))
+
+        def merge(self, stack, k):
+            # (slots, raw), the order of ops.merge_pairs' (ids, scores)
+            raws, slots = zip(*(_unpack_pairs(s) for s in stack.numpy()))
+            raw, slot = ivf.merge_shards(list(raws), list(slots), k)
+            return slot, raw
+
+        def finish(self, query, probe_ids, k, width, slots, raw, divisor):
+            ids, scores = ivf.finish_shards(query.numpy(), probe_ids.numpy(), g["offsets"], g["sizes"],
+                                            g["sort_perm"], g["gs"], raw, slots)
+            return ids, scores
+
+    index = OracleShards(torch.from_numpy(g["codes"][lo:hi]), lo, g["offsets"], g["sizes"],
+                         torch.from_numpy(g["sort_perm"]), torch.from_numpy(g["gs"]))
+    ids, scores = index.search(torch.from_numpy(g["query"]), torch.from_numpy(g["probe"]), k, width)
+    out[rank] = (ids, scores)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_ivf_search_equals_single_search(world):
+    """Row-sharded st::search (whole clusters a rank): local (raw, slot) pairs in the whole
+    table's slot layout, one all-gather, the (raw desc, slot asc) merge and the slot -> id
+    finish give the single-table search bit for bit, ties included (the tie-heavy fixture
+    case)."""
+    from pathlib import Path
+
+    from oracle import ivf
+
+    golden = np.load(Path(__file__).resolve().parent / "golden" / "golden_ivf.npz")
+    p = "c6_"
+    g = {key[len(p):]: golden[key] for key in golden.files if key.startswith(p)}
+    n_lists, max_size, n_probe, d, k, b, width, div, ties = g["shape"].tolist()
+    assert ties
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    port = 29700 + 11 * world
+    mp.start_processes(_ivf_worker, args=(world, port, (g, k, width), out), nprocs=world, join=True,
+                       start_method="spawn")
+    want_i, want_s = ivf.search(g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"],
+                                g["gs"], k, width)
+    k_sel = min(k, ivf.padded_width(width))
+    for r in range(world):
+        ids, scores = out[r]
+        assert np.array_equal(ids, want_i[:, :k_sel]) and np.array_equal(scores, want_s[:, :k_sel])

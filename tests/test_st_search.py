@@ -477,3 +477,40 @@ def test_bloom_index_build_on_device():
         index_f, boff_f = st.bloom_index_build_fixed(*t, bits, int(BLOOM["k"]))
         want_i, want_b = ivf.bloom_index_build(fid, off, val, 2.0, int(BLOOM["k"]), bits_per_doc=bits)
         assert np.array_equal(boff_f.cpu().numpy(), want_b) and np.array_equal(index_f.cpu().numpy(), want_i)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 3, 8])
+@pytest.mark.parametrize("ci", [0, 3, 6])
+def test_sharded_search_on_one_gpu(world, ci):
+    """The row-sharded search's three steps on one GPU (the shards called in turn): the
+    [W, B, k'] pairs of rb_st_search_shard, rb_merge_pairs and rb_st_search_finish equal
+    the single-table st::search bit for bit, ties included, unfiltered and with the exact
+    clauses (whole-table filter tables on every shard)."""
+    _st()
+    from retrieve_b200 import ops, st
+    from retrieve_b200.shard import ivf_shard_bounds
+
+    g, meta = _case(ci)
+    t = {key: torch.from_numpy(np.ascontiguousarray(g[key])).cuda()
+         for key in ("query", "probe", "offsets", "sizes", "codes", "sort_perm")}
+    gs = torch.from_numpy(g["gs"]).cuda()
+    k, width = meta["k"], meta["width"]
+    rng = np.random.default_rng(ci)
+    _, rev, _, slots_t, clause_slots, qq = _exact_inputs(rng, g["codes"].shape[0], meta["b"])
+    exact = dict(item_clause_attrs=torch.from_numpy(slots_t).cuda(),
+                 clause_slots=torch.from_numpy(clause_slots).cuda(), clause_is_reverse=torch.from_numpy(rev).cuda(),
+                 query_clause_attrs=torch.from_numpy(qq).cuda())
+    for filters in ({}, exact):
+        want = torch.ops.st.search(t["query"], t["probe"], t["offsets"], t["sizes"], t["codes"], t["sort_perm"], gs,
+                                   k, width, **filters)
+        pairs = []
+        for r in range(world):
+            _, _, lo, hi = ivf_shard_bounds(g["offsets"], world, r)
+            pairs.append(st.search_shard(t["query"], t["probe"], t["offsets"], t["sizes"], g["codes"].shape[0], lo,
+                                         t["codes"][lo:hi], k, width, **filters))
+        stack = torch.stack(pairs).contiguous()
+        slots, raw = ops.merge_pairs(stack, stack.shape[2])
+        ids, scores = st.search_finish(t["query"], t["probe"], t["offsets"], t["sizes"], t["sort_perm"], gs, k,
+                                       width, slots, raw)
+        _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), want[0].cpu().numpy(), want[1].cpu().numpy())
