@@ -38,178 +38,13 @@
 #include "rb_capi_internal.h"
 #include "rb_common.cuh"
 #include "rb_select.cuh"
+#include "st_filters.cuh"
 
 namespace rb {
 
 constexpr int kExpandThreads = 256;
 constexpr int kMaxProbes = 2048;  // per-probe table: 20 bytes a probe in shared memory
 constexpr int kMaxSearchD = 1024;
-
-__device__ __forceinline__ void probe_range(const int64_t* __restrict__ offsets, const int64_t* __restrict__ sizes,
-                                            int64_t n_lists, int64_t N, int64_t c, int64_t& start, int64_t& len) {
-  start = 0;
-  len = 0;
-  if (c < 0 || c >= n_lists) return;
-  const int64_t s = offsets[c];
-  const int64_t l = sizes[c];
-  if (s < 0 || s >= N || l <= 0) return;
-  start = s;
-  len = l < N - s ? l : N - s;
-}
-
-// The exact clause filter (silvertorch/ops/csrc/fork_filters.cuh:15-41): attrs is the
-// clause-major int32 [rows, docs] slot table, clause c in slots
-// [clause_slots[c], clause_slots[c + 1]), each doc's values sorted descending with -1
-// pads last; a clause with query value -1 passes, otherwise it matches when one of the
-// doc's values equals the query's and passes when the match differs from reverse[c].
-// Consecutive lanes test consecutive positions, so each slot row reads coalesced.
-struct ExactArgs {
-  const int32_t* attrs;  // null: no exact filter
-  int64_t rows, docs;
-  const int64_t* clause_slots;
-  const uint8_t* reverse;
-  const int32_t* query;  // [B, n_clauses]
-  int n_clauses;
-};
-
-__device__ __forceinline__ bool exact_pass(const ExactArgs& ex, const int32_t* __restrict__ q, int64_t doc) {
-  for (int c = 0; c < ex.n_clauses; ++c) {
-    const int32_t qv = q[c];
-    if (qv == -1) continue;
-    bool match = false;
-    const int64_t s1 = min(ex.clause_slots[c + 1], ex.rows);
-    for (int64_t s = max(ex.clause_slots[c], int64_t{0}); s < s1; ++s) {
-      const int32_t v = ex.attrs[s * ex.docs + doc];
-      if (v == qv || v == -1) {
-        match = v == qv;
-        break;
-      }
-    }
-    if (match == (ex.reverse[c] != 0)) return false;
-  }
-  return true;
-}
-
-// SilverTorch's bloom filter on its own index and prepared plans (the op's `plans`
-// without the exact recheck; bloom_index_search_cuda.cu:304-349, 469-544). The index
-// is bundle-major: docs in bundles of 2048 (32 columns of 64), bundle i holding
-// B_i = bundle_b_offsets[i + 1] - bundle_b_offsets[i] bit rows; doc d's bit of row r is
-// bit 63 - d % 64 of word (bundle_b_offsets[d / 2048] + r) * 32 + (d / 64) % 32. The
-// plans blob holds, per plan slot, the parser's eight byte offsets (operators uint8,
-// their parameter offsets int32, parameters int32, stored hashes uint64) into the data
-// after the 8 * slots header words. A plan runs as a postfix stack over the doc's
-// column word: a term ANDs the rows of its first k distinct positions hash % B_i among
-// its hash_k hashes; AND / OR fold as many entries as their parameter range holds;
-// NOT complements; EMPTY is all ones. Every offset and index is checked against the
-// sizes passed in; a malformed plan fails the doc.
-constexpr int kBloomMaxK = 10;    // MAX_K_V2
-constexpr int kBloomStack = 16;   // deepest plan stack served
-constexpr int kBundleColumns = 32;
-
-struct BloomArgs {
-  const uint64_t* index;  // null: no bloom filter
-  int64_t index_words;
-  const int64_t* bundle_offsets;  // [n_bundles + 1]
-  int64_t n_bundles;
-  const int64_t* blob;
-  int64_t blob_words;
-  int slots;
-  const int64_t* plan_index;  // [B], or null: row b runs plan b
-  int k, hash_k;
-};
-
-__device__ bool bloom_pass(const BloomArgs& a, int64_t row, int64_t doc) {
-  const int64_t p = a.plan_index ? a.plan_index[row] : row;
-  if (p < 0 || p >= a.slots) return false;
-  const int64_t data_bytes = (a.blob_words - 8 * static_cast<int64_t>(a.slots)) * 8;
-  int64_t o[8];
-  for (int i = 0; i < 8; ++i) o[i] = a.blob[8 * p + i];
-  for (int i = 0; i < 8; i += 2)
-    if (o[i] < 0 || o[i] > o[i + 1] || o[i + 1] > data_bytes) return false;
-  if ((o[2] & 3) || (o[6] & 7)) return false;
-  const uint8_t* data = reinterpret_cast<const uint8_t*>(a.blob + 8 * static_cast<int64_t>(a.slots));
-  const uint8_t* ops = data + o[0];
-  const int64_t n_ops = o[1] - o[0];
-  const int32_t* op_off = reinterpret_cast<const int32_t*>(data + o[2]);
-  const int64_t n_off = (o[3] - o[2]) / 4;
-  const uint64_t* hashes = reinterpret_cast<const uint64_t*>(data + o[6]);
-  const int64_t n_hash = (o[7] - o[6]) / 8;
-  const int64_t column = doc >> 6;
-  const int64_t bundle = column / kBundleColumns;
-  if (bundle >= a.n_bundles) return false;
-  const int64_t b0 = a.bundle_offsets[bundle];
-  const int64_t bb = a.bundle_offsets[bundle + 1] - b0;
-  if (bb <= 0) return false;
-  const int64_t col = column % kBundleColumns;
-  uint64_t stack[kBloomStack];
-  int sp = 0;
-  int64_t term = 0;
-  for (int64_t j = 0; j < n_ops; ++j) {
-    const uint8_t op = ops[j];
-    if (op == 4) {  // TERM
-      uint64_t w = ~0ull;
-      if ((term + 1) * a.hash_k > n_hash) {
-        w = 0;
-      } else {
-        const uint64_t* h = hashes + term * a.hash_k;
-        int64_t used[kBloomMaxK];
-        int resolved = 0;
-        for (int q = 0; q < a.hash_k && resolved < a.k; ++q) {
-          const int64_t pos = static_cast<int64_t>(h[q] % static_cast<uint64_t>(bb));
-          bool dup = false;
-          for (int i = 0; i < resolved; ++i) dup |= used[i] == pos;
-          if (!dup) used[resolved++] = pos;
-        }
-        for (int i = 0; i < resolved; ++i) {
-          const int64_t wi = (b0 + used[i]) * kBundleColumns + col;
-          w &= (wi >= 0 && wi < a.index_words) ? a.index[wi] : 0ull;
-        }
-      }
-      ++term;
-      if (sp < kBloomStack) stack[sp++] = w; else return false;
-    } else if (op == 1 || op == 2) {  // AND, OR
-      const int64_t children = j + 1 < n_off ? static_cast<int64_t>(op_off[j + 1]) - op_off[j] : 0;
-      uint64_t acc = op == 1 ? ~0ull : 0ull;
-      for (int64_t i = 0; i < children; ++i) {
-        if (sp == 0) return false;
-        const uint64_t v = stack[--sp];
-        acc = op == 1 ? (acc & v) : (acc | v);
-      }
-      if (sp < kBloomStack) stack[sp++] = acc; else return false;
-    } else if (op == 3) {  // NOT
-      if (sp == 0) return false;
-      stack[sp - 1] = ~stack[sp - 1];
-    } else if (op == 5) {  // EMPTY
-      if (sp < kBloomStack) stack[sp++] = ~0ull; else return false;
-    }
-  }
-  if (sp == 0) return false;
-  return (stack[sp - 1] >> (63 - (doc & 63))) & 1ull;
-}
-
-// The filters of one search: at most one of a full-N mask (high bit first), the exact
-// clauses, the bloom plans.
-struct FilterSet {
-  const uint64_t* mask;
-  int64_t mask_words;
-  ExactArgs ex;
-  BloomArgs bloom;
-};
-
-// BLOOM = false compiles the bloom test out (the scan kernels without a bloom filter keep
-// their registers).
-template <bool BLOOM>
-__device__ __forceinline__ bool pos_passes(const FilterSet& f, int64_t row, int64_t position) {
-  if (f.mask != nullptr) {
-    const int64_t w = position >> 6;
-    if (w < f.mask_words && ((f.mask[row * f.mask_words + w] >> (63 - (position & 63))) & 1ull) == 0) return false;
-  }
-  if (f.ex.attrs != nullptr && !exact_pass(f.ex, f.ex.query + row * f.ex.n_clauses, position)) return false;
-  if constexpr (BLOOM) {
-    if (f.bloom.index != nullptr && !bloom_pass(f.bloom, row, position)) return false;
-  }
-  return true;
-}
 
 // Block-wide inclusive scan of two int64 values (kExpandThreads threads).
 __device__ __forceinline__ void block_scan2(int64_t (&part)[2][kExpandThreads], int64_t& a, int64_t& b) {
@@ -554,15 +389,6 @@ static size_t group_smem_bytes(int D) {
   return static_cast<size_t>(group_pairs_per_task(D)) * dp + kGroupTile * (dp + 16);
 }
 
-// Clipped length of probe (row, j) and its warp-aligned part, as probe_expand_kernel.
-__device__ __forceinline__ void clipped_probe(const int64_t* __restrict__ offsets, const int64_t* __restrict__ sizes,
-                                              int64_t n_lists, int64_t N, int64_t c, int width, int64_t& start,
-                                              int64_t& len, int64_t& full) {
-  probe_range(offsets, sizes, n_lists, N, c, start, len);
-  if (len > width) len = width;
-  full = len / 32 * 32;
-}
-
 __global__ void pair_count_kernel(const int64_t* __restrict__ probe, int64_t n_pairs, int64_t n_lists,
                                   int* __restrict__ cnt) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_pairs;
@@ -620,22 +446,8 @@ __global__ void slot_starts_kernel(const int64_t* __restrict__ probe, int B, int
                                    int64_t* __restrict__ row_total) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
-  const int64_t* prow = probe + static_cast<int64_t>(b) * P;
-  int64_t h = 0;
-  for (int j = 0; j < P; ++j) {
-    int64_t start, len, full;
-    clipped_probe(offsets, sizes, n_lists, N, prow[j], width, start, len, full);
-    head[static_cast<int64_t>(b) * P + j] = h;
-    h += full;
-  }
-  int64_t t = h;
-  for (int j = 0; j < P; ++j) {
-    int64_t start, len, full;
-    clipped_probe(offsets, sizes, n_lists, N, prow[j], width, start, len, full);
-    tail[static_cast<int64_t>(b) * P + j] = t;
-    t += len - full;
-  }
-  row_total[b] = t;
+  const int64_t o = static_cast<int64_t>(b) * P;
+  row_total[b] = row_slot_starts(probe + o, P, offsets, sizes, n_lists, N, width, head + o, tail + o);
 }
 
 struct GroupArgs {
@@ -811,20 +623,12 @@ __global__ void st_group_epilogue_kernel(const int64_t* __restrict__ slots, cons
       const int64_t slot = slots[b * k_sel + jo];
       const int64_t* hrow = head + b * P;
       const int64_t* trow = tail + b * P;
-      const int64_t total_head = trow[0];
       if (slot >= 0 && slot < width && slot < row_total[b]) {
-        const bool in_head = slot < total_head;
-        // smallest j whose range [start_j, start_{j+1}) ends past the slot
-        int lo = 0, hi = P - 1;
-        while (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          const int64_t end = in_head ? (mid + 1 < P ? hrow[mid + 1] : total_head)
-                                      : (mid + 1 < P ? trow[mid + 1] : row_total[b]);
-          if (end > slot) hi = mid; else lo = mid + 1;
-        }
+        bool in_head;
+        const int lo = slot_to_probe(hrow, trow, row_total[b], P, slot, in_head);
         int64_t start, len, full;
         clipped_probe(offsets, sizes, n_lists, N, probe[b * P + lo], width, start, len, full);
-        const int64_t in_cluster = in_head ? slot - hrow[lo] : full + (slot - trow[lo]);
+        const int64_t in_cluster = in_head ? slot - hrow[lo] : full + (slot - trow[lo]);  // row in the cluster
         const int64_t p = start + in_cluster;
         if (in_cluster >= 0 && in_cluster < len && p >= 0 && p < N) {
           id = sort_perm[p];
