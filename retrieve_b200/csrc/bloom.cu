@@ -6,42 +6,10 @@
 #include <algorithm>
 #include <cstdint>
 
+#include "bloom_hash.cuh"
 #include "rb_capi_internal.h"
 
 namespace rb {
-
-__device__ __forceinline__ uint64_t rotl64(uint64_t x, int r) { return (x << r) | (x >> (64 - r)); }
-
-__device__ __forceinline__ uint64_t fmix64(uint64_t k) {
-  k ^= k >> 33;
-  k *= 0xff51afd7ed558ccdull;
-  k ^= k >> 33;
-  k *= 0xc4ceb9fe1a85ec53ull;
-  k ^= k >> 33;
-  return k;
-}
-
-__device__ __forceinline__ uint64_t murmur3_pair(uint64_t x, uint64_t y, uint64_t seed) {
-  const uint64_t c1 = 0x87c37b91114253d5ull, c2 = 0x4cf5ad432745937full;
-  uint64_t h1 = seed, h2 = seed;
-  uint64_t k1 = rotl64(x * c1, 31) * c2;
-  h1 ^= k1;
-  h1 = rotl64(h1, 27) + h2;
-  h1 = h1 * 5 + 0x52dce729ull;
-  uint64_t k2 = rotl64(y * c2, 33) * c1;
-  h2 ^= k2;
-  h2 = rotl64(h2, 31) + h1;
-  h2 = h2 * 5 + 0x38495ab5ull;
-  h1 ^= 16;
-  h2 ^= 16;
-  h1 += h2;
-  h2 += h1;
-  h1 = fmix64(h1);
-  h2 = fmix64(h2);
-  h1 += h2;
-  h2 += h1;
-  return h1 ^ h2;
-}
 
 __global__ void bloom_build_kernel(const int64_t* __restrict__ attrs, int N, int C, int A, int k,
                                    uint64_t* __restrict__ words) {
@@ -82,8 +50,6 @@ __global__ void bloom_build_kernel(const int64_t* __restrict__ attrs, int N, int
 // ---------------------------------------------------------------------------
 constexpr int kBundleDocs = 2048;
 constexpr int kBloomThreads = 256;
-constexpr int kBloomMaxBuildK = 64;     // MAX_K
-constexpr int kBloomSeedLimit = 4096;   // seeds tried for k distinct positions
 
 __global__ void __launch_bounds__(kBloomThreads) bloom_bundle_width_kernel(
     const int64_t* __restrict__ feature_offsets, int64_t N, int C, int k, double b_multiplier, int64_t fixed_b,
@@ -101,7 +67,7 @@ __global__ void __launch_bounds__(kBloomThreads) bloom_bundle_width_kernel(
   if (threadIdx.x == 0) {
     int64_t mm = 0;
     for (int w = 0; w < kBloomThreads / 32; ++w) mm = max(mm, red[w]);
-    widths[bundle] = fixed_b > 0 ? fixed_b : static_cast<int64_t>(static_cast<double>(mm * k) * b_multiplier);
+    widths[bundle] = bloom_bundle_width(mm, k, b_multiplier, fixed_b);
   }
 }
 
@@ -142,8 +108,7 @@ __global__ void bloom_index_fill_kernel(const int32_t* __restrict__ feature_ids,
     const int64_t b0 = bundle_offsets[bundle];
     const int64_t bb = bundle_offsets[bundle + 1] - b0;
     if (bb <= 0) continue;
-    const int64_t col = (d % kBundleDocs) / 64;
-    const unsigned long long bit = 1ull << (63 - (d & 63));
+    const unsigned long long bit = bloom_bit(d);
     for (int c = 0; c < C; ++c) {
       const uint64_t fid = static_cast<uint64_t>(static_cast<int64_t>(feature_ids[c]));
       const int64_t v0 = max(feature_offsets[d * C + c], int64_t{0});
@@ -151,16 +116,9 @@ __global__ void bloom_index_fill_kernel(const int32_t* __restrict__ feature_ids,
       for (int64_t v = v0; v < v1; ++v) {
         const uint64_t value = static_cast<uint64_t>(feature_values[v]);
         int64_t used[kBloomMaxBuildK];
-        int n_used = 0;
-        for (int seed = 0; seed < kBloomSeedLimit && n_used < k; ++seed) {
-          const int64_t p = static_cast<int64_t>(murmur3_pair(fid, value, static_cast<uint64_t>(seed)) %
-                                                 static_cast<uint64_t>(bb));
-          bool dup = false;
-          for (int i = 0; i < n_used; ++i) dup |= used[i] == p;
-          if (!dup) used[n_used++] = p;
-        }
+        const int n_used = bloom_build_positions(fid, value, bb, k, used);
         for (int i = 0; i < n_used; ++i) {
-          const int64_t w = (b0 + used[i]) * 32 + col;
+          const int64_t w = bloom_word(b0, used[i], d);
           if (w >= 0 && w < index_words) atomicOr(index + w, bit);
         }
       }

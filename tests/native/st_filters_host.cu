@@ -60,3 +60,42 @@ int64_t host_slot_positions(const int64_t* prow, int P, const int64_t* offsets, 
 }
 
 }  // extern "C"
+
+#include "bloom_hash.cuh"
+
+extern "C" {
+
+// SilverTorch's bundle-major bloom index built on the CPU with the device build's functions
+// (bloom_hash.cuh): widths and offsets (n_bundles + 1 entries, caller-sized), then the words
+// (index: offsets[n_bundles] * 32 words, zeroed by the caller when index is not null).
+int host_bloom_build(const int32_t* feature_ids, const int64_t* feature_offsets, const int64_t* feature_values,
+                     int64_t N, int C, int k, double b_multiplier, int64_t fixed_b, int64_t* offsets,
+                     uint64_t* index) {
+  const int64_t n_bundles = (N + 2047) / 2048;
+  offsets[0] = 0;
+  for (int64_t i = 0; i < n_bundles; ++i) {
+    int64_t m = 0;
+    for (int64_t d = i * 2048; d < N && d < (i + 1) * 2048; ++d) {
+      const int64_t cnt = feature_offsets[(d + 1) * C] - feature_offsets[d * C];
+      m = cnt > m ? cnt : m;
+    }
+    offsets[i + 1] = offsets[i] + bloom_bundle_width(m, k, b_multiplier, fixed_b);
+  }
+  if (index == nullptr) return 0;
+  for (int64_t d = 0; d < N; ++d) {
+    const int64_t bundle = d / 2048;
+    const int64_t b0 = offsets[bundle], bb = offsets[bundle + 1] - b0;
+    if (bb <= 0) continue;
+    for (int c = 0; c < C; ++c) {
+      for (int64_t v = feature_offsets[d * C + c]; v < feature_offsets[d * C + c + 1]; ++v) {
+        int64_t used[kBloomMaxBuildK];
+        const int n_used = bloom_build_positions(static_cast<uint64_t>(static_cast<int64_t>(feature_ids[c])),
+                                                 static_cast<uint64_t>(feature_values[v]), bb, k, used);
+        for (int i = 0; i < n_used; ++i) index[bloom_word(b0, used[i], d)] |= bloom_bit(d);
+      }
+    }
+  }
+  return 0;
+}
+
+}  // extern "C"

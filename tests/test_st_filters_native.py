@@ -130,3 +130,19 @@ def test_slot_arithmetic_reproduces_the_scorer_layout(host):
     total = f(_p(prow), 3, _p(offsets), _p(sizes), 2, 73, 96, _p(np.zeros(3, np.int64)), _p(np.zeros(3, np.int64)),
               _p(got))
     assert total == 73 and np.array_equal(got[:73], ivf.probe_slots(np.array([0, 1]), offsets, sizes))
+
+
+def test_bloom_build_code_reproduces_reference_index(host):
+    """The device bloom build's hash, positions, widths and word / bit arithmetic
+    (csrc/bloom_hash.cuh) rebuild the reference's CPU-built index bit for bit."""
+    fid, off, val = (np.ascontiguousarray(x) for x in ivf.attrs_to_features(BLOOM["attrs"]))
+    n, c = BLOOM["attrs"].shape[:2]
+    f = host.host_bloom_build
+    f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                  ctypes.c_double, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+    boff = np.zeros((n + 2047) // 2048 + 1, np.int64)
+    f(_p(fid), _p(off), _p(val), n, c, int(BLOOM["k"]), 10.0, 0, _p(boff), None)
+    assert np.array_equal(boff, BLOOM["bundle_b_offsets"])
+    index = np.zeros(int(boff[-1]) * 32, np.uint64)
+    f(_p(fid), _p(off), _p(val), n, c, int(BLOOM["k"]), 10.0, 0, _p(boff), _p(index))
+    assert np.array_equal(index.view(np.int64), BLOOM["bloom_index"])
