@@ -480,6 +480,29 @@ RB_API int rb_st_search_finish(const float* query, int B, int D, const int64_t* 
                                size_t workspace_bytes, void* stream);
 
 /*
+ * The upstream-shaped raw scorer on int8 codes, replacing the CUDA impl of
+ *   st::fused_kmean_ann(Tensor cluster_offsets, Tensor cluster_ids, Tensor cluster_length,
+ *                       Tensor embeddings, Tensor queries, int max_tensor_size_per_row,
+ *                       Tensor? filtering_bit_mask=None, int invalid_index_value=-1,
+ *                       int divisor_for_int8=-1, ...) -> (Tensor, Tensor)
+ * (silvertorch/ops/csrc/fused_kmean_ann.cpp:86-228 for the CPU form; fused_kmean_ann_cuda.cu
+ * :2126-2262). cluster_ids / cluster_length [B, P] int64 (the probed clusters and their
+ * lengths), embeddings [N, D] and queries [B, D] int8. Output [B, round_up(width, 32)]: in
+ * the CUDA scorer's slot order (warp-aligned prefixes, then remainders), out_raw holds the
+ * int32 dot (divisor -1) or fp16(fp32(dot) / divisor), out_idx the int32 position; empty,
+ * filtered (filtering_bit_mask [B, mask_words], high bit first) and padding slots hold
+ * INT32_MIN / -65504 and invalid_index_value. Workspace from
+ * rb_st_fused_kmean_ann_workspace_size.
+ */
+RB_API int rb_st_fused_kmean_ann_workspace_size(int B, int P, int max_tensor_size_per_row, size_t* bytes);
+RB_API int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
+                                 const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
+                                 const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+                                 const int64_t* filtering_bit_mask, int64_t mask_words, int invalid_index_value,
+                                 int divisor_for_int8, void* out_raw, int32_t* out_idx, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/*
  * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)
  *   -> (codes int8 [B, D], scales fp32 [B], cluster_ids int64 [B, P],
  *       cluster_length int64 [B, P], cluster_offsets int64 [B, P], warps int32 [B * P],

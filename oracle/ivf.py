@@ -206,6 +206,48 @@ def search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_pe
                         global_scale, k, max_tensor_size_per_row, divisor_for_int8, filtering_bit_mask, exact)
 
 
+def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_codes, max_tensor_size_per_row,
+                    divisor_for_int8=-1, filtering_bit_mask=None, invalid_index_value=-1):
+    """``st::fused_kmean_ann`` on int8 codes as its CUDA impl returns it
+    (silvertorch/ops/csrc/fused_kmean_ann_cuda.cu:2126-2262, outputs pre-filled at
+    :1491-1510): ``(raw [B, W], idx [B, W] int32)``, ``W = padded_width(...)``. Row ``b``
+    holds its probes' positions in the slot order of ``probe_slots`` (lengths
+    ``cluster_length[b, j]``, not the cluster table's), clipped to ``W`` slots; a slot
+    holds the raw score (int32 dot, or fp16 ``dot / divisor``) and the int32 position,
+    or ``INT32_MIN`` / fp16 ``-65504`` (``0xfbff``, simple_index_mm.cuh:100-101) and
+    ``invalid_index_value`` where nothing was scored: past the row's positions, and where
+    the high-bit-first ``filtering_bit_mask`` bit is clear."""
+    q_codes = np.asarray(q_codes, dtype=np.int8)
+    offsets = np.asarray(cluster_offsets, dtype=np.int64)
+    cids = np.asarray(cluster_ids, dtype=np.int64)
+    clen = np.asarray(cluster_length, dtype=np.int64)
+    n = np.asarray(item_codes).shape[0]
+    width = padded_width(max_tensor_size_per_row)
+    b = q_codes.shape[0]
+    half = divisor_for_int8 != -1
+    raw = np.full((b, width), np.float16(-65504.0) if half else INT32_MIN,
+                  dtype=np.float16 if half else np.int32)
+    idx = np.full((b, width), invalid_index_value, dtype=np.int32)
+    for row in range(b):
+        heads, tails = [], []
+        for c, length in zip(cids[row].tolist(), clen[row].tolist()):
+            if not 0 <= c < offsets.size - 1 or not 0 <= offsets[c] < n or length <= 0:
+                continue
+            start = int(offsets[c])
+            length = min(length, n - start, width)
+            full = length // WARP * WARP
+            heads.append(np.arange(start, start + full, dtype=np.int64))
+            tails.append(np.arange(start + full, start + length, dtype=np.int64))
+        pos = np.concatenate(heads + tails)[:width] if heads else np.zeros(0, dtype=np.int64)
+        slot = np.arange(pos.size)
+        if filtering_bit_mask is not None:
+            keep = mask_bit_high_first(np.asarray(filtering_bit_mask)[row], pos)
+            pos, slot = pos[keep], slot[keep]
+        raw[row, slot] = raw_scores(q_codes[row], item_codes, pos, divisor_for_int8)
+        idx[row, slot] = pos.astype(np.int32)
+    return raw, idx
+
+
 def probe_prep(query, probe_ids, cluster_offsets, cluster_sizes):
     """``st::probe_prep`` (fork_search.cpp:43-49; fork_search_cuda.cu:1529-1546): the
     nine outputs the reference checks (retrieve/tests/parity/test_official.py:676-697):

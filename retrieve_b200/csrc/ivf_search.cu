@@ -70,7 +70,8 @@ __device__ __forceinline__ void block_scan2(int64_t (&part)[2][kExpandThreads], 
 __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
     const int64_t* __restrict__ probe_ids, int P, const int64_t* __restrict__ offsets,
     const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, FilterSet f, int width, int64_t pos_lo,
-    int64_t pos_hi, int64_t* __restrict__ pos, int64_t* __restrict__ counts) {
+    int64_t pos_hi, int64_t* __restrict__ pos, int64_t* __restrict__ counts,
+    const int64_t* __restrict__ pair_lengths = nullptr) {
   // per probe: start (int64), len, head slot, tail slot (int32, slots clipped to width)
   extern __shared__ __align__(16) uint8_t sm[];
   int64_t* p_start = reinterpret_cast<int64_t*>(sm);
@@ -88,7 +89,11 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
   int64_t head = 0, tail = 0;
   for (int j = j0; j < j1; ++j) {
     int64_t start, len;
-    probe_range(offsets, sizes, n_lists, N, prow[j], start, len);
+    // cluster lengths from the cluster table, or given per (row, probe) (st::fused_kmean_ann)
+    if (pair_lengths != nullptr)
+      probe_range_len(offsets, n_lists, N, prow[j], pair_lengths[static_cast<int64_t>(b) * P + j], start, len);
+    else
+      probe_range(offsets, sizes, n_lists, N, prow[j], start, len);
     // A cluster longer than the row contributes at most the row. width is a
     // multiple of 32, so the clipped cluster is whole warps and every later
     // slot lands past the width, as it would unclipped.
@@ -132,6 +137,52 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
     for (int i = lane; i < full; i += 32) emit(hs + i, start + i);
     for (int i = lane; i < len - full; i += 32) emit(ts + i, start + full + i);
   }
+}
+
+// st::fused_kmean_ann's output (fused_kmean_ann_cuda.cu:2126-2262): per (row, slot) of the
+// row's slot layout the raw score of the position there — the int32 dot, or
+// fp16(fp32(dot) / divisor) — and the position as int32; empty, filtered and padding slots
+// hold the dtype's lowest value (INT32_MIN, or -65504 = 0xfbff) and invalid_index_value.
+template <bool HALF>
+__global__ void raw_scores_kernel(const int8_t* __restrict__ items, int64_t N, int D, const int8_t* __restrict__ q,
+                                  const int64_t* __restrict__ pos, const int64_t* __restrict__ counts, int width,
+                                  int divisor, int invalid, void* __restrict__ out_raw, int32_t* __restrict__ out_idx) {
+  extern __shared__ __align__(16) uint8_t raw_sm[];
+  int8_t* sq = reinterpret_cast<int8_t*>(raw_sm);
+  const int64_t b = blockIdx.y;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) sq[d] = q[b * D + d];
+  __syncthreads();
+  const int64_t slot = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (slot >= width) return;
+  const int64_t o = b * width + slot;
+  const int64_t p = slot < counts[b] ? pos[o] : -1;
+  if (p < 0 || p >= N) {
+    if constexpr (HALF)
+      reinterpret_cast<__half*>(out_raw)[o] = __ushort_as_half(0xfbffu);
+    else
+      reinterpret_cast<int32_t*>(out_raw)[o] = INT32_MIN;
+    out_idx[o] = invalid;
+    return;
+  }
+  const int8_t* row = items + p * D;
+  int acc = 0;
+  if ((D & 15) == 0 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+    for (int d = 0; d < D; d += 16) {
+      const int4 x = *reinterpret_cast<const int4*>(row + d);
+      const int4 y = *reinterpret_cast<const int4*>(sq + d);
+      acc = __dp4a(x.x, y.x, acc);
+      acc = __dp4a(x.y, y.y, acc);
+      acc = __dp4a(x.z, y.z, acc);
+      acc = __dp4a(x.w, y.w, acc);
+    }
+  } else {
+    for (int d = 0; d < D; ++d) acc += static_cast<int>(row[d]) * static_cast<int>(sq[d]);
+  }
+  if constexpr (HALF)
+    reinterpret_cast<__half*>(out_raw)[o] = __float2half_rn(__fdiv_rn(static_cast<float>(acc), static_cast<float>(divisor)));
+  else
+    reinterpret_cast<int32_t*>(out_raw)[o] = acc;
+  out_idx[o] = static_cast<int32_t>(p);
 }
 
 // Winners' slots and raw scores -> (ids, scores) [B, k]; columns past k_sel and
@@ -957,6 +1008,62 @@ int rb_st_search_finish(const float* query, int B, int D, const int64_t* probe_i
   st_group_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, kin, probe_ids, P, cluster_offsets, cluster_sizes, n_lists,
                                                 head, tail, total, width, sort_perm, N, q_scales, global_scale,
                                                 divisor_for_int8, B, k, out_ids, out_scores);
+  return launch_status();
+}
+
+int rb_st_fused_kmean_ann_workspace_size(int B, int P, int max_tensor_size_per_row, size_t* bytes) {
+  if (bytes == nullptr || B < 0 || P < 0 || max_tensor_size_per_row < 0 || max_tensor_size_per_row > INT32_MAX - 31) {
+    set_last_error("fused_kmean_ann_workspace_size: bad arguments");
+    return RB_ERR_INVALID_ARG;
+  }
+  const int width = st_width(max_tensor_size_per_row);
+  *bytes = align_up(static_cast<size_t>(B) * width * sizeof(int64_t), 256) +
+           align_up(static_cast<size_t>(B) * sizeof(int64_t), 256);
+  return RB_OK;
+}
+
+int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
+                          const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
+                          const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+                          const int64_t* filtering_bit_mask, int64_t mask_words, int invalid_index_value,
+                          int divisor_for_int8, void* out_raw, int32_t* out_idx, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (B < 0 || D <= 0 || P < 0 || n_lists < 0 || N < 0 || max_tensor_size_per_row < 0 ||
+      max_tensor_size_per_row > INT32_MAX - 31 || (filtering_bit_mask != nullptr && mask_words < 0) ||
+      (divisor_for_int8 != -1 && divisor_for_int8 <= 0)) {
+    set_last_error("fused_kmean_ann: bad sizes or divisor");
+    return RB_ERR_INVALID_ARG;
+  }
+  if (P > kMaxProbes || B > 65535 || N > INT32_MAX || D > 16384) {
+    set_last_error("fused_kmean_ann: more than 2048 probes, 65535 rows, 2^31 docs or D > 16384 is not supported");
+    return RB_ERR_UNSUPPORTED;
+  }
+  const int width = st_width(max_tensor_size_per_row);
+  if (B == 0 || width == 0) return RB_OK;
+  const size_t pos_bytes = align_up(static_cast<size_t>(B) * width * sizeof(int64_t), 256);
+  if (workspace == nullptr || workspace_bytes < pos_bytes + align_up(static_cast<size_t>(B) * sizeof(int64_t), 256)) {
+    set_last_error("fused_kmean_ann: workspace too small");
+    return RB_ERR_WORKSPACE;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int64_t* pos = static_cast<int64_t*>(workspace);
+  int64_t* counts = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(workspace) + pos_bytes);
+  FilterSet fs{reinterpret_cast<const uint64_t*>(filtering_bit_mask), filtering_bit_mask ? mask_words : 0,
+               ExactArgs{nullptr, 0, 0, nullptr, nullptr, nullptr, 0},
+               BloomArgs{nullptr, 0, nullptr, 0, nullptr, 0, 0, nullptr, 0, 0}};
+  const size_t smem = static_cast<size_t>(P) * (sizeof(int64_t) + 3 * sizeof(int));
+  probe_expand_kernel<<<B, kExpandThreads, smem, s>>>(cluster_ids, P, cluster_offsets, nullptr, n_lists, N, fs, width,
+                                                      0, N, pos, counts, cluster_length);
+  int rc = launch_status();
+  if (rc != RB_OK) return rc;
+  const dim3 grid(static_cast<unsigned>((width + 255) / 256), static_cast<unsigned>(B));
+  const size_t qsm = align_up(static_cast<size_t>(D), 16);
+  if (divisor_for_int8 == -1)
+    raw_scores_kernel<false><<<grid, 256, qsm, s>>>(embeddings, N, D, queries, pos, counts, width, divisor_for_int8,
+                                                    invalid_index_value, out_raw, out_idx);
+  else
+    raw_scores_kernel<true><<<grid, 256, qsm, s>>>(embeddings, N, D, queries, pos, counts, width, divisor_for_int8,
+                                                   invalid_index_value, out_raw, out_idx);
   return launch_status();
 }
 

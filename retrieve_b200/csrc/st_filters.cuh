@@ -14,16 +14,25 @@
 
 namespace rb {
 
-RB_HD inline void probe_range(const int64_t* __restrict__ offsets, const int64_t* __restrict__ sizes,
-                                            int64_t n_lists, int64_t N, int64_t c, int64_t& start, int64_t& len) {
+// The sorted positions [start, start + len) of cluster c with l items, clipped to [0, N); an
+// invalid cluster id is an empty cluster.
+RB_HD inline void probe_range_len(const int64_t* offsets, int64_t n_lists, int64_t N, int64_t c, int64_t l,
+                                  int64_t& start, int64_t& len) {
   start = 0;
   len = 0;
   if (c < 0 || c >= n_lists) return;
   const int64_t s = offsets[c];
-  const int64_t l = sizes[c];
   if (s < 0 || s >= N || l <= 0) return;
   start = s;
   len = l < N - s ? l : N - s;
+}
+
+RB_HD inline void probe_range(const int64_t* offsets, const int64_t* sizes, int64_t n_lists, int64_t N, int64_t c,
+                              int64_t& start, int64_t& len) {
+  start = 0;
+  len = 0;
+  if (c < 0 || c >= n_lists) return;
+  probe_range_len(offsets, n_lists, N, c, sizes[c], start, len);
 }
 
 // The exact clause filter (silvertorch/ops/csrc/fork_filters.cuh:15-41): attrs is the

@@ -362,6 +362,75 @@ def bloom_index_build_fixed(feature_ids: Tensor, feature_offsets: Tensor, featur
     return _bloom_build(feature_ids, feature_offsets, feature_values, 2.0, bits_per_doc, k)
 
 
+FUSED_KMEAN_ANN_SCHEMA = (
+    "fused_kmean_ann(Tensor cluster_offsets, Tensor cluster_ids, Tensor cluster_length, Tensor embeddings, "
+    "Tensor queries, int max_tensor_size_per_row, Tensor? filtering_bit_mask=None, int invalid_index_value=-1, "
+    "int divisor_for_int8=-1, Tensor? filtering_bit_index=None, Tensor? per_embedding_scale=None) "
+    "-> (Tensor, Tensor)"
+)
+
+
+def fused_kmean_ann(cluster_offsets: Tensor, cluster_ids: Tensor, cluster_length: Tensor, embeddings: Tensor,
+                    queries: Tensor, max_tensor_size_per_row: int, filtering_bit_mask: Tensor | None = None,
+                    invalid_index_value: int = -1, divisor_for_int8: int = -1,
+                    filtering_bit_index: Tensor | None = None,
+                    per_embedding_scale: Tensor | None = None) -> tuple[Tensor, Tensor]:
+    """``st::fused_kmean_ann`` on int8 codes (the form the reference adapter's official path
+    calls, retrieve/src/retrieve/ops/official/adapter.py:289-335): ``(raw [B, W] int32 or
+    fp16, idx [B, W] int32)``, ``W = round_up(max_tensor_size_per_row, 32)``, in the CUDA
+    scorer's slot order, ``INT32_MIN`` / ``-65504`` and ``invalid_index_value`` where nothing
+    was scored. Float embeddings, ``filtering_bit_index`` and ``per_embedding_scale`` are the
+    reference's and not served here."""
+    if embeddings.dtype != torch.int8 or queries.dtype != torch.int8:
+        raise NotImplementedError("st::fused_kmean_ann: only int8 embeddings and queries are served here")
+    if filtering_bit_index is not None or per_embedding_scale is not None:
+        raise NotImplementedError("st::fused_kmean_ann: filtering_bit_index / per_embedding_scale are not served")
+    for name, t in (("cluster_offsets", cluster_offsets), ("cluster_ids", cluster_ids),
+                    ("cluster_length", cluster_length), ("embeddings", embeddings), ("queries", queries)):
+        _check(t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
+    _check(cluster_offsets.dim() == 1 and cluster_ids.dim() == 2 and cluster_length.dim() == 2
+           and embeddings.dim() == 2 and queries.dim() == 2, "bad ranks")
+    _check(cluster_ids.shape == cluster_length.shape and cluster_ids.shape[0] == queries.shape[0]
+           and embeddings.shape[1] == queries.shape[1], "shape mismatch")
+    dev = queries.device
+    b, d = queries.shape
+    p = cluster_ids.shape[1]
+    width = (int(max_tensor_size_per_row) + 31) // 32 * 32
+    offs = cluster_offsets.to(torch.int64).contiguous()
+    cids = cluster_ids.to(torch.int64).contiguous()
+    clen = cluster_length.to(torch.int64).contiguous()
+    raw = torch.empty((b, width), dtype=torch.int32 if divisor_for_int8 == -1 else torch.float16, device=dev)
+    idx = torch.empty((b, width), dtype=torch.int32, device=dev)
+    mask = None
+    if filtering_bit_mask is not None:
+        _check(filtering_bit_mask.dim() == 2 and filtering_bit_mask.shape[0] == b, "filtering_bit_mask must be [B, W]")
+        mask = filtering_bit_mask.to(device=dev, dtype=torch.int64).contiguous()
+    if b == 0 or width == 0:
+        return raw, idx
+    lib = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _call(lib.rb_st_fused_kmean_ann_workspace_size(b, p, int(max_tensor_size_per_row), ctypes.byref(nbytes)),
+          "st::fused_kmean_ann")
+    ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
+    rc = lib.rb_st_fused_kmean_ann(
+        _ptr(offs), offs.numel() - 1 if offs.numel() else 0, _ptr(cids), _ptr(clen), p, _ptr(embeddings),
+        embeddings.shape[0], _ptr(queries), b, d, int(max_tensor_size_per_row), _ptr(mask),
+        0 if mask is None else mask.shape[1], int(invalid_index_value), int(divisor_for_int8), _ptr(raw), _ptr(idx),
+        _ptr(ws), ws.numel(), _stream(dev),
+    )
+    _call(rc, "st::fused_kmean_ann")
+    return raw, idx
+
+
+def _fake_fused_kmean_ann(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
+                          filtering_bit_mask=None, invalid_index_value=-1, divisor_for_int8=-1,
+                          filtering_bit_index=None, per_embedding_scale=None):
+    width = (int(max_tensor_size_per_row) + 31) // 32 * 32
+    b = queries.shape[0]
+    dt = torch.int32 if divisor_for_int8 == -1 else torch.float16
+    return queries.new_empty((b, width), dtype=dt), queries.new_empty((b, width), dtype=torch.int32)
+
+
 def _fake_bloom(feature_ids, feature_offsets, feature_values, *args, **kwargs):
     # the index length depends on the data (the reference's builders read it back too)
     n = (feature_offsets.shape[0] - 1) // max(feature_ids.shape[0], 1)
@@ -407,7 +476,9 @@ def _register() -> None:
                                      ("probe_prep", PROBE_PREP_SCHEMA, probe_prep, _fake_probe_prep),
                                      ("bloom_index_build", BLOOM_BUILD_SCHEMA, bloom_index_build, _fake_bloom),
                                      ("bloom_index_build_fixed", BLOOM_BUILD_FIXED_SCHEMA, bloom_index_build_fixed,
-                                      _fake_bloom)):
+                                      _fake_bloom),
+                                     ("fused_kmean_ann", FUSED_KMEAN_ANN_SCHEMA, fused_kmean_ann,
+                                      _fake_fused_kmean_ann)):
         ours = not _defined(name)
         if ours:
             _LIBRARY.define(schema)

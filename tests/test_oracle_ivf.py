@@ -81,6 +81,54 @@ def test_raw_dots_match_reference_scorer(ci):
         assert got == sorted(zip(pos.tolist(), dots.tolist()))
 
 
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_fused_kmean_ann_rows_match_reference_scorer(ci):
+    """``ivf.fused_kmean_ann`` (the CUDA op's row, slot order and pads) holds per row the
+    same (position, raw) multiset as the reference's CPU scorer, whose rows follow probe
+    order; the fp16 path's raws are the int32 dots divided and rounded."""
+    g, meta = _case(ci)
+    codes, _ = knn.quantize_int8(g["query"])
+    lengths = g["sizes"][g["probe"]]
+    raw, idx = ivf.fused_kmean_ann(codes, g["offsets"], g["probe"], lengths, g["codes"], meta["width"])
+    assert raw.shape == g["raw"].shape and raw.dtype == np.int32 and idx.dtype == np.int32
+    for r in range(meta["b"]):
+        valid = g["idx"][r] >= 0
+        want = sorted(zip(g["idx"][r][valid].tolist(), g["raw"][r][valid].tolist()))
+        assert sorted(zip(idx[r][idx[r] >= 0].tolist(), raw[r][idx[r] >= 0].tolist())) == want
+        assert (raw[r][idx[r] < 0] == ivf.INT32_MIN).all()
+    r16, i16 = ivf.fused_kmean_ann(codes, g["offsets"], g["probe"], lengths, g["codes"], meta["width"],
+                                   divisor_for_int8=meta["div"], invalid_index_value=-7)
+    assert r16.dtype == np.float16 and (i16 == np.where(idx >= 0, idx, -7)).all()
+    kept = idx >= 0
+    assert (r16[kept] == (raw[kept].astype(np.float32) / np.float32(meta["div"])).astype(np.float16)).all()
+    assert (r16[~kept].view(np.uint16) == 0xFBFF).all()
+
+
+def test_fused_kmean_ann_mask_and_clipping():
+    """A cluster longer than the row fills the row's whole warps; slots whose mask bit is
+    clear keep the pads."""
+    sizes = np.array([70, 5, 40], dtype=np.int64)
+    offsets = np.r_[0, np.cumsum(sizes)]
+    rng = np.random.default_rng(3)
+    codes = rng.integers(-127, 128, (int(sizes.sum()), 8), dtype=np.int8)
+    q = rng.integers(-127, 128, (2, 8), dtype=np.int8)
+    probe = np.array([[1, 0, 2], [2, 1, 0]])
+    raw, idx = ivf.fused_kmean_ann(q, offsets, probe, sizes[probe], codes, 64)
+    # positions: cluster 0 = 0..69, cluster 1 = 70..74, cluster 2 = 75..114
+    # row 0: cluster 1 has no whole warp, cluster 0 clipped to 64 fills the row
+    assert idx[0].tolist() == list(range(0, 64))
+    # row 1: cluster 2's first warp, then the first 32 of cluster 0's clipped 64
+    assert idx[1].tolist() == list(range(75, 107)) + list(range(0, 32))
+    mask = np.ones((2, int(sizes.sum())), dtype=bool)
+    mask[:, 10] = False
+    rm, im = ivf.fused_kmean_ann(q, offsets, probe, sizes[probe], codes, 64,
+                                 filtering_bit_mask=ivf.pack_mask_high_first(mask))
+    assert im[0, 10] == -1 and rm[0, 10] == ivf.INT32_MIN and im[1, 42] == -1 and rm[1, 42] == ivf.INT32_MIN
+    im[0, 10], im[1, 42] = idx[0, 10], idx[1, 42]
+    rm[0, 10], rm[1, 42] = raw[0, 10], raw[1, 42]
+    assert (im == idx).all() and (rm == raw).all()
+
+
 def test_slot_order_is_warp_prefixes_then_remainders():
     """Clusters of 33 and 5 items probed as [1, 0], every item tied: the kept ids
     follow the CUDA scorer's slots (cluster 0's first 32, then the remainders in

@@ -62,11 +62,66 @@ PINNED_BLOOM_BUILD = (
 )
 
 
+PINNED_FUSED = (
+    "st::fused_kmean_ann(Tensor cluster_offsets, Tensor cluster_ids, Tensor cluster_length, Tensor embeddings, "
+    "Tensor queries, int max_tensor_size_per_row, Tensor? filtering_bit_mask=None, int invalid_index_value=-1, "
+    "int divisor_for_int8=-1, Tensor? filtering_bit_index=None, Tensor? per_embedding_scale=None) "
+    "-> (Tensor, Tensor)"
+)
+
+
 def test_schemas_are_the_reference_ones():
     st = _st()
     assert str(st.search.default._schema) == PINNED_SEARCH
     assert str(st.probe_prep.default._schema) == PINNED_PROBE_PREP
     assert str(st.bloom_index_build.default._schema) == PINNED_BLOOM_BUILD
+    # silvertorch/ops/csrc/fused_kmean_ann.cpp:401-414
+    assert str(st.fused_kmean_ann.default._schema) == PINNED_FUSED
+
+
+def test_fused_kmean_ann_fake_and_argument_errors():
+    st = _st()
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    from retrieve_b200 import st as rst
+
+    with FakeTensorMode():
+        raw, idx = st.fused_kmean_ann(torch.empty(9, dtype=torch.int64), torch.empty(4, 3, dtype=torch.int64),
+                                      torch.empty(4, 3, dtype=torch.int64), torch.empty(100, 64, dtype=torch.int8),
+                                      torch.empty(4, 64, dtype=torch.int8), 90)
+        assert raw.shape == idx.shape == (4, 96) and raw.dtype == idx.dtype == torch.int32
+        raw, _ = st.fused_kmean_ann(torch.empty(9, dtype=torch.int64), torch.empty(4, 3, dtype=torch.int64),
+                                    torch.empty(4, 3, dtype=torch.int64), torch.empty(100, 64, dtype=torch.int8),
+                                    torch.empty(4, 64, dtype=torch.int8), 90, divisor_for_int8=8)
+        assert raw.dtype == torch.float16
+    off, ids, lens = torch.tensor([0, 4]), torch.zeros(2, 1, dtype=torch.int64), torch.full((2, 1), 4)
+    with pytest.raises(NotImplementedError, match="int8"):
+        rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64), torch.zeros(2, 64), 4)
+    with pytest.raises(NotImplementedError, match="per_embedding_scale"):
+        rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64, dtype=torch.int8), torch.zeros(2, 64, dtype=torch.int8),
+                            4, per_embedding_scale=torch.ones(4, dtype=torch.float16))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64, dtype=torch.int8), torch.zeros(2, 64, dtype=torch.int8),
+                            4)
+
+
+def test_fused_kmean_ann_capi_checks_need_no_device():
+    lib = _lib.lib()
+    n = ctypes.c_size_t(0)
+    assert lib.rb_st_fused_kmean_ann_workspace_size(4, 8, 90, ctypes.byref(n)) == 0
+    assert n.value >= 4 * 96 * 8
+    assert lib.rb_st_fused_kmean_ann_workspace_size(-1, 8, 90, ctypes.byref(n)) == _lib.RB_ERR_INVALID_ARG
+
+    def call(b=4, d=64, p=8, width=90, div=-1, ws=None, ws_bytes=0, mask_words=2):
+        return lib.rb_st_fused_kmean_ann(None, 8, None, None, p, None, 100, None, b, d, width, None, mask_words, -1,
+                                         div, None, None, ws, ws_bytes, None)
+
+    assert call(div=0) == _lib.RB_ERR_INVALID_ARG
+    assert call(d=0) == _lib.RB_ERR_INVALID_ARG
+    assert call(p=4096) == _lib.RB_ERR_UNSUPPORTED
+    assert call(b=70000) == _lib.RB_ERR_UNSUPPORTED
+    assert call() == _lib.RB_ERR_WORKSPACE
+    assert call(b=0) == _lib.RB_OK and call(width=0) == _lib.RB_OK
 
 
 def test_fake_shapes():
@@ -123,8 +178,8 @@ REF_CPU_LIB = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "silv
 @pytest.mark.skipif(not REF_CPU_LIB.exists(), reason="the reference's CPU st ops are not built here")
 def test_registers_beside_the_reference_cpu_ops():
     """The drop-in layout: the reference's CPU build defines the st:: schemas and
-    its CPU ops; importing retrieve_b200.st then adds CUDA kernels for search and
-    probe_prep only. Run in a child process (one registry per process)."""
+    its CPU ops; importing retrieve_b200.st then adds the CUDA kernels (search,
+    probe_prep, fused_kmean_ann, ...). Run in a child process (one registry per process)."""
     import subprocess
     import sys
 
@@ -134,7 +189,7 @@ def test_registers_beside_the_reference_cpu_ops():
         "import retrieve_b200.st\n"
         "has = torch._C._dispatch_has_kernel_for_dispatch_key\n"
         "assert has('st::search', 'CUDA') and has('st::probe_prep', 'CUDA')\n"
-        "assert has('st::fused_kmean_ann', 'CPU')\n"
+        "assert has('st::fused_kmean_ann', 'CPU') and has('st::fused_kmean_ann', 'CUDA')\n"
     )
     root = Path(__file__).resolve().parent.parent
     r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
@@ -514,3 +569,61 @@ def test_sharded_search_on_one_gpu(world, ci):
         ids, scores = st.search_finish(t["query"], t["probe"], t["offsets"], t["sizes"], t["sort_perm"], gs, k,
                                        width, slots, raw)
         _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), want[0].cpu().numpy(), want[1].cpu().numpy())
+
+
+def _fused_inputs(g):
+    codes, _ = knn.quantize_int8(g["query"])
+    lengths = g["sizes"][g["probe"]]
+    t = dict(offsets=g["offsets"], ids=g["probe"], lengths=lengths, codes=g["codes"], q=codes)
+    return {key: torch.from_numpy(np.ascontiguousarray(v)).cuda() for key, v in t.items()}, codes, lengths
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_fused_kmean_ann_rows(ci):
+    """st::fused_kmean_ann on int8 codes: the int32 and fp16 rows equal the restatement's bit
+    for bit (slot order, pads, invalid_index_value), with and without a full-N mask, and hold
+    the reference CPU scorer's (position, dot) multiset per row."""
+    st = _st()
+    g, meta = _case(ci)
+    t, codes, lengths = _fused_inputs(g)
+    width = meta["width"]
+    raw, idx = st.fused_kmean_ann(t["offsets"], t["ids"], t["lengths"], t["codes"], t["q"], width)
+    want_r, want_i = ivf.fused_kmean_ann(codes, g["offsets"], g["probe"], lengths, g["codes"], width)
+    assert raw.dtype == torch.int32 and idx.dtype == torch.int32
+    assert np.array_equal(raw.cpu().numpy(), want_r) and np.array_equal(idx.cpu().numpy(), want_i)
+    for r in range(meta["b"]):
+        valid = g["idx"][r] >= 0
+        got = idx.cpu().numpy()[r]
+        assert sorted(zip(got[got >= 0].tolist(), raw.cpu().numpy()[r][got >= 0].tolist())) == sorted(
+            zip(g["idx"][r][valid].tolist(), g["raw"][r][valid].tolist()))
+    words = ivf.pack_mask_high_first(g["mask"])
+    r16, i16 = st.fused_kmean_ann(t["offsets"], t["ids"], t["lengths"], t["codes"], t["q"], width,
+                                  filtering_bit_mask=torch.from_numpy(words).cuda(), invalid_index_value=-3,
+                                  divisor_for_int8=meta["div"])
+    w16, wi16 = ivf.fused_kmean_ann(codes, g["offsets"], g["probe"], lengths, g["codes"], width,
+                                    divisor_for_int8=meta["div"], filtering_bit_mask=words, invalid_index_value=-3)
+    assert r16.dtype == torch.float16
+    assert np.array_equal(r16.cpu().numpy().view(np.uint16), w16.view(np.uint16))
+    assert np.array_equal(i16.cpu().numpy(), wi16)
+
+
+@pytest.mark.gpu
+def test_fused_kmean_ann_lengths_and_clipping():
+    """Per-(row, probe) lengths shorter than the clusters, zero and negative lengths, a
+    cluster longer than the row, repeated probes and a row width that is not a multiple of 32."""
+    st = _st()
+    rng = np.random.default_rng(11)
+    sizes = rng.integers(0, 150, 40)
+    offsets = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    n, d, b, p = int(offsets[-1]), 96, 24, 6
+    codes = rng.integers(-127, 128, (n, d), dtype=np.int8)
+    q = rng.integers(-127, 128, (b, d), dtype=np.int8)
+    probe = rng.integers(0, 40, (b, p)).astype(np.int64)
+    probe[0, :3] = 7  # repeated probes
+    lengths = np.minimum(sizes[probe], rng.integers(-5, 150, (b, p))).astype(np.int64)
+    for width in (100, 160, 700):
+        dev = [torch.from_numpy(np.ascontiguousarray(v)).cuda() for v in (offsets, probe, lengths, codes, q)]
+        raw, idx = st.fused_kmean_ann(*dev, width)
+        want_r, want_i = ivf.fused_kmean_ann(q, offsets, probe, lengths, codes, width)
+        assert np.array_equal(raw.cpu().numpy(), want_r) and np.array_equal(idx.cpu().numpy(), want_i)
