@@ -503,6 +503,58 @@ RB_API int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists
                                  size_t workspace_bytes, void* stream);
 
 /*
+ * st::fused_kmean_ann_with_partial_masks on int8 codes (schema
+ * silvertorch/ops/csrc/fused_kmean_ann.cpp:416-437; CUDA fused_kmean_ann_cuda.cu:661-845):
+ * rb_st_fused_kmean_ann with the bloom filter of the probed clusters only, the triple of
+ * rb_st_bloom_partial_search: probe j of row b keeps the i-th doc of its range when bit
+ * first_item_offset_in_column[b P + j] + i of column_results from word
+ * column_counts_cumsum[b P + j - 1] on (word 0 for the first range) is set, high bit first.
+ * n_column_results words are readable; a bit past them drops the doc.
+ */
+RB_API int rb_st_fused_kmean_ann_with_partial_masks(
+    const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids, const int64_t* cluster_length, int P,
+    const int8_t* embeddings, int64_t N, const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+    const int32_t* column_counts_cumsum, const int8_t* first_item_offset_in_column, const int64_t* column_results,
+    int64_t n_column_results, int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * SilverTorch's bloom searches over the bundle-major index (layout of rb_bloom_index_fill), on
+ * prepared plans (the blob st::search reads: 8 int64 offsets per plan slot, then the parser's
+ * bytes; max_stack_size <= 16, 1 <= k <= 10):
+ *
+ * rb_st_bloom_search replaces st::bloom_index_search_batch(_prepared)
+ * (silvertorch/ops/csrc/bloom_index_search.cpp:550-588; bloom_index_search_cuda.cu:1504-1640,
+ * 1832-1859): plan q over every 64-doc column, out int64 [plan_count, n_bundles * 32] (doc
+ * 64 c + i at bit 63 - i of word c) or, with return_bool_mask, uint8 0 / 1
+ * [plan_count, n_bundles * 2048].
+ *
+ * rb_st_bloom_column_info replaces st::generate_column_info_for_clusters
+ * (bloom_index_search.cpp:494-538): per range (start, length), int32 column count
+ * ceil((length + start % 64) / 64) (0 when length <= 0), int32 first column start / 64,
+ * int8 start % 64; with out_column_counts_cumsum not null also the inclusive int32 cumsum.
+ *
+ * rb_st_bloom_partial_search replaces the words of
+ * st::bloom_index_search_batch_return_partial_response(_prepared) (bloom_index_search.cpp
+ * :244-374; bloom_index_search_cuda.cu:1780-1944): over the B x P ranges of
+ * rb_st_bloom_column_info, the words of each range's columns in order, row b running plan
+ * query_plan_index[b] (or b); out [max_columns] int64, zero past the total.
+ */
+RB_API int rb_st_bloom_search(const int64_t* bloom_index, int64_t index_words, const int64_t* bundle_b_offsets,
+                              int64_t n_bundles, const int64_t* plans, int64_t plan_words, int plan_count,
+                              int max_stack_size, int k, int hash_k, int return_bool_mask, void* out, void* stream);
+RB_API int rb_st_bloom_column_info(const int64_t* selected_cluster_offsets, const int64_t* selected_cluster_lengths,
+                                   int64_t n, int32_t* out_column_counts, int32_t* out_start_column_ids,
+                                   int8_t* out_first_item_offsets, int32_t* out_column_counts_cumsum, void* stream);
+RB_API int rb_st_bloom_partial_search(const int64_t* bloom_index, int64_t index_words,
+                                      const int64_t* bundle_b_offsets, int64_t n_bundles, const int64_t* plans,
+                                      int64_t plan_words, int plan_count, int max_stack_size,
+                                      const int64_t* query_plan_index, int B, int P,
+                                      const int32_t* column_counts_cumsum, const int32_t* start_column_ids, int k,
+                                      int hash_k, int64_t* out_column_mask_response, int64_t max_columns,
+                                      void* stream);
+
+/*
  * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)
  *   -> (codes int8 [B, D], scales fp32 [B], cluster_ids int64 [B, P],
  *       cluster_length int64 [B, P], cluster_offsets int64 [B, P], warps int32 [B * P],

@@ -207,7 +207,7 @@ def search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_pe
 
 
 def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_codes, max_tensor_size_per_row,
-                    divisor_for_int8=-1, filtering_bit_mask=None, invalid_index_value=-1):
+                    divisor_for_int8=-1, filtering_bit_mask=None, invalid_index_value=-1, partial=None):
     """``st::fused_kmean_ann`` on int8 codes as its CUDA impl returns it
     (silvertorch/ops/csrc/fused_kmean_ann_cuda.cu:2126-2262, outputs pre-filled at
     :1491-1510): ``(raw [B, W], idx [B, W] int32)``, ``W = padded_width(...)``. Row ``b``
@@ -216,7 +216,9 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
     holds the raw score (int32 dot, or fp16 ``dot / divisor``) and the int32 position,
     or ``INT32_MIN`` / fp16 ``-65504`` (``0xfbff``, simple_index_mm.cuh:100-101) and
     ``invalid_index_value`` where nothing was scored: past the row's positions, and where
-    the high-bit-first ``filtering_bit_mask`` bit is clear."""
+    the high-bit-first ``filtering_bit_mask`` bit is clear. ``partial`` = ``(cumsum, first,
+    words)`` is ``fused_kmean_ann_with_partial_masks``' filter (``partial_mask_keep`` per doc
+    of each probed range)."""
     q_codes = np.asarray(q_codes, dtype=np.int8)
     offsets = np.asarray(cluster_offsets, dtype=np.int64)
     cids = np.asarray(cluster_ids, dtype=np.int64)
@@ -228,9 +230,10 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
     raw = np.full((b, width), np.float16(-65504.0) if half else INT32_MIN,
                   dtype=np.float16 if half else np.int32)
     idx = np.full((b, width), invalid_index_value, dtype=np.int32)
+    p = cids.shape[1] if cids.ndim == 2 else 0
     for row in range(b):
-        heads, tails = [], []
-        for c, length in zip(cids[row].tolist(), clen[row].tolist()):
+        heads, tails, keep_h, keep_t = [], [], [], []
+        for j, (c, length) in enumerate(zip(cids[row].tolist(), clen[row].tolist())):
             if not 0 <= c < offsets.size - 1 or not 0 <= offsets[c] < n or length <= 0:
                 continue
             start = int(offsets[c])
@@ -238,8 +241,15 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
             full = length // WARP * WARP
             heads.append(np.arange(start, start + full, dtype=np.int64))
             tails.append(np.arange(start + full, start + length, dtype=np.int64))
+            if partial is not None:
+                keep = partial_mask_keep(*partial, row * p + j, np.arange(length))
+                keep_h.append(keep[:full])
+                keep_t.append(keep[full:])
         pos = np.concatenate(heads + tails)[:width] if heads else np.zeros(0, dtype=np.int64)
         slot = np.arange(pos.size)
+        if partial is not None and heads:
+            keep = np.concatenate(keep_h + keep_t)[:width]
+            pos, slot = pos[keep], slot[keep]
         if filtering_bit_mask is not None:
             keep = mask_bit_high_first(np.asarray(filtering_bit_mask)[row], pos)
             pos, slot = pos[keep], slot[keep]
@@ -352,6 +362,60 @@ def bloom_plan_mask(bloom_index, bundle_b_offsets, data, offsets, p, k, hash_k, 
     words = stack.pop()
     d = np.arange(n)
     return ((words[d // 64] >> (np.uint64(63) - (d % 64).astype(np.uint64))) & np.uint64(1)).astype(bool)
+
+
+def bloom_full_words(bloom_index, bundle_b_offsets, data, offsets, k, hash_k):
+    """``st.bloom_index_search_batch(..., return_bool_mask=False)``
+    (bloom_index_search.cpp:178-241): plan ``q`` over every 64-doc column of the index,
+    ``[Q, n_bundles * 32]`` int64, doc ``64 c + i`` at bit ``63 - i``."""
+    n_docs = (len(bundle_b_offsets) - 1) * BUNDLE_COLUMNS * 64
+    q = len(offsets) // 8
+    masks = np.stack([bloom_plan_mask(bloom_index, bundle_b_offsets, data, offsets, p, k, hash_k, n_docs)
+                      for p in range(q)]) if q else np.zeros((0, n_docs), dtype=bool)
+    return pack_mask_high_first(masks)
+
+
+def column_info(selected_cluster_offsets, selected_cluster_lengths):
+    """``st.generate_column_info_for_clusters`` (bloom_index_search.cpp:494-538) for
+    non-negative starts: per range the column count ``ceil((length + start % 64) / 64)`` (0 for
+    ``length <= 0``), the first column ``start // 64`` and the bit offset ``start % 64``."""
+    start = np.asarray(selected_cluster_offsets, dtype=np.int64).reshape(-1)
+    length = np.asarray(selected_cluster_lengths, dtype=np.int64).reshape(-1)
+    first = start % 64
+    counts = np.where(length > 0, (length + first + 63) // 64, 0)
+    return counts.astype(np.int32), (start // 64).astype(np.int32), first.astype(np.int8)
+
+
+def bloom_partial_response(bloom_index, bundle_b_offsets, data, offsets, selected_cluster_offsets,
+                           selected_cluster_lengths, k, hash_k, query_plan_index=None):
+    """``st.bloom_index_search_batch_return_partial_response`` (bloom_index_search.cpp:244-374):
+    ``(column_counts_cumsum int32 [B P], first_item_offset_in_column int8 [B P],
+    column_mask_response int64 [total])`` — range after range (row-major over ``[B, P]``), the
+    full search's words of the range's columns, row ``b`` running plan
+    ``query_plan_index[b]`` (or ``b``)."""
+    full = bloom_full_words(bloom_index, bundle_b_offsets, data, offsets, k, hash_k)
+    sel = np.asarray(selected_cluster_offsets, dtype=np.int64)
+    counts, starts, first = column_info(sel, selected_cluster_lengths)
+    b, p = sel.shape
+    plans = np.arange(b) if query_plan_index is None else np.asarray(query_plan_index, dtype=np.int64)
+    words = [full[plans[i // p], starts[i] : starts[i] + counts[i]] for i in range(b * p)]
+    resp = np.concatenate(words) if words else np.zeros(0, dtype=np.int64)
+    return np.cumsum(counts, dtype=np.int32), first, resp.astype(np.int64)
+
+
+def partial_mask_keep(cumsum, first, words, idx, i):
+    """Whether ``fused_kmean_ann_with_partial_masks`` keeps doc ``i`` of range ``idx``
+    (fused_kmean_ann_cuda.cu:661-721, 800-845): bit ``first[idx] + i`` of the words from
+    ``cumsum[idx - 1]`` on, high bit first; a bit past the words drops the doc."""
+    base = 0 if idx == 0 else int(cumsum[idx - 1])
+    bit = int(first[idx]) + np.asarray(i, dtype=np.int64)
+    w = base + bit // 64
+    words = np.asarray(words, dtype=np.int64).view(np.uint64)
+    ok = w < words.size
+    out = np.zeros(np.shape(bit), dtype=bool)
+    shift = (63 - bit[ok] % 64).astype(np.uint64)
+    out[ok] = ((words[w[ok]] >> shift) & np.uint64(1)).astype(bool)
+    return out
 
 
 def attrs_to_features(attrs):

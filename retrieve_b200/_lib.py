@@ -109,6 +109,20 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _c_i64, _vp, _vp, _c_int, _vp, _c_i64, _vp, _c_int, _c_int, _c_int, _vp, _c_i64, _c_int, _c_int, _vp,
          _vp, _vp, _c_size, _vp],
     ),
+    "rb_st_fused_kmean_ann_with_partial_masks": (
+        _c_int,
+        [_vp, _c_i64, _vp, _vp, _c_int, _vp, _c_i64, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_i64, _c_int, _c_int,
+         _vp, _vp, _vp, _c_size, _vp],
+    ),
+    "rb_st_bloom_search": (
+        _c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp]
+    ),
+    "rb_st_bloom_column_info": (_c_int, [_vp, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp]),
+    "rb_st_bloom_partial_search": (
+        _c_int,
+        [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _vp,
+         _c_i64, _vp],
+    ),
     "rb_st_probe_prep": (
         _c_int,
         [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],

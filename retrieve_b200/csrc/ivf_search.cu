@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
     const int64_t* __restrict__ probe_ids, int P, const int64_t* __restrict__ offsets,
     const int64_t* __restrict__ sizes, int64_t n_lists, int64_t N, FilterSet f, int width, int64_t pos_lo,
     int64_t pos_hi, int64_t* __restrict__ pos, int64_t* __restrict__ counts,
-    const int64_t* __restrict__ pair_lengths = nullptr) {
+    const int64_t* __restrict__ pair_lengths = nullptr, PartialMask pm = PartialMask{nullptr, nullptr, nullptr, 0, 0}) {
   // per probe: start (int64), len, head slot, tail slot (int32, slots clipped to width)
   extern __shared__ __align__(16) uint8_t sm[];
   int64_t* p_start = reinterpret_cast<int64_t*>(sm);
@@ -122,20 +122,23 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
 
   const int warp = tid >> 5, lane = tid & 31;
   int64_t* out = pos + static_cast<int64_t>(b) * width;
-  auto emit = [&](int64_t slot, int64_t position) {
+  // slot <- position, the i-th doc of probe j's range
+  auto emit = [&](int64_t slot, int64_t position, int j, int i) {
     if (slot >= width) return;
     // positions outside this table's window [pos_lo, pos_hi) keep their slot but are not scored;
     // the scorer reads the row position - pos_lo of its table
     const bool in = position >= pos_lo && position < pos_hi;
-    out[slot] = in && pos_passes<true>(f, b, position) ? position - pos_lo : -1;
+    const bool keep = in && pos_passes<true>(f, b, position) &&
+                      (pm.cumsum == nullptr || partial_mask_pass(pm, b, j, i));
+    out[slot] = keep ? position - pos_lo : -1;
   };
   for (int j = warp; j < P; j += kExpandThreads / 32) {
     const int64_t start = p_start[j];
     const int len = p_len[j];
     const int full = len / 32 * 32;
     const int64_t hs = p_head[j], ts = p_tail[j];
-    for (int i = lane; i < full; i += 32) emit(hs + i, start + i);
-    for (int i = lane; i < len - full; i += 32) emit(ts + i, start + full + i);
+    for (int i = lane; i < full; i += 32) emit(hs + i, start + i, j, i);
+    for (int i = lane; i < len - full; i += 32) emit(ts + i, start + full + i, j, full + i);
   }
 }
 
@@ -1022,12 +1025,14 @@ int rb_st_fused_kmean_ann_workspace_size(int B, int P, int max_tensor_size_per_r
   return RB_OK;
 }
 
-int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
-                          const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
-                          const int8_t* queries, int B, int D, int max_tensor_size_per_row,
-                          const int64_t* filtering_bit_mask, int64_t mask_words, int invalid_index_value,
-                          int divisor_for_int8, void* out_raw, int32_t* out_idx, void* workspace,
-                          size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
+                                const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
+                                const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+                                const int64_t* filtering_bit_mask, int64_t mask_words, const PartialMask& pm,
+                                int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
+                                void* workspace, size_t workspace_bytes, void* stream) {
   if (B < 0 || D <= 0 || P < 0 || n_lists < 0 || N < 0 || max_tensor_size_per_row < 0 ||
       max_tensor_size_per_row > INT32_MAX - 31 || (filtering_bit_mask != nullptr && mask_words < 0) ||
       (divisor_for_int8 != -1 && divisor_for_int8 <= 0)) {
@@ -1053,7 +1058,7 @@ int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const
                BloomArgs{nullptr, 0, nullptr, 0, nullptr, 0, 0, nullptr, 0, 0}};
   const size_t smem = static_cast<size_t>(P) * (sizeof(int64_t) + 3 * sizeof(int));
   probe_expand_kernel<<<B, kExpandThreads, smem, s>>>(cluster_ids, P, cluster_offsets, nullptr, n_lists, N, fs, width,
-                                                      0, N, pos, counts, cluster_length);
+                                                      0, N, pos, counts, cluster_length, pm);
   int rc = launch_status();
   if (rc != RB_OK) return rc;
   const dim3 grid(static_cast<unsigned>((width + 255) / 256), static_cast<unsigned>(B));
@@ -1065,6 +1070,43 @@ int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const
     raw_scores_kernel<true><<<grid, 256, qsm, s>>>(embeddings, N, D, queries, pos, counts, width, divisor_for_int8,
                                                    invalid_index_value, out_raw, out_idx);
   return launch_status();
+}
+
+extern "C" {
+
+int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
+                          const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
+                          const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+                          const int64_t* filtering_bit_mask, int64_t mask_words, int invalid_index_value,
+                          int divisor_for_int8, void* out_raw, int32_t* out_idx, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, B, D,
+                              max_tensor_size_per_row, filtering_bit_mask, mask_words,
+                              PartialMask{nullptr, nullptr, nullptr, 0, 0}, invalid_index_value, divisor_for_int8,
+                              out_raw, out_idx, workspace, workspace_bytes, stream);
+}
+
+int rb_st_fused_kmean_ann_with_partial_masks(const int64_t* cluster_offsets, int64_t n_lists,
+                                             const int64_t* cluster_ids, const int64_t* cluster_length, int P,
+                                             const int8_t* embeddings, int64_t N, const int8_t* queries, int B, int D,
+                                             int max_tensor_size_per_row, const int32_t* column_counts_cumsum,
+                                             const int8_t* first_item_offset_in_column,
+                                             const int64_t* column_results, int64_t n_column_results,
+                                             int invalid_index_value, int divisor_for_int8, void* out_raw,
+                                             int32_t* out_idx, void* workspace, size_t workspace_bytes,
+                                             void* stream) {
+  if (n_column_results < 0 || (static_cast<int64_t>(B) * P > 0 &&
+                               (column_counts_cumsum == nullptr || first_item_offset_in_column == nullptr)) ||
+      (n_column_results > 0 && column_results == nullptr)) {
+    set_last_error("fused_kmean_ann_with_partial_masks: the partial mask needs its cumsum, offsets and words");
+    return RB_ERR_INVALID_ARG;
+  }
+  // an empty word array filters every doc out: partial_mask_pass never reads past n_words
+  const PartialMask pm{column_counts_cumsum, first_item_offset_in_column,
+                       reinterpret_cast<const uint64_t*>(column_results), n_column_results, P};
+  return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, B, D,
+                              max_tensor_size_per_row, nullptr, 0, pm, invalid_index_value, divisor_for_int8, out_raw,
+                              out_idx, workspace, workspace_bytes, stream);
 }
 
 int rb_st_probe_prep(const float* query, int B, int D, const int64_t* probe_ids, int P, const int64_t* cluster_offsets,

@@ -96,15 +96,16 @@ struct BloomArgs {
   int k, hash_k;
 };
 
-RB_HD inline bool bloom_pass(const BloomArgs& a, int64_t row, int64_t doc) {
-  const int64_t p = a.plan_index ? a.plan_index[row] : row;
-  if (p < 0 || p >= a.slots) return false;
+// Plan p evaluated on one 64-doc column of the index: bit 63 - i is doc 64 * column + i
+// (high bit first). A malformed plan, a column past the index or an empty bundle gives 0.
+RB_HD inline uint64_t bloom_plan_word(const BloomArgs& a, int64_t p, int64_t column) {
+  if (p < 0 || p >= a.slots || column < 0) return 0;
   const int64_t data_bytes = (a.blob_words - 8 * static_cast<int64_t>(a.slots)) * 8;
   int64_t o[8];
   for (int i = 0; i < 8; ++i) o[i] = a.blob[8 * p + i];
   for (int i = 0; i < 8; i += 2)
-    if (o[i] < 0 || o[i] > o[i + 1] || o[i + 1] > data_bytes) return false;
-  if ((o[2] & 3) || (o[6] & 7)) return false;
+    if (o[i] < 0 || o[i] > o[i + 1] || o[i + 1] > data_bytes) return 0;
+  if ((o[2] & 3) || (o[6] & 7)) return 0;
   const uint8_t* data = reinterpret_cast<const uint8_t*>(a.blob + 8 * static_cast<int64_t>(a.slots));
   const uint8_t* ops = data + o[0];
   const int64_t n_ops = o[1] - o[0];
@@ -112,12 +113,11 @@ RB_HD inline bool bloom_pass(const BloomArgs& a, int64_t row, int64_t doc) {
   const int64_t n_off = (o[3] - o[2]) / 4;
   const uint64_t* hashes = reinterpret_cast<const uint64_t*>(data + o[6]);
   const int64_t n_hash = (o[7] - o[6]) / 8;
-  const int64_t column = doc >> 6;
   const int64_t bundle = column / kBundleColumns;
-  if (bundle >= a.n_bundles) return false;
+  if (bundle >= a.n_bundles) return 0;
   const int64_t b0 = a.bundle_offsets[bundle];
   const int64_t bb = a.bundle_offsets[bundle + 1] - b0;
-  if (bb <= 0) return false;
+  if (bb <= 0) return 0;
   const int64_t col = column % kBundleColumns;
   uint64_t stack[kBloomStack];
   int sp = 0;
@@ -144,25 +144,52 @@ RB_HD inline bool bloom_pass(const BloomArgs& a, int64_t row, int64_t doc) {
         }
       }
       ++term;
-      if (sp < kBloomStack) stack[sp++] = w; else return false;
+      if (sp < kBloomStack) stack[sp++] = w; else return 0;
     } else if (op == 1 || op == 2) {  // AND, OR
       const int64_t children = j + 1 < n_off ? static_cast<int64_t>(op_off[j + 1]) - op_off[j] : 0;
       uint64_t acc = op == 1 ? ~0ull : 0ull;
       for (int64_t i = 0; i < children; ++i) {
-        if (sp == 0) return false;
+        if (sp == 0) return 0;
         const uint64_t v = stack[--sp];
         acc = op == 1 ? (acc & v) : (acc | v);
       }
-      if (sp < kBloomStack) stack[sp++] = acc; else return false;
+      if (sp < kBloomStack) stack[sp++] = acc; else return 0;
     } else if (op == 3) {  // NOT
-      if (sp == 0) return false;
+      if (sp == 0) return 0;
       stack[sp - 1] = ~stack[sp - 1];
     } else if (op == 5) {  // EMPTY
-      if (sp < kBloomStack) stack[sp++] = ~0ull; else return false;
+      if (sp < kBloomStack) stack[sp++] = ~0ull; else return 0;
     }
   }
-  if (sp == 0) return false;
-  return (stack[sp - 1] >> (63 - (doc & 63))) & 1ull;
+  return sp == 0 ? 0 : stack[sp - 1];
+}
+
+RB_HD inline bool bloom_pass(const BloomArgs& a, int64_t row, int64_t doc) {
+  const int64_t p = a.plan_index ? a.plan_index[row] : row;
+  return (bloom_plan_word(a, p, doc >> 6) >> (63 - (doc & 63))) & 1ull;
+}
+
+// fused_kmean_ann_with_partial_masks' filter (silvertorch/ops/csrc/fused_kmean_ann_cuda.cu
+// :661-721, 800-845; the triple of bloom_index_search_batch_return_partial_response): probe j
+// of row b keeps the i-th doc of its cluster range when bit first[b P + j] + i of the words
+// from words[cumsum[b P + j - 1]] on (from words[0] for the first range) is set, bits counted
+// high bit first (bloom_index_util.cuh:137-180). A bit past the words drops the doc.
+struct PartialMask {
+  const int32_t* cumsum;  // [B P] inclusive column cumsum; null: no partial mask
+  const int8_t* first;    // [B P] bit offset of each range's first doc
+  const uint64_t* words;
+  int64_t n_words;
+  int P;
+};
+
+RB_HD inline bool partial_mask_pass(const PartialMask& m, int64_t b, int64_t j, int64_t i) {
+  const int64_t idx = b * m.P + j;
+  const int64_t base = idx == 0 ? 0 : m.cumsum[idx - 1];
+  const int64_t bit = static_cast<int64_t>(m.first[idx]) + i;
+  if (base < 0 || bit < 0) return false;
+  const int64_t w = base + bit / 64;
+  if (w >= m.n_words) return false;
+  return (m.words[w] >> (63 - bit % 64)) & 1ull;
 }
 
 // The filters of one search: at most one of a full-N mask (high bit first), the exact

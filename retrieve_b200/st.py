@@ -28,7 +28,8 @@ import ctypes
 import torch
 from torch import Tensor
 
-from retrieve_b200 import _lib
+from retrieve_b200 import _lib, st_bloom
+from retrieve_b200._st_common import _call, _check, _ptr, _stream
 
 SEARCH_SCHEMA = (
     "search(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes, "
@@ -43,25 +44,6 @@ PROBE_PREP_SCHEMA = (
     "probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes) "
     "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)"
 )
-
-
-def _ptr(t: Tensor | None) -> ctypes.c_void_p:
-    return ctypes.c_void_p(0 if t is None else t.data_ptr())
-
-
-def _stream(device: torch.device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
-
-
-def _call(rc: int, what: str) -> None:
-    if rc != _lib.RB_OK:
-        msg = _lib.lib().rb_last_error().decode(errors="replace")
-        raise RuntimeError(f"{what}: {msg} (status {rc})")
-
-
-def _check(cond: bool, msg: str) -> None:
-    if not cond:
-        raise RuntimeError(msg)
 
 
 def _layout_args(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor):
@@ -362,6 +344,16 @@ def bloom_index_build_fixed(feature_ids: Tensor, feature_offsets: Tensor, featur
     return _bloom_build(feature_ids, feature_offsets, feature_values, 2.0, bits_per_doc, k)
 
 
+FUSED_PARTIAL_SCHEMA = (
+    "fused_kmean_ann_with_partial_masks(Tensor cluster_offsets, Tensor cluster_ids, Tensor cluster_length, "
+    "Tensor embeddings, Tensor queries, int max_tensor_size_per_row, Tensor partial_mask_column_counts_cumsum, "
+    "Tensor partial_mask_first_item_offset_in_column, Tensor partial_mask_column_results, "
+    "int invalid_index_value=-1, int divisor_for_int8=-1, Tensor? filtering_bit_index=None, "
+    "Tensor? per_embedding_scale=None, Tensor? cluster_warp_size=None, "
+    "Tensor? cluster_warp_rounded_length_cumsum=None, Tensor? cluster_remaining_length_cumsum=None, "
+    "Tensor? cluster_warp_size_cumsum=None, int total_cluster_rounded_warps=0, "
+    "int total_cluster_remaining_warps=0) -> (Tensor, Tensor)"
+)
 FUSED_KMEAN_ANN_SCHEMA = (
     "fused_kmean_ann(Tensor cluster_offsets, Tensor cluster_ids, Tensor cluster_length, Tensor embeddings, "
     "Tensor queries, int max_tensor_size_per_row, Tensor? filtering_bit_mask=None, int invalid_index_value=-1, "
@@ -381,10 +373,42 @@ def fused_kmean_ann(cluster_offsets: Tensor, cluster_ids: Tensor, cluster_length
     scorer's slot order, ``INT32_MIN`` / ``-65504`` and ``invalid_index_value`` where nothing
     was scored. Float embeddings, ``filtering_bit_index`` and ``per_embedding_scale`` are the
     reference's and not served here."""
+    return _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
+                  filtering_bit_mask, None, invalid_index_value, divisor_for_int8, filtering_bit_index,
+                  per_embedding_scale, "st::fused_kmean_ann")
+
+
+def fused_kmean_ann_with_partial_masks(
+        cluster_offsets: Tensor, cluster_ids: Tensor, cluster_length: Tensor, embeddings: Tensor, queries: Tensor,
+        max_tensor_size_per_row: int, partial_mask_column_counts_cumsum: Tensor,
+        partial_mask_first_item_offset_in_column: Tensor, partial_mask_column_results: Tensor,
+        invalid_index_value: int = -1, divisor_for_int8: int = -1, filtering_bit_index: Tensor | None = None,
+        per_embedding_scale: Tensor | None = None, cluster_warp_size: Tensor | None = None,
+        cluster_warp_rounded_length_cumsum: Tensor | None = None,
+        cluster_remaining_length_cumsum: Tensor | None = None, cluster_warp_size_cumsum: Tensor | None = None,
+        total_cluster_rounded_warps: int = 0, total_cluster_remaining_warps: int = 0) -> tuple[Tensor, Tensor]:
+    """``st::fused_kmean_ann_with_partial_masks`` on int8 codes (fused_kmean_ann_cuda.cu:661-845):
+    ``fused_kmean_ann`` with the bloom of the probed clusters only, the triple of
+    ``bloom_index_search_batch_return_partial_response`` for the same ``(cluster_offsets[cluster_ids],
+    cluster_length)`` ranges: probe ``j`` of row ``b`` keeps its ``i``-th doc when bit
+    ``first[b P + j] + i`` of the words from ``cumsum[b P + j - 1]`` on is set (high bit first).
+    The slot layout follows from ``cluster_length``; the precomputed warp cumsums of
+    ``st::probe_prep`` (``cluster_warp_size`` ... ``total_cluster_remaining_warps``) are accepted and
+    not read."""
+    partial = (partial_mask_column_counts_cumsum, partial_mask_first_item_offset_in_column,
+               partial_mask_column_results)
+    return _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row, None,
+                  partial, invalid_index_value, divisor_for_int8, filtering_bit_index, per_embedding_scale,
+                  "st::fused_kmean_ann_with_partial_masks")
+
+
+def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
+           filtering_bit_mask, partial, invalid_index_value, divisor_for_int8, filtering_bit_index,
+           per_embedding_scale, what):
     if embeddings.dtype != torch.int8 or queries.dtype != torch.int8:
-        raise NotImplementedError("st::fused_kmean_ann: only int8 embeddings and queries are served here")
+        raise NotImplementedError(f"{what}: only int8 embeddings and queries are served here")
     if filtering_bit_index is not None or per_embedding_scale is not None:
-        raise NotImplementedError("st::fused_kmean_ann: filtering_bit_index / per_embedding_scale are not served")
+        raise NotImplementedError(f"{what}: filtering_bit_index / per_embedding_scale are not served")
     for name, t in (("cluster_offsets", cluster_offsets), ("cluster_ids", cluster_ids),
                     ("cluster_length", cluster_length), ("embeddings", embeddings), ("queries", queries)):
         _check(t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
@@ -405,20 +429,32 @@ def fused_kmean_ann(cluster_offsets: Tensor, cluster_ids: Tensor, cluster_length
     if filtering_bit_mask is not None:
         _check(filtering_bit_mask.dim() == 2 and filtering_bit_mask.shape[0] == b, "filtering_bit_mask must be [B, W]")
         mask = filtering_bit_mask.to(device=dev, dtype=torch.int64).contiguous()
+    if partial is not None:
+        cumsum, first, words = partial
+        for name, t in (("partial_mask_column_counts_cumsum", cumsum),
+                        ("partial_mask_first_item_offset_in_column", first),
+                        ("partial_mask_column_results", words)):
+            _check(t.is_cuda, f"{name} must be a CUDA tensor")
+        _check(cumsum.numel() == b * p and first.numel() == b * p,
+               "the partial mask needs one column cumsum and one bit offset per (row, probe)")
+        cumsum = cumsum.to(torch.int32).contiguous()
+        first = first.to(torch.int8).contiguous()
+        words = words.to(torch.int64).contiguous()
     if b == 0 or width == 0:
         return raw, idx
     lib = _lib.lib()
     nbytes = ctypes.c_size_t(0)
-    _call(lib.rb_st_fused_kmean_ann_workspace_size(b, p, int(max_tensor_size_per_row), ctypes.byref(nbytes)),
-          "st::fused_kmean_ann")
+    _call(lib.rb_st_fused_kmean_ann_workspace_size(b, p, int(max_tensor_size_per_row), ctypes.byref(nbytes)), what)
     ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
-    rc = lib.rb_st_fused_kmean_ann(
-        _ptr(offs), offs.numel() - 1 if offs.numel() else 0, _ptr(cids), _ptr(clen), p, _ptr(embeddings),
-        embeddings.shape[0], _ptr(queries), b, d, int(max_tensor_size_per_row), _ptr(mask),
-        0 if mask is None else mask.shape[1], int(invalid_index_value), int(divisor_for_int8), _ptr(raw), _ptr(idx),
-        _ptr(ws), ws.numel(), _stream(dev),
-    )
-    _call(rc, "st::fused_kmean_ann")
+    common = (_ptr(offs), offs.numel() - 1 if offs.numel() else 0, _ptr(cids), _ptr(clen), p, _ptr(embeddings),
+              embeddings.shape[0], _ptr(queries), b, d, int(max_tensor_size_per_row))
+    tail = (int(invalid_index_value), int(divisor_for_int8), _ptr(raw), _ptr(idx), _ptr(ws), ws.numel(), _stream(dev))
+    if partial is None:
+        rc = lib.rb_st_fused_kmean_ann(*common, _ptr(mask), 0 if mask is None else mask.shape[1], *tail)
+    else:
+        rc = lib.rb_st_fused_kmean_ann_with_partial_masks(*common, _ptr(cumsum), _ptr(first), _ptr(words),
+                                                          words.numel(), *tail)
+    _call(rc, what)
     return raw, idx
 
 
@@ -429,6 +465,15 @@ def _fake_fused_kmean_ann(cluster_offsets, cluster_ids, cluster_length, embeddin
     b = queries.shape[0]
     dt = torch.int32 if divisor_for_int8 == -1 else torch.float16
     return queries.new_empty((b, width), dtype=dt), queries.new_empty((b, width), dtype=torch.int32)
+
+
+def _fake_fused_partial(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
+                        *args, invalid_index_value=-1, divisor_for_int8=-1, **kwargs):
+    # positional form: args = (cumsum, first, words, invalid_index_value, divisor_for_int8, ...)
+    if len(args) >= 5:
+        divisor_for_int8 = args[4]
+    return _fake_fused_kmean_ann(cluster_offsets, cluster_ids, cluster_length, embeddings, queries,
+                                 max_tensor_size_per_row, divisor_for_int8=divisor_for_int8)
 
 
 def _fake_bloom(feature_ids, feature_offsets, feature_values, *args, **kwargs):
@@ -478,7 +523,10 @@ def _register() -> None:
                                      ("bloom_index_build_fixed", BLOOM_BUILD_FIXED_SCHEMA, bloom_index_build_fixed,
                                       _fake_bloom),
                                      ("fused_kmean_ann", FUSED_KMEAN_ANN_SCHEMA, fused_kmean_ann,
-                                      _fake_fused_kmean_ann)):
+                                      _fake_fused_kmean_ann),
+                                     ("fused_kmean_ann_with_partial_masks", FUSED_PARTIAL_SCHEMA,
+                                      fused_kmean_ann_with_partial_masks, _fake_fused_partial),
+                                     *st_bloom.OPS):
         ours = not _defined(name)
         if ours:
             _LIBRARY.define(schema)

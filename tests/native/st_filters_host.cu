@@ -20,6 +20,26 @@ int host_bloom_pass(const int64_t* index, int64_t index_words, const int64_t* bu
   return 0;
 }
 
+// out[q * n_cols + c] = plan q over column c (bloom_plan_word, the body of the device full
+// search and partial search), for q < plan_count, c < n_cols.
+int host_bloom_words(const int64_t* index, int64_t index_words, const int64_t* bundle_offsets, int64_t n_bundles,
+                     const int64_t* blob, int64_t blob_words, int slots, int k, int hash_k, int plan_count,
+                     int64_t n_cols, int64_t* out) {
+  const BloomArgs a{reinterpret_cast<const uint64_t*>(index), index_words, bundle_offsets, n_bundles, blob,
+                    blob_words, slots, nullptr, k, hash_k};
+  for (int64_t q = 0; q < plan_count; ++q)
+    for (int64_t c = 0; c < n_cols; ++c) out[q * n_cols + c] = static_cast<int64_t>(bloom_plan_word(a, q, c));
+  return 0;
+}
+
+// out[i] = fused_kmean_ann_with_partial_masks' test of doc docs[i] of range (rows[i], probes[i]).
+int host_partial_keep(const int32_t* cumsum, const int8_t* first, const int64_t* words, int64_t n_words, int P,
+                      const int64_t* rows, const int64_t* probes, const int64_t* docs, int64_t n, uint8_t* out) {
+  const PartialMask m{cumsum, first, reinterpret_cast<const uint64_t*>(words), n_words, P};
+  for (int64_t i = 0; i < n; ++i) out[i] = partial_mask_pass(m, rows[i], probes[i], docs[i]) ? 1 : 0;
+  return 0;
+}
+
 // out[i] = the exact clause test of doc docs[i] for query row rows[i].
 int host_exact_pass(const int32_t* attrs, int64_t attr_rows, int64_t attr_docs, const int64_t* clause_slots,
                     const uint8_t* reverse, const int32_t* query, int n_clauses, const int64_t* rows,

@@ -64,6 +64,49 @@ def test_bloom_code_reproduces_reference_masks(host):
     assert np.array_equal(got[0], want[3]) and np.array_equal(got[2], want[0]) and not got[3].any()
 
 
+def test_bloom_word_code_reproduces_reference_search(host):
+    """bloom_plan_word, the per-column body of the device bloom searches, gives the
+    reference's packed st.bloom_index_search_batch words for every plan and column."""
+    want = BLOOM["words"]
+    n_plans, n_cols = want.shape
+    blob = np.ascontiguousarray(ivf.plan_blob(BLOOM["plan_data"], BLOOM["plan_offsets"], n_plans))
+    index = np.ascontiguousarray(BLOOM["bloom_index"])
+    boff = np.ascontiguousarray(BLOOM["bundle_b_offsets"])
+    out = np.zeros((n_plans, n_cols), dtype=np.int64)
+    f = host.host_bloom_words
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                  ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p]
+    f(_p(index), index.size, _p(boff), boff.size - 1, _p(blob), blob.size, n_plans, int(BLOOM["k"]),
+      int(BLOOM["hash_k"]), n_plans, n_cols, _p(out))
+    assert np.array_equal(out, want)
+
+
+def test_partial_mask_code_reads_the_reference_partial_response(host):
+    """partial_mask_pass over the reference's partial response (one plan a row) keeps doc i of
+    probed range (b, j) exactly when the reference's full search passes its sorted position."""
+    probe = BLOOM["probe"]
+    b, p = probe.shape
+    coff, sizes = BLOOM["cluster_offsets"], BLOOM["cluster_sizes"]
+    n = int(BLOOM["n"])
+    full = np.unpackbits(BLOOM["mask_bits"], axis=1)[:, :n].astype(bool)
+    rows, probes, docs, want = [], [], [], []
+    for r in range(b):
+        for j in range(p):
+            c = probe[r, j]
+            for i in range(int(sizes[c])):
+                rows.append(r), probes.append(j), docs.append(i), want.append(full[r, coff[c] + i])
+    rows, probes, docs = (np.ascontiguousarray(np.array(x, dtype=np.int64)) for x in (rows, probes, docs))
+    out = np.zeros(rows.size, dtype=np.uint8)
+    cumsum = np.ascontiguousarray(BLOOM["p_cumsum"])
+    first = np.ascontiguousarray(BLOOM["p_first"])
+    words = np.ascontiguousarray(BLOOM["p_words"])
+    f = host.host_partial_keep
+    f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
+                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+    f(_p(cumsum), _p(first), _p(words), words.size, p, _p(rows), _p(probes), _p(docs), rows.size, _p(out))
+    assert np.array_equal(out.astype(bool), np.array(want))
+
+
 def test_exact_code_reproduces_clause_predicate(host):
     rng = np.random.default_rng(4)
     n, c = 900, 4
