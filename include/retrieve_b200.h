@@ -555,6 +555,23 @@ RB_API int rb_st_bloom_partial_search(const int64_t* bloom_index, int64_t index_
                                       void* stream);
 
 /*
+ * SilverTorch's expression parser on the host, replacing
+ *   st::parse_expression_query_batch(str[] expressions, Tensor silvertorch_ks, int bloom_hash_k,
+ *                                    bool return_query_plan=True, int max_sub_queries=5)
+ * (silvertorch/ops/csrc/expression_query_parser.cpp:395-430; encoding
+ * bloom_index_util.cpp:27-127): n_expressions strings (bytes and lengths, no terminator
+ * needed) compiled to the parser's plan bytes, byte-identical to the reference's. Writes
+ * *out_data_bytes and *out_max_stack; with out_data and out_offsets both NULL that is all
+ * (a size query), else out_data (data_capacity >= *out_data_bytes bytes) receives the plan
+ * bytes and out_offsets the 8 byte offsets of each plan. A malformed expression returns
+ * RB_ERR_INVALID_ARG with the position in rb_last_error(). 1 <= bloom_hash_k <= 2^20.
+ */
+RB_API int rb_st_parse_expression_batch(const char* const* expressions, const int64_t* lengths, int n_expressions,
+                                        int64_t bloom_hash_k, int64_t max_sub_queries, int8_t* out_data,
+                                        int64_t data_capacity, int64_t* out_offsets, int64_t* out_data_bytes,
+                                        int64_t* out_max_stack);
+
+/*
  * st::probe_prep(Tensor query, Tensor probe_ids, Tensor cluster_offsets, Tensor cluster_sizes)
  *   -> (codes int8 [B, D], scales fp32 [B], cluster_ids int64 [B, P],
  *       cluster_length int64 [B, P], cluster_offsets int64 [B, P], warps int32 [B * P],

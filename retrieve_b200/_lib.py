@@ -123,6 +123,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _vp,
          _c_i64, _vp],
     ),
+    "rb_st_parse_expression_batch": (
+        _c_int, [_vp, _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64, _vp, _vp, _vp]
+    ),
     "rb_st_probe_prep": (
         _c_int,
         [_vp, _c_int, _c_int, _vp, _c_int, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],

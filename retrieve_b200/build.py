@@ -1,7 +1,8 @@
 """Builds ``libretrieve_b200.so`` in-tree with nvcc for sm_100a.
 
 ``python -m retrieve_b200.build`` (or ``build()``) compiles every ``csrc/*.cu``
-into one shared library next to this file. The library exports only the
+(nvcc) and ``csrc/*.cpp`` (host code, the C++ compiler) into one shared library
+next to this file. The library exports only the
 ``extern "C"`` entry points declared in ``include/retrieve_b200.h``; it links
 the CUDA runtime statically so that the only runtime dependency is the driver.
 """
@@ -41,8 +42,18 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found")
 
 
+CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-DRB_BUILD"]
+
+
+def cxx_path() -> str:
+    for cand in (os.environ.get("CXX"), shutil.which("g++"), shutil.which("c++")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("no C++ compiler found")
+
+
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
 
 
 def _stale(obj: Path, src: Path) -> bool:
@@ -64,9 +75,12 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> Path:
         objs.append(obj)
         if not _stale(obj, src) and not ptxas_verbose:
             continue
-        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
-        if ptxas_verbose:
-            cmd.insert(1, "-Xptxas=-v")
+        if src.suffix == ".cpp":
+            cmd = [cxx_path(), *CXX_FLAGS, "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
+        else:
+            cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
+            if ptxas_verbose:
+                cmd.insert(1, "-Xptxas=-v")
         if verbose:
             print(" ".join(cmd), flush=True)
         cmds.append(cmd)

@@ -533,6 +533,14 @@ def _register() -> None:
         _LIBRARY.impl(name, impl, "CUDA")
         if ours:
             torch.library.register_fake(f"st::{name}", fake, lib=_LIBRARY)
+    # the host parser: for CPU ks tensors too, unless a loaded build (the reference's CPU
+    # ops) already serves the CPU key with the same parser
+    name = "parse_expression_query_batch"
+    ours = not _defined(name)
+    if ours:
+        _LIBRARY.define(st_bloom.PARSE_SCHEMA)
+        _LIBRARY.impl(name, st_bloom.parse_expression_query_batch, "CPU")
+    _LIBRARY.impl(name, st_bloom.parse_expression_query_batch, "CUDA")
 
 
 _register()

@@ -57,6 +57,11 @@ PARTIAL_PREPARED_SCHEMA = (
     "Tensor? query_plan_index, int max_columns) -> (Tensor, Tensor, Tensor)"
 )
 
+PARSE_SCHEMA = (
+    "parse_expression_query_batch(str[] expressions, Tensor silvertorch_ks, int bloom_hash_k, "
+    "bool return_query_plan=True, int max_sub_queries=5) -> (int, Tensor[])"
+)
+
 DOCS_PER_BUNDLE = 2048
 COLUMNS_PER_BUNDLE = 32
 _OP_AND, _OP_OR, _OP_NOT, _OP_TERM, _OP_EMPTY = 1, 2, 3, 4, 5
@@ -96,6 +101,33 @@ def prepare_plans(data: Tensor, offsets: Tensor, device: torch.device) -> tuple[
     blob[: offs.size] = offs
     blob[8 * slots :].view(np.uint8)[: raw.size] = raw
     return torch.from_numpy(blob).to(device), slots, plan_stack_depth(raw, offs)
+
+
+def parse_expression_query_batch(expressions: list[str], silvertorch_ks: Tensor, bloom_hash_k: int,
+                                 return_query_plan: bool = True,
+                                 max_sub_queries: int = 5) -> tuple[int, list[Tensor]]:
+    """``st::parse_expression_query_batch`` (expression_query_parser.cpp:395-430) by the
+    library's host parser: ``(max_stack_size, [plans_data int8, plans_offsets int64])`` on the
+    CPU, byte-identical to the reference's; both tensors empty when ``return_query_plan`` is
+    false. ``silvertorch_ks`` is accepted and ignored, as upstream. A malformed expression
+    raises ``RuntimeError``."""
+    raw = [e.encode("utf-8") for e in expressions]
+    n = len(raw)
+    bufs = (ctypes.c_char_p * max(n, 1))(*raw) if n else None
+    lengths = (ctypes.c_int64 * max(n, 1))(*[len(r) for r in raw])
+    nbytes, stack = ctypes.c_int64(0), ctypes.c_int64(0)
+    lib = _lib.lib()
+    what = "st::parse_expression_query_batch"
+    _call(lib.rb_st_parse_expression_batch(bufs, lengths, n, int(bloom_hash_k), int(max_sub_queries), None, 0, None,
+                                           ctypes.byref(nbytes), ctypes.byref(stack)), what)
+    if not return_query_plan:
+        return int(stack.value), [torch.empty(0, dtype=torch.int8), torch.empty(0, dtype=torch.int64)]
+    data = torch.empty(int(nbytes.value), dtype=torch.int8)
+    offsets = torch.empty(8 * n, dtype=torch.int64)
+    _call(lib.rb_st_parse_expression_batch(bufs, lengths, n, int(bloom_hash_k), int(max_sub_queries), _ptr(data),
+                                           data.numel(), _ptr(offsets), ctypes.byref(nbytes), ctypes.byref(stack)),
+          what)
+    return int(stack.value), [data, offsets]
 
 
 def _index_args(bloom_index: Tensor, bloom_bundle_b_offsets: Tensor):
