@@ -1,13 +1,15 @@
-"""``torch.ops.st.search`` and ``torch.ops.st.probe_prep`` on ``libretrieve_b200.so``.
+"""The ``torch.ops.st`` namespace on ``libretrieve_b200.so``.
 
-SilverTorch's one-op IVF forward (silvertorch/ops/csrc/fork_search.cpp:13-49,
-fork_search_cuda.cu:1256-1546), reached by the reference through
-``adapter.fork_search`` (retrieve/src/retrieve/ops/official/adapter.py:495-544).
-Importing this module registers CUDA implementations of both ops under the
-reference's exact schemas: it defines the schemas when no other library has
-(``torch.ops.st`` absent), and otherwise adds the CUDA kernels to the
-definitions already loaded (the reference's CPU build of the other ``st::``
-ops keeps serving them).
+SilverTorch's one-op IVF forward ``st::search`` and its prep ``st::probe_prep``
+(silvertorch/ops/csrc/fork_search.cpp:13-49, fork_search_cuda.cu:1256-1546), reached
+by the reference through ``adapter.fork_search``
+(retrieve/src/retrieve/ops/official/adapter.py:495-544), and the upstream-shaped ops
+of the reference's loader list around it: the raw scorers ``st::fused_kmean_ann`` and
+``st::fused_kmean_ann_with_partial_masks`` (int8 codes), the bloom index builds, the
+bloom searches and the expression parser (``retrieve_b200.st_bloom``). Importing this
+module registers their implementations under the reference's exact schemas: it defines
+a schema when no other library has, and otherwise adds the CUDA kernels to the
+definitions already loaded (the reference's CPU build keeps serving the CPU key).
 
 Semantics: int8 query prep as ``quantize_int8`` on a CUDA tensor, the probed
 clusters' positions in the reference scorer's slot order, exact int32 dots,
