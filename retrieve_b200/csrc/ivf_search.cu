@@ -122,6 +122,36 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
 
   const int warp = tid >> 5, lane = tid & 31;
   int64_t* out = pos + static_cast<int64_t>(b) * width;
+  if (f.bloom.index != nullptr && pm.cumsum == nullptr) {
+    // The bloom plan gives one 64-bit word per 64-doc column: each lane evaluates the plan on
+    // one of 32 consecutive columns, and every position takes its bit from the lane that
+    // holds its column's word (one evaluation per column instead of one per position).
+    const int64_t plan = f.bloom.plan_index ? f.bloom.plan_index[b] : b;
+    for (int j = warp; j < P; j += kExpandThreads / 32) {
+      const int64_t start = p_start[j];
+      const int len = p_len[j];
+      if (len == 0) continue;
+      const int full = len / 32 * 32;
+      const int64_t hs = p_head[j], ts = p_tail[j];
+      const int64_t c_last = (start + len - 1) >> 6;
+      for (int64_t cb = start >> 6; cb <= c_last; cb += 32) {
+        const uint64_t word = cb + lane <= c_last ? bloom_plan_word(f.bloom, plan, cb + lane) : 0ull;
+        const int64_t lo = max(start, cb * 64), hi = min(start + len, (cb + 32) * 64);
+        for (int64_t p0 = lo; p0 < hi; p0 += 32) {  // warp-uniform: every lane takes part in the shuffle
+          const int64_t position = p0 + lane;
+          const uint64_t w = __shfl_sync(RB_FULL_MASK, word, static_cast<int>(((position >> 6) - cb) & 31));
+          if (position >= hi) continue;
+          const int64_t i = position - start;
+          const int64_t slot = i < full ? hs + i : ts + (i - full);
+          if (slot >= width) continue;
+          const bool keep = position >= pos_lo && position < pos_hi && ((w >> (63 - (position & 63))) & 1ull) &&
+                            pos_passes<false>(f, b, position);
+          out[slot] = keep ? position - pos_lo : -1;
+        }
+      }
+    }
+    return;
+  }
   // slot <- position, the i-th doc of probe j's range
   auto emit = [&](int64_t slot, int64_t position, int j, int i) {
     if (slot >= width) return;
@@ -427,6 +457,7 @@ static int st_check(int B, int D, int P, int64_t n_lists, int64_t N, int k, int 
 constexpr int kGroupThreads = 256;
 constexpr int kGroupWarps = kGroupThreads / 32;
 constexpr int kGroupTile = 128;  // cluster rows staged per step: 4 per lane
+static_assert(kGroupTile <= 64 * 30, "a tile's bloom columns must fit the warp's lanes");
 // candidate-list capacity per (row, probe): 256 entries up to k = 224, 1280 up to k = 1024
 constexpr int kGroupCap = 256;
 constexpr int kGroupCapLarge = 1280;
@@ -594,16 +625,30 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
       uint2* list = a.lists + static_cast<int64_t>(pr) * CAP;
       const int64_t hs = a.head[pr], ts = a.tail[pr];
       const int4* q = reinterpret_cast<const int4*>(sq + g * dp);
+      // bloom: the tile's rows span at most 3 64-doc columns; lanes 0..2 evaluate the row's plan
+      // on them once, and each position takes its bit by shuffle
+      uint64_t cword = 0;
+      const int64_t cb = (start + t0) >> 6;
+      if constexpr (BLOOM) {
+        const int64_t c_last = (start + t0 + rows - 1) >> 6;
+        const int64_t plan = a.f.bloom.plan_index ? a.f.bloom.plan_index[b] : b;
+        if (cb + lane <= c_last) cword = bloom_plan_word(a.f.bloom, plan, cb + lane);
+      }
 #pragma unroll 1
       for (int r = 0; r < kGroupTile / 32; ++r) {
         const int li = r * 32 + lane;
         const int64_t i = t0 + li;  // row within the cluster
+        const int64_t position = start + i;
+        bool bit = true;
+        if constexpr (BLOOM) {
+          const uint64_t w = __shfl_sync(RB_FULL_MASK, cword, static_cast<int>(((position >> 6) - cb) & 31));
+          bit = (w >> (63 - (position & 63))) & 1ull;
+        }
         float s = __int_as_float(0x7fc00000);  // NaN: never passes
         uint32_t slot32 = 0;
         if (li < rows) {
           const int64_t slot = i < full ? hs + i : ts + (i - full);
-          const int64_t position = start + i;
-          const bool ok = slot < a.width && pos_passes<BLOOM>(a.f, b, position);
+          const bool ok = slot < a.width && bit && pos_passes<false>(a.f, b, position);
           if (ok) {
             const int4* x = reinterpret_cast<const int4*>(sx + li * rs);
             int acc = 0;
