@@ -404,6 +404,51 @@ def fused_kmean_ann_with_partial_masks(
                   "st::fused_kmean_ann_with_partial_masks")
 
 
+FUSED_PARTIAL_MULTIPLE_SCHEMA = (
+    "fused_kmean_ann_with_partial_masks_multiple(Tensor queries, Tensor[] list_cluster_offsets, "
+    "Tensor[] list_selected_cluster_ids, Tensor[] list_selected_cluster_lengths, Tensor[] list_embeddings, "
+    "int[] list_max_tensor_size_per_row, Tensor[] list_partial_mask_column_counts_cumsum, "
+    "Tensor[] list_partial_mask_first_item_offset_in_column, Tensor[] list_partial_mask_column_results, "
+    "int invalid_index_value=-1, int divisor_for_int8=-1, Tensor? filtering_bit_index=None, "
+    "Tensor[]? list_per_embedding_scale=None, bool fuse=False) -> (Tensor[], Tensor[])"
+)
+
+
+def fused_kmean_ann_with_partial_masks_multiple(
+        queries: Tensor, list_cluster_offsets: list[Tensor], list_selected_cluster_ids: list[Tensor],
+        list_selected_cluster_lengths: list[Tensor], list_embeddings: list[Tensor],
+        list_max_tensor_size_per_row: list[int], list_partial_mask_column_counts_cumsum: list[Tensor],
+        list_partial_mask_first_item_offset_in_column: list[Tensor], list_partial_mask_column_results: list[Tensor],
+        invalid_index_value: int = -1, divisor_for_int8: int = -1, filtering_bit_index: Tensor | None = None,
+        list_per_embedding_scale: list[Tensor] | None = None,
+        fuse: bool = False) -> tuple[list[Tensor], list[Tensor]]:
+    """``st::fused_kmean_ann_with_partial_masks_multiple`` (fused_kmean_ann.cpp:438-456; CUDA
+    fused_kmean_ann_cuda.cu:2503-2600): the partial-mask scorer over an index held in chunks, one
+    ``(raw, idx)`` pair per chunk, each the single op's result on that chunk. ``fuse`` groups the
+    reference's launches and does not change the results; here every chunk is one call."""
+    n = len(list_cluster_offsets)
+    for name, lst in (("list_selected_cluster_ids", list_selected_cluster_ids),
+                      ("list_selected_cluster_lengths", list_selected_cluster_lengths),
+                      ("list_embeddings", list_embeddings),
+                      ("list_max_tensor_size_per_row", list_max_tensor_size_per_row),
+                      ("list_partial_mask_column_counts_cumsum", list_partial_mask_column_counts_cumsum),
+                      ("list_partial_mask_first_item_offset_in_column", list_partial_mask_first_item_offset_in_column),
+                      ("list_partial_mask_column_results", list_partial_mask_column_results)):
+        _check(len(lst) == n, f"{name} must have the same size as list_cluster_offsets")
+    if list_per_embedding_scale is not None:
+        raise NotImplementedError("st::fused_kmean_ann_with_partial_masks_multiple: per_embedding_scale is not served")
+    raws, idxs = [], []
+    for i in range(n):
+        raw, idx = fused_kmean_ann_with_partial_masks(
+            list_cluster_offsets[i], list_selected_cluster_ids[i], list_selected_cluster_lengths[i],
+            list_embeddings[i], queries, int(list_max_tensor_size_per_row[i]),
+            list_partial_mask_column_counts_cumsum[i], list_partial_mask_first_item_offset_in_column[i],
+            list_partial_mask_column_results[i], invalid_index_value, divisor_for_int8, filtering_bit_index)
+        raws.append(raw)
+        idxs.append(idx)
+    return raws, idxs
+
+
 def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
            filtering_bit_mask, partial, invalid_index_value, divisor_for_int8, filtering_bit_index,
            per_embedding_scale, what):
@@ -478,6 +523,18 @@ def _fake_fused_partial(cluster_offsets, cluster_ids, cluster_length, embeddings
                                  max_tensor_size_per_row, divisor_for_int8=divisor_for_int8)
 
 
+def _fake_fused_partial_multiple(queries, list_cluster_offsets, list_selected_cluster_ids,
+                                 list_selected_cluster_lengths, list_embeddings, list_max_tensor_size_per_row,
+                                 *args, invalid_index_value=-1, divisor_for_int8=-1, **kwargs):
+    if len(args) >= 5:
+        divisor_for_int8 = args[4]
+    b = queries.shape[0]
+    dt = torch.int32 if divisor_for_int8 == -1 else torch.float16
+    widths = [(int(m) + 31) // 32 * 32 for m in list_max_tensor_size_per_row]
+    return ([queries.new_empty((b, w), dtype=dt) for w in widths],
+            [queries.new_empty((b, w), dtype=torch.int32) for w in widths])
+
+
 def _fake_bloom(feature_ids, feature_offsets, feature_values, *args, **kwargs):
     # the index length depends on the data (the reference's builders read it back too)
     n = (feature_offsets.shape[0] - 1) // max(feature_ids.shape[0], 1)
@@ -528,6 +585,8 @@ def _register() -> None:
                                       _fake_fused_kmean_ann),
                                      ("fused_kmean_ann_with_partial_masks", FUSED_PARTIAL_SCHEMA,
                                       fused_kmean_ann_with_partial_masks, _fake_fused_partial),
+                                     ("fused_kmean_ann_with_partial_masks_multiple", FUSED_PARTIAL_MULTIPLE_SCHEMA,
+                                      fused_kmean_ann_with_partial_masks_multiple, _fake_fused_partial_multiple),
                                      *st_bloom.OPS):
         ours = not _defined(name)
         if ours:

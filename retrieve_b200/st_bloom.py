@@ -57,6 +57,12 @@ PARTIAL_PREPARED_SCHEMA = (
     "Tensor? query_plan_index, int max_columns) -> (Tensor, Tensor, Tensor)"
 )
 
+PARTIAL_MULTIPLE_SCHEMA = (
+    "bloom_index_search_batch_return_partial_response_multiple(Tensor[] list_bloom_index, "
+    "Tensor[] list_bloom_bundle_b_offsets, Tensor bloom_query_plans_data, Tensor bloom_query_plans_offsets, "
+    "Tensor[] list_selected_cluster_offsets, Tensor[] list_selected_cluster_lengths, int k, int hash_k, "
+    "Tensor? query_plan_index=None, bool fuse=False) -> (Tensor[], Tensor[], Tensor[])"
+)
 PARSE_SCHEMA = (
     "parse_expression_query_batch(str[] expressions, Tensor silvertorch_ks, int bloom_hash_k, "
     "bool return_query_plan=True, int max_sub_queries=5) -> (int, Tensor[])"
@@ -264,6 +270,34 @@ def bloom_index_search_batch_return_partial_response_prepared(
                     int(max_columns), "st::bloom_index_search_batch_return_partial_response_prepared")
 
 
+def bloom_index_search_batch_return_partial_response_multiple(
+        list_bloom_index: list[Tensor], list_bloom_bundle_b_offsets: list[Tensor], bloom_query_plans_data: Tensor,
+        bloom_query_plans_offsets: Tensor, list_selected_cluster_offsets: list[Tensor],
+        list_selected_cluster_lengths: list[Tensor], k: int, hash_k: int, query_plan_index: Tensor | None = None,
+        fuse: bool = False) -> tuple[list[Tensor], list[Tensor], list[Tensor]]:
+    """``st::bloom_index_search_batch_return_partial_response_multiple`` (bloom_index_search.cpp
+    :411-474; CUDA bloom_index_search_cuda.cu:2312-2450): the partial search over an index held in
+    chunks, the plans read once, one triple per chunk equal to the single op's on that chunk.
+    ``fuse`` groups the reference's launches and does not change the results."""
+    n = len(list_bloom_index)
+    what = "st::bloom_index_search_batch_return_partial_response_multiple"
+    _check(n > 0, "bloom_index_search_batch_return_partial_response_multiple: list_bloom_index should not be empty.")
+    for name, lst in (("list_bloom_bundle_b_offsets", list_bloom_bundle_b_offsets),
+                      ("list_selected_cluster_offsets", list_selected_cluster_offsets),
+                      ("list_selected_cluster_lengths", list_selected_cluster_lengths)):
+        _check(len(lst) == n, f"list_bloom_index and {name} should have the same size, got {n} vs {len(lst)}")
+    _check(list_bloom_index[0].is_cuda, "bloom_index must be a CUDA tensor")
+    blob, slots, depth = prepare_plans(bloom_query_plans_data, bloom_query_plans_offsets, list_bloom_index[0].device)
+    out = ([], [], [])
+    for i in range(n):
+        triple = _partial(list_bloom_index[i], list_bloom_bundle_b_offsets[i], blob, slots, depth,
+                          list_selected_cluster_offsets[i], list_selected_cluster_lengths[i], k, hash_k,
+                          query_plan_index, None, what)
+        for acc, t in zip(out, triple):
+            acc.append(t)
+    return out
+
+
 # --- fakes (shapes for tracing) ------------------------------------------------------------
 
 
@@ -308,6 +342,19 @@ def _fake_partial_prepared(bloom_index, bloom_bundle_b_offsets, plans, plan_coun
             bloom_index.new_empty((max_columns,), dtype=torch.int64))
 
 
+def _fake_partial_multiple(list_bloom_index, list_bloom_bundle_b_offsets, data, offsets,
+                           list_selected_cluster_offsets, list_selected_cluster_lengths, k, hash_k,
+                           query_plan_index=None, fuse=False):
+    ctx = torch.library.get_ctx()
+    outs = ([], [], [])
+    for index, lens in zip(list_bloom_index, list_selected_cluster_lengths):
+        n = lens.numel()
+        outs[0].append(lens.new_empty((n,), dtype=torch.int32))
+        outs[1].append(lens.new_empty((n,), dtype=torch.int8))
+        outs[2].append(index.new_empty((ctx.new_dynamic_size(),), dtype=torch.int64))
+    return outs
+
+
 OPS = (
     ("bloom_index_search_batch", BLOOM_SEARCH_SCHEMA, bloom_index_search_batch, _fake_search),
     ("bloom_index_search_batch_prepared", BLOOM_SEARCH_PREPARED_SCHEMA, bloom_index_search_batch_prepared,
@@ -317,4 +364,6 @@ OPS = (
      bloom_index_search_batch_return_partial_response, _fake_partial),
     ("bloom_index_search_batch_return_partial_response_prepared", PARTIAL_PREPARED_SCHEMA,
      bloom_index_search_batch_return_partial_response_prepared, _fake_partial_prepared),
+    ("bloom_index_search_batch_return_partial_response_multiple", PARTIAL_MULTIPLE_SCHEMA,
+     bloom_index_search_batch_return_partial_response_multiple, _fake_partial_multiple),
 )

@@ -54,6 +54,20 @@ PINNED = {  # retrieve/tests/parity/test_official.py:65-102; bloom_index_search.
         "Tensor selected_cluster_offsets, Tensor selected_cluster_lengths, int k, int hash_k, "
         "Tensor? query_plan_index, int max_columns) -> (Tensor, Tensor, Tensor)"
     ),
+    "fused_kmean_ann_with_partial_masks_multiple": (  # fused_kmean_ann.cpp:438-456
+        "st::fused_kmean_ann_with_partial_masks_multiple(Tensor queries, Tensor[] list_cluster_offsets, "
+        "Tensor[] list_selected_cluster_ids, Tensor[] list_selected_cluster_lengths, Tensor[] list_embeddings, "
+        "int[] list_max_tensor_size_per_row, Tensor[] list_partial_mask_column_counts_cumsum, "
+        "Tensor[] list_partial_mask_first_item_offset_in_column, Tensor[] list_partial_mask_column_results, "
+        "int invalid_index_value=-1, int divisor_for_int8=-1, Tensor? filtering_bit_index=None, "
+        "Tensor[]? list_per_embedding_scale=None, bool fuse=False) -> (Tensor[], Tensor[])"
+    ),
+    "bloom_index_search_batch_return_partial_response_multiple": (
+        "st::bloom_index_search_batch_return_partial_response_multiple(Tensor[] list_bloom_index, "
+        "Tensor[] list_bloom_bundle_b_offsets, Tensor bloom_query_plans_data, Tensor bloom_query_plans_offsets, "
+        "Tensor[] list_selected_cluster_offsets, Tensor[] list_selected_cluster_lengths, int k, int hash_k, "
+        "Tensor? query_plan_index=None, bool fuse=False) -> (Tensor[], Tensor[], Tensor[])"
+    ),
     "generate_column_info_for_clusters": (
         "st::generate_column_info_for_clusters(Tensor selected_cluster_offsets, "
         "Tensor selected_cluster_lengths) -> (Tensor, Tensor, Tensor)"
@@ -162,6 +176,20 @@ def test_argument_errors_raise():
     with pytest.raises(RuntimeError, match="CUDA"):
         st_bloom.generate_column_info_for_clusters(torch.zeros(2, 3, dtype=torch.int64),
                                                    torch.zeros(2, 3, dtype=torch.int64))
+
+
+def test_multiple_variants_check_their_lists():
+    _st()
+    from retrieve_b200 import st, st_bloom
+
+    t = torch.zeros(4, dtype=torch.int64)
+    with pytest.raises(RuntimeError, match="should not be empty"):
+        st_bloom.bloom_index_search_batch_return_partial_response_multiple([], [], t, t, [], [], 5, 7)
+    with pytest.raises(RuntimeError, match="same size"):
+        st_bloom.bloom_index_search_batch_return_partial_response_multiple([t, t], [t], t, t, [t, t], [t, t], 5, 7)
+    q = torch.zeros(2, 64, dtype=torch.int8)
+    with pytest.raises(RuntimeError, match="list_embeddings must have the same size"):
+        st.fused_kmean_ann_with_partial_masks_multiple(q, [t, t], [t, t], [t, t], [q], [8, 8], [t, t], [t, t], [t, t])
 
 
 def test_capi_checks_need_no_device():
@@ -276,3 +304,39 @@ def test_fused_kmean_ann_with_partial_masks(divisor):
                                         invalid_index_value=-2, divisor_for_int8=divisor)
     assert torch.equal(full_i, idx) and torch.equal(full_r.view(torch.int16) if divisor != -1 else full_r,
                                                     raw.view(torch.int16) if divisor != -1 else raw)
+
+
+@pytest.mark.gpu
+def test_multiple_variants_equal_their_single_ops():
+    """The chunked-index variants: one result per chunk, each equal to the single op on that
+    chunk (the reference's loop; fuse changes nothing), here with the index given twice and two
+    different probe selections."""
+    st = _st()
+    index, boff, data, offs = _dev(BLOOM["bloom_index"], BLOOM["bundle_b_offsets"], BLOOM["plan_data"],
+                                   BLOOM["plan_offsets"])
+    off_a, len_a = _dev(*_selection())
+    rows = BLOOM["probe"].shape[0]
+    probe_b = BLOOM["probe2"][:rows]
+    off_b = torch.from_numpy(BLOOM["cluster_offsets"][probe_b].astype(np.int64)).cuda()
+    len_b = torch.from_numpy(BLOOM["cluster_sizes"][probe_b].astype(np.int64)).cuda()
+    for fuse in (False, True):
+        cs, fi, ws = st.bloom_index_search_batch_return_partial_response_multiple(
+            [index, index], [boff, boff], data, offs, [off_a, off_b], [len_a, len_b], K, HASH_K, None, fuse)
+        for c, (o, ln) in enumerate(((off_a, len_a), (off_b, len_b))):
+            want = ivf.bloom_partial_response(BLOOM["bloom_index"], BLOOM["bundle_b_offsets"], BLOOM["plan_data"],
+                                              BLOOM["plan_offsets"], o.cpu().numpy(), ln.cpu().numpy(), K, HASH_K)
+            for got, w in zip((cs[c], fi[c], ws[c]), want):
+                assert np.array_equal(got.cpu().numpy(), w)
+    rng = np.random.default_rng(9)
+    n, d = int(BLOOM["n"]), 64
+    codes = torch.from_numpy(rng.integers(-127, 128, (n, d), dtype=np.int8)).cuda()
+    q = torch.from_numpy(rng.integers(-127, 128, (rows, d), dtype=np.int8)).cuda()
+    coff = torch.from_numpy(BLOOM["cluster_offsets"]).cuda()
+    ids = [torch.from_numpy(BLOOM["probe"]).cuda(), torch.from_numpy(probe_b.astype(np.int64)).cuda()]
+    widths = [int(len_a.sum(1).max()), int(len_b.sum(1).max())]
+    raws, idxs = st.fused_kmean_ann_with_partial_masks_multiple(
+        q, [coff, coff], ids, [len_a, len_b], [codes, codes], widths, cs, fi, ws, -1, 16)
+    for c in range(2):
+        raw, idx = st.fused_kmean_ann_with_partial_masks(coff, ids[c], [len_a, len_b][c], codes, q, widths[c], cs[c],
+                                                         fi[c], ws[c], -1, 16)
+        assert torch.equal(raws[c], raw) and torch.equal(idxs[c], idx)
