@@ -490,17 +490,22 @@ RB_API int rb_st_search_finish(const float* query, int B, int D, const int64_t* 
  * lengths), embeddings [N, D] and queries [B, D] int8. Output [B, round_up(width, 32)]: in
  * the CUDA scorer's slot order (warp-aligned prefixes, then remainders), out_raw holds the
  * int32 dot (divisor -1) or fp16(fp32(dot) / divisor), out_idx the int32 position; empty,
- * filtered (filtering_bit_mask [B, mask_words], high bit first) and padding slots hold
- * INT32_MIN / -65504 and invalid_index_value. Workspace from
+ * filtered (filtering_bit_mask [mask_rows, mask_words], high bit first) and padding slots
+ * hold INT32_MIN / -65504 and invalid_index_value. filtering_bit_index (int64 [B] or NULL)
+ * makes row b read mask row filtering_bit_index[b] (an index outside [0, mask_rows) filters
+ * the whole row out); without it mask_rows >= B. per_embedding_scale (fp16 bits [N] or NULL)
+ * replaces the divisor by a per-doc one: fp16 raw fp16(fp32(fp16(dot)) / fp32(scale[doc])),
+ * the CUDA scorer's order (index_mm_helpers.cuh:49-53). Workspace from
  * rb_st_fused_kmean_ann_workspace_size.
  */
 RB_API int rb_st_fused_kmean_ann_workspace_size(int B, int P, int max_tensor_size_per_row, size_t* bytes);
 RB_API int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
                                  const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
                                  const int8_t* queries, int B, int D, int max_tensor_size_per_row,
-                                 const int64_t* filtering_bit_mask, int64_t mask_words, int invalid_index_value,
-                                 int divisor_for_int8, void* out_raw, int32_t* out_idx, void* workspace,
-                                 size_t workspace_bytes, void* stream);
+                                 const int64_t* filtering_bit_mask, int64_t mask_rows, int64_t mask_words,
+                                 const int64_t* filtering_bit_index, const uint16_t* per_embedding_scale,
+                                 int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
+                                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * st::fused_kmean_ann_with_partial_masks on int8 codes (schema
@@ -509,14 +514,18 @@ RB_API int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists
  * rb_st_bloom_partial_search: probe j of row b keeps the i-th doc of its range when bit
  * first_item_offset_in_column[b P + j] + i of column_results from word
  * column_counts_cumsum[b P + j - 1] on (word 0 for the first range) is set, high bit first.
- * n_column_results words are readable; a bit past them drops the doc.
+ * n_column_results words are readable; a bit past them drops the doc. The triple covers
+ * mask_rows x P ranges; filtering_bit_index (int64 [B] or NULL) makes row b read the ranges of
+ * mask row filtering_bit_index[b] (outside [0, mask_rows): the whole row filtered out), else
+ * mask_rows >= B. per_embedding_scale as in rb_st_fused_kmean_ann.
  */
 RB_API int rb_st_fused_kmean_ann_with_partial_masks(
     const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids, const int64_t* cluster_length, int P,
     const int8_t* embeddings, int64_t N, const int8_t* queries, int B, int D, int max_tensor_size_per_row,
     const int32_t* column_counts_cumsum, const int8_t* first_item_offset_in_column, const int64_t* column_results,
-    int64_t n_column_results, int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
-    void* workspace, size_t workspace_bytes, void* stream);
+    int64_t n_column_results, int64_t mask_rows, const int64_t* filtering_bit_index,
+    const uint16_t* per_embedding_scale, int invalid_index_value, int divisor_for_int8, void* out_raw,
+    int32_t* out_idx, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * SilverTorch's bloom searches over the bundle-major index (layout of rb_bloom_index_fill), on

@@ -207,7 +207,8 @@ def search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_pe
 
 
 def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_codes, max_tensor_size_per_row,
-                    divisor_for_int8=-1, filtering_bit_mask=None, invalid_index_value=-1, partial=None):
+                    divisor_for_int8=-1, filtering_bit_mask=None, invalid_index_value=-1, partial=None,
+                    filtering_bit_index=None, per_embedding_scale=None):
     """``st::fused_kmean_ann`` on int8 codes as its CUDA impl returns it
     (silvertorch/ops/csrc/fused_kmean_ann_cuda.cu:2126-2262, outputs pre-filled at
     :1491-1510): ``(raw [B, W], idx [B, W] int32)``, ``W = padded_width(...)``. Row ``b``
@@ -218,7 +219,11 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
     ``invalid_index_value`` where nothing was scored: past the row's positions, and where
     the high-bit-first ``filtering_bit_mask`` bit is clear. ``partial`` = ``(cumsum, first,
     words)`` is ``fused_kmean_ann_with_partial_masks``' filter (``partial_mask_keep`` per doc
-    of each probed range)."""
+    of each probed range). ``filtering_bit_index`` [B] maps row ``b`` to the mask row (and the
+    partial masks' row) it reads. ``per_embedding_scale`` (fp16 [N], a per-doc divisor that
+    takes the divisor's place) gives the fp16 raw ``fp16(fp32(fp16(dot)) / fp32(scale[pos]))``,
+    the CUDA scorer's order (index_mm_helpers.cuh:49-56: the dot rounded to fp16 first; the CPU
+    scorer divides the unrounded dot, fused_kmean_ann.cpp:196-199, equal for |dot| <= 2048)."""
     q_codes = np.asarray(q_codes, dtype=np.int8)
     offsets = np.asarray(cluster_offsets, dtype=np.int64)
     cids = np.asarray(cluster_ids, dtype=np.int64)
@@ -226,11 +231,13 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
     n = np.asarray(item_codes).shape[0]
     width = padded_width(max_tensor_size_per_row)
     b = q_codes.shape[0]
-    half = divisor_for_int8 != -1
+    scale = None if per_embedding_scale is None else np.asarray(per_embedding_scale, dtype=np.float16)
+    half = divisor_for_int8 != -1 or scale is not None
     raw = np.full((b, width), np.float16(-65504.0) if half else INT32_MIN,
                   dtype=np.float16 if half else np.int32)
     idx = np.full((b, width), invalid_index_value, dtype=np.int32)
     p = cids.shape[1] if cids.ndim == 2 else 0
+    rows = np.arange(b) if filtering_bit_index is None else np.asarray(filtering_bit_index, dtype=np.int64)
     for row in range(b):
         heads, tails, keep_h, keep_t = [], [], [], []
         for j, (c, length) in enumerate(zip(cids[row].tolist(), clen[row].tolist())):
@@ -242,7 +249,7 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
             heads.append(np.arange(start, start + full, dtype=np.int64))
             tails.append(np.arange(start + full, start + length, dtype=np.int64))
             if partial is not None:
-                keep = partial_mask_keep(*partial, row * p + j, np.arange(length))
+                keep = partial_mask_keep(*partial, rows[row] * p + j, np.arange(length))
                 keep_h.append(keep[:full])
                 keep_t.append(keep[full:])
         pos = np.concatenate(heads + tails)[:width] if heads else np.zeros(0, dtype=np.int64)
@@ -251,9 +258,14 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
             keep = np.concatenate(keep_h + keep_t)[:width]
             pos, slot = pos[keep], slot[keep]
         if filtering_bit_mask is not None:
-            keep = mask_bit_high_first(np.asarray(filtering_bit_mask)[row], pos)
+            keep = mask_bit_high_first(np.asarray(filtering_bit_mask)[rows[row]], pos)
             pos, slot = pos[keep], slot[keep]
-        raw[row, slot] = raw_scores(q_codes[row], item_codes, pos, divisor_for_int8)
+        if scale is not None:
+            dots = raw_scores(q_codes[row], item_codes, pos, -1)
+            raw[row, slot] = (dots.astype(np.float32).astype(np.float16).astype(np.float32)
+                              / scale[pos].astype(np.float32)).astype(np.float16)
+        else:
+            raw[row, slot] = raw_scores(q_codes[row], item_codes, pos, divisor_for_int8)
         idx[row, slot] = pos.astype(np.int32)
     return raw, idx
 

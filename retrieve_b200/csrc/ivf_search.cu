@@ -176,10 +176,14 @@ __global__ void __launch_bounds__(kExpandThreads) probe_expand_kernel(
 // row's slot layout the raw score of the position there — the int32 dot, or
 // fp16(fp32(dot) / divisor) — and the position as int32; empty, filtered and padding slots
 // hold the dtype's lowest value (INT32_MIN, or -65504 = 0xfbff) and invalid_index_value.
+// With a per-doc fp16 scale (per_embedding_scale, which takes the divisor's place) the raw
+// score is fp16(fp32(fp16(dot)) / fp32(scale[p])): the CUDA scorer divides a Half by a Half
+// (index_mm_helpers.cuh:49-53), the dot rounded to fp16 first.
 template <bool HALF>
 __global__ void raw_scores_kernel(const int8_t* __restrict__ items, int64_t N, int D, const int8_t* __restrict__ q,
                                   const int64_t* __restrict__ pos, const int64_t* __restrict__ counts, int width,
-                                  int divisor, int invalid, void* __restrict__ out_raw, int32_t* __restrict__ out_idx) {
+                                  int divisor, const __half* __restrict__ scale, int invalid,
+                                  void* __restrict__ out_raw, int32_t* __restrict__ out_idx) {
   extern __shared__ __align__(16) uint8_t raw_sm[];
   int8_t* sq = reinterpret_cast<int8_t*>(raw_sm);
   const int64_t b = blockIdx.y;
@@ -211,9 +215,11 @@ __global__ void raw_scores_kernel(const int8_t* __restrict__ items, int64_t N, i
   } else {
     for (int d = 0; d < D; ++d) acc += static_cast<int>(row[d]) * static_cast<int>(sq[d]);
   }
-  if constexpr (HALF)
-    reinterpret_cast<__half*>(out_raw)[o] = __float2half_rn(__fdiv_rn(static_cast<float>(acc), static_cast<float>(divisor)));
-  else
+  if constexpr (HALF) {
+    const float num = scale ? __half2float(__float2half_rn(static_cast<float>(acc))) : static_cast<float>(acc);
+    const float den = scale ? __half2float(scale[p]) : static_cast<float>(divisor);
+    reinterpret_cast<__half*>(out_raw)[o] = __float2half_rn(__fdiv_rn(num, den));
+  } else
     reinterpret_cast<int32_t*>(out_raw)[o] = acc;
   out_idx[o] = static_cast<int32_t>(p);
 }
@@ -1075,11 +1081,15 @@ int rb_st_fused_kmean_ann_workspace_size(int B, int P, int max_tensor_size_per_r
 static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
                                 const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
                                 const int8_t* queries, int B, int D, int max_tensor_size_per_row,
-                                const int64_t* filtering_bit_mask, int64_t mask_words, const PartialMask& pm,
-                                int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+                                const int64_t* filtering_bit_mask, int64_t mask_rows, int64_t mask_words,
+                                const int64_t* filtering_bit_index, const PartialMask& pm,
+                                const uint16_t* per_embedding_scale, int invalid_index_value, int divisor_for_int8,
+                                void* out_raw, int32_t* out_idx, void* workspace, size_t workspace_bytes,
+                                void* stream) {
   if (B < 0 || D <= 0 || P < 0 || n_lists < 0 || N < 0 || max_tensor_size_per_row < 0 ||
-      max_tensor_size_per_row > INT32_MAX - 31 || (filtering_bit_mask != nullptr && mask_words < 0) ||
+      max_tensor_size_per_row > INT32_MAX - 31 ||
+      (filtering_bit_mask != nullptr && (mask_words < 0 || mask_rows < 0)) ||
+      (filtering_bit_mask != nullptr && filtering_bit_index == nullptr && mask_rows < B) ||
       (divisor_for_int8 != -1 && divisor_for_int8 <= 0)) {
     set_last_error("fused_kmean_ann: bad sizes or divisor");
     return RB_ERR_INVALID_ARG;
@@ -1100,7 +1110,8 @@ static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists,
   int64_t* counts = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(workspace) + pos_bytes);
   FilterSet fs{reinterpret_cast<const uint64_t*>(filtering_bit_mask), filtering_bit_mask ? mask_words : 0,
                ExactArgs{nullptr, 0, 0, nullptr, nullptr, nullptr, 0},
-               BloomArgs{nullptr, 0, nullptr, 0, nullptr, 0, 0, nullptr, 0, 0}};
+               BloomArgs{nullptr, 0, nullptr, 0, nullptr, 0, 0, nullptr, 0, 0},
+               filtering_bit_mask ? filtering_bit_index : nullptr, mask_rows};
   const size_t smem = static_cast<size_t>(P) * (sizeof(int64_t) + 3 * sizeof(int));
   probe_expand_kernel<<<B, kExpandThreads, smem, s>>>(cluster_ids, P, cluster_offsets, nullptr, n_lists, N, fs, width,
                                                       0, N, pos, counts, cluster_length, pm);
@@ -1108,12 +1119,13 @@ static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists,
   if (rc != RB_OK) return rc;
   const dim3 grid(static_cast<unsigned>((width + 255) / 256), static_cast<unsigned>(B));
   const size_t qsm = align_up(static_cast<size_t>(D), 16);
-  if (divisor_for_int8 == -1)
+  const __half* scale = reinterpret_cast<const __half*>(per_embedding_scale);
+  if (divisor_for_int8 == -1 && scale == nullptr)
     raw_scores_kernel<false><<<grid, 256, qsm, s>>>(embeddings, N, D, queries, pos, counts, width, divisor_for_int8,
-                                                    invalid_index_value, out_raw, out_idx);
+                                                    nullptr, invalid_index_value, out_raw, out_idx);
   else
     raw_scores_kernel<true><<<grid, 256, qsm, s>>>(embeddings, N, D, queries, pos, counts, width, divisor_for_int8,
-                                                   invalid_index_value, out_raw, out_idx);
+                                                   scale, invalid_index_value, out_raw, out_idx);
   return launch_status();
 }
 
@@ -1122,13 +1134,14 @@ extern "C" {
 int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
                           const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
                           const int8_t* queries, int B, int D, int max_tensor_size_per_row,
-                          const int64_t* filtering_bit_mask, int64_t mask_words, int invalid_index_value,
-                          int divisor_for_int8, void* out_raw, int32_t* out_idx, void* workspace,
-                          size_t workspace_bytes, void* stream) {
+                          const int64_t* filtering_bit_mask, int64_t mask_rows, int64_t mask_words,
+                          const int64_t* filtering_bit_index, const uint16_t* per_embedding_scale,
+                          int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
+                          void* workspace, size_t workspace_bytes, void* stream) {
   return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, B, D,
-                              max_tensor_size_per_row, filtering_bit_mask, mask_words,
-                              PartialMask{nullptr, nullptr, nullptr, 0, 0}, invalid_index_value, divisor_for_int8,
-                              out_raw, out_idx, workspace, workspace_bytes, stream);
+                              max_tensor_size_per_row, filtering_bit_mask, mask_rows, mask_words, filtering_bit_index,
+                              PartialMask{nullptr, nullptr, nullptr, 0, 0}, per_embedding_scale, invalid_index_value,
+                              divisor_for_int8, out_raw, out_idx, workspace, workspace_bytes, stream);
 }
 
 int rb_st_fused_kmean_ann_with_partial_masks(const int64_t* cluster_offsets, int64_t n_lists,
@@ -1137,21 +1150,26 @@ int rb_st_fused_kmean_ann_with_partial_masks(const int64_t* cluster_offsets, int
                                              int max_tensor_size_per_row, const int32_t* column_counts_cumsum,
                                              const int8_t* first_item_offset_in_column,
                                              const int64_t* column_results, int64_t n_column_results,
-                                             int invalid_index_value, int divisor_for_int8, void* out_raw,
-                                             int32_t* out_idx, void* workspace, size_t workspace_bytes,
-                                             void* stream) {
-  if (n_column_results < 0 || (static_cast<int64_t>(B) * P > 0 &&
-                               (column_counts_cumsum == nullptr || first_item_offset_in_column == nullptr)) ||
-      (n_column_results > 0 && column_results == nullptr)) {
-    set_last_error("fused_kmean_ann_with_partial_masks: the partial mask needs its cumsum, offsets and words");
+                                             int64_t mask_rows, const int64_t* filtering_bit_index,
+                                             const uint16_t* per_embedding_scale, int invalid_index_value,
+                                             int divisor_for_int8, void* out_raw, int32_t* out_idx, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+  if (n_column_results < 0 || mask_rows < 0 ||
+      (static_cast<int64_t>(B) * P > 0 &&
+       (column_counts_cumsum == nullptr || first_item_offset_in_column == nullptr)) ||
+      (n_column_results > 0 && column_results == nullptr) || (filtering_bit_index == nullptr && mask_rows < B)) {
+    set_last_error("fused_kmean_ann_with_partial_masks: the partial mask needs its cumsum, offsets and words for "
+                   "mask_rows x P ranges (mask_rows >= B without filtering_bit_index)");
     return RB_ERR_INVALID_ARG;
   }
   // an empty word array filters every doc out: partial_mask_pass never reads past n_words
   const PartialMask pm{column_counts_cumsum, first_item_offset_in_column,
-                       reinterpret_cast<const uint64_t*>(column_results), n_column_results, P};
+                       reinterpret_cast<const uint64_t*>(column_results), n_column_results, P, filtering_bit_index,
+                       mask_rows};
   return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, B, D,
-                              max_tensor_size_per_row, nullptr, 0, pm, invalid_index_value, divisor_for_int8, out_raw,
-                              out_idx, workspace, workspace_bytes, stream);
+                              max_tensor_size_per_row, nullptr, 0, 0, nullptr, pm, per_embedding_scale,
+                              invalid_index_value, divisor_for_int8, out_raw, out_idx, workspace, workspace_bytes,
+                              stream);
 }
 
 int rb_st_probe_prep(const float* query, int B, int D, const int64_t* probe_ids, int P, const int64_t* cluster_offsets,

@@ -174,15 +174,23 @@ RB_HD inline bool bloom_pass(const BloomArgs& a, int64_t row, int64_t doc) {
 // of row b keeps the i-th doc of its cluster range when bit first[b P + j] + i of the words
 // from words[cumsum[b P + j - 1]] on (from words[0] for the first range) is set, bits counted
 // high bit first (bloom_index_util.cuh:137-180). A bit past the words drops the doc.
+// With rows (filtering_bit_index, fused_kmean_ann_cuda.cu:710-713) row b reads the ranges of
+// mask row rows[b] < n_rows instead of its own (a row index outside drops every doc).
 struct PartialMask {
-  const int32_t* cumsum;  // [B P] inclusive column cumsum; null: no partial mask
-  const int8_t* first;    // [B P] bit offset of each range's first doc
+  const int32_t* cumsum;  // [R P] inclusive column cumsum; null: no partial mask
+  const int8_t* first;    // [R P] bit offset of each range's first doc
   const uint64_t* words;
   int64_t n_words;
   int P;
+  const int64_t* rows = nullptr;  // [B] row -> mask row, or null: row b reads mask row b
+  int64_t n_rows = 0;             // R, with rows
 };
 
 RB_HD inline bool partial_mask_pass(const PartialMask& m, int64_t b, int64_t j, int64_t i) {
+  if (m.rows != nullptr) {
+    b = m.rows[b];
+    if (b < 0 || b >= m.n_rows) return false;
+  }
   const int64_t idx = b * m.P + j;
   const int64_t base = idx == 0 ? 0 : m.cumsum[idx - 1];
   const int64_t bit = static_cast<int64_t>(m.first[idx]) + i;
@@ -199,6 +207,10 @@ struct FilterSet {
   int64_t mask_words;
   ExactArgs ex;
   BloomArgs bloom;
+  // st::fused_kmean_ann's filtering_bit_index: row b reads mask row mask_rows[b] < mask_n_rows
+  // (a row index outside drops every doc); null: mask row b
+  const int64_t* mask_rows = nullptr;
+  int64_t mask_n_rows = 0;
 };
 
 // BLOOM = false compiles the bloom test out (the scan kernels without a bloom filter keep
@@ -206,8 +218,13 @@ struct FilterSet {
 template <bool BLOOM>
 RB_HD inline bool pos_passes(const FilterSet& f, int64_t row, int64_t position) {
   if (f.mask != nullptr) {
+    int64_t mr = row;
+    if (f.mask_rows != nullptr) {
+      mr = f.mask_rows[row];
+      if (mr < 0 || mr >= f.mask_n_rows) return false;
+    }
     const int64_t w = position >> 6;
-    if (w < f.mask_words && ((f.mask[row * f.mask_words + w] >> (63 - (position & 63))) & 1ull) == 0) return false;
+    if (w < f.mask_words && ((f.mask[mr * f.mask_words + w] >> (63 - (position & 63))) & 1ull) == 0) return false;
   }
   if (f.ex.attrs != nullptr && !exact_pass(f.ex, f.ex.query + row * f.ex.n_clauses, position)) return false;
   if constexpr (BLOOM) {

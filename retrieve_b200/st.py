@@ -373,8 +373,10 @@ def fused_kmean_ann(cluster_offsets: Tensor, cluster_ids: Tensor, cluster_length
     calls, retrieve/src/retrieve/ops/official/adapter.py:289-335): ``(raw [B, W] int32 or
     fp16, idx [B, W] int32)``, ``W = round_up(max_tensor_size_per_row, 32)``, in the CUDA
     scorer's slot order, ``INT32_MIN`` / ``-65504`` and ``invalid_index_value`` where nothing
-    was scored. Float embeddings, ``filtering_bit_index`` and ``per_embedding_scale`` are the
-    reference's and not served here."""
+    was scored. ``filtering_bit_index`` [B] makes row ``b`` read mask row
+    ``filtering_bit_index[b]``; ``per_embedding_scale`` (fp16 [N], a per-doc divisor in the
+    divisor's place) gives fp16 ``fp16(fp32(fp16(dot)) / fp32(scale))``, the CUDA scorer's order.
+    Float embeddings are the reference's and not served here."""
     return _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
                   filtering_bit_mask, None, invalid_index_value, divisor_for_int8, filtering_bit_index,
                   per_embedding_scale, "st::fused_kmean_ann")
@@ -436,14 +438,16 @@ def fused_kmean_ann_with_partial_masks_multiple(
                       ("list_partial_mask_column_results", list_partial_mask_column_results)):
         _check(len(lst) == n, f"{name} must have the same size as list_cluster_offsets")
     if list_per_embedding_scale is not None:
-        raise NotImplementedError("st::fused_kmean_ann_with_partial_masks_multiple: per_embedding_scale is not served")
+        _check(len(list_per_embedding_scale) == n, "list_per_embedding_scale must have the same size as "
+                                                   "list_cluster_offsets")
     raws, idxs = [], []
     for i in range(n):
         raw, idx = fused_kmean_ann_with_partial_masks(
             list_cluster_offsets[i], list_selected_cluster_ids[i], list_selected_cluster_lengths[i],
             list_embeddings[i], queries, int(list_max_tensor_size_per_row[i]),
             list_partial_mask_column_counts_cumsum[i], list_partial_mask_first_item_offset_in_column[i],
-            list_partial_mask_column_results[i], invalid_index_value, divisor_for_int8, filtering_bit_index)
+            list_partial_mask_column_results[i], invalid_index_value, divisor_for_int8, filtering_bit_index,
+            None if list_per_embedding_scale is None else list_per_embedding_scale[i])
         raws.append(raw)
         idxs.append(idx)
     return raws, idxs
@@ -454,8 +458,6 @@ def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, ma
            per_embedding_scale, what):
     if embeddings.dtype != torch.int8 or queries.dtype != torch.int8:
         raise NotImplementedError(f"{what}: only int8 embeddings and queries are served here")
-    if filtering_bit_index is not None or per_embedding_scale is not None:
-        raise NotImplementedError(f"{what}: filtering_bit_index / per_embedding_scale are not served")
     for name, t in (("cluster_offsets", cluster_offsets), ("cluster_ids", cluster_ids),
                     ("cluster_length", cluster_length), ("embeddings", embeddings), ("queries", queries)):
         _check(t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
@@ -470,20 +472,40 @@ def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, ma
     offs = cluster_offsets.to(torch.int64).contiguous()
     cids = cluster_ids.to(torch.int64).contiguous()
     clen = cluster_length.to(torch.int64).contiguous()
-    raw = torch.empty((b, width), dtype=torch.int32 if divisor_for_int8 == -1 else torch.float16, device=dev)
+    scale = None
+    if per_embedding_scale is not None:  # the reference's checks, fused_kmean_ann_cuda.cu:2186-2200
+        _check(per_embedding_scale.is_cuda, "per_embedding_scale is not on GPU")
+        _check(per_embedding_scale.is_contiguous(), "per_embedding_scale is not contiguous")
+        _check(per_embedding_scale.dim() == 1, "per_embedding_scale is not 1D")
+        _check(per_embedding_scale.shape[0] == embeddings.shape[0],
+               "per_embedding_scale size does not match embedding size")
+        _check(per_embedding_scale.dtype == torch.float16, "per_embedding_scale is not half")
+        scale = per_embedding_scale
+    rows_index = None
+    if filtering_bit_index is not None:  # row b reads mask row filtering_bit_index[b]
+        _check(filtering_bit_index.is_cuda and filtering_bit_index.dim() == 1 and filtering_bit_index.shape[0] == b,
+               "filtering_bit_index must be a 1-D CUDA tensor of one mask row per query row")
+        rows_index = filtering_bit_index.to(torch.int64).contiguous()
+    half = divisor_for_int8 != -1 or scale is not None
+    raw = torch.empty((b, width), dtype=torch.float16 if half else torch.int32, device=dev)
     idx = torch.empty((b, width), dtype=torch.int32, device=dev)
     mask = None
     if filtering_bit_mask is not None:
-        _check(filtering_bit_mask.dim() == 2 and filtering_bit_mask.shape[0] == b, "filtering_bit_mask must be [B, W]")
+        _check(filtering_bit_mask.dim() == 2 and (rows_index is not None or filtering_bit_mask.shape[0] == b),
+               "filtering_bit_mask must be [B, W] (or [R, W] with filtering_bit_index)")
         mask = filtering_bit_mask.to(device=dev, dtype=torch.int64).contiguous()
+    mask_rows = 0 if mask is None else mask.shape[0]
     if partial is not None:
         cumsum, first, words = partial
         for name, t in (("partial_mask_column_counts_cumsum", cumsum),
                         ("partial_mask_first_item_offset_in_column", first),
                         ("partial_mask_column_results", words)):
             _check(t.is_cuda, f"{name} must be a CUDA tensor")
-        _check(cumsum.numel() == b * p and first.numel() == b * p,
-               "the partial mask needs one column cumsum and one bit offset per (row, probe)")
+        ranges = cumsum.numel()
+        _check(first.numel() == ranges and (ranges == b * p or (rows_index is not None and p > 0 and ranges % p == 0)),
+               "the partial mask needs one column cumsum and one bit offset per (row, probe) "
+               "(per (mask row, probe) with filtering_bit_index)")
+        mask_rows = ranges // p if p else b
         cumsum = cumsum.to(torch.int32).contiguous()
         first = first.to(torch.int8).contiguous()
         words = words.to(torch.int64).contiguous()
@@ -495,12 +517,14 @@ def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, ma
     ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
     common = (_ptr(offs), offs.numel() - 1 if offs.numel() else 0, _ptr(cids), _ptr(clen), p, _ptr(embeddings),
               embeddings.shape[0], _ptr(queries), b, d, int(max_tensor_size_per_row))
-    tail = (int(invalid_index_value), int(divisor_for_int8), _ptr(raw), _ptr(idx), _ptr(ws), ws.numel(), _stream(dev))
+    tail = (_ptr(scale), int(invalid_index_value), int(divisor_for_int8), _ptr(raw), _ptr(idx), _ptr(ws), ws.numel(),
+            _stream(dev))
     if partial is None:
-        rc = lib.rb_st_fused_kmean_ann(*common, _ptr(mask), 0 if mask is None else mask.shape[1], *tail)
+        rc = lib.rb_st_fused_kmean_ann(*common, _ptr(mask), mask_rows, 0 if mask is None else mask.shape[1],
+                                       _ptr(rows_index), *tail)
     else:
         rc = lib.rb_st_fused_kmean_ann_with_partial_masks(*common, _ptr(cumsum), _ptr(first), _ptr(words),
-                                                          words.numel(), *tail)
+                                                          words.numel(), mask_rows, _ptr(rows_index), *tail)
     _call(rc, what)
     return raw, idx
 
@@ -510,17 +534,19 @@ def _fake_fused_kmean_ann(cluster_offsets, cluster_ids, cluster_length, embeddin
                           filtering_bit_index=None, per_embedding_scale=None):
     width = (int(max_tensor_size_per_row) + 31) // 32 * 32
     b = queries.shape[0]
-    dt = torch.int32 if divisor_for_int8 == -1 else torch.float16
+    dt = torch.int32 if divisor_for_int8 == -1 and per_embedding_scale is None else torch.float16
     return queries.new_empty((b, width), dtype=dt), queries.new_empty((b, width), dtype=torch.int32)
 
 
 def _fake_fused_partial(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
                         *args, invalid_index_value=-1, divisor_for_int8=-1, **kwargs):
-    # positional form: args = (cumsum, first, words, invalid_index_value, divisor_for_int8, ...)
+    # positional form: args = (cumsum, first, words, invalid_index_value, divisor_for_int8,
+    # filtering_bit_index, per_embedding_scale, ...)
     if len(args) >= 5:
         divisor_for_int8 = args[4]
+    scale = args[6] if len(args) >= 7 else kwargs.get("per_embedding_scale")
     return _fake_fused_kmean_ann(cluster_offsets, cluster_ids, cluster_length, embeddings, queries,
-                                 max_tensor_size_per_row, divisor_for_int8=divisor_for_int8)
+                                 max_tensor_size_per_row, divisor_for_int8=divisor_for_int8, per_embedding_scale=scale)
 
 
 def _fake_fused_partial_multiple(queries, list_cluster_offsets, list_selected_cluster_ids,
@@ -528,8 +554,9 @@ def _fake_fused_partial_multiple(queries, list_cluster_offsets, list_selected_cl
                                  *args, invalid_index_value=-1, divisor_for_int8=-1, **kwargs):
     if len(args) >= 5:
         divisor_for_int8 = args[4]
+    scales = args[6] if len(args) >= 7 else kwargs.get("list_per_embedding_scale")
     b = queries.shape[0]
-    dt = torch.int32 if divisor_for_int8 == -1 else torch.float16
+    dt = torch.int32 if divisor_for_int8 == -1 and scales is None else torch.float16
     widths = [(int(m) + 31) // 32 * 32 for m in list_max_tensor_size_per_row]
     return ([queries.new_empty((b, w), dtype=dt) for w in widths],
             [queries.new_empty((b, w), dtype=torch.int32) for w in widths])

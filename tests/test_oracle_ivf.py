@@ -104,6 +104,53 @@ def test_fused_kmean_ann_rows_match_reference_scorer(ci):
     assert (r16[~kept].view(np.uint16) == 0xFBFF).all()
 
 
+FUSED = np.load(Path(__file__).resolve().parent / "golden" / "golden_fused.npz")
+
+
+def _fused_cases():
+    words = ivf.pack_mask_high_first(FUSED["mask"])
+    return {"scaled": dict(per_embedding_scale=FUSED["scale"]),
+            "scaled_div": dict(per_embedding_scale=FUSED["scale"], divisor_for_int8=16),
+            "index_i32": dict(filtering_bit_mask=words, filtering_bit_index=FUSED["mask_index"]),
+            "index_scaled": dict(filtering_bit_mask=words, filtering_bit_index=FUSED["mask_index"],
+                                 per_embedding_scale=FUSED["scale"], invalid_index_value=-5)}
+
+
+@pytest.mark.parametrize("name", ["scaled", "scaled_div", "index_i32", "index_scaled"])
+def test_fused_kmean_ann_scale_and_mask_rows_match_reference(name):
+    """``per_embedding_scale`` (which wins over the divisor) and ``filtering_bit_index`` against
+    the reference's CPU scorer (tests/golden/make_golden_fused.py): per row the same (position,
+    raw bits) multiset, dtype and pads; the fixture's dots are below 2048, where the CPU and
+    CUDA orders of the scaled division agree."""
+    kw = _fused_cases()[name]
+    raw, idx = ivf.fused_kmean_ann(FUSED["q"], FUSED["offsets"], FUSED["probe"], FUSED["lengths"], FUSED["codes"],
+                                   int(FUSED["width"]), **kw)
+    want_r, want_i = FUSED[f"{name}_raw"], FUSED[f"{name}_idx"]
+    assert raw.dtype == want_r.dtype and raw.shape == want_r.shape
+    bits = np.uint16 if raw.dtype == np.float16 else np.int32
+    for r in range(raw.shape[0]):
+        got, want = idx[r] >= 0, want_i[r] >= 0
+        assert sorted(zip(idx[r][got].tolist(), raw[r][got].view(bits).tolist())) == sorted(
+            zip(want_i[r][want].tolist(), want_r[r][want].view(bits).tolist()))
+        assert (idx[r][~got] == kw.get("invalid_index_value", -1)).all()
+
+
+def test_scaled_division_rounds_the_dot_to_fp16_first():
+    """The CUDA scorer divides Half(dot) by the Half scale (index_mm_helpers.cuh:49-53); above
+    2048 an integer dot is not exact in fp16, so its result differs from the CPU scorer's
+    Half(float(dot) / scale) (fused_kmean_ann.cpp:196-199) for some dots: the restatement follows
+    the CUDA op it replaces."""
+    codes = np.ones((1, 65), dtype=np.int8)
+    q = np.full((1, 65), 32, dtype=np.int8)
+    q[0, 64] = 1  # dot 2049: fp16 rounds it to 2048
+    scale = np.array([3.0], dtype=np.float16)
+    raw, _ = ivf.fused_kmean_ann(q, np.array([0, 1]), np.array([[0]]), np.array([[1]]), codes, 32,
+                                 per_embedding_scale=scale)
+    cuda_form = np.float16(np.float32(np.float16(2049.0)) / np.float32(3.0))  # 682.5
+    cpu_form = np.float16(np.float32(2049.0) / np.float32(3.0))  # 683
+    assert raw[0, 0] == cuda_form and cuda_form != cpu_form
+
+
 def test_fused_kmean_ann_mask_and_clipping():
     """A cluster longer than the row fills the row's whole warps; slots whose mask bit is
     clear keep the pads."""

@@ -94,12 +94,14 @@ def test_fused_kmean_ann_fake_and_argument_errors():
                                     torch.empty(4, 3, dtype=torch.int64), torch.empty(100, 64, dtype=torch.int8),
                                     torch.empty(4, 64, dtype=torch.int8), 90, divisor_for_int8=8)
         assert raw.dtype == torch.float16
+        raw, _ = st.fused_kmean_ann(torch.empty(9, dtype=torch.int64), torch.empty(4, 3, dtype=torch.int64),
+                                    torch.empty(4, 3, dtype=torch.int64), torch.empty(100, 64, dtype=torch.int8),
+                                    torch.empty(4, 64, dtype=torch.int8), 90,
+                                    per_embedding_scale=torch.empty(100, dtype=torch.float16))
+        assert raw.dtype == torch.float16  # a per-doc divisor makes the raw scores fp16
     off, ids, lens = torch.tensor([0, 4]), torch.zeros(2, 1, dtype=torch.int64), torch.full((2, 1), 4)
     with pytest.raises(NotImplementedError, match="int8"):
         rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64), torch.zeros(2, 64), 4)
-    with pytest.raises(NotImplementedError, match="per_embedding_scale"):
-        rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64, dtype=torch.int8), torch.zeros(2, 64, dtype=torch.int8),
-                            4, per_embedding_scale=torch.ones(4, dtype=torch.float16))
     with pytest.raises(RuntimeError, match="CUDA"):
         rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64, dtype=torch.int8), torch.zeros(2, 64, dtype=torch.int8),
                             4)
@@ -112,10 +114,14 @@ def test_fused_kmean_ann_capi_checks_need_no_device():
     assert n.value >= 4 * 96 * 8
     assert lib.rb_st_fused_kmean_ann_workspace_size(-1, 8, 90, ctypes.byref(n)) == _lib.RB_ERR_INVALID_ARG
 
-    def call(b=4, d=64, p=8, width=90, div=-1, ws=None, ws_bytes=0, mask_words=2):
-        return lib.rb_st_fused_kmean_ann(None, 8, None, None, p, None, 100, None, b, d, width, None, mask_words, -1,
-                                         div, None, None, ws, ws_bytes, None)
+    fake = ctypes.c_void_p(16)  # never dereferenced: the checks fail first
 
+    def call(b=4, d=64, p=8, width=90, div=-1, ws=None, ws_bytes=0, mask=None, mask_rows=4, index=None):
+        return lib.rb_st_fused_kmean_ann(None, 8, None, None, p, None, 100, None, b, d, width, mask, mask_rows, 2,
+                                         index, None, -1, div, None, None, ws, ws_bytes, None)
+
+    assert call(mask=fake, mask_rows=3) == _lib.RB_ERR_INVALID_ARG  # fewer mask rows than query rows
+    assert call(mask=fake, mask_rows=3, index=fake) == _lib.RB_ERR_WORKSPACE  # rows picked by filtering_bit_index
     assert call(div=0) == _lib.RB_ERR_INVALID_ARG
     assert call(d=0) == _lib.RB_ERR_INVALID_ARG
     assert call(p=4096) == _lib.RB_ERR_UNSUPPORTED
@@ -627,3 +633,78 @@ def test_fused_kmean_ann_lengths_and_clipping():
         raw, idx = st.fused_kmean_ann(*dev, width)
         want_r, want_i = ivf.fused_kmean_ann(q, offsets, probe, lengths, codes, width)
         assert np.array_equal(raw.cpu().numpy(), want_r) and np.array_equal(idx.cpu().numpy(), want_i)
+
+
+FUSED = np.load(Path(__file__).resolve().parent / "golden" / "golden_fused.npz")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["scaled", "scaled_div", "index_i32", "index_scaled"])
+def test_fused_kmean_ann_scale_and_mask_rows(case):
+    """per_embedding_scale and filtering_bit_index on the device: bit for bit the restatement
+    (pinned to the reference's CPU scorer by the fixture), slot order and pads included."""
+    st = _st()
+    words = ivf.pack_mask_high_first(FUSED["mask"])
+    kw = {"scaled": dict(per_embedding_scale=FUSED["scale"]),
+          "scaled_div": dict(per_embedding_scale=FUSED["scale"], divisor_for_int8=16),
+          "index_i32": dict(filtering_bit_mask=words, filtering_bit_index=FUSED["mask_index"]),
+          "index_scaled": dict(filtering_bit_mask=words, filtering_bit_index=FUSED["mask_index"],
+                               per_embedding_scale=FUSED["scale"], invalid_index_value=-5)}[case]
+    dev = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda() if isinstance(v, np.ndarray) else v
+           for k, v in kw.items()}
+    t = [torch.from_numpy(np.ascontiguousarray(FUSED[k])).cuda() for k in ("offsets", "probe", "lengths", "codes", "q")]
+    width = int(FUSED["width"])
+    raw, idx = st.fused_kmean_ann(*t, width, **dev)
+    want_r, want_i = ivf.fused_kmean_ann(FUSED["q"], FUSED["offsets"], FUSED["probe"], FUSED["lengths"],
+                                         FUSED["codes"], width, **kw)
+    got_r = raw.cpu().numpy()
+    assert got_r.dtype == want_r.dtype
+    bits = np.uint16 if got_r.dtype == np.float16 else np.int32
+    assert np.array_equal(got_r.view(bits), want_r.view(bits)) and np.array_equal(idx.cpu().numpy(), want_i)
+
+
+@pytest.mark.gpu
+def test_fused_kmean_ann_scale_rounds_large_dots_like_the_cuda_scorer():
+    """Full-range codes (dots up to ~10^6 at D = 64): the scaled raw is
+    fp16(fp32(fp16(dot)) / scale), the CUDA scorer's order, bit for bit; and a partial-mask call
+    whose rows read the partial masks of other rows through filtering_bit_index."""
+    st = _st()
+    rng = np.random.default_rng(31)
+    sizes = rng.integers(0, 300, 30)
+    offsets = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    n, d, b, p = int(offsets[-1]), 64, 20, 5
+    codes = rng.integers(-128, 128, (n, d), dtype=np.int8)
+    q = rng.integers(-128, 128, (b, d), dtype=np.int8)
+    probe = np.argsort(rng.random((b, 30)), axis=1)[:, :p].astype(np.int64)
+    lengths = sizes[probe].astype(np.int64)
+    width = int(lengths.sum(1).max())
+    scale = (rng.random(n) * 8 + 0.01).astype(np.float16)
+    t = [torch.from_numpy(np.ascontiguousarray(x)).cuda() for x in (offsets, probe, lengths, codes, q)]
+    raw, idx = st.fused_kmean_ann(*t, width, per_embedding_scale=torch.from_numpy(scale).cuda())
+    want_r, want_i = ivf.fused_kmean_ann(q, offsets, probe, lengths, codes, width, per_embedding_scale=scale)
+    assert np.array_equal(raw.cpu().numpy().view(np.uint16), want_r.view(np.uint16))
+    assert np.array_equal(idx.cpu().numpy(), want_i)
+    # partial masks of 7 "mask rows" (ranges of row r's probes), rows mapped onto them
+    mask = rng.random((7, n)) < 0.5
+    words = ivf.pack_mask_high_first(mask)
+    rows_map = rng.integers(0, 7, b).astype(np.int64)
+    sel_rows = np.arange(7) % b
+    sel_off, sel_len = offsets[probe[sel_rows]], lengths[sel_rows]
+    counts, _, first = ivf.column_info(sel_off, sel_len)
+    cumsum = np.cumsum(counts, dtype=np.int32)
+    chunks = []
+    for i in range(7 * p):
+        start, cnt = int(sel_off.reshape(-1)[i]) // 64, int(counts[i])
+        chunks.append(words[i // p, start:start + cnt])
+    resp = np.concatenate(chunks).astype(np.int64)
+    # rows whose mask row holds the same probes as themselves see their own ranges
+    probe2 = probe.copy()
+    probe2[:] = probe[sel_rows[rows_map]]
+    lengths2 = sizes[probe2].astype(np.int64)
+    t2 = [torch.from_numpy(np.ascontiguousarray(x)).cuda() for x in (offsets, probe2, lengths2, codes, q)]
+    part = [torch.from_numpy(np.ascontiguousarray(x)).cuda() for x in (cumsum, first, resp)]
+    w2 = int(lengths2.sum(1).max())
+    raw2, idx2 = st.fused_kmean_ann_with_partial_masks(*t2, w2, *part,
+                                                       filtering_bit_index=torch.from_numpy(rows_map).cuda())
+    want2 = ivf.fused_kmean_ann(q, offsets, probe2, lengths2, codes, w2, filtering_bit_mask=words[rows_map])
+    assert np.array_equal(raw2.cpu().numpy(), want2[0]) and np.array_equal(idx2.cpu().numpy(), want2[1])
