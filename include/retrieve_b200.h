@@ -564,6 +564,21 @@ RB_API int rb_st_bloom_partial_search(const int64_t* bloom_index, int64_t index_
                                       void* stream);
 
 /*
+ * The centroid update of the IVF build's k-means, replacing KMeans._cluster_sums
+ * (retrieve/src/retrieve/indexing/kmeans.py:98-119, an fp64 one-hot GEMM per row chunk):
+ * out_sums [n_lists, D] fp64 = per cluster the sum of its rows of embs [N, D] (dtype RB_F32,
+ * RB_F16 or RB_BF16), out_counts [n_lists] int64 = its rows, for assignments [N] int64 (rows
+ * assigned outside [0, n_lists) are left out). Each cluster's rows are added in increasing row
+ * order in fp64 after a stable counting sort: bit-for-bit reproducible, equal to the reference's
+ * sums whenever the fp64 additions are exact. 1 <= n_lists <= 2^24. Workspace from
+ * rb_kmeans_cluster_sums_workspace_size.
+ */
+RB_API int rb_kmeans_cluster_sums_workspace_size(int64_t N, int64_t n_lists, size_t* bytes);
+RB_API int rb_kmeans_cluster_sums(const void* embs, int dtype, int64_t N, int D, const int64_t* assignments,
+                                  int64_t n_lists, double* out_sums, int64_t* out_counts, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/*
  * SilverTorch's expression parser on the host, replacing
  *   st::parse_expression_query_batch(str[] expressions, Tensor silvertorch_ks, int bloom_hash_k,
  *                                    bool return_query_plan=True, int max_sub_queries=5)
