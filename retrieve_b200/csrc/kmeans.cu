@@ -116,8 +116,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_tiles_kernel(int64_t* __res
   if (threadIdx.x == 0) totals[blockIdx.x] = total;
 }
 
-__global__ void __launch_bounds__(kScanThreads) scan_totals_kernel(int64_t* __restrict__ totals, int64_t n,
-                                                                    int64_t* __restrict__ grand_total) {
+__global__ void __launch_bounds__(kScanThreads) scan_totals_kernel(int64_t* __restrict__ totals, int64_t n) {
   __shared__ int64_t part[kScanThreads];
   const int64_t per = (n + kScanThreads - 1) / kScanThreads;
   const int64_t i0 = min(n, threadIdx.x * per), i1 = min(n, i0 + per);
@@ -130,7 +129,6 @@ __global__ void __launch_bounds__(kScanThreads) scan_totals_kernel(int64_t* __re
     totals[i] = acc;
     acc += v;
   }
-  if (threadIdx.x == 0) *grand_total = total;
 }
 
 __global__ void __launch_bounds__(kScanThreads) scan_add_kernel(int64_t* __restrict__ a, int64_t n,
@@ -189,7 +187,7 @@ int rb_kmeans_cluster_sums_workspace_size(int64_t N, int64_t n_lists, size_t* by
   }
   const Plan p = plan_for(N, n_lists);
   *bytes = align_up(static_cast<size_t>(p.entries) * 8, 256) + align_up(static_cast<size_t>(p.tiles) * 8, 256) +
-           align_up(8, 256) + align_up(static_cast<size_t>(std::max<int64_t>(N, 1)) * 8, 256);
+           align_up(static_cast<size_t>(std::max<int64_t>(N, 1)) * 8, 256);
   return RB_OK;
 }
 
@@ -218,8 +216,6 @@ int rb_kmeans_cluster_sums(const void* embs, int dtype, int64_t N, int D, const 
   ws += align_up(static_cast<size_t>(p.entries) * 8, 256);
   int64_t* totals = reinterpret_cast<int64_t*>(ws);
   ws += align_up(static_cast<size_t>(p.tiles) * 8, 256);
-  int64_t* grand = reinterpret_cast<int64_t*>(ws);
-  ws += align_up(8, 256);
   int64_t* order = reinterpret_cast<int64_t*>(ws);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
@@ -233,7 +229,7 @@ int rb_kmeans_cluster_sums(const void* embs, int dtype, int64_t N, int D, const 
     km_walk_kernel<false><<<walk_blocks, 32 * kWarpsPerBlock, 0, s>>>(assignments, N, n_lists, p.chunk, p.n_chunks,
                                                                       table, order);
   scan_tiles_kernel<<<static_cast<unsigned>(p.tiles), kScanThreads, 0, s>>>(table, p.entries, totals);
-  scan_totals_kernel<<<1, kScanThreads, 0, s>>>(totals, p.tiles, grand);
+  scan_totals_kernel<<<1, kScanThreads, 0, s>>>(totals, p.tiles);
   scan_add_kernel<<<static_cast<unsigned>(p.tiles), kScanThreads, 0, s>>>(table, p.entries, totals);
   int rc = launch_status();
   if (rc != RB_OK) return rc;
