@@ -708,3 +708,41 @@ def test_fused_kmean_ann_scale_rounds_large_dots_like_the_cuda_scorer():
                                                        filtering_bit_index=torch.from_numpy(rows_map).cuda())
     want2 = ivf.fused_kmean_ann(q, offsets, probe2, lengths2, codes, w2, filtering_bit_mask=words[rows_map])
     assert np.array_equal(raw2.cpu().numpy(), want2[0]) and np.array_equal(idx2.cpu().numpy(), want2[1])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("grouped", [False, True])
+def test_search_replays_in_a_cuda_graph(grouped):
+    """st::search allocates only through the caller's allocator and never waits on the host, so it
+    captures into a CUDA graph (the reference's capture test, test_silvertorch_compile.py:196-270):
+    replays with new query values equal eager calls, bit for bit."""
+    _st()
+    from retrieve_b200 import st
+
+    g, meta = _case(3)
+    t = {key: torch.from_numpy(np.ascontiguousarray(g[key])).cuda()
+         for key in ("query", "probe", "offsets", "sizes", "codes", "sort_perm")}
+    gs = torch.from_numpy(g["gs"]).cuda()
+    fn = st.search_grouped if grouped else torch.ops.st.search
+    q = t["query"].clone()
+
+    def call():
+        return fn(q, t["probe"], t["offsets"], t["sizes"], t["codes"], t["sort_perm"], gs, meta["k"], meta["width"])
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            call()  # warm-up outside the capture
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ids_g, scores_g = call()
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    for _ in range(3):
+        q.copy_(torch.randn(q.shape, generator=gen, device="cuda"))
+        graph.replay()
+        ids, scores = call()
+        torch.cuda.synchronize()
+        assert torch.equal(ids_g, ids) and torch.equal(scores_g, scores)
+    del graph
