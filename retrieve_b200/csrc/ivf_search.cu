@@ -960,8 +960,12 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   rc = launch_status();
   if (rc != RB_OK) return rc;
   const size_t smem = group_smem_bytes(D);
-  static bool smem_set = false;
-  if (!smem_set) {
+  // the limit is a per-device setting of the function: raised once on each device used
+  static bool smem_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool known = dev >= 0 && dev < 64;
+  if (!known || !smem_set[dev]) {
     // the largest tile (D = 1024) needs about 150 KB of the 227 KB a block may opt into
     const int most = static_cast<int>(group_smem_bytes(kMaxSearchD));
     const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
@@ -972,7 +976,7 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
       set_last_error("st::search: cannot raise the grouped scan's shared memory limit");
       return RB_ERR_CUDA;
     }
-    smem_set = true;
+    if (known) smem_set[dev] = true;
   }
   const int64_t max_tasks = (n_pairs + G - 1) / G + std::min<int64_t>(n_lists, n_pairs);
   GroupArgs ga{item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask,
