@@ -487,7 +487,11 @@ RB_API int rb_st_search_finish(const float* query, int B, int D, const int64_t* 
  *                       int divisor_for_int8=-1, ...) -> (Tensor, Tensor)
  * (silvertorch/ops/csrc/fused_kmean_ann.cpp:86-228 for the CPU form; fused_kmean_ann_cuda.cu
  * :2126-2262). cluster_ids / cluster_length [B, P] int64 (the probed clusters and their
- * lengths), embeddings [N, D] and queries [B, D] int8. Output [B, round_up(width, 32)]: in
+ * lengths), embeddings [N, D] and queries [B, D] of one dtype: RB_I8, or RB_F32 / RB_F16 /
+ * RB_BF16, for which out_raw has the embeddings' type and holds the CUDA scorer's fused
+ * multiply-add chains (blocks of 256 or 384 bytes, fp16 / bf16 in even / odd pairs; D a
+ * multiple of 16 bytes; pads -FLT_MAX / -65504 / bf16 0xff7f; divisor and per-doc scale unused).
+ * Output [B, round_up(width, 32)]: in
  * the CUDA scorer's slot order (warp-aligned prefixes, then remainders), out_raw holds the
  * int32 dot (divisor -1) or fp16(fp32(dot) / divisor), out_idx the int32 position; empty,
  * filtered (filtering_bit_mask [mask_rows, mask_words], high bit first) and padding slots
@@ -500,8 +504,8 @@ RB_API int rb_st_search_finish(const float* query, int B, int D, const int64_t* 
  */
 RB_API int rb_st_fused_kmean_ann_workspace_size(int B, int P, int max_tensor_size_per_row, size_t* bytes);
 RB_API int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
-                                 const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
-                                 const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+                                 const int64_t* cluster_length, int P, const void* embeddings, int64_t N,
+                                 const void* queries, int dtype, int B, int D, int max_tensor_size_per_row,
                                  const int64_t* filtering_bit_mask, int64_t mask_rows, int64_t mask_words,
                                  const int64_t* filtering_bit_index, const uint16_t* per_embedding_scale,
                                  int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
@@ -521,7 +525,7 @@ RB_API int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists
  */
 RB_API int rb_st_fused_kmean_ann_with_partial_masks(
     const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids, const int64_t* cluster_length, int P,
-    const int8_t* embeddings, int64_t N, const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+    const void* embeddings, int64_t N, const void* queries, int dtype, int B, int D, int max_tensor_size_per_row,
     const int32_t* column_counts_cumsum, const int8_t* first_item_offset_in_column, const int64_t* column_results,
     int64_t n_column_results, int64_t mask_rows, const int64_t* filtering_bit_index,
     const uint16_t* per_embedding_scale, int invalid_index_value, int divisor_for_int8, void* out_raw,

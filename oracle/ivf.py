@@ -206,9 +206,13 @@ def search(query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_pe
                         global_scale, k, max_tensor_size_per_row, divisor_for_int8, filtering_bit_mask, exact)
 
 
+FLOAT_PADS = {"fp32": np.float32(-np.finfo(np.float32).max), "fp16": np.float16(-65504.0),
+              "bf16": np.uint32(0xFF7F0000).view(np.float32)}
+
+
 def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_codes, max_tensor_size_per_row,
                     divisor_for_int8=-1, filtering_bit_mask=None, invalid_index_value=-1, partial=None,
-                    filtering_bit_index=None, per_embedding_scale=None):
+                    filtering_bit_index=None, per_embedding_scale=None, float_format=None):
     """``st::fused_kmean_ann`` on int8 codes as its CUDA impl returns it
     (silvertorch/ops/csrc/fused_kmean_ann_cuda.cu:2126-2262, outputs pre-filled at
     :1491-1510): ``(raw [B, W], idx [B, W] int32)``, ``W = padded_width(...)``. Row ``b``
@@ -223,7 +227,14 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
     partial masks' row) it reads. ``per_embedding_scale`` (fp16 [N], a per-doc divisor that
     takes the divisor's place) gives the fp16 raw ``fp16(fp32(fp16(dot)) / fp32(scale[pos]))``,
     the CUDA scorer's order (index_mm_helpers.cuh:49-56: the dot rounded to fp16 first; the CPU
-    scorer divides the unrounded dot, fused_kmean_ann.cpp:196-199, equal for |dot| <= 2048)."""
+    scorer divides the unrounded dot, fused_kmean_ann.cpp:196-199, equal for |dot| <= 2048).
+    ``float_format`` ("fp32", "fp16", "bf16"; embeddings and queries given as float arrays of
+    values in that format) scores by the CUDA scorer's chains (``oracle.fdot.dot``): raw of the
+    format (bf16 values as float32), pads -FLT_MAX / -65504 / bf16 0xff7f; no divisor or scale."""
+    if float_format is not None:
+        return _fused_float(q_codes, cluster_offsets, cluster_ids, cluster_length, item_codes,
+                            max_tensor_size_per_row, float_format, filtering_bit_mask, invalid_index_value,
+                            filtering_bit_index)
     q_codes = np.asarray(q_codes, dtype=np.int8)
     offsets = np.asarray(cluster_offsets, dtype=np.int64)
     cids = np.asarray(cluster_ids, dtype=np.int64)
@@ -268,6 +279,28 @@ def fused_kmean_ann(q_codes, cluster_offsets, cluster_ids, cluster_length, item_
             raw[row, slot] = raw_scores(q_codes[row], item_codes, pos, divisor_for_int8)
         idx[row, slot] = pos.astype(np.int32)
     return raw, idx
+
+
+def _fused_float(q, cluster_offsets, cluster_ids, cluster_length, items, max_tensor_size_per_row, fmt,
+                 filtering_bit_mask, invalid_index_value, filtering_bit_index):
+    from oracle import fdot
+
+    items = np.asarray(items, dtype=np.float64)
+    q = np.asarray(q, dtype=np.float64)
+    # the slot layout and the filters of the int8 restatement, on stand-in codes
+    zeros = np.zeros(items.shape, dtype=np.int8)
+    _, idx = fused_kmean_ann(np.zeros(q.shape, dtype=np.int8), cluster_offsets, cluster_ids, cluster_length, zeros,
+                             max_tensor_size_per_row, filtering_bit_mask=filtering_bit_mask,
+                             invalid_index_value=-1, filtering_bit_index=filtering_bit_index)
+    out_dtype = np.float16 if fmt == "fp16" else np.float32
+    raw = np.full(idx.shape, fdot_pad(fmt), dtype=out_dtype)
+    for b, s in zip(*np.nonzero(idx >= 0)):
+        raw[b, s] = fdot.dot(items[idx[b, s]], q[b], fmt)
+    return raw, np.where(idx >= 0, idx, invalid_index_value).astype(np.int32)
+
+
+def fdot_pad(fmt):
+    return FLOAT_PADS[fmt]
 
 
 def probe_prep(query, probe_ids, cluster_offsets, cluster_sizes):

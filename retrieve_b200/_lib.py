@@ -106,13 +106,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_st_fused_kmean_ann_workspace_size": (_c_int, [_c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]),
     "rb_st_fused_kmean_ann": (
         _c_int,
-        [_vp, _c_i64, _vp, _vp, _c_int, _vp, _c_i64, _vp, _c_int, _c_int, _c_int, _vp, _c_i64, _c_i64, _vp, _vp,
-         _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp],
+        [_vp, _c_i64, _vp, _vp, _c_int, _vp, _c_i64, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _c_i64, _c_i64, _vp,
+         _vp, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp],
     ),
     "rb_st_fused_kmean_ann_with_partial_masks": (
         _c_int,
-        [_vp, _c_i64, _vp, _vp, _c_int, _vp, _c_i64, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_i64, _c_i64, _vp,
-         _vp, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp],
+        [_vp, _c_i64, _vp, _vp, _c_int, _vp, _c_i64, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_i64,
+         _c_i64, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp],
     ),
     "rb_st_bloom_search": (
         _c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp]

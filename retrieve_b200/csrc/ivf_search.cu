@@ -30,9 +30,11 @@
 // clipped to [0, N), and slots past the row width are dropped (the
 // reference's CUDA scorer requires the probed total to fit the width and does
 // not check it).
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cfloat>
 #include <cstdint>
 
 #include "rb_capi_internal.h"
@@ -221,6 +223,87 @@ __global__ void raw_scores_kernel(const int8_t* __restrict__ items, int64_t N, i
     reinterpret_cast<__half*>(out_raw)[o] = __float2half_rn(__fdiv_rn(num, den));
   } else
     reinterpret_cast<int32_t*>(out_raw)[o] = acc;
+  out_idx[o] = static_cast<int32_t>(p);
+}
+
+// st::fused_kmean_ann on float embeddings (fp32, fp16, bf16), the CUDA scorer's arithmetic
+// (simple_index_mm.cuh:41-56, 96-151, 160-300): per doc one fused multiply-add chain per block
+// of `unit` elements in element order — fp32 in one float, fp16 / bf16 in a packed pair (even
+// elements in the low half, odd in the high), rounded at every step — the blocks added in
+// order onto zero (a single block is taken as it is), the pair's halves added last. The raw
+// score has the embeddings' type; divisor and per-doc scales do not apply.
+template <typename T>
+struct FloatDot;
+
+template <>
+struct FloatDot<float> {
+  using Acc = float;
+  __device__ static Acc zero() { return 0.0f; }
+  __device__ static Acc block(const float* x, const float* q, int n) {
+    float a = 0.0f;
+    for (int i = 0; i < n; ++i) a = __fmaf_rn(x[i], q[i], a);
+    return a;
+  }
+  __device__ static Acc add(Acc a, Acc b) { return __fadd_rn(a, b); }
+  __device__ static float finish(Acc a) { return a; }
+};
+
+template <>
+struct FloatDot<__half> {
+  using Acc = __half2;
+  __device__ static Acc zero() { return __float2half2_rn(0.0f); }
+  __device__ static Acc block(const __half* x, const __half* q, int n) {
+    __half2 a = zero();
+    for (int i = 0; i < n; i += 2) a = __hfma2(__halves2half2(x[i], x[i + 1]), __halves2half2(q[i], q[i + 1]), a);
+    return a;
+  }
+  __device__ static Acc add(Acc a, Acc b) { return __hadd2(a, b); }
+  __device__ static __half finish(Acc a) { return __hadd(__low2half(a), __high2half(a)); }
+};
+
+template <>
+struct FloatDot<__nv_bfloat16> {
+  using Acc = __nv_bfloat162;
+  __device__ static Acc zero() { return __float2bfloat162_rn(0.0f); }
+  __device__ static Acc block(const __nv_bfloat16* x, const __nv_bfloat16* q, int n) {
+    __nv_bfloat162 a = zero();
+    for (int i = 0; i < n; i += 2)
+      a = __hfma2(__halves2bfloat162(x[i], x[i + 1]), __halves2bfloat162(q[i], q[i + 1]), a);
+    return a;
+  }
+  __device__ static Acc add(Acc a, Acc b) { return __hadd2(a, b); }
+  __device__ static __nv_bfloat16 finish(Acc a) { return __hadd(__low2bfloat16(a), __high2bfloat16(a)); }
+};
+
+template <typename T>
+__global__ void raw_scores_float_kernel(const T* __restrict__ items, int64_t N, int D, int unit,
+                                        const T* __restrict__ q, const int64_t* __restrict__ pos,
+                                        const int64_t* __restrict__ counts, int width, int invalid, T pad,
+                                        T* __restrict__ out_raw, int32_t* __restrict__ out_idx) {
+  extern __shared__ __align__(16) uint8_t fraw_sm[];
+  T* sq = reinterpret_cast<T*>(fraw_sm);
+  const int64_t b = blockIdx.y;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) sq[d] = q[b * D + d];
+  __syncthreads();
+  const int64_t slot = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (slot >= width) return;
+  const int64_t o = b * width + slot;
+  const int64_t p = slot < counts[b] ? pos[o] : -1;
+  if (p < 0 || p >= N) {
+    out_raw[o] = pad;
+    out_idx[o] = invalid;
+    return;
+  }
+  const T* row = items + p * D;
+  using F = FloatDot<T>;
+  typename F::Acc acc;
+  if (unit == D) {
+    acc = F::block(row, sq, D);
+  } else {
+    acc = F::zero();
+    for (int b0 = 0; b0 < D; b0 += unit) acc = F::add(acc, F::block(row + b0, sq + b0, unit));
+  }
+  out_raw[o] = F::finish(acc);
   out_idx[o] = static_cast<int32_t>(p);
 }
 
@@ -1082,9 +1165,20 @@ int rb_st_fused_kmean_ann_workspace_size(int B, int P, int max_tensor_size_per_r
 
 }  // extern "C"
 
+// Block length of the float scorer's chains (simple_index_mm.cuh:237-300): the whole row when it
+// fits 256 bytes, else 256 bytes' worth when that divides D, else 384 bytes' worth; 0 when
+// neither divides D (the reference has no kernel for that D).
+static int float_dot_unit(int D, int elem_bytes) {
+  if (D % (16 / elem_bytes) != 0) return 0;
+  if (D * elem_bytes <= 256) return D;
+  if (D % (256 / elem_bytes) == 0) return 256 / elem_bytes;
+  if (D % (384 / elem_bytes) == 0) return 384 / elem_bytes;
+  return 0;
+}
+
 static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
-                                const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
-                                const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+                                const int64_t* cluster_length, int P, const void* embeddings, int64_t N,
+                                const void* queries, int dtype, int B, int D, int max_tensor_size_per_row,
                                 const int64_t* filtering_bit_mask, int64_t mask_rows, int64_t mask_words,
                                 const int64_t* filtering_bit_index, const PartialMask& pm,
                                 const uint16_t* per_embedding_scale, int invalid_index_value, int divisor_for_int8,
@@ -1100,6 +1194,16 @@ static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists,
   }
   if (P > kMaxProbes || B > 65535 || N > INT32_MAX || D > 16384) {
     set_last_error("fused_kmean_ann: more than 2048 probes, 65535 rows, 2^31 docs or D > 16384 is not supported");
+    return RB_ERR_UNSUPPORTED;
+  }
+  if (dtype != RB_I8 && dtype != RB_F32 && dtype != RB_F16 && dtype != RB_BF16) {
+    set_last_error("fused_kmean_ann: embeddings must be int8, fp32, fp16 or bf16");
+    return RB_ERR_TYPE;
+  }
+  const int unit = dtype == RB_I8 ? D : float_dot_unit(D, dtype == RB_F32 ? 4 : 2);
+  if (unit == 0) {
+    set_last_error("fused_kmean_ann: D must be a multiple of 16 bytes, and past 256 bytes a multiple of 256 or "
+                   "384 bytes, for float embeddings");
     return RB_ERR_UNSUPPORTED;
   }
   const int width = st_width(max_tensor_size_per_row);
@@ -1122,13 +1226,34 @@ static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists,
   int rc = launch_status();
   if (rc != RB_OK) return rc;
   const dim3 grid(static_cast<unsigned>((width + 255) / 256), static_cast<unsigned>(B));
+  if (dtype == RB_F32) {
+    raw_scores_float_kernel<float><<<grid, 256, align_up(static_cast<size_t>(D) * 4, 16), s>>>(
+        static_cast<const float*>(embeddings), N, D, unit, static_cast<const float*>(queries), pos, counts, width,
+        invalid_index_value, -FLT_MAX, static_cast<float*>(out_raw), out_idx);
+    return launch_status();
+  }
+  if (dtype == RB_F16) {
+    raw_scores_float_kernel<__half><<<grid, 256, align_up(static_cast<size_t>(D) * 2, 16), s>>>(
+        static_cast<const __half*>(embeddings), N, D, unit, static_cast<const __half*>(queries), pos, counts, width,
+        invalid_index_value, __ushort_as_half(0xfbffu), static_cast<__half*>(out_raw), out_idx);
+    return launch_status();
+  }
+  if (dtype == RB_BF16) {
+    raw_scores_float_kernel<__nv_bfloat16><<<grid, 256, align_up(static_cast<size_t>(D) * 2, 16), s>>>(
+        static_cast<const __nv_bfloat16*>(embeddings), N, D, unit, static_cast<const __nv_bfloat16*>(queries), pos,
+        counts, width, invalid_index_value, __ushort_as_bfloat16(0xff7fu), static_cast<__nv_bfloat16*>(out_raw),
+        out_idx);
+    return launch_status();
+  }
   const size_t qsm = align_up(static_cast<size_t>(D), 16);
+  const int8_t* codes = static_cast<const int8_t*>(embeddings);
+  const int8_t* qcodes = static_cast<const int8_t*>(queries);
   const __half* scale = reinterpret_cast<const __half*>(per_embedding_scale);
   if (divisor_for_int8 == -1 && scale == nullptr)
-    raw_scores_kernel<false><<<grid, 256, qsm, s>>>(embeddings, N, D, queries, pos, counts, width, divisor_for_int8,
+    raw_scores_kernel<false><<<grid, 256, qsm, s>>>(codes, N, D, qcodes, pos, counts, width, divisor_for_int8,
                                                     nullptr, invalid_index_value, out_raw, out_idx);
   else
-    raw_scores_kernel<true><<<grid, 256, qsm, s>>>(embeddings, N, D, queries, pos, counts, width, divisor_for_int8,
+    raw_scores_kernel<true><<<grid, 256, qsm, s>>>(codes, N, D, qcodes, pos, counts, width, divisor_for_int8,
                                                    scale, invalid_index_value, out_raw, out_idx);
   return launch_status();
 }
@@ -1136,21 +1261,23 @@ static int fused_kmean_ann_impl(const int64_t* cluster_offsets, int64_t n_lists,
 extern "C" {
 
 int rb_st_fused_kmean_ann(const int64_t* cluster_offsets, int64_t n_lists, const int64_t* cluster_ids,
-                          const int64_t* cluster_length, int P, const int8_t* embeddings, int64_t N,
-                          const int8_t* queries, int B, int D, int max_tensor_size_per_row,
+                          const int64_t* cluster_length, int P, const void* embeddings, int64_t N,
+                          const void* queries, int dtype, int B, int D, int max_tensor_size_per_row,
                           const int64_t* filtering_bit_mask, int64_t mask_rows, int64_t mask_words,
                           const int64_t* filtering_bit_index, const uint16_t* per_embedding_scale,
                           int invalid_index_value, int divisor_for_int8, void* out_raw, int32_t* out_idx,
                           void* workspace, size_t workspace_bytes, void* stream) {
-  return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, B, D,
-                              max_tensor_size_per_row, filtering_bit_mask, mask_rows, mask_words, filtering_bit_index,
+  return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, dtype,
+                              B, D, max_tensor_size_per_row, filtering_bit_mask, mask_rows, mask_words,
+                              filtering_bit_index,
                               PartialMask{nullptr, nullptr, nullptr, 0, 0}, per_embedding_scale, invalid_index_value,
                               divisor_for_int8, out_raw, out_idx, workspace, workspace_bytes, stream);
 }
 
 int rb_st_fused_kmean_ann_with_partial_masks(const int64_t* cluster_offsets, int64_t n_lists,
                                              const int64_t* cluster_ids, const int64_t* cluster_length, int P,
-                                             const int8_t* embeddings, int64_t N, const int8_t* queries, int B, int D,
+                                             const void* embeddings, int64_t N, const void* queries, int dtype,
+                                             int B, int D,
                                              int max_tensor_size_per_row, const int32_t* column_counts_cumsum,
                                              const int8_t* first_item_offset_in_column,
                                              const int64_t* column_results, int64_t n_column_results,
@@ -1170,8 +1297,8 @@ int rb_st_fused_kmean_ann_with_partial_masks(const int64_t* cluster_offsets, int
   const PartialMask pm{column_counts_cumsum, first_item_offset_in_column,
                        reinterpret_cast<const uint64_t*>(column_results), n_column_results, P, filtering_bit_index,
                        mask_rows};
-  return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, B, D,
-                              max_tensor_size_per_row, nullptr, 0, 0, nullptr, pm, per_embedding_scale,
+  return fused_kmean_ann_impl(cluster_offsets, n_lists, cluster_ids, cluster_length, P, embeddings, N, queries, dtype,
+                              B, D, max_tensor_size_per_row, nullptr, 0, 0, nullptr, pm, per_embedding_scale,
                               invalid_index_value, divisor_for_int8, out_raw, out_idx, workspace, workspace_bytes,
                               stream);
 }

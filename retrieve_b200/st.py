@@ -376,7 +376,8 @@ def fused_kmean_ann(cluster_offsets: Tensor, cluster_ids: Tensor, cluster_length
     was scored. ``filtering_bit_index`` [B] makes row ``b`` read mask row
     ``filtering_bit_index[b]``; ``per_embedding_scale`` (fp16 [N], a per-doc divisor in the
     divisor's place) gives fp16 ``fp16(fp32(fp16(dot)) / fp32(scale))``, the CUDA scorer's order.
-    Float embeddings are the reference's and not served here."""
+    Float embeddings (fp32 / fp16 / bf16, queries of the same dtype) give raw scores of their
+    own type by the CUDA scorer's fused multiply-add chains."""
     return _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
                   filtering_bit_mask, None, invalid_index_value, divisor_for_int8, filtering_bit_index,
                   per_embedding_scale, "st::fused_kmean_ann")
@@ -456,8 +457,11 @@ def fused_kmean_ann_with_partial_masks_multiple(
 def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, max_tensor_size_per_row,
            filtering_bit_mask, partial, invalid_index_value, divisor_for_int8, filtering_bit_index,
            per_embedding_scale, what):
-    if embeddings.dtype != torch.int8 or queries.dtype != torch.int8:
-        raise NotImplementedError(f"{what}: only int8 embeddings and queries are served here")
+    codes = {torch.int8: _lib.RB_I8, torch.float32: _lib.RB_F32, torch.float16: _lib.RB_F16,
+             torch.bfloat16: _lib.RB_BF16}
+    _check(embeddings.dtype in codes, f"{what}: unsupported scalar type {embeddings.dtype}")
+    _check(queries.dtype == embeddings.dtype, f"{what}: queries must have the embeddings' dtype")
+    is_int8 = embeddings.dtype == torch.int8
     for name, t in (("cluster_offsets", cluster_offsets), ("cluster_ids", cluster_ids),
                     ("cluster_length", cluster_length), ("embeddings", embeddings), ("queries", queries)):
         _check(t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
@@ -487,7 +491,8 @@ def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, ma
                "filtering_bit_index must be a 1-D CUDA tensor of one mask row per query row")
         rows_index = filtering_bit_index.to(torch.int64).contiguous()
     half = divisor_for_int8 != -1 or scale is not None
-    raw = torch.empty((b, width), dtype=torch.float16 if half else torch.int32, device=dev)
+    raw_dtype = (torch.float16 if half else torch.int32) if is_int8 else embeddings.dtype
+    raw = torch.empty((b, width), dtype=raw_dtype, device=dev)
     idx = torch.empty((b, width), dtype=torch.int32, device=dev)
     mask = None
     if filtering_bit_mask is not None:
@@ -516,7 +521,7 @@ def _fused(cluster_offsets, cluster_ids, cluster_length, embeddings, queries, ma
     _call(lib.rb_st_fused_kmean_ann_workspace_size(b, p, int(max_tensor_size_per_row), ctypes.byref(nbytes)), what)
     ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=dev)
     common = (_ptr(offs), offs.numel() - 1 if offs.numel() else 0, _ptr(cids), _ptr(clen), p, _ptr(embeddings),
-              embeddings.shape[0], _ptr(queries), b, d, int(max_tensor_size_per_row))
+              embeddings.shape[0], _ptr(queries), codes[embeddings.dtype], b, d, int(max_tensor_size_per_row))
     tail = (_ptr(scale), int(invalid_index_value), int(divisor_for_int8), _ptr(raw), _ptr(idx), _ptr(ws), ws.numel(),
             _stream(dev))
     if partial is None:
@@ -535,6 +540,8 @@ def _fake_fused_kmean_ann(cluster_offsets, cluster_ids, cluster_length, embeddin
     width = (int(max_tensor_size_per_row) + 31) // 32 * 32
     b = queries.shape[0]
     dt = torch.int32 if divisor_for_int8 == -1 and per_embedding_scale is None else torch.float16
+    if embeddings.dtype != torch.int8:
+        dt = embeddings.dtype
     return queries.new_empty((b, width), dtype=dt), queries.new_empty((b, width), dtype=torch.int32)
 
 
@@ -557,6 +564,8 @@ def _fake_fused_partial_multiple(queries, list_cluster_offsets, list_selected_cl
     scales = args[6] if len(args) >= 7 else kwargs.get("list_per_embedding_scale")
     b = queries.shape[0]
     dt = torch.int32 if divisor_for_int8 == -1 and scales is None else torch.float16
+    if list_embeddings and list_embeddings[0].dtype != torch.int8:
+        dt = list_embeddings[0].dtype
     widths = [(int(m) + 31) // 32 * 32 for m in list_max_tensor_size_per_row]
     return ([queries.new_empty((b, w), dtype=dt) for w in widths],
             [queries.new_empty((b, w), dtype=torch.int32) for w in widths])

@@ -1,7 +1,7 @@
 """Regenerates ``tests/golden/golden_fused.npz``: the REFERENCE's CPU scorer
 ``st.fused_kmean_ann`` (silvertorch/ops/csrc/fused_kmean_ann.cpp:86-228) with its two
 options the adapter's official path leaves unset, ``per_embedding_scale`` (a per-doc fp16
-divisor) and ``filtering_bit_index`` (query row -> mask row):
+divisor) and ``filtering_bit_index`` (query row -> mask row), and on float embeddings:
 
     python oracle/build_ref.py <reference checkout>
     python tests/golden/make_golden_fused.py
@@ -64,6 +64,21 @@ def main() -> None:
     for name, kw in cases.items():
         raw, idx = st.fused_kmean_ann(*args, **kw)
         out[f"{name}_raw"] = raw.numpy()
+        out[f"{name}_idx"] = idx.numpy()
+    # float embeddings with entries in {-1, 0, 1}: every partial dot is a small integer, exact in
+    # fp32 and fp16, so the CPU scorer's fp64 dot and the CUDA scorer's rounded chains agree. (bf16:
+    # the CPU scorer fails to fill its output with -FLT_MAX, which bf16 cannot hold —
+    # fused_kmean_ann.cpp:151-156, "value cannot be converted to type c10::BFloat16 without
+    # overflow"; the CUDA scorer fills with the lowest finite bf16, 0xff7f.)
+    tern_x = torch.randint(-1, 2, (n, d), generator=g)
+    tern_q = torch.randint(-1, 2, (b, d), generator=g)
+    out["tern_x"], out["tern_q"] = tern_x.to(torch.int8).numpy(), tern_q.to(torch.int8).numpy()
+    for name, dt in (("f32", torch.float32), ("f16", torch.float16)):
+        raw, idx = st.fused_kmean_ann(offsets, probe, lengths, tern_x.to(dt), tern_q.to(dt), width,
+                                      filtering_bit_mask=pack_low_first(mask), filtering_bit_index=mask_index,
+                                      invalid_index_value=-2)
+        assert raw.dtype == dt
+        out[f"{name}_raw"] = raw.float().numpy()
         out[f"{name}_idx"] = idx.numpy()
     np.savez_compressed(HERE / "golden_fused.npz", **out)
     print("wrote", HERE / "golden_fused.npz", {k: v.shape for k, v in out.items()})

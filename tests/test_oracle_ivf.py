@@ -135,6 +135,40 @@ def test_fused_kmean_ann_scale_and_mask_rows_match_reference(name):
         assert (idx[r][~got] == kw.get("invalid_index_value", -1)).all()
 
 
+@pytest.mark.parametrize("name,fmt", [("f32", "fp32"), ("f16", "fp16")])
+def test_fused_kmean_ann_float_rows_match_reference(name, fmt):
+    """Float embeddings (entries in {-1, 0, 1}, every partial dot exact) against the reference's
+    CPU scorer: the same (position, raw) multiset per row, its pads (-FLT_MAX, -65504) and the
+    mask-row index."""
+    words = ivf.pack_mask_high_first(FUSED["mask"])
+    raw, idx = ivf.fused_kmean_ann(FUSED["tern_q"].astype(np.float32), FUSED["offsets"], FUSED["probe"],
+                                   FUSED["lengths"], FUSED["tern_x"].astype(np.float32), int(FUSED["width"]),
+                                   filtering_bit_mask=words, filtering_bit_index=FUSED["mask_index"],
+                                   invalid_index_value=-2, float_format=fmt)
+    want_r, want_i = FUSED[f"{name}_raw"], FUSED[f"{name}_idx"]
+    for r in range(raw.shape[0]):
+        got, want = idx[r] >= 0, want_i[r] >= 0
+        assert sorted(zip(idx[r][got].tolist(), raw[r][got].astype(np.float32).tolist())) == sorted(
+            zip(want_i[r][want].tolist(), want_r[r][want].tolist()))
+        assert (raw[r][~got].astype(np.float32) == want_r[r][~want]).all() and (idx[r][~got] == -2).all()
+
+
+def test_float_chains_round_every_step():
+    """The CUDA scorer's fp16 chain rounds after every fused multiply-add and keeps even and odd
+    elements apart (simple_index_mm.cuh:96-115): 2048 + 1 + 1 ... stays at 2048 in one lane,
+    while the odd lane counts up exactly; fp32 carries both."""
+    from oracle import fdot
+
+    x = np.zeros(16)
+    x[0::2] = [2048, 1, 1, 1, 1, 1, 1, 1]
+    x[1::2] = 1
+    q = np.ones(16)
+    assert fdot.dot(x, q, "fp16") == 2048 + 8  # even lane stuck at 2048, odd lane 8
+    assert fdot.dot(x, q, "fp32") == 2048 + 7 + 8
+    assert fdot.unit(96, "fp32") == 96 and fdot.unit(256, "fp32") == 64 and fdot.unit(192, "fp16") == 192
+    assert fdot.unit(72, "fp32") == 0 and fdot.unit(20, "fp16") == 0
+
+
 def test_scaled_division_rounds_the_dot_to_fp16_first():
     """The CUDA scorer divides Half(dot) by the Half scale (index_mm_helpers.cuh:49-53); above
     2048 an integer dot is not exact in fp16, so its result differs from the CPU scorer's

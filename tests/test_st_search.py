@@ -100,8 +100,10 @@ def test_fused_kmean_ann_fake_and_argument_errors():
                                     per_embedding_scale=torch.empty(100, dtype=torch.float16))
         assert raw.dtype == torch.float16  # a per-doc divisor makes the raw scores fp16
     off, ids, lens = torch.tensor([0, 4]), torch.zeros(2, 1, dtype=torch.int64), torch.full((2, 1), 4)
-    with pytest.raises(NotImplementedError, match="int8"):
-        rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64), torch.zeros(2, 64), 4)
+    with pytest.raises(RuntimeError, match="dtype"):
+        rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64), torch.zeros(2, 64, dtype=torch.float16), 4)
+    with pytest.raises(RuntimeError, match="scalar type"):
+        rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64, dtype=torch.float64), torch.zeros(2, 64), 4)
     with pytest.raises(RuntimeError, match="CUDA"):
         rst.fused_kmean_ann(off, ids, lens, torch.zeros(4, 64, dtype=torch.int8), torch.zeros(2, 64, dtype=torch.int8),
                             4)
@@ -116,9 +118,15 @@ def test_fused_kmean_ann_capi_checks_need_no_device():
 
     fake = ctypes.c_void_p(16)  # never dereferenced: the checks fail first
 
-    def call(b=4, d=64, p=8, width=90, div=-1, ws=None, ws_bytes=0, mask=None, mask_rows=4, index=None):
-        return lib.rb_st_fused_kmean_ann(None, 8, None, None, p, None, 100, None, b, d, width, mask, mask_rows, 2,
-                                         index, None, -1, div, None, None, ws, ws_bytes, None)
+    def call(b=4, d=64, p=8, width=90, div=-1, ws=None, ws_bytes=0, mask=None, mask_rows=4, index=None,
+             dtype=_lib.RB_I8):
+        return lib.rb_st_fused_kmean_ann(None, 8, None, None, p, None, 100, None, dtype, b, d, width, mask, mask_rows,
+                                         2, index, None, -1, div, None, None, ws, ws_bytes, None)
+
+    assert call(dtype=_lib.RB_E4M3) == _lib.RB_ERR_TYPE
+    assert call(dtype=_lib.RB_F32, d=72) == _lib.RB_ERR_UNSUPPORTED  # 288 bytes: neither 256 nor 384 divides
+    assert call(dtype=_lib.RB_F16, d=20) == _lib.RB_ERR_UNSUPPORTED  # not a multiple of 16 bytes
+    assert call(dtype=_lib.RB_F32, d=96) == _lib.RB_ERR_WORKSPACE  # one 384-byte chain
 
     assert call(mask=fake, mask_rows=3) == _lib.RB_ERR_INVALID_ARG  # fewer mask rows than query rows
     assert call(mask=fake, mask_rows=3, index=fake) == _lib.RB_ERR_WORKSPACE  # rows picked by filtering_bit_index
@@ -746,3 +754,39 @@ def test_search_replays_in_a_cuda_graph(grouped):
         torch.cuda.synchronize()
         assert torch.equal(ids_g, ids) and torch.equal(scores_g, scores)
     del graph
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,fmt", [(torch.float32, "fp32"), (torch.float16, "fp16"), (torch.bfloat16, "bf16")])
+@pytest.mark.parametrize("d", [64, 96, 192, 256])
+def test_fused_kmean_ann_float_embeddings(dtype, fmt, d):
+    """Float embeddings: the CUDA scorer's fused multiply-add chains (one block, 256-byte and
+    384-byte blocks, fp16 / bf16 in even / odd lanes), bit for bit the restatement's exact-rounding
+    emulation, slot order, pads and mask included."""
+    from oracle import fdot
+
+    st = _st()
+    if fdot.unit(d, fmt) == 0:
+        pytest.skip("no chain for this D (the reference has no kernel for it either)")
+    rng = np.random.default_rng(d)
+    sizes = rng.integers(0, 70, 9)
+    offsets = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    n, b, p = int(offsets[-1]), 3, 3
+    x = fdot.to_format(rng.standard_normal((n, d)), fmt)
+    q = fdot.to_format(rng.standard_normal((b, d)), fmt)
+    probe = np.argsort(rng.random((b, 9)), axis=1)[:, :p].astype(np.int64)
+    lengths = sizes[probe].astype(np.int64)
+    width = int(lengths.sum(1).max())
+    mask = rng.random((b, n)) < 0.7
+    words = ivf.pack_mask_high_first(mask)
+    dev = [torch.from_numpy(np.ascontiguousarray(v)).cuda() for v in (offsets, probe, lengths)]
+    xt = torch.from_numpy(x).to(dtype).cuda()
+    qt = torch.from_numpy(q).to(dtype).cuda()
+    raw, idx = st.fused_kmean_ann(*dev, xt, qt, width, filtering_bit_mask=torch.from_numpy(words).cuda(),
+                                  invalid_index_value=-4)
+    want_r, want_i = ivf.fused_kmean_ann(q, offsets, probe, lengths, x, width, filtering_bit_mask=words,
+                                         invalid_index_value=-4, float_format=fmt)
+    assert raw.dtype == dtype
+    assert np.array_equal(idx.cpu().numpy(), want_i)
+    got = raw.float().cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want_r.astype(np.float32).view(np.uint32))
