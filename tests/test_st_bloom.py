@@ -214,11 +214,11 @@ def test_capi_checks_need_no_device():
     assert lib.rb_st_bloom_partial_search(fake, 100, fake, 3, fake, 80, 10, 3, None, 4, 2, fake, fake, 5, 7, None,
                                           0, None) == _lib.RB_OK  # no words asked
     assert lib.rb_st_fused_kmean_ann_with_partial_masks(
-        None, 8, None, None, 2, None, 100, None, 4, 64, 90, None, None, None, 0, 4, None, None, -1, -1, None, None,
-        None, 0, None) == _lib.RB_ERR_INVALID_ARG  # ranges without their cumsum
+        None, 8, None, None, 2, None, 100, None, _lib.RB_I8, 4, 64, 90, None, None, None, 0, 4, None, None, -1, -1,
+        None, None, None, 0, None) == _lib.RB_ERR_INVALID_ARG  # ranges without their cumsum
     assert lib.rb_st_fused_kmean_ann_with_partial_masks(
-        None, 8, None, None, 2, None, 100, None, 4, 64, 90, fake, fake, None, 0, 3, None, None, -1, -1, None, None,
-        None, 0, None) == _lib.RB_ERR_INVALID_ARG  # 3 mask rows for 4 query rows, no filtering_bit_index
+        None, 8, None, None, 2, None, 100, None, _lib.RB_I8, 4, 64, 90, fake, fake, None, 0, 3, None, None, -1, -1,
+        None, None, None, 0, None) == _lib.RB_ERR_INVALID_ARG  # 3 mask rows for 4 query rows, no filtering_bit_index
 
 
 # --- GPU -----------------------------------------------------------------------------------
