@@ -343,3 +343,63 @@ def test_multiple_variants_equal_their_single_ops():
         raw, idx = st.fused_kmean_ann_with_partial_masks(coff, ids[c], [len_a, len_b][c], codes, q, widths[c], cs[c],
                                                          fi[c], ws[c], -1, 16)
         assert torch.equal(raws[c], raw) and torch.equal(idxs[c], idx)
+
+
+# The reference's known answers for its bloom path (retrieve/tests/parity/test_official.py:229-245,
+# 355-373, 414-430, 515-522): a 4-doc corpus with 2 features (language; category), its index at
+# b_multiplier 5.0 and 3 positions a value, three expressions parsed with 7 stored hashes a term.
+README_CORPUS = np.array([
+    [[100, -1], [200, 201]],  # doc 0: en; music, pop
+    [[100, 101], [200, -1]],  # doc 1: en, es; music
+    [[102, -1], [202, -1]],  # doc 2: ja; news
+    [[100, -1], [200, 203]],  # doc 3: en; music, rock
+])
+README_QUERIES = ["0:100", "0:100 AND NOT 1:201", "0:102 OR 1:203"]
+README_HITS = [[0, 1, 3], [1, 3], [2, 3]]
+
+
+def _readme_plans():
+    _st()
+    _, (data, offsets) = torch.ops.st.parse_expression_query_batch(
+        README_QUERIES + [""], torch.ones(4, dtype=torch.int64), 7, True, 5)
+    return data.numpy(), offsets.numpy()
+
+
+def test_readme_known_answers_on_the_restatement():
+    """The library's parser and the restated bloom build and search give the reference's hits,
+    the match-all empty expression, and its partial response over two 2-doc ranges."""
+    fid, foff, fval = ivf.attrs_to_features(README_CORPUS)
+    index, boff = ivf.bloom_index_build(fid, foff, fval, 5.0, 3)
+    assert len(boff) == 2  # one 2048-doc bundle
+    data, offsets = _readme_plans()
+    for p, hits in enumerate(README_HITS + [[0, 1, 2, 3]]):
+        mask = ivf.bloom_plan_mask(index, boff, data, offsets, p, 3, 7, 4)
+        assert np.nonzero(mask)[0].tolist() == hits
+    sel_off, sel_len = np.array([[0, 2]] * 3), np.array([[2, 2]] * 3)
+    cumsum, first, words = ivf.bloom_partial_response(index, boff, data, offsets[:24], sel_off, sel_len, 3, 7)
+    assert cumsum.tolist() == [1, 2, 3, 4, 5, 6] and first.tolist() == [0, 2] * 3
+    for r, hits in enumerate(README_HITS):
+        kept = [2 * j + i for j in range(2) for i in range(2)
+                if ivf.partial_mask_keep(cumsum, first, words, r * 2 + j, np.array([i]))[0]]
+        assert sorted(kept) == hits
+
+
+@pytest.mark.gpu
+def test_readme_known_answers_on_the_device():
+    st = _st()
+    fid, foff, fval = (torch.from_numpy(np.ascontiguousarray(a)).cuda()
+                       for a in ivf.attrs_to_features(README_CORPUS))
+    index, boff = st.bloom_index_build(fid, foff, fval, 5.0, 3)
+    data, offsets = (torch.from_numpy(a) for a in _readme_plans())
+    full = st.bloom_index_search_batch(index, boff, data, offsets, 3, 7, True)
+    assert full.dtype == torch.bool and full.shape == (4, 2048)
+    for row, hits in zip(full[:, :4].cpu().tolist(), README_HITS + [[0, 1, 2, 3]]):
+        assert [i for i, h in enumerate(row) if h] == hits
+    packed = st.bloom_index_search_batch(index, boff, data, offsets, 3, 7, False)
+    assert packed.shape == (4, 32)
+    assert np.array_equal(packed.cpu().numpy(), ivf.pack_mask_high_first(full.cpu().numpy()))
+    sel_off = torch.tensor([[0, 2]] * 3).cuda()
+    sel_len = torch.tensor([[2, 2]] * 3).cuda()
+    cumsum, first, words = st.bloom_index_search_batch_return_partial_response(
+        index, boff, data, offsets[:24], sel_off, sel_len, 3, 7)
+    assert cumsum.tolist() == [1, 2, 3, 4, 5, 6] and first.tolist() == [0, 2] * 3
