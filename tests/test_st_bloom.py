@@ -403,3 +403,73 @@ def test_readme_known_answers_on_the_device():
     cumsum, first, words = st.bloom_index_search_batch_return_partial_response(
         index, boff, data, offsets[:24], sel_off, sel_len, 3, 7)
     assert cumsum.tolist() == [1, 2, 3, 4, 5, 6] and first.tolist() == [0, 2] * 3
+
+
+def _expressions(query_attrs, reverse):
+    """The adapter's AND-only expressions (retrieve/src/retrieve/ops/official/adapter.py:127-157):
+    one ``c:v`` term per active clause, ``NOT`` on reversed clauses, "" when none is active."""
+    out = []
+    for row in np.asarray(query_attrs).tolist():
+        terms = [("NOT " if reverse[c] else "") + f"{c}:{v}" for c, v in enumerate(row) if v != -1]
+        out.append(" AND ".join(terms))
+    return out
+
+
+def _bloom_corpus(seed=7, n=6000, c=2, a_max=3, vocab=50):
+    rng = np.random.default_rng(seed)
+    attrs = rng.integers(0, vocab, (n, c, a_max))
+    attrs[rng.random((n, c, a_max)) < 0.4] = -1
+    return attrs
+
+
+def test_bloom_keeps_every_exact_match_and_not_flips_the_guarantee():
+    """The reference's T4 properties (test_official.py:455-508) on the restatement with the
+    library's parser: an AND of terms never loses a doc the exact predicate accepts and lets
+    through under 5 % of the rest at b_multiplier 10; a single NOT term never admits a doc that
+    holds the value."""
+    from oracle import filters
+
+    attrs = _bloom_corpus()
+    n, c, _ = attrs.shape
+    fid, foff, fval = ivf.attrs_to_features(attrs)
+    index, boff = ivf.bloom_index_build(fid, foff, fval, 10.0, K)
+    rng = np.random.default_rng(42)
+    qa = rng.integers(0, 50, (16, c))
+    _st()
+    for reverse in ([False, False], [True, False]):
+        q = qa.copy()
+        if reverse[0]:
+            q[:, 1] = -1
+        exprs = _expressions(q, reverse)
+        _, (data, offsets) = torch.ops.st.parse_expression_query_batch(exprs, torch.ones(len(exprs)), HASH_K, True, 5)
+        bloom = np.stack([ivf.bloom_plan_mask(index, boff, data.numpy(), offsets.numpy(), p, K, HASH_K, n)
+                          for p in range(len(exprs))])
+        exact = filters.clause_mask(attrs, np.array(reverse), q)
+        if not reverse[0]:
+            assert not (exact & ~bloom).any(), "the bloom lost an exact match"
+            assert (bloom & ~exact).sum() / max((~exact).sum(), 1) < 0.05
+        else:
+            assert not (bloom & ~exact).any(), "a bloom NOT admitted a doc holding the value"
+
+
+@pytest.mark.gpu
+def test_bloom_properties_on_the_device():
+    """The same on the device build and search, which equal the restatement's masks."""
+    from oracle import filters
+
+    st = _st()
+    attrs = _bloom_corpus(seed=9)
+    n, c, _ = attrs.shape
+    fid, foff, fval = ivf.attrs_to_features(attrs)
+    index, boff = st.bloom_index_build(*(torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (fid, foff, fval)),
+                                       10.0, K)
+    rng = np.random.default_rng(43)
+    qa = rng.integers(0, 50, (16, c))
+    exprs = _expressions(qa, [False, False])
+    _, (data, offsets) = torch.ops.st.parse_expression_query_batch(exprs, torch.ones(len(exprs)), HASH_K, True, 5)
+    full = st.bloom_index_search_batch(index, boff, data, offsets, K, HASH_K, True)[:, :n].cpu().numpy()
+    exact = filters.clause_mask(attrs, np.zeros(c, dtype=bool), qa)
+    assert not (exact & ~full).any()
+    assert (full & ~exact).sum() / max((~exact).sum(), 1) < 0.05
+    want_index, want_boff = ivf.bloom_index_build(fid, foff, fval, 10.0, K)
+    assert np.array_equal(index.cpu().numpy(), want_index) and np.array_equal(boff.cpu().numpy(), want_boff)
