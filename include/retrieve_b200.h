@@ -568,6 +568,17 @@ RB_API int rb_st_bloom_partial_search(const int64_t* bloom_index, int64_t index_
                                       void* stream);
 
 /*
+ * st::is_topk(Tensor scores, Tensor ks, Tensor(a!) is_topk_output, bool largest=True)
+ * (silvertorch/ops/csrc/is_topk.cpp:84-90; CUDA is_topk_cuda.cu:83-149): for each row b of
+ * scores [B, n] (dtype RB_F32, RB_F16 or RB_BF16) the value kth at position
+ * clamp(ks[b] - 1, 0, n - 1) of the row sorted descending (ascending when largest is 0; NaN
+ * sorts as the largest value), then out[b, j] = scores[b, j] >= kth (<= when smallest),
+ * compared in fp32, as 1 / 0 in the scores' dtype. ks: int64 [B] on the device. n < 2^32.
+ */
+RB_API int rb_st_is_topk(const void* scores, int dtype, int64_t B, int64_t n, const int64_t* ks, int largest,
+                         void* out, void* stream);
+
+/*
  * The centroid update of the IVF build's k-means, replacing KMeans._cluster_sums
  * (retrieve/src/retrieve/indexing/kmeans.py:98-119, an fp64 one-hot GEMM per row chunk):
  * out_sums [n_lists, D] fp64 = per cluster the sum of its rows of embs [N, D] (dtype RB_F32,

@@ -71,3 +71,22 @@ def merge_topk(parts_ids: list[np.ndarray], parts_scores: list[np.ndarray], k: i
     sc = np.concatenate(parts_scores, axis=1).astype(np.float32)
     valid = ids >= 0
     return topk_strict(sc, k, ids=np.where(valid, ids, np.iinfo(np.int64).max), valid=valid, sentinel=True)
+
+
+def is_topk(scores, ks, largest=True):
+    """``st::is_topk`` as SilverTorch's CUDA op computes it (silvertorch/ops/csrc/is_topk_cuda.cu
+    :63-72, 83-149): per row the value at position ``clamp(k - 1, 0, n - 1)`` of the row sorted
+    descending (ascending when not ``largest``), NaN sorting as the largest value, then every
+    score ``>=`` (``<=``) it, compared in fp32, flagged 1. Returns float32 0 / 1 flags."""
+    s = np.asarray(scores, dtype=np.float32)
+    b, n = s.shape
+    out = np.zeros((b, n), dtype=np.float32)
+    if n == 0:
+        return out
+    for r in range(b):
+        asc = np.sort(s[r])  # NaN last: the largest
+        kk = min(max(int(ks[r]) - 1, 0), n - 1)
+        kth = asc[::-1][kk] if largest else asc[kk]
+        with np.errstate(invalid="ignore"):
+            out[r] = (s[r] >= kth) if largest else (s[r] <= kth)
+    return out

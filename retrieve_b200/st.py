@@ -30,7 +30,7 @@ import ctypes
 import torch
 from torch import Tensor
 
-from retrieve_b200 import _lib, st_bloom
+from retrieve_b200 import _lib, st_bloom, st_select
 from retrieve_b200._st_common import _call, _check, _ptr, _stream
 
 SEARCH_SCHEMA = (
@@ -623,7 +623,7 @@ def _register() -> None:
                                       fused_kmean_ann_with_partial_masks, _fake_fused_partial),
                                      ("fused_kmean_ann_with_partial_masks_multiple", FUSED_PARTIAL_MULTIPLE_SCHEMA,
                                       fused_kmean_ann_with_partial_masks_multiple, _fake_fused_partial_multiple),
-                                     *st_bloom.OPS):
+                                     *st_bloom.OPS, *st_select.OPS):
         ours = not _defined(name)
         if ours:
             _LIBRARY.define(schema)
