@@ -579,6 +579,29 @@ RB_API int rb_st_is_topk(const void* scores, int dtype, int64_t B, int64_t n, co
                          void* out, void* stream);
 
 /*
+ * st::take_top_k_and_gather_from_main_and_fresh (silvertorch/ops/csrc/
+ * fresh_index_post_processing.cpp:226-286), in two calls:
+ *
+ * rb_st_fresh_topk: per row b the top k' = min(k, mf + mm) of the fresh scores [B, mf] followed
+ * by the main scores [B, mm] (dtype RB_F32 / RB_F16 / RB_BF16), largest first with NaN the
+ * largest and ties to the lower merged column: out_scores [B, k'] (the scores' dtype), out_idx
+ * [B, k'] int64 merged columns (fresh j -> j, main j -> mf + j), out_is_fresh [B, k'] bool.
+ * mf + mm <= 4096.
+ *
+ * rb_st_fresh_gather: for the [B, k_out] merged columns top_idx, the data row of each winner
+ * copied to out [B * k_out, row_elems] (elem_bytes 1, 2, 4 or 8 a value): fresh_data
+ * [fresh_rows, row_elems] at fresh_indices[b, col] for col < mf, main_data at
+ * main_indices[b, col - mf] otherwise (indices int32 or int64, [B, mf] and [B, mm]); an index
+ * outside its table reads row 0.
+ */
+RB_API int rb_st_fresh_topk(const void* fresh_scores, int64_t mf, const void* main_scores, int64_t mm, int dtype,
+                            int64_t B, int k, void* out_scores, int64_t* out_idx, bool* out_is_fresh, void* stream);
+RB_API int rb_st_fresh_gather(const int64_t* top_idx, int64_t B, int k_out, int64_t mf, int64_t mm,
+                              const void* fresh_indices, const void* main_indices, int indices_are_int64,
+                              const void* fresh_data, int64_t fresh_rows, const void* main_data, int64_t main_rows,
+                              int64_t row_elems, int elem_bytes, void* out, void* stream);
+
+/*
  * The centroid update of the IVF build's k-means, replacing KMeans._cluster_sums
  * (retrieve/src/retrieve/indexing/kmeans.py:98-119, an fp64 one-hot GEMM per row chunk):
  * out_sums [n_lists, D] fp64 = per cluster the sum of its rows of embs [N, D] (dtype RB_F32,

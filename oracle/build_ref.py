@@ -4,7 +4,7 @@ golden fixtures in the build container:
 
     python oracle/build_ref.py <reference checkout>
 
-The six C++ sources are compiled where they lie (read-only) with torch's
+The C++ sources are compiled where they lie (read-only) with torch's
 ``cpp_extension`` (they need the ATen headers torch ships); the library lands in
 ``oracle/_ref/`` (git-ignored) and registers ``torch.ops.st.*`` (CPU kernels:
 bloom_index_build, bloom_index_search_batch, parse_expression_query_batch,
@@ -25,6 +25,8 @@ SOURCES = [
     "expression_query_parser.cpp",
     "fused_kmean_ann.cpp",
     "fork_search.cpp",
+    "is_topk.cpp",
+    "fresh_index_post_processing.cpp",
 ]
 
 

@@ -90,3 +90,35 @@ def is_topk(scores, ks, largest=True):
         with np.errstate(invalid="ignore"):
             out[r] = (s[r] >= kth) if largest else (s[r] <= kth)
     return out
+
+
+def take_top_k_and_gather(main_scores, fresh_scores, main_indices, fresh_indices, k, main_data, fresh_data):
+    """``st::take_top_k_and_gather_from_main_and_fresh`` (silvertorch/ops/csrc/
+    fresh_index_post_processing.cpp:33-128, 226-272) for one data key: the top ``min(k, Mf + Mm)``
+    of ``[fresh | main]`` per row, largest first with NaN the largest and ties to the lower merged
+    column (the reference's ``torch.topk`` leaves them open), whether each comes from fresh, and
+    the winners' data rows (``fresh_data[fresh_indices[b, j]]`` / ``main_data[main_indices[b, j -
+    Mf]]``, row 0 for an index outside the table)."""
+    main_scores = np.asarray(main_scores, dtype=np.float64)
+    fresh_scores = np.asarray(fresh_scores, dtype=np.float64)
+    b, mm = main_scores.shape
+    mf = fresh_scores.shape[1]
+    merged = np.concatenate([fresh_scores, main_scores], axis=1)
+    kk = max(0, min(int(k), mf + mm))
+    cols = np.zeros((b, kk), dtype=np.int64)
+    for r in range(b):
+        nan = np.isnan(merged[r])
+        key = np.where(nan, np.inf, merged[r])
+        order = np.lexsort((np.arange(mf + mm), -key, ~nan))  # NaN first, then larger, then lower column
+        cols[r] = order[:kk]
+    top = np.take_along_axis(merged, cols, axis=1)
+    rows = []
+    for r in range(b):
+        for c in cols[r]:
+            if c < mf:
+                i, table = int(np.asarray(fresh_indices)[r, c]), np.asarray(fresh_data)
+            else:
+                i, table = int(np.asarray(main_indices)[r, c - mf]), np.asarray(main_data)
+            rows.append(table[i if 0 <= i < table.shape[0] else 0])
+    data = np.stack(rows) if rows else np.zeros((0,) + np.asarray(main_data).shape[1:], np.asarray(main_data).dtype)
+    return top, cols, cols < mf, data

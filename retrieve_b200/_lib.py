@@ -123,6 +123,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _vp,
          _c_i64, _vp],
     ),
+    "rb_st_fresh_topk": (_c_int, [_vp, _c_i64, _vp, _c_i64, _c_int, _c_i64, _c_int, _vp, _vp, _vp, _vp]),
+    "rb_st_fresh_gather": (
+        _c_int,
+        [_vp, _c_i64, _c_int, _c_i64, _c_i64, _vp, _vp, _c_int, _vp, _c_i64, _vp, _c_i64, _c_i64, _c_int, _vp, _vp],
+    ),
     "rb_st_is_topk": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _c_int, _vp, _vp]),
     "rb_kmeans_cluster_sums_workspace_size": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(_c_size)]),
     "rb_kmeans_cluster_sums": (
