@@ -585,7 +585,7 @@ RB_API int rb_st_is_topk(const void* scores, int dtype, int64_t B, int64_t n, co
  * rb_st_fresh_topk: per row b the top k' = min(k, mf + mm) of the fresh scores [B, mf] followed
  * by the main scores [B, mm] (dtype RB_F32 / RB_F16 / RB_BF16), largest first with NaN the
  * largest and ties to the lower merged column: out_scores [B, k'] (the scores' dtype), out_idx
- * [B, k'] int64 merged columns (fresh j -> j, main j -> mf + j), out_is_fresh [B, k'] bool.
+ * [B, k'] int64 merged columns (fresh j -> j, main j -> mf + j), out_is_fresh [B, k'] 0 / 1 bytes.
  * mf + mm <= 4096.
  *
  * rb_st_fresh_gather: for the [B, k_out] merged columns top_idx, the data row of each winner
@@ -595,7 +595,8 @@ RB_API int rb_st_is_topk(const void* scores, int dtype, int64_t B, int64_t n, co
  * outside its table reads row 0.
  */
 RB_API int rb_st_fresh_topk(const void* fresh_scores, int64_t mf, const void* main_scores, int64_t mm, int dtype,
-                            int64_t B, int k, void* out_scores, int64_t* out_idx, bool* out_is_fresh, void* stream);
+                            int64_t B, int k, void* out_scores, int64_t* out_idx, uint8_t* out_is_fresh,
+                            void* stream);
 RB_API int rb_st_fresh_gather(const int64_t* top_idx, int64_t B, int k_out, int64_t mf, int64_t mm,
                               const void* fresh_indices, const void* main_indices, int indices_are_int64,
                               const void* fresh_data, int64_t fresh_rows, const void* main_data, int64_t main_rows,

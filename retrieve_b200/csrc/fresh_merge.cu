@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(kThreads) fresh_topk_kernel(const void* __rest
                                                               const void* __restrict__ main_, int64_t mm, int dtype,
                                                               int kk, int m_pow2, void* __restrict__ out_scores,
                                                               int64_t* __restrict__ out_idx,
-                                                              bool* __restrict__ out_fresh) {
+                                                              uint8_t* __restrict__ out_fresh) {
   extern __shared__ __align__(16) uint64_t keys[];
   const int64_t b = blockIdx.x;
   const int64_t m = mf + mm;
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kThreads) fresh_topk_kernel(const void* __rest
     const int64_t col = static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(keys[j] & 0xffffffffu));
     const int64_t o = b * kk + j;
     out_idx[o] = col;
-    out_fresh[o] = col < mf;
+    out_fresh[o] = col < mf ? 1 : 0;
     if (col < mf)
       copy_score(fresh, b * mf + col, out_scores, o, dtype);
     else
@@ -135,7 +135,7 @@ using namespace rb;
 extern "C" {
 
 int rb_st_fresh_topk(const void* fresh_scores, int64_t mf, const void* main_scores, int64_t mm, int dtype,
-                     int64_t B, int k, void* out_scores, int64_t* out_idx, bool* out_is_fresh, void* stream) {
+                     int64_t B, int k, void* out_scores, int64_t* out_idx, uint8_t* out_is_fresh, void* stream) {
   if (B < 0 || mf < 0 || mm < 0 || k < 0 || B > INT32_MAX) {
     set_last_error("take_top_k_and_gather_from_main_and_fresh: bad sizes");
     return RB_ERR_INVALID_ARG;
