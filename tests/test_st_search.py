@@ -790,3 +790,43 @@ def test_fused_kmean_ann_float_embeddings(dtype, fmt, d):
     assert np.array_equal(idx.cpu().numpy(), want_i)
     got = raw.float().cpu().numpy()
     assert np.array_equal(got.view(np.uint32), want_r.astype(np.float32).view(np.uint32))
+
+
+@pytest.mark.skipif(not REF_CPU_LIB.exists(), reason="the reference's CPU st ops are not built here")
+def test_every_reference_st_op_is_served():
+    """Every op the reference's SilverTorch build registers under ``st::`` is defined by this
+    library alone with the same schema, and gets a CUDA kernel beside the reference's CPU build
+    (each in a child process: one registry per process)."""
+    import subprocess
+    import sys
+
+    listing = (
+        "import torch, json\n"
+        "{load}\n"
+        "ops = sorted(n for n in torch._C._dispatch_get_all_op_names() if n.startswith('st::'))\n"
+        "print(json.dumps({{n: str(getattr(torch.ops.st, n[4:].split('.')[0]).default._schema) for n in ops}}))\n"
+    )
+    root = Path(__file__).resolve().parent.parent
+
+    def run(load):
+        r = subprocess.run([sys.executable, "-c", listing.format(load=load)], cwd=root, capture_output=True, text=True,
+                           timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        import json
+
+        return json.loads(r.stdout.strip().splitlines()[-1])
+
+    ref = run(f"torch.ops.load_library({str(REF_CPU_LIB)!r})")
+    ours = run("import retrieve_b200.st")
+    assert set(ref) <= set(ours), sorted(set(ref) - set(ours))
+    assert all(ours[n] == ref[n] for n in ref)
+    code = (
+        "import torch\n"
+        f"torch.ops.load_library({str(REF_CPU_LIB)!r})\n"
+        "import retrieve_b200.st\n"
+        "has = torch._C._dispatch_has_kernel_for_dispatch_key\n"
+        "missing = [n for n in torch._C._dispatch_get_all_op_names() if n.startswith('st::') and not has(n, 'CUDA')]\n"
+        "assert not missing, missing\n"
+    )
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
