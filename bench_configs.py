@@ -247,7 +247,7 @@ def run_c3(args, dev):
            "mode": "bloom test + exact recheck (exact results)", "sweep": results},
           {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
            "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops_sustained)",
-           "note": "2*B*N*D dense-masked flops (the figure the config judges) at 10 % selectivity"},
+           "note": "2*B*N*D dense-masked flops (the figure the config is measured by) at 10 % selectivity"},
           clocks, "fp16")
 
 

@@ -47,5 +47,7 @@ def build(reference: str | Path):
 
 
 if __name__ == "__main__":
-    build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python oracle/build_ref.py <reference checkout>")
+    build(sys.argv[1])
     print("built into", OUT)
