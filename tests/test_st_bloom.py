@@ -473,3 +473,47 @@ def test_bloom_properties_on_the_device():
     assert (full & ~exact).sum() / max((~exact).sum(), 1) < 0.05
     want_index, want_boff = ivf.bloom_index_build(fid, foff, fval, 10.0, K)
     assert np.array_equal(index.cpu().numpy(), want_index) and np.array_equal(boff.cpu().numpy(), want_boff)
+
+
+@pytest.mark.gpu
+def test_prepared_ops_replay_in_a_cuda_graph():
+    """The prepared bloom searches and the raw scorers never wait on the host, so they capture into
+    a CUDA graph: replays after new inputs are copied in equal eager calls."""
+    st = _st()
+    index, boff = _dev(BLOOM["bloom_index"], BLOOM["bundle_b_offsets"])
+    n_plans = BLOOM["words"].shape[0]
+    blob = torch.from_numpy(ivf.plan_blob(BLOOM["plan_data"], BLOOM["plan_offsets"], n_plans)).cuda()
+    off, lens = _dev(*_selection())
+    rng = np.random.default_rng(4)
+    n, d = int(BLOOM["n"]), 64
+    codes = torch.from_numpy(rng.integers(-127, 128, (n, d), dtype=np.int8)).cuda()
+    q = torch.from_numpy(rng.integers(-127, 128, (off.shape[0], d), dtype=np.int8)).cuda()
+    coff = torch.from_numpy(BLOOM["cluster_offsets"]).cuda()
+    probe = torch.from_numpy(BLOOM["probe"]).cuda()
+    width = int(lens.sum(1).max())
+    cap = int(BLOOM["p_words"].size) + 64
+
+    def call():
+        words = st.bloom_index_search_batch_prepared(index, boff, blob, n_plans, int(BLOOM["max_stack"]), K, HASH_K)
+        cs, fi, pw = st.bloom_index_search_batch_return_partial_response_prepared(
+            index, boff, blob, n_plans, int(BLOOM["max_stack"]), off, lens, K, HASH_K, None, cap)
+        raw, idx = st.fused_kmean_ann_with_partial_masks(coff, probe, lens, codes, q, width, cs, fi, pw)
+        return words, pw, raw, idx
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            call()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        outs = call()
+    for seed in range(2):
+        q.copy_(torch.from_numpy(np.random.default_rng(seed).integers(-127, 128, tuple(q.shape), dtype=np.int8)))
+        graph.replay()
+        want = call()
+        torch.cuda.synchronize()
+        for a, b in zip(outs, want):
+            assert torch.equal(a, b)
+    del graph
