@@ -830,3 +830,53 @@ def test_every_reference_st_op_is_served():
     )
     r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
+
+
+def _pack_low_first(mask):
+    m = np.asarray(mask, dtype=bool)
+    b, n = m.shape
+    w = (n + 63) // 64
+    padded = np.zeros((b, w * 64), dtype=bool)
+    padded[:, :n] = m
+    return np.bitwise_or.reduce(padded.reshape(b, w, 64).astype(np.uint64) << np.arange(64, dtype=np.uint64),
+                                axis=2).view(np.int64)
+
+
+def _scored_docs(doc, packer, device):
+    """The reference's bit-order probe (test_official.py:376-410): one 70-doc cluster (docs 0-63
+    in the first mask word and on the warp-aligned path, 64-69 in the second and on the remainder
+    path) scored under a mask with exactly ``doc`` set, packed by ``packer``."""
+    n, d = 70, 16
+    rng = np.random.default_rng(11)
+    codes = rng.integers(-128, 128, (n, d), dtype=np.int8)
+    q = rng.integers(-128, 128, (1, d), dtype=np.int8)
+    mask = np.zeros((1, n), dtype=bool)
+    mask[0, doc] = True
+    words = packer(mask)
+    args = (np.array([0, n]), np.zeros((1, 1), dtype=np.int64), np.array([[n]]))
+    if device:
+        st = _st()
+        t = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (*args, codes, q)]
+        _, idx = st.fused_kmean_ann(*t, n, filtering_bit_mask=torch.from_numpy(words).cuda())
+        idx = idx.cpu().numpy()
+    else:
+        _, idx = ivf.fused_kmean_ann(q, args[0], args[1], args[2], codes, n, filtering_bit_mask=words)
+    return sorted(idx[idx >= 0].tolist())
+
+
+@pytest.mark.parametrize("doc", [0, 5, 40, 69])
+def test_scorer_reads_the_mask_high_bit_first(doc):
+    """The known answer of the reference's T3 test on the restatement: packed high bit first, the
+    one set doc and only it is scored; packed low bit first, its mirror in the word (or nothing
+    when the mirror lies past the cluster)."""
+    assert _scored_docs(doc, ivf.pack_mask_high_first, device=False) == [doc]
+    mirror = (doc // 64) * 64 + (63 - doc % 64)
+    assert _scored_docs(doc, _pack_low_first, device=False) == ([mirror] if mirror < 70 else [])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("doc", [0, 5, 40, 69])
+def test_device_scorer_reads_the_mask_high_bit_first(doc):
+    assert _scored_docs(doc, ivf.pack_mask_high_first, device=True) == [doc]
+    mirror = (doc // 64) * 64 + (63 - doc % 64)
+    assert _scored_docs(doc, _pack_low_first, device=True) == ([mirror] if mirror < 70 else [])
