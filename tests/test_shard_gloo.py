@@ -85,14 +85,16 @@ def _ivf_worker(rank, world, port, case, out):
     from oracle import ivf
     from retrieve_b200.shard import ShardedIVFSearch, ivf_shard_bounds
 
-    g, k, width = case
+    g, k, width, words = case
     _, _, lo, hi = ivf_shard_bounds(g["offsets"], world, rank)
 
     class OracleShards(ShardedIVFSearch):
         # the host logic of the exchange with the oracle in place of the kernels (CPU ranks)
         def local(self, query, probe_ids, k, width, divisor, filters):
+            mask = filters.get("filtering_bit_mask")
             raw, slot = ivf.search_shard(query.numpy(), probe_ids.numpy(), g["offsets"], g["sizes"],
-                                         self.codes.numpy(), self.pos_lo, k, width)
+                                         self.codes.numpy(), self.pos_lo, k, width,
+                                         filtering_bit_mask=None if mask is None else mask.numpy())
             return torch.from_numpy(_pack_pairs(raw, slot))
 
         def merge(self, stack, k):
@@ -108,13 +110,15 @@ def _ivf_worker(rank, world, port, case, out):
 
     index = OracleShards(torch.from_numpy(g["codes"][lo:hi]), lo, g["offsets"], g["sizes"],
                          torch.from_numpy(g["sort_perm"]), torch.from_numpy(g["gs"]))
-    ids, scores = index.search(torch.from_numpy(g["query"]), torch.from_numpy(g["probe"]), k, width)
+    filters = {} if words is None else {"filtering_bit_mask": torch.from_numpy(words)}
+    ids, scores = index.search(torch.from_numpy(g["query"]), torch.from_numpy(g["probe"]), k, width, **filters)
     out[rank] = (ids, scores)
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("masked", [False, True])
 @pytest.mark.parametrize("world", [2, 3])
-def test_sharded_ivf_search_equals_single_search(world):
+def test_sharded_ivf_search_equals_single_search(world, masked):
     """Row-sharded st::search (whole clusters a rank): local (raw, slot) pairs in the whole
     table's slot layout, one all-gather, the (raw desc, slot asc) merge and the slot -> id
     finish give the single-table search bit for bit, ties included (the tie-heavy fixture
@@ -130,11 +134,12 @@ def test_sharded_ivf_search_equals_single_search(world):
     assert ties
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
-    port = 29700 + 11 * world
-    mp.start_processes(_ivf_worker, args=(world, port, (g, k, width), out), nprocs=world, join=True,
+    port = 29700 + 11 * world + (5 if masked else 0)
+    words = ivf.pack_mask_high_first(g["mask"]) if masked else None
+    mp.start_processes(_ivf_worker, args=(world, port, (g, k, width, words), out), nprocs=world, join=True,
                        start_method="spawn")
     want_i, want_s = ivf.search(g["query"], g["probe"], g["offsets"], g["sizes"], g["codes"], g["sort_perm"],
-                                g["gs"], k, width)
+                                g["gs"], k, width, filtering_bit_mask=words)
     k_sel = min(k, ivf.padded_width(width))
     for r in range(world):
         ids, scores = out[r]
