@@ -4,8 +4,9 @@ tests use it, as the checker.
 
 Per doc one fused multiply-add chain per block of ``unit`` elements, each step rounded once to
 the format (round to nearest, ties to even): fp32 in one accumulator; fp16 / bf16 in a packed
-pair, even elements in one half and odd in the other. Blocks are added in order onto zero (a
-row of one block is taken as it is) and the pair's halves added last. ``unit`` is the whole row
+pair, even elements in one half and odd in the other. Blocks are added in order onto zero (a row
+of at most 256 bytes is one block taken as it is; a single 384-byte block is still added onto
+zero, which turns a -0 into +0) and the pair's halves added last. ``unit`` is the whole row
 when it fits 256 bytes, else 256 bytes' worth of elements when that divides D, else 384 bytes'
 worth (simple_index_mm.cuh:237-300).
 
@@ -115,9 +116,9 @@ def dot(x_row, q_row, fmt: str) -> float:
             od = fma(x[i + 1], q[i + 1], od, fmt)
         return (ev, od)
 
-    if u == d:
+    if d * ELEM_BYTES[fmt] <= 256:  # one block, taken as it is
         acc = block(0)
-    else:
+    else:  # blocks added onto zero, even when one block (384 bytes) is the whole row
         acc = (0.0, 0.0) if pair else (0.0,)
         for lo in range(0, d, u):
             blk = block(lo)

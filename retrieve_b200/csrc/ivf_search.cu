@@ -297,9 +297,9 @@ __global__ void raw_scores_float_kernel(const T* __restrict__ items, int64_t N, 
   const T* row = items + p * D;
   using F = FloatDot<T>;
   typename F::Acc acc;
-  if (unit == D) {
+  if (D * static_cast<int>(sizeof(T)) <= 256) {  // one block, taken as it is
     acc = F::block(row, sq, D);
-  } else {
+  } else {  // blocks added onto zero, even when one block is the whole row
     acc = F::zero();
     for (int b0 = 0; b0 < D; b0 += unit) acc = F::add(acc, F::block(row + b0, sq + b0, unit));
   }
