@@ -208,16 +208,19 @@ RB_API int rb_set_profile_events(void* start_event, void* stop_event);
 
 /*
  * rb_dense_topk without a caller workspace, for callers that cannot allocate
- * device memory on the call path (a host recording the search into a CUDA
- * graph, where cudaMalloc is not allowed during capture, or a host whose device
- * memory is fixed at start-up by another allocator). The scratch is one static
- * device array of rb_dense_topk_noalloc_scratch_bytes() bytes (32 MiB) that
- * every GPU loading this library keeps until the process exits; calls whose
- * scratch need is larger return RB_ERR_WORKSPACE. The first call on a device
- * looks the array's device address up (it may load the module): make it before
- * any stream capture. All calls share the array: calls that overlap on the GPU
- * race and must be serialised. Same arguments, results and limits as
- * rb_dense_topk otherwise. This entry point has no counterpart in the reference.
+ * device memory on the call path: a host whose device memory is owned by
+ * another allocator and fixed at start-up, or a foreign-language runtime with
+ * no caching allocator, where a cudaMalloc per call would synchronise the
+ * device. The scratch is one static device array of
+ * rb_dense_topk_noalloc_scratch_bytes() bytes (32 MiB) that every GPU loading
+ * this library keeps until the process exits; calls whose scratch need is
+ * larger return RB_ERR_WORKSPACE. The first call on a device looks the array's
+ * device address up (it may load the module): make it before any stream
+ * capture. The stream must belong to the current device (else
+ * RB_ERR_INVALID_ARG), and a device reset leaves the looked-up address stale.
+ * All calls share the array: calls that overlap on the GPU race and must be
+ * serialised. Same arguments, results, checks and error codes as rb_dense_topk
+ * otherwise. This entry point has no counterpart in the reference.
  */
 RB_API size_t rb_dense_topk_noalloc_scratch_bytes(void);
 RB_API int rb_dense_topk_noalloc(const void* queries, const void* items, int B, int N, int D, int dtype, int k,

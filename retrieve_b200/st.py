@@ -62,17 +62,49 @@ def _layout_args(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, clus
     return q, probe, offsets, sizes
 
 
-def search(*args, **kwargs) -> tuple[Tensor, Tensor]:
+# The schema's filter arguments, in schema order (fork_search.cpp:24-37). The dispatcher
+# passes every argument up to the last one given positionally, as the reference's
+# adapter.fork_search does (adapter.py:522-544), so the impls name each one.
+FILTER_ARGS = ("filtering_bit_mask", "bloom_index", "bloom_bundle_b_offsets", "plans", "plan_count",
+               "max_stack_size", "query_plan_index", "bloom_k", "hash_k", "item_clause_attrs", "clause_slots",
+               "clause_is_reverse", "query_clause_attrs")
+
+
+def search(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor, item_codes: Tensor,
+           sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int = -1,
+           filtering_bit_mask: Tensor | None = None, bloom_index: Tensor | None = None,
+           bloom_bundle_b_offsets: Tensor | None = None, plans: Tensor | None = None, plan_count: int = 0,
+           max_stack_size: int = 0, query_plan_index: Tensor | None = None, bloom_k: int = 0, hash_k: int = 0,
+           item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
+           clause_is_reverse: Tensor | None = None,
+           query_clause_attrs: Tensor | None = None) -> tuple[Tensor, Tensor]:
     """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``, scored row by row
-    (each row's probed positions expanded, then the int8 candidate scan)."""
-    return _search(False, *args, **kwargs)
+    (each row's probed positions expanded, then the int8 candidate scan). Takes the
+    schema's 23 arguments positionally or by name."""
+    filters = dict(zip(FILTER_ARGS, (filtering_bit_mask, bloom_index, bloom_bundle_b_offsets, plans, plan_count,
+                                     max_stack_size, query_plan_index, bloom_k, hash_k, item_clause_attrs,
+                                     clause_slots, clause_is_reverse, query_clause_attrs)))
+    return _search(False, query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm, global_scale, k,
+                   max_tensor_size_per_row, divisor_for_int8, filters)
 
 
-def search_grouped(*args, **kwargs) -> tuple[Tensor, Tensor]:
+def search_grouped(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor,
+                   item_codes: Tensor, sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int,
+                   divisor_for_int8: int = -1, filtering_bit_mask: Tensor | None = None,
+                   bloom_index: Tensor | None = None, bloom_bundle_b_offsets: Tensor | None = None,
+                   plans: Tensor | None = None, plan_count: int = 0, max_stack_size: int = 0,
+                   query_plan_index: Tensor | None = None, bloom_k: int = 0, hash_k: int = 0,
+                   item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
+                   clause_is_reverse: Tensor | None = None,
+                   query_clause_attrs: Tensor | None = None) -> tuple[Tensor, Tensor]:
     """``st::search`` with the scoring grouped by cluster (``rb_st_search_grouped``): the
     same arguments and results; each probed cluster is read once per group of up to 64
     probing rows. Up to 1024 probes a row."""
-    return _search(True, *args, **kwargs)
+    filters = dict(zip(FILTER_ARGS, (filtering_bit_mask, bloom_index, bloom_bundle_b_offsets, plans, plan_count,
+                                     max_stack_size, query_plan_index, bloom_k, hash_k, item_clause_attrs,
+                                     clause_slots, clause_is_reverse, query_clause_attrs)))
+    return _search(True, query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm, global_scale, k,
+                   max_tensor_size_per_row, divisor_for_int8, filters)
 
 
 _FILTER_DOC = """Filters: a full-``N`` ``filtering_bit_mask``; the exact clauses
@@ -165,8 +197,8 @@ def _codes_check(item_codes: Tensor, query: Tensor) -> None:
 def _search(
     grouped: bool,
     query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor, item_codes: Tensor,
-    sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int = -1,
-    **filters,
+    sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int, divisor_for_int8: int,
+    filters: dict,
 ) -> tuple[Tensor, Tensor]:
     _codes_check(item_codes, query)
     flt, keep = _filter(query, item_codes.shape[0], **filters)

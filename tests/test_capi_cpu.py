@@ -88,6 +88,22 @@ def test_new_entry_points_validate_before_touching_a_device():
     assert lib.rb_merge_pairs(None, 2, 4, 10, 2000, None, None, None) == _lib.RB_ERR_UNSUPPORTED
 
 
+def test_noalloc_checks_arguments_like_the_workspace_entry_point():
+    """The entry point without a workspace answers a bad call with rb_dense_topk's code,
+    even when that call would also need more than its static scratch."""
+    lib = _lib.lib()
+    big = (4096, 10_000_000)
+    for dtype, d, k, want in ((_lib.RB_I8, 128, 100, _lib.RB_ERR_TYPE), (_lib.RB_E4M3, 128, 100, _lib.RB_ERR_TYPE),
+                              (_lib.RB_BF16, 128, 2000, _lib.RB_ERR_UNSUPPORTED),
+                              (_lib.RB_BF16, 96, 100, _lib.RB_ERR_UNSUPPORTED),
+                              (_lib.RB_BF16, 128, 0, _lib.RB_ERR_INVALID_ARG)):
+        ref = lib.rb_dense_topk(None, None, *big, d, dtype, k, 0, None, None, None, 0, None)
+        got = lib.rb_dense_topk_noalloc(None, None, *big, d, dtype, k, 0, None, None, None)
+        assert ref == got == want, (dtype, d, k)
+    rc = lib.rb_dense_topk_noalloc(None, None, *big, 128, _lib.RB_BF16, 100, 0, None, None, None)
+    assert rc == _lib.RB_ERR_WORKSPACE and b"static" in lib.rb_last_error()
+
+
 def test_filter_struct_layout_matches_the_header(tmp_path):
     """The ctypes twin of rb_st_filter has the C compiler's field offsets and size (a
     mismatch would hand the kernels shifted pointers)."""

@@ -186,6 +186,44 @@ def test_argument_errors_raise_runtime_error():
                   plans=torch.zeros(8, dtype=torch.int64))
 
 
+def _adapter_positional(q, probe, off, sz, codes, perm, gs, mask=None, bloom=None, exact=None):
+    """The 23 arguments in the order the reference's ``adapter.fork_search`` passes them, all
+    positionally (retrieve/src/retrieve/ops/official/adapter.py:522-544); the dispatcher hands
+    them to the registered CUDA impl the same way."""
+    b = bloom
+    return (q, probe, off, sz, codes, perm, gs, 2, 4, -1, mask,
+            None if b is None else b[0], None if b is None else b[1], None if b is None else b[2],
+            0 if b is None else 2, 0 if b is None else 4, None, 0 if b is None else 3, 0 if b is None else 7,
+            *(exact if exact is not None else (None, None, None, None)))
+
+
+@pytest.mark.parametrize("grouped", [False, True])
+def test_search_binds_the_adapters_positional_call(grouped):
+    """Every filter form passed positionally, as the dispatcher does, binds to the impl's
+    parameters and reaches its argument checks (no TypeError)."""
+    _st()
+    from retrieve_b200 import st
+
+    fn = st.search_grouped if grouped else st.search
+    q = torch.zeros(2, 64)
+    probe = torch.zeros(2, 1, dtype=torch.int64)
+    off, sz = torch.tensor([0, 4]), torch.tensor([4])
+    perm, gs = torch.arange(4), torch.tensor(1.0)
+    codes = torch.zeros(4, 64, dtype=torch.int8)
+    mask = torch.zeros(2, 1, dtype=torch.int64)
+    exact = (torch.zeros(1, 4, dtype=torch.int32), torch.tensor([0, 1]), torch.tensor([False]),
+             torch.zeros(2, 1, dtype=torch.int32))
+    bloom = (torch.zeros(64, dtype=torch.int64), torch.tensor([0, 2]), torch.zeros(16, dtype=torch.int64))
+    args = _adapter_positional(q, probe, off, sz, codes, perm, gs, mask=mask, exact=exact)
+    assert len(args) == 23
+    with pytest.raises(RuntimeError, match="one filter"):
+        fn(*args)
+    # each filter alone binds and fails later, on the CPU tensors (the impl serves CUDA)
+    for kw in ({"mask": mask}, {"exact": exact}, {"bloom": bloom}, {"bloom": bloom, "exact": exact}):
+        with pytest.raises(RuntimeError, match="CUDA|device"):
+            fn(*_adapter_positional(q, probe, off, sz, codes, perm, gs, **kw))
+
+
 REF_CPU_LIB = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "silvertorch_ref_cpu.so"
 
 

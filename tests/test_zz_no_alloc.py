@@ -1,8 +1,9 @@
 """rb_dense_topk_noalloc: the dense top-k entry point that allocates nothing.
 
-Callers that cannot allocate device memory on the call path (a CUDA graph
-capture, where cudaMalloc is not allowed, or a host whose memory is fixed at
-start-up by another allocator) get their scratch from one static device array.
+Callers that cannot allocate device memory on the call path (a host whose
+device memory is reserved once at start-up by another allocator, or a binding
+with no caching allocator, where a cudaMalloc per call would synchronise the
+device) get their scratch from one static device array.
 This file checks, through the C-ABI, that two calls in a row return exactly what
 rb_dense_topk returns with a caller workspace (integer-valued inputs make every
 score exact, so the comparison is bit for bit), and that a call needing more
