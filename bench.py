@@ -17,8 +17,9 @@ Rank 0 prints one JSON line. ``value`` is queries/s with the inputs resident in
 HBM, timed with CUDA events, max over ranks; ``e2e`` is the same metric through
 the public op with the query batch copied from pinned host memory and the
 (ids, scores) copied back every step. ``--impl reference`` times the
-reference's CPU path for this workload (the oracle port of FullScanKNN:
-fp32 matmul + top-k with ties to the lower id) on the host cores.
+reference's CPU path for this workload on the host cores: its own FullScanKNN
+(fp32 torch matmul + topk) from the reference package installed under
+baseline/_ref, or the oracle's numpy restatement of it when that is absent.
 """
 
 from __future__ import annotations
@@ -56,6 +57,8 @@ def parse_args():
     p.add_argument("--ref-sample", type=int, default=32,
                    help="queries per step of --impl reference (each step a bounded sample)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-configs", action="store_true",
+                   help="skip the records of configs 3, 4, 5 and the IVF search that follow the headline at N=1")
     p.add_argument("--workload", choices=("c2", "c3", "c4", "c5", "ivf", "ops"), default="c2",
                    help="c2 (default, the headline); c3/c4/c5 and ops: one-GPU measurements of the other configs "
                         "and of every other kernel")
@@ -173,35 +176,69 @@ class ClockSampler:
             "sm_max_mhz": max(mx) if mx else None,
             "reasons": reasons + errors,
             "samples": len(sm),
-            "source": "NVML, every rank's GPU, sampled every 2 ms during both timed loops",
+            "source": "NVML, every rank's GPU, sampled every 2 ms during the timed regions",
         }
         return out
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle port of the reference CPU path, on a bounded sample
+# CPU baseline: the reference's own CPU torch path (FullScanKNN from the
+# reference package installed under baseline/_ref), else the oracle port
 # ---------------------------------------------------------------------------
+REF_SITE = ROOT / "baseline" / "_ref"
+
+
 def host_copy(q_dev: torch.Tensor, x_dev: torch.Tensor, sample: int):
-    """fp32 host copies of the corpus and of the first ``sample`` queries."""
-    import numpy as np
+    """fp32 host copies (torch tensors) of the corpus and of the first ``sample`` queries."""
+    xs = torch.empty((x_dev.shape[0], x_dev.shape[1]), dtype=torch.float32)
+    for lo in range(0, x_dev.shape[0], BLOCK_ROWS):
+        xs[lo : lo + BLOCK_ROWS] = x_dev[lo : lo + BLOCK_ROWS].float().cpu()
+    return q_dev[:sample].float().cpu(), xs
 
-    xs = [x_dev[lo : lo + BLOCK_ROWS].float().cpu().numpy() for lo in range(0, x_dev.shape[0], BLOCK_ROWS)]
-    return q_dev[:sample].float().cpu().numpy(), np.concatenate(xs, axis=0)
 
+def reference_cpu_search(x_host: torch.Tensor, k: int):
+    """``(search, kind)``: ``search(q) -> (ids, scores)`` over the fp32 host corpus on every
+    host core. ``kind`` "reference" runs the reference's ``FullScanKNN``
+    (retrieve/src/retrieve/modules/knn.py:125-170: ``query @ item_embs.t()`` then
+    ``torch.topk``) from its installed package, 32 queries per forward call; "port" runs the
+    oracle's numpy restatement of the same path when that package is absent."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    if (REF_SITE / "retrieve").is_dir():
+        if str(REF_SITE) not in sys.path:
+            sys.path.insert(0, str(REF_SITE))
+        from retrieve.modules.knn import FullScanKNN
 
-def cpu_baseline(q_host, x_host, k: int):
-    """One timed run of the oracle port on the host cores → (queries/s, seconds, ids, scores)."""
+        module = FullScanKNN(k=k)
+        module.register_index(x_host)
+
+        def search(q: torch.Tensor):
+            outs = [module(q[i : i + 32]) for i in range(0, q.shape[0], 32)]
+            return torch.cat([o[0] for o in outs]), torch.cat([o[1] for o in outs])
+
+        return search, "reference"
     from oracle.dense import dense_topk as oracle_dense_topk
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    xn = x_host.numpy()
+
+    def search_port(q: torch.Tensor):
+        ids, sc = oracle_dense_topk(q.numpy(), xn, k, item_chunk=1 << 20, query_batch=q.shape[0])
+        return torch.from_numpy(ids), torch.from_numpy(sc)
+
+    return search_port, "port"
+
+
+def cpu_baseline(q_host: torch.Tensor, x_host: torch.Tensor, k: int):
+    """One timed run of the reference CPU path on the host cores →
+    (queries/s, seconds, ids, kind)."""
+    search, kind = reference_cpu_search(x_host, k)
     t0 = time.perf_counter()
-    ref_i, ref_s = oracle_dense_topk(q_host, x_host, k, item_chunk=1 << 20, query_batch=q_host.shape[0])
+    ref_i, _ = search(q_host)
     dt = time.perf_counter() - t0
-    return q_host.shape[0] / dt, dt, ref_i, ref_s
+    return q_host.shape[0] / dt, dt, ref_i.numpy(), kind
 
 
 def reference_arm(args):
-    """--impl reference: the reference CPU path (oracle port) on the host cores."""
+    """--impl reference: the reference's CPU path on the host cores, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -213,12 +250,17 @@ def reference_arm(args):
     cores = os.cpu_count() or 1
     q_host, x_host = host_copy(q, x, args.ref_sample)
     del x
+    search, kind = reference_cpu_search(x_host, args.k)
     vals = []
     for i in range(args.warmup + args.steps):
-        v, dt, _, _ = cpu_baseline(q_host, x_host, args.k)
+        t0 = time.perf_counter()
+        search(q_host)
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
-            vals.append(v)
+            vals.append(q_host.shape[0] / dt)
     value = statistics.median(vals)
+    what = ("the reference's FullScanKNN (torch matmul + topk, fp32)" if kind == "reference"
+            else "the oracle port of FullScanKNN (numpy)")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -232,8 +274,8 @@ def reference_arm(args):
         "data": "synthetic",
         "config": config_dict(args),
         "cpu_baseline": {
-            "value": value, "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"{args.ref_sample} queries x full {args.n_items}-item corpus per step",
+            "value": value, "unit": "queries/s", "cores": cores, "kind": kind,
+            "sample": f"{args.ref_sample} queries x full {args.n_items}-item corpus per step, {what}",
         },
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -297,11 +339,12 @@ def main():
     torch.cuda.synchronize()
     barrier()
 
-    # the K timed steps captured back to back as ONE CUDA graph, each step's
-    # full-corpus pass bracketed by its own event pair; e2e below replays a
-    # one-search graph (GraphedSearch, the public API)
+    # value: K back-to-back replays of the one-search graph (GraphedSearch, the
+    # public API's captured search), inputs resident in HBM, nothing else in it
     stream = torch.cuda.current_stream(dev)
     graphed = GraphedSearch(index, q, warmup=1)
+    # kernel time: the same K searches captured as one graph with an event pair
+    # around each full-corpus pass (timed in a region of its own, after value's)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for ka, kb in kev:
         ka.record(stream)
@@ -315,22 +358,32 @@ def main():
     lib.rb_set_profile_events(None, None)
     for _ in range(args.warmup):
         graphed.replay()
-    steps_graph.replay()  # first launch of the K-step graph (upload), untimed
+    steps_graph.replay()  # first launch of the instrumented graph (upload), untimed
     torch.cuda.synchronize()
     barrier()
 
     sampler = ClockSampler(dev)
     sampler.start()
-    # device-resident timed region: one replay of the K-step graph
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    steps_graph.replay()
+    for _ in range(args.steps):
+        graphed.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     t_ms = e0.elapsed_time(e1)
+
+    barrier()
+    torch.cuda.synchronize()
+    i0, i1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    i0.record(stream)
+    steps_graph.replay()
+    i1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    inst_ms = i0.elapsed_time(i1)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
 
     # end to end through the public API: pinned host query batch in, results out
@@ -357,10 +410,10 @@ def main():
         per_rank = gathered
     clocks = ClockSampler.summary(per_rank)
 
-    times = torch.tensor([t_ms, e2e_ms, kern_ms], device=dev)
+    times = torch.tensor([t_ms, e2e_ms, kern_ms, inst_ms], device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, kern_ms = times.tolist()
+    t_ms, e2e_ms, kern_ms, inst_ms = times.tolist()
     value = b * args.steps / (t_ms / 1e3)
     e2e_value = b * args.steps / (e2e_ms / 1e3)
 
@@ -368,10 +421,13 @@ def main():
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
         peaks = json.loads(pk.read_text())
-    peak = peaks.get("bf16_tflops_sustained")
-    peak_note = "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    # The scan runs for milliseconds at a time inside a region of well under a
+    # second, at the clocks sampled below: its denominator is the burst GEMM peak.
+    peak = peaks.get("bf16_tflops")
+    peak_note = "measured (MEASURED_PEAKS.json bf16_tflops, the burst figure)"
     if peak is None:
-        peak, peak_note = 1400.0, "fallback (sustained 1.4 PFLOP/s)"
+        peak, peak_note = 1590.0, "fallback (burst 1.59 PFLOP/s)"
+    peak_sustained = peaks.get("bf16_tflops_sustained")
     flops = 2.0 * b * (hi - lo) * DIM
     achieved = flops / (kern_ms / 1e3) / 1e12
     traffic = None
@@ -410,10 +466,12 @@ def main():
             "peak_source": peak_note,
             "unit": "TFLOP/s",
             "frac": achieved / peak,
+            "frac_of_sustained": achieved / peak_sustained if peak_sustained else None,
             "traffic": traffic,
             "kernel_ms": kern_ms,
-            "kernel_ms_source": "CUDA events around the pass in every timed step (event nodes of the "
-                                "K-step graph), mean over steps, max over ranks",
+            "kernel_ms_source": "CUDA events around the full-corpus pass of each of K searches (event nodes of "
+                                "a K-search graph timed in a region of its own), mean over searches, max over ranks",
+            "instrumented_ms_per_step": inst_ms / args.steps,
         },
         "gpu_launches": launches,
         "clocks": clocks,
@@ -421,19 +479,28 @@ def main():
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         q_host, x_host = host_copy(q, x, args.cpu_sample)
-        v, dt, ref_i, ref_s = cpu_baseline(q_host, x_host, k)
+        v, dt, ref_i, kind = cpu_baseline(q_host, x_host, k)
+        del x_host
         ours_i, _ = index.search(q[: args.cpu_sample])
         from oracle.dense import recall_at_k
 
         line["cpu_baseline"] = {
-            "value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
+            "value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": kind,
             "sample": f"{args.cpu_sample} queries x full {n}-item corpus ({dt:.1f} s)",
         }
         line["recall_vs_ref"] = recall_at_k(ours_i.cpu().numpy(), ref_i)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     steps_graph.reset()
     graphed.release()
+    if world == 1 and not args.no_configs:
+        # the other configurations, one GPU each, after the headline's inputs are freed
+        from bench_configs import measure_configs
+
+        del index, x, q
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        line["configs"] = measure_configs(args, dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 

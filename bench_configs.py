@@ -48,19 +48,55 @@ def _blocks(n: int, fn, block: int = 1 << 20):
         yield lo, min(lo + block, n), fn(min(lo + block, n) - lo, 1000 + b)
 
 
-def _time(step, warmup: int, steps: int) -> tuple[float, list[float]]:
-    """Mean ms per step over K timed steps (CUDA events per step), after W warm-ups."""
+def _time(step, warmup: int, steps: int, kernel: bool = True) -> tuple[float, float | None]:
+    """(mean ms per step, mean ms of the step's dominant kernel or None) over K timed
+    steps after W warm-ups. Each step is bracketed by CUDA events on the launching
+    stream; with ``kernel`` the library's profiling hook (``rb_set_profile_events``)
+    records a second event pair around the dominant kernel of the step's last call
+    that has one (the dense scan's full-corpus pass, or st::search's scorer)."""
+    from retrieve_b200 import _lib
+
+    lib = _lib.lib()
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    for a, b in evs:
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for ka, kb in kev:  # a torch event gets its CUDA handle at its first record
+        ka.record()
+        kb.record()
+    torch.cuda.synchronize()
+    for (a, b), (ka, kb) in zip(evs, kev):
+        if kernel:
+            lib.rb_set_profile_events(ka.cuda_event, kb.cuda_event)
         a.record()
         step()
         b.record()
+    lib.rb_set_profile_events(None, None)
     torch.cuda.synchronize()
     ts = [a.elapsed_time(b) for a, b in evs]
-    return statistics.mean(ts), ts
+    kms = None
+    if kernel:
+        try:
+            kms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+        except RuntimeError:  # the step made no call with a hooked kernel
+            kms = None
+    return statistics.mean(ts), kms
+
+
+def _cpu(fn, sample_desc: str, scale: float, kind: str, cores: int | None = None) -> dict:
+    """Times ``fn()`` once on the host (every core torch may use) → a cpu_baseline dict;
+    ``scale`` turns one call into queries of the full workload (queries / fraction of the
+    corpus covered)."""
+    import os
+    import time
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    t0 = time.perf_counter()
+    fn()
+    dt = time.perf_counter() - t0
+    return {"value": scale / dt, "unit": "queries/s", "cores": cores or os.cpu_count(), "kind": kind,
+            "sample": f"{sample_desc} ({dt:.1f} s)"}
 
 
 def _peaks() -> dict:
@@ -78,7 +114,7 @@ def _line(metric, value, unit, config, roofline, clocks, dtype, higher=True, **e
 # ---------------------------------------------------------------------------
 # C4: int8
 # ---------------------------------------------------------------------------
-def run_c4(args, dev):
+def run_c4(args, dev) -> dict:
     from retrieve_b200 import ops
 
     n = args.n_items if args.n_items != bench.N_ITEMS else 30_000_000
@@ -95,17 +131,34 @@ def run_c4(args, dev):
     torch.cuda.synchronize()
     sampler = bench.ClockSampler(dev)
     sampler.start()
-    ms, _ = _time(lambda: ops.int8_topk(q, codes, scales, k), args.warmup, args.steps)
+    ms, kms = _time(lambda: ops.int8_topk(q, codes, scales, k), args.warmup, args.steps)
     clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
-    peak = 2 * _peaks().get("bf16_tflops_sustained", 1400.0)
-    achieved = 2.0 * b * n * d / (ms / 1e3) / 1e12
-    _line("queries/s @30M items d=256 int8 per-row scales, B=4096, k=100", b / (ms / 1e3), "queries/s",
-          {"workload": "int8 scoring (BASELINE config 4)", "n_items": n, "dim": d, "batch": b, "k": k,
-           "corpus": "1024-centre Gaussian mixture, sigma 0.15, per-row symmetric int8"},
-          {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
-           "peak_source": "derived: 2 x measured bf16 sustained (int8 tensor rate is twice bf16)",
-           "step_ms": ms, "note": "step = query quantization + int8 scan (kind::i8) + merge"},
-          clocks, "int8 -> int32")
+    peak = 2 * _peaks().get("bf16_tflops", 1590.0)
+    ops_ = 2.0 * b * n * d
+    achieved = ops_ / (kms / 1e3) / 1e12
+    # CPU: the int32 scoring path restated in torch (int8 values in fp32 give exact int32
+    # dots below 2^24), dequant (fp32(dot) * q_scale) * item_scale, top-k, on a sample
+    qs_n, m = 4, min(n, 2_000_000)
+    q_codes, q_scales = ops.quantize_int8(q[:qs_n])
+    qc, qsc = q_codes.float().cpu(), q_scales.cpu()
+    xc, xsc = codes[:m].float().cpu(), scales[:m].cpu()
+
+    def cpu_step():
+        sc_ = ((qc @ xc.t()) * qsc[:, None]) * xsc[None, :]
+        return torch.topk(sc_, k, dim=1)
+
+    cpu = _cpu(cpu_step, f"{qs_n} queries x the first {m} of {n} items (int32 dots as exact fp32 matmul, "
+               "dequant, top-k; a restatement of the SilverTorch int32 path)", qs_n * m / n, "port")
+    del codes, scales
+    return {"metric": "queries/s @30M items d=256 int8 per-row scales, B=4096, k=100", "value": b / (ms / 1e3),
+            "unit": "queries/s", "ms_per_step": ms, "higher_is_better": True, "dtype": "int8 -> int32",
+            "config": {"workload": "int8 scoring (BASELINE config 4)", "n_items": n, "dim": d, "batch": b, "k": k,
+                       "corpus": "1024-centre Gaussian mixture, sigma 0.15, per-row symmetric int8",
+                       "step": "query quantization + int8 scan (tcgen05 kind::i8) + merge"},
+            "roofline": {"bound": "tensor", "kernel": "dense_scan (int8, full-corpus pass)", "achieved": achieved,
+                         "peak": peak, "unit": "TOP/s", "frac": achieved / peak, "kernel_ms": kms,
+                         "peak_source": "derived: 2 x measured bf16 burst (the int8 tensor rate is twice bf16)"},
+            "clocks": clocks, "cpu_baseline": cpu}
 
 
 # ---------------------------------------------------------------------------
@@ -118,7 +171,7 @@ def _simhash(x: torch.Tensor, r: torch.Tensor) -> torch.Tensor:
     return (bits.view(-1, w, 64) << shifts).sum(dim=2)  # disjoint bits: the sum is the OR
 
 
-def run_c5(args, dev):
+def run_c5(args, dev) -> dict:
     from retrieve_b200.bitknn import PackedBitsIndex, onebit_rerank_topk
     from retrieve_b200.quantize import project_simhash_1bit_query
 
@@ -135,6 +188,8 @@ def run_c5(args, dev):
         del x
     qf = _mixture(cent, b, 7)
     q = qf.to(torch.float16)
+    m = min(n, 2_000_000)
+    codes_host, items_host = codes[:m].cpu(), items[:m].cpu()
     index = PackedBitsIndex(codes)
     del codes
     torch.cuda.synchronize()
@@ -146,20 +201,48 @@ def run_c5(args, dev):
 
     sampler = bench.ClockSampler(dev)
     sampler.start()
-    ms, _ = _time(step, args.warmup, args.steps)
+    ms, kms = _time(step, args.warmup, args.steps)
     clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
-    peak = 2 * _peaks().get("bf16_tflops_sustained", 1400.0)
-    achieved = 2.0 * b * n * nbits / (ms / 1e3) / 1e12  # the +-1 int8 scan's ops over the whole step
-    _line("queries/s @30M items 512-bit codes, pool 1000 + fp16 rerank d=128 to k=100, B=1024",
-          b / (ms / 1e3), "queries/s",
-          {"workload": "1-bit coarse retrieval + rerank (BASELINE config 5)", "n_items": n, "bits": nbits,
-           "batch": b, "pool": pool, "k": k, "codes": "SimHash (N(0,1) projections, seed 0) of the mixture",
-           "stage1": "codes as a +-1 fp8 table, kind::f8f6f4 scan, exact 64W - 2*hamming scores",
-           "step": "query SimHash projection + sign packing, 1-bit pool, fp16 rerank"},
-          {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
-           "peak_source": "derived: 2 x measured bf16 sustained (int8 tensor rate is twice bf16)",
-           "step_ms": ms, "note": "achieved counts the stage-1 scan's ops over the whole step (rerank included)"},
-          clocks, "int8 (+-1) -> int32; fp16 rerank")
+    peak = 2 * _peaks().get("bf16_tflops", 1590.0)
+    ops_ = 2.0 * b * n * nbits  # the +-1 fp8 scan's multiply-adds
+    achieved = ops_ / (kms / 1e3) / 1e12 if kms else None
+    # CPU: the reference's own torch ops (popcount Hamming top-pool, then the gather + bmm
+    # rerank), from its installed package, on a sample; else no CPU figure
+    cpu = None
+    ref_site = bench.REF_SITE
+    if (ref_site / "retrieve").is_dir():
+        import sys
+
+        if str(ref_site) not in sys.path:
+            sys.path.insert(0, str(ref_site))
+        from retrieve.ops.reference.fused_masked_knn_topk import fused_masked_knn_topk as ref_rerank
+        from retrieve.ops.reference.oporp_1bit_match_topk import oporp_1bit_match_topk_full as ref_hamming
+
+        qs_n = 2
+        qbits_host = project_simhash_1bit_query(qf[:qs_n], proj).cpu()
+        q_host = q[:qs_n].cpu()
+
+        def cpu_step():
+            cand, _ = ref_hamming(qbits_host, codes_host, pool)
+            cnt = torch.full((qs_n,), pool, dtype=torch.int64)
+            return ref_rerank(q_host, items_host, cand, cnt, k)
+
+        cpu = _cpu(cpu_step, f"{qs_n} queries x the first {m} of {n} items, the reference's torch ops "
+                   "oporp_1bit_match_topk_full + fused_masked_knn_topk", qs_n * m / n, "reference")
+    del index, items
+    return {"metric": "queries/s @30M items 512-bit codes, pool 1000 + fp16 rerank d=128 to k=100, B=1024",
+            "value": b / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms, "higher_is_better": True,
+            "dtype": "fp8 (+-1) -> fp32 exact; fp16 rerank",
+            "config": {"workload": "1-bit coarse retrieval + rerank (BASELINE config 5)", "n_items": n,
+                       "bits": nbits, "batch": b, "pool": pool, "k": k,
+                       "codes": "SimHash (N(0,1) projections, seed 0) of the mixture",
+                       "stage1": "codes as a +-1 fp8 table, kind::f8f6f4 scan, exact 64W - 2*hamming scores",
+                       "step": "query SimHash projection + sign packing, 1-bit pool, fp16 rerank"},
+            "roofline": {"bound": "tensor", "kernel": "dense_scan (+-1 fp8, stage-1 pass)", "achieved": achieved,
+                         "peak": peak, "unit": "TOP/s", "frac": achieved / peak if achieved else None,
+                         "kernel_ms": kms,
+                         "peak_source": "derived: 2 x measured bf16 burst (the fp8 tensor rate is twice bf16)"},
+            "clocks": clocks, "cpu_baseline": cpu}
 
 
 # ---------------------------------------------------------------------------
@@ -211,7 +294,18 @@ def _predicates_for(attrs: torch.Tensor, b: int, target: float, seed: int) -> li
     return out
 
 
-def run_c3(args, dev):
+def _expr_mask(a: torch.Tensor, e: str) -> torch.Tensor:
+    """Items of ``a`` [M, C] (one value per clause) passing one expression of the forms
+    ``_predicates_for`` writes: one term, an AND of two, an OR of up to three."""
+    op = " OR " if " OR " in e else " AND "
+    hits = [a[:, int(t.split(":")[0])] == int(t.split(":")[1]) for t in e.split(op)]
+    m = hits[0]
+    for h in hits[1:]:
+        m = (m | h) if op == " OR " else (m & h)
+    return m
+
+
+def run_c3(args, dev) -> dict:
     from retrieve_b200 import ops
     from retrieve_b200.predicates import from_expressions
 
@@ -232,40 +326,47 @@ def run_c3(args, dev):
         preds = from_expressions(exprs).to(dev)
         sel = _selectivity(attrs, exprs)
         torch.cuda.synchronize()
-        ms, _ = _time(lambda: ops.dense_topk_filtered(q, items, k, preds.terms, preds.n_terms, "bloom_recheck",
-                                                      attrs, bloom), args.warmup, args.steps)
-        results[f"{int(target * 100)}%"] = {"queries_per_s": b / (ms / 1e3), "step_ms": ms,
+        ms, kms = _time(lambda: ops.dense_topk_filtered(q, items, k, preds.terms, preds.n_terms, "bloom_recheck",
+                                                        attrs, bloom), args.warmup, args.steps)
+        results[f"{int(target * 100)}%"] = {"queries_per_s": b / (ms / 1e3), "ms_per_step": ms, "kernel_ms": kms,
                                             "measured_selectivity": sel}
     clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
-    peak = _peaks().get("bf16_tflops_sustained", 1400.0)
-    ms10 = results["10%"]["step_ms"]
-    achieved = 2.0 * b * n * bench.DIM / (ms10 / 1e3) / 1e12
-    _line("queries/s @10M items d=128 fp16, 8 attrs + 64-bit bloom, B=1024, k=100 (10 % selectivity)",
-          results["10%"]["queries_per_s"], "queries/s",
-          {"workload": "attribute-filtered kNN (BASELINE config 3)", "n_items": n, "dim": bench.DIM, "batch": b,
-           "k": k, "attrs": "8 categorical, cardinalities 10..1000, Zipf(1.1)", "bloom": "64-bit, 3 hashes",
-           "mode": "bloom test + exact recheck (exact results)", "sweep": results},
-          {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-           "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops_sustained)",
-           "note": "2*B*N*D dense-masked flops (the figure the config is measured by) at 10 % selectivity"},
-          clocks, "fp16")
+    peak = _peaks().get("bf16_tflops", 1590.0)
+    r10 = results["10%"]
+    achieved = 2.0 * b * n * bench.DIM / (r10["kernel_ms"] / 1e3) / 1e12 if r10["kernel_ms"] else None
+    # CPU: fp32 scores, the predicates restated as torch masks, masked top-k, on a sample
+    qs_n, m = 4, min(n, 1_000_000)
+    exprs10 = _predicates_for(attrs, b, 0.10, seed=100)[:qs_n]
+    xh, ah, qh = items[:m].float().cpu(), attrs[:m, :, 0].cpu(), q[:qs_n].float().cpu()
+
+    def cpu_step():
+        sc = qh @ xh.t()
+        mask = torch.stack([_expr_mask(ah, e) for e in exprs10])
+        return torch.topk(sc.masked_fill(~mask, float("-inf")), k, dim=1)
+
+    cpu = _cpu(cpu_step, f"{qs_n} queries (10 % selectivity) x the first {m} of {n} items: fp32 scores, "
+               "predicate masks, top-k (a restatement)", qs_n * m / n, "port")
+    del items, attrs, bloom
+    return {"metric": "queries/s @10M items d=128 fp16, 8 attrs + 64-bit bloom, B=1024, k=100 (10 % selectivity)",
+            "value": r10["queries_per_s"], "unit": "queries/s", "ms_per_step": r10["ms_per_step"],
+            "higher_is_better": True, "dtype": "fp16",
+            "config": {"workload": "attribute-filtered kNN (BASELINE config 3)", "n_items": n, "dim": bench.DIM,
+                       "batch": b, "k": k, "attrs": "8 categorical, cardinalities 10..1000, Zipf(1.1)",
+                       "bloom": "64-bit, 3 hashes", "mode": "bloom test + exact recheck (exact results)",
+                       "sweep": results},
+            "roofline": {"bound": "tensor", "kernel": "dense_scan (fp16, filtered full-corpus pass)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak if achieved else None, "kernel_ms": r10["kernel_ms"],
+                         "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)",
+                         "note": "2*B*N*D dense flops at 10 % selectivity"},
+            "clocks": clocks, "cpu_baseline": cpu}
 
 
 def _selectivity(attrs, exprs: list[str], sample: int = 1 << 20) -> float:
-    """Mean exact fraction of a strided item sample passing each query's
-    expression (the forms ``_predicates_for`` writes: one term, an AND of two,
-    an OR of up to three)."""
+    """Mean exact fraction of a strided item sample passing each query's expression."""
     idx = torch.linspace(0, attrs.shape[0] - 1, sample, device=attrs.device).long()
     a = attrs[idx, :, 0]
-    fracs = []
-    for e in exprs:
-        op = " OR " if " OR " in e else " AND "
-        hits = [a[:, int(t.split(":")[0])] == int(t.split(":")[1]) for t in e.split(op)]
-        m = hits[0]
-        for h in hits[1:]:
-            m = (m | h) if op == " OR " else (m & h)
-        fracs.append(m.float().mean())
-    return float(torch.stack(fracs).mean())
+    return float(torch.stack([_expr_mask(a, e).float().mean() for e in exprs]).mean())
 
 
 # ---------------------------------------------------------------------------
@@ -281,7 +382,7 @@ def run_ops(args, dev):
     sampler.start()
 
     def measure(name, fn, bytes_, note, ops_=None, unit=None):
-        ms, _ = _time(fn, args.warmup, args.steps)
+        ms, _ = _time(fn, args.warmup, args.steps, kernel=False)
         r = {"op": name, "ms": ms, "algorithmic_bytes": bytes_, "GB_s": bytes_ / (ms / 1e3) / 1e9,
              "frac_of_hbm": bytes_ / (ms / 1e3) / 1e9 / hbm, "note": note}
         if ops_ is not None:
@@ -399,29 +500,32 @@ def run_ivf(args, dev):
     same = bool(torch.equal(a[0], b_[0]) and torch.equal(a[1], b_[1]))
     sampler = bench.ClockSampler(dev)
     sampler.start()
-    ms, _ = _time(step, args.warmup, args.steps)
-    ms_grouped, _ = _time(step_grouped, args.warmup, args.steps)
+    ms, kms = _time(step, args.warmup, args.steps)
+    ms_grouped, kms_grouped = _time(step_grouped, args.warmup, args.steps)
     bloom = _ivf_bloom_timing(args, dev, q, qb, centroids, n_probe, offsets, sizes, codes_sorted, perm, gs, k, width)
     clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
     scored = float(sizes[probe0].sum())  # probed (query, item) pairs per batch
     hbm = _peaks().get("hbm_gbs", 6650.0)
-    achieved = scored * d / (ms / 1e3) / 1e9
+    achieved = scored * d / (kms / 1e3) / 1e9 if kms else None
     cpu = _ivf_cpu_baseline(q, probe0, offsets, sizes, codes_sorted, perm, gs, k, width)
-    _line("queries/s, IVF phase 1 + st::search @10M items d=128 int8 (global scale), 1024 lists, 16 probes, "
-          "B=1024, k=100", b / (ms / 1e3), "queries/s",
-          {"workload": "SilverTorch IVF search (st::search semantics)", "n_items": n, "dim": d, "batch": b, "k": k,
-           "n_lists": n_lists, "n_probe": n_probe, "max_tensor_size_per_row": width,
-           "probed_pairs_per_batch": scored,
-           "scorer": "row path (the registered op)",
-           "grouped": {"queries_per_s": b / (ms_grouped / 1e3), "step_ms": ms_grouped,
-                       "identical_to_row_path": same},
-           "bloom": bloom,
-           "corpus": "the C2 mixture, clustered by its nearest normalised centre, int8 with one global scale"},
-          {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-           "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
-           "note": "probed code bytes (pairs x D) per second; rows probed by several queries of a batch are "
-                   "re-read from L2, so this can exceed the HBM copy rate", "step_ms": ms},
-          clocks, "int8 -> int32", cpu_baseline=cpu)
+    del codes_sorted
+    return {"metric": "queries/s, IVF phase 1 + st::search @10M items d=128 int8 (global scale), 1024 lists, "
+                      "16 probes, B=1024, k=100", "value": b / (ms / 1e3), "unit": "queries/s", "ms_per_step": ms,
+            "higher_is_better": True, "dtype": "int8 -> int32",
+            "config": {"workload": "SilverTorch IVF search (st::search semantics)", "n_items": n, "dim": d,
+                       "batch": b, "k": k, "n_lists": n_lists, "n_probe": n_probe, "max_tensor_size_per_row": width,
+                       "probed_pairs_per_batch": scored, "scorer": "row path (the registered op)",
+                       "grouped": {"queries_per_s": b / (ms_grouped / 1e3), "ms_per_step": ms_grouped,
+                                   "kernel_ms": kms_grouped, "identical_to_row_path": same},
+                       "bloom": bloom,
+                       "corpus": "the C2 mixture, clustered by its nearest normalised centre, int8 with one global "
+                                 "scale"},
+            "roofline": {"bound": "hbm", "kernel": "st::search scorer", "achieved": achieved, "peak": hbm,
+                         "unit": "GB/s", "frac": achieved / hbm if achieved else None, "kernel_ms": kms,
+                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)",
+                         "note": "probed code bytes (pairs x D) per second of the scorer; rows probed by several "
+                                 "queries of a batch are re-read from L2, so this can exceed the HBM copy rate"},
+            "clocks": clocks, "cpu_baseline": cpu}
 
 
 def _ivf_bloom_timing(args, dev, q, qb, centroids, n_probe, offsets, sizes, codes_sorted, perm, gs, k, width):
@@ -461,14 +565,29 @@ def _ivf_bloom_timing(args, dev, q, qb, centroids, n_probe, offsets, sizes, code
         r1, r2 = step_bloom(), step_bloom_grouped()
         same = bool(torch.equal(r1[0], r2[0]) and torch.equal(r1[1], r2[1]))
         kept = float((r1[0] >= 0).float().mean())
-        ms_b, _ = _time(step_bloom, args.warmup, args.steps)
-        ms_bg, _ = _time(step_bloom_grouped, args.warmup, args.steps)
+        ms_b, _ = _time(step_bloom, args.warmup, args.steps, kernel=False)
+        ms_bg, _ = _time(step_bloom_grouped, args.warmup, args.steps, kernel=False)
         return {"queries_per_s": b / (ms_b / 1e3), "step_ms": ms_b,
                 "grouped_queries_per_s": b / (ms_bg / 1e3), "grouped_step_ms": ms_bg,
                 "grouped_identical_to_row_path": same, "filled_result_fraction": kept,
                 "filter": "one attribute term per query, 64-bit bloom, 3 positions, hash_k 7, no recheck"}
     except Exception as exc:  # noqa: BLE001  (a secondary measurement; the headline stands)
         return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+
+def measure_configs(args, dev, names=("c3", "c4", "c5", "ivf")) -> dict:
+    """The other configurations' records, one after another on this GPU (each frees its
+    inputs before the next); a failure is recorded in place of its record."""
+    out = {}
+    runners = {"c3": run_c3, "c4": run_c4, "c5": run_c5, "ivf": run_ivf}
+    for name in names:
+        try:
+            out[name] = runners[name](args, dev)
+        except Exception as exc:  # noqa: BLE001  (one config's failure leaves the others and the headline)
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_workload(args):
@@ -478,4 +597,11 @@ def run_workload(args):
         raise SystemExit("--workload c3/c4/c5/ivf/ops runs on one GPU (no torchrun)")
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    {"c3": run_c3, "c4": run_c4, "c5": run_c5, "ivf": run_ivf, "ops": run_ops}[args.workload](args, dev)
+    if args.workload == "ops":
+        run_ops(args, dev)
+        return
+    rec = {"c3": run_c3, "c4": run_c4, "c5": run_c5, "ivf": run_ivf}[args.workload](args, dev)
+    line = {"metric": rec.pop("metric"), "value": rec.pop("value"), "unit": rec.pop("unit"), "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "data": "synthetic"}
+    line.update(rec)
+    print(json.dumps(line), flush=True)

@@ -200,9 +200,9 @@ RB_API int rb_merge_topk(const int64_t* ids, const float* scores, int W, int B, 
 
 /*
  * Profiling hook: records two caller-owned cudaEvent_t on the call's stream
- * around the dominant kernel (the full-corpus scan) of every later call made
- * from this thread; pass NULL, NULL to stop. Used by bench.py to time that
- * kernel on the stream it runs on.
+ * around the dominant kernel of every later call made from this thread (the
+ * dense scan's full-corpus pass; rb_st_search's scorer); pass NULL, NULL to
+ * stop. Used by bench.py to time that kernel on the stream it runs on.
  */
 RB_API int rb_set_profile_events(void* start_event, void* stop_event);
 

@@ -28,7 +28,7 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Records a profiling event; inside a CUDA graph capture as an event record
 // node, so that every replay of the graph records it.
-static void record_profile_event(cudaEvent_t ev, cudaStream_t stream) {
+void record_profile_event(cudaEvent_t ev, cudaStream_t stream) {
   cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &st) == cudaSuccess && st == cudaStreamCaptureStatusActive)
     cudaEventRecordWithFlags(ev, stream, cudaEventRecordExternal);

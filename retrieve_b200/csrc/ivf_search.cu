@@ -902,9 +902,13 @@ static int st_row_search(const float* query, int B, int D, const int64_t* probe_
                                                       fs, width, pos_lo, pos_hi, pos, counts);
   rc = launch_status();
   if (rc != RB_OK) return rc;
+  ProfileEvents& pe = profile_events();
+  if (pe.start) record_profile_event(pe.start, s);
   rc = cand_i8_topk(q_codes, item_codes, static_cast<int>(pos_hi - pos_lo), D, pos, width, counts, B, k_sel,
                     divisor_for_int8, slots, raw, ws + lay.cand, s, reinterpret_cast<uint2*>(out_pairs));
-  if (rc != RB_OK || out_pairs != nullptr) return rc;
+  if (rc != RB_OK) return rc;
+  if (pe.stop) record_profile_event(pe.stop, s);
+  if (out_pairs != nullptr) return rc;
   const int64_t n = static_cast<int64_t>(B) * k;
   const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
   st_epilogue_kernel<<<grid, 256, 0, s>>>(slots, raw, k_sel, pos, counts, width, sort_perm, n_total, q_scales,
@@ -1066,6 +1070,8 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
                head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts};
   const unsigned grid_tasks = static_cast<unsigned>(max_tasks);
   const bool bloom = fs.bloom.index != nullptr;
+  ProfileEvents& pe = profile_events();
+  if (pe.start) record_profile_event(pe.start, s);
   if (group_cap(k_sel) == kGroupCap) {
     if (bloom)
       ivf_group_scan_kernel<kGroupCap, true><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
@@ -1079,6 +1085,7 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   }
   rc = launch_status();
   if (rc != RB_OK) return rc;
+  if (pe.stop) record_profile_event(pe.stop, s);
   rc = merge_lists(lists, lcounts, B, P, group_cap(k_sel), k_sel, 0, slots, raw, nullptr, s);
   if (rc != RB_OK) return rc;
   const int64_t n = static_cast<int64_t>(B) * k;

@@ -77,5 +77,7 @@ struct ProfileEvents {
   cudaEvent_t start = nullptr, stop = nullptr;
 };
 ProfileEvents& profile_events();
+// Records ev on the stream (inside a stream capture: as an external event node).
+void record_profile_event(cudaEvent_t ev, cudaStream_t stream);
 
 }  // namespace rb
