@@ -20,10 +20,10 @@ def pytest_configure(config):
 
 # Modules run in this order after all others (a stable sort): SilverTorch's ops by how central
 # they are to the search path, then the build-time tools and the end-to-end pipeline built from
-# them, and the no-allocation entry point's test last of all. Under ``-x`` a failure in one of
-# these leaves every test before it already run.
+# them, the reference's own modules on this library, and the no-allocation entry point's test
+# last of all. Under ``-x`` a failure in one of these leaves every test before it already run.
 LATE_MODULES = ("test_st_search", "test_st_bloom", "test_st_select", "test_quantizers", "test_kmeans",
-                "test_ivf_pipeline", "test_zz_no_alloc")
+                "test_ivf_pipeline", "test_dropin_reference", "test_zz_no_alloc")
 
 
 def _rank(item) -> int:

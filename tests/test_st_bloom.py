@@ -241,13 +241,17 @@ def test_full_search_on_device():
     n = int(BLOOM["n"])
     assert mask.dtype == torch.bool
     assert np.array_equal(mask.cpu().numpy()[:, :n], np.unpackbits(BLOOM["mask_bits"], axis=1)[:, :n].astype(bool))
+    # the adapter's blob holds `slots` plan slots and passes `slots` as plan_count; the data
+    # follows the 8 * slots offset words (adapter.py:219-236), the spare slots' offsets are zero
     n_plans = BLOOM["words"].shape[0]
-    blob = torch.from_numpy(ivf.plan_blob(BLOOM["plan_data"], BLOOM["plan_offsets"], n_plans + 3)).cuda()
-    words_p = st.bloom_index_search_batch_prepared(index, boff, blob, n_plans, int(BLOOM["max_stack"]), K, HASH_K)
-    assert np.array_equal(words_p.cpu().numpy(), BLOOM["words"])
-    mask_p = st.bloom_index_search_batch_prepared(index, boff, blob, n_plans, int(BLOOM["max_stack"]), K, HASH_K,
+    slots = n_plans + 3
+    blob = torch.from_numpy(ivf.plan_blob(BLOOM["plan_data"], BLOOM["plan_offsets"], slots)).cuda()
+    words_p = st.bloom_index_search_batch_prepared(index, boff, blob, slots, int(BLOOM["max_stack"]), K, HASH_K)
+    assert words_p.shape[0] == slots
+    assert np.array_equal(words_p[:n_plans].cpu().numpy(), BLOOM["words"])
+    mask_p = st.bloom_index_search_batch_prepared(index, boff, blob, slots, int(BLOOM["max_stack"]), K, HASH_K,
                                                   True)
-    assert torch.equal(mask_p, mask)
+    assert torch.equal(mask_p[:n_plans], mask)
 
 
 @pytest.mark.gpu
