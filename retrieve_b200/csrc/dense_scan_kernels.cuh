@@ -182,21 +182,20 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         p.chunk_max[static_cast<size_t>(q) * p.chunk_stride + chunk0 + ch] = max32(r[ch]);
     }
   } else {
-    // Threshold filter on the FMA pipe (paired fp32 subtracts) and the ALU
-    // (AND tree): the sign bit of sg[ch] is set iff no score of chunk ch
-    // passes; then the exact append of the chunks that may pass.
-    const uint64_t tt = pack_pair(thresh);
-    uint32_t sg[NCH];
-    uint32_t all = 0xffffffffu;
+    // Threshold filter: a chunk may hold a passing score iff its max (three-
+    // input maxima, NaN ignored) is >= thresh; then the exact append of those
+    // chunks, score by score.
+    float cm[NCH];
+    float all = -INFINITY;
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      sg[ch] = chunk_all_below(r[ch], tt);
-      all &= sg[ch];
+      cm[ch] = max32(r[ch]);
+      all = fmaxf(all, cm[ch]);
     }
-    if (__any_sync(RB_FULL_MASK, valid_q && !(all >> 31))) {
+    if (__any_sync(RB_FULL_MASK, valid_q && all >= thresh)) {
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
-        if (valid_q && !(sg[ch] >> 31)) {
+        if (valid_q && cm[ch] >= thresh) {
           if constexpr (!FILT) {
             append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
           } else {

@@ -163,37 +163,6 @@ __device__ __forceinline__ uint32_t pred_pass_bits(const FilterArgs& f, int q, u
   return out;
 }
 
-// (t, t) as the 64-bit operand of the paired fp32 instructions.
-__device__ __forceinline__ uint64_t pack_pair(float t) {
-  uint64_t tt;
-  asm("mov.b64 %0, {%1, %1};" : "=l"(tt) : "r"(__float_as_uint(t)));
-  return tt;
-}
-
-// (s0 - t, s1 - t) as bit patterns: one paired fp32 subtract, rounded to
-// nearest like two scalar subtracts.
-__device__ __forceinline__ void sub_pair(uint32_t s0, uint32_t s1, uint64_t tt, uint32_t& d0, uint32_t& d1) {
-  uint64_t x, d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "r"(s0), "r"(s1));
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(tt));
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(d0), "=r"(d1) : "l"(d));
-}
-
-// AND over a chunk of the bit patterns of (s[j] - t): s - t is negative
-// exactly when s < t (a difference of floats that is >= 0 never rounds below
-// 0), so the sign bit of the result is set iff every s[j] < t. NaN scores count
-// as passing here and are rejected by the exact test of the append.
-__device__ __forceinline__ uint32_t chunk_all_below(const uint32_t (&s)[32], uint64_t tt) {
-  uint32_t d[32];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) sub_pair(s[2 * i], s[2 * i + 1], tt, d[2 * i], d[2 * i + 1]);
-  uint32_t a[11];
-#pragma unroll
-  for (int i = 0; i < 10; ++i) a[i] = d[3 * i] & d[3 * i + 1] & d[3 * i + 2];
-  a[10] = d[30] & d[31];
-  const uint32_t b0 = a[0] & a[1] & a[2], b1 = a[3] & a[4] & a[5], b2 = a[6] & a[7] & a[8];
-  return b0 & b1 & b2 & a[9] & a[10];
-}
 
 // Appends the entries s[j] >= thresh of a 32-item chunk (items id0 + j).
 // Padding slots hold NaN, which never passes.
@@ -233,17 +202,25 @@ __device__ __forceinline__ void append_chunk_mask(uint2* list, int& count, const
   count = static_cast<int>(w - list);
 }
 
-// Max of 32 fp32 values (raw bits) as a balanced tree (depth 5).
+// Three-input fp32 max (sm_100: one instruction). NaN operands are ignored
+// as by fmaxf: the result is NaN only when all three are.
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Max of 32 fp32 values (raw bits): 16 instructions, three-input maxima in a
+// tree of depth 4 (32 -> 11 -> 4 -> 2 -> 1). NaN entries are ignored.
 __device__ __forceinline__ float max32(const uint32_t (&s)[32]) {
-  float a[16];
+  float a[11];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) a[i] = fmaxf(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
-#pragma unroll
-  for (int w = 8; w >= 1; w >>= 1) {
-#pragma unroll
-    for (int i = 0; i < w; ++i) a[i] = fmaxf(a[2 * i], a[2 * i + 1]);
-  }
-  return a[0];
+  for (int i = 0; i < 10; ++i)
+    a[i] = fmax3f(__uint_as_float(s[3 * i]), __uint_as_float(s[3 * i + 1]), __uint_as_float(s[3 * i + 2]));
+  a[10] = fmaxf(__uint_as_float(s[30]), __uint_as_float(s[31]));
+  const float b0 = fmax3f(a[0], a[1], a[2]), b1 = fmax3f(a[3], a[4], a[5]), b2 = fmax3f(a[6], a[7], a[8]);
+  const float b3 = fmaxf(a[9], a[10]);
+  return fmaxf(fmax3f(b0, b1, b2), b3);
 }
 
 // ---------------------------------------------------------------------------
