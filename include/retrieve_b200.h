@@ -331,6 +331,17 @@ RB_API int rb_bits_to_pm1_e4m3(const int64_t* bits, int N, int W, uint8_t* out, 
 RB_API int rb_workspace_device_error(const void* workspace, size_t workspace_bytes, int* err_out);
 
 /*
+ * Test aid for the bounded waits: launches one CTA whose producer, MMA and
+ * epilogue roles each wait, through the scan kernels' own bounded wait, on an
+ * mbarrier that nothing completes, with a limit of limit_ns (1 us .. 2 s) in
+ * place of the kernels' 2 s. The first role to give up writes its timeout code
+ * (1 producer, 2 MMA, 3 epilogue) to the error word at the end of `workspace`
+ * (read it with rb_workspace_device_error) and the kernel returns. No
+ * counterpart in the reference.
+ */
+RB_API int rb_wait_probe(int64_t limit_ns, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Row-sharded search with one threshold for all shards (no counterpart in the
  * reference, which is single-GPU). A shard of N of the n_total corpus rows:
  *

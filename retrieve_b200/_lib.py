@@ -64,6 +64,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "rb_merge_topk": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_size, _vp]),
     "rb_set_profile_events": (_c_int, [_vp, _vp]),
     "rb_workspace_device_error": (_c_int, [_vp, _c_size, ctypes.POINTER(_c_int)]),
+    "rb_wait_probe": (_c_int, [_c_i64, _vp, _c_size, _vp]),
     "rb_dense_seed_sample": (
         _c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _c_size, _vp]
     ),

@@ -163,8 +163,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return done != 0;
 }
 // Waits for the phase with the given parity to complete. Returns false when
-// the wait ran past kWaitLimitNs or another role of the CTA raised `abort`.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// the wait ran past `limit_ns` (kWaitLimitNs unless a caller passes a shorter
+// limit) or another role of the CTA raised `abort`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -175,7 +177,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 16; ++i)
       if (mbar_try_wait(addr, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 

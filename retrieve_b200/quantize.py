@@ -28,8 +28,6 @@ from retrieve_b200 import _lib, ops
 
 _lib.lib()  # no fallback: a missing library fails the import
 
-_CHUNK_ROWS = 1 << 16  # rows projected at a time in the 1-bit builds
-
 
 def _stream(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
@@ -92,76 +90,98 @@ def pack_signs(values: Tensor) -> Tensor:
     return out.view(*prefix, d // 64)
 
 
-def _pack_chunked(embs: Tensor, w: int, project) -> Tensor:
-    bits = torch.empty((embs.shape[0], w), dtype=torch.int64, device=embs.device)
-    for start in range(0, embs.shape[0], _CHUNK_ROWS):
-        bits[start : start + _CHUNK_ROWS] = pack_signs(project(embs[start : start + _CHUNK_ROWS]))
-    return bits
+# --- 1-bit codes ------------------------------------------------------------------------------
+# A 1-bit code is the sign pattern of a random linear sketch of the embedding, packed by
+# ``pack_signs``. The sketches are drawn from a torch generator seeded like the reference's
+# builds (the same draws in the same order, on the embeddings' device), so a table and its
+# queries built here carry the reference's bits; everything around the draws (blocking,
+# packing, validation) is this module's own.
+
+_BLOCK_ROWS = 1 << 16  # table rows sketched per block: bounds the fp32 sketch buffer
 
 
-def _simhash_r(d: int, k_bits: int, seed: int, device: torch.device) -> Tensor:
-    g = torch.Generator(device=device).manual_seed(int(seed))
-    return torch.randn(k_bits, d, generator=g, device=device)
+def _matrix(x: Tensor, what: str) -> None:
+    if x.dim() != 2:
+        raise ValueError(f"{what} must be a 2-D [rows, dim] tensor, got shape {tuple(x.shape)}")
+    _cuda(x)
+
+
+def _codes(embs: Tensor, n_bits: int, sketch) -> Tensor:
+    """``[N, n_bits // 64]`` int64 sign words of ``sketch(embs)``, one row block at a time."""
+    n = embs.shape[0]
+    out = torch.empty((n, n_bits // 64), dtype=torch.int64, device=embs.device)
+    lo = 0
+    while lo < n:
+        hi = min(n, lo + _BLOCK_ROWS)
+        out[lo:hi] = pack_signs(sketch(embs[lo:hi]))
+        lo = hi
+    return out
+
+
+def _gaussian_sketch(d: int, n_bits: int, seed: int, device: torch.device) -> Tensor:
+    """SimHash's ``[n_bits, D]`` N(0, 1) projection: one ``randn`` from a generator seeded
+    with ``seed`` on ``device`` (indexing/quantize.py:143-145 draws it so)."""
+    gen = torch.Generator(device=device).manual_seed(int(seed))
+    return torch.randn(n_bits, d, generator=gen, device=device)
 
 
 def quantize_simhash_1bit(embs: Tensor, k_bits: int, seed: int = 0) -> tuple[Tensor, Tensor]:
-    """SimHash codes ``(bits [N, k_bits // 64] int64, r [k_bits, D] fp32)``."""
-    if embs.dim() != 2:
-        raise ValueError(f"expected 2-D [N, D] embeddings, got shape {tuple(embs.shape)}")
-    if k_bits % 64 != 0:
-        raise ValueError(f"k_bits must be a multiple of 64, got {k_bits}")
-    _cuda(embs)
-    r = _simhash_r(embs.shape[1], k_bits, seed, embs.device)
-    return _pack_chunked(embs, k_bits // 64, lambda x: x @ r.t()), r
+    """SimHash codes ``(bits [N, k_bits // 64] int64, r [k_bits, D] fp32)``: bit ``j`` of a
+    row is the sign of its dot with row ``j`` of ``r``."""
+    _matrix(embs, "embs")
+    if k_bits <= 0 or k_bits % 64:
+        raise ValueError(f"SimHash codes are packed in 64-bit words: k_bits={k_bits} is not a positive multiple "
+                         "of 64")
+    r = _gaussian_sketch(embs.shape[1], k_bits, seed, embs.device)
+    return _codes(embs, k_bits, lambda rows: rows @ r.t()), r
 
 
 def project_simhash_1bit_query(query: Tensor, r: Tensor) -> Tensor:
-    """The same projection for a query batch: ``[B, k_bits // 64]`` int64."""
-    if query.dim() != 2:
-        raise ValueError(f"expected 2-D [B, D] query, got shape {tuple(query.shape)}")
-    _cuda(query)
+    """A query batch's SimHash code under the table's ``r``: ``[B, k_bits // 64]`` int64."""
+    _matrix(query, "query")
     return pack_signs(query @ r.t())
 
 
-def _oporp_k_bits(d: int, k_bits: int) -> int:
-    if k_bits == 0:
-        k_bits = d
-    if d % k_bits != 0:
-        raise ValueError(f"k_bits must divide D; got k_bits={k_bits}, D={d}")
-    if k_bits % 64 != 0:
-        raise ValueError(f"k_bits (D when 0) must be a multiple of 64, got {k_bits}")
-    return k_bits
+def _oporp_bits(d: int, k_bits: int) -> int:
+    """Sign-OPORP's code length: ``k_bits`` (0: one bit per coordinate), which must split the
+    ``d`` coordinates into equal bins and fill whole 64-bit words."""
+    bits = d if k_bits == 0 else k_bits
+    if bits <= 0 or d % bits:
+        raise ValueError(f"Sign-OPORP bins the {d} coordinates into k_bits equal groups: {bits} does not divide {d}")
+    if bits % 64:
+        raise ValueError(f"Sign-OPORP codes are packed in 64-bit words: k_bits={bits} is not a multiple of 64")
+    return bits
 
 
-def _oporp_params(d: int, seed: int, device: torch.device) -> tuple[Tensor, Tensor]:
-    g = torch.Generator(device=device)
-    g.manual_seed(int(seed))
-    signs = torch.randint(0, 2, (d,), generator=g, device=device, dtype=torch.int8) * 2 - 1
-    perm = torch.randperm(d, generator=g, device=device)
-    return signs, perm
+def _oporp_draws(d: int, seed: int, device: torch.device) -> tuple[Tensor, Tensor]:
+    """The random sign flips (int8 +-1) and the coordinate permutation, drawn in that order
+    from one generator seeded with ``seed`` on ``device`` (the reference's order,
+    indexing/quantize.py:55-60: a ``randint`` then a ``randperm``)."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(int(seed))
+    flips = torch.randint(0, 2, (d,), generator=gen, device=device, dtype=torch.int8) * 2 - 1
+    order = torch.randperm(d, generator=gen, device=device)
+    return flips, order
 
 
-def _oporp_sketch(x: Tensor, signs: Tensor, perm: Tensor, k_bits: int) -> Tensor:
-    n, d = x.shape
-    proj = (x * signs.to(x.dtype)).index_select(1, perm)
-    binned = proj.view(n, k_bits, d // k_bits).sum(dim=-1)
-    return binned / binned.norm(dim=-1, keepdim=True).clamp_min(1e-8)
+def _oporp_sketch(rows: Tensor, flips: Tensor, order: Tensor, n_bits: int) -> Tensor:
+    """Flip, permute, sum each run of ``D / n_bits`` consecutive coordinates into one bin, and
+    scale every row to unit norm (norms below 1e-8 taken as 1e-8): the reference's arithmetic
+    (indexing/quantize.py:97-105), so each bin's sign is the reference's bit."""
+    permuted = (rows * flips.to(rows.dtype))[:, order]
+    bins = permuted.reshape(rows.shape[0], n_bits, -1).sum(dim=-1)
+    return bins / bins.norm(dim=-1, keepdim=True).clamp_min(1e-8)
 
 
 def quantize_oporp_1bit(embs: Tensor, seed: int = 0, k_bits: int = 0) -> tuple[Tensor, Tensor, Tensor]:
     """Sign-OPORP codes ``(bits [N, k_bits // 64] int64, signs [D] int8, perm [D] int64)``."""
-    if embs.dim() != 2:
-        raise ValueError(f"expected 2-D [N, D] embeddings, got shape {tuple(embs.shape)}")
-    _cuda(embs)
-    k_bits = _oporp_k_bits(embs.shape[1], k_bits)
-    signs, perm = _oporp_params(embs.shape[1], seed, embs.device)
-    bits = _pack_chunked(embs, k_bits // 64, lambda x: _oporp_sketch(x, signs, perm, k_bits))
-    return bits, signs, perm
+    _matrix(embs, "embs")
+    n_bits = _oporp_bits(embs.shape[1], k_bits)
+    flips, order = _oporp_draws(embs.shape[1], seed, embs.device)
+    return _codes(embs, n_bits, lambda rows: _oporp_sketch(rows, flips, order, n_bits)), flips, order
 
 
 def project_oporp_1bit_query(query: Tensor, signs: Tensor, perm: Tensor, k_bits: int = 0) -> Tensor:
-    """The same Sign-OPORP projection for a query batch."""
-    if query.dim() != 2:
-        raise ValueError(f"expected 2-D [B, D] query, got shape {tuple(query.shape)}")
-    _cuda(query)
-    return pack_signs(_oporp_sketch(query, signs, perm, _oporp_k_bits(query.shape[1], k_bits)))
+    """A query batch's Sign-OPORP code under the table's ``signs`` and ``perm``."""
+    _matrix(query, "query")
+    return pack_signs(_oporp_sketch(query, signs, perm, _oporp_bits(query.shape[1], k_bits)))

@@ -144,3 +144,45 @@ def test_sharded_ivf_search_equals_single_search(world, masked):
     for r in range(world):
         ids, scores = out[r]
         assert np.array_equal(ids, want_i[:, :k_sel]) and np.array_equal(scores, want_s[:, :k_sel])
+
+
+def _leaving_worker(rank, world, port, q, x, k, out):
+    """Step 1 on every rank; then rank 1 leaves between steps (no collective of step 2
+    in flight) and rank 0's step 2 must end with an error from the process group's
+    short timeout instead of waiting for good."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import time
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    from oracle.dense import dense_topk
+
+    lo, hi = shard_bounds(x.shape[0], world, rank)
+    li, ls = dense_topk(q, x[lo:hi], k)
+    li = np.where(li >= 0, li + lo, -1)
+    exchange_and_merge(torch.from_numpy(li), torch.from_numpy(ls), k, merge=_oracle_merge)
+    out[f"step1_{rank}"] = True
+    if rank == 1:
+        time.sleep(8)  # gone for longer than the timeout: never joins step 2
+        out["left"] = True
+        return
+    t0 = time.monotonic()
+    try:
+        exchange_and_merge(torch.from_numpy(li), torch.from_numpy(ls), k, merge=_oracle_merge)
+        out["step2_0"] = "completed"
+    except Exception as exc:  # noqa: BLE001  (the timeout surfaces as a backend-specific error type)
+        out["step2_0"] = type(exc).__name__
+    out["waited_s"] = time.monotonic() - t0
+
+
+def test_rank_leaving_between_steps_ends_the_next_exchange_with_an_error():
+    g = torch.Generator().manual_seed(5)
+    q = torch.randint(-3, 4, (8, 32), generator=g).float().numpy()
+    x = torch.randint(-3, 4, (2001, 32), generator=g).float().numpy()
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_leaving_worker, args=(2, 29611, q, x, 20, out), nprocs=2, join=True, start_method="spawn")
+    assert out["step1_0"] and out["step1_1"] and out["left"]
+    assert out["step2_0"] != "completed"
+    assert out["waited_s"] < 30.0
