@@ -340,8 +340,10 @@ static CandPlan cand_plan(int B, int P) {
 
 static size_t cand_ws_bytes(int B, int P) {
   const CandPlan pl = cand_plan(B, P);
-  return align_up(static_cast<size_t>(B) * pl.n_lists * kCandCap * sizeof(uint2), 256) +
-         align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
+  const size_t lists = align_up(static_cast<size_t>(B) * pl.n_lists * kCandCap * sizeof(uint2), 256) +
+                       align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
+  // the Hamming candidate scan past 224 winners runs the counting select (W <= 16, k <= P)
+  return std::max(lists, ham_select_ws_bytes(B, P, 16, P));
 }
 
 // The int8 scan's list capacity: 256 entries up to k = 224, 1280 (40 a lane) up to k = 1024.
@@ -420,7 +422,7 @@ int rb_candidate_topk(int kind, const void* query, int query_dtype, const void* 
     set_last_error("candidate_topk: bad sizes");
     return RB_ERR_INVALID_ARG;
   }
-  if (k > 1024) {
+  if (kind == 0 && k > 1024) {
     set_last_error("candidate_topk: k > 1024 is not supported");
     return RB_ERR_UNSUPPORTED;
   }
@@ -434,15 +436,19 @@ int rb_candidate_topk(int kind, const void* query, int query_dtype, const void* 
   }
   const int k_sel = (kind == 1) ? std::min(k, std::max(P, 0)) : k;
   if (B == 0 || k_sel == 0) return RB_OK;
-  if (kind == 1 && k_sel > kCandCap - 32) {
-    set_last_error("candidate_topk: min(k, P) > 224 is not supported on the candidate path");
-    return RB_ERR_UNSUPPORTED;
-  }
   if (workspace == nullptr || workspace_bytes < cand_ws_bytes(B, P)) {
     set_last_error("candidate_topk: workspace too small");
     return RB_ERR_WORKSPACE;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kind == 1 && k_sel > kCandCap - 32) {  // more winners than the lists hold: the counting select
+    if (D > 16) {
+      set_last_error("candidate_topk: the Hamming candidate scan takes at most 16 words");
+      return RB_ERR_UNSUPPORTED;
+    }
+    return ham_select_topk(static_cast<const uint64_t*>(query), static_cast<const uint64_t*>(items), N, D,
+                           positive_indices, P, counts, B, k_sel, out_ids, out_scores, workspace, workspace_bytes, s);
+  }
   const CandPlan pl = cand_plan(B, P);
   uint2* lists = static_cast<uint2*>(workspace);
   int* lcounts = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
@@ -475,7 +481,7 @@ int rb_hamming_topk_workspace_size(int B, int N, int W, int k, size_t* bytes) {
     set_last_error("hamming_topk_workspace_size: bad arguments");
     return RB_ERR_INVALID_ARG;
   }
-  *bytes = ham_ws_bytes(B, N, k);
+  *bytes = (k > 1024 || (W & 1)) ? ham_select_ws_bytes(B, N, W, k) : ham_ws_bytes(B, N, k);
   return RB_OK;
 }
 
@@ -485,12 +491,8 @@ int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, int B, 
     set_last_error("hamming_topk: bad sizes");
     return RB_ERR_INVALID_ARG;
   }
-  if (W > kHamMaxW || (W & 1)) {
-    set_last_error("hamming_topk: W must be even and <= 16 words");
-    return RB_ERR_UNSUPPORTED;
-  }
-  if (k > 1024) {
-    set_last_error("hamming_topk: k > 1024 is not supported by the full-scan kernel");
+  if (W > kHamMaxW) {
+    set_last_error("hamming_topk: at most 16 words");
     return RB_ERR_UNSUPPORTED;
   }
   if (B == 0) return RB_OK;
@@ -498,6 +500,14 @@ int rb_hamming_topk(const int64_t* query_bits, const int64_t* item_bits, int B, 
   if (N == 0) {
     fill_empty(out_ids, out_scores, static_cast<size_t>(B) * k, s);
     return check_launch();
+  }
+  if (k > 1024 || (W & 1)) {  // past the list kernel (k, or an odd word count): the counting select
+    if (workspace == nullptr || workspace_bytes < ham_select_ws_bytes(B, N, W, k)) {
+      set_last_error("hamming_topk: workspace too small");
+      return RB_ERR_WORKSPACE;
+    }
+    return ham_select_topk(reinterpret_cast<const uint64_t*>(query_bits), reinterpret_cast<const uint64_t*>(item_bits),
+                           N, W, nullptr, N, nullptr, B, k, out_ids, out_scores, workspace, workspace_bytes, s);
   }
   if (workspace == nullptr || workspace_bytes < ham_ws_bytes(B, N, k)) {
     set_last_error("hamming_topk: workspace too small");

@@ -67,6 +67,14 @@ int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const
 
 void fill_empty_pairs(uint2* out, size_t n, cudaStream_t stream);
 
+// Exact Hamming top-k by counting select (ham_select.cu), any k: over the N rows of
+// `items` (pos null) or over each row's candidate slots pos[b, :counts[b]] (P wide).
+// Ties go to the lower row / slot. W <= 16 words.
+size_t ham_select_ws_bytes(int B, int L, int W, int k);
+int ham_select_topk(const uint64_t* qbits, const uint64_t* items, int N, int W, const int64_t* pos, int P,
+                    const int64_t* counts, int B, int k, int64_t* out_ids, float* out_scores, void* ws,
+                    size_t ws_bytes, cudaStream_t s);
+
 int merge_shard_lists(const int64_t* ids, const float* scores, int W, int B, int kin, int k, int64_t* out_ids,
                       float* out_scores, void* ws, cudaStream_t stream);
 size_t merge_shard_ws_bytes(int W, int B, int kin);

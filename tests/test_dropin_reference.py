@@ -193,7 +193,8 @@ def test_linr_v3_matches_the_torch_backend():
     _repoint()
     from retrieve.modules.linr import LiNRV3
 
-    ours, ref, q, _ = _linr_pair(LiNRV3, 50, False, candidate_pool=2000)
+    ours, ref, q, _ = _linr_pair(LiNRV3, 50, False)  # the reference's default pool (5000)
+    assert ours.stage1.k == 5000
     _close_topk(*ours(q), *ref(q))
 
 
@@ -274,9 +275,12 @@ def test_silvertorch_module_on_this_library(filter_mode):
     if filter_mode == "exact":  # the module's own exact layout and the prepared query attrs
         exact = (m.item_clause_attrs.cpu().numpy(), m.clause_slots.cpu().numpy(), m.clause_is_reverse.cpu().numpy(),
                  prepared.query_attrs.cpu().numpy())
+    # the module's score path: the default OfficialConfig scores on the fp16 path
+    cfg = m.official
+    div = -1 if cfg.score_path == "int32" else (cfg.divisor or ivf.default_divisor(d))
     want_i, want_s = ivf.search(q.cpu().numpy(), probe.cpu().numpy(), m.cluster_offsets.cpu().numpy(),
                                 m.cluster_sizes.cpu().numpy(), m.item_codes.cpu().numpy(),
                                 m.sort_perm.cpu().numpy(), m.global_scale.reshape(-1).cpu().numpy(), k,
-                                m._probe_width, exact=exact)
+                                m._probe_width, divisor_for_int8=div, exact=exact)
     assert np.array_equal(scores.cpu().numpy(), want_s)
     assert np.array_equal(ids.cpu().numpy(), want_i)

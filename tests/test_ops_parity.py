@@ -147,6 +147,35 @@ def test_oporp_full_exact(b, n, w, k):
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
 
 
+@pytest.mark.parametrize("b,n,w,k", [(4, 20_000, 2, 3000), (3, 9000, 3, 100), (2, 5000, 1, 5000), (5, 70_000, 8, 1500)])
+def test_oporp_full_counting_select_exact(b, n, w, k):
+    """k past the list kernel (or an odd word count): the counting select, bit for bit the
+    oracle with ties to the lower row (w = 1 leaves 65 distinct scores: ties at every rank)."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(n + w)
+    qb = torch.randint(-(2**63), 2**63 - 1, (b, w), generator=g, dtype=torch.int64)
+    xb = torch.randint(-(2**63), 2**63 - 1, (n, w), generator=g, dtype=torch.int64)
+    ids, scores = ops.oporp_1bit_match_topk_full(qb.cuda(), xb.cuda(), k)
+    ref_ids, ref_scores = knn.oporp_full(qb.numpy(), xb.numpy(), k)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+
+
+def test_oporp_indirect_counting_select_exact():
+    """min(k, P) past 224 (LiNR V3's candidate pools, 5000 by default): the counting select over
+    each row's candidate slots, ragged counts included, bit for bit the oracle."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(77)
+    b, n, w, p, k = 6, 30_000, 2, 3000, 2000
+    qb = torch.randint(-(2**63), 2**63 - 1, (b, w), generator=g, dtype=torch.int64)
+    xb = torch.randint(-(2**63), 2**63 - 1, (n, w), generator=g, dtype=torch.int64)
+    pos = torch.stack([torch.randperm(n, generator=g)[:p] for _ in range(b)])
+    counts = torch.tensor([3000, 2500, 2000, 1999, 10, 0])
+    ids, scores = ops.oporp_1bit_match_topk_indirect(qb.cuda(), xb.cuda(), k, pos.cuda(), counts.cuda())
+    ref_ids, ref_scores = knn.oporp_indirect(qb.numpy(), xb.numpy(), k, pos.numpy(), counts.numpy())
+    assert ids.shape == (b, k)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+
+
 def test_oporp_indirect_exact_golden_inputs():
     ops = _ops()
     qb, xb, pos, counts = gi.oporp_inputs()
