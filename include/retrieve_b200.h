@@ -266,8 +266,12 @@ typedef struct {
  * (LiNR V1 with its filter, retrieve/src/retrieve/modules/linr.py:75-79, and the
  * bloom-filtered scan): items failing the predicate never enter the top-k; rows
  * with fewer than k passing items end in -1 / -inf. Other arguments and limits
- * as rb_dense_topk; workspace as rb_dense_topk_workspace_size.
+ * as rb_dense_topk. Workspace: rb_dense_topk_filtered_workspace_size, which for
+ * the Bloom modes adds room for the words bit-sliced (8 bytes an item), so that
+ * the scans test a 32-item chunk per term with one AND; a workspace of
+ * rb_dense_topk_workspace_size bytes still works, testing item by item.
  */
+RB_API int rb_dense_topk_filtered_workspace_size(int B, int N, int D, int dtype, int k, int mode, size_t* bytes);
 RB_API int rb_dense_topk_filtered(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
                                   int64_t id_offset, const rb_filter* filter, int64_t* out_ids, float* out_scores,
                                   void* workspace, size_t workspace_bytes, void* stream);

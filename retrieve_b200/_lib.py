@@ -52,6 +52,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int,
         [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp, _c_size, _vp],
     ),
+    "rb_dense_topk_filtered_workspace_size": (
+        _c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size)]
+    ),
     "rb_dense_topk_filtered": (
         _c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_size, _vp]
     ),

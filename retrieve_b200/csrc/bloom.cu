@@ -37,6 +37,46 @@ __global__ void bloom_build_kernel(const int64_t* __restrict__ attrs, int N, int
   }
 }
 
+// The per-item words bit-sliced for the filtered dense scan: per 32-item chunk c,
+// word p (of 64) holds bit p of items 32 c .. 32 c + 31 (bit j = item 32 c + j);
+// chunks past N (up to whole 128-item tiles) are zero. One warp per chunk: 64
+// ballots, then lane l stores words l and l + 32.
+__global__ void bloom_slices_kernel(const uint64_t* __restrict__ words, int64_t N, int64_t n_chunks,
+                                    uint32_t* __restrict__ slices) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); c < n_chunks;
+       c += warps) {
+    const int64_t item = 32 * c + lane;
+    const uint64_t w = item < N ? words[item] : 0ull;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int pos = 0; pos < 32; ++pos) {
+      const uint32_t b0 = __ballot_sync(0xffffffffu, (w >> pos) & 1ull);
+      const uint32_t b1 = __ballot_sync(0xffffffffu, (w >> (pos + 32)) & 1ull);
+      if (lane == pos) {
+        lo = b0;
+        hi = b1;
+      }
+    }
+    slices[64 * c + lane] = lo;
+    slices[64 * c + 32 + lane] = hi;
+  }
+}
+
+size_t bloom_slices_bytes(int64_t N) {
+  const int64_t tiles = (N + 127) / 128;
+  return static_cast<size_t>(tiles) * 4 * 64 * sizeof(uint32_t);
+}
+
+int bloom_slices(const uint64_t* words, int64_t N, uint32_t* slices, cudaStream_t stream) {
+  const int64_t n_chunks = (N + 127) / 128 * 4;
+  if (n_chunks == 0) return RB_OK;
+  const int64_t blocks = std::min<int64_t>((n_chunks + 7) / 8, 4096);
+  bloom_slices_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(words, N, n_chunks, slices);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_ERR_CUDA;
+}
+
 // ---------------------------------------------------------------------------
 // SilverTorch's bundle-major bloom index (st::bloom_index_build and the CUDA-only
 // st::bloom_index_build_fixed; silvertorch/ops/csrc/bloom_indexer.cpp:26-114,

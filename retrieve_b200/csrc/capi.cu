@@ -124,6 +124,18 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
     return fail(RB_ERR_UNSUPPORTED, "dense_topk_filtered: k <= 384 and rows of up to 256 bytes");
   const size_t need = dense_workspace_bytes(B, N, k, row_bytes, elem >= 2);
   if (workspace == nullptr || workspace_bytes < need) return fail(RB_ERR_WORKSPACE, "dense_topk: workspace too small");
+  // A Bloom filter with room for its bit-sliced words (rb_dense_topk_filtered_workspace_size):
+  // they go where a workspace of exactly `need` bytes keeps its error word, and the scans
+  // test 32 items per term and AND. A smaller workspace keeps the per-item test.
+  FilterArgs sliced_filter;
+  if (filter != nullptr && (filter->mode == kFilterBloom || filter->mode == kFilterBloomRecheck) &&
+      filter->slices == nullptr && workspace_bytes >= need + bloom_slices_bytes(N)) {
+    sliced_filter = *filter;
+    uint32_t* slices = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + need - 256);
+    if (bloom_slices(filter->bloom, N, slices, stream) != RB_OK) return fail(RB_ERR_CUDA, "bloom slices launch failed");
+    sliced_filter.slices = slices;
+    filter = &sliced_filter;
+  }
 
   DensePlan pl;
   dense_plan(B, N, k, row_bytes, pl, shared ? shared->n_total : N, elem >= 2);
@@ -221,12 +233,21 @@ int rb_dense_topk(const void* queries, const void* items, int B, int N, int D, i
                          out_scores, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+int rb_dense_topk_filtered_workspace_size(int B, int N, int D, int dtype, int k, int mode, size_t* bytes) {
+  const int rc = rb_dense_topk_workspace_size(B, N, D, dtype, k, bytes);
+  if (rc != RB_OK) return rc;
+  if (mode < RB_FILTER_NONE || mode > RB_FILTER_BLOOM_RECHECK)
+    return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered_workspace_size: unknown filter mode");
+  if (mode == RB_FILTER_BLOOM || mode == RB_FILTER_BLOOM_RECHECK) *bytes += bloom_slices_bytes(N);
+  return RB_OK;
+}
+
 int rb_dense_topk_filtered(const void* queries, const void* items, int B, int N, int D, int dtype, int k,
                            int64_t id_offset, const rb_filter* filter, int64_t* out_ids, float* out_scores,
                            void* workspace, size_t workspace_bytes, void* stream) {
   if (dtype != RB_F16 && dtype != RB_BF16) return fail(RB_ERR_TYPE, "dense_topk_filtered: dtype must be f16 or bf16");
   if (filter == nullptr) return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: filter is null");
-  FilterArgs f;
+  FilterArgs f{};
   f.mode = filter->mode;
   f.terms = static_cast<const PredTerm*>(filter->terms);
   f.n_terms = filter->n_terms;

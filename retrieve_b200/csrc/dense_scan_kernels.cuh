@@ -64,16 +64,20 @@ struct alignas(64) DenseScanParams {
   int k, cap;
 };
 
-template <int KB, int NG, int STAGES>
+// Bit-sliced Bloom words of one 128-item tile: 4 chunks x 64 words.
+constexpr int kTileSliceWords = 4 * 64;
+
+template <int KB, int NG, int STAGES, bool FILT = false>
 struct DenseSmemLayout {
   static constexpr int kOpTile = kQTile * 128;  // bytes of one 128-row x 128-byte K-block
   static constexpr int kA = NG * KB * kOpTile;
   static constexpr int kB = STAGES * KB * kOpTile;
   static constexpr int kEpiWarps = 4 * NG;
   static constexpr int kHist = kEpiWarps * 256 * 4;
+  static constexpr int kSlices = FILT ? kEpiWarps * kTileSliceWords * 4 : 0;  // one tile's slices a warp
   static constexpr int kBar = (2 * STAGES + 2 + 4 + 1) * 8;
   static constexpr int kMisc = 16;
-  static constexpr int kTotal = kA + kB + kHist + kBar + kMisc + 1024;  // + alignment slack
+  static constexpr int kTotal = kA + kB + kHist + kSlices + kBar + kMisc + 1024;  // + alignment slack
 };
 
 __device__ __forceinline__ void split_range(int split, int n_splits, int pass_tiles, int& lo, int& hi) {
@@ -108,10 +112,15 @@ __device__ __forceinline__ float raw_to_float(uint32_t raw) {
 
 // `stage` is the calling warp's 1 KB of shared scratch (its list-compaction
 // histogram, idle here): the int8 path stages the tile's 128 item scales in it.
+// The filtered variants (FILT) with `use_sl` test the Bloom form of the query's
+// predicate (`st`) on the tile's bit-sliced Bloom words `sl` (shared memory, 64
+// words a chunk), a chunk of 32 items per term and AND; the exact form (recheck
+// mode), and queries without `use_sl`, test item by item from global memory.
 template <int MODE, int NCH, int ELEM, bool FILT, int KB>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
-                                               uint2* list, uint32_t* stage) {
+                                               uint2* list, uint32_t* stage, const uint32_t* sl,
+                                               const SlicedTerms& st, bool use_sl) {
   if constexpr (ELEM == 2) {
     const float qs = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
     const bool unit_x = p.x_scale == nullptr;
@@ -167,7 +176,13 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         const uint32_t id0 = row0 + ch * 32;
         const uint32_t n_in = id0 >= static_cast<uint32_t>(p.N) ? 0u : min(32u, static_cast<uint32_t>(p.N) - id0);
         const uint32_t valid = n_in == 32 ? 0xffffffffu : ((1u << n_in) - 1u);
-        const uint32_t pm = pred_pass_bits(p.filter, q, id0, valid);
+        uint32_t pm;
+        if (use_sl) {
+          pm = bloom_chunk_mask(sl + ch * 64, st) & valid;
+          if (p.filter.mode == kFilterBloomRecheck) pm = pred_exact_bits(p.filter, q, id0, pm);
+        } else {
+          pm = pred_pass_bits(p.filter, q, id0, valid);
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (!((pm >> j) & 1u)) r[ch][j] = 0x7fc00000u;
@@ -195,12 +210,29 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
     if (__any_sync(RB_FULL_MASK, valid_q && all >= thresh)) {
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
+        if constexpr (FILT) {
+          // the Bloom test of the chunks the score test keeps: failing items
+          // become NaN, and the chunk's max is taken again over the others
+          if (__any_sync(RB_FULL_MASK, use_sl && cm[ch] >= thresh)) {
+            if (use_sl) {
+              const uint32_t pm = bloom_chunk_mask(sl + ch * 64, st);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (!((pm >> j) & 1u)) r[ch][j] = 0x7fc00000u;
+              cm[ch] = max32(r[ch]);
+            }
+          }
+        }
         if (valid_q && cm[ch] >= thresh) {
           if constexpr (!FILT) {
             append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
           } else {
             const uint32_t id0 = row0 + ch * 32;
-            const uint32_t pm = pred_pass_bits(p.filter, q, id0, chunk_pass_bits(r[ch], thresh));
+            uint32_t pm = chunk_pass_bits(r[ch], thresh);
+            if (!use_sl)
+              pm = pred_pass_bits(p.filter, q, id0, pm);
+            else if (p.filter.mode == kFilterBloomRecheck)
+              pm = pred_exact_bits(p.filter, q, id0, pm);
             append_chunk_mask(list, count, r[ch], pm, id0);
           }
         }
@@ -212,7 +244,7 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
 template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 __global__ void __launch_bounds__(64 + 128 * NG, 1)
     dense_scan_kernel(const __grid_constant__ DenseScanParams p) {
-  using L = DenseSmemLayout<KB, NG, STAGES>;
+  using L = DenseSmemLayout<KB, NG, STAGES, FILT>;
   constexpr int kElemBytes = (ELEM == 2 || ELEM == 4) ? 1 : 2;
   constexpr int kElemsPerKBlock = 128 / kElemBytes;
   constexpr int kKSteps = 128 / 32;  // MMA K = 32 bytes per instruction
@@ -226,7 +258,8 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + L::kA;
   uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist);
+  uint32_t* slices_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB + L::kHist);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist + L::kSlices);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* a_full = bars + 2 * STAGES;
@@ -386,6 +419,10 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
     const int g = ew >> 2;               // query group
     const int quad = warp & 3;           // TMEM lane quadrant this warp may access
     uint32_t* hist = hist_all + ew * 256;
+    // filtered variants: this warp's copy of the current tile's bit-sliced Bloom words
+    uint32_t* sl = slices_all + ew * kTileSliceWords;
+    const bool sliced = FILT && p.filter.slices != nullptr &&
+                        (p.filter.mode == kFilterBloom || p.filter.mode == kFilterBloomRecheck);
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
@@ -395,6 +432,15 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
       const bool valid_q = q < p.B;
       float thresh = (valid_q && p.seed != nullptr) ? p.seed[q] : -INFINITY;
       int count = 0;
+      // filtered variants: the query's Bloom terms for the bit-sliced test
+      SlicedTerms st{};
+      bool use_sl = false;
+      if constexpr (FILT) {
+        if (sliced) {
+          st = load_sliced_terms(p.filter, q, valid_q);
+          use_sl = valid_q && st.ok;
+        }
+      }
       uint2* list = p.lists + (static_cast<size_t>(valid_q ? q : 0) * p.n_splits + split) * p.cap;
       int lo, hi;
       split_range(split, p.n_splits, p.pass_tiles, lo, hi);
@@ -405,6 +451,16 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
           // across the (non-inlined) compaction.
           const bool need = valid_q && (count > p.cap - kTileItems);
           if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        }
+        if constexpr (FILT) {
+          if (sliced) {  // this tile's slices, 32 bytes a lane, while the MMA runs
+            const size_t tile = static_cast<size_t>(pt * p.tile_stride + p.tile_offset);
+            const uint32_t* src = p.filter.slices + tile * kTileSliceWords + lane * 8;
+            __syncwarp();  // every lane is done with the previous tile's slices
+            cp_async16(sl + lane * 8, src);
+            cp_async16(sl + lane * 8 + 4, src + 4);
+            cp_async_commit();
+          }
         }
         if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
           if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
@@ -425,7 +481,14 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist);
+        if constexpr (FILT) {
+          if (sliced) {
+            cp_async_wait_all();
+            __syncwarp();
+          }
+        }
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
+                                                use_sl);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -438,6 +501,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
     }
   }
 
+  if constexpr (FILT) cp_async_wait_all();  // slice copies of an early exit land before the CTA ends
   __syncwarp();
   tc_fence_before();
   __syncthreads();
@@ -460,7 +524,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
 // ===========================================================================
 constexpr int kHalfItems = kTileItems / 2;
 
-template <int KB, int NG, int STAGES>
+template <int KB, int NG, int STAGES, bool FILT = false>
 struct Dense2SmLayout {
   static constexpr int kATile = kQTile * 128;     // 128 query rows x 128 bytes
   static constexpr int kBTile = kHalfItems * 128;  // 64 item rows x 128 bytes
@@ -468,15 +532,16 @@ struct Dense2SmLayout {
   static constexpr int kB = STAGES * KB * kBTile;
   static constexpr int kEpiWarps = 4 * NG;  // (group, lane quadrant)
   static constexpr int kHist = kEpiWarps * 256 * 4;
+  static constexpr int kSlices = FILT ? kEpiWarps * kTileSliceWords * 4 : 0;  // one tile's slices a warp
   static constexpr int kBar = (2 * STAGES + 2 + 2 * 4 + 1) * 8;
   static constexpr int kMisc = 16;
-  static constexpr int kTotal = kA + kB + kHist + kBar + kMisc + 1024;
+  static constexpr int kTotal = kA + kB + kHist + kSlices + kBar + kMisc + 1024;
 };
 
 template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     dense_scan_2sm_kernel(const __grid_constant__ DenseScanParams p) {
-  using L = Dense2SmLayout<KB, NG, STAGES>;
+  using L = Dense2SmLayout<KB, NG, STAGES, FILT>;
   constexpr int kElemBytes = (ELEM == 2 || ELEM == 4) ? 1 : 2;
   constexpr int kElemsPerKBlock = 128 / kElemBytes;
   constexpr int kKSteps = 128 / 32;
@@ -491,7 +556,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + L::kA;
   uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist);
+  uint32_t* slices_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB + L::kHist);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist + L::kSlices);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* a_full = bars + 2 * STAGES;
@@ -679,6 +745,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     const int g = ew >> 2;
     const int quad = warp & 3;
     uint32_t* hist = hist_all + ew * 256;
+    // filtered variants: this warp's copy of the current tile's bit-sliced Bloom words
+    uint32_t* sl = slices_all + ew * kTileSliceWords;
+    const bool sliced = FILT && p.filter.slices != nullptr &&
+                        (p.filter.mode == kFilterBloom || p.filter.mode == kFilterBloomRecheck);
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
@@ -689,6 +759,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       const bool valid_q = q < p.B;
       float thresh = (valid_q && p.seed != nullptr) ? p.seed[q] : -INFINITY;
       int count = 0;
+      // filtered variants: the query's Bloom terms for the bit-sliced test
+      SlicedTerms st{};
+      bool use_sl = false;
+      if constexpr (FILT) {
+        if (sliced) {
+          st = load_sliced_terms(p.filter, q, valid_q);
+          use_sl = valid_q && st.ok;
+        }
+      }
       const size_t list_id = static_cast<size_t>(valid_q ? q : 0) * p.n_splits + split;
       uint2* list = p.lists + list_id * p.cap;
       int lo, hi;
@@ -698,6 +777,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         if constexpr (MODE == 0) {
           const bool need = valid_q && (count > p.cap - kTileItems);
           if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
+        }
+        if constexpr (FILT) {
+          if (sliced) {  // this tile's slices, 32 bytes a lane, while the MMA runs
+            const size_t tile = static_cast<size_t>(pt * p.tile_stride + p.tile_offset);
+            const uint32_t* src = p.filter.slices + tile * kTileSliceWords + lane * 8;
+            __syncwarp();  // every lane is done with the previous tile's slices
+            cp_async16(sl + lane * 8, src);
+            cp_async16(sl + lane * 8 + 4, src + 4);
+            cp_async_commit();
+          }
         }
         if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
           if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
@@ -716,7 +805,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
-        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist);
+        if constexpr (FILT) {
+          if (sliced) {
+            cp_async_wait_all();
+            __syncwarp();
+          }
+        }
+        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
+                                                use_sl);
         if (++acc == kAcc) {
           acc = 0;
           acc_phase ^= 1;
@@ -731,6 +827,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     }
   }
 
+  if constexpr (FILT) cp_async_wait_all();  // slice copies of an early exit land before the CTA ends
   __syncwarp();
   if (*abort_flag) {
     // Error path only: a load of this CTA may still be in flight towards its
@@ -749,7 +846,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
 
 template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaStream_t stream) {
-  using L = DenseSmemLayout<KB, NG, STAGES>;
+  using L = DenseSmemLayout<KB, NG, STAGES, FILT>;
   auto kern = dense_scan_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
@@ -759,7 +856,7 @@ static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaS
 
 template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 static cudaError_t launch_dense_scan_2sm(const DenseScanParams& prm, int n_pairs, cudaStream_t stream) {
-  using L = Dense2SmLayout<KB, NG, STAGES>;
+  using L = Dense2SmLayout<KB, NG, STAGES, FILT>;
   auto kern = dense_scan_2sm_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
@@ -791,6 +888,10 @@ static cudaError_t launch_1sm_variant(int mode, int epl, const DenseScanParams& 
 
 // CTA pairs of the 2-SM kernel that fit on the device at once (dense_scan_e1.cu).
 int dense_max_pairs();
+
+// 2-D K-major tensor map over rows x cols elements (elem: 0 fp16, 1 bf16, 2 / 4
+// one-byte codes), boxes of box_rows x 128 bytes, 128-byte swizzle.
+bool make_tmap_2d(CUtensorMap* map, const void* base, int elem, uint64_t rows, uint64_t cols, int box_rows);
 
 // Launches the pass for one element type; false if no variant matches.
 bool dense_launch_e0(bool two_sm, int mode, int kb, int ng, bool filtered, int epl, const DenseScanParams& prm,

@@ -46,7 +46,7 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // 2-D K-major tensor map: rows x cols elements, box box_rows x 128 bytes, 128-B swizzle.
-static bool make_tmap(CUtensorMap* map, const void* base, int elem, uint64_t rows, uint64_t cols, int box_rows) {
+bool make_tmap_2d(CUtensorMap* map, const void* base, int elem, uint64_t rows, uint64_t cols, int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const int eb = (elem == 2 || elem == 4) ? 1 : 2;
@@ -158,8 +158,8 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
   const int eb = (elem == 2 || elem == 4) ? 1 : 2;
   const int row_bytes = D * eb;
   const int item_box = pl.two_sm ? kHalfItems : kTileItems;
-  if (!make_tmap(&prm.tmap_q, q, elem, static_cast<uint64_t>(B), static_cast<uint64_t>(D), kQTile) ||
-      !make_tmap(&prm.tmap_x, x, elem, static_cast<uint64_t>(N), static_cast<uint64_t>(D), item_box)) {
+  if (!make_tmap_2d(&prm.tmap_q, q, elem, static_cast<uint64_t>(B), static_cast<uint64_t>(D), kQTile) ||
+      !make_tmap_2d(&prm.tmap_x, x, elem, static_cast<uint64_t>(N), static_cast<uint64_t>(D), item_box)) {
     set_last_error("cuTensorMapEncodeTiled failed (alignment or driver entry point)");
     return RB_ERR_CUDA;
   }

@@ -34,6 +34,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <cstdint>
 
@@ -916,6 +917,71 @@ static int st_row_search(const float* query, int B, int D, const int64_t* probe_
   return launch_status();
 }
 
+namespace rb {
+
+// The tensor-core form of the grouped scan (ivf_tc.cu): int8 rows of 128, 256 or
+// 512 bytes, no bloom plans, k_sel <= 128 or > 224 (lists of 256 / 1280 entries).
+bool ivf_tc_supported(int D, int k_sel, bool bloom);
+int ivf_tc_cap(int k_sel);
+size_t ivf_tc_ws_bytes(int64_t n_pairs, int64_t n_lists, int D);
+int ivf_tc_scan(const int8_t* q_codes, int B, int D, int P, const int8_t* item_codes, int64_t N,
+                const int64_t* offsets, const int64_t* sizes, int64_t n_lists, const int32_t* pairs,
+                const int64_t* cpo, const int64_t* ctask, const int64_t* head, const int64_t* tail, int width,
+                int k_sel, int divisor, const FilterSet& fs, uint2* lists, int* list_counts, int* err, void* ws,
+                cudaStream_t s);
+
+// The SIMT grouped scan (ivf_group_scan_kernel) over the tasks of G pairs.
+static int group_scan(const int8_t* item_codes, int64_t N, int D, const int8_t* q_codes, const int64_t* probe_ids,
+                      int P, const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
+                      const int32_t* pairs, const int64_t* cpo, const int64_t* ctask, const int64_t* head,
+                      const int64_t* tail, int width, int G, int k_sel, int divisor_for_int8, const FilterSet& fs,
+                      uint2* lists, int* lcounts, int64_t n_pairs, cudaStream_t s) {
+  int rc = RB_OK;
+  const size_t smem = group_smem_bytes(D);
+  // the limit is a per-device setting of the function: raised once on each device used
+  static std::atomic<uint64_t> smem_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool known = dev >= 0 && dev < 64;
+  if (!known || !((smem_set.load() >> dev) & 1u)) {
+    // the largest tile (D = 1024) needs about 150 KB of the 227 KB a block may opt into
+    const int most = static_cast<int>(group_smem_bytes(kMaxSearchD));
+    const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    if (cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap, false>, attr, most) != cudaSuccess ||
+        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap, true>, attr, most) != cudaSuccess ||
+        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge, false>, attr, most) != cudaSuccess ||
+        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge, true>, attr, most) != cudaSuccess) {
+      set_last_error("st::search: cannot raise the grouped scan's shared memory limit");
+      return RB_ERR_CUDA;
+    }
+    if (known) smem_set.fetch_or(uint64_t{1} << dev);
+  }
+  const int64_t max_tasks = (n_pairs + G - 1) / G + std::min<int64_t>(n_lists, n_pairs);
+  GroupArgs ga{item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask,
+               head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts};
+  const unsigned grid_tasks = static_cast<unsigned>(max_tasks);
+  const bool bloom = fs.bloom.index != nullptr;
+  ProfileEvents& pe = profile_events();
+  if (pe.start) record_profile_event(pe.start, s);
+  if (group_cap(k_sel) == kGroupCap) {
+    if (bloom)
+      ivf_group_scan_kernel<kGroupCap, true><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+    else
+      ivf_group_scan_kernel<kGroupCap, false><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+  } else {
+    if (bloom)
+      ivf_group_scan_kernel<kGroupCapLarge, true><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+    else
+      ivf_group_scan_kernel<kGroupCapLarge, false><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+  }
+  rc = launch_status();
+  if (rc != RB_OK) return rc;
+  if (pe.stop) record_profile_event(pe.stop, s);
+  return RB_OK;
+}
+
+}  // namespace rb
+
 extern "C" {
 
 int rb_st_search(const float* query, int B, int D, const int64_t* probe_ids, int P, const int64_t* cluster_offsets,
@@ -946,7 +1012,7 @@ int rb_st_search_shard(const float* query, int B, int D, const int64_t* probe_id
 // cpo, ctask [L + 1] | pairs [B P] int32 | head, tail [B P] | row totals [B] |
 // lists [B P, cap] | list counts [B P] | winner slots, raw [B, k_sel].
 struct GroupWs {
-  size_t codes, scales, cnt, fill, cpo, ctask, pairs, head, tail, total, lists, lcounts, slots, raw, bytes;
+  size_t codes, scales, cnt, fill, cpo, ctask, pairs, head, tail, total, lists, lcounts, slots, raw, tc, err, bytes;
 };
 
 static GroupWs group_ws_layout(int B, int D, int P, int64_t n_lists, int k_sel) {
@@ -972,6 +1038,9 @@ static GroupWs group_ws_layout(int B, int D, int P, int64_t n_lists, int k_sel) 
   w.lcounts = take(pairs * sizeof(int));
   w.slots = take(static_cast<size_t>(B) * k_sel * sizeof(int64_t));
   w.raw = take(static_cast<size_t>(B) * k_sel * sizeof(float));
+  // the tensor-core scan's gathered query blocks and task records, where it may run
+  w.tc = take(ivf_tc_supported(D, k_sel, false) ? ivf_tc_ws_bytes(static_cast<int64_t>(B) * P, n_lists, D) : 0);
+  w.err = take(256);  // the device error word of the tensor-core scan's bounded waits, last
   w.bytes = off;
   return w;
 }
@@ -1034,7 +1103,9 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   int64_t* slots = reinterpret_cast<int64_t*>(ws + lay.slots);
   float* raw = reinterpret_cast<float*>(ws + lay.raw);
   const int64_t n_pairs = static_cast<int64_t>(B) * P;
-  const int G = group_pairs_per_task(D);
+  const bool bloom = fs.bloom.index != nullptr;
+  const bool tc = ivf_tc_supported(D, k_sel, bloom);
+  const int G = tc ? 128 : group_pairs_per_task(D);
   cudaMemsetAsync(cnt, 0, static_cast<size_t>(n_lists) * sizeof(int), s);
   cudaMemsetAsync(fill, 0, static_cast<size_t>(n_lists) * sizeof(int), s);
   cudaMemsetAsync(lcounts, 0, static_cast<size_t>(n_pairs) * sizeof(int), s);
@@ -1046,47 +1117,21 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
                                                       width, head, tail, total);
   rc = launch_status();
   if (rc != RB_OK) return rc;
-  const size_t smem = group_smem_bytes(D);
-  // the limit is a per-device setting of the function: raised once on each device used
-  static bool smem_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const bool known = dev >= 0 && dev < 64;
-  if (!known || !smem_set[dev]) {
-    // the largest tile (D = 1024) needs about 150 KB of the 227 KB a block may opt into
-    const int most = static_cast<int>(group_smem_bytes(kMaxSearchD));
-    const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
-    if (cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap, false>, attr, most) != cudaSuccess ||
-        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCap, true>, attr, most) != cudaSuccess ||
-        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge, false>, attr, most) != cudaSuccess ||
-        cudaFuncSetAttribute(ivf_group_scan_kernel<kGroupCapLarge, true>, attr, most) != cudaSuccess) {
-      set_last_error("st::search: cannot raise the grouped scan's shared memory limit");
-      return RB_ERR_CUDA;
-    }
-    if (known) smem_set[dev] = true;
-  }
-  const int64_t max_tasks = (n_pairs + G - 1) / G + std::min<int64_t>(n_lists, n_pairs);
-  GroupArgs ga{item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask,
-               head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts};
-  const unsigned grid_tasks = static_cast<unsigned>(max_tasks);
-  const bool bloom = fs.bloom.index != nullptr;
-  ProfileEvents& pe = profile_events();
-  if (pe.start) record_profile_event(pe.start, s);
-  if (group_cap(k_sel) == kGroupCap) {
-    if (bloom)
-      ivf_group_scan_kernel<kGroupCap, true><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
-    else
-      ivf_group_scan_kernel<kGroupCap, false><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+  if (tc) {
+    int* err = reinterpret_cast<int*>(ws + lay.err);
+    cudaMemsetAsync(err, 0, sizeof(int), s);
+    ProfileEvents& pe = profile_events();
+    if (pe.start) record_profile_event(pe.start, s);
+    rc = ivf_tc_scan(q_codes, B, D, P, item_codes, N, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask, head,
+                     tail, width, k_sel, divisor_for_int8, fs, lists, lcounts, err, ws + lay.tc, s);
+    if (rc != RB_OK) return rc;
+    if (pe.stop) record_profile_event(pe.stop, s);
   } else {
-    if (bloom)
-      ivf_group_scan_kernel<kGroupCapLarge, true><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
-    else
-      ivf_group_scan_kernel<kGroupCapLarge, false><<<grid_tasks, kGroupThreads, smem, s>>>(ga);
+    rc = group_scan(item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo,
+                    ctask, head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts, n_pairs, s);
+    if (rc != RB_OK) return rc;
   }
-  rc = launch_status();
-  if (rc != RB_OK) return rc;
-  if (pe.stop) record_profile_event(pe.stop, s);
-  rc = merge_lists(lists, lcounts, B, P, group_cap(k_sel), k_sel, 0, slots, raw, nullptr, s);
+  rc = merge_lists(lists, lcounts, B, P, tc ? ivf_tc_cap(k_sel) : group_cap(k_sel), k_sel, 0, slots, raw, nullptr, s);
   if (rc != RB_OK) return rc;
   const int64_t n = static_cast<int64_t>(B) * k;
   const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4096));
@@ -1095,6 +1140,7 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
                                                 global_scale, divisor_for_int8, B, k, out_ids, out_scores);
   return launch_status();
 }
+
 
 static size_t finish_ws(int B, int D, int P, size_t* at) {
   size_t off = 0;

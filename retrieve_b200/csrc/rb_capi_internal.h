@@ -67,6 +67,11 @@ int cand_i8_topk(const int8_t* q_codes, const int8_t* items, int N, int D, const
 
 void fill_empty_pairs(uint2* out, size_t n, cudaStream_t stream);
 
+// Bit-sliced Bloom words for the filtered dense scan (bloom.cu): bytes for N items
+// (whole 128-item tiles) and the device build from the per-item words.
+size_t bloom_slices_bytes(int64_t N);
+int bloom_slices(const uint64_t* words, int64_t N, uint32_t* slices, cudaStream_t stream);
+
 // Exact Hamming top-k by counting select (ham_select.cu), any k: over the N rows of
 // `items` (pos null) or over each row's candidate slots pos[b, :counts[b]] (P wide).
 // Ties go to the lower row / slot. W <= 16 words.

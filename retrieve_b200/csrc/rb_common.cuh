@@ -99,7 +99,82 @@ struct FilterArgs {
   const int64_t* attrs;   // [N, C, A] int64, -1 pads (exact / recheck)
   int C, A;
   const uint64_t* bloom;  // [N] (bloom / recheck)
+  // The same Bloom words bit-sliced, or null: per 32-item chunk 64 words, word p
+  // holding bit p of the chunk's 32 items (bit j = item 32 chunk + j), whole
+  // 128-item tiles (zero words past N). The scans then test a chunk's 32 items
+  // against a term with one AND of the term's positions' words.
+  const uint32_t* slices;
 };
+
+// A query's Bloom terms for the bit-sliced test, one word a term: bits 0-23 up
+// to 4 bit positions (6 bits each), 24-26 their count, 27 negate, 28 last term
+// of its group (the terms come grouped). `ok` is false when a term's mask has
+// more than 4 bits or a group's terms are not contiguous: that query then uses
+// the per-item test.
+struct SlicedTerms {
+  uint32_t t[kMaxTerms];
+  int n;
+  bool ok;
+};
+
+__device__ __forceinline__ SlicedTerms load_sliced_terms(const FilterArgs& f, int q, bool valid_q) {
+  SlicedTerms st;
+  st.n = valid_q ? min(f.n_terms[q], kMaxTerms) : 0;
+  st.ok = true;
+  const PredTerm* tm = f.terms + static_cast<size_t>(q) * kMaxTerms;
+  uint32_t closed = 0;  // groups whose run of terms has ended
+#pragma unroll
+  for (int i = 0; i < kMaxTerms; ++i) {
+    st.t[i] = 0;
+    if (i < st.n) {
+      uint64_t m = tm[i].bloom_mask;
+      const int flags = tm[i].flags;
+      const int bits = __popcll(m);
+      if (bits > 4 || (closed >> (flags & 7)) & 1u) st.ok = false;  // wide mask, or a group split in two runs
+      uint32_t w = 0;
+      for (int j = 0; j < 4 && m != 0; ++j) {
+        const int p = __ffsll(static_cast<long long>(m)) - 1;
+        w |= static_cast<uint32_t>(p) << (6 * j);
+        m &= m - 1;
+      }
+      w |= static_cast<uint32_t>(min(bits, 4)) << 24;
+      if (flags & 8) w |= 1u << 27;
+      const bool last = (i + 1 == st.n) || ((tm[i + 1].flags & 7) != (flags & 7));
+      if (last) {
+        w |= 1u << 28;
+        closed |= 1u << (flags & 7);
+      }
+      st.t[i] = w;
+    }
+  }
+  return st;
+}
+
+// Bit j set iff item j of the chunk passes the Bloom form of the predicate,
+// from the chunk's 64 slice words `sl` (shared memory). An empty predicate
+// passes everything.
+__device__ __forceinline__ uint32_t bloom_chunk_mask(const uint32_t* sl, const SlicedTerms& st) {
+  uint32_t res = 0xffffffffu, cur = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxTerms; ++i) {
+    if (i < st.n) {
+      const uint32_t w = st.t[i];
+      const int cnt = (w >> 24) & 7;
+      uint32_t m = 0xffffffffu;
+      if (cnt > 0) m &= sl[w & 63];
+      if (cnt > 1) m &= sl[(w >> 6) & 63];
+      if (cnt > 2) m &= sl[(w >> 12) & 63];
+      if (cnt > 3) m &= sl[(w >> 18) & 63];
+      if (w & (1u << 27)) m = ~m;
+      cur |= m;
+      if (w & (1u << 28)) {
+        res &= cur;
+        cur = 0;
+      }
+    }
+  }
+  return res;
+}
 
 __device__ __forceinline__ bool pred_eval_one(const PredTerm* t, int nt, bool use_bloom, const int64_t* row,
                                               int A, uint64_t word) {
@@ -134,6 +209,15 @@ __device__ __forceinline__ bool pred_pass(const FilterArgs& f, int q, uint32_t i
     ok = pred_eval_one(t, nt, false, f.attrs + static_cast<size_t>(id) * f.C * f.A, f.A, 0ull);
   return ok;
 }
+
+// ---------------------------------------------------------------------------
+// cp.async (16-byte global -> shared copies, completed per thread).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // mbarrier (shared::cta) with bounded waits.

@@ -164,6 +164,22 @@ __device__ __forceinline__ uint32_t pred_pass_bits(const FilterArgs& f, int q, u
 }
 
 
+// Of the items id0 + j with bit j set in sel, those that pass query q's exact
+// (attribute) predicate; the Bloom form is not consulted.
+__device__ __forceinline__ uint32_t pred_exact_bits(const FilterArgs& f, int q, uint32_t id0, uint32_t sel) {
+  const PredTerm* t = f.terms + static_cast<size_t>(q) * kMaxTerms;
+  const int nt = f.n_terms[q];
+  if (nt == 0) return sel;
+  uint32_t out = 0;
+  while (sel) {
+    const int j = __ffs(sel) - 1;
+    sel &= sel - 1;
+    const int64_t* row = f.attrs + static_cast<size_t>(id0 + j) * f.C * f.A;
+    if (pred_eval_one(t, nt, false, row, f.A, 0ull)) out |= 1u << j;
+  }
+  return out;
+}
+
 // Appends the entries s[j] >= thresh of a 32-item chunk (items id0 + j).
 // Padding slots hold NaN, which never passes.
 __device__ __forceinline__ void append_chunk_bits(uint2* list, int& count, float thresh, const uint32_t (&s)[32],

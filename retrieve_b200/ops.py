@@ -286,7 +286,8 @@ def dense_topk_filtered(
     lib = _lib.lib()
     code = _DTYPE_CODE[item_embs.dtype]
     nb = ctypes.c_size_t(0)
-    _lib.check(lib.rb_dense_topk_workspace_size(b, n, q.shape[1], code, k, ctypes.byref(nb)), "dense_topk_filtered")
+    _lib.check(lib.rb_dense_topk_filtered_workspace_size(b, n, q.shape[1], code, k, m, ctypes.byref(nb)),
+               "dense_topk_filtered")
     ws = torch.empty(max(int(nb.value), 256), dtype=torch.uint8, device=dev)
     rc = lib.rb_dense_topk_filtered(_ptr(q), _ptr(item_embs), b, n, q.shape[1], code, k, 0, ctypes.addressof(f),
                                     _ptr(ids), _ptr(scores), _ptr(ws), ws.numel(), _stream_ptr(dev))

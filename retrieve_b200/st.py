@@ -78,9 +78,32 @@ def search(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_si
            item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
            clause_is_reverse: Tensor | None = None,
            query_clause_attrs: Tensor | None = None) -> tuple[Tensor, Tensor]:
-    """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``, scored row by row
-    (each row's probed positions expanded, then the int8 candidate scan). Takes the
-    schema's 23 arguments positionally or by name."""
+    """``st::search`` → ``(ids int64 [B, k], scores fp32 [B, k])``. Takes the schema's 23
+    arguments positionally or by name. Scored by cluster (``search_grouped``: each probed
+    cluster read once per group of probing rows) up to 1024 probes a row unless bloom plans
+    are given without the exact recheck; else row by row (each row's probed positions
+    expanded, then the int8 candidate scan), where the bloom plans are evaluated once per
+    64-doc column. Both give the same results."""
+    filters = dict(zip(FILTER_ARGS, (filtering_bit_mask, bloom_index, bloom_bundle_b_offsets, plans, plan_count,
+                                     max_stack_size, query_plan_index, bloom_k, hash_k, item_clause_attrs,
+                                     clause_slots, clause_is_reverse, query_clause_attrs)))
+    bloom_only = plans is not None and query_clause_attrs is None
+    grouped = not bloom_only and probe_ids.dim() == 2 and probe_ids.shape[1] <= 1024
+    return _search(grouped, query, probe_ids, cluster_offsets, cluster_sizes, item_codes, sort_perm, global_scale, k,
+                   max_tensor_size_per_row, divisor_for_int8, filters)
+
+
+def search_rows(query: Tensor, probe_ids: Tensor, cluster_offsets: Tensor, cluster_sizes: Tensor,
+                item_codes: Tensor, sort_perm: Tensor, global_scale: Tensor, k: int, max_tensor_size_per_row: int,
+                divisor_for_int8: int = -1, filtering_bit_mask: Tensor | None = None,
+                bloom_index: Tensor | None = None, bloom_bundle_b_offsets: Tensor | None = None,
+                plans: Tensor | None = None, plan_count: int = 0, max_stack_size: int = 0,
+                query_plan_index: Tensor | None = None, bloom_k: int = 0, hash_k: int = 0,
+                item_clause_attrs: Tensor | None = None, clause_slots: Tensor | None = None,
+                clause_is_reverse: Tensor | None = None,
+                query_clause_attrs: Tensor | None = None) -> tuple[Tensor, Tensor]:
+    """``st::search`` scored row by row (``rb_st_search``) whatever the filter: the same
+    arguments and results as ``search``."""
     filters = dict(zip(FILTER_ARGS, (filtering_bit_mask, bloom_index, bloom_bundle_b_offsets, plans, plan_count,
                                      max_stack_size, query_plan_index, bloom_k, hash_k, item_clause_attrs,
                                      clause_slots, clause_is_reverse, query_clause_attrs)))

@@ -83,3 +83,56 @@ def test_linr_clause_queries_filtered():
                                           attrs.cuda(), None)
     ref_ids, ref_scores = _oracle(q, x, k, filters.clause_mask(attrs.numpy(), rev.numpy(), qa.numpy()))
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+
+
+@pytest.mark.parametrize("mode", ["bloom", "bloom_recheck"])
+def test_sliced_bloom_test_equals_the_per_item_test(mode):
+    """The Bloom words bit-sliced (a workspace of rb_dense_topk_filtered_workspace_size) and
+    tested item by item (a workspace of rb_dense_topk_workspace_size) give the same top-k;
+    rows whose terms split a group (the per-item test on those queries) too."""
+    import ctypes
+
+    from retrieve_b200 import _lib, ops
+
+    b, n, k = 200, 50_000, 100
+    attrs = gi.zipf_attrs(n, seed=11)
+    attrs3 = attrs[:, :, None].contiguous().cuda()
+    q, x = make_int_rows(b, 128, seed=5).cuda(), make_int_rows(n, 128, seed=6).cuda()
+    exprs = [EXPRS[i % len(EXPRS)] for i in range(b)]
+    preds = P.from_expressions(exprs)
+    terms = preds.terms.clone()
+    rec = terms.view(b, 8, 24)
+    nt = preds.n_terms
+    for r in range(0, b, 7):  # rotate a row's terms: a group's terms are then not contiguous
+        if nt[r] >= 3:
+            rec[r, : nt[r]] = torch.roll(rec[r, : nt[r]].clone(), 1, dims=0)
+    terms, nt = terms.cuda(), nt.to(torch.int32).cuda()
+    words = ops.bloom_build(attrs3, 3)
+    m = ops.FILTER_MODES[mode]
+    lib = _lib.lib()
+    f = ops._RbFilter(m, terms.data_ptr(), nt.data_ptr(), attrs3.data_ptr(), attrs3.shape[1], attrs3.shape[2],
+                      words.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out = []
+    for sliced in (False, True):
+        nb = ctypes.c_size_t(0)
+        if sliced:
+            _lib.check(lib.rb_dense_topk_filtered_workspace_size(b, n, 128, _lib.RB_BF16, k, m, ctypes.byref(nb)),
+                       "ws")
+        else:
+            _lib.check(lib.rb_dense_topk_workspace_size(b, n, 128, _lib.RB_BF16, k, ctypes.byref(nb)), "ws")
+        ws = torch.empty(nb.value, dtype=torch.uint8, device="cuda")
+        ids = torch.empty(b, k, dtype=torch.int64, device="cuda")
+        sc = torch.empty(b, k, dtype=torch.float32, device="cuda")
+        _lib.check(lib.rb_dense_topk_filtered(ctypes.c_void_p(q.data_ptr()), ctypes.c_void_p(x.data_ptr()), b, n, 128,
+                                              _lib.RB_BF16, k, 0, ctypes.addressof(f), ctypes.c_void_p(ids.data_ptr()),
+                                              ctypes.c_void_p(sc.data_ptr()), ctypes.c_void_p(ws.data_ptr()), nb.value,
+                                              stream), "filtered")
+        out.append((ids.cpu().numpy(), sc.cpu().numpy()))
+    assert np.array_equal(out[0][1], out[1][1]) and np.array_equal(out[0][0], out[1][0])
+    wn = words.cpu().numpy().view(np.uint64)
+    masks = _masks(exprs, b, words=wn)
+    if mode == "bloom_recheck":
+        masks &= _masks(exprs, b, attrs=attrs.numpy())
+    ref_ids, ref_scores = _oracle(q.cpu(), x.cpu(), k, masks)
+    assert_topk_exact(out[1][0], out[1][1], ref_ids, ref_scores)

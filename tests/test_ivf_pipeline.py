@@ -58,7 +58,7 @@ def test_built_index_searches_like_the_restatement(grouped):
     stack, (data, plan_off) = torch.ops.st.parse_expression_query_batch(exprs, torch.ones(b), 7, True, 5)
     blob = torch.from_numpy(ivf.plan_blob(data.numpy(), plan_off.numpy(), b)).cuda()
 
-    fn = st.search_grouped if grouped else torch.ops.st.search
+    fn = st.search_grouped if grouped else st.search_rows
     args = (q, probe, offsets, sizes, codes, perm, gst, k, width)
     ids, scores = fn(*args)
     host = [t.cpu().numpy() for t in (q, probe, offsets, sizes, codes, perm)]

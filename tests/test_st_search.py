@@ -204,7 +204,7 @@ def test_search_binds_the_adapters_positional_call(grouped):
     _st()
     from retrieve_b200 import st
 
-    fn = st.search_grouped if grouped else st.search
+    fn = st.search_grouped if grouped else st.search_rows
     q = torch.zeros(2, 64)
     probe = torch.zeros(2, 1, dtype=torch.int64)
     off, sz = torch.tensor([0, 4]), torch.tensor([4])
@@ -556,7 +556,7 @@ def test_search_bloom_plans(grouped, plan_index):
     rows = np.arange(b) % n_plans if plan_index else np.arange(b)
     blob = ivf.plan_blob(BLOOM["plan_data"], BLOOM["plan_offsets"], n_plans)
     t = [torch.from_numpy(x).cuda() for x in (q, probe, offsets, sizes, codes, perm)]
-    fn = st.search_grouped if grouped else st.search
+    fn = st.search_grouped if grouped else st.search_rows
     ids, scores = fn(*t, torch.tensor(0.02).cuda(), 50, width,
                      bloom_index=torch.from_numpy(BLOOM["bloom_index"]).cuda(),
                      bloom_bundle_b_offsets=torch.from_numpy(BLOOM["bundle_b_offsets"]).cuda(),
@@ -567,6 +567,79 @@ def test_search_bloom_plans(grouped, plan_index):
     words = ivf.pack_mask_high_first(want_mask[rows])
     want = ivf.search(q, probe, offsets, sizes, codes, perm, np.float32(0.02), 50, width, filtering_bit_mask=words)
     _assert_exact(ids.cpu().numpy(), scores.cpu().numpy(), *want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ci", range(N_CASES))
+def test_registered_op_equals_the_row_scorer_for_every_filter(ci):
+    """torch.ops.st.search picks its scorer (grouped unless bloom plans come without the exact
+    recheck, or more than 1024 probes a row): through the dispatcher, with all 23 arguments
+    positional as the reference's adapter passes them, it equals the row scorer bit for bit
+    unfiltered, with a full-N mask and with the exact clauses."""
+    _st()
+    from retrieve_b200 import st
+
+    g, meta = _case(ci)
+    t = [torch.from_numpy(np.ascontiguousarray(g[key])).cuda()
+         for key in ("query", "probe", "offsets", "sizes", "codes", "sort_perm")]
+    gs = torch.from_numpy(g["gs"]).cuda()
+    k, width, div = meta["k"], meta["width"], meta["div"]
+    n, b = g["codes"].shape[0], meta["b"]
+    rng = np.random.default_rng(100 + ci)
+    mask = torch.from_numpy(ivf.pack_mask_high_first(rng.random((b, n)) < 0.6)).cuda()
+    _, rev, _, slots_t, clause_slots, qq = _exact_inputs(rng, n, b)
+    exact = (torch.from_numpy(slots_t).cuda(), torch.from_numpy(clause_slots).cuda(), torch.from_numpy(rev).cuda(),
+             torch.from_numpy(qq).cuda())
+    for m, ex in ((None, None), (mask, None), (None, exact)):
+        args = (*t, gs, k, width, div, m, None, None, None, 0, 0, None, 0, 0,
+                *(ex if ex is not None else (None, None, None, None)))
+        got = torch.ops.st.search(*args)
+        want = st.search_rows(*args)
+        assert torch.equal(got[0], want[0]) and torch.equal(got[1], want[1])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("d,k", [(128, 100), (256, 10), (512, 100), (128, 300), (128, 1)])
+def test_grouped_tensor_core_scan_equals_the_row_scorer(d, k):
+    """The grouped scorer's tensor-core form (int8 rows of 128 / 256 / 512 bytes, no bloom plans):
+    ragged and empty clusters, more than 128 rows probing one cluster, fp16 and int32 raw scores,
+    unfiltered, full-N mask and exact clauses: bit for bit the row scorer and the oracle; and a
+    width that cuts rows, against the row scorer."""
+    _st()
+    from retrieve_b200 import st
+
+    rng = np.random.default_rng(d + k)
+    n_lists, b, p = 40, 300, 6
+    sizes = rng.integers(0, 700, n_lists).astype(np.int64)
+    sizes[3] = 0
+    sizes[7] = 2500
+    offsets = np.r_[0, np.cumsum(sizes)].astype(np.int64)
+    n = int(offsets[-1])
+    codes = rng.integers(-128, 128, (n, d)).astype(np.int8)
+    codes[: n // 3, : d // 2] = 1  # ties among many rows
+    perm = rng.permutation(n).astype(np.int64)
+    probe = np.argsort(rng.random((b, n_lists)), axis=1)[:, :p].astype(np.int64)
+    probe[:150, 0] = 7  # 150 rows probe the long cluster: two tasks of it
+    q = rng.standard_normal((b, d)).astype(np.float32)
+    width = 8192  # every row's probed total fits (the oracle's requirement)
+    gs = np.float32(0.013)
+    t = [torch.from_numpy(x).cuda() for x in (q, probe, offsets, sizes, codes, perm)]
+    mask = ivf.pack_mask_high_first(rng.random((b, n)) < 0.7)
+    _, rev, _, slots_t, clause_slots, qq = _exact_inputs(rng, n, b)
+    exact = dict(item_clause_attrs=torch.from_numpy(slots_t).cuda(), clause_slots=torch.from_numpy(clause_slots).cuda(),
+                 clause_is_reverse=torch.from_numpy(rev).cuda(), query_clause_attrs=torch.from_numpy(qq).cuda())
+    for div in (-1, ivf.default_divisor(d)):
+        for flt in ({}, {"filtering_bit_mask": torch.from_numpy(mask).cuda()}, exact):
+            got = st.search_grouped(*t, torch.tensor(gs).cuda(), k, width, div, **flt)
+            rows = st.search_rows(*t, torch.tensor(gs).cuda(), k, width, div, **flt)
+            assert torch.equal(got[0], rows[0]) and torch.equal(got[1], rows[1])
+            ex = (slots_t, clause_slots, rev, qq) if "item_clause_attrs" in flt else None
+            want = ivf.search(q, probe, offsets, sizes, codes, perm, gs, k, width, div,
+                              filtering_bit_mask=mask if "filtering_bit_mask" in flt else None, exact=ex)
+            _assert_exact(got[0].cpu().numpy(), got[1].cpu().numpy(), *want)
+    got = st.search_grouped(*t, torch.tensor(gs).cuda(), k, 1024)
+    rows = st.search_rows(*t, torch.tensor(gs).cuda(), k, 1024)
+    assert torch.equal(got[0], rows[0]) and torch.equal(got[1], rows[1])
 
 
 @pytest.mark.gpu
@@ -769,7 +842,7 @@ def test_search_replays_in_a_cuda_graph(grouped):
     t = {key: torch.from_numpy(np.ascontiguousarray(g[key])).cuda()
          for key in ("query", "probe", "offsets", "sizes", "codes", "sort_perm")}
     gs = torch.from_numpy(g["gs"]).cuda()
-    fn = st.search_grouped if grouped else torch.ops.st.search
+    fn = st.search_grouped if grouped else st.search_rows
     q = t["query"].clone()
 
     def call():
