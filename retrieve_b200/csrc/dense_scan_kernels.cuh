@@ -121,6 +121,9 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list, uint32_t* stage, const uint32_t* sl,
                                                const SlicedTerms& st, bool use_sl) {
+  // Chunks whose scores may pass (bit ch); the full int8 pass clears the bits of
+  // chunks it proves below the threshold before dequantizing them.
+  uint32_t live = (1u << NCH) - 1u;
   if constexpr (ELEM == 2) {
     const float qs = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
     const bool unit_x = p.x_scale == nullptr;
@@ -128,6 +131,7 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
     // once (one float4 per lane, coalesced) into shared memory, and each lane
     // then reads them as broadcasts instead of 32 dependent global loads.
     float4* sx = reinterpret_cast<float4*>(stage);
+    float lmax = 1.f, lmin = 1.f;  // this lane's 4 scales' max and min (chunk lane / 8)
     if (!unit_x) {
       const int lane = threadIdx.x & 31;
       const uint32_t id = row0 + 4 * static_cast<uint32_t>(lane);
@@ -141,10 +145,47 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         v.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
       }
       sx[lane] = v;
+      lmax = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      lmin = fminf(fminf(v.x, v.y), fminf(v.z, v.w));
+    }
+    if constexpr (MODE == 0 && NCH == 4) {
+      // A bound per chunk before any dequantization. With q_scale >= 0 and the
+      // chunk's item scales in [xmin, xmax], xmin >= 0, every rounded product is
+      // monotonic, so each score fl(fl(dot * qs) * x) is at most fl(A * xmax)
+      // (A >= 0) or fl(A * xmin) (A < 0), A = fl(fl(max dot) * qs). A chunk whose
+      // bound is below the threshold for every lane is never dequantized. NaN
+      // scales or scales below zero leave the chunk live.
+#pragma unroll
+      for (int off = 4; off >= 1; off >>= 1) {
+        lmax = fmaxf(lmax, __shfl_xor_sync(RB_FULL_MASK, lmax, off));
+        lmin = fminf(lmin, __shfl_xor_sync(RB_FULL_MASK, lmin, off));
+      }
+      uint32_t need = 0;
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const float xmax = __shfl_sync(RB_FULL_MASK, lmax, 8 * ch), xmin = __shfl_sync(RB_FULL_MASK, lmin, 8 * ch);
+        int m[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) m[i] = max(static_cast<int>(r[ch][2 * i]), static_cast<int>(r[ch][2 * i + 1]));
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1) {
+#pragma unroll
+          for (int i = 0; i < w; ++i) m[i] = max(m[2 * i], m[2 * i + 1]);
+        }
+        const float a = __fmul_rn(raw_to_float<ELEM, KB>(static_cast<uint32_t>(m[0])), qs);
+        const bool monotone = qs >= 0.f && xmin >= 0.f;
+        const float bound = a >= 0.f ? __fmul_rn(a, xmax) : __fmul_rn(a, xmin);
+        if (valid_q && (!monotone || !(bound < thresh))) need |= 1u << ch;
+      }
+      // the warp dequantizes a chunk if any lane may pass in it (the scales are shared)
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch)
+        if (!__any_sync(RB_FULL_MASK, (need >> ch) & 1u)) live &= ~(1u << ch);
     }
     __syncwarp();
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
+      if (!((live >> ch) & 1u)) continue;  // warp-uniform
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
         const float4 xs = unit_x ? make_float4(1.f, 1.f, 1.f, 1.f) : sx[ch * 8 + j4];
@@ -204,7 +245,8 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
     float all = -INFINITY;
 #pragma unroll
     for (int ch = 0; ch < NCH; ++ch) {
-      cm[ch] = max32(r[ch]);
+      // a chunk proved below the threshold: NaN, which passes no test and fmaxf ignores
+      cm[ch] = ((live >> ch) & 1u) ? max32(r[ch]) : __uint_as_float(0x7fc00000u);
       all = fmaxf(all, cm[ch]);
     }
     if (__any_sync(RB_FULL_MASK, valid_q && all >= thresh)) {
