@@ -920,7 +920,7 @@ static int st_row_search(const float* query, int B, int D, const int64_t* probe_
 namespace rb {
 
 // The tensor-core form of the grouped scan (ivf_tc.cu): int8 rows of 128, 256 or
-// 512 bytes, no bloom plans, k_sel <= 128 or > 224 (lists of 256 / 1280 entries).
+// 512 bytes, no bloom plans (lists of ivf_tc_cap entries).
 bool ivf_tc_supported(int D, int k_sel, bool bloom);
 int ivf_tc_cap(int k_sel);
 size_t ivf_tc_ws_bytes(int64_t n_pairs, int64_t n_lists, int D);
@@ -1034,7 +1034,8 @@ static GroupWs group_ws_layout(int B, int D, int P, int64_t n_lists, int k_sel) 
   w.head = take(pairs * sizeof(int64_t));
   w.tail = take(pairs * sizeof(int64_t));
   w.total = take(static_cast<size_t>(B) * sizeof(int64_t));
-  w.lists = take(pairs * group_cap(k_sel) * sizeof(uint2));
+  const int cap = std::max(group_cap(k_sel), ivf_tc_supported(D, k_sel, false) ? ivf_tc_cap(k_sel) : 0);
+  w.lists = take(pairs * cap * sizeof(uint2));
   w.lcounts = take(pairs * sizeof(int));
   w.slots = take(static_cast<size_t>(B) * k_sel * sizeof(int64_t));
   w.raw = take(static_cast<size_t>(B) * k_sel * sizeof(float));
@@ -1053,7 +1054,7 @@ int rb_st_search_grouped_workspace_size(int B, int D, int P, int64_t n_lists, in
     return RB_ERR_INVALID_ARG;
   }
   const int width = st_width(max_tensor_size_per_row);
-  *bytes = group_ws_layout(B, D, P, n_lists, std::min(k, width)).bytes;
+  *bytes = group_ws_layout(B, D, P, n_lists, std::max(std::min(k, width), 1)).bytes;  // as the search lays it out
   return RB_OK;
 }
 

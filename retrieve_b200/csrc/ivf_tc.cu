@@ -9,7 +9,8 @@
 //    shape: warp 0 loads the task's query block once and the cluster's row
 //    tiles (TMA, 128-byte swizzle) through a STAGES-deep ring; warp 1 issues the
 //    MMAs into a double-buffered TMEM accumulator (s32); warps 2-5 read one
-//    pair's 128 dots a tile (thread = pair), keep the rows of the cluster that
+//    pair's 128 dots a tile (thread = pair; the pairs dealt round the four
+//    warps), keep the rows of the cluster that
 //    land inside the row's width, rank them on the raw score (the int32 dot, or
 //    fp16(dot / divisor)) and append (raw, slot) to the pair's list in
 //    ascending slot order, testing the full-N mask or the exact clauses only
@@ -83,10 +84,13 @@ __global__ void tc_gather_kernel(const int8_t* __restrict__ q_codes, int D, int 
   const int64_t p0 = cpo[lo] + (t - ctask[lo]) * kTcRows;
   const int m = static_cast<int>(min(static_cast<int64_t>(kTcRows), cpo[lo + 1] - p0));
   if (threadIdx.x == 0) tasks[t] = TcTask{lo, p0, m, 0};
+  // pair r of the task goes to MMA row (r % 4) * 32 + r / 4: the task's pairs spread over the
+  // four TMEM lane quadrants, so all four epilogue warps share their lists' work
   const int words = D / 16;  // D is a multiple of 128 here
   int4* dst = reinterpret_cast<int4*>(out + t * kTcRows * D);
   for (int i = threadIdx.x; i < kTcRows * words; i += blockDim.x) {
-    const int r = i / words, w = i - r * words;
+    const int row = i / words, w = i - row * words;
+    const int r = (row & 31) * 4 + (row >> 5);
     int4 v = make_int4(0, 0, 0, 0);
     if (r < m) v = reinterpret_cast<const int4*>(q_codes + static_cast<int64_t>(pairs[p0 + r] / P) * D)[w];
     dst[i] = v;
@@ -290,7 +294,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
       int m;
       task_range(t, start, len, full, m, p0);
       if (len == 0) continue;  // its pairs keep the zero count they start with
-      const int r = quad * 32 + lane;  // the task's pair this lane scores
+      const int r = lane * 4 + quad;  // the task's pair this lane scores (its MMA row: quad * 32 + lane)
       const bool valid = r < m;
       const int32_t pair = valid ? p.pairs[p0 + r] : 0;
       const int64_t b = pair / p.P;
@@ -310,6 +314,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
           break;
         }
         tc_fence_after();
+        if (quad >= m) {  // no pair of this task in the warp's quadrant: release the tile at once
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1;
+          continue;
+        }
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * kTcRows);
         uint32_t v[4][32];
         __syncwarp();
@@ -389,16 +400,18 @@ cudaError_t launch_tc(const TcParams& prm, int grid, cudaStream_t s) {
 template <int KB, int STAGES>
 cudaError_t launch_tc_kb(const TcParams& prm, bool filt, bool large, int grid, cudaStream_t s) {
   if (large) return filt ? launch_tc<KB, STAGES, 40, true>(prm, grid, s) : launch_tc<KB, STAGES, 40, false>(prm, grid, s);
-  return filt ? launch_tc<KB, STAGES, 8, true>(prm, grid, s) : launch_tc<KB, STAGES, 8, false>(prm, grid, s);
+  return filt ? launch_tc<KB, STAGES, 16, true>(prm, grid, s) : launch_tc<KB, STAGES, 16, false>(prm, grid, s);
 }
 
 }  // namespace
 
 bool ivf_tc_supported(int D, int k_sel, bool bloom) {
-  return !bloom && (D == 128 || D == 256 || D == 512) && (k_sel <= 128 || k_sel > 224);
+  return !bloom && (D == 128 || D == 256 || D == 512) && k_sel <= 1024;
 }
 
-int ivf_tc_cap(int k_sel) { return k_sel <= 128 ? 256 : 1280; }
+// A pair's list holds k winners plus a whole tile of appends; the room past k + 128 spaces
+// the compactions out (a list of 512 is compacted about once per 380 appends).
+int ivf_tc_cap(int k_sel) { return k_sel <= 384 ? 512 : 1280; }
 
 size_t ivf_tc_ws_bytes(int64_t n_pairs, int64_t n_lists, int D) {
   const int64_t tasks = (n_pairs + kTcRows - 1) / kTcRows + std::min(n_lists, n_pairs);

@@ -155,13 +155,15 @@ def _leaving_worker(rank, world, port, q, x, k, out):
     import time
     from datetime import timedelta
 
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    # a generous timeout for the rendezvous (process start-up varies), a short one for the steps
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    short = dist.new_group(list(range(world)), timeout=timedelta(seconds=3))
     from oracle.dense import dense_topk
 
     lo, hi = shard_bounds(x.shape[0], world, rank)
     li, ls = dense_topk(q, x[lo:hi], k)
     li = np.where(li >= 0, li + lo, -1)
-    exchange_and_merge(torch.from_numpy(li), torch.from_numpy(ls), k, merge=_oracle_merge)
+    exchange_and_merge(torch.from_numpy(li), torch.from_numpy(ls), k, group=short, merge=_oracle_merge)
     out[f"step1_{rank}"] = True
     if rank == 1:
         time.sleep(8)  # gone for longer than the timeout: never joins step 2
@@ -169,7 +171,7 @@ def _leaving_worker(rank, world, port, q, x, k, out):
         return
     t0 = time.monotonic()
     try:
-        exchange_and_merge(torch.from_numpy(li), torch.from_numpy(ls), k, merge=_oracle_merge)
+        exchange_and_merge(torch.from_numpy(li), torch.from_numpy(ls), k, group=short, merge=_oracle_merge)
         out["step2_0"] = "completed"
     except Exception as exc:  # noqa: BLE001  (the timeout surfaces as a backend-specific error type)
         out["step2_0"] = type(exc).__name__
