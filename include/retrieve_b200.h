@@ -387,6 +387,30 @@ RB_API int rb_merge_pairs(const uint64_t* pairs, int W, int B, int kin, int k, i
                           void* stream);
 
 /*
+ * The all-gather of the row-sharded search through the peers' memory on one
+ * node, in place of NCCL's (no counterpart in the reference: it is single-GPU).
+ * Every rank allocates one exchange buffer of rb_peer_buffer_bytes(W,
+ * slot_bytes) with rb_ipc_alloc, passes the 64-byte IPC handle to its peers
+ * (any host channel) and maps theirs with rb_ipc_open. rb_peer_allgather then
+ * pushes this rank's `bytes` (a multiple of 16, at most slot_bytes) into every
+ * rank's buffer with plain peer stores, raises this rank's flag there, waits
+ * (bounded: 2 s) until every rank's flag for the step is up in its own buffer
+ * and writes the [W, bytes] stack, in rank order, to `out` (device). `bases`
+ * is a host array of the W buffers (index = rank; this rank's own allocation
+ * at `rank`); `step` (int64), `done` (int) are this rank's device counters,
+ * zeroed once, and `err` its error word (5 = a peer did not arrive in time).
+ * Every rank calls it the same number of times, on its own GPU; the step
+ * counter lives on the device, so a captured graph replays it. No multicast.
+ */
+RB_API int rb_ipc_alloc(size_t bytes, void** ptr, void* handle);
+RB_API int rb_ipc_open(const void* handle, void** ptr);
+RB_API int rb_ipc_close(void* ptr);
+RB_API int rb_ipc_free(void* ptr);
+RB_API size_t rb_peer_buffer_bytes(int W, int64_t slot_bytes);
+RB_API int rb_peer_allgather(void* const* bases, int W, int rank, int64_t slot_bytes, const void* src, int64_t bytes,
+                             int64_t* step, int* done, int* err, void* out, void* stream);
+
+/*
  * The filter of one st::search call: at most one of the three groups is set (NULL
  * pointers for the others), or pass a NULL rb_st_filter* for none.
  *   filtering_bit_mask [B, mask_words] int64 over sorted positions, high bit first

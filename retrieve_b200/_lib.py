@@ -77,6 +77,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _c_size, _vp],
     ),
     "rb_merge_pairs": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp]),
+    "rb_ipc_alloc": (_c_int, [_c_size, ctypes.POINTER(_vp), _vp]),
+    "rb_ipc_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "rb_ipc_close": (_c_int, [_vp]),
+    "rb_ipc_free": (_c_int, [_vp]),
+    "rb_peer_buffer_bytes": (_c_size, [_c_int, _c_i64]),
+    "rb_peer_allgather": (
+        _c_int, [ctypes.POINTER(_vp), _c_int, _c_int, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp]
+    ),
     "rb_quantize_int8_global_workspace_size": (_c_int, [ctypes.POINTER(_c_size)]),
     "rb_quantize_int8_global": (_c_int, [_vp, _c_i64, _c_int, _vp, _c_i64, _vp, _vp, _vp, _c_size, _vp]),
     "rb_pack_signs": (_c_int, [_vp, _c_i64, _c_int, _vp, _vp]),

@@ -17,6 +17,12 @@ Exact for any ``W``: the global top-k is contained in the union of the local
 top-k lists (the shared seed never drops a global top-k item), and a shard's
 scores do not depend on which shard scores it.
 
+The two all-gathers run through NCCL (``exchange="nccl"``) or through the peers'
+memory (``exchange="peer"``, :class:`PeerExchange`): every rank pushes its block
+into every peer's exchange buffer with plain peer stores and raises a flag there,
+and reads the stack from its own buffer once every flag is up (one node, CUDA
+IPC mappings, no multicast).
+
 The reference is single-GPU (its harness merges chunked top-k lists the same
 way on one device, evaluation/bench/oracle.py:83-92); this module is the
 multi-GPU extension of ``PostfilterKNN`` (retrieve/src/retrieve/modules/knn.py:23-76).
@@ -76,6 +82,91 @@ def exchange_and_merge(ids: Tensor, scores: Tensor, k: int, group=None, merge=No
     return (merge or merge_topk)(all_i.view(world, b, kin), all_s.view(world, b, kin), k)
 
 
+class PeerExchange:
+    """A fixed-size all-gather through the peers' memory on one node
+    (``rb_peer_allgather``): ``allgather(t)`` returns the ``[W, *t.shape]`` stack of every
+    rank's ``t`` in rank order, in a buffer owned by this object (the next call
+    overwrites it). Built collectively (every rank of ``group`` constructs it with the
+    same ``slot_bytes``); every rank then calls ``allgather`` the same number of times.
+    The step counter lives on the device, so calls captured in a CUDA graph replay."""
+
+    def __init__(self, slot_bytes: int, device: torch.device, group=None) -> None:
+        lib = _lib.lib()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.device = torch.device(device)
+        self.slot_bytes = (int(slot_bytes) + 15) // 16 * 16
+        nbytes = lib.rb_peer_buffer_bytes(self.world, self.slot_bytes)
+        own = ctypes.c_void_p(0)
+        handle = (ctypes.c_ubyte * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.rb_ipc_alloc(nbytes, ctypes.byref(own), handle), "peer exchange buffer")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        bases, self._opened = [], []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                p = ctypes.c_void_p(0)
+                _lib.check(lib.rb_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(p)),
+                           "peer exchange mapping")
+                bases.append(p.value)
+                self._opened.append(p.value)
+        self._bases = (ctypes.c_void_p * self.world)(*bases)
+        # step (int64), push-completion count (int32), error word (int32)
+        self._counters = torch.zeros(16, dtype=torch.uint8, device=self.device)
+        self._out: Tensor | None = None
+        self._stage: Tensor | None = None
+        dist.barrier(group=group)  # every buffer is zeroed and mapped before any push
+
+    def allgather(self, t: Tensor) -> Tensor:
+        t = t.contiguous()
+        nbytes = t.numel() * t.element_size()
+        padded = (nbytes + 15) // 16 * 16
+        if padded > self.slot_bytes:
+            raise ValueError(f"peer exchange: {nbytes} bytes do not fit the {self.slot_bytes}-byte slots")
+        src = t
+        if padded != nbytes:  # blocks move in 16-byte units: stage the tail
+            if self._stage is None or self._stage.numel() != padded:
+                self._stage = torch.zeros(padded, dtype=torch.uint8, device=self.device)
+            self._stage[:nbytes].copy_(t.view(-1).view(torch.uint8))
+            src = self._stage
+        if self._out is None or self._out.numel() != self.world * padded:
+            self._out = torch.empty((self.world, padded), dtype=torch.uint8, device=self.device)
+        c = self._counters.data_ptr()
+        rc = _lib.lib().rb_peer_allgather(
+            self._bases, self.world, self.rank, self.slot_bytes, ctypes.c_void_p(src.data_ptr()), padded,
+            ctypes.c_void_p(c), ctypes.c_void_p(c + 8), ctypes.c_void_p(c + 12), ctypes.c_void_p(self._out.data_ptr()),
+            ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream),
+        )
+        _lib.check(rc, "peer allgather")
+        stack = self._out if padded == nbytes else self._out[:, :nbytes].contiguous()
+        return stack.view(t.dtype).view(self.world, *t.shape)
+
+    def device_error(self) -> int:
+        """The error word: 0, or 5 when a peer's flag did not come up within the wait limit."""
+        return int(self._counters[12:16].view(torch.int32).item())
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (collective: no rank may still
+        be pushing or reading)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        lib = _lib.lib()
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                lib.rb_ipc_close(ctypes.c_void_p(p))
+            self._opened = []
+            dist.barrier(group=self.group)
+            if self._own:
+                lib.rb_ipc_free(ctypes.c_void_p(self._own))
+                self._own = 0
+
+
 class ShardedDenseTopK:
     """The local shard of a row-sharded dense index plus the exchange steps.
 
@@ -89,7 +180,12 @@ class ShardedDenseTopK:
     their union — the seed one GPU would take over the whole corpus — so each
     shard appends about 1/W of the candidates a shard-local seed would."""
 
-    def __init__(self, item_shard: Tensor, id_offset: int, k: int, group=None, n_total: int | None = None) -> None:
+    def __init__(self, item_shard: Tensor, id_offset: int, k: int, group=None, n_total: int | None = None,
+                 exchange: str = "nccl") -> None:
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange must be 'nccl' or 'peer', got {exchange!r}")
+        self.exchange = exchange
+        self._peer: dict[str, PeerExchange] = {}
         ops.check_contiguous(item_shard=item_shard)
         self.items = item_shard
         self.id_offset = int(id_offset)
@@ -129,15 +225,34 @@ class ShardedDenseTopK:
         m = self.sample_width
         vals = ops.dense_seed_sample(query, self.items, self.k, self.n_total, ws, m)
         b = vals.shape[0]
-        gathered = torch.empty((self.world * b, m), dtype=vals.dtype, device=vals.device)
-        dist.all_gather_into_tensor(gathered, vals, group=self.group)
+        gathered = self._allgather("samples", vals)
         pairs = ops.dense_topk_seeded(
             query, self.items, self.k, self.id_offset, self.n_total, gathered.view(self.world, b, m), ws,
             pairs=True,
         )
-        all_pairs = torch.empty((self.world * b, self.k), dtype=pairs.dtype, device=pairs.device)
-        dist.all_gather_into_tensor(all_pairs, pairs, group=self.group)
+        all_pairs = self._allgather("pairs", pairs)
         return ops.merge_pairs(all_pairs.view(self.world, b, self.k), self.k)
+
+    def _allgather(self, what: str, t: Tensor) -> Tensor:
+        """``[W, *t.shape]`` stack of every rank's ``t`` (NCCL, or the peers' memory)."""
+        if self.exchange == "nccl":
+            out = torch.empty((self.world * t.shape[0], *t.shape[1:]), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+            return out.view(self.world, *t.shape)
+        nbytes = t.numel() * t.element_size()
+        ex = self._peer.get(what)
+        if ex is None or ex.slot_bytes < nbytes:  # built at the first (eager) search, collectively
+            if ex is not None:
+                ex.close()
+            ex = PeerExchange(nbytes, t.device, self.group)
+            self._peer[what] = ex
+        return ex.allgather(t)
+
+    def close(self) -> None:
+        """Releases the peer exchange buffers (collective)."""
+        for ex in self._peer.values():
+            ex.close()
+        self._peer = {}
 
     def launches_per_search(self, b: int) -> int:
         """Kernels of this library one search launches (NCCL's not counted)."""
