@@ -539,7 +539,11 @@ static int st_check(int B, int D, int P, int64_t n_lists, int64_t N, int k, int 
 //     128-row tiles of the cluster staged in shared memory; each warp takes
 //     pairs and scores a whole tile for each (4 rows a lane, dp4a), appending
 //     (raw score, slot) in ascending slot order to the pair's list, so ties keep
-//     the lower slot exactly as in the row path.
+//     the lower slot exactly as in the row path. A compacted list holds k
+//     candidates of its row at or above its k-th raw score; that score goes to
+//     the row's bound (atomicMax), and every pair of the row skips what falls
+//     under the bound from its next tile on (ties kept: the other pairs' slots
+//     interleave with its own).
 //  4. merge_lists over each row's P lists, then st_group_epilogue_kernel: slot
 //     -> (probe, row in cluster) by binary search over the row's slot ends ->
 //     position -> sort_perm, and the dequantization.
@@ -647,6 +651,7 @@ struct GroupArgs {
   FilterSet f;
   uint2* lists;      // [B * P, CAP]
   int* list_counts;  // [B * P]
+  uint32_t* row_bound;  // [B] f2ord of a lower bound on the row's k-th raw score (0: none yet)
 };
 
 template <int CAP, bool BLOOM>
@@ -711,7 +716,9 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
       const int pr = s_pair[g];
       const int64_t b = pr / a.P;
       int count = s_count[g];
-      float thresh = s_thresh[g];
+      // the row's bound: the k-th score of some compacted list of the row (another pair's rows
+      // may have lower slots, so ties stay: the test is >=)
+      float thresh = fmaxf(s_thresh[g], ord2f(__ldcg(a.row_bound + b)));
       uint2* list = a.lists + static_cast<int64_t>(pr) * CAP;
       const int64_t hs = a.head[pr], ts = a.tail[pr];
       const int4* q = reinterpret_cast<const int4*>(sq + g * dp);
@@ -760,6 +767,8 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
             warp_compact_lists<CAP / 32>(list, count, thresh, lane == 0, a.k, hist[warp]);
             count = __shfl_sync(RB_FULL_MASK, count, 0);
             thresh = __shfl_sync(RB_FULL_MASK, thresh, 0);
+            // the list now holds k candidates of the row at or above one step below thresh
+            if (lane == 0) atomicMax(a.row_bound + b, f2ord(thresh) - 1u);
           }
           const bool pass2 = s >= thresh;
           const uint32_t bal2 = __ballot_sync(RB_FULL_MASK, pass2);
@@ -784,6 +793,8 @@ __global__ void __launch_bounds__(kGroupThreads) ivf_group_scan_kernel(GroupArgs
       warp_compact_lists<CAP / 32>(a.lists + static_cast<int64_t>(pr) * CAP, count, thresh, lane == 0,
                                          a.k, hist[warp]);
       count = __shfl_sync(RB_FULL_MASK, count, 0);
+      thresh = __shfl_sync(RB_FULL_MASK, thresh, 0);
+      if (lane == 0) atomicMax(a.row_bound + pr / a.P, f2ord(thresh) - 1u);
     }
     if (lane == 0) a.list_counts[pr] = count;
   }
@@ -927,15 +938,15 @@ size_t ivf_tc_ws_bytes(int64_t n_pairs, int64_t n_lists, int D);
 int ivf_tc_scan(const int8_t* q_codes, int B, int D, int P, const int8_t* item_codes, int64_t N,
                 const int64_t* offsets, const int64_t* sizes, int64_t n_lists, const int32_t* pairs,
                 const int64_t* cpo, const int64_t* ctask, const int64_t* head, const int64_t* tail, int width,
-                int k_sel, int divisor, const FilterSet& fs, uint2* lists, int* list_counts, int* err, void* ws,
-                cudaStream_t s);
+                int k_sel, int divisor, const FilterSet& fs, uint2* lists, int* list_counts, uint32_t* row_bound,
+                int* err, void* ws, cudaStream_t s);
 
 // The SIMT grouped scan (ivf_group_scan_kernel) over the tasks of G pairs.
 static int group_scan(const int8_t* item_codes, int64_t N, int D, const int8_t* q_codes, const int64_t* probe_ids,
                       int P, const int64_t* cluster_offsets, const int64_t* cluster_sizes, int64_t n_lists,
                       const int32_t* pairs, const int64_t* cpo, const int64_t* ctask, const int64_t* head,
                       const int64_t* tail, int width, int G, int k_sel, int divisor_for_int8, const FilterSet& fs,
-                      uint2* lists, int* lcounts, int64_t n_pairs, cudaStream_t s) {
+                      uint2* lists, int* lcounts, uint32_t* row_bound, int64_t n_pairs, cudaStream_t s) {
   int rc = RB_OK;
   const size_t smem = group_smem_bytes(D);
   // the limit is a per-device setting of the function: raised once on each device used
@@ -958,7 +969,7 @@ static int group_scan(const int8_t* item_codes, int64_t N, int D, const int8_t* 
   }
   const int64_t max_tasks = (n_pairs + G - 1) / G + std::min<int64_t>(n_lists, n_pairs);
   GroupArgs ga{item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask,
-               head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts};
+               head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts, row_bound};
   const unsigned grid_tasks = static_cast<unsigned>(max_tasks);
   const bool bloom = fs.bloom.index != nullptr;
   ProfileEvents& pe = profile_events();
@@ -1012,7 +1023,8 @@ int rb_st_search_shard(const float* query, int B, int D, const int64_t* probe_id
 // cpo, ctask [L + 1] | pairs [B P] int32 | head, tail [B P] | row totals [B] |
 // lists [B P, cap] | list counts [B P] | winner slots, raw [B, k_sel].
 struct GroupWs {
-  size_t codes, scales, cnt, fill, cpo, ctask, pairs, head, tail, total, lists, lcounts, slots, raw, tc, err, bytes;
+  size_t codes, scales, cnt, fill, cpo, ctask, pairs, head, tail, total, lists, lcounts, slots, raw, bound, tc, err,
+      bytes;
 };
 
 static GroupWs group_ws_layout(int B, int D, int P, int64_t n_lists, int k_sel) {
@@ -1039,6 +1051,7 @@ static GroupWs group_ws_layout(int B, int D, int P, int64_t n_lists, int k_sel) 
   w.lcounts = take(pairs * sizeof(int));
   w.slots = take(static_cast<size_t>(B) * k_sel * sizeof(int64_t));
   w.raw = take(static_cast<size_t>(B) * k_sel * sizeof(float));
+  w.bound = take(static_cast<size_t>(B) * sizeof(uint32_t));  // each row's bound on its k-th raw score
   // the tensor-core scan's gathered query blocks and task records, where it may run
   w.tc = take(ivf_tc_supported(D, k_sel, false) ? ivf_tc_ws_bytes(static_cast<int64_t>(B) * P, n_lists, D) : 0);
   w.err = take(256);  // the device error word of the tensor-core scan's bounded waits, last
@@ -1110,6 +1123,8 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
   cudaMemsetAsync(cnt, 0, static_cast<size_t>(n_lists) * sizeof(int), s);
   cudaMemsetAsync(fill, 0, static_cast<size_t>(n_lists) * sizeof(int), s);
   cudaMemsetAsync(lcounts, 0, static_cast<size_t>(n_pairs) * sizeof(int), s);
+  uint32_t* row_bound = reinterpret_cast<uint32_t*>(ws + lay.bound);
+  cudaMemsetAsync(row_bound, 0, static_cast<size_t>(B) * sizeof(uint32_t), s);
   const int pgrid = static_cast<int>(std::min<int64_t>((n_pairs + 255) / 256, 4096));
   pair_count_kernel<<<pgrid, 256, 0, s>>>(probe_ids, n_pairs, n_lists, cnt);
   cluster_scan_kernel<<<1, kExpandThreads, 0, s>>>(cnt, n_lists, G, cpo, ctask);
@@ -1124,12 +1139,12 @@ int rb_st_search_grouped(const float* query, int B, int D, const int64_t* probe_
     ProfileEvents& pe = profile_events();
     if (pe.start) record_profile_event(pe.start, s);
     rc = ivf_tc_scan(q_codes, B, D, P, item_codes, N, cluster_offsets, cluster_sizes, n_lists, pairs, cpo, ctask, head,
-                     tail, width, k_sel, divisor_for_int8, fs, lists, lcounts, err, ws + lay.tc, s);
+                     tail, width, k_sel, divisor_for_int8, fs, lists, lcounts, row_bound, err, ws + lay.tc, s);
     if (rc != RB_OK) return rc;
     if (pe.stop) record_profile_event(pe.stop, s);
   } else {
     rc = group_scan(item_codes, N, D, q_codes, probe_ids, P, cluster_offsets, cluster_sizes, n_lists, pairs, cpo,
-                    ctask, head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts, n_pairs, s);
+                    ctask, head, tail, width, G, k_sel, divisor_for_int8, fs, lists, lcounts, row_bound, n_pairs, s);
     if (rc != RB_OK) return rc;
   }
   rc = merge_lists(lists, lcounts, B, P, tc ? ivf_tc_cap(k_sel) : group_cap(k_sel), k_sel, 0, slots, raw, nullptr, s);

@@ -1,27 +1,39 @@
 // st::search's scorer on the tensor cores (kind::i8): the grouped IVF scan with
 // each task (a probed cluster and up to 128 of the (row, probe) pairs probing it)
-// run as one M = 128 x N = 128 x K = D int8 MMA per 128-row tile of the cluster.
+// run as one M = 128 cluster rows x N = (pairs, rounded up to 16) x K = D int8
+// MMA per 128-row tile of the cluster.
 //
 //  * tc_gather_kernel: per task, the pairs' int8 query codes gathered into rows
-//    [128 t, 128 t + 128) of a [tasks x 128, D] block (zero rows past the
-//    task's pairs), and the task's (cluster, first pair, pairs) record.
+//    [128 t, 128 t + m) of a [tasks x 128, D] block (zero rows after them), and
+//    the task's (cluster, first pair, pairs) record.
 //  * ivf_tc_scan_kernel: one persistent CTA per SM, the dense scan's pipeline
 //    shape: warp 0 loads the task's query block once and the cluster's row
 //    tiles (TMA, 128-byte swizzle) through a STAGES-deep ring; warp 1 issues the
-//    MMAs into a double-buffered TMEM accumulator (s32); warps 2-5 read one
-//    pair's 128 dots a tile (thread = pair; the pairs dealt round the four
-//    warps), keep the rows of the cluster that
-//    land inside the row's width, rank them on the raw score (the int32 dot, or
-//    fp16(dot / divisor)) and append (raw, slot) to the pair's list in
-//    ascending slot order, testing the full-N mask or the exact clauses only
-//    for the rows over the list's threshold; a list that fills is compacted to
-//    the k best (ties to the lower slot) and its threshold rises.
+//    MMAs (A = the cluster's rows, B = the pairs' queries) into a
+//    double-buffered TMEM accumulator (s32: TMEM lane = cluster row, column =
+//    pair); warps 2-5 each read 32 rows of the tile for every pair (thread =
+//    row, 32 pairs a load) and, pair by pair, ballot the rows that land inside
+//    the pair's row width and reach the pair's list threshold (compared on the
+//    int32 dot: the smallest dot whose raw score reaches it), testing the
+//    full-N mask or the exact clauses only for those rows; the passing rows are
+//    appended to the pair's list together, at an offset taken from the pair's
+//    shared count.
+//  * Between tiles (named barrier of the 4 epilogue warps) each thread owns one
+//    pair: a list with less than a tile's room left is compacted to the k best
+//    (ties to the lower slot: every later row of the pair has a higher slot, so
+//    the threshold can be strict), and the row's bound is raised and read back:
+//    a compacted list holds k candidates of its row at or above its k-th raw
+//    score, so that score bounds the row's k-th from below and every pair of the
+//    row may skip what falls under it (ties kept: another pair's rows may have
+//    lower slots). Pairs of one row meet in different tasks, so the bound cuts
+//    the appends the pairs of later tasks make.
 // The lists then go through the same merge and slot -> id epilogue as the SIMT
 // grouped scorer (ivf_search.cu), so the results are the row path's, bit for bit.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstdint>
 #include <cstring>
 
@@ -32,9 +44,10 @@ namespace rb {
 
 namespace {
 
-constexpr int kTcRows = 128;      // pairs a task (MMA M) and cluster rows a tile (MMA N)
+constexpr int kTcRows = 128;   // cluster rows a tile (MMA M, TMEM lanes) and most pairs a task (MMA N)
 constexpr int kTcEpiWarps = 4;
-constexpr int kTcThreads = 64 + 32 * kTcEpiWarps;
+constexpr int kTcEpiThreads = 32 * kTcEpiWarps;
+constexpr int kTcThreads = 64 + kTcEpiThreads;
 
 struct TcTask {
   int64_t cluster;
@@ -43,9 +56,24 @@ struct TcTask {
   int32_t pad;
 };
 
+// A pair's state during its task (shared memory). The first four words are read
+// together for every (row, pair) test.
+struct alignas(16) TcPair {
+  int ithr;         // smallest int32 dot whose raw score reaches `thresh`
+  uint32_t hlim;    // a head row i (i < full) lies inside the row's width iff i < hlim
+  uint32_t tlim;    // a tail row i (i >= full) does iff i < tlim
+  int count;        // entries in the pair's list
+  float thresh;     // the list's threshold on the raw score (>=)
+  uint32_t head32;  // slot of head row i: head32 + i (mod 2^32)
+  uint32_t tail32;  // slot of tail row i: tail32 + i (mod 2^32)
+  int pair;         // b * P + j
+  int row;          // b
+  int pad[3];
+};
+
 struct alignas(64) TcParams {
-  CUtensorMap tmap_q;  // [tasks x 128, D] gathered query codes
-  CUtensorMap tmap_x;  // [N, D] cluster-sorted item codes, 128-row boxes
+  CUtensorMap tmap_q;  // [tasks x 128, D] gathered query codes (B operand)
+  CUtensorMap tmap_x;  // [N, D] cluster-sorted item codes (A operand), 128-row boxes
   const TcTask* tasks;
   const int64_t* n_tasks;  // device count (ctask[n_lists])
   const int32_t* pairs;    // pair ids b * P + j, grouped by cluster
@@ -58,17 +86,19 @@ struct alignas(64) TcParams {
   FilterSet f;  // full-N mask / exact clauses (no bloom plans on this path)
   uint2* lists;
   int* list_counts;
+  uint32_t* row_bound;  // [B] f2ord of a lower bound on the row's k-th raw score (0: none yet)
   int* err;
 };
 
 template <int KB, int STAGES>
 struct TcLayout {
   static constexpr int kOpTile = kTcRows * 128;
-  static constexpr int kA = KB * kOpTile;
-  static constexpr int kB = STAGES * KB * kOpTile;
+  static constexpr int kA = KB * kOpTile;            // the task's query block
+  static constexpr int kB = STAGES * KB * kOpTile;   // cluster row tiles
   static constexpr int kHist = kTcEpiWarps * 256 * 4;
+  static constexpr int kPairs = kTcRows * static_cast<int>(sizeof(TcPair));
   static constexpr int kBar = (2 * STAGES + 2 + 4 + 1) * 8;
-  static constexpr int kTotal = kA + kB + kHist + kBar + 16 + 1024;
+  static constexpr int kTotal = kA + kB + kHist + kPairs + kBar + 16 + 1024;
 };
 
 __global__ void tc_gather_kernel(const int8_t* __restrict__ q_codes, int D, int P, const int32_t* __restrict__ pairs,
@@ -84,13 +114,10 @@ __global__ void tc_gather_kernel(const int8_t* __restrict__ q_codes, int D, int 
   const int64_t p0 = cpo[lo] + (t - ctask[lo]) * kTcRows;
   const int m = static_cast<int>(min(static_cast<int64_t>(kTcRows), cpo[lo + 1] - p0));
   if (threadIdx.x == 0) tasks[t] = TcTask{lo, p0, m, 0};
-  // pair r of the task goes to MMA row (r % 4) * 32 + r / 4: the task's pairs spread over the
-  // four TMEM lane quadrants, so all four epilogue warps share their lists' work
   const int words = D / 16;  // D is a multiple of 128 here
   int4* dst = reinterpret_cast<int4*>(out + t * kTcRows * D);
   for (int i = threadIdx.x; i < kTcRows * words; i += blockDim.x) {
-    const int row = i / words, w = i - row * words;
-    const int r = (row & 31) * 4 + (row >> 5);
+    const int r = i / words, w = i - r * words;
     int4 v = make_int4(0, 0, 0, 0);
     if (r < m) v = reinterpret_cast<const int4*>(q_codes + static_cast<int64_t>(pairs[p0 + r] / P) * D)[w];
     dst[i] = v;
@@ -98,22 +125,76 @@ __global__ void tc_gather_kernel(const int8_t* __restrict__ q_codes, int D, int 
 }
 
 // Raw score of an int32 dot: the dot itself (divisor -1) or fp16(dot / divisor),
-// the reference scorer's ranking value. Monotonic non-decreasing in the dot.
+// the reference scorer's ranking value. Non-decreasing in the dot (divisor > 0).
 __device__ __forceinline__ float tc_raw(int dot, int divisor) {
   const float s = static_cast<float>(dot);  // exact: |dot| < 2^24 for D <= 512
   return divisor == -1 ? s : __half2float(__float2half_rn(__fdiv_rn(s, static_cast<float>(divisor))));
 }
 
-__device__ __forceinline__ int max32_s32(const uint32_t (&r)[32]) {
-  int a[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) a[i] = max(static_cast<int>(r[2 * i]), static_cast<int>(r[2 * i + 1]));
-#pragma unroll
-  for (int w = 8; w >= 1; w >>= 1) {
-#pragma unroll
-    for (int i = 0; i < w; ++i) a[i] = max(a[2 * i], a[2 * i + 1]);
+// The smallest int32 dot d with tc_raw(d) >= thresh (INT_MIN: every dot does; INT_MAX:
+// none does). |dot| < 2^24 for 8-bit codes and D <= 512.
+__device__ int dot_threshold(float thresh, int divisor) {
+  constexpr int kLim = 1 << 24;
+  if (!(thresh > -INFINITY)) return INT_MIN;
+  if (divisor == -1) {
+    if (thresh > static_cast<float>(kLim)) return INT_MAX;
+    if (thresh < -static_cast<float>(kLim)) return INT_MIN;
+    return static_cast<int>(ceilf(thresh));  // float(d) is exact, so d >= thresh iff d >= ceil(thresh)
   }
-  return a[0];
+  if (tc_raw(-kLim, divisor) >= thresh) return INT_MIN;
+  if (tc_raw(kLim, divisor) < thresh) return INT_MAX;
+  int lo = -kLim, hi = kLim;  // tc_raw(lo) < thresh <= tc_raw(hi)
+  while (hi - lo > 1) {
+    const int mid = lo + (hi - lo) / 2;
+    if (tc_raw(mid, divisor) >= thresh) hi = mid; else lo = mid;
+  }
+  return hi;
+}
+
+// Named barrier 1 over the four epilogue warps, and its AND-reduction form.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory"); }
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kTcEpiThreads)
+      : "memory");
+  return r != 0;
+}
+
+// Between tiles: thread `et` owns pair et of the task (et < m). Raises the pair's
+// threshold to the row's bound `rb`, compacts the list to the k best when it holds
+// more than `limit` entries, publishes the compacted list's k-th score as the row's
+// bound, and stores the state back (`last`: writes the list's count out instead).
+// Called by every lane of the epilogue warps.
+template <int EPL>
+__device__ __forceinline__ void tc_pair_update(const TcParams& p, TcPair* sp, int et, int m, uint32_t rb, int limit,
+                                               uint32_t* hist, bool last) {
+  const bool mine = et < m;
+  TcPair* s = sp + (mine ? et : 0);
+  float th = mine ? fmaxf(s->thresh, ord2f(rb)) : -INFINITY;  // ord2f(0) is NaN: ignored
+  int cnt = mine ? s->count : 0;
+  uint2* list = p.lists + static_cast<int64_t>(mine ? s->pair : 0) * p.cap;
+  const bool need = mine && cnt > limit;
+  if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, cnt, th, need, p.k, hist);
+  // the strict threshold sits one step above the k-th score: one step below it is
+  // that score (or, for a threshold raised by the bound, less than the bound)
+  if (need) atomicMax(p.row_bound + s->row, f2ord(th) - 1u);
+  if (mine) {
+    if (last) {
+      p.list_counts[s->pair] = cnt;
+    } else {
+      if (th != s->thresh) {
+        s->thresh = th;
+        s->ithr = dot_threshold(th, p.divisor);
+      }
+      s->count = cnt;
+    }
+  }
 }
 
 template <int KB, int STAGES, int EPL, bool FILT>
@@ -121,14 +202,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
   using L = TcLayout<KB, STAGES>;
   constexpr int kKSteps = 4;  // 32-byte K steps per 128-byte K-block
   constexpr uint32_t kTmemCols = 2 * kTcRows;
-  constexpr uint32_t kIdesc = make_idesc(2, 1, kTcRows, kTcRows);  // s32 accumulate, signed int8 operands
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + L::kA;
   uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist);
+  TcPair* sp = reinterpret_cast<TcPair*>(smem + L::kA + L::kB + L::kHist);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist + L::kPairs);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* a_full = bars + 2 * STAGES;
@@ -232,12 +313,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
       int acc = 0;
       uint32_t acc_phase = 0;
       int a_iter = 0;
-      const uint32_t a_base = smem_u32(smA), b_base = smem_u32(smB);
+      const uint32_t q_base = smem_u32(smA), x_base = smem_u32(smB);
       for (int64_t t = blockIdx.x; t < n_tasks && !*abort_flag; t += gridDim.x) {
         int64_t start, len, full, p0;
         int m;
         task_range(t, start, len, full, m, p0);
         if (len == 0) continue;
+        // M = 128 cluster rows, N = the task's pairs rounded up to 16 (zero query rows past m)
+        const uint32_t idesc = make_idesc(2, 1, kTcRows, static_cast<uint32_t>((m + 15) & ~15));
         if (!mbar_wait(a_full, a_iter & 1, abort_flag)) {
           atomicCAS(p.err, 0, kDevTimeoutMma);
           *abort_flag = 1;
@@ -261,9 +344,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
           for (int kb = 0; kb < KB; ++kb) {
 #pragma unroll
             for (int j = 0; j < kKSteps; ++j) {
-              const uint64_t ad = sw128_kmajor_desc(a_base + kb * L::kOpTile + j * 32);
-              const uint64_t bd = sw128_kmajor_desc(b_base + (stage * KB + kb) * L::kOpTile + j * 32);
-              mma_i8(d_col, ad, bd, kIdesc, (kb | j) != 0);
+              const uint64_t ad = sw128_kmajor_desc(x_base + (stage * KB + kb) * L::kOpTile + j * 32);
+              const uint64_t bd = sw128_kmajor_desc(q_base + kb * L::kOpTile + j * 32);
+              mma_i8(d_col, ad, bd, idesc, (kb | j) != 0);
             }
           }
           mma_commit(&empty_bar[stage]);
@@ -284,92 +367,92 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
   } else {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int et = threadIdx.x - 64;  // 0 .. 127: the pair this thread owns between tiles
+    const int quad = warp & 3;        // TMEM lane quadrant this warp may access: rows 32 quad ..
     uint32_t* hist = hist_all + ew * 256;
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    for (int64_t t = blockIdx.x; t < n_tasks; t += gridDim.x) {
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < n_tasks && ok; t += gridDim.x) {
       int64_t start, len, full, p0;
       int m;
       task_range(t, start, len, full, m, p0);
       if (len == 0) continue;  // its pairs keep the zero count they start with
-      const int r = lane * 4 + quad;  // the task's pair this lane scores (its MMA row: quad * 32 + lane)
-      const bool valid = r < m;
-      const int32_t pair = valid ? p.pairs[p0 + r] : 0;
-      const int64_t b = pair / p.P;
-      const int64_t hs = valid ? p.head[pair] : 0, ts = valid ? p.tail[pair] : 0;
-      uint2* list = p.lists + static_cast<int64_t>(pair) * p.cap;
-      int count = 0;
-      float thresh = -INFINITY;
+      epi_sync();              // every thread is done with the previous task's pairs
+      if (et < m) {
+        TcPair s;
+        s.pair = p.pairs[p0 + et];
+        s.row = s.pair / p.P;
+        const int64_t hs = p.head[s.pair], ts = p.tail[s.pair];
+        s.count = 0;
+        s.thresh = fmaxf(-INFINITY, ord2f(__ldcg(p.row_bound + s.row)));
+        s.ithr = dot_threshold(s.thresh, p.divisor);
+        s.hlim = static_cast<uint32_t>(min(full, max(int64_t{0}, static_cast<int64_t>(p.width) - hs)));
+        s.tlim = static_cast<uint32_t>(full + min(len - full, max(int64_t{0}, static_cast<int64_t>(p.width) - ts)));
+        s.head32 = static_cast<uint32_t>(hs);
+        s.tail32 = static_cast<uint32_t>(ts - full);
+        sp[et] = s;
+      }
+      epi_sync();
       const int tiles = static_cast<int>((len + kTcRows - 1) / kTcRows);
-      bool ok = true;
+      const int groups = (m + 31) >> 5;  // 32-pair column groups
       for (int tile = 0; tile < tiles; ++tile) {
-        const bool need = valid && count > p.cap - kTcRows;  // room for a whole tile of appends
-        if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
-        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
-          if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
+        // the row's bound for this thread's pair, read while the tile's MMA runs
+        const uint32_t rb = et < m ? __ldcg(p.row_bound + sp[et].row) : 0u;
+        const bool got = mbar_wait(&acc_full[acc], acc_phase, abort_flag);
+        if (!epi_all(got)) {  // the same decision in all four warps: no one is left at a barrier
+          if (!got && lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
           *abort_flag = 1;
           ok = false;
           break;
         }
         tc_fence_after();
-        if (quad >= m) {  // no pair of this task in the warp's quadrant: release the tile at once
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
-          acc ^= 1;
-          if (acc == 0) acc_phase ^= 1;
-          continue;
-        }
+        // this thread's cluster row (< 2^31 + 128: rows and limits stay in uint32)
+        const uint32_t i = static_cast<uint32_t>(tile) * kTcRows + quad * 32 + lane;
+        const bool in_head = static_cast<int64_t>(i) < full;
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * kTcRows);
-        uint32_t v[4][32];
-        __syncwarp();
+#pragma unroll 1
+        for (int g = 0; g < groups; ++g) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32x32(col0 + g * 32, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, v[ch]);
-        tmem_wait_ld();
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = g * 32 + jj;
+            if (j >= m) break;  // warp-uniform
+            const int4 st = *reinterpret_cast<const int4*>(sp + j);  // ithr, hlim, tlim, count
+            const int d = static_cast<int>(v[jj]);
+            bool pass = i < (in_head ? static_cast<uint32_t>(st.y) : static_cast<uint32_t>(st.z)) && d >= st.x;
+            if constexpr (FILT) {
+              if (pass) pass = pos_passes<false>(p.f, sp[j].row, start + i);
+            }
+            const uint32_t bal = __ballot_sync(RB_FULL_MASK, pass);
+            if (bal != 0u) {
+              int base = 0;
+              if (lane == 0) base = atomicAdd(&sp[j].count, __popc(bal));
+              base = __shfl_sync(RB_FULL_MASK, base, 0);
+              if (pass) {
+                const uint32_t slot = (in_head ? sp[j].head32 : sp[j].tail32) + i;
+                p.lists[static_cast<int64_t>(sp[j].pair) * p.cap + base + __popc(bal & lanemask_lt())] =
+                    make_uint2(__float_as_uint(tc_raw(d, p.divisor)), slot);
+              }
+            }
+          }
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
-        // rows i0 .. i0 + 127 of the cluster; the row's slots of this tile all lie inside
-        // the cluster and the width unless the tile is the cluster's last or the width cuts it
-        const int64_t i0 = static_cast<int64_t>(tile) * kTcRows;
-        const int64_t i_end = min(len, i0 + kTcRows);
-        const int64_t last_slot = (i_end - 1) < full ? hs + (i_end - 1) : ts + (i_end - 1 - full);
-        const bool clean = i_end - i0 == kTcRows && last_slot < p.width;
-        int cm[4];
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) cm[ch] = max32_s32(v[ch]);
-        bool any = false;
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) any |= tc_raw(cm[ch], p.divisor) >= thresh;
-        if (!__any_sync(RB_FULL_MASK, valid && any)) continue;
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          if (!(valid && tc_raw(cm[ch], p.divisor) >= thresh)) continue;
-          uint2* w = list + count;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t i = i0 + ch * 32 + j;
-            const float s = tc_raw(static_cast<int>(v[ch][j]), p.divisor);
-            if (s >= thresh) {
-              const int64_t slot = i < full ? hs + i : ts + (i - full);
-              bool keep = clean || (i < len && slot < p.width);
-              if constexpr (FILT) keep = keep && pos_passes<false>(p.f, b, start + i);
-              if (keep) {
-                *w = make_uint2(__float_as_uint(s), static_cast<uint32_t>(slot));
-                ++w;
-              }
-            }
-          }
-          count = static_cast<int>(w - list);
-        }
+        epi_sync();  // every append of the tile is in
+        // room for the next tile's appends (at most 128 a pair), the row's bound, the thresholds
+        tc_pair_update<EPL>(p, sp, et, m, rb, p.cap - kTcRows, hist, false);
+        epi_sync();
       }
       if (!ok) break;
-      const bool need = valid && count > p.k;
-      warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
-      if (valid) p.list_counts[pair] = count;
+      tc_pair_update<EPL>(p, sp, et, m, 0u, p.k, hist, true);
     }
   }
 
@@ -403,6 +486,10 @@ cudaError_t launch_tc_kb(const TcParams& prm, bool filt, bool large, int grid, c
   return filt ? launch_tc<KB, STAGES, 16, true>(prm, grid, s) : launch_tc<KB, STAGES, 16, false>(prm, grid, s);
 }
 
+size_t tc_query_block_bytes(int64_t max_tasks, int D) {
+  return align_up(static_cast<size_t>(max_tasks) * kTcRows * D, 256);
+}
+
 }  // namespace
 
 bool ivf_tc_supported(int D, int k_sel, bool bloom) {
@@ -413,22 +500,24 @@ bool ivf_tc_supported(int D, int k_sel, bool bloom) {
 // the compactions out (a list of 512 is compacted about once per 380 appends).
 int ivf_tc_cap(int k_sel) { return k_sel <= 384 ? 512 : 1280; }
 
+// Gathered query blocks | task records.
 size_t ivf_tc_ws_bytes(int64_t n_pairs, int64_t n_lists, int D) {
   const int64_t tasks = (n_pairs + kTcRows - 1) / kTcRows + std::min(n_lists, n_pairs);
-  return align_up(static_cast<size_t>(tasks) * kTcRows * D, 256) + align_up(static_cast<size_t>(tasks) * sizeof(TcTask), 256);
+  return tc_query_block_bytes(tasks, D) + align_up(static_cast<size_t>(tasks) * sizeof(TcTask), 256);
 }
 
 int ivf_tc_scan(const int8_t* q_codes, int B, int D, int P, const int8_t* item_codes, int64_t N,
                 const int64_t* offsets, const int64_t* sizes, int64_t n_lists, const int32_t* pairs,
                 const int64_t* cpo, const int64_t* ctask, const int64_t* head, const int64_t* tail, int width,
-                int k_sel, int divisor, const FilterSet& fs, uint2* lists, int* list_counts, int* err, void* ws,
-                cudaStream_t s) {
+                int k_sel, int divisor, const FilterSet& fs, uint2* lists, int* list_counts, uint32_t* row_bound,
+                int* err, void* ws, cudaStream_t s) {
   const int64_t n_pairs = static_cast<int64_t>(B) * P;
   const int64_t max_tasks = (n_pairs + kTcRows - 1) / kTcRows + std::min(n_lists, n_pairs);
   if (max_tasks == 0) return RB_OK;
   uint8_t* w8 = static_cast<uint8_t*>(ws);
   int8_t* qblock = reinterpret_cast<int8_t*>(w8);
-  TcTask* tasks = reinterpret_cast<TcTask*>(w8 + align_up(static_cast<size_t>(max_tasks) * kTcRows * D, 256));
+  const size_t task_off = tc_query_block_bytes(max_tasks, D);
+  TcTask* tasks = reinterpret_cast<TcTask*>(w8 + task_off);
   tc_gather_kernel<<<static_cast<unsigned>(max_tasks), 256, 0, s>>>(q_codes, D, P, pairs, cpo, ctask, n_lists, qblock,
                                                                       tasks);
   if (cudaGetLastError() != cudaSuccess) {
@@ -460,9 +549,10 @@ int ivf_tc_scan(const int8_t* q_codes, int B, int D, int P, const int8_t* item_c
   prm.f = fs;
   prm.lists = lists;
   prm.list_counts = list_counts;
+  prm.row_bound = row_bound;
   prm.err = err;
   const bool filt = fs.mask != nullptr || fs.ex.attrs != nullptr;
-  const bool large = prm.cap > 256;
+  const bool large = prm.cap > 512;  // lists of 1280: 40 entries a lane in the compaction
   const int grid = static_cast<int>(std::min<int64_t>(max_tasks, num_sms()));
   cudaError_t e;
   if (D == 128)
