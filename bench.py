@@ -57,6 +57,8 @@ def parse_args():
     p.add_argument("--ref-sample", type=int, default=32,
                    help="queries per step of --impl reference (each step a bounded sample)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--exchange", choices=("nccl", "peer"), default="nccl",
+                   help="the sharded search's two all-gathers: NCCL, or stores into the peers' memory")
     p.add_argument("--no-configs", action="store_true",
                    help="skip the records of configs 3, 4, 5 and the IVF search that follow the headline at N=1")
     p.add_argument("--workload", choices=("c2", "c3", "c4", "c5", "ivf", "ops"), default="c2",
@@ -290,7 +292,9 @@ def config_dict(args) -> dict:
         "batch": args.batch,
         "k": args.k,
         "corpus": f"{N_CENTRES}-centre Gaussian mixture, sigma {SIGMA}, L2-normalised, bf16",
-        "parallelism": f"row-shard x{args.gpus}, shared seed; 2 NCCL all-gathers per step; one CUDA graph per step",
+        "parallelism": f"row-shard x{args.gpus}, shared seed; 2 all-gathers per step "
+                       f"({'stores into peer memory' if args.exchange == 'peer' else 'NCCL'}); "
+                       "one CUDA graph per step",
         "l2": "no flush: the corpus (2.56 GB, or its shard) is larger than L2 (126 MB)",
     }
 
@@ -326,7 +330,7 @@ def main():
     lo, hi = shard_bounds(n, world, rank)
     x = corpus_rows(cent, lo, hi, n)
     q = queries(cent, b)
-    index = ShardedDenseTopK(x, lo, k, n_total=n)
+    index = ShardedDenseTopK(x, lo, k, n_total=n, exchange=args.exchange)
     torch.cuda.synchronize()
 
     def barrier():
@@ -487,6 +491,8 @@ def main():
         }
         line["recall_vs_ref"] = recall_at_k(ours_i.cpu().numpy(), ref_i)
     graphed.release()
+    if world > 1:
+        index.close()  # the peer exchange buffers (collective; nothing with NCCL)
     if world == 1 and not args.no_configs:
         # the other configurations, one GPU each, after the headline's inputs are freed
         from bench_configs import measure_configs

@@ -85,6 +85,21 @@ static int dense_check(int elem, const void* queries, const float* q_scale, cons
   return RB_OK;
 }
 
+// After a pass from the speculative seed: a row whose k-th output is padding found fewer
+// than k candidates at or above that seed, and is scanned again from the safe seed (the
+// k-th sampled chunk max); every other row keeps its output (seed NaN: nothing passes).
+__global__ void spec_check_kernel(const int64_t* __restrict__ out_ids, int B, int k, const float* __restrict__ safe,
+                                  float* __restrict__ seed, int* __restrict__ row_live, int* __restrict__ qsg_live,
+                                  int queries_per_group) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= B) return;
+  // (a row whose safe seed is no lower, e.g. both -inf, already ran from the safe seed)
+  const bool again = out_ids[static_cast<int64_t>(q) * k + (k - 1)] < 0 && safe[q] < seed[q];
+  row_live[q] = again ? 1 : 0;
+  seed[q] = again ? safe[q] : __int_as_float(0x7fc00000);
+  if (again) atomicOr(&qsg_live[q / queries_per_group], 1);
+}
+
 struct DenseWs {
   uint2* lists;
   int* counts;
@@ -138,12 +153,18 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   }
 
   DensePlan pl;
+  const bool filtered = filter != nullptr && filter->mode != kFilterNone;
   dense_plan(B, N, k, row_bytes, pl, shared ? shared->n_total : N, elem >= 2);
   const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
   if (cudaMemsetAsync(d.err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
 
   ProfileEvents& pe = profile_events();
   const float* seed = nullptr;
+  // Filtered searches seed the full pass speculatively: the ceil(3k / s)-th largest sampled
+  // chunk max instead of the k-th (s = the sample's tile stride). About 3k items of the
+  // corpus pass it, so the rows append and test about s / 3 times fewer candidates; a row
+  // that still finds fewer than k runs again from the safe seed (spec_check_kernel).
+  bool spec = false;
   if (shared != nullptr) {
     // k-th largest of the union of the shards' samples (a [W, B, k] stack)
     rc = row_kth_lower_bound(shared->vals, B, shared->m, shared->m, shared->W, static_cast<int64_t>(B) * shared->m,
@@ -156,16 +177,43 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
                          stream, q_scale, x_scale, filter);
     if (rc != RB_OK) return rc;
     const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
-    rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, k, d.thresh, nullptr, stream);
+    const int k_spec = (3 * k + pl.sample_stride - 1) / pl.sample_stride;
+    spec = filtered && out_pairs == nullptr && k_spec < k;
+    rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, spec ? k_spec : k, d.thresh, nullptr, stream);
     if (rc != RB_OK) return rc;
+    if (spec) {  // the safe seed, kept for the rows that need a second pass
+      rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, k, d.thresh + B, nullptr, stream);
+      if (rc != RB_OK) return rc;
+    }
     seed = d.thresh;
   }
   if (pe.start) record_profile_event(pe.start, stream);
   rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, d.lists, d.counts, nullptr, d.err, stream,
                        q_scale, x_scale, filter);
   if (rc != RB_OK) return rc;
+  if (!spec) {
+    if (pe.stop) record_profile_event(pe.stop, stream);
+    return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, out_pairs,
+                       stream);
+  }
+  rc = merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream);
+  if (rc != RB_OK) return rc;
+  int* row_live = reinterpret_cast<int*>(d.thresh + 2 * static_cast<size_t>(B));
+  int* qsg_live = reinterpret_cast<int*>(d.thresh + 3 * static_cast<size_t>(B));
+  if (cudaMemsetAsync(qsg_live, 0, static_cast<size_t>(pl.n_qsg) * sizeof(int), stream) != cudaSuccess)
+    return fail(RB_ERR_CUDA, "memset failed");
+  // queries of one query group: ng MMA tiles of 128 rows, doubled across a CTA pair
+  const int per_group = pl.ng * (pl.two_sm ? 256 : 128);
+  spec_check_kernel<<<(B + 255) / 256, 256, 0, stream>>>(out_ids, B, k, d.thresh + B, d.thresh, row_live, qsg_live,
+                                                         per_group);
+  if (cudaGetLastError() != cudaSuccess) return fail(RB_ERR_CUDA, "spec_check launch failed");
+  // the second pass scans only the query groups holding such a row
+  rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, d.thresh, d.lists, d.counts, nullptr, d.err, stream,
+                       q_scale, x_scale, filter, qsg_live);
+  if (rc != RB_OK) return rc;
   if (pe.stop) record_profile_event(pe.stop, stream);
-  return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, out_pairs, stream);
+  return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream,
+                     row_live);
 }
 
 int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, int D, int dtype, int k, int m,

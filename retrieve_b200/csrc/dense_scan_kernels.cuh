@@ -62,7 +62,12 @@ struct alignas(64) DenseScanParams {
   int n_qsg, n_splits;
   int tile_stride, tile_offset, pass_tiles;
   int k, cap;
+  const int* qsg_live;  // null: every query group; else only groups with a nonzero entry are scanned
 };
+
+__device__ __forceinline__ bool task_live(const DenseScanParams& p, int t) {
+  return p.qsg_live == nullptr || p.qsg_live[t % p.n_qsg] != 0;
+}
 
 // Bit-sliced Bloom words of one 128-item tile: 4 chunks x 64 words.
 constexpr int kTileSliceWords = 4 * 64;
@@ -252,30 +257,27 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
     if (__any_sync(RB_FULL_MASK, valid_q && all >= thresh)) {
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
-        if constexpr (FILT) {
-          // the Bloom test of the chunks the score test keeps: failing items
-          // become NaN, and the chunk's max is taken again over the others
-          if (__any_sync(RB_FULL_MASK, use_sl && cm[ch] >= thresh)) {
-            if (use_sl) {
-              const uint32_t pm = bloom_chunk_mask(sl + ch * 64, st);
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (!((pm >> j) & 1u)) r[ch][j] = 0x7fc00000u;
-              cm[ch] = max32(r[ch]);
-            }
-          }
-        }
-        if (valid_q && cm[ch] >= thresh) {
-          if constexpr (!FILT) {
-            append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
-          } else {
+        if constexpr (!FILT) {
+          if (valid_q && cm[ch] >= thresh) append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
+        } else {
+          // the items over the threshold, then the Bloom test of the chunk (32 items a
+          // term) on those; the predicate item by item only where some item is left
+          if (__any_sync(RB_FULL_MASK, valid_q && cm[ch] >= thresh)) {
             const uint32_t id0 = row0 + ch * 32;
-            uint32_t pm = chunk_pass_bits(r[ch], thresh);
-            if (!use_sl)
-              pm = pred_pass_bits(p.filter, q, id0, pm);
-            else if (p.filter.mode == kFilterBloomRecheck)
-              pm = pred_exact_bits(p.filter, q, id0, pm);
-            append_chunk_mask(list, count, r[ch], pm, id0);
+            uint32_t pm = 0;
+            if (valid_q && cm[ch] >= thresh) {
+              pm = chunk_pass_bits(r[ch], thresh);
+              if (use_sl) pm &= bloom_chunk_mask(sl + ch * 64, st);
+            }
+            if (__any_sync(RB_FULL_MASK, pm != 0u)) {
+              if (pm != 0u) {
+                if (!use_sl)
+                  pm = pred_pass_bits(p.filter, q, id0, pm);
+                else if (p.filter.mode == kFilterBloomRecheck)
+                  pm = pred_exact_bits(p.filter, q, id0, pm);
+              }
+              if (pm != 0u) append_chunk_mask(list, count, r[ch], pm, id0);
+            }
           }
         }
       }
@@ -352,6 +354,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
       int a_iter = 0;
       uint32_t armed = 0;  // item stages armed in total
       for (int t = blockIdx.x; t < n_tasks && !*abort_flag; t += gridDim.x) {
+        if (!task_live(p, t)) continue;  // every role skips the same tasks
         const int qsg = t % p.n_qsg, split = t / p.n_qsg;
         if (a_iter > 0 && !mbar_wait(a_empty, (a_iter - 1) & 1, abort_flag)) {
           atomicCAS(p.err, 0, kDevTimeoutProducer);
@@ -401,6 +404,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
       int a_iter = 0;
       const uint32_t a_base = smem_u32(smA), b_base = smem_u32(smB);
       for (int t = blockIdx.x; t < n_tasks && !*abort_flag; t += gridDim.x) {
+        if (!task_live(p, t)) continue;  // every role skips the same tasks
         const int split = t / p.n_qsg;
         if (!mbar_wait(a_full, a_iter & 1, abort_flag)) {
           atomicCAS(p.err, 0, kDevTimeoutMma);
@@ -469,6 +473,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
     uint32_t acc_phase = 0;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     for (int t = blockIdx.x; t < n_tasks; t += gridDim.x) {
+      if (!task_live(p, t)) continue;  // every role skips the same tasks
       const int qsg = t % p.n_qsg, split = t / p.n_qsg;
       const int q = qsg * NG * kQTile + g * kQTile + quad * 32 + lane;
       const bool valid_q = q < p.B;
@@ -654,6 +659,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       int a_iter = 0;
       uint32_t armed = 0;
       for (int t = pair; t < n_tasks && !*abort_flag; t += n_pairs) {
+        if (!task_live(p, t)) continue;  // every role skips the same tasks
         const int qsg = t % p.n_qsg, split = t / p.n_qsg;
         if (a_iter > 0 && !mbar_wait(a_empty, (a_iter - 1) & 1, abort_flag)) {
           atomicCAS(p.err, 0, kDevTimeoutProducer);
@@ -711,6 +717,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       const uint32_t accf0 = mapa_shared(smem_u32(acc_full), 0), accf1 = mapa_shared(smem_u32(acc_full), 1);
       const uint32_t ae0 = mapa_shared(smem_u32(a_empty), 0), ae1 = mapa_shared(smem_u32(a_empty), 1);
       for (int t = pair; t < n_tasks && !*abort_flag; t += n_pairs) {
+        if (!task_live(p, t)) continue;  // every role skips the same tasks
         const int split = t / p.n_qsg;
         if (!__all_sync(RB_FULL_MASK, mbar_wait(a_full, a_iter & 1, abort_flag))) {
           if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutMma);
@@ -796,6 +803,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t release0 = mapa_shared(smem_u32(acc_empty), 0);
     for (int t = pair; t < n_tasks; t += n_pairs) {
+      if (!task_live(p, t)) continue;  // every role skips the same tasks
       const int qsg = t % p.n_qsg, split = t / p.n_qsg;
       const int q = qsg * kQPerPair + g * 2 * kQTile + static_cast<int>(rank) * kQTile + quad * 32 + lane;
       const bool valid_q = q < p.B;

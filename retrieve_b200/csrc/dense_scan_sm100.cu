@@ -140,7 +140,8 @@ size_t dense_workspace_bytes(int B, int N, int k, int row_bytes, bool scaled) {
   dense_plan(B, N, k, row_bytes, pl, N, scaled);
   size_t lists = static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2);
   size_t counts = static_cast<size_t>(B) * pl.n_lists * sizeof(int);
-  size_t th = 2 * static_cast<size_t>(B) * sizeof(float);
+  // seeds [B] | safe seeds [B] | row flags [B] | query-group flags (at most B / 128 + 1)
+  size_t th = (4 * static_cast<size_t>(B) + 64) * sizeof(float);
   size_t cm = static_cast<size_t>(B) * dense_chunk_stride(pl) * sizeof(float);
   // the chunk maxima are dead once the seed is known: they share the list space
   return align_up(std::max(lists, cm), 256) + align_up(counts, 256) + align_up(th, 256) + 256;
@@ -148,7 +149,8 @@ size_t dense_workspace_bytes(int B, int N, int k, int row_bytes, bool scaled) {
 
 int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
                     int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
-                    cudaStream_t stream, const float* q_scale, const float* x_scale, const FilterArgs* filter) {
+                    cudaStream_t stream, const float* q_scale, const float* x_scale, const FilterArgs* filter,
+                    const int* qsg_live) {
   DenseScanParams prm;
   std::memset(&prm, 0, sizeof(prm));
   const bool filtered = filter != nullptr && filter->mode != kFilterNone;
@@ -179,6 +181,7 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
   prm.pass_tiles = (pl.tiles + stride - 1) / stride;
   prm.k = k;
   prm.cap = pl.cap;
+  prm.qsg_live = qsg_live;
   const int n_tasks = pl.n_qsg * pl.n_splits;
   cudaError_t e = cudaSuccess;
   const int kb = row_bytes / 128;

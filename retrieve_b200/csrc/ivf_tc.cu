@@ -19,7 +19,8 @@
 //    appended to the pair's list together, at an offset taken from the pair's
 //    shared count.
 //  * Between tiles (named barrier of the 4 epilogue warps) each thread owns one
-//    pair: a list with less than a tile's room left is compacted to the k best
+//    pair (pair j: warp j % 4, lane j / 4, so a task's compactions spread over
+//    the warps): a list with less than a tile's room left is compacted to the k best
 //    (ties to the lower slot: every later row of the pair has a higher slot, so
 //    the threshold can be strict), and the row's bound is raised and read back:
 //    a compacted list holds k candidates of its row at or above its k-th raw
@@ -90,15 +91,18 @@ struct alignas(64) TcParams {
   int* err;
 };
 
+// ABUF query blocks (two: the next task's block loads while the current one runs;
+// one at D = 512, where two do not fit beside the row ring).
 template <int KB, int STAGES>
 struct TcLayout {
   static constexpr int kOpTile = kTcRows * 128;
-  static constexpr int kA = KB * kOpTile;            // the task's query block
+  static constexpr int kABuf = KB == 4 ? 1 : 2;
+  static constexpr int kA = KB * kOpTile;            // one query block
   static constexpr int kB = STAGES * KB * kOpTile;   // cluster row tiles
   static constexpr int kHist = kTcEpiWarps * 256 * 4;
   static constexpr int kPairs = kTcRows * static_cast<int>(sizeof(TcPair));
-  static constexpr int kBar = (2 * STAGES + 2 + 4 + 1) * 8;
-  static constexpr int kTotal = kA + kB + kHist + kPairs + kBar + 16 + 1024;
+  static constexpr int kBar = (2 * STAGES + 2 * kABuf + 4 + 1) * 8;
+  static constexpr int kTotal = kABuf * kA + kB + kHist + kPairs + kBar + 16 + 1024;
 };
 
 __global__ void tc_gather_kernel(const int8_t* __restrict__ q_codes, int D, int P, const int32_t* __restrict__ pairs,
@@ -166,7 +170,7 @@ __device__ __forceinline__ bool epi_all(bool v) {
   return r != 0;
 }
 
-// Between tiles: thread `et` owns pair et of the task (et < m). Raises the pair's
+// Between tiles: each thread owns pair `et` of the task (et < m). Raises the pair's
 // threshold to the row's bound `rb`, compacts the list to the k best when it holds
 // more than `limit` entries, publishes the compacted list's k-th score as the row's
 // bound, and stores the state back (`last`: writes the list's count out instead).
@@ -205,19 +209,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smA = smem;
-  uint8_t* smB = smem + L::kA;
-  uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
-  TcPair* sp = reinterpret_cast<TcPair*>(smem + L::kA + L::kB + L::kHist);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist + L::kPairs);
+  constexpr int kABuf = L::kABuf;
+  uint8_t* smA = smem;  // [kABuf] query blocks
+  uint8_t* smB = smem + kABuf * L::kA;
+  uint32_t* hist_all = reinterpret_cast<uint32_t*>(smB + L::kB);
+  TcPair* sp = reinterpret_cast<TcPair*>(smB + L::kB + L::kHist);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smB + L::kB + L::kHist + L::kPairs);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
-  uint64_t* a_full = bars + 2 * STAGES;
-  uint64_t* a_empty = a_full + 1;
-  uint64_t* acc_full = a_full + 2;   // [2]
-  uint64_t* acc_empty = a_full + 4;  // [2]
-  uint64_t* drain_bar = a_full + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
+  uint64_t* a_full = bars + 2 * STAGES;  // [kABuf]
+  uint64_t* a_empty = a_full + kABuf;    // [kABuf]
+  uint64_t* acc_full = a_empty + kABuf;  // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -229,8 +234,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(a_full, 1);
-    mbar_init(a_empty, 1);
+    for (int b = 0; b < kABuf; ++b) {
+      mbar_init(&a_full[b], 1);
+      mbar_init(&a_empty[b], 1);
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kTcEpiWarps);
@@ -272,14 +279,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
         int m;
         task_range(t, start, len, full, m, p0);
         if (len == 0) continue;
-        if (a_iter > 0 && !mbar_wait(a_empty, (a_iter - 1) & 1, abort_flag)) {
+        const int slot = a_iter % kABuf;
+        const uint32_t use = static_cast<uint32_t>(a_iter / kABuf);  // earlier fills of this block
+        if (use > 0 && !mbar_wait(&a_empty[slot], (use - 1) & 1, abort_flag)) {
           atomicCAS(p.err, 0, kDevTimeoutProducer);
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(a_full, KB * L::kOpTile);
+        mbar_arrive_expect_tx(&a_full[slot], KB * L::kOpTile);
         for (int kb = 0; kb < KB; ++kb)
-          tma_load_2d(smA + kb * L::kOpTile, &p.tmap_q, a_full, kb * 128, static_cast<int>(t * kTcRows));
+          tma_load_2d(smA + slot * L::kA + kb * L::kOpTile, &p.tmap_q, &a_full[slot], kb * 128,
+                      static_cast<int>(t * kTcRows));
         ++a_iter;
         const int tiles = static_cast<int>((len + kTcRows - 1) / kTcRows);
         for (int tile = 0; tile < tiles; ++tile) {
@@ -299,7 +309,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
           }
         }
       }
-      if (a_iter > 0) mbar_wait_drain(a_full, (a_iter - 1) & 1);
+      for (int b = 0; b < kABuf; ++b) {
+        const int n_b = (a_iter + kABuf - 1 - b) / kABuf;  // fills of block b
+        if (n_b > 0) mbar_wait_drain(&a_full[b], (n_b - 1) & 1);
+      }
       for (int s = 0; s < STAGES; ++s) {
         const uint32_t n_s = armed / STAGES + (static_cast<uint32_t>(s) < armed % STAGES ? 1u : 0u);
         if (n_s > 0) mbar_wait_drain(&full_bar[s], (n_s - 1) & 1);
@@ -321,13 +334,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
         if (len == 0) continue;
         // M = 128 cluster rows, N = the task's pairs rounded up to 16 (zero query rows past m)
         const uint32_t idesc = make_idesc(2, 1, kTcRows, static_cast<uint32_t>((m + 15) & ~15));
-        if (!mbar_wait(a_full, a_iter & 1, abort_flag)) {
+        const int slot = a_iter % kABuf;
+        if (!mbar_wait(&a_full[slot], static_cast<uint32_t>(a_iter / kABuf) & 1, abort_flag)) {
           atomicCAS(p.err, 0, kDevTimeoutMma);
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         ++a_iter;
+        const uint32_t qa = q_base + static_cast<uint32_t>(slot * L::kA);
         const int tiles = static_cast<int>((len + kTcRows - 1) / kTcRows);
         bool ok = true;
         for (int tile = 0; tile < tiles; ++tile) {
@@ -345,7 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
 #pragma unroll
             for (int j = 0; j < kKSteps; ++j) {
               const uint64_t ad = sw128_kmajor_desc(x_base + (stage * KB + kb) * L::kOpTile + j * 32);
-              const uint64_t bd = sw128_kmajor_desc(q_base + kb * L::kOpTile + j * 32);
+              const uint64_t bd = sw128_kmajor_desc(qa + kb * L::kOpTile + j * 32);
               mma_i8(d_col, ad, bd, idesc, (kb | j) != 0);
             }
           }
@@ -359,7 +374,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
           if (acc == 0) acc_phase ^= 1;
         }
         if (!ok) break;
-        mma_commit(a_empty);
+        mma_commit(&a_empty[slot]);
       }
       mma_commit(drain_bar);
       mbar_wait_drain(drain_bar, 0);
@@ -367,92 +382,113 @@ __global__ void __launch_bounds__(kTcThreads, 1) ivf_tc_scan_kernel(const __grid
   } else {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
-    const int et = threadIdx.x - 64;  // 0 .. 127: the pair this thread owns between tiles
+    const int et = threadIdx.x - 64;  // 0 .. 127: the pair this thread sets up at a task's start
+    // the pair this thread owns at the updates: pairs dealt round the four warps, so the
+    // compactions of a task with few pairs spread over all of them
+    const int own = lane * kTcEpiWarps + ew;
     const int quad = warp & 3;        // TMEM lane quadrant this warp may access: rows 32 quad ..
     uint32_t* hist = hist_all + ew * 256;
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    // Tiles between two updates: a list holds at most `room` entries after an update
+    // (compacted to k above it), so the U tiles up to the next one (128 appends a pair
+    // each at most) fit its capacity.
+    const int U = max(1, min(4, (p.cap - 2 * p.k) / kTcRows - 1));  // room >= 2k + 128: compactions stay rare
+    const int room = p.cap - U * kTcRows;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < n_tasks && ok; t += gridDim.x) {
       int64_t start, len, full, p0;
       int m;
       task_range(t, start, len, full, m, p0);
       if (len == 0) continue;  // its pairs keep the zero count they start with
-      epi_sync();              // every thread is done with the previous task's pairs
-      if (et < m) {
+      const int n16 = (m + 15) >> 4;  // 16-pair column groups (the MMA's N / 16)
+      epi_sync();                     // every thread is done with the previous task's pairs
+      if (et < n16 * 16) {
         TcPair s;
-        s.pair = p.pairs[p0 + et];
-        s.row = s.pair / p.P;
-        const int64_t hs = p.head[s.pair], ts = p.tail[s.pair];
-        s.count = 0;
-        s.thresh = fmaxf(-INFINITY, ord2f(__ldcg(p.row_bound + s.row)));
-        s.ithr = dot_threshold(s.thresh, p.divisor);
-        s.hlim = static_cast<uint32_t>(min(full, max(int64_t{0}, static_cast<int64_t>(p.width) - hs)));
-        s.tlim = static_cast<uint32_t>(full + min(len - full, max(int64_t{0}, static_cast<int64_t>(p.width) - ts)));
-        s.head32 = static_cast<uint32_t>(hs);
-        s.tail32 = static_cast<uint32_t>(ts - full);
+        if (et < m) {
+          s.pair = p.pairs[p0 + et];
+          s.row = s.pair / p.P;
+          const int64_t hs = p.head[s.pair], ts = p.tail[s.pair];
+          s.count = 0;
+          s.thresh = fmaxf(-INFINITY, ord2f(__ldcg(p.row_bound + s.row)));
+          s.ithr = dot_threshold(s.thresh, p.divisor);
+          s.hlim = static_cast<uint32_t>(min(full, max(int64_t{0}, static_cast<int64_t>(p.width) - hs)));
+          s.tlim =
+              static_cast<uint32_t>(full + min(len - full, max(int64_t{0}, static_cast<int64_t>(p.width) - ts)));
+          s.head32 = static_cast<uint32_t>(hs);
+          s.tail32 = static_cast<uint32_t>(ts - full);
+        } else {  // a padding column of the last group: no row passes
+          s = TcPair{};
+          s.ithr = INT_MAX;
+          s.thresh = INFINITY;
+        }
         sp[et] = s;
       }
       epi_sync();
       const int tiles = static_cast<int>((len + kTcRows - 1) / kTcRows);
-      const int groups = (m + 31) >> 5;  // 32-pair column groups
+      bool failed = false;  // this warp's wait ran out: it skips to the next update, where all stop
       for (int tile = 0; tile < tiles; ++tile) {
+        const bool last = tile == tiles - 1;
+        const bool update = last || tile % U == U - 1;
         // the row's bound for this thread's pair, read while the tile's MMA runs
-        const uint32_t rb = et < m ? __ldcg(p.row_bound + sp[et].row) : 0u;
-        const bool got = mbar_wait(&acc_full[acc], acc_phase, abort_flag);
-        if (!epi_all(got)) {  // the same decision in all four warps: no one is left at a barrier
-          if (!got && lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // this thread's cluster row (< 2^31 + 128: rows and limits stay in uint32)
-        const uint32_t i = static_cast<uint32_t>(tile) * kTcRows + quad * 32 + lane;
-        const bool in_head = static_cast<int64_t>(i) < full;
-        const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * kTcRows);
+        const uint32_t rb = (update && own < m) ? __ldcg(p.row_bound + sp[own].row) : 0u;
+        if (!failed) failed = !mbar_wait(&acc_full[acc], acc_phase, abort_flag);
+        if (!failed) {
+          tc_fence_after();
+          // this thread's cluster row (< 2^31 + 128: rows and limits stay in uint32)
+          const uint32_t i = static_cast<uint32_t>(tile) * kTcRows + quad * 32 + lane;
+          const bool in_head = static_cast<int64_t>(i) < full;
+          const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * kTcRows);
 #pragma unroll 1
-        for (int g = 0; g < groups; ++g) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld_32x32(col0 + g * 32, v);
-          tmem_wait_ld();
+          for (int g = 0; g < n16; ++g) {
+            uint32_t v[16];
+            __syncwarp();
+            tmem_ld_32x16(col0 + g * 16, v);
+            tmem_wait_ld();
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int j = g * 32 + jj;
-            if (j >= m) break;  // warp-uniform
-            const int4 st = *reinterpret_cast<const int4*>(sp + j);  // ithr, hlim, tlim, count
-            const int d = static_cast<int>(v[jj]);
-            bool pass = i < (in_head ? static_cast<uint32_t>(st.y) : static_cast<uint32_t>(st.z)) && d >= st.x;
-            if constexpr (FILT) {
-              if (pass) pass = pos_passes<false>(p.f, sp[j].row, start + i);
-            }
-            const uint32_t bal = __ballot_sync(RB_FULL_MASK, pass);
-            if (bal != 0u) {
-              int base = 0;
-              if (lane == 0) base = atomicAdd(&sp[j].count, __popc(bal));
-              base = __shfl_sync(RB_FULL_MASK, base, 0);
-              if (pass) {
-                const uint32_t slot = (in_head ? sp[j].head32 : sp[j].tail32) + i;
-                p.lists[static_cast<int64_t>(sp[j].pair) * p.cap + base + __popc(bal & lanemask_lt())] =
-                    make_uint2(__float_as_uint(tc_raw(d, p.divisor)), slot);
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = g * 16 + jj;
+              const int4 st = *reinterpret_cast<const int4*>(sp + j);  // ithr, hlim, tlim, count
+              const int d = static_cast<int>(v[jj]);
+              bool pass = i < (in_head ? static_cast<uint32_t>(st.y) : static_cast<uint32_t>(st.z)) && d >= st.x;
+              if constexpr (FILT) {
+                if (pass) pass = pos_passes<false>(p.f, sp[j].row, start + i);
+              }
+              const uint32_t bal = __ballot_sync(RB_FULL_MASK, pass);
+              if (bal != 0u) {
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&sp[j].count, __popc(bal));
+                base = __shfl_sync(RB_FULL_MASK, base, 0);
+                if (pass) {
+                  const uint32_t slot = (in_head ? sp[j].head32 : sp[j].tail32) + i;
+                  p.lists[static_cast<int64_t>(sp[j].pair) * p.cap + base + __popc(bal & lanemask_lt())] =
+                      make_uint2(__float_as_uint(tc_raw(d, p.divisor)), slot);
+                }
               }
             }
           }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
-        epi_sync();  // every append of the tile is in
-        // room for the next tile's appends (at most 128 a pair), the row's bound, the thresholds
-        tc_pair_update<EPL>(p, sp, et, m, rb, p.cap - kTcRows, hist, false);
-        epi_sync();
+        if (update) {
+          // every append of the tiles since the last update is in; the same decision in all
+          // four warps, so no one is left at a barrier
+          if (!epi_all(!failed)) {
+            if (failed && lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          // the row's bound, the thresholds, and room for the next U tiles (or, after the
+          // last, the k best and the list's count)
+          tc_pair_update<EPL>(p, sp, own, m, rb, last ? p.k : room, hist, last);
+          if (!last) epi_sync();
+        }
       }
-      if (!ok) break;
-      tc_pair_update<EPL>(p, sp, et, m, 0u, p.k, hist, true);
     }
   }
 
@@ -496,8 +532,8 @@ bool ivf_tc_supported(int D, int k_sel, bool bloom) {
   return !bloom && (D == 128 || D == 256 || D == 512) && k_sel <= 1024;
 }
 
-// A pair's list holds k winners plus a whole tile of appends; the room past k + 128 spaces
-// the compactions out (a list of 512 is compacted about once per 380 appends).
+// A pair's list holds k winners plus the appends of the tiles between two updates (one tile
+// at these sizes: the thresholds rise at every tile, which keeps the appends few).
 int ivf_tc_cap(int k_sel) { return k_sel <= 384 ? 512 : 1280; }
 
 // Gathered query blocks | task records.
@@ -552,7 +588,7 @@ int ivf_tc_scan(const int8_t* q_codes, int B, int D, int P, const int8_t* item_c
   prm.row_bound = row_bound;
   prm.err = err;
   const bool filt = fs.mask != nullptr || fs.ex.attrs != nullptr;
-  const bool large = prm.cap > 512;  // lists of 1280: 40 entries a lane in the compaction
+  const bool large = prm.cap > 512;  // lists of 1280: 40 entries a lane in the compaction (else 16)
   const int grid = static_cast<int>(std::min<int64_t>(max_tasks, num_sms()));
   cudaError_t e;
   if (D == 128)

@@ -148,9 +148,10 @@ template <bool PAIRS>
 __global__ void __launch_bounds__(kMergeThreads) merge_lists_kernel(
     const uint2* __restrict__ lists, const int* __restrict__ counts, int n_lists, int64_t q_stride, int64_t r_stride,
     int cap, int k, int64_t id_offset, int64_t* __restrict__ out_ids, float* __restrict__ out_scores,
-    uint2* __restrict__ out_pairs) {
+    uint2* __restrict__ out_pairs, const int* __restrict__ row_live) {
   __shared__ SelectShared sh;
   const int q = blockIdx.x;
+  if (row_live != nullptr && row_live[q] == 0) return;  // the whole block: this row keeps its output
   const int tid = threadIdx.x;
   const uint2* qlists = lists + static_cast<int64_t>(q) * q_stride;
 
@@ -360,7 +361,7 @@ __global__ void fill_empty_kernel(int64_t* out_ids, float* out_scores, size_t n)
 
 static int merge_launch(const uint2* lists, const int* counts, int B, int n_lists, int64_t q_stride,
                         int64_t r_stride, int cap, int k, int64_t id_offset, int64_t* out_ids, float* out_scores,
-                        uint2* out_pairs, cudaStream_t stream) {
+                        uint2* out_pairs, cudaStream_t stream, const int* row_live = nullptr) {
   if (k < 1 || k > kMaxK) {
     set_last_error("merge: k must be in [1, 1024]");
     return RB_ERR_INVALID_ARG;
@@ -372,10 +373,10 @@ static int merge_launch(const uint2* lists, const int* counts, int B, int n_list
   if (B == 0) return RB_OK;
   if (out_pairs != nullptr)
     merge_lists_kernel<true><<<B, kMergeThreads, 0, stream>>>(lists, counts, n_lists, q_stride, r_stride, cap, k,
-                                                               id_offset, nullptr, nullptr, out_pairs);
+                                                               id_offset, nullptr, nullptr, out_pairs, row_live);
   else
     merge_lists_kernel<false><<<B, kMergeThreads, 0, stream>>>(lists, counts, n_lists, q_stride, r_stride, cap, k,
-                                                                id_offset, out_ids, out_scores, nullptr);
+                                                                id_offset, out_ids, out_scores, nullptr, row_live);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_last_error(cudaGetErrorString(e));
@@ -385,9 +386,9 @@ static int merge_launch(const uint2* lists, const int* counts, int B, int n_list
 }
 
 int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,
-                int64_t* out_ids, float* out_scores, uint2* out_pairs, cudaStream_t stream) {
+                int64_t* out_ids, float* out_scores, uint2* out_pairs, cudaStream_t stream, const int* row_live) {
   return merge_launch(lists, counts, B, n_lists, static_cast<int64_t>(n_lists) * stride, stride, stride, k, id_offset,
-                      out_ids, out_scores, out_pairs, stream);
+                      out_ids, out_scores, out_pairs, stream, row_live);
 }
 
 int merge_pair_stack(const uint2* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,

@@ -39,15 +39,17 @@ size_t dense_chunk_stride(const DensePlan& pl);
 int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
                     int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
                     cudaStream_t stream, const float* q_scale = nullptr, const float* x_scale = nullptr,
-                    const FilterArgs* filter = nullptr);
+                    const FilterArgs* filter = nullptr, const int* qsg_live = nullptr);
 // Per row of vals [B, n] (row stride `stride`): a lower bound on the k-th
 // largest value (exact to 22 leading key bits), -inf when n < k.
 int row_kth_lower_bound(const float* vals, int B, int n, int64_t stride, int nseg, int64_t seg_stride, int k,
                         float* out, float* out_vals, cudaStream_t stream);
 
 // Merge of per-(query, split) candidate lists into the final sorted top-k.
+// row_live (optional): only rows with a nonzero entry are written.
 int merge_lists(const uint2* lists, const int* counts, int B, int n_lists, int stride, int k, int64_t id_offset,
-                int64_t* out_ids, float* out_scores, uint2* out_pairs, cudaStream_t stream);
+                int64_t* out_ids, float* out_scores, uint2* out_pairs, cudaStream_t stream,
+                const int* row_live = nullptr);
 int merge_pair_stack(const uint2* pairs, int W, int B, int kin, int k, int64_t* out_ids, float* out_scores,
                      cudaStream_t stream);
 

@@ -65,6 +65,36 @@ def test_filtered_topk_exact(mode, b, n, k):
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
 
 
+@pytest.mark.parametrize("mode", ["exact", "bloom_recheck"])
+@pytest.mark.parametrize("b,n,k", [(200, 400_000, 10), (130, 1_000_000, 100)])
+def test_speculative_seed_and_second_pass(mode, b, n, k):
+    """Corpora large enough for a sampled seed: the full pass starts from the speculative
+    seed (the ceil(3k / s)-th sampled chunk max); rows that come back with fewer than k
+    results (a value no item holds, a rare conjunction, an unlucky sample) run again from
+    the safe seed. Bit for bit the oracle's either way."""
+    from retrieve_b200 import ops
+
+    attrs = gi.zipf_attrs(n, seed=n + 1)
+    attrs3 = attrs[:, :, None].contiguous()
+    q = make_int_rows(b, 128, seed=7)
+    x = make_int_rows(n, 128, seed=8)
+    exprs = [EXPRS[i % len(EXPRS)] for i in range(b)]
+    for r in range(0, b, 9):
+        exprs[r] = "0:12345"  # no item holds the value
+    for r in range(4, b, 9):
+        exprs[r] = "5:0 AND 6:1 AND 7:2 AND 1:3"  # a few hundred items at most
+    preds = P.from_expressions(exprs).to("cuda")
+    words = ops.bloom_build(attrs3.cuda(), 3)
+    ids, scores = ops.dense_topk_filtered(q.cuda(), x.cuda(), k, preds.terms, preds.n_terms, mode,
+                                          attrs3.cuda(), words)
+    masks = _masks(exprs, b, attrs=attrs.numpy())
+    if mode == "bloom_recheck":
+        masks &= _masks(exprs, b, words=words.cpu().numpy().view(np.uint64))
+    assert not masks[0].any()
+    ref_ids, ref_scores = _oracle(q, x, k, masks)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+
+
 def test_linr_clause_queries_filtered():
     """LiNR V1 semantics: AND of clause values with reverse clauses."""
     from oracle import filters
