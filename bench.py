@@ -319,6 +319,9 @@ def main():
     if world > 1:
         from datetime import timedelta
 
+        # NCCL's communicator lines (ranks per communicator) stay in the log
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     from retrieve_b200 import _lib

@@ -100,6 +100,103 @@ __global__ void spec_check_kernel(const int64_t* __restrict__ out_ids, int B, in
   if (again) atomicOr(&qsg_live[q / queries_per_group], 1);
 }
 
+// The same for batches of more than kSpecRows rows, one block: the first kSpecRows short rows
+// (in row order) go to fail_rows for the compact second pass; any further ones are marked for
+// the pass over their query groups (row_live, seed, qsg_live) as spec_check_kernel does.
+// fail_rows is padded with -1; *c_live says whether the compact pass has a row.
+__global__ void __launch_bounds__(1024) spec_select_kernel(const int64_t* __restrict__ out_ids, int B, int k,
+                                                           const float* __restrict__ safe, float* __restrict__ seed,
+                                                           int* __restrict__ row_live, int* __restrict__ qsg_live,
+                                                           int queries_per_group, int* __restrict__ fail_rows,
+                                                           int* __restrict__ c_live) {
+  __shared__ int warp_count[32];
+  __shared__ int found;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (threadIdx.x == 0) found = 0;
+  __syncthreads();
+  for (int q0 = 0; q0 < B; q0 += blockDim.x) {
+    const int q = q0 + static_cast<int>(threadIdx.x);
+    const bool again = q < B && out_ids[static_cast<int64_t>(q) * k + (k - 1)] < 0 && safe[q] < seed[q];
+    const uint32_t bal = __ballot_sync(RB_FULL_MASK, again);
+    if (lane == 0) warp_count[w] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) {
+      before += i < w ? warp_count[i] : 0;
+      total += warp_count[i];
+    }
+    const int pos = found + before + __popc(bal & lanemask_lt());
+    if (q < B) {
+      if (again && pos < kSpecRows) {
+        fail_rows[pos] = q;  // the compact pass takes it
+        row_live[q] = 0;
+        seed[q] = __int_as_float(0x7fc00000);
+      } else if (again) {
+        row_live[q] = 1;
+        seed[q] = safe[q];
+        atomicOr(&qsg_live[q / queries_per_group], 1);
+      } else {
+        row_live[q] = 0;
+        seed[q] = __int_as_float(0x7fc00000);
+      }
+    }
+    __syncthreads();  // every thread has read `found` and warp_count
+    if (threadIdx.x == 0) found += total;
+    __syncthreads();
+  }
+  for (int c = found + static_cast<int>(threadIdx.x); c < kSpecRows; c += blockDim.x) fail_rows[c] = -1;
+  if (threadIdx.x == 0) *c_live = found > 0 ? 1 : 0;
+}
+
+// Row c of the compact batch: short row fail_rows[c]'s query, query scale, safe seed and
+// predicate terms (zero query, NaN seed and no terms for a padding row).
+__global__ void spec_gather_kernel(const int* __restrict__ fail_rows, const uint8_t* __restrict__ queries,
+                                   int row_bytes, const float* __restrict__ q_scale, const float* __restrict__ safe,
+                                   const PredTerm* __restrict__ terms, const int* __restrict__ n_terms,
+                                   uint8_t* __restrict__ qc, float* __restrict__ qsc, float* __restrict__ seedc,
+                                   PredTerm* __restrict__ termsc, int* __restrict__ ntc, int* __restrict__ row_live_c) {
+  const int c = blockIdx.x;
+  const int src = fail_rows[c];
+  const int n16 = row_bytes / 16;
+  int4* dst = reinterpret_cast<int4*>(qc + static_cast<size_t>(c) * row_bytes);
+  const int4* from = reinterpret_cast<const int4*>(queries + static_cast<size_t>(src < 0 ? 0 : src) * row_bytes);
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src >= 0 ? from[i] : make_int4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    qsc[c] = (src >= 0 && q_scale != nullptr) ? q_scale[src] : 1.f;
+    seedc[c] = src >= 0 ? safe[src] : __int_as_float(0x7fc00000);
+    row_live_c[c] = src >= 0 ? 1 : 0;
+    if (terms != nullptr) ntc[c] = src >= 0 ? n_terms[src] : 0;
+  }
+  if (terms != nullptr && static_cast<int>(threadIdx.x) < kMaxTerms)
+    termsc[c * kMaxTerms + threadIdx.x] =
+        src >= 0 ? terms[static_cast<size_t>(src) * kMaxTerms + threadIdx.x] : PredTerm{0, 0, 0, 0};
+}
+
+// The compact pass's results back to their rows.
+__global__ void spec_scatter_kernel(const int* __restrict__ fail_rows, int k, const int64_t* __restrict__ idsc,
+                                    const float* __restrict__ scoresc, int64_t* __restrict__ out_ids,
+                                    float* __restrict__ out_scores) {
+  const int c = blockIdx.x;
+  const int src = fail_rows[c];
+  if (src < 0) return;
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    out_ids[static_cast<int64_t>(src) * k + j] = idsc[static_cast<int64_t>(c) * k + j];
+    out_scores[static_cast<int64_t>(src) * k + j] = scoresc[static_cast<int64_t>(c) * k + j];
+  }
+}
+
+// The rank of the speculative seed among the sampled chunk maxima (dense_topk_impl), and
+// where it pays: the filtered and dequantizing epilogues cost in proportion to the chunks
+// that reach the threshold; the plain fp16/bf16 epilogue is cheap enough that the second
+// pass a short row sets off (its query group's MMAs again) costs more than it saves.
+constexpr int kSpecFactor = 3;
+static bool dense_spec_applies(int elem, const FilterArgs* filter) {
+  return elem == 2 || (filter != nullptr && filter->mode != kFilterNone);
+}
+static int dense_spec_rank(int k, const DensePlan& pl) {
+  return static_cast<int>((static_cast<int64_t>(kSpecFactor) * k + pl.sample_stride - 1) / pl.sample_stride);
+}
+
 struct DenseWs {
   uint2* lists;
   int* counts;
@@ -107,16 +204,59 @@ struct DenseWs {
   int* err;
 };
 
+// The layout of dense_workspace_bytes: the candidate lists share their region with the
+// sampling pass's chunk maxima, so the counts and seeds start past the larger of the two
+// (the seeds are written while the chunk maxima are still being read).
 static DenseWs dense_ws(void* workspace, size_t workspace_bytes, int B, const DensePlan& pl) {
   DenseWs d;
   uint8_t* w = static_cast<uint8_t*>(workspace);
   d.lists = reinterpret_cast<uint2*>(w);
-  w += align_up(static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2), 256);
+  const size_t lists = static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2);
+  const size_t cm = static_cast<size_t>(B) * dense_chunk_stride(pl) * sizeof(float);
+  w += align_up(std::max(lists, cm), 256);
   d.counts = reinterpret_cast<int*>(w);
   w += align_up(static_cast<size_t>(B) * pl.n_lists * sizeof(int), 256);
   d.thresh = reinterpret_cast<float*>(w);
   d.err = ws_err_word(workspace, workspace_bytes);
   return d;
+}
+
+// The compact second pass's buffers, after the seeds: kSpecRows query rows (up to 512 bytes)
+// | their terms | ids | scores [kSpecRows, k] | row indices, query scales, seeds, term counts,
+// row flags (kSpecRows each) | the pass's live flag (dense_workspace_bytes reserves them).
+struct SpecWs {
+  uint8_t* queries;
+  PredTerm* terms;
+  int64_t* ids;
+  float* scores;
+  int* fail_rows;
+  float* q_scale;
+  float* seed;
+  int* n_terms;
+  int* row_live;
+  int* live;
+};
+
+static SpecWs spec_ws(const DenseWs& d, int B, const DensePlan& pl, int k) {
+  (void)pl;
+  uint8_t* w = reinterpret_cast<uint8_t*>(d.thresh) + align_up((4 * static_cast<size_t>(B) + 64) * sizeof(float), 256);
+  SpecWs c;
+  auto take = [&](size_t bytes) {
+    uint8_t* at = w;
+    w += align_up(bytes, 256);
+    return at;
+  };
+  c.queries = take(static_cast<size_t>(kSpecRows) * 512);
+  c.terms = reinterpret_cast<PredTerm*>(take(static_cast<size_t>(kSpecRows) * kMaxTerms * sizeof(PredTerm)));
+  c.ids = reinterpret_cast<int64_t*>(take(static_cast<size_t>(kSpecRows) * k * sizeof(int64_t)));
+  c.scores = reinterpret_cast<float*>(take(static_cast<size_t>(kSpecRows) * k * sizeof(float)));
+  c.fail_rows = reinterpret_cast<int*>(take(kSpecRows * sizeof(int)));
+  c.q_scale = reinterpret_cast<float*>(take(kSpecRows * sizeof(float)));
+  c.seed = reinterpret_cast<float*>(take(kSpecRows * sizeof(float)));
+  c.n_terms = reinterpret_cast<int*>(take(kSpecRows * sizeof(int)));
+  c.row_live = reinterpret_cast<int*>(take(kSpecRows * sizeof(int)));
+  c.live = reinterpret_cast<int*>(take(sizeof(int)));
+  return c;
 }
 
 static int dense_topk_impl(int elem, const void* queries, const float* q_scale, const void* items,
@@ -153,17 +293,19 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   }
 
   DensePlan pl;
-  const bool filtered = filter != nullptr && filter->mode != kFilterNone;
   dense_plan(B, N, k, row_bytes, pl, shared ? shared->n_total : N, elem >= 2);
   const DenseWs d = dense_ws(workspace, workspace_bytes, B, pl);
   if (cudaMemsetAsync(d.err, 0, sizeof(int), stream) != cudaSuccess) return fail(RB_ERR_CUDA, "memset failed");
 
   ProfileEvents& pe = profile_events();
   const float* seed = nullptr;
-  // Filtered searches seed the full pass speculatively: the ceil(3k / s)-th largest sampled
-  // chunk max instead of the k-th (s = the sample's tile stride). About 3k items of the
-  // corpus pass it, so the rows append and test about s / 3 times fewer candidates; a row
-  // that still finds fewer than k runs again from the safe seed (spec_check_kernel).
+  // Filtered and int8 searches start the full pass from a speculative seed: the
+  // ceil(kSpecFactor k / s)-th largest
+  // sampled chunk max instead of the k-th (s = the sample's tile stride). About kSpecFactor k
+  // items of the corpus pass it (a count whose spread is about 1 / sqrt(kSpecFactor k / s)),
+  // so the rows test about s / kSpecFactor times fewer candidates; a row that still finds
+  // fewer than k runs again from the safe seed (spec_check_kernel), and with it the rest of
+  // its query group's MMAs (rare: a row's count falls below k / 3 of its mean).
   bool spec = false;
   if (shared != nullptr) {
     // k-th largest of the union of the shards' samples (a [W, B, k] stack)
@@ -177,8 +319,8 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
                          stream, q_scale, x_scale, filter);
     if (rc != RB_OK) return rc;
     const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
-    const int k_spec = (3 * k + pl.sample_stride - 1) / pl.sample_stride;
-    spec = filtered && out_pairs == nullptr && k_spec < k;
+    const int k_spec = dense_spec_rank(k, pl);
+    spec = dense_spec_applies(elem, filter) && out_pairs == nullptr && k_spec < k;
     rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, spec ? k_spec : k, d.thresh, nullptr, stream);
     if (rc != RB_OK) return rc;
     if (spec) {  // the safe seed, kept for the rows that need a second pass
@@ -204,10 +346,47 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
     return fail(RB_ERR_CUDA, "memset failed");
   // queries of one query group: ng MMA tiles of 128 rows, doubled across a CTA pair
   const int per_group = pl.ng * (pl.two_sm ? 256 : 128);
-  spec_check_kernel<<<(B + 255) / 256, 256, 0, stream>>>(out_ids, B, k, d.thresh + B, d.thresh, row_live, qsg_live,
-                                                         per_group);
-  if (cudaGetLastError() != cudaSuccess) return fail(RB_ERR_CUDA, "spec_check launch failed");
-  // the second pass scans only the query groups holding such a row
+  if (B <= kSpecRows) {
+    spec_check_kernel<<<(B + 255) / 256, 256, 0, stream>>>(out_ids, B, k, d.thresh + B, d.thresh, row_live,
+                                                           qsg_live, per_group);
+    if (cudaGetLastError() != cudaSuccess) return fail(RB_ERR_CUDA, "spec_check launch failed");
+  } else {
+    // Up to kSpecRows short rows run again as one compact 128-row batch on the 1-SM kernel
+    // (their queries, scales, seeds and terms gathered), its lists in the main lists region.
+    const SpecWs c = spec_ws(d, B, pl, k);
+    spec_select_kernel<<<1, 1024, 0, stream>>>(out_ids, B, k, d.thresh + B, d.thresh, row_live, qsg_live,
+                                               per_group, c.fail_rows, c.live);
+    const int row_bytes_q = (elem == 2 || elem == 4) ? D : 2 * D;
+    FilterArgs fc{};
+    if (filter != nullptr) fc = *filter;
+    spec_gather_kernel<<<kSpecRows, 128, 0, stream>>>(
+        c.fail_rows, static_cast<const uint8_t*>(queries), row_bytes_q, q_scale, d.thresh + B,
+        filter != nullptr ? filter->terms : nullptr, filter != nullptr ? filter->n_terms : nullptr, c.queries,
+        c.q_scale, c.seed, c.terms, c.n_terms, c.row_live);
+    if (cudaGetLastError() != cudaSuccess) return fail(RB_ERR_CUDA, "spec gather launch failed");
+    fc.terms = c.terms;
+    fc.n_terms = c.n_terms;
+    DensePlan pc;
+    dense_plan(kSpecRows, N, k, row_bytes_q, pc, N, elem >= 2);
+    // as many splits as the main lists region (and counts region) holds
+    const size_t region = align_up(std::max(static_cast<size_t>(B) * pl.n_lists * pl.cap * sizeof(uint2),
+                                            static_cast<size_t>(B) * dense_chunk_stride(pl) * sizeof(float)),
+                                   256);
+    const int64_t fit_lists = static_cast<int64_t>(region / (static_cast<size_t>(kSpecRows) * pc.cap * sizeof(uint2)));
+    const int64_t fit_counts = static_cast<int64_t>(B) * pl.n_lists / kSpecRows;
+    pc.n_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({fit_lists, fit_counts, pc.n_splits})));
+    pc.n_lists = pc.n_splits;
+    rc = dense_scan_pass(0, elem, c.queries, items, kSpecRows, N, D, pc, k, c.seed, d.lists, d.counts, nullptr, d.err,
+                         stream, q_scale != nullptr ? c.q_scale : nullptr, x_scale, filter != nullptr ? &fc : nullptr,
+                         c.live);
+    if (rc != RB_OK) return rc;
+    rc = merge_lists(d.lists, d.counts, kSpecRows, pc.n_lists, pc.cap, k, id_offset, c.ids, c.scores, nullptr, stream,
+                     c.row_live);
+    if (rc != RB_OK) return rc;
+    spec_scatter_kernel<<<kSpecRows, 128, 0, stream>>>(c.fail_rows, k, c.ids, c.scores, out_ids, out_scores);
+    if (cudaGetLastError() != cudaSuccess) return fail(RB_ERR_CUDA, "spec scatter launch failed");
+  }
+  // the rows left scan again with their query groups (no group: every task skipped)
   rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, d.thresh, d.lists, d.counts, nullptr, d.err, stream,
                        q_scale, x_scale, filter, qsg_live);
   if (rc != RB_OK) return rc;
@@ -346,7 +525,13 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
   }
   DensePlan pl;
   dense_plan(B, N, k, dense_row_bytes(D, dtype), pl, N, dense_scaled(dtype));
-  *n_launches = (pl.sample_stride > 0) ? 4 : 2;
+  if (pl.sample_stride == 0) {
+    *n_launches = 2;  // full pass, merge
+  } else if (dense_spec_applies(dtype == RB_I8 ? 2 : 0, nullptr) && dense_spec_rank(k, pl) < k) {
+    *n_launches = 8;  // sample pass, 2 row selects, full pass, merge, check, second pass, merge
+  } else {
+    *n_launches = 4;  // sample pass, row select, full pass, merge
+  }
   return RB_OK;
 }
 

@@ -144,7 +144,15 @@ size_t dense_workspace_bytes(int B, int N, int k, int row_bytes, bool scaled) {
   size_t th = (4 * static_cast<size_t>(B) + 64) * sizeof(float);
   size_t cm = static_cast<size_t>(B) * dense_chunk_stride(pl) * sizeof(float);
   // the chunk maxima are dead once the seed is known: they share the list space
-  return align_up(std::max(lists, cm), 256) + align_up(counts, 256) + align_up(th, 256) + 256;
+  return align_up(std::max(lists, cm), 256) + align_up(counts, 256) + align_up(th, 256) + dense_spec_ws_bytes(k) +
+         256;
+}
+
+size_t dense_spec_ws_bytes(int k) {
+  const size_t r = kSpecRows;
+  return align_up(r * 512, 256) + align_up(r * kMaxTerms * sizeof(PredTerm), 256) +
+         align_up(r * static_cast<size_t>(k) * sizeof(int64_t), 256) +
+         align_up(r * static_cast<size_t>(k) * sizeof(float), 256) + 5 * align_up(r * sizeof(int), 256) + 256;
 }
 
 int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,

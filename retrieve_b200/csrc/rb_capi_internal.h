@@ -28,6 +28,10 @@ struct DensePlan {
 };
 
 void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_total = 0, bool scaled = false);
+// Rows a speculative search's compact second pass takes (one 128-row query group), and the
+// workspace its buffers need past the seeds (capi.cu's SpecWs).
+constexpr int kSpecRows = 128;
+size_t dense_spec_ws_bytes(int k);
 size_t dense_workspace_bytes(int B, int N, int k, int row_bytes, bool scaled = false);
 // Element types with the per-query / per-item dequant in the epilogue.
 inline bool dense_scaled(int dtype) { return dtype == RB_I8 || dtype == RB_E4M3; }

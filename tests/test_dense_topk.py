@@ -58,6 +58,37 @@ def test_dense_topk_sampled_levels_exact():
     assert_topk_exact(ids, scores, ref_ids, ref_scores)
 
 
+def _device_topk_ties_low(q, x, k, chunk=1 << 18):
+    """Plain PyTorch reference on the GPU for integer-valued rows: fp32 matmul (exact here),
+    then top-k on the 64-bit key (score << 32 | ~id), so ties go to the lower id."""
+    best = None
+    for lo in range(0, x.shape[0], chunk):
+        s = (q.float() @ x[lo : lo + chunk].float().t()).to(torch.int64)
+        ids = torch.arange(lo, lo + s.shape[1], device=q.device, dtype=torch.int64)
+        key = (s << 32) | (0xFFFFFFFF - ids)[None, :]
+        if best is not None:
+            key = torch.cat([best, key], dim=1)
+        best = torch.topk(key, min(k, key.shape[1]), dim=1).values
+    ids = 0xFFFFFFFF - (best & 0xFFFFFFFF)
+    return ids, (best >> 32).to(torch.float32)
+
+
+def test_dense_topk_10m_integer_exact_on_device():
+    """At the benchmark's shape (10M x 128 bf16, B = 1024, k = 100) the sampling pass's chunk
+    maxima fill more workspace than the candidate lists; the seeds and counts sit past both.
+    Checked against the PyTorch reference on the device (integer values: exact)."""
+    from retrieve_b200 import ops
+
+    b, n, d, k = 1024, 10_000_000, 128, 100
+    g = torch.Generator(device="cuda").manual_seed(51)
+    q = torch.randint(-8, 9, (b, d), generator=g, device="cuda").to(torch.bfloat16)
+    x = torch.randint(-8, 9, (n, d), generator=g, device="cuda").to(torch.bfloat16)
+    ids, scores = ops.dense_topk(q, x, k)
+    ref_ids, ref_scores = _device_topk_ties_low(q, x, k)
+    assert torch.equal(scores, ref_scores)
+    assert torch.equal(ids, ref_ids)
+
+
 def test_dense_topk_ascending_scores_compaction_storm():
     """Items ordered so every query's scores rise with the id: every item beats
     the running threshold, forcing list compaction on every chunk."""

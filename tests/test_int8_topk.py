@@ -34,6 +34,33 @@ def test_int8_topk_bit_exact(b, n, d, k):
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
 
 
+@pytest.mark.parametrize("short_rows", [1, 150])
+def test_int8_speculative_seed_second_pass(short_rows):
+    """The int8 full pass starts from a speculative seed (a high sampled chunk max). The first
+    `short_rows` queries see their best items only in the sampled tiles (one per 32-item
+    chunk, every 16th tile), so fewer than k items reach that seed: those rows come back
+    short and run again from the safe seed, the first 128 as one compact batch, the rest
+    with their query groups. The other rows are random. Bit for bit the oracle's."""
+    from retrieve_b200 import ops
+
+    b, n, d, k = 200, 400_000, 128, 10
+    g = torch.Generator().manual_seed(43)
+    codes = torch.randint(-3, 4, (n, d), generator=g).to(torch.int8)
+    scales = torch.ones(n, dtype=torch.float32)
+    q = torch.randn(b, d, generator=g)
+    q[:short_rows] = 0
+    q[:short_rows, 0], q[:short_rows, 1] = 16.0, 1.0  # quantized to codes 127 and 8
+    tiles = torch.arange(0, n // 128, 16)
+    heads = (tiles[:, None] * 128 + torch.arange(0, 128, 32)[None, :]).reshape(-1)
+    r = torch.arange(heads.numel())
+    codes[heads, 0] = (20 + r // 16).to(torch.int8)  # dots 127 x0 + 8 x1, distinct and rising with r
+    codes[heads, 1] = (r % 16).to(torch.int8)
+    ids, scores = ops.int8_topk(q.cuda(), codes.cuda(), scales.cuda(), k)
+    ref_ids, ref_scores = knn.int8_topk(q.numpy(), codes.numpy(), scales.numpy(), k)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+    assert set(ref_ids[0].tolist()) <= set(heads.tolist())
+
+
 def test_int8_global_scale_equals_silvertorch_full_probe():
     """With one global item scale the ranking is the raw int32 dot's, as in
     SilverTorch's st::search with every cluster probed."""
