@@ -185,16 +185,20 @@ __global__ void spec_scatter_kernel(const int* __restrict__ fail_rows, int k, co
   }
 }
 
-// The rank of the speculative seed among the sampled chunk maxima (dense_topk_impl), and
-// where it pays: the filtered and dequantizing epilogues cost in proportion to the chunks
-// that reach the threshold; the plain fp16/bf16 epilogue is cheap enough that the second
-// pass a short row sets off (its query group's MMAs again) costs more than it saves.
-constexpr int kSpecFactor = 3;
+// The rank F k / s of the speculative seed among the sampled chunk maxima (dense_topk_impl),
+// and where it pays: the filtered and dequantizing epilogues cost in proportion to the chunks
+// that reach the threshold; the plain fp16/bf16 epilogue is cheap enough that the extra
+// passes cost more than they save.
+// F = 2 for the filtered scan (measured at 10M items, 10 % selectivity: 12.2 ms a pass against
+// 13.8 at F = 3); F = 3 for int8, whose second passes cost more (38.2 ms at F = 3, 40.5 at F = 2).
 static bool dense_spec_applies(int elem, const FilterArgs* filter) {
   return elem == 2 || (filter != nullptr && filter->mode != kFilterNone);
 }
-static int dense_spec_rank(int k, const DensePlan& pl) {
-  return static_cast<int>((static_cast<int64_t>(kSpecFactor) * k + pl.sample_stride - 1) / pl.sample_stride);
+static int dense_spec_factor(const FilterArgs* filter) {
+  return (filter != nullptr && filter->mode != kFilterNone) ? 2 : 3;
+}
+static int dense_spec_rank(int k, const DensePlan& pl, int factor) {
+  return static_cast<int>((static_cast<int64_t>(factor) * k + pl.sample_stride - 1) / pl.sample_stride);
 }
 
 struct DenseWs {
@@ -300,12 +304,11 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   ProfileEvents& pe = profile_events();
   const float* seed = nullptr;
   // Filtered and int8 searches start the full pass from a speculative seed: the
-  // ceil(kSpecFactor k / s)-th largest
-  // sampled chunk max instead of the k-th (s = the sample's tile stride). About kSpecFactor k
-  // items of the corpus pass it (a count whose spread is about 1 / sqrt(kSpecFactor k / s)),
-  // so the rows test about s / kSpecFactor times fewer candidates; a row that still finds
-  // fewer than k runs again from the safe seed (spec_check_kernel), and with it the rest of
-  // its query group's MMAs (rare: a row's count falls below k / 3 of its mean).
+  // ceil(F k / s)-th largest sampled chunk max instead of the k-th (s = the sample's tile
+  // stride). About F k items of the corpus reach it (a count whose spread is about
+  // 1 / sqrt(F k / s)), so the rows test about s / F times fewer candidates; a row that still
+  // finds fewer than k runs again from the safe seed, in the compact batch of up to 128 such
+  // rows or, past those, with its query group.
   bool spec = false;
   if (shared != nullptr) {
     // k-th largest of the union of the shards' samples (a [W, B, k] stack)
@@ -319,7 +322,7 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
                          stream, q_scale, x_scale, filter);
     if (rc != RB_OK) return rc;
     const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
-    const int k_spec = dense_spec_rank(k, pl);
+    const int k_spec = dense_spec_rank(k, pl, dense_spec_factor(filter));
     spec = dense_spec_applies(elem, filter) && out_pairs == nullptr && k_spec < k;
     rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, spec ? k_spec : k, d.thresh, nullptr, stream);
     if (rc != RB_OK) return rc;
@@ -527,7 +530,7 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
   dense_plan(B, N, k, dense_row_bytes(D, dtype), pl, N, dense_scaled(dtype));
   if (pl.sample_stride == 0) {
     *n_launches = 2;  // full pass, merge
-  } else if (dense_spec_applies(dtype == RB_I8 ? 2 : 0, nullptr) && dense_spec_rank(k, pl) < k) {
+  } else if (dense_spec_applies(dtype == RB_I8 ? 2 : 0, nullptr) && dense_spec_rank(k, pl, 3) < k) {
     *n_launches = 8;  // sample pass, 2 row selects, full pass, merge, check, second pass, merge
   } else {
     *n_launches = 4;  // sample pass, row select, full pass, merge
