@@ -225,13 +225,26 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         uint32_t pm;
         if (use_sl) {
           pm = bloom_chunk_mask(sl + ch * 64, st) & valid;
-          if (p.filter.mode == kFilterBloomRecheck) pm = pred_exact_bits(p.filter, q, id0, pm);
         } else {
           pm = pred_pass_bits(p.filter, q, id0, valid);
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (!((pm >> j) & 1u)) r[ch][j] = 0x7fc00000u;
+        if (use_sl && p.filter.mode == kFilterBloomRecheck) {
+          // recheck only the chunk's best Bloom-passing item (the lowest index among equal
+          // scores): the chunk then counts that item if it passes exactly, else nothing.
+          // Either way the sampled maxima stay scores of distinct passing items.
+          const float mx = max32(r[ch]);
+          uint32_t at = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) at |= static_cast<uint32_t>(__uint_as_float(r[ch][j]) == mx) << j;
+          at &= pm;
+          const uint32_t keep = at != 0u ? pred_exact_bits(p.filter, q, id0, at & (~at + 1u)) : 0u;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (!((keep >> j) & 1u)) r[ch][j] = 0x7fc00000u;
+        }
       }
     }
   }
