@@ -531,24 +531,42 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_after();
         const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
-        // The whole 128-column row in one go, then the accumulator goes back to
-        // the MMA warp before any filtering work.
-        uint32_t r[4][32];
-        __syncwarp();
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r[ch]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        // Unfiltered: the whole 128-column row in one go, then the accumulator goes
+        // back to the MMA warp before any filtering work.
         if constexpr (FILT) {
+          // One 32-item chunk at a time, TMEM as the staging: a single copy of the filtered
+          // chunk code (four unrolled copies overflow the instruction cache), and 32 score
+          // registers instead of 128. The accumulator goes back after its last load.
           if (sliced) {
             cp_async_wait_all();
             __syncwarp();
           }
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t r1[1][32];
+            __syncwarp();
+            tmem_ld_32x32(col0 + ch * 32, r1[0]);
+            tmem_wait_ld();
+            if (ch == 3) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            }
+            process_chunks<MODE, 1, ELEM, FILT, KB>(p, r1, row0 + ch * 32, pt * 4 + ch, valid_q, q, thresh, count,
+                                                    list, hist, sl + ch * 64, st, use_sl);
+          }
+        } else {
+          uint32_t r[4][32];
+          __syncwarp();
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r[ch]);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
+                                                  use_sl);
         }
-        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
-                                                use_sl);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -860,22 +878,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_after();
         const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
-        uint32_t r[4][32];
-        __syncwarp();
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r[ch]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
         if constexpr (FILT) {
+          // One 32-item chunk at a time, TMEM as the staging: a single copy of the filtered
+          // chunk code (four unrolled copies overflow the instruction cache), and 32 score
+          // registers instead of 128. The accumulator goes back after its last load.
           if (sliced) {
             cp_async_wait_all();
             __syncwarp();
           }
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t r1[1][32];
+            __syncwarp();
+            tmem_ld_32x32(col0 + ch * 32, r1[0]);
+            tmem_wait_ld();
+            if (ch == 3) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
+            }
+            process_chunks<MODE, 1, ELEM, FILT, KB>(p, r1, row0 + ch * 32, pt * 4 + ch, valid_q, q, thresh, count,
+                                                    list, hist, sl + ch * 64, st, use_sl);
+          }
+        } else {
+          uint32_t r[4][32];
+          __syncwarp();
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r[ch]);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
+          process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
+                                                  use_sl);
         }
-        process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
-                                                use_sl);
         if (++acc == kAcc) {
           acc = 0;
           acc_phase ^= 1;
