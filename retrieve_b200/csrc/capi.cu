@@ -185,14 +185,17 @@ __global__ void spec_scatter_kernel(const int* __restrict__ fail_rows, int k, co
   }
 }
 
-// The rank F k / s of the speculative seed among the sampled chunk maxima (dense_topk_impl),
-// and where it pays: the filtered and dequantizing epilogues cost in proportion to the chunks
-// that reach the threshold; the plain fp16/bf16 epilogue is cheap enough that the extra
-// passes cost more than they save.
+// The rank F k / s of the speculative seed among the sampled chunk maxima (dense_topk_impl).
+// Every epilogue costs in proportion to the chunks that reach the threshold: from the safe
+// seed (rank about k s) the plain fp16 / bf16 pass appends in about half of its 32 x 128
+// warp-tiles, and those appends, not the MMA, set its pace.
 // F = 2 for the filtered scan (measured at 10M items, 10 % selectivity: 12.2 ms a pass against
-// 13.8 at F = 3); F = 3 for int8, whose second passes cost more (38.2 ms at F = 3, 40.5 at F = 2).
+// 13.8 at F = 3); F = 3 for int8, whose second passes cost more (38.2 ms at F = 3, 40.5 at F = 2),
+// and for fp16 / bf16.
 static bool dense_spec_applies(int elem, const FilterArgs* filter) {
-  return elem == 2 || (filter != nullptr && filter->mode != kFilterNone);
+  (void)elem;
+  (void)filter;
+  return true;
 }
 static int dense_spec_factor(const FilterArgs* filter) {
   return (filter != nullptr && filter->mode != kFilterNone) ? 2 : 3;
@@ -531,7 +534,9 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
   if (pl.sample_stride == 0) {
     *n_launches = 2;  // full pass, merge
   } else if (dense_spec_applies(dtype == RB_I8 ? 2 : 0, nullptr) && dense_spec_rank(k, pl, 3) < k) {
-    *n_launches = 8;  // sample pass, 2 row selects, full pass, merge, check, second pass, merge
+    // sample pass, 2 row selects, full pass, merge, then (B <= 128) check, second pass, merge;
+    // or (B > 128) select, gather, compact pass, merge, scatter, second pass, merge
+    *n_launches = B <= kSpecRows ? 8 : 12;
   } else {
     *n_launches = 4;  // sample pass, row select, full pass, merge
   }

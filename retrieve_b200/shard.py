@@ -264,7 +264,7 @@ class ShardedDenseTopK:
         )
         if self.world == 1:
             return n.value
-        sampled = n.value == 4
+        sampled = n.value >= 4
         # sample pass + row select (or the -inf fill), union select, full pass,
         # list merge into pairs, then the merge of the gathered pairs
         return (2 if sampled else 1) + 1 + 2 + 1
