@@ -268,11 +268,17 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
       all = fmaxf(all, cm[ch]);
     }
     if (__any_sync(RB_FULL_MASK, valid_q && all >= thresh)) {
+      if constexpr (!FILT) {
+        // the warp appends the chunks some lane may keep (stage: the upper half of the
+        // warp's scratch; the int8 item scales use the lower half)
+        uint32_t pass = 0;
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch) pass |= static_cast<uint32_t>(valid_q && cm[ch] >= thresh) << ch;
+        warp_append_chunks<NCH>(list, count, thresh, r, pass, row0, stage + 128);
+      }
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
-        if constexpr (!FILT) {
-          if (valid_q && cm[ch] >= thresh) append_chunk_bits(list, count, thresh, r[ch], row0 + ch * 32);
-        } else {
+        if constexpr (FILT) {
           // the items over the threshold, then the Bloom test of the chunk (32 items a
           // term) on those; the predicate item by item only where some item is left
           if (__any_sync(RB_FULL_MASK, valid_q && cm[ch] >= thresh)) {

@@ -195,6 +195,44 @@ __device__ __forceinline__ void append_chunk_bits(uint2* list, int& count, float
   count = static_cast<int>(w - list);
 }
 
+// Appends, with the whole warp, the entries >= thresh of every (lane, chunk) whose bit ch is
+// set in that lane's `pass`: r[ch][j] = the lane's score of item row0 + 32 ch + j, `list` =
+// the lane's candidate list, `stage` = 32 words of the warp's shared scratch (16-byte
+// aligned). The owning lane stages its chunk in shared memory; then lane j tests item j
+// against the owner's threshold and the kept entries go to the owner's list in one
+// coalesced store, in item order. Padding scores are NaN, which never passes. The code is
+// one short loop per chunk position, instead of 32 predicated stores by one lane.
+template <int NCH>
+__device__ __forceinline__ void warp_append_chunks(uint2* list, int& count, float thresh,
+                                                   const uint32_t (&r)[NCH][32], uint32_t pass, uint32_t row0,
+                                                   uint32_t* stage) {
+  const int lane = threadIdx.x & 31;
+  uint4* stage4 = reinterpret_cast<uint4*>(stage);
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    uint32_t who = __ballot_sync(RB_FULL_MASK, (pass >> ch) & 1u);
+    while (who != 0u) {
+      const int src = __ffs(who) - 1;
+      who &= who - 1u;
+      if (lane == src) {
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+          stage4[j4] = make_uint4(r[ch][4 * j4], r[ch][4 * j4 + 1], r[ch][4 * j4 + 2], r[ch][4 * j4 + 3]);
+      }
+      __syncwarp();
+      const uint32_t v = stage[lane];
+      const bool keep = __uint_as_float(v) >= __shfl_sync(RB_FULL_MASK, thresh, src);
+      const uint32_t kept = __ballot_sync(RB_FULL_MASK, keep);
+      const int base = __shfl_sync(RB_FULL_MASK, count, src);
+      uint2* dst = reinterpret_cast<uint2*>(
+          __shfl_sync(RB_FULL_MASK, reinterpret_cast<unsigned long long>(list), src));
+      if (keep) dst[base + __popc(kept & lanemask_lt())] = make_uint2(v, row0 + 32u * ch + lane);
+      if (lane == src) count += __popc(kept);
+      __syncwarp();  // every lane has read the staged chunk before the next one is written
+    }
+  }
+}
+
 // Bit j set iff s[j] >= thresh. Every index into s is a compile-time constant,
 // so the score array stays in registers.
 __device__ __forceinline__ uint32_t chunk_pass_bits(const uint32_t (&s)[32], float thresh) {
