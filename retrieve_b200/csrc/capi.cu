@@ -188,17 +188,18 @@ __global__ void spec_scatter_kernel(const int* __restrict__ fail_rows, int k, co
 // The rank F k / s of the speculative seed among the sampled chunk maxima (dense_topk_impl).
 // Every epilogue costs in proportion to the chunks that reach the threshold: from the safe
 // seed (rank about k s) the plain fp16 / bf16 pass appends in about half of its 32 x 128
-// warp-tiles, and those appends, not the MMA, set its pace.
-// F = 2 for the filtered scan (measured at 10M items, 10 % selectivity: 12.2 ms a pass against
-// 13.8 at F = 3); F = 3 for int8, whose second passes cost more (38.2 ms at F = 3, 40.5 at F = 2),
-// and for fp16 / bf16.
+// warp-tiles, and those appends, not the MMA, set its pace. F = 3 for every scan (measured
+// at 10M items: bf16 2.02 ms a search against 2.39 from the safe seed and 2.07 at F = 4; the
+// filtered pass at 10 % selectivity 4.8 ms at F = 3 against 5.4 at F = 2, where the compact
+// second pass ran in every batch, and at F = 4; int8 38.2 ms at F = 3 against 40.5 at F = 2).
 static bool dense_spec_applies(int elem, const FilterArgs* filter) {
   (void)elem;
   (void)filter;
   return true;
 }
 static int dense_spec_factor(const FilterArgs* filter) {
-  return (filter != nullptr && filter->mode != kFilterNone) ? 2 : 3;
+  (void)filter;
+  return 3;
 }
 static int dense_spec_rank(int k, const DensePlan& pl, int factor) {
   return static_cast<int>((static_cast<int64_t>(factor) * k + pl.sample_stride - 1) / pl.sample_stride);

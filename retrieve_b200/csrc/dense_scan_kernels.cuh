@@ -72,6 +72,22 @@ __device__ __forceinline__ bool task_live(const DenseScanParams& p, int t) {
 // Bit-sliced Bloom words of one 128-item tile: 4 chunks x 64 words.
 constexpr int kTileSliceWords = 4 * 64;
 
+// A filtered chunk whose threshold test passes in at most this many lanes is appended by the
+// whole warp, one owning lane after another (warp_filter_append); with more, each lane tests
+// its own items (measured at 10M items: the warp form is faster at 10 % and 50 % selectivity,
+// the per-lane form at 1 %, where about 8 lanes pass per chunk).
+constexpr int kCoopFilterLanes = 4;
+
+// One tile's bit-sliced Bloom words into this warp's buffer (pt & 1) of two, 32 bytes a
+// lane (cp.async, committed by the caller).
+__device__ __forceinline__ void copy_tile_slices(uint32_t* sl_base, const DenseScanParams& p, int pt, int lane) {
+  const size_t tile = static_cast<size_t>(pt * p.tile_stride + p.tile_offset);
+  const uint32_t* src = p.filter.slices + tile * kTileSliceWords + lane * 8;
+  uint32_t* dst = sl_base + (pt & 1) * kTileSliceWords + lane * 8;
+  cp_async16(dst, src);
+  cp_async16(dst + 4, src + 4);
+}
+
 template <int KB, int NG, int STAGES, bool FILT = false>
 struct DenseSmemLayout {
   static constexpr int kOpTile = kQTile * 128;  // bytes of one 128-row x 128-byte K-block
@@ -79,7 +95,7 @@ struct DenseSmemLayout {
   static constexpr int kB = STAGES * KB * kOpTile;
   static constexpr int kEpiWarps = 4 * NG;
   static constexpr int kHist = kEpiWarps * 256 * 4;
-  static constexpr int kSlices = FILT ? kEpiWarps * kTileSliceWords * 4 : 0;  // one tile's slices a warp
+  static constexpr int kSlices = FILT ? kEpiWarps * 2 * kTileSliceWords * 4 : 0;  // two tiles' slices a warp
   static constexpr int kBar = (2 * STAGES + 2 + 4 + 1) * 8;
   static constexpr int kMisc = 16;
   static constexpr int kTotal = kA + kB + kHist + kSlices + kBar + kMisc + 1024;  // + alignment slack
@@ -279,23 +295,28 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         if constexpr (FILT) {
-          // the items over the threshold, then the Bloom test of the chunk (32 items a
-          // term) on those; the predicate item by item only where some item is left
-          if (__any_sync(RB_FULL_MASK, valid_q && cm[ch] >= thresh)) {
+          // the lanes whose chunk max reached the threshold: each one's Bloom mask of the
+          // chunk (32 items a term), then the warp tests and appends their items together
+          const bool lp = valid_q && cm[ch] >= thresh;
+          const uint32_t who = __ballot_sync(RB_FULL_MASK, lp);
+          if (who != 0u) {
             const uint32_t id0 = row0 + ch * 32;
-            uint32_t pm = 0;
-            if (valid_q && cm[ch] >= thresh) {
-              pm = chunk_pass_bits(r[ch], thresh);
-              if (use_sl) pm &= bloom_chunk_mask(sl + ch * 64, st);
-            }
-            if (__any_sync(RB_FULL_MASK, pm != 0u)) {
-              if (pm != 0u) {
-                if (!use_sl)
-                  pm = pred_pass_bits(p.filter, q, id0, pm);
-                else if (p.filter.mode == kFilterBloomRecheck)
-                  pm = pred_exact_bits(p.filter, q, id0, pm);
+            const uint32_t bm = (lp && use_sl) ? bloom_chunk_mask(sl + ch * 64, st) : 0xffffffffu;
+            if (__popc(who) <= kCoopFilterLanes) {
+              warp_filter_append(p.filter, list, count, thresh, r[ch], who, bm, use_sl, q, id0, stage + 128);
+            } else {
+              // many lanes at once (selective predicates, low thresholds): each lane tests its
+              // own items, the predicate item by item only where some item is left
+              uint32_t pm = lp ? (chunk_pass_bits(r[ch], thresh) & bm) : 0u;
+              if (__any_sync(RB_FULL_MASK, pm != 0u)) {
+                if (pm != 0u) {
+                  if (!use_sl)
+                    pm = pred_pass_bits(p.filter, q, id0, pm);
+                  else if (p.filter.mode == kFilterBloomRecheck)
+                    pm = pred_exact_bits(p.filter, q, id0, pm);
+                }
+                if (pm != 0u) append_chunk_mask(list, count, r[ch], pm, id0);
               }
-              if (pm != 0u) append_chunk_mask(list, count, r[ch], pm, id0);
             }
           }
         }
@@ -484,8 +505,8 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
     const int g = ew >> 2;               // query group
     const int quad = warp & 3;           // TMEM lane quadrant this warp may access
     uint32_t* hist = hist_all + ew * 256;
-    // filtered variants: this warp's copy of the current tile's bit-sliced Bloom words
-    uint32_t* sl = slices_all + ew * kTileSliceWords;
+    // filtered variants: this warp's copies of the current and next tiles' bit-sliced Bloom words
+    uint32_t* const sl_base = slices_all + ew * 2 * kTileSliceWords;
     const bool sliced = FILT && p.filter.slices != nullptr &&
                         (p.filter.mode == kFilterBloom || p.filter.mode == kFilterBloomRecheck);
     int acc = 0;
@@ -519,12 +540,15 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
           if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
         }
         if constexpr (FILT) {
-          if (sliced) {  // this tile's slices, 32 bytes a lane, while the MMA runs
-            const size_t tile = static_cast<size_t>(pt * p.tile_stride + p.tile_offset);
-            const uint32_t* src = p.filter.slices + tile * kTileSliceWords + lane * 8;
-            __syncwarp();  // every lane is done with the previous tile's slices
-            cp_async16(sl + lane * 8, src);
-            cp_async16(sl + lane * 8 + 4, src + 4);
+          if (sliced) {
+            // the next tile's slices (32 bytes a lane) land while this one is scanned; a
+            // task's first tile is fetched here too
+            __syncwarp();  // every lane is done with the buffer the next tile reuses
+            if (pt == lo) {
+              copy_tile_slices(sl_base, p, pt, lane);
+              cp_async_commit();
+            }
+            if (pt + 1 < hi) copy_tile_slices(sl_base, p, pt + 1, lane);
             cp_async_commit();
           }
         }
@@ -537,6 +561,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_after();
         const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
+        uint32_t* const sl = sl_base + (pt & 1) * kTileSliceWords;
         // Unfiltered: the whole 128-column row in one go, then the accumulator goes
         // back to the MMA warp before any filtering work.
         if constexpr (FILT) {
@@ -544,7 +569,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
           // chunk code (four unrolled copies overflow the instruction cache), and 32 score
           // registers instead of 128. The accumulator goes back after its last load.
           if (sliced) {
-            cp_async_wait_all();
+            cp_async_wait_group1();  // this tile's slices (the next tile's may still be in flight)
             __syncwarp();
           }
 #pragma unroll 1
@@ -616,7 +641,7 @@ struct Dense2SmLayout {
   static constexpr int kB = STAGES * KB * kBTile;
   static constexpr int kEpiWarps = 4 * NG;  // (group, lane quadrant)
   static constexpr int kHist = kEpiWarps * 256 * 4;
-  static constexpr int kSlices = FILT ? kEpiWarps * kTileSliceWords * 4 : 0;  // one tile's slices a warp
+  static constexpr int kSlices = FILT ? kEpiWarps * 2 * kTileSliceWords * 4 : 0;  // two tiles' slices a warp
   static constexpr int kBar = (2 * STAGES + 2 + 2 * 4 + 1) * 8;
   static constexpr int kMisc = 16;
   static constexpr int kTotal = kA + kB + kHist + kSlices + kBar + kMisc + 1024;
@@ -831,8 +856,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     const int g = ew >> 2;
     const int quad = warp & 3;
     uint32_t* hist = hist_all + ew * 256;
-    // filtered variants: this warp's copy of the current tile's bit-sliced Bloom words
-    uint32_t* sl = slices_all + ew * kTileSliceWords;
+    // filtered variants: this warp's copies of the current and next tiles' bit-sliced Bloom words
+    uint32_t* const sl_base = slices_all + ew * 2 * kTileSliceWords;
     const bool sliced = FILT && p.filter.slices != nullptr &&
                         (p.filter.mode == kFilterBloom || p.filter.mode == kFilterBloomRecheck);
     int acc = 0;
@@ -866,12 +891,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
           if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
         }
         if constexpr (FILT) {
-          if (sliced) {  // this tile's slices, 32 bytes a lane, while the MMA runs
-            const size_t tile = static_cast<size_t>(pt * p.tile_stride + p.tile_offset);
-            const uint32_t* src = p.filter.slices + tile * kTileSliceWords + lane * 8;
-            __syncwarp();  // every lane is done with the previous tile's slices
-            cp_async16(sl + lane * 8, src);
-            cp_async16(sl + lane * 8 + 4, src + 4);
+          if (sliced) {
+            // the next tile's slices (32 bytes a lane) land while this one is scanned; a
+            // task's first tile is fetched here too
+            __syncwarp();  // every lane is done with the buffer the next tile reuses
+            if (pt == lo) {
+              copy_tile_slices(sl_base, p, pt, lane);
+              cp_async_commit();
+            }
+            if (pt + 1 < hi) copy_tile_slices(sl_base, p, pt + 1, lane);
             cp_async_commit();
           }
         }
@@ -884,12 +912,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_after();
         const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
+        uint32_t* const sl = sl_base + (pt & 1) * kTileSliceWords;
         if constexpr (FILT) {
           // One 32-item chunk at a time, TMEM as the staging: a single copy of the filtered
           // chunk code (four unrolled copies overflow the instruction cache), and 32 score
           // registers instead of 128. The accumulator goes back after its last load.
           if (sliced) {
-            cp_async_wait_all();
+            cp_async_wait_group1();  // this tile's slices (the next tile's may still be in flight)
             __syncwarp();
           }
 #pragma unroll 1

@@ -197,6 +197,34 @@ __device__ __forceinline__ bool pred_eval_one(const PredTerm* t, int nt, bool us
   return (got & need) == need;
 }
 
+// The exact form of pred_eval_one on item `id`, its attribute row (at most 8 cells) read
+// whole before the first compare: 8 independent loads, so a recheck costs one memory round
+// trip for the row instead of one per term (the query's terms stay in L1). Wider rows go
+// term by term through pred_eval_one. The result is pred_eval_one's.
+__device__ __forceinline__ bool pred_exact_item(const FilterArgs& f, const PredTerm* t, int nt, uint32_t id) {
+  if (nt == 0) return true;
+  const int ca = f.C * f.A;
+  const int64_t* row = f.attrs + static_cast<size_t>(id) * ca;
+  if (ca > 8) return pred_eval_one(t, nt, false, row, f.A, 0ull);
+  int64_t cell[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) cell[c] = c < ca ? __ldg(row + c) : 0;
+  uint32_t need = 0, got = 0;
+#pragma unroll 1
+  for (int i = 0; i < nt; ++i) {
+    const PredTerm tm = t[i];
+    const uint32_t g = 1u << (tm.flags & 7);
+    need |= g;
+    bool m = false;
+    const int lo = tm.clause * f.A;  // the clause's cells: lo .. lo + A - 1
+#pragma unroll
+    for (int c = 0; c < 8; ++c) m |= c < ca && c >= lo && c < lo + f.A && cell[c] == tm.value;
+    if (tm.flags & 8) m = !m;
+    if (m) got |= g;
+  }
+  return (got & need) == need;
+}
+
 // Does item `id` pass query q's predicate?
 __device__ __forceinline__ bool pred_pass(const FilterArgs& f, int q, uint32_t id) {
   const PredTerm* t = f.terms + static_cast<size_t>(q) * kMaxTerms;
@@ -206,7 +234,7 @@ __device__ __forceinline__ bool pred_pass(const FilterArgs& f, int q, uint32_t i
   if (f.mode == kFilterBloom || f.mode == kFilterBloomRecheck)
     ok = pred_eval_one(t, nt, true, nullptr, 0, f.bloom[id]);
   if (ok && (f.mode == kFilterExact || f.mode == kFilterBloomRecheck))
-    ok = pred_eval_one(t, nt, false, f.attrs + static_cast<size_t>(id) * f.C * f.A, f.A, 0ull);
+    ok = pred_exact_item(f, t, nt, id);
   return ok;
 }
 
@@ -218,6 +246,8 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Every committed group but the most recent one has landed.
+__device__ __forceinline__ void cp_async_wait_group1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // mbarrier (shared::cta) with bounded waits.

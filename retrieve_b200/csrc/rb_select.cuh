@@ -174,8 +174,7 @@ __device__ __forceinline__ uint32_t pred_exact_bits(const FilterArgs& f, int q, 
   while (sel) {
     const int j = __ffs(sel) - 1;
     sel &= sel - 1;
-    const int64_t* row = f.attrs + static_cast<size_t>(id0 + j) * f.C * f.A;
-    if (pred_eval_one(t, nt, false, row, f.A, 0ull)) out |= 1u << j;
+    if (pred_exact_item(f, t, nt, id0 + j)) out |= 1u << j;
   }
   return out;
 }
@@ -230,6 +229,50 @@ __device__ __forceinline__ void warp_append_chunks(uint2* list, int& count, floa
       if (lane == src) count += __popc(kept);
       __syncwarp();  // every lane has read the staged chunk before the next one is written
     }
+  }
+}
+
+// The filtered form of warp_append_chunks for one 32-item chunk (items id0 + j): `who` = the
+// lanes whose chunk max reached their threshold, `bm` = each such lane's Bloom mask of the
+// chunk from the bit-sliced words (all ones when the lane has none: `use_sl` false). For each
+// such lane in turn the warp stages its scores, lane j keeps item j if it reaches the owner's
+// threshold and passes the owner's predicate, and the kept entries go to the owner's list in
+// one coalesced store. The predicate work is spread over the items: lane j tests item j
+// (the Bloom word or attributes of consecutive items, the owner's terms read by every lane at
+// one address), instead of one lane walking the chunk's items one after another.
+__device__ __forceinline__ void warp_filter_append(const FilterArgs& f, uint2* list, int& count, float thresh,
+                                                   const uint32_t (&s)[32], uint32_t who, uint32_t bm, bool use_sl,
+                                                   int q, uint32_t id0, uint32_t* stage) {
+  const int lane = threadIdx.x & 31;
+  uint4* stage4 = reinterpret_cast<uint4*>(stage);
+  while (who != 0u) {
+    const int src = __ffs(who) - 1;
+    who &= who - 1u;
+    if (lane == src) {
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) stage4[j4] = make_uint4(s[4 * j4], s[4 * j4 + 1], s[4 * j4 + 2], s[4 * j4 + 3]);
+    }
+    __syncwarp();
+    const uint32_t v = stage[lane];
+    const int qs = __shfl_sync(RB_FULL_MASK, q, src);
+    const bool sliced = __shfl_sync(RB_FULL_MASK, static_cast<int>(use_sl), src) != 0;
+    const uint32_t bms = __shfl_sync(RB_FULL_MASK, bm, src);
+    bool keep = __uint_as_float(v) >= __shfl_sync(RB_FULL_MASK, thresh, src) && ((bms >> lane) & 1u) != 0u;
+    if (__any_sync(RB_FULL_MASK, keep) && keep) {
+      const uint32_t id = id0 + static_cast<uint32_t>(lane);
+      if (!sliced) {
+        keep = pred_pass(f, qs, id);  // the item's Bloom word and / or attributes
+      } else if (f.mode == kFilterBloomRecheck) {
+        keep = pred_exact_item(f, f.terms + static_cast<size_t>(qs) * kMaxTerms, f.n_terms[qs], id);
+      }
+    }
+    const uint32_t kept = __ballot_sync(RB_FULL_MASK, keep);
+    const int base = __shfl_sync(RB_FULL_MASK, count, src);
+    uint2* dst =
+        reinterpret_cast<uint2*>(__shfl_sync(RB_FULL_MASK, reinterpret_cast<unsigned long long>(list), src));
+    if (keep) dst[base + __popc(kept & lanemask_lt())] = make_uint2(v, id0 + static_cast<uint32_t>(lane));
+    if (lane == src) count += __popc(kept);
+    __syncwarp();  // every lane has read the staged chunk before the next one is written
   }
 }
 
