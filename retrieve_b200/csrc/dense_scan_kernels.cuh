@@ -137,11 +137,18 @@ __device__ __forceinline__ float raw_to_float(uint32_t raw) {
 // predicate (`st`) on the tile's bit-sliced Bloom words `sl` (shared memory, 64
 // words a chunk), a chunk of 32 items per term and AND; the exact form (recheck
 // mode), and queries without `use_sl`, test item by item from global memory.
+// The filtered sampling pass with an exact recheck: the best Bloom-passing item of the tile
+// seen so far (score NaN: none yet).
+struct TileBest {
+  float sc;
+  uint32_t id;
+};
+
 template <int MODE, int NCH, int ELEM, bool FILT, int KB>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list, uint32_t* stage, const uint32_t* sl,
-                                               const SlicedTerms& st, bool use_sl) {
+                                               const SlicedTerms& st, bool use_sl, TileBest& tb) {
   // Chunks whose scores may pass (bit ch); the full int8 pass clears the bits of
   // chunks it proves below the threshold before dequantizing them.
   uint32_t live = (1u << NCH) - 1u;
@@ -248,25 +255,38 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         for (int j = 0; j < 32; ++j)
           if (!((pm >> j) & 1u)) r[ch][j] = 0x7fc00000u;
         if (use_sl && p.filter.mode == kFilterBloomRecheck) {
-          // recheck only the chunk's best Bloom-passing item (the lowest index among equal
-          // scores): the chunk then counts that item if it passes exactly, else nothing.
-          // Either way the sampled maxima stay scores of distinct passing items.
+          // Only the tile's best Bloom-passing item (the lowest index among equal scores) is
+          // rechecked, once, after the tile's last chunk: the tile then counts that item if
+          // it passes exactly (its first slot), else nothing; its other slots hold NaN. The
+          // sampled values stay scores of distinct passing items, at one recheck a tile.
           const float mx = max32(r[ch]);
-          uint32_t at = 0;
+          if (mx > tb.sc || (tb.sc != tb.sc && mx == mx)) {
+            uint32_t at = 0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) at |= static_cast<uint32_t>(__uint_as_float(r[ch][j]) == mx) << j;
-          at &= pm;
-          const uint32_t keep = at != 0u ? pred_exact_bits(p.filter, q, id0, at & (~at + 1u)) : 0u;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (!((keep >> j) & 1u)) r[ch][j] = 0x7fc00000u;
+            for (int j = 0; j < 32; ++j) at |= static_cast<uint32_t>(__uint_as_float(r[ch][j]) == mx) << j;
+            at &= pm;
+            tb.sc = mx;
+            tb.id = id0 + static_cast<uint32_t>(__ffs(at) - 1);
+          }
+          if (((chunk0 + ch) & 3) == 3) {
+            const bool ok = tb.sc == tb.sc &&
+                            pred_exact_item(p.filter, p.filter.terms + static_cast<size_t>(q) * kMaxTerms,
+                                            p.filter.n_terms[q], tb.id);
+            float* dst = p.chunk_max + static_cast<size_t>(q) * p.chunk_stride + (chunk0 + ch - 3);
+            dst[0] = ok ? tb.sc : __uint_as_float(0x7fc00000u);
+            dst[1] = dst[2] = dst[3] = __uint_as_float(0x7fc00000u);
+            tb.sc = __uint_as_float(0x7fc00000u);
+          }
         }
       }
     }
   }
   if constexpr (MODE == 1) {
-    // sampling pass: the max of every 32-item chunk, nothing else
-    if (valid_q) {
+    // sampling pass: the max of every 32-item chunk, nothing else (the recheck form above
+    // writes its tile's slots itself)
+    bool tile_form = false;
+    if constexpr (FILT) tile_form = use_sl && p.filter.mode == kFilterBloomRecheck;
+    if (valid_q && !tile_form) {
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch)
         p.chunk_max[static_cast<size_t>(q) * p.chunk_stride + chunk0 + ch] = max32(r[ch]);
@@ -521,6 +541,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
       int count = 0;
       // filtered variants: the query's Bloom terms for the bit-sliced test
       SlicedTerms st{};
+      TileBest tb{__uint_as_float(0x7fc00000u), 0u};
       bool use_sl = false;
       if constexpr (FILT) {
         if (sliced) {
@@ -584,7 +605,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
               if (lane == 0) mbar_arrive(&acc_empty[acc]);
             }
             process_chunks<MODE, 1, ELEM, FILT, KB>(p, r1, row0 + ch * 32, pt * 4 + ch, valid_q, q, thresh, count,
-                                                    list, hist, sl + ch * 64, st, use_sl);
+                                                    list, hist, sl + ch * 64, st, use_sl, tb);
           }
         } else {
           uint32_t r[4][32];
@@ -596,7 +617,7 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
           process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
-                                                  use_sl);
+                                                  use_sl, tb);
         }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
@@ -873,6 +894,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       int count = 0;
       // filtered variants: the query's Bloom terms for the bit-sliced test
       SlicedTerms st{};
+      TileBest tb{__uint_as_float(0x7fc00000u), 0u};
       bool use_sl = false;
       if constexpr (FILT) {
         if (sliced) {
@@ -933,7 +955,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
               if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
             }
             process_chunks<MODE, 1, ELEM, FILT, KB>(p, r1, row0 + ch * 32, pt * 4 + ch, valid_q, q, thresh, count,
-                                                    list, hist, sl + ch * 64, st, use_sl);
+                                                    list, hist, sl + ch * 64, st, use_sl, tb);
           }
         } else {
           uint32_t r[4][32];
@@ -945,7 +967,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
           process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
-                                                  use_sl);
+                                                  use_sl, tb);
         }
         if (++acc == kAcc) {
           acc = 0;
