@@ -23,7 +23,7 @@ bool dense_launch_e0(bool two_sm, int mode, int kb, int ng, bool filtered, int e
   RB_V2(1, 1, 12, true)
   RB_V2(1, 2, 12, true)
   RB_V2(2, 1, 8, true)
-  RB_V2(2, 2, 8, true)
+  RB_V2(2, 2, 5, true)
   RB_V1(1, 1, 8, false)
   RB_V1(2, 1, 4, false)
   RB_V1(4, 1, 2, false)

@@ -45,6 +45,7 @@ namespace rb {
 constexpr int kTileItems = 128;  // N of one MMA = items per pipeline stage
 constexpr int kQTile = 128;      // M of one MMA = queries per group
 constexpr int kSampleStride = 16;  // sampling pass: every 16th tile
+constexpr int kMaxSmemPerCta = 232448;  // opt-in dynamic shared memory of one CTA on sm_100 (227 KB)
 
 struct alignas(64) DenseScanParams {
   CUtensorMap tmap_q;
@@ -63,6 +64,8 @@ struct alignas(64) DenseScanParams {
   int tile_stride, tile_offset, pass_tiles;
   int k, cap;
   const int* qsg_live;  // null: every query group; else only groups with a nonzero entry are scanned
+  int ring;             // 2-SM filtered kernel: bit 0 the Bloom slices, bit 1 the attribute rows of
+                        // each tile come through the shared-memory ring (host: dense_scan_pass)
 };
 
 __device__ __forceinline__ bool task_live(const DenseScanParams& p, int t) {
@@ -71,6 +74,12 @@ __device__ __forceinline__ bool task_live(const DenseScanParams& p, int t) {
 
 // Bit-sliced Bloom words of one 128-item tile: 4 chunks x 64 words.
 constexpr int kTileSliceWords = 4 * 64;
+
+// The 2-SM filtered kernel's ring: kRingSlots tiles in flight, each its 1 KB of Bloom slices
+// and up to 8 KB of attribute rows (128 items of at most 8 int64 cells).
+constexpr int kRingSlots = 4;
+constexpr int kRingRowBytes = kTileItems * 8 * 8;
+constexpr int kRingSlotBytes = kTileSliceWords * 4 + kRingRowBytes;
 
 // A filtered chunk whose threshold test passes in at most this many lanes is appended by the
 // whole warp, one owning lane after another (warp_filter_append); with more, each lane tests
@@ -148,7 +157,9 @@ template <int MODE, int NCH, int ELEM, bool FILT, int KB>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list, uint32_t* stage, const uint32_t* sl,
-                                               const SlicedTerms& st, bool use_sl, TileBest& tb) {
+                                               const SlicedTerms& st, bool use_sl, TileBest& tb,
+                                               const int64_t* tile_rows = nullptr,
+                                               const ExactTerm* wterms = nullptr, int ent = 0) {
   // Chunks whose scores may pass (bit ch); the full int8 pass clears the bits of
   // chunks it proves below the threshold before dequantizing them.
   uint32_t live = (1u << NCH) - 1u;
@@ -249,7 +260,7 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         if (use_sl) {
           pm = bloom_chunk_mask(sl + ch * 64, st) & valid;
         } else {
-          pm = pred_pass_bits(p.filter, q, id0, valid);
+          pm = pred_pass_bits(p.filter, q, id0, valid, tile_rows, row0 - 32u * (chunk0 & 3));
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
@@ -269,9 +280,16 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
             tb.id = id0 + static_cast<uint32_t>(__ffs(at) - 1);
           }
           if (((chunk0 + ch) & 3) == 3) {
-            const bool ok = tb.sc == tb.sc &&
-                            pred_exact_item(p.filter, p.filter.terms + static_cast<size_t>(q) * kMaxTerms,
-                                            p.filter.n_terms[q], tb.id);
+            bool ok = tb.sc == tb.sc;
+            if (ok && wterms != nullptr) {
+              const int ca = p.filter.C * p.filter.A;
+              ok = pred_exact_row_sm(wterms + (threadIdx.x & 31) * kMaxTerms, ent,
+                                     tile_rows + static_cast<size_t>(tb.id - (row0 + 32u * ch - 96u)) * ca, ca,
+                                     p.filter.A);
+            } else if (ok) {
+              ok = pred_exact_item(p.filter, p.filter.terms + static_cast<size_t>(q) * kMaxTerms, p.filter.n_terms[q],
+                                   tb.id, tile_rows, row0 + 32u * ch - 96u);
+            }
             float* dst = p.chunk_max + static_cast<size_t>(q) * p.chunk_stride + (chunk0 + ch - 3);
             dst[0] = ok ? tb.sc : __uint_as_float(0x7fc00000u);
             dst[1] = dst[2] = dst[3] = __uint_as_float(0x7fc00000u);
@@ -323,17 +341,19 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
             const uint32_t id0 = row0 + ch * 32;
             const uint32_t bm = (lp && use_sl) ? bloom_chunk_mask(sl + ch * 64, st) : 0xffffffffu;
             if (__popc(who) <= kCoopFilterLanes) {
-              warp_filter_append(p.filter, list, count, thresh, r[ch], who, bm, use_sl, q, id0, stage + 128);
+              warp_filter_append(p.filter, list, count, thresh, r[ch], who, bm, use_sl, q, id0, stage + 128,
+                                 tile_rows, row0 - 32u * (chunk0 & 3), wterms, ent);
             } else {
               // many lanes at once (selective predicates, low thresholds): each lane tests its
               // own items, the predicate item by item only where some item is left
               uint32_t pm = lp ? (chunk_pass_bits(r[ch], thresh) & bm) : 0u;
               if (__any_sync(RB_FULL_MASK, pm != 0u)) {
                 if (pm != 0u) {
+                  const uint32_t tile0 = row0 - 32u * (chunk0 & 3);
                   if (!use_sl)
-                    pm = pred_pass_bits(p.filter, q, id0, pm);
+                    pm = pred_pass_bits(p.filter, q, id0, pm, tile_rows, tile0);
                   else if (p.filter.mode == kFilterBloomRecheck)
-                    pm = pred_exact_bits(p.filter, q, id0, pm);
+                    pm = pred_exact_bits(p.filter, q, id0, pm, tile_rows, tile0, wterms, ent);
                 }
                 if (pm != 0u) append_chunk_mask(list, count, r[ch], pm, id0);
               }
@@ -588,18 +608,40 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
         if constexpr (FILT) {
           // One 32-item chunk at a time, TMEM as the staging: a single copy of the filtered
           // chunk code (four unrolled copies overflow the instruction cache), and 32 score
-          // registers instead of 128. The accumulator goes back after its last load.
+          // registers instead of 128.
           if (sliced) {
             cp_async_wait_group1();  // this tile's slices (the next tile's may still be in flight)
             __syncwarp();
           }
+// Chunks to process (bit ch). The full pass first takes the tile's four chunk maxima
+          // with all four loads in flight, and goes back to TMEM only for the chunks where some
+          // lane's max reaches its threshold; the sampling pass evaluates every chunk.
+          uint32_t todo = 0xfu;
+          if constexpr (MODE == 0) {
+            uint32_t r4[4][32];
+            __syncwarp();
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r4[ch]);
+            tmem_wait_ld();
+            uint32_t mine = 0;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) mine |= static_cast<uint32_t>(valid_q && max32(r4[ch]) >= thresh) << ch;
+            todo = __reduce_or_sync(RB_FULL_MASK, mine);
+          }
+          if (todo == 0u) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          }
+          const int last = todo == 0u ? -1 : 31 - __clz(todo);
 #pragma unroll 1
-          for (int ch = 0; ch < 4; ++ch) {
+          for (int ch = 0; ch <= last; ++ch) {
+            if (!((todo >> ch) & 1u)) continue;  // warp-uniform
             uint32_t r1[1][32];
             __syncwarp();
             tmem_ld_32x32(col0 + ch * 32, r1[0]);
             tmem_wait_ld();
-            if (ch == 3) {
+            if (ch == last) {  // the accumulator goes back after the tile's last load
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -662,10 +704,13 @@ struct Dense2SmLayout {
   static constexpr int kB = STAGES * KB * kBTile;
   static constexpr int kEpiWarps = 4 * NG;  // (group, lane quadrant)
   static constexpr int kHist = kEpiWarps * 256 * 4;
-  static constexpr int kSlices = FILT ? kEpiWarps * 2 * kTileSliceWords * 4 : 0;  // two tiles' slices a warp
-  static constexpr int kBar = (2 * STAGES + 2 + 2 * 4 + 1) * 8;
+  // filtered variants: a ring of kRingSlots tiles, each its Bloom slices and attribute rows
+  static constexpr int kRing = FILT ? kRingSlots * kRingSlotBytes : 0;
+  // and each epilogue warp's table of its 32 queries' exact terms
+  static constexpr int kTerms = FILT ? kEpiWarps * 32 * kMaxTerms * static_cast<int>(sizeof(ExactTerm)) : 0;
+  static constexpr int kBar = (2 * STAGES + 2 + 2 * 4 + 1 + (FILT ? 2 * kRingSlots : 0)) * 8;
   static constexpr int kMisc = 16;
-  static constexpr int kTotal = kA + kB + kHist + kSlices + kBar + kMisc + 1024;
+  static constexpr int kTotal = kA + kB + kHist + kRing + kTerms + kBar + kMisc + 1024;
 };
 
 template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
@@ -686,8 +731,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
   uint8_t* smA = smem;
   uint8_t* smB = smem + L::kA;
   uint32_t* hist_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB);
-  uint32_t* slices_all = reinterpret_cast<uint32_t*>(smem + L::kA + L::kB + L::kHist);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist + L::kSlices);
+  uint8_t* ring = smem + L::kA + L::kB + L::kHist;  // filtered variants
+  ExactTerm* terms_all = reinterpret_cast<ExactTerm*>(smem + L::kA + L::kB + L::kHist + L::kRing);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kA + L::kB + L::kHist + L::kRing + L::kTerms);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* a_full = bars + 2 * STAGES;
@@ -695,7 +741,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
   uint64_t* acc_full = a_full + 2;         // [kAcc]
   uint64_t* acc_empty = acc_full + kAcc;  // [kAcc], used on CTA 0
   uint64_t* drain_bar = acc_empty + kAcc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* ring_full = drain_bar + 1;           // [kRingSlots] (filtered variants)
+  uint64_t* ring_empty = ring_full + kRingSlots;  // [kRingSlots]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1 + (FILT ? 2 * kRingSlots : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -717,6 +765,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       mbar_init(&acc_empty[b], 2 * L::kEpiWarps);
     }
     mbar_init(drain_bar, 1);
+    if constexpr (FILT) {
+      for (int s = 0; s < kRingSlots; ++s) {
+        mbar_init(&ring_full[s], 1);
+        mbar_init(&ring_empty[s], L::kEpiWarps);
+      }
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -741,6 +795,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       uint32_t phase = 0;
       int a_iter = 0;
       uint32_t armed = 0;
+      int rslot = 0;
+      uint32_t rphase = 0, r_armed = 0;
       for (int t = pair; t < n_tasks && !*abort_flag; t += n_pairs) {
         if (!task_live(p, t)) continue;  // every role skips the same tasks
         const int qsg = t % p.n_qsg, split = t / p.n_qsg;
@@ -769,10 +825,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
             tma_load_2d_pair(smB + (stage * KB + kb) * L::kBTile, &p.tmap_x, &full_bar[stage],
                              kb * kElemsPerKBlock, tile * kTileItems + static_cast<int>(rank) * kHalfItems);
           ++armed;
+          if constexpr (FILT) {
+            if (p.ring != 0) {
+              // this CTA's copy of the tile's Bloom slices and attribute rows, once the
+              // epilogue warps are done with the slot's previous tile
+              if (!mbar_wait(&ring_empty[rslot], rphase ^ 1, abort_flag)) {
+                atomicCAS(p.err, 0, kDevTimeoutProducer);
+                *abort_flag = 1;
+                break;
+              }
+              uint8_t* slot = ring + rslot * kRingSlotBytes;
+              const int ca = p.filter.C * p.filter.A;
+              const uint32_t n_in = static_cast<uint32_t>(min(kTileItems, p.N - tile * kTileItems));
+              const uint32_t sl_bytes = (p.ring & 1) ? kTileSliceWords * 4u : 0u;
+              const uint32_t row_bytes = (p.ring & 2) ? n_in * static_cast<uint32_t>(ca) * 8u : 0u;
+              mbar_arrive_expect_tx(&ring_full[rslot], sl_bytes + row_bytes);
+              if (sl_bytes != 0u)
+                bulk_load(slot, p.filter.slices + static_cast<size_t>(tile) * kTileSliceWords, sl_bytes,
+                          &ring_full[rslot]);
+              if (row_bytes != 0u)
+                bulk_load(slot + kTileSliceWords * 4,
+                          p.filter.attrs + static_cast<size_t>(tile) * kTileItems * static_cast<size_t>(ca), row_bytes,
+                          &ring_full[rslot]);
+              ++r_armed;
+              if (++rslot == kRingSlots) {
+                rslot = 0;
+                rphase ^= 1;
+              }
+            }
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
+        }
+      }
+      if constexpr (FILT) {  // this CTA's ring copies have landed
+        for (int s = 0; s < kRingSlots; ++s) {
+          const uint32_t n_s = r_armed / kRingSlots + (static_cast<uint32_t>(s) < r_armed % kRingSlots ? 1u : 0u);
+          if (n_s > 0) mbar_wait_drain(&ring_full[s], (n_s - 1) & 1);
         }
       }
       // Drain (CTA 0's barriers count both CTAs' bytes): every load has landed.
@@ -877,10 +968,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     const int g = ew >> 2;
     const int quad = warp & 3;
     uint32_t* hist = hist_all + ew * 256;
-    // filtered variants: this warp's copies of the current and next tiles' bit-sliced Bloom words
-    uint32_t* const sl_base = slices_all + ew * 2 * kTileSliceWords;
-    const bool sliced = FILT && p.filter.slices != nullptr &&
-                        (p.filter.mode == kFilterBloom || p.filter.mode == kFilterBloomRecheck);
+    // filtered variants: the tile's Bloom slices (and attribute rows) from the ring
+    const bool sliced = FILT && (p.ring & 1) != 0;
+    // with the attribute rows in the ring: this warp's table of its queries' exact terms
+    ExactTerm* const wterms = (FILT && (p.ring & 2) != 0) ? terms_all + ew * 32 * kMaxTerms : nullptr;
+    int rslot = 0;
+    uint32_t rphase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
@@ -896,10 +989,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       SlicedTerms st{};
       TileBest tb{__uint_as_float(0x7fc00000u), 0u};
       bool use_sl = false;
+      int ent = 0;
       if constexpr (FILT) {
         if (sliced) {
           st = load_sliced_terms(p.filter, q, valid_q);
           use_sl = valid_q && st.ok;
+        }
+        if (wterms != nullptr) {
+          __syncwarp();  // every lane is done with the previous task's table
+          ent = valid_q ? min(p.filter.n_terms[q], kMaxTerms) : 0;
+          const PredTerm* tq = p.filter.terms + static_cast<size_t>(valid_q ? q : 0) * kMaxTerms;
+#pragma unroll 1
+          for (int i = 0; i < kMaxTerms; ++i) {
+            ExactTerm et{0, 0, 0};
+            if (i < ent) {
+              const PredTerm t = tq[i];
+              et = ExactTerm{t.value, t.clause * p.filter.A, t.flags};
+            }
+            wterms[lane * kMaxTerms + i] = et;
+          }
+          __syncwarp();
         }
       }
       const size_t list_id = static_cast<size_t>(valid_q ? q : 0) * p.n_splits + split;
@@ -912,19 +1021,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
           const bool need = valid_q && (count > p.cap - kTileItems);
           if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
         }
-        if constexpr (FILT) {
-          if (sliced) {
-            // the next tile's slices (32 bytes a lane) land while this one is scanned; a
-            // task's first tile is fetched here too
-            __syncwarp();  // every lane is done with the buffer the next tile reuses
-            if (pt == lo) {
-              copy_tile_slices(sl_base, p, pt, lane);
-              cp_async_commit();
-            }
-            if (pt + 1 < hi) copy_tile_slices(sl_base, p, pt + 1, lane);
-            cp_async_commit();
-          }
-        }
         if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
           if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
           *abort_flag = 1;
@@ -934,28 +1030,69 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         tc_fence_after();
         const uint32_t row0 = static_cast<uint32_t>((pt * p.tile_stride + p.tile_offset) * kTileItems);
         const uint32_t col0 = tmem_base + lane_addr + static_cast<uint32_t>(acc * NG * 128 + g * 128);
-        uint32_t* const sl = sl_base + (pt & 1) * kTileSliceWords;
+        const uint32_t* sl = nullptr;
+        const int64_t* tile_rows = nullptr;
+        if constexpr (FILT) {
+          if (p.ring != 0) {
+            if (!mbar_wait(&ring_full[rslot], rphase, abort_flag)) {
+              if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            const uint8_t* slot = ring + rslot * kRingSlotBytes;
+            sl = reinterpret_cast<const uint32_t*>(slot);
+            if (p.ring & 2) tile_rows = reinterpret_cast<const int64_t*>(slot + kTileSliceWords * 4);
+          }
+        }
         if constexpr (FILT) {
           // One 32-item chunk at a time, TMEM as the staging: a single copy of the filtered
           // chunk code (four unrolled copies overflow the instruction cache), and 32 score
-          // registers instead of 128. The accumulator goes back after its last load.
-          if (sliced) {
-            cp_async_wait_group1();  // this tile's slices (the next tile's may still be in flight)
+          // registers instead of 128.
+// Chunks to process (bit ch). The full pass first takes the tile's four chunk maxima
+          // with all four loads in flight, and goes back to TMEM only for the chunks where some
+          // lane's max reaches its threshold; the sampling pass evaluates every chunk.
+          uint32_t todo = 0xfu;
+          if constexpr (MODE == 0) {
+            uint32_t r4[4][32];
             __syncwarp();
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) tmem_ld_32x32(col0 + ch * 32, r4[ch]);
+            tmem_wait_ld();
+            uint32_t mine = 0;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) mine |= static_cast<uint32_t>(valid_q && max32(r4[ch]) >= thresh) << ch;
+            todo = __reduce_or_sync(RB_FULL_MASK, mine);
           }
+          if (todo == 0u) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
+          }
+          const int last = todo == 0u ? -1 : 31 - __clz(todo);
 #pragma unroll 1
-          for (int ch = 0; ch < 4; ++ch) {
+          for (int ch = 0; ch <= last; ++ch) {
+            if (!((todo >> ch) & 1u)) continue;  // warp-uniform
             uint32_t r1[1][32];
             __syncwarp();
             tmem_ld_32x32(col0 + ch * 32, r1[0]);
             tmem_wait_ld();
-            if (ch == 3) {
+            if (ch == last) {  // the accumulator goes back after the tile's last load
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
             }
             process_chunks<MODE, 1, ELEM, FILT, KB>(p, r1, row0 + ch * 32, pt * 4 + ch, valid_q, q, thresh, count,
-                                                    list, hist, sl + ch * 64, st, use_sl, tb);
+                                                    list, hist, sl + ch * 64, st, use_sl, tb, tile_rows, wterms,
+                                                    ent);
+          }
+          if (p.ring != 0) {  // the slot goes back once every lane is done with it
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ring_empty[rslot]);
+            if (++rslot == kRingSlots) {
+              rslot = 0;
+              rphase ^= 1;
+            }
           }
         } else {
           uint32_t r[4][32];
@@ -983,7 +1120,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     }
   }
 
-  if constexpr (FILT) cp_async_wait_all();  // slice copies of an early exit land before the CTA ends
   __syncwarp();
   if (*abort_flag) {
     // Error path only: a load of this CTA may still be in flight towards its
@@ -1003,9 +1139,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
 template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaStream_t stream) {
   using L = DenseSmemLayout<KB, NG, STAGES, FILT>;
+  static_assert(L::kTotal <= kMaxSmemPerCta, "1-SM scan variant exceeds the shared memory of one CTA");
   auto kern = dense_scan_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return e;
+  }
   kern<<<grid, 64 + 128 * NG, L::kTotal, stream>>>(prm);
   return cudaGetLastError();
 }
@@ -1013,9 +1153,13 @@ static cudaError_t launch_dense_scan(const DenseScanParams& prm, int grid, cudaS
 template <int MODE, int ELEM, int KB, int NG, int STAGES, int EPL, bool FILT>
 static cudaError_t launch_dense_scan_2sm(const DenseScanParams& prm, int n_pairs, cudaStream_t stream) {
   using L = Dense2SmLayout<KB, NG, STAGES, FILT>;
+  static_assert(L::kTotal <= kMaxSmemPerCta, "2-SM scan variant exceeds the shared memory of one CTA");
   auto kern = dense_scan_2sm_kernel<MODE, ELEM, KB, NG, STAGES, EPL, FILT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // the attribute's error is reported by the return value, not left pending
+    return e;
+  }
   kern<<<2 * n_pairs, 64 + 128 * NG, L::kTotal, stream>>>(prm);
   return cudaGetLastError();
 }

@@ -190,6 +190,17 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
   prm.k = k;
   prm.cap = pl.cap;
   prm.qsg_live = qsg_live;
+  if (filtered && pl.two_sm) {
+    // The 2-SM filtered kernel streams each tile's Bloom slices and (rows of at most 8 cells,
+    // a whole number of 16-byte units, 16-byte aligned) attribute rows through a shared-memory
+    // ring beside the item tiles; other rows are read from global memory item by item.
+    const FilterArgs& f = prm.filter;
+    const bool sliced = f.slices != nullptr && (f.mode == kFilterBloom || f.mode == kFilterBloomRecheck);
+    const int ca = f.C * f.A;
+    const bool rows = f.attrs != nullptr && (f.mode == kFilterExact || f.mode == kFilterBloomRecheck) && ca >= 1 &&
+                      ca <= 8 && ca % 2 == 0 && (reinterpret_cast<uintptr_t>(f.attrs) & 15u) == 0;
+    prm.ring = (sliced ? 1 : 0) | (rows ? 2 : 0);
+  }
   const int n_tasks = pl.n_qsg * pl.n_splits;
   cudaError_t e = cudaSuccess;
   const int kb = row_bytes / 128;
@@ -208,7 +219,10 @@ int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int
     return RB_ERR_UNSUPPORTED;
   }
   if (e != cudaSuccess) {
-    set_last_error(cudaGetErrorString(e));
+    char msg[256];
+    std::snprintf(msg, sizeof(msg), "%s (dense scan launch: pass %d, %s kernel, %d K-blocks, %d query tiles%s)",
+                  cudaGetErrorString(e), mode, pl.two_sm ? "2-SM" : "1-SM", kb, pl.ng, filtered ? ", filtered" : "");
+    set_last_error(msg);
     return RB_ERR_CUDA;
   }
   return RB_OK;

@@ -160,11 +160,13 @@ __device__ __forceinline__ uint32_t bloom_chunk_mask(const uint32_t* sl, const S
     if (i < st.n) {
       const uint32_t w = st.t[i];
       const int cnt = (w >> 24) & 7;
-      uint32_t m = 0xffffffffu;
-      if (cnt > 0) m &= sl[w & 63];
-      if (cnt > 1) m &= sl[(w >> 6) & 63];
-      if (cnt > 2) m &= sl[(w >> 12) & 63];
-      if (cnt > 3) m &= sl[(w >> 18) & 63];
+      // the four position words are read whatever the term's bit count (position 0 pads
+      // the unused ones), so that the loads go out together
+      const uint32_t a = sl[w & 63], b = sl[(w >> 6) & 63], c = sl[(w >> 12) & 63], d = sl[(w >> 18) & 63];
+      uint32_t m = cnt > 0 ? a : 0xffffffffu;
+      if (cnt > 1) m &= b;
+      if (cnt > 2) m &= c;
+      if (cnt > 3) m &= d;
       if (w & (1u << 27)) m = ~m;
       cur |= m;
       if (w & (1u << 28)) {
@@ -197,18 +199,15 @@ __device__ __forceinline__ bool pred_eval_one(const PredTerm* t, int nt, bool us
   return (got & need) == need;
 }
 
-// The exact form of pred_eval_one on item `id`, its attribute row (at most 8 cells) read
-// whole before the first compare: 8 independent loads, so a recheck costs one memory round
-// trip for the row instead of one per term (the query's terms stay in L1). Wider rows go
-// term by term through pred_eval_one. The result is pred_eval_one's.
-__device__ __forceinline__ bool pred_exact_item(const FilterArgs& f, const PredTerm* t, int nt, uint32_t id) {
+// The exact form of pred_eval_one on one attribute row of ca <= 8 cells (global or shared
+// memory), read whole before the first compare: the cells' loads are independent, so a
+// recheck costs one memory round trip for the row instead of one per term (the query's
+// terms stay in L1). The result is pred_eval_one's.
+__device__ __forceinline__ bool pred_exact_row(const PredTerm* t, int nt, const int64_t* row, int ca, int A) {
   if (nt == 0) return true;
-  const int ca = f.C * f.A;
-  const int64_t* row = f.attrs + static_cast<size_t>(id) * ca;
-  if (ca > 8) return pred_eval_one(t, nt, false, row, f.A, 0ull);
   int64_t cell[8];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) cell[c] = c < ca ? __ldg(row + c) : 0;
+  for (int c = 0; c < 8; ++c) cell[c] = c < ca ? row[c] : 0;
   uint32_t need = 0, got = 0;
 #pragma unroll 1
   for (int i = 0; i < nt; ++i) {
@@ -216,17 +215,62 @@ __device__ __forceinline__ bool pred_exact_item(const FilterArgs& f, const PredT
     const uint32_t g = 1u << (tm.flags & 7);
     need |= g;
     bool m = false;
-    const int lo = tm.clause * f.A;  // the clause's cells: lo .. lo + A - 1
+    const int lo = tm.clause * A;  // the clause's cells: lo .. lo + A - 1
 #pragma unroll
-    for (int c = 0; c < 8; ++c) m |= c < ca && c >= lo && c < lo + f.A && cell[c] == tm.value;
+    for (int c = 0; c < 8; ++c) m |= c < ca && c >= lo && c < lo + A && cell[c] == tm.value;
     if (tm.flags & 8) m = !m;
     if (m) got |= g;
   }
   return (got & need) == need;
 }
 
+// A term's exact test as the filtered 2-SM scan keeps it in shared memory, one table of
+// kMaxTerms a query: lo = the clause's first cell (clause * A).
+struct ExactTerm {
+  int64_t value;
+  int32_t lo;
+  int32_t flags;
+};
+
+// pred_exact_row with the terms from such a table.
+__device__ __forceinline__ bool pred_exact_row_sm(const ExactTerm* t, int nt, const int64_t* row, int ca, int A) {
+  if (nt == 0) return true;
+  int64_t cell[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) cell[c] = c < ca ? row[c] : 0;
+  uint32_t need = 0, got = 0;
+#pragma unroll 1
+  for (int i = 0; i < nt; ++i) {
+    const ExactTerm tm = t[i];
+    const uint32_t g = 1u << (tm.flags & 7);
+    need |= g;
+    bool m = false;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) m |= c < ca && c >= tm.lo && c < tm.lo + A && cell[c] == tm.value;
+    if (tm.flags & 8) m = !m;
+    if (m) got |= g;
+  }
+  return (got & need) == need;
+}
+
+// The exact predicate of terms t[0..nt) on item `id`: its row read whole when it has at
+// most 8 cells, term by term (pred_eval_one) otherwise. `tile_rows`, when not null, holds
+// the rows of the items tile0 .. tile0 + 127 in shared memory (the filtered scan's ring),
+// which then serve instead of global memory.
+__device__ __forceinline__ bool pred_exact_item(const FilterArgs& f, const PredTerm* t, int nt, uint32_t id,
+                                                const int64_t* tile_rows = nullptr, uint32_t tile0 = 0) {
+  if (nt == 0) return true;
+  const int ca = f.C * f.A;
+  if (ca > 8) return pred_eval_one(t, nt, false, f.attrs + static_cast<size_t>(id) * ca, f.A, 0ull);
+  const int64_t* row = tile_rows != nullptr ? tile_rows + static_cast<size_t>(id - tile0) * ca
+                                            : f.attrs + static_cast<size_t>(id) * ca;
+  return pred_exact_row(t, nt, row, ca, f.A);
+}
+
 // Does item `id` pass query q's predicate?
-__device__ __forceinline__ bool pred_pass(const FilterArgs& f, int q, uint32_t id) {
+// (`tile_rows` / `tile0`: as pred_exact_item.)
+__device__ __forceinline__ bool pred_pass(const FilterArgs& f, int q, uint32_t id, const int64_t* tile_rows = nullptr,
+                                          uint32_t tile0 = 0) {
   const PredTerm* t = f.terms + static_cast<size_t>(q) * kMaxTerms;
   const int nt = f.n_terms[q];
   if (nt == 0) return true;
@@ -234,7 +278,7 @@ __device__ __forceinline__ bool pred_pass(const FilterArgs& f, int q, uint32_t i
   if (f.mode == kFilterBloom || f.mode == kFilterBloomRecheck)
     ok = pred_eval_one(t, nt, true, nullptr, 0, f.bloom[id]);
   if (ok && (f.mode == kFilterExact || f.mode == kFilterBloomRecheck))
-    ok = pred_exact_item(f, t, nt, id);
+    ok = pred_exact_item(f, t, nt, id, tile_rows, tile0);
   return ok;
 }
 
@@ -319,6 +363,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
 }
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory, completing on `bar`'s transaction count.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // ---------------------------------------------------------------------------

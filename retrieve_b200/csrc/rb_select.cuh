@@ -153,20 +153,38 @@ __device__ __noinline__ void warp_compact_lists(uint2* list, int& count, float& 
 
 // Of the items id0 + j with bit j set in sel, those that pass query q's
 // attribute predicate (bit j of the result). Touches no register array.
-__device__ __forceinline__ uint32_t pred_pass_bits(const FilterArgs& f, int q, uint32_t id0, uint32_t sel) {
+__device__ __forceinline__ uint32_t pred_pass_bits(const FilterArgs& f, int q, uint32_t id0, uint32_t sel,
+                                                   const int64_t* tile_rows = nullptr, uint32_t tile0 = 0) {
   uint32_t out = 0;
   while (sel) {
     const int j = __ffs(sel) - 1;
     sel &= sel - 1;
-    if (pred_pass(f, q, id0 + j)) out |= 1u << j;
+    if (pred_pass(f, q, id0 + j, tile_rows, tile0)) out |= 1u << j;
   }
   return out;
 }
 
 
 // Of the items id0 + j with bit j set in sel, those that pass query q's exact
-// (attribute) predicate; the Bloom form is not consulted.
-__device__ __forceinline__ uint32_t pred_exact_bits(const FilterArgs& f, int q, uint32_t id0, uint32_t sel) {
+// (attribute) predicate; the Bloom form is not consulted. `tile_rows` / `tile0`: as
+// pred_exact_item.
+// `wterms` / `ent`, when not null: the calling lane's query's terms in the warp's shared
+// table (kMaxTerms a lane) and their count; the rows then come from `tile_rows`.
+__device__ __forceinline__ uint32_t pred_exact_bits(const FilterArgs& f, int q, uint32_t id0, uint32_t sel,
+                                                    const int64_t* tile_rows = nullptr, uint32_t tile0 = 0,
+                                                    const ExactTerm* wterms = nullptr, int ent = 0) {
+  if (wterms != nullptr) {
+    const ExactTerm* mine = wterms + (threadIdx.x & 31) * kMaxTerms;
+    const int ca = f.C * f.A;
+    uint32_t out = 0;
+    while (sel) {
+      const int j = __ffs(sel) - 1;
+      sel &= sel - 1;
+      if (pred_exact_row_sm(mine, ent, tile_rows + static_cast<size_t>(id0 + j - tile0) * ca, ca, f.A))
+        out |= 1u << j;
+    }
+    return out;
+  }
   const PredTerm* t = f.terms + static_cast<size_t>(q) * kMaxTerms;
   const int nt = f.n_terms[q];
   if (nt == 0) return sel;
@@ -174,7 +192,7 @@ __device__ __forceinline__ uint32_t pred_exact_bits(const FilterArgs& f, int q, 
   while (sel) {
     const int j = __ffs(sel) - 1;
     sel &= sel - 1;
-    if (pred_exact_item(f, t, nt, id0 + j)) out |= 1u << j;
+    if (pred_exact_item(f, t, nt, id0 + j, tile_rows, tile0)) out |= 1u << j;
   }
   return out;
 }
@@ -237,12 +255,15 @@ __device__ __forceinline__ void warp_append_chunks(uint2* list, int& count, floa
 // chunk from the bit-sliced words (all ones when the lane has none: `use_sl` false). For each
 // such lane in turn the warp stages its scores, lane j keeps item j if it reaches the owner's
 // threshold and passes the owner's predicate, and the kept entries go to the owner's list in
-// one coalesced store. The predicate work is spread over the items: lane j tests item j
+// one coalesced store (`tile_rows` / `tile0`: the tile's attribute rows in shared memory, as
+// pred_exact_item; `wterms` / `ent`: as pred_exact_bits). The predicate work is spread over the items: lane j tests item j
 // (the Bloom word or attributes of consecutive items, the owner's terms read by every lane at
 // one address), instead of one lane walking the chunk's items one after another.
 __device__ __forceinline__ void warp_filter_append(const FilterArgs& f, uint2* list, int& count, float thresh,
                                                    const uint32_t (&s)[32], uint32_t who, uint32_t bm, bool use_sl,
-                                                   int q, uint32_t id0, uint32_t* stage) {
+                                                   int q, uint32_t id0, uint32_t* stage,
+                                                   const int64_t* tile_rows = nullptr, uint32_t tile0 = 0,
+                                                   const ExactTerm* wterms = nullptr, int ent = 0) {
   const int lane = threadIdx.x & 31;
   uint4* stage4 = reinterpret_cast<uint4*>(stage);
   while (who != 0u) {
@@ -257,13 +278,21 @@ __device__ __forceinline__ void warp_filter_append(const FilterArgs& f, uint2* l
     const int qs = __shfl_sync(RB_FULL_MASK, q, src);
     const bool sliced = __shfl_sync(RB_FULL_MASK, static_cast<int>(use_sl), src) != 0;
     const uint32_t bms = __shfl_sync(RB_FULL_MASK, bm, src);
+    const int ents = __shfl_sync(RB_FULL_MASK, ent, src);
     bool keep = __uint_as_float(v) >= __shfl_sync(RB_FULL_MASK, thresh, src) && ((bms >> lane) & 1u) != 0u;
     if (__any_sync(RB_FULL_MASK, keep) && keep) {
       const uint32_t id = id0 + static_cast<uint32_t>(lane);
       if (!sliced) {
-        keep = pred_pass(f, qs, id);  // the item's Bloom word and / or attributes
+        keep = pred_pass(f, qs, id, tile_rows, tile0);  // the item's Bloom word and / or attributes
       } else if (f.mode == kFilterBloomRecheck) {
-        keep = pred_exact_item(f, f.terms + static_cast<size_t>(qs) * kMaxTerms, f.n_terms[qs], id);
+        if (wterms != nullptr) {  // the owner's terms from the warp's table, the row from the ring
+          const int ca = f.C * f.A;
+          keep = pred_exact_row_sm(wterms + src * kMaxTerms, ents, tile_rows + static_cast<size_t>(id - tile0) * ca,
+                                   ca, f.A);
+        } else {
+          keep = pred_exact_item(f, f.terms + static_cast<size_t>(qs) * kMaxTerms, f.n_terms[qs], id, tile_rows,
+                                 tile0);
+        }
       }
     }
     const uint32_t kept = __ballot_sync(RB_FULL_MASK, keep);
