@@ -82,10 +82,10 @@ constexpr int kRingRowBytes = kTileItems * 8 * 8;
 constexpr int kRingSlotBytes = kTileSliceWords * 4 + kRingRowBytes;
 
 // A filtered chunk whose threshold test passes in at most this many lanes is appended by the
-// whole warp, one owning lane after another (warp_filter_append); with more, each lane tests
-// its own items (measured at 10M items: the warp form is faster at 10 % and 50 % selectivity,
-// the per-lane form at 1 %, where about 8 lanes pass per chunk).
-constexpr int kCoopFilterLanes = 4;
+// whole warp (warp_filter_append); with more, each lane tests its own items. Measured at 10M
+// items (C3, queries/s at 1 / 10 / 50 % selectivity): 74.5k / 188k / 254k with 4, 83.4k /
+// 190k / 253k with 1, 87.3k / 195k / 239k with 0 (per-lane only).
+constexpr int kCoopFilterLanes = 1;
 
 // One tile's bit-sliced Bloom words into this warp's buffer (pt & 1) of two, 32 bytes a
 // lane (cp.async, committed by the caller).
