@@ -350,8 +350,8 @@ RB_API int rb_wait_probe(int64_t limit_ns, void* workspace, size_t workspace_byt
  * reference, which is single-GPU). A shard of N of the n_total corpus rows:
  *
  *   rb_dense_seed_sample writes out_vals [B, m] fp32 (1 <= m <= k): per query,
- *   m chunk maxima (max of 32 consecutive items) from this shard's sampling
- *   pass, all at or above the shard's own m-th largest chunk max (-inf where
+ *   m tile maxima (max of 128 consecutive items) from this shard's sampling
+ *   pass, all at or above the shard's own m-th largest tile max (-inf where
  *   the shard sampled fewer). The caller gathers every shard's [B, m] into a
  *   [W, B, m] stack (one all-gather) and passes it to
  *

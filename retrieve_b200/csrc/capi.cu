@@ -87,7 +87,7 @@ static int dense_check(int elem, const void* queries, const float* q_scale, cons
 
 // After a pass from the speculative seed: a row whose k-th output is padding found fewer
 // than k candidates at or above that seed, and is scanned again from the safe seed (the
-// k-th sampled chunk max); every other row keeps its output (seed NaN: nothing passes).
+// k-th sampled tile max); every other row keeps its output (seed NaN: nothing passes).
 __global__ void spec_check_kernel(const int64_t* __restrict__ out_ids, int B, int k, const float* __restrict__ safe,
                                   float* __restrict__ seed, int* __restrict__ row_live, int* __restrict__ qsg_live,
                                   int queries_per_group) {
@@ -185,7 +185,7 @@ __global__ void spec_scatter_kernel(const int* __restrict__ fail_rows, int k, co
   }
 }
 
-// The rank F k / s of the speculative seed among the sampled chunk maxima (dense_topk_impl).
+// The rank F k / s of the speculative seed among the sampled tile maxima (dense_topk_impl).
 // Every epilogue costs in proportion to the chunks that reach the threshold: from the safe
 // seed (rank about k s) the plain fp16 / bf16 pass appends in about half of its 32 x 128
 // warp-tiles, and those appends, not the MMA, set its pace. F = 3 for every scan (measured
@@ -213,8 +213,8 @@ struct DenseWs {
 };
 
 // The layout of dense_workspace_bytes: the candidate lists share their region with the
-// sampling pass's chunk maxima, so the counts and seeds start past the larger of the two
-// (the seeds are written while the chunk maxima are still being read).
+// sampling pass's tile maxima, so the counts and seeds start past the larger of the two
+// (the seeds are written while the tile maxima are still being read).
 static DenseWs dense_ws(void* workspace, size_t workspace_bytes, int B, const DensePlan& pl) {
   DenseWs d;
   uint8_t* w = static_cast<uint8_t*>(workspace);
@@ -308,7 +308,7 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   ProfileEvents& pe = profile_events();
   const float* seed = nullptr;
   // Filtered and int8 searches start the full pass from a speculative seed: the
-  // ceil(F k / s)-th largest sampled chunk max instead of the k-th (s = the sample's tile
+  // ceil(F k / s)-th largest sampled tile max instead of the k-th (s = the sample's tile
   // stride). About F k items of the corpus reach it (a count whose spread is about
   // 1 / sqrt(F k / s)), so the rows test about s / F times fewer candidates; a row that still
   // finds fewer than k runs again from the safe seed, in the compact batch of up to 128 such
@@ -328,20 +328,19 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
     const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
     const int k_spec = dense_spec_rank(k, pl, dense_spec_factor(filter));
     spec = dense_spec_applies(elem, filter) && out_pairs == nullptr && k_spec < k;
-    rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, spec ? k_spec : k, d.thresh, nullptr, stream);
+    if (spec)  // the speculative seed, and the safe one kept for the rows that need a second pass
+      rc = row_kth2_lower_bounds(chunk_max, B, n_chunks, n_chunks, k_spec, k, d.thresh, d.thresh + B, stream);
+    else
+      rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, k, d.thresh, nullptr, stream);
     if (rc != RB_OK) return rc;
-    if (spec) {  // the safe seed, kept for the rows that need a second pass
-      rc = row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, k, d.thresh + B, nullptr, stream);
-      if (rc != RB_OK) return rc;
-    }
     seed = d.thresh;
   }
   if (pe.start) record_profile_event(pe.start, stream);
   rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, seed, d.lists, d.counts, nullptr, d.err, stream,
                        q_scale, x_scale, filter);
   if (rc != RB_OK) return rc;
+  if (pe.stop) record_profile_event(pe.stop, stream);  // the profiled span: the full pass alone
   if (!spec) {
-    if (pe.stop) record_profile_event(pe.stop, stream);
     return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, out_pairs,
                        stream);
   }
@@ -397,7 +396,6 @@ static int dense_topk_impl(int elem, const void* queries, const float* q_scale, 
   rc = dense_scan_pass(0, elem, queries, items, B, N, D, pl, k, d.thresh, d.lists, d.counts, nullptr, d.err, stream,
                        q_scale, x_scale, filter, qsg_live);
   if (rc != RB_OK) return rc;
-  if (pe.stop) record_profile_event(pe.stop, stream);
   return merge_lists(d.lists, d.counts, B, pl.n_lists, pl.cap, k, id_offset, out_ids, out_scores, nullptr, stream,
                      row_live);
 }
@@ -428,7 +426,7 @@ int rb_dense_seed_sample(const void* queries, const void* items, int B, int N, i
                        nullptr, nullptr, nullptr);
   if (rc != RB_OK) return rc;
   const int n_chunks = static_cast<int>(dense_chunk_stride(pl));
-  // m values at or above the shard's m-th largest chunk max: its top m, up to
+  // m values at or above the shard's m-th largest tile max: its top m, up to
   // the 22-bit rounding of the bound
   return row_kth_lower_bound(chunk_max, B, n_chunks, n_chunks, 1, 0, m, d.thresh, out_vals, stream);
 }
@@ -535,9 +533,9 @@ int rb_dense_topk_launches(int B, int N, int D, int dtype, int k, int* n_launche
   if (pl.sample_stride == 0) {
     *n_launches = 2;  // full pass, merge
   } else if (dense_spec_applies(dtype == RB_I8 ? 2 : 0, nullptr) && dense_spec_rank(k, pl, 3) < k) {
-    // sample pass, 2 row selects, full pass, merge, then (B <= 128) check, second pass, merge;
-    // or (B > 128) select, gather, compact pass, merge, scatter, second pass, merge
-    *n_launches = B <= kSpecRows ? 8 : 12;
+    // sample pass, row select (both seeds), full pass, merge, then (B <= 128) check, second
+    // pass, merge; or (B > 128) select, gather, compact pass, merge, scatter, second pass, merge
+    *n_launches = B <= kSpecRows ? 7 : 11;
   } else {
     *n_launches = 4;  // sample pass, row select, full pass, merge
   }

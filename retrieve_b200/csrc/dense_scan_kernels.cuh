@@ -268,8 +268,7 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
         if (use_sl && p.filter.mode == kFilterBloomRecheck) {
           // Only the tile's best Bloom-passing item (the lowest index among equal scores) is
           // rechecked, once, after the tile's last chunk: the tile then counts that item if
-          // it passes exactly (its first slot), else nothing; its other slots hold NaN. The
-          // sampled values stay scores of distinct passing items, at one recheck a tile.
+          // it passes exactly, else nothing.
           const float mx = max32(r[ch]);
           if (mx > tb.sc || (tb.sc != tb.sc && mx == mx)) {
             uint32_t at = 0;
@@ -290,24 +289,37 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
               ok = pred_exact_item(p.filter, p.filter.terms + static_cast<size_t>(q) * kMaxTerms, p.filter.n_terms[q],
                                    tb.id, tile_rows, row0 + 32u * ch - 96u);
             }
-            float* dst = p.chunk_max + static_cast<size_t>(q) * p.chunk_stride + (chunk0 + ch - 3);
-            dst[0] = ok ? tb.sc : __uint_as_float(0x7fc00000u);
-            dst[1] = dst[2] = dst[3] = __uint_as_float(0x7fc00000u);
-            tb.sc = __uint_as_float(0x7fc00000u);
+            if (!ok) tb.sc = __uint_as_float(0x7fc00000u);
           }
+        } else {
+          // the tile's max over its passing items, chunk by chunk
+          tb.sc = fmaxf(tb.sc, max32(r[ch]));
         }
       }
     }
   }
   if constexpr (MODE == 1) {
-    // sampling pass: the max of every 32-item chunk, nothing else (the recheck form above
-    // writes its tile's slots itself)
-    bool tile_form = false;
-    if constexpr (FILT) tile_form = use_sl && p.filter.mode == kFilterBloomRecheck;
-    if (valid_q && !tile_form) {
+    // Sampling pass: one value per sampled tile, the max of its 128 scores (of its passing
+    // items in the filtered variants: tb carries it over the tile's chunks). k sampled tiles
+    // are k distinct items, so the k-th largest value is a lower bound on the k-th best score.
+    if (valid_q) {
+      float* dst = p.chunk_max + static_cast<size_t>(q) * p.chunk_stride;
+      if constexpr (FILT) {
+        if (((chunk0 + NCH - 1) & 3) == 3) {
+          dst[(chunk0 + NCH - 1) >> 2] = tb.sc;
+          tb.sc = __uint_as_float(0x7fc00000u);
+        }
+      } else {
+        float m = -INFINITY;
+        bool any = false;
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch)
-        p.chunk_max[static_cast<size_t>(q) * p.chunk_stride + chunk0 + ch] = max32(r[ch]);
+        for (int ch = 0; ch < NCH; ++ch) {
+          const float c = max32(r[ch]);
+          any |= c == c;
+          m = fmaxf(m, c);
+        }
+        if (((chunk0 + NCH - 1) & 3) == 3) dst[(chunk0 + NCH - 1) >> 2] = any ? m : __uint_as_float(0x7fc00000u);
+      }
     }
   } else {
     // Threshold filter: a chunk may hold a passing score iff its max (three-

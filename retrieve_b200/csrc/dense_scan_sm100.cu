@@ -110,29 +110,29 @@ void dense_plan(int B, int N, int k, int row_bytes, DensePlan& pl, int64_t n_tot
   }
   pl.cap = list_cap(k);
   pl.tiles = (N + kTileItems - 1) / kTileItems;
-  // Optional sampling pass over every s-th tile: it records the max of each
-  // 32-item chunk; the k-th largest chunk max is a lower bound on the k-th best
-  // score of the corpus (k distinct items reach it) and seeds the full pass.
-  // That bound sits near rank k * s of the corpus, so the full pass appends
-  // about k * s candidates per query: s is the sparsest stride (at most
-  // kSampleStride) that keeps those at no more than 0.1 per query row and
-  // 128-item tile (over a corpus of n_total items: the union of every shard's
-  // sample when the seed is shared) and still samples at least 4k chunks.
+  // Optional sampling pass over every s-th tile: it records the max score of each sampled
+  // tile; the k-th largest tile max is a lower bound on the k-th best score of the corpus
+  // (k distinct items reach it) and seeds the full pass. That bound sits near rank k * s of
+  // the corpus, so the full pass appends about k * s candidates per query: s is the sparsest
+  // stride (at most kSampleStride) that keeps those at no more than 0.1 per query row and
+  // 128-item tile (over a corpus of n_total items: the union of every shard's sample when the
+  // seed is shared) and still samples at least 4k tiles.
   pl.sample_stride = 0;
   const int64_t n_scale = std::max<int64_t>(n_total, N);
   for (int s = kSampleStride; s >= 1; s >>= 1) {
-    const int64_t chunks = (pl.tiles + s - 1) / s * 4;
+    const int64_t sampled = (pl.tiles + s - 1) / s;
     const bool dense_enough = static_cast<double>(k) * s * kTileItems <= 0.1 * static_cast<double>(n_scale);
-    if (chunks >= 4 * static_cast<int64_t>(k) && (dense_enough || s == 1)) {
+    if (sampled >= 4 * static_cast<int64_t>(k) && (dense_enough || s == 1)) {
       pl.sample_stride = s;
       break;
     }
   }
 }
 
+// Values per query row of the sampling pass: one per sampled tile.
 size_t dense_chunk_stride(const DensePlan& pl) {
   if (pl.sample_stride == 0) return 0;
-  return static_cast<size_t>((pl.tiles + pl.sample_stride - 1) / pl.sample_stride) * 4;
+  return static_cast<size_t>((pl.tiles + pl.sample_stride - 1) / pl.sample_stride);
 }
 
 size_t dense_workspace_bytes(int B, int N, int k, int row_bytes, bool scaled) {

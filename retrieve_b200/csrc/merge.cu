@@ -339,6 +339,71 @@ __global__ void __launch_bounds__(kMergeThreads) row_kth_kernel(const float* __r
   for (int i = static_cast<int>(sh.n_out) + threadIdx.x; i < k; i += kMergeThreads) dst[i] = -INFINITY;
 }
 
+// Two lower bounds per row in one read pair: out1[q] / out2[q] bound the k1-th / k2-th largest
+// value of row q (-inf where the row holds fewer), with row_kth_kernel's 22-bit precision.
+// The top 11 bits' histogram serves both ranks; the next 11 bits get one histogram each.
+__global__ void __launch_bounds__(kMergeThreads) row_kth2_kernel(const float* __restrict__ vals, int n, int64_t stride,
+                                                                 int k1, int k2, float* __restrict__ out1,
+                                                                 float* __restrict__ out2) {
+  __shared__ RowSelectShared sh[2];
+  const int q = blockIdx.x;
+  const float* row = vals + static_cast<int64_t>(q) * stride;
+  const int kk[2] = {k1, k2};
+  uint32_t prefix[2] = {0u, 0u}, need[2] = {static_cast<uint32_t>(k1), static_cast<uint32_t>(k2)};
+  if (n >= min(k1, k2)) {
+    for (int i = threadIdx.x; i < kBins; i += kMergeThreads) sh[0].hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kMergeThreads) {
+      const float v = row[i];
+      atomicAdd(&sh[0].hist[(isnan(v) ? 0u : f2ord(v)) >> 21], 1u);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (n >= kk[t]) {  // block-uniform
+        block_find_digit_n<kBins / kMergeThreads>(sh[0], need[t]);
+        prefix[t] = sh[0].digit << 21;
+        need[t] -= sh[0].above;
+      }
+      __syncthreads();
+    }
+    for (int i = threadIdx.x; i < kBins; i += kMergeThreads) sh[0].hist[i] = sh[1].hist[i] = 0;
+    __syncthreads();
+    const uint32_t mask = 0x7ffu << 21;
+    for (int i = threadIdx.x; i < n; i += kMergeThreads) {
+      const float v = row[i];
+      const uint32_t key = isnan(v) ? 0u : f2ord(v);
+      if (n >= k1 && (key & mask) == prefix[0]) atomicAdd(&sh[0].hist[(key >> 10) & 0x7ffu], 1u);
+      if (n >= k2 && (key & mask) == prefix[1]) atomicAdd(&sh[1].hist[(key >> 10) & 0x7ffu], 1u);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (n >= kk[t]) {
+        block_find_digit_n<kBins / kMergeThreads>(sh[t], need[t]);
+        prefix[t] |= sh[t].digit << 10;
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x == 0) {
+    out1[q] = (n < k1 || prefix[0] <= f2ord_bits(0xff800000u)) ? -INFINITY : ord2f(prefix[0]);
+    out2[q] = (n < k2 || prefix[1] <= f2ord_bits(0xff800000u)) ? -INFINITY : ord2f(prefix[1]);
+  }
+}
+
+int row_kth2_lower_bounds(const float* vals, int B, int n, int64_t stride, int k1, int k2, float* out1, float* out2,
+                          cudaStream_t stream) {
+  if (B == 0) return RB_OK;
+  row_kth2_kernel<<<B, kMergeThreads, 0, stream>>>(vals, n, stride, k1, k2, out1, out2);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error(cudaGetErrorString(e));
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
 int row_kth_lower_bound(const float* vals, int B, int n, int64_t stride, int nseg, int64_t seg_stride, int k,
                         float* out, float* out_vals, cudaStream_t stream) {
   if (B == 0) return RB_OK;

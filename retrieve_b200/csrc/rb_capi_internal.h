@@ -39,11 +39,14 @@ inline bool dense_scaled(int dtype) { return dtype == RB_I8 || dtype == RB_E4M3;
 inline int dense_row_bytes(int D, int dtype) { return (dtype == RB_I8 || dtype == RB_E4M3) ? D : 2 * D; }
 int num_sms();
 size_t dense_chunk_stride(const DensePlan& pl);
-// mode 0: candidate pass over every tile; mode 1: chunk-max sampling pass.
+// mode 0: candidate pass over every tile; mode 1: sampling pass (one max per sampled tile).
 int dense_scan_pass(int mode, int elem, const void* q, const void* x, int B, int N, int D, const DensePlan& pl,
                     int k, const float* seed, uint2* lists, int* counts, float* chunk_max, int* err,
                     cudaStream_t stream, const float* q_scale = nullptr, const float* x_scale = nullptr,
                     const FilterArgs* filter = nullptr, const int* qsg_live = nullptr);
+// The same for two ranks at once (nseg 1, no values): out1 / out2 bound the k1-th / k2-th.
+int row_kth2_lower_bounds(const float* vals, int B, int n, int64_t stride, int k1, int k2, float* out1, float* out2,
+                          cudaStream_t stream);
 // Per row of vals [B, n] (row stride `stride`): a lower bound on the k-th
 // largest value (exact to 22 leading key bits), -inf when n < k.
 int row_kth_lower_bound(const float* vals, int B, int n, int64_t stride, int nseg, int64_t seg_stride, int k,

@@ -102,7 +102,7 @@ def dense_workspace(query: Tensor, item_shard: Tensor, k: int) -> Tensor:
 def dense_seed_sample(
     query: Tensor, item_shard: Tensor, k: int, n_total: int, ws: Tensor | None = None, m: int | None = None
 ) -> Tensor:
-    """Per query, this shard's top ``m`` (default k) sampled chunk maxima
+    """Per query, this shard's top ``m`` (default k) sampled tile maxima
     (``[B, m]`` fp32) for the threshold shared by all shards (C-ABI
     ``rb_dense_seed_sample``)."""
     m = k if m is None else int(m)

@@ -4,7 +4,7 @@ The corpus is split row-wise into contiguous shards; rank ``r`` holds rows
 ``[offset_r, offset_r + n_r)``. A query batch (replicated on every rank) is
 scored against the local shard with the fused kernel. One search is:
 
-1. every rank samples its shard (``dense_seed_sample``: k chunk maxima per
+1. every rank samples its shard (``dense_seed_sample``: k tile maxima per
    query) and one NCCL all-gather brings the ``[W, B, k]`` samples to every rank;
 2. every rank runs the full pass over its shard seeded by the k-th largest
    value of the union — a lower bound on the global k-th score — and keeps its
@@ -199,7 +199,7 @@ class ShardedDenseTopK:
                 dist.all_reduce(t, group=group)
                 n_total = int(t.item())
         self.n_total = int(n_total)
-        # each shard sends its top m sampled chunk maxima per query: any subset
+        # each shard sends its top m sampled tile maxima per query: any subset
         # keeps the union's k-th a valid bound, and about 2k/W keeps it as tight
         # as all k unless one shard holds more than m of the global top chunks
         self.sample_width = min(self.k, max(16, -(-2 * self.k // max(self.world, 1))))

@@ -79,8 +79,8 @@ def test_shared_seed_uneven_shards_with_unsampled_one():
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_i.cpu().numpy(), ref_s.cpu().numpy())
 
 
-def test_seed_sample_values_are_chunk_maxima_bounds():
-    # every sampled value is the max of some 32-item chunk of the shard, so at
+def test_seed_sample_values_are_tile_maxima_bounds():
+    # every sampled value is the max of some 128-item tile of the shard, so at
     # least k distinct items score >= the k-th largest sample value
     b, n, k = 200, 500_000, 50
     q = make_int_rows(b, 128, seed=31, device="cuda")
