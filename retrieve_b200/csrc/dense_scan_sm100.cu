@@ -21,6 +21,7 @@
 // toward the lower item id.
 #include "dense_scan_kernels.cuh"
 
+#include <atomic>
 #include <mutex>
 
 namespace rb {
@@ -78,14 +79,24 @@ int list_cap(int k) {
 // Entries per lane of the register-resident list compaction for a list of cap.
 static int dense_epl(int cap) { return cap <= 256 ? 8 : (cap <= 512 ? 16 : 40); }
 
+// SMs of the current device, looked up once per device ordinal (thread-safe).
 int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+  static std::atomic<int> cached[kMaxCachedDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxCachedDevices) {
+    cudaGetLastError();
+    dev = -1;
   }
+  if (dev >= 0) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int n = 0;
+  if (dev < 0 || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = 148;
+  }
+  if (dev >= 0) cached[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 

@@ -11,6 +11,9 @@
 
 namespace rb {
 
+// Device ordinals whose per-device lookups (SM count, CTA-pair occupancy) are cached.
+constexpr int kMaxCachedDevices = 64;
+
 void set_last_error(const char* msg);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }

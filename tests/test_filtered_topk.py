@@ -166,3 +166,44 @@ def test_sliced_bloom_test_equals_the_per_item_test(mode):
         masks &= _masks(exprs, b, attrs=attrs.numpy())
     ref_ids, ref_scores = _oracle(q.cpu(), x.cpu(), k, masks)
     assert_topk_exact(out[1][0], out[1][1], ref_ids, ref_scores)
+
+
+@pytest.mark.parametrize("layout", ["two_values", "odd_row", "unaligned"])
+@pytest.mark.parametrize("mode", ["exact", "bloom_recheck"])
+def test_attribute_rows_outside_the_ring(layout, mode):
+    """The 2-SM filtered kernel (B > 128) streams attribute rows of at most 8 cells, a whole
+    number of 16-byte units at a 16-byte aligned address, through its shared-memory ring;
+    other rows are rechecked from global memory: 16 cells (8 clauses x 2 values), 5 cells
+    (an odd row) and 8 cells at an address 8 bytes off alignment. Bit for bit the oracle's."""
+    from retrieve_b200 import ops
+
+    b, n, k = 260, 80_000, 50
+    base = gi.zipf_attrs(n, seed=21)
+    if layout == "two_values":
+        second = gi.zipf_attrs(n, seed=22)
+        second[torch.rand(n, 8, generator=torch.Generator().manual_seed(5)) < 0.5] = -1
+        attrs3 = torch.stack([base, second], dim=2).contiguous()  # [n, 8, 2]
+        exprs = [EXPRS[i % len(EXPRS)] for i in range(b)]
+    elif layout == "odd_row":
+        attrs3 = base[:, :5, None].contiguous()  # [n, 5, 1]
+        exprs = ["0:0", "1:3 OR 2:7", "0:1 AND 3:2", "NOT 0:0", "(4:5 OR 1:1) AND 0:2", "1:0 AND NOT 2:0"]
+        exprs = [exprs[i % len(exprs)] for i in range(b)]
+    else:
+        attrs3 = base[:, :, None].contiguous()
+        exprs = [EXPRS[i % len(EXPRS)] for i in range(b)]
+    q = make_int_rows(b, 128, seed=23)
+    x = make_int_rows(n, 128, seed=24)
+    preds = P.from_expressions(exprs).to("cuda")
+    dev_attrs = attrs3.cuda()
+    if layout == "unaligned":
+        flat = torch.empty(attrs3.numel() + 1, dtype=torch.int64, device="cuda")
+        flat[1:] = dev_attrs.reshape(-1)
+        dev_attrs = flat[1:].view(attrs3.shape)  # 8 bytes past a 16-byte boundary
+        assert dev_attrs.data_ptr() % 16 == 8
+    words = ops.bloom_build(dev_attrs, 3)
+    ids, scores = ops.dense_topk_filtered(q.cuda(), x.cuda(), k, preds.terms, preds.n_terms, mode, dev_attrs, words)
+    masks = _masks(exprs, b, attrs=attrs3.numpy())
+    if mode == "bloom_recheck":
+        masks &= _masks(exprs, b, words=words.cpu().numpy().view(np.uint64))
+    ref_ids, ref_scores = _oracle(q, x, k, masks)
+    assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
