@@ -153,18 +153,40 @@ struct TileBest {
   uint32_t id;
 };
 
+// int8: this lane's four item scales of a tile (items row0 + 4 lane .. + 3; 0 past N) and
+// the query's scale, loaded one tile ahead by the epilogue loop so that the loads' latency
+// hides behind the previous tile's work.
+struct ScalePrefetch {
+  float4 xs;
+  float qs;
+  bool on;
+};
+
+__device__ __forceinline__ float4 load_tile_scales(const DenseScanParams& p, uint32_t row0) {
+  const uint32_t id = row0 + 4u * (threadIdx.x & 31);
+  if (p.x_scale == nullptr) return make_float4(1.f, 1.f, 1.f, 1.f);
+  if (row0 + kTileItems <= static_cast<uint32_t>(p.N)) return __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
+  float4 v;
+  v.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
+  v.y = id + 1 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 1] : 0.f;
+  v.z = id + 2 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 2] : 0.f;
+  v.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
+  return v;
+}
+
 template <int MODE, int NCH, int ELEM, bool FILT, int KB>
 __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_t (&r)[NCH][32], uint32_t row0,
                                                int chunk0, bool valid_q, int q, float thresh, int& count,
                                                uint2* list, uint32_t* stage, const uint32_t* sl,
                                                const SlicedTerms& st, bool use_sl, TileBest& tb,
                                                const int64_t* tile_rows = nullptr,
-                                               const ExactTerm* wterms = nullptr, int ent = 0) {
+                                               const ExactTerm* wterms = nullptr, int ent = 0,
+                                               ScalePrefetch sp = ScalePrefetch{}) {
   // Chunks whose scores may pass (bit ch); the full int8 pass clears the bits of
   // chunks it proves below the threshold before dequantizing them.
   uint32_t live = (1u << NCH) - 1u;
   if constexpr (ELEM == 2) {
-    const float qs = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
+    const float qs = sp.on ? sp.qs : (!valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f));
     const bool unit_x = p.x_scale == nullptr;
     // Every lane needs all 128 item scales of the tile: the warp loads them
     // once (one float4 per lane, coalesced) into shared memory, and each lane
@@ -173,15 +195,19 @@ __device__ __forceinline__ void process_chunks(const DenseScanParams& p, uint32_
     float lmax = 1.f, lmin = 1.f;  // this lane's 4 scales' max and min (chunk lane / 8)
     if (!unit_x) {
       const int lane = threadIdx.x & 31;
-      const uint32_t id = row0 + 4 * static_cast<uint32_t>(lane);
       float4 v;
-      if (row0 + NCH * 32 <= static_cast<uint32_t>(p.N)) {
-        v = __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
+      if (sp.on) {
+        v = sp.xs;
       } else {
-        v.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
-        v.y = id + 1 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 1] : 0.f;
-        v.z = id + 2 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 2] : 0.f;
-        v.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
+        const uint32_t id = row0 + 4 * static_cast<uint32_t>(lane);
+        if (row0 + NCH * 32 <= static_cast<uint32_t>(p.N)) {
+          v = __ldg(reinterpret_cast<const float4*>(p.x_scale + id));
+        } else {
+          v.x = id < static_cast<uint32_t>(p.N) ? p.x_scale[id] : 0.f;
+          v.y = id + 1 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 1] : 0.f;
+          v.z = id + 2 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 2] : 0.f;
+          v.w = id + 3 < static_cast<uint32_t>(p.N) ? p.x_scale[id + 3] : 0.f;
+        }
       }
       sx[lane] = v;
       lmax = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
@@ -585,7 +611,21 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
       int lo, hi;
       split_range(split, p.n_splits, p.pass_tiles, lo, hi);
       bool ok = true;
+      // int8: the item scales one tile ahead, the query's scale once per task
+      ScalePrefetch sp_cur{}, sp_next{};
+      if constexpr (ELEM == 2 && !FILT) {
+        const float qsv = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
+        sp_cur.qs = sp_next.qs = qsv;
+        sp_cur.on = sp_next.on = true;
+        if (lo < hi)
+          sp_cur.xs = load_tile_scales(p, static_cast<uint32_t>((lo * p.tile_stride + p.tile_offset) * kTileItems));
+      }
       for (int pt = lo; pt < hi; ++pt) {
+        if constexpr (ELEM == 2 && !FILT) {
+          if (pt + 1 < hi)
+            sp_next.xs =
+                load_tile_scales(p, static_cast<uint32_t>(((pt + 1) * p.tile_stride + p.tile_offset) * kTileItems));
+        }
         if constexpr (MODE == 0) {
           // Room for a whole tile of appends; compacting here keeps no scores live
           // across the (non-inlined) compaction.
@@ -671,7 +711,8 @@ __global__ void __launch_bounds__(64 + 128 * NG, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
           process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
-                                                  use_sl, tb);
+                                                  use_sl, tb, nullptr, nullptr, 0, sp_cur);
+          if constexpr (ELEM == 2 && !FILT) sp_cur = sp_next;
         }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
@@ -1028,7 +1069,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
       int lo, hi;
       split_range(split, p.n_splits, p.pass_tiles, lo, hi);
       bool ok = true;
+      // int8: the item scales one tile ahead, the query's scale once per task
+      ScalePrefetch sp_cur{}, sp_next{};
+      if constexpr (ELEM == 2 && !FILT) {
+        const float qsv = !valid_q ? 0.f : (p.q_scale != nullptr ? p.q_scale[q] : 1.f);
+        sp_cur.qs = sp_next.qs = qsv;
+        sp_cur.on = sp_next.on = true;
+        if (lo < hi)
+          sp_cur.xs = load_tile_scales(p, static_cast<uint32_t>((lo * p.tile_stride + p.tile_offset) * kTileItems));
+      }
       for (int pt = lo; pt < hi; ++pt) {
+        if constexpr (ELEM == 2 && !FILT) {
+          if (pt + 1 < hi)
+            sp_next.xs =
+                load_tile_scales(p, static_cast<uint32_t>(((pt + 1) * p.tile_stride + p.tile_offset) * kTileItems));
+        }
         if constexpr (MODE == 0) {
           const bool need = valid_q && (count > p.cap - kTileItems);
           if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
@@ -1116,7 +1171,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
           process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
-                                                  use_sl, tb);
+                                                  use_sl, tb, nullptr, nullptr, 0, sp_cur);
+          if constexpr (ELEM == 2 && !FILT) sp_cur = sp_next;
         }
         if (++acc == kAcc) {
           acc = 0;
