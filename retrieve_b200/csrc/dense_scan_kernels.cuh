@@ -791,9 +791,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* a_full = bars + 2 * STAGES;
   uint64_t* a_empty = a_full + 1;
-  uint64_t* acc_full = a_full + 2;         // [kAcc]
-  uint64_t* acc_empty = acc_full + kAcc;  // [kAcc], used on CTA 0
-  uint64_t* drain_bar = acc_empty + kAcc;
+  uint64_t* acc_full = a_full + 2;              // [kAcc][NG]
+  uint64_t* acc_empty = acc_full + kAcc * NG;  // [kAcc][NG], used on CTA 0
+  uint64_t* drain_bar = acc_empty + kAcc * NG;
   uint64_t* ring_full = drain_bar + 1;           // [kRingSlots] (filtered variants)
   uint64_t* ring_empty = ring_full + kRingSlots;  // [kRingSlots]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1 + (FILT ? 2 * kRingSlots : 0));
@@ -813,9 +813,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
     }
     mbar_init(a_full, 1);
     mbar_init(a_empty, 1);
-    for (int b = 0; b < kAcc; ++b) {
+    for (int b = 0; b < kAcc * NG; ++b) {  // one pair per (buffer, query group): 4 warps a CTA each
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 2 * L::kEpiWarps);
+      mbar_init(&acc_empty[b], 2 * 4);
     }
     mbar_init(drain_bar, 1);
     if constexpr (FILT) {
@@ -957,20 +957,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
         split_range(split, p.n_splits, p.pass_tiles, lo, hi);
         bool ok = true;
         for (int pt = lo; pt < hi; ++pt) {
-          const bool ready = mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag) &&
-                             mbar_wait(&full_bar[stage], phase, abort_flag);
-          if (!__all_sync(RB_FULL_MASK, ready)) {
+          if (!__all_sync(RB_FULL_MASK, mbar_wait(&full_bar[stage], phase, abort_flag))) {
             if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutMma);
             *abort_flag = 1;
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t d_col = tmem_base + static_cast<uint32_t>(acc * NG * 128);
           const uint64_t b_stage = b_desc0 + static_cast<uint64_t>((stage * KB * L::kBTile) >> 4);
-          if (elect_one()) {
+          // Each query group's MMAs go as soon as that group's epilogue warps have released
+          // its accumulator, so one group's slow warp does not hold the other group back.
 #pragma unroll
-            for (int g = 0; g < NG; ++g) {
+          for (int g = 0; g < NG; ++g) {
+            if (!__all_sync(RB_FULL_MASK, mbar_wait(&acc_empty[acc * NG + g], acc_phase ^ 1, abort_flag))) {
+              if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutMma);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            if (elect_one()) {
 #pragma unroll
               for (int kb = 0; kb < KB; ++kb) {
 #pragma unroll
@@ -985,12 +991,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
                     mma_f16_pair(d_col + g * 128, ad, bd, kIdesc, (kb | j) != 0);
                 }
               }
+              const uint32_t ao = static_cast<uint32_t>(acc * NG + g) * 8u;
+              mma_commit_pair(accf0 + ao);
+              mma_commit_pair(accf1 + ao);
             }
-            const uint32_t so = static_cast<uint32_t>(stage) * 8u, ao = static_cast<uint32_t>(acc) * 8u;
+            __syncwarp();
+          }
+          if (!ok) break;
+          if (elect_one()) {  // the item stage goes back once every group's MMAs are done with it
+            const uint32_t so = static_cast<uint32_t>(stage) * 8u;
             mma_commit_pair(empty0 + so);
             mma_commit_pair(empty1 + so);
-            mma_commit_pair(accf0 + ao);
-            mma_commit_pair(accf1 + ao);
           }
           __syncwarp();
           if (++stage == STAGES) {
@@ -1088,7 +1099,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
           const bool need = valid_q && (count > p.cap - kTileItems);
           if (__any_sync(RB_FULL_MASK, need)) warp_compact_lists<EPL>(list, count, thresh, need, p.k, hist);
         }
-        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag)) {
+        if (!mbar_wait(&acc_full[acc * NG + g], acc_phase, abort_flag)) {
           if (lane == 0) atomicCAS(p.err, 0, kDevTimeoutEpilogue);
           *abort_flag = 1;
           ok = false;
@@ -1134,7 +1145,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
           if (todo == 0u) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
+            if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc * NG + g) * 8u);
           }
           const int last = todo == 0u ? -1 : 31 - __clz(todo);
 #pragma unroll 1
@@ -1147,7 +1158,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
             if (ch == last) {  // the accumulator goes back after the tile's last load
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
+              if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc * NG + g) * 8u);
             }
             process_chunks<MODE, 1, ELEM, FILT, KB>(p, r1, row0 + ch * 32, pt * 4 + ch, valid_q, q, thresh, count,
                                                     list, hist, sl + ch * 64, st, use_sl, tb, tile_rows, wterms,
@@ -1169,7 +1180,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 128 * NG, 1)
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc) * 8u);
+          if (lane == 0) mbar_arrive_cluster(release0 + static_cast<uint32_t>(acc * NG + g) * 8u);
           process_chunks<MODE, 4, ELEM, FILT, KB>(p, r, row0, pt * 4, valid_q, q, thresh, count, list, hist, sl, st,
                                                   use_sl, tb, nullptr, nullptr, 0, sp_cur);
           if constexpr (ELEM == 2 && !FILT) sp_cur = sp_next;
