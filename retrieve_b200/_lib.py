@@ -59,6 +59,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_size, _vp]
     ),
     "rb_bloom_build": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
+    "rb_bloom_slices_bytes": (_c_int, [_c_i64, ctypes.POINTER(_c_size)]),
+    "rb_bloom_slices": (_c_int, [_vp, _c_i64, _vp, _vp]),
     "rb_dense_topk_i8": (
         _c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_i64, _vp, _vp, _vp, _c_size, _vp]
     ),

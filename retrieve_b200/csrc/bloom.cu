@@ -170,6 +170,31 @@ __global__ void bloom_index_fill_kernel(const int32_t* __restrict__ feature_ids,
 
 using namespace rb;
 
+extern "C" int rb_bloom_slices_bytes(int64_t N, size_t* bytes) {
+  if (bytes == nullptr || N < 0) {
+    rb::set_last_error("bloom_slices_bytes: bad arguments");
+    return RB_ERR_INVALID_ARG;
+  }
+  *bytes = rb::bloom_slices_bytes(N);
+  return RB_OK;
+}
+
+extern "C" int rb_bloom_slices(const uint64_t* item_bloom, int64_t N, uint32_t* out_slices, void* stream) {
+  if (N < 0 || (N > 0 && (item_bloom == nullptr || out_slices == nullptr))) {
+    rb::set_last_error("bloom_slices: bad arguments");
+    return RB_ERR_INVALID_ARG;
+  }
+  if ((reinterpret_cast<uintptr_t>(out_slices) & 15u) != 0) {
+    rb::set_last_error("bloom_slices: out_slices must be 16-byte aligned");
+    return RB_ERR_INVALID_ARG;
+  }
+  if (rb::bloom_slices(item_bloom, N, out_slices, static_cast<cudaStream_t>(stream)) != RB_OK) {
+    rb::set_last_error("bloom_slices: launch failed");
+    return RB_ERR_CUDA;
+  }
+  return RB_OK;
+}
+
 extern "C" int rb_bloom_build(const int64_t* item_attrs, int N, int C, int A, int k, uint64_t* out_words,
                               void* stream) {
   if (N < 0 || C <= 0 || A <= 0 || k < 1 || k > 64) {

@@ -49,7 +49,7 @@ extern "C" {
 
 const char* rb_last_error(void) { return g_last_error.c_str(); }
 
-int rb_abi_version(void) { return 1; }
+int rb_abi_version(void) { return 2; }
 
 int rb_dense_topk_workspace_size(int B, int N, int D, int dtype, int k, size_t* bytes) {
   if (bytes == nullptr) return fail(RB_ERR_INVALID_ARG, "bytes is null");
@@ -487,6 +487,11 @@ int rb_dense_topk_filtered(const void* queries, const void* items, int B, int N,
   f.C = filter->n_clauses;
   f.A = filter->attr_width;
   f.bloom = filter->item_bloom;
+  if (f.mode == RB_FILTER_BLOOM || f.mode == RB_FILTER_BLOOM_RECHECK) {
+    f.slices = filter->item_bloom_slices;  // null: built into the workspace below
+    if (f.slices != nullptr && (reinterpret_cast<uintptr_t>(f.slices) & 15u) != 0)
+      return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: item_bloom_slices must be 16-byte aligned");
+  }
   if (f.mode < RB_FILTER_NONE || f.mode > RB_FILTER_BLOOM_RECHECK)
     return fail(RB_ERR_INVALID_ARG, "dense_topk_filtered: unknown filter mode");
   if (f.mode != RB_FILTER_NONE && (f.terms == nullptr || f.n_terms == nullptr))

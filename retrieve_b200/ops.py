@@ -225,6 +225,7 @@ class _RbFilter(ctypes.Structure):
         ("n_clauses", ctypes.c_int),
         ("attr_width", ctypes.c_int),
         ("item_bloom", ctypes.c_void_p),
+        ("item_bloom_slices", ctypes.c_void_p),
     ]
 
 
@@ -238,6 +239,7 @@ def dense_topk_filtered(
     mode: str,
     item_attrs: Tensor | None = None,
     item_bloom: Tensor | None = None,
+    item_bloom_slices: Tensor | None = None,
 ) -> tuple[Tensor, Tensor]:
     """``dense_topk`` over the items that pass each query's predicate
     (``retrieve_b200.predicates``): ``mode`` ``"exact"`` tests ``item_attrs
@@ -245,7 +247,9 @@ def dense_topk_filtered(
     (false positives possible, no false negatives for NOT-free predicates),
     ``"bloom_recheck"`` both. Rows with fewer than k passing items end in
     ``-1`` / ``-inf``. The predicate is evaluated inside the fused scan, only on
-    items whose score already clears the running top-k threshold."""
+    items whose score already clears the running top-k threshold.
+    ``item_bloom_slices`` (optional, the Bloom modes): ``bloom_slices(item_bloom)``
+    built once with the index; without it the call builds them into its workspace."""
     if mode not in FILTER_MODES:
         raise ValueError(f"mode must be one of {sorted(FILTER_MODES)}, got {mode!r}")
     if query.dim() != 2 or item_embs.dim() != 2:
@@ -270,6 +274,12 @@ def dense_topk_filtered(
         if item_bloom is None or item_bloom.shape != (n,) or item_bloom.dtype not in (torch.int64, torch.uint64):
             raise ValueError("bloom filtering needs item_bloom [N] 64-bit words")
         check_contiguous(item_bloom=item_bloom)
+        if item_bloom_slices is not None:
+            if (item_bloom_slices.dim() != 1 or item_bloom_slices.dtype != torch.int32
+                    or item_bloom_slices.numel() < (n + 127) // 128 * 256):
+                raise ValueError("item_bloom_slices must be bloom_slices(item_bloom): int32, 256 words per 128 items")
+            _require_cuda(item_bloom_slices)
+            check_contiguous(item_bloom_slices=item_bloom_slices)
     q = query.to(item_embs.dtype).contiguous()
     tt = terms.contiguous()
     nt = n_terms.to(torch.int32).contiguous()
@@ -282,6 +292,7 @@ def dense_topk_filtered(
         m, tt.data_ptr(), nt.data_ptr(), 0 if attrs is None else attrs.data_ptr(),
         0 if attrs is None else attrs.shape[1], 0 if attrs is None else attrs.shape[2],
         0 if item_bloom is None else item_bloom.data_ptr(),
+        0 if item_bloom_slices is None or m not in (2, 3) else item_bloom_slices.data_ptr(),
     )
     lib = _lib.lib()
     code = _DTYPE_CODE[item_embs.dtype]
@@ -296,7 +307,7 @@ def dense_topk_filtered(
 
 
 @dense_topk_filtered.register_fake
-def _(query, item_embs, k, terms, n_terms, mode, item_attrs=None, item_bloom=None):
+def _(query, item_embs, k, terms, n_terms, mode, item_attrs=None, item_bloom=None, item_bloom_slices=None):
     b = query.shape[0]
     return query.new_empty((b, k), dtype=torch.int64), query.new_empty((b, k), dtype=torch.float32)
 
@@ -311,6 +322,23 @@ def bloom_build(item_attrs: Tensor, k: int = 3) -> Tensor:
     out = torch.empty((a.shape[0],), dtype=torch.int64, device=a.device)
     rc = _lib.lib().rb_bloom_build(_ptr(a), a.shape[0], a.shape[1], a.shape[2], k, _ptr(out), _stream_ptr(a.device))
     _lib.check(rc, "bloom_build")
+    return out
+
+
+def bloom_slices(item_bloom: Tensor) -> Tensor:
+    """The per-item Bloom words ``item_bloom [N]`` (``bloom_build``) bit-sliced for the
+    filtered scans (``rb_bloom_slices``): per 32-item chunk 64 int32 words, word p
+    holding bit p of the chunk's items, whole 128-item tiles. Build time; pass the
+    result to ``dense_topk_filtered(..., item_bloom_slices=...)``."""
+    if item_bloom.dim() != 1 or item_bloom.dtype != torch.int64:
+        raise ValueError("item_bloom must be [N] int64 (bloom_build)")
+    _require_cuda(item_bloom)
+    w = item_bloom.contiguous()
+    nb = ctypes.c_size_t(0)
+    lib = _lib.lib()
+    _lib.check(lib.rb_bloom_slices_bytes(w.shape[0], ctypes.byref(nb)), "bloom_slices")
+    out = torch.zeros((max(int(nb.value) // 4, 4),), dtype=torch.int32, device=w.device)
+    _lib.check(lib.rb_bloom_slices(_ptr(w), w.shape[0], _ptr(out), _stream_ptr(w.device)), "bloom_slices")
     return out
 
 

@@ -21,7 +21,7 @@ def test_library_exports_every_header_symbol():
 
 
 def test_abi_version():
-    assert _lib.lib().rb_abi_version() == 1
+    assert _lib.lib().rb_abi_version() == 2
 
 
 def test_dense_workspace_query_is_host_only():

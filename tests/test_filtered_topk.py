@@ -207,3 +207,25 @@ def test_attribute_rows_outside_the_ring(layout, mode):
         masks &= _masks(exprs, b, words=words.cpu().numpy().view(np.uint64))
     ref_ids, ref_scores = _oracle(q, x, k, masks)
     assert_topk_exact(ids.cpu().numpy(), scores.cpu().numpy(), ref_ids, ref_scores)
+
+
+@pytest.mark.parametrize("b", [64, 300])
+@pytest.mark.parametrize("mode", ["bloom", "bloom_recheck"])
+def test_prebuilt_bloom_slices_equal_per_call_build(mode, b):
+    """Bloom words bit-sliced once at build time (``bloom_slices``) and passed to the search give
+    the same top-k as the slices the call builds into its workspace (1-SM and 2-SM kernels)."""
+    from retrieve_b200 import ops
+
+    n, k = 90_000, 40
+    attrs = gi.zipf_attrs(n, seed=41)[:, :, None].contiguous().cuda()
+    q = make_int_rows(b, 128, seed=42).cuda()
+    x = make_int_rows(n, 128, seed=43).cuda()
+    exprs = [EXPRS[i % len(EXPRS)] for i in range(b)]
+    preds = P.from_expressions(exprs).to("cuda")
+    words = ops.bloom_build(attrs, 3)
+    slices = ops.bloom_slices(words)
+    assert slices.numel() == (n + 127) // 128 * 256
+    ids0, sc0 = ops.dense_topk_filtered(q, x, k, preds.terms, preds.n_terms, mode, attrs, words)
+    ids1, sc1 = ops.dense_topk_filtered(q, x, k, preds.terms, preds.n_terms, mode, attrs, words, slices)
+    assert torch.equal(ids0, ids1)
+    assert torch.equal(sc0, sc1)
