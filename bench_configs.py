@@ -22,6 +22,7 @@ step streams more than L2), so no flush is needed.
 from __future__ import annotations
 
 import json
+from pathlib import Path
 import statistics
 
 import torch
@@ -458,8 +459,11 @@ def _ivf_cpu_baseline(q, probe, offsets, sizes, codes_sorted, perm, gs, k, width
             "sample": f"{sample} queries of the batch, phase 2 + 3 only (probe lists given)"}
 
 
-def run_ivf(args, dev):
-    import retrieve_b200.st  # noqa: F401  (registers torch.ops.st.search)
+def _ivf_inputs(args, dev):
+    """The IVF workload's index and query batch (C2's mixture clustered by its nearest
+    normalised centre, int8 codes with one global scale), built with this library's
+    ``retrieve::`` ops only (no ``st`` schema), so that the reference arm can build the same
+    inputs beside the reference's own ``st`` library."""
     from retrieve_b200 import ops
     from retrieve_b200.quantize import quantize_int8_global
 
@@ -486,6 +490,25 @@ def run_ivf(args, dev):
     probe0 = ops.dense_topk(qb, centroids, n_probe)[0]
     width = int(sizes[probe0].sum(1).max()) + 32 * n_probe  # room for other batches' probe totals
     torch.cuda.synchronize()
+    return dict(n=n, d=d, b=b, k=k, n_probe=n_probe, n_lists=n_lists, centroids=centroids, perm=perm,
+                sizes=sizes, offsets=offsets, codes_sorted=codes_sorted, gs=gs, q=q, qb=qb, probe0=probe0,
+                width=width)
+
+
+def _ids_digest(ids: torch.Tensor) -> str:
+    import hashlib
+
+    return hashlib.sha256(ids.to(torch.int64).cpu().numpy().tobytes()).hexdigest()[:16]
+
+
+def run_ivf(args, dev):
+    import retrieve_b200.st  # noqa: F401  (registers torch.ops.st.search)
+    from retrieve_b200 import ops
+
+    w = _ivf_inputs(args, dev)
+    n, d, b, k, n_probe, n_lists = w["n"], w["d"], w["b"], w["k"], w["n_probe"], w["n_lists"]
+    centroids, perm, sizes, offsets = w["centroids"], w["perm"], w["sizes"], w["offsets"]
+    codes_sorted, gs, q, qb, probe0, width = w["codes_sorted"], w["gs"], w["q"], w["qb"], w["probe0"], w["width"]
 
     from retrieve_b200 import st
 
@@ -499,10 +522,15 @@ def run_ivf(args, dev):
 
     a, b_ = step(), step_rows()
     same = bool(torch.equal(a[0], b_[0]) and torch.equal(a[1], b_[1]))
+    digest = _ids_digest(torch.ops.st.search(q, probe0, offsets, sizes, codes_sorted, perm, gs, k, width)[0])
     sampler = bench.ClockSampler(dev)
     sampler.start()
     ms, kms = _time(step, args.warmup, args.steps)
     ms_rows, kms_rows = _time(step_rows, args.warmup, args.steps)
+    # st::search alone on phase 1's probes: the span `--impl reference --workload ivf` times
+    # for the reference's own CUDA op
+    ms_search, _ = _time(lambda: torch.ops.st.search(q, probe0, offsets, sizes, codes_sorted, perm, gs, k, width),
+                         args.warmup, args.steps, kernel=False)
     bloom = _ivf_bloom_timing(args, dev, q, qb, centroids, n_probe, offsets, sizes, codes_sorted, perm, gs, k, width)
     clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
     scored = float(sizes[probe0].sum())  # probed (query, item) pairs per batch
@@ -520,6 +548,9 @@ def run_ivf(args, dev):
                                  "up to 128 probing rows, tcgen05 kind::i8 MMA",
                        "rows": {"queries_per_s": b / (ms_rows / 1e3), "ms_per_step": ms_rows,
                                 "kernel_ms": kms_rows, "identical_to_the_op": same},
+                       "search_only": {"queries_per_s": b / (ms_search / 1e3), "ms_per_step": ms_search,
+                                       "ids_sha256_16": digest,
+                                       "note": "torch.ops.st.search alone on fixed probes (phase 2 + 3)"},
                        "bloom": bloom,
                        "corpus": "the C2 mixture, clustered by its nearest normalised centre, int8 with one global "
                                  "scale"},
@@ -593,6 +624,36 @@ def measure_configs(args, dev, names=("c3", "c4", "c5", "ivf")) -> dict:
     return out
 
 
+def reference_ivf(args, dev) -> dict:
+    """The reference's own CUDA ``st::search`` (SilverTorch fork_search_cuda.cu, built from its
+    sources by ``oracle/build_ref.py --cuda``) on the IVF workload's inputs, timed like this
+    library's op: the same index and probes, ``torch.ops.st.search`` alone (phase 2 + 3)."""
+    lib = Path(__file__).resolve().parent / "oracle" / "_ref" / "silvertorch_ref_cuda" / "silvertorch_ref_cuda.so"
+    if not lib.exists():
+        return {"impl": "reference", "unavailable": "the reference's CUDA ops were not built "
+                "(python oracle/build_ref.py <checkout> --cuda)"}
+    torch.ops.load_library(str(lib))
+    w = _ivf_inputs(args, dev)
+    b, k = w["b"], w["k"]
+    call = (w["q"], w["probe0"], w["offsets"], w["sizes"], w["codes_sorted"], w["perm"], w["gs"], k, w["width"])
+    out = torch.ops.st.search(*call)
+    digest = _ids_digest(out[0])
+    sampler = bench.ClockSampler(dev)
+    sampler.start()
+    ms, _ = _time(lambda: torch.ops.st.search(*call), args.warmup, args.steps, kernel=False)
+    clocks = bench.ClockSampler.summary([(sampler.stop(), sampler.error)])
+    value = b / (ms / 1e3)
+    return {"metric": "queries/s, st::search alone (phase 2 + 3) @10M items d=128 int8 (global scale), 1024 "
+                      "lists, 16 probes, B=1024, k=100", "value": value, "unit": "queries/s", "ms_per_step": ms,
+            "higher_is_better": True, "impl": "reference", "dtype": "int8 -> int32",
+            "config": {"workload": "SilverTorch IVF search (st::search), the reference's own CUDA op",
+                       "n_items": w["n"], "batch": b, "k": k, "n_probe": w["n_probe"],
+                       "max_tensor_size_per_row": w["width"], "ids_sha256_16": digest,
+                       "library": "oracle/_ref/silvertorch_ref_cuda (the reference's *.cpp + *_cuda.cu, sm_100a)"},
+            "clocks": clocks,
+            "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def run_workload(args):
     import os
 
@@ -602,6 +663,16 @@ def run_workload(args):
     torch.cuda.set_device(dev)
     if args.workload == "ops":
         run_ops(args, dev)
+        return
+    if getattr(args, "impl", "ours") == "reference":
+        if args.workload != "ivf":
+            print(json.dumps({"impl": "reference", "unavailable": f"no reference arm for --workload {args.workload} "
+                              "(its CPU baseline is part of the configuration's own line)"}), flush=True)
+            return
+        rec = reference_ivf(args, dev)
+        line = {"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "data": "synthetic"}
+        line.update(rec)
+        print(json.dumps(line), flush=True)
         return
     rec = {"c3": run_c3, "c4": run_c4, "c5": run_c5, "ivf": run_ivf}[args.workload](args, dev)
     line = {"metric": rec.pop("metric"), "value": rec.pop("value"), "unit": rec.pop("unit"), "n_gpus": 1,
