@@ -57,6 +57,9 @@ def parse_args():
     p.add_argument("--ref-sample", type=int, default=32,
                    help="queries per step of --impl reference (each step a bounded sample)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--reference-device", choices=("cpu", "cuda"), default="cpu",
+                   help="--impl reference: the reference's CPU path (FullScanKNN on the host cores, the "
+                        "default) or its own GPU path (PostfilterKNN: cuBLAS fp16 scores + masked_topk)")
     p.add_argument("--exchange", choices=("nccl", "peer"), default="nccl",
                    help="the sharded search's two all-gathers: NCCL, or stores into the peers' memory")
     p.add_argument("--no-configs", action="store_true",
@@ -239,8 +242,59 @@ def cpu_baseline(q_host: torch.Tensor, x_host: torch.Tensor, k: int):
     return q_host.shape[0] / dt, dt, ref_i.numpy(), kind
 
 
+def reference_gpu_arm(args):
+    """--impl reference --reference-device cuda: the reference's own GPU path for this search,
+    ``PostfilterKNN`` (retrieve/src/retrieve/modules/knn.py:23-76: the corpus cast to fp16 and
+    pre-transposed, cuBLAS ``torch.mm(..., out_dtype=float32)`` over every item, then
+    ``masked_topk``'s two-level top-k) from its installed package, on the same corpus and query
+    batch, the whole batch per call, CUDA events around each call. Rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    if not (REF_SITE / "retrieve").is_dir():
+        print(json.dumps({"impl": "reference", "unavailable": "the reference package is not installed under "
+                          "baseline/_ref"}), flush=True)
+        return
+    if str(REF_SITE) not in sys.path:
+        sys.path.insert(0, str(REF_SITE))
+    from retrieve.modules.knn import PostfilterKNN
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cent = centres(dev)
+    x = corpus_rows(cent, 0, args.n_items, args.n_items)
+    q = queries(cent, args.batch)
+    module = PostfilterKNN(k=args.k, backend="torch")
+    module.register_index(x)
+    del x
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        module(q)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in ev:
+        a.record()
+        module(q)
+        b.record()
+    torch.cuda.synchronize()
+    ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+    value = args.batch / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "fp16 scores in fp32", "data": "synthetic", "config": config_dict(args),
+        "reference_device": "cuda",
+        "reference_path": "PostfilterKNN (torch backend): cuBLAS fp16 x fp16 -> fp32 [B, N] scores, masked_topk",
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def reference_arm(args):
     """--impl reference: the reference's CPU path on the host cores, rank 0 only."""
+    if getattr(args, "reference_device", "cpu") == "cuda":
+        reference_gpu_arm(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
